@@ -1,0 +1,420 @@
+"""Benchmark of the affine 4-bit MoE hot path on B200.
+
+Workload (N = 1): config 1 of the spec -- one MoE layer decoding one token
+(H 4096, 128 experts, top-8, expert F 1536, 4-bit g64), synthetic seeded
+inputs. A step is one full layer for one token (router, routing, gate|up +
+SwiGLU, down + weighted combine). To keep the selected experts cold in L2,
+steps rotate over 8 independent layers (10.9 GB of expert weights) and a fresh
+token per step. Config 2 (prefill, 2048 tokens) is reported under "prefill".
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2q|reference]
+
+Prints ONE JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mlxfast-qwen38-125b-a6b-engine_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+H, E, F, TOPK, GS = 4096, 128, 1536, 8, 64
+PREFILL_T = 2048
+N_LAYERS = 8
+N_TOKENS = 4096
+# Algorithmic bytes of one decode step (8 experts x (gate + up + down) packed
+# weights with scales/biases, the bf16 router, activations): 86,049,344 B.
+EXPERT_BYTES = 3 * (F * (H // 2 + 2 * 2 * H // GS))  # gate/up/down are the same size here
+DECODE_BYTES = TOPK * EXPERT_BYTES + E * H * 2 + 65_536
+PREFILL_FLOP = PREFILL_T * TOPK * (2 * 2 * F * H + 2 * H * F) + 2 * PREFILL_T * E * H
+METRIC = "decode tok/s (bs=1) + gather_qmv HBM GB/s and % of 8 TB/s; prefill tok/s"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic(name):
+    """ncu DRAM bytes per launch recorded in profiles/<name>.json (or None)."""
+    p = os.path.join(ROOT, "profiles", name)
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"b2q_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        loaded = [r[0] for r in rows if r[2] > 200.0] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+
+
+# --------------------------------------------------------------------------
+# CPU baselines (the reference's own MLX CPU quantized kernels)
+# --------------------------------------------------------------------------
+_REF_STATE = {}
+
+
+def _ref_init(seed, rows):
+    """Pool initializer: build one process's weight rows once (outside any timing)."""
+    import numpy as np
+
+    from oracle.oracle import MlxRef, Oracle, bf16_to_f32, f32_to_bf16
+
+    rng = np.random.default_rng(seed)
+    K = H
+    wq = rng.integers(0, 2**32, size=(rows, K // 8), dtype=np.uint64).astype(np.uint32)
+    s = f32_to_bf16(rng.uniform(0.002, 0.02, (rows, K // GS)).astype(np.float32))
+    b = f32_to_bf16(-8.0 * bf16_to_f32(s) + rng.normal(0, 1e-3, s.shape).astype(np.float32))
+    x = f32_to_bf16(rng.standard_normal((1, K)).astype(np.float32))
+    _REF_STATE.update(ref=MlxRef() if MlxRef.available() else None, orc=Oracle(), wq=wq, s=s, b=b, x=x,
+                      out=np.zeros((1, rows), np.uint16))
+
+
+def _ref_run(reps):
+    """Time `reps` passes of this process's rows through the MLX CPU kernel (seconds)."""
+    st = _REF_STATE
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        if st["ref"] is not None:
+            st["ref"].qmm(st["x"], st["wq"], st["s"], st["b"], GS, 4, out=st["out"])
+        else:
+            st["orc"].qmm_mlx_cpu(st["x"], st["wq"], st["s"], st["b"], GS, 4)
+    return time.perf_counter() - t0
+
+
+def _ref_worker(args):
+    seed, rows, reps = args
+    _ref_init(seed, rows)
+    return _ref_run(reps)
+
+
+def cpu_row_cost():
+    """Seconds per 4096-element qmm row on one core (reference kernel)."""
+    rows = 256
+    t = _ref_worker((0, rows, 3))
+    return t / (3 * rows)
+
+
+def decode_rows_per_token():
+    # gate/up: 2 x 1536 rows of K = 4096; down: 4096 rows of K = 1536 = 1536 rows of K = 4096 equivalent
+    return TOPK * (2 * F + H * F // H)
+
+
+def cpu_baseline_sample(budget_s=12.0):
+    """Single core, the reference CPU kernel, bounded sample of config 1."""
+    from oracle.oracle import MlxRef
+
+    kind = "reference" if MlxRef.available() else "port"
+    t_row = cpu_row_cost()
+    rows = max(64, min(4096, int(budget_s / 3 / t_row)))
+    t = _ref_worker((1, rows, 3))
+    per_row = t / (3 * rows)
+    tok_s = 1.0 / (per_row * decode_rows_per_token())
+    sample = (f"{3 * rows} rows of K=4096 4-bit g64 qmv through the reference's MLX CPU kernel "
+              f"(backend/cpu/quantized.cpp _qmm_t, bf16 sum) on 1 core; tok/s = 1/(row time x "
+              f"{decode_rows_per_token()} row-equivalents per token); router/SwiGLU/combine (<2% of work) omitted")
+    return {"value": tok_s, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle.oracle import MlxRef
+
+    kind = "reference" if MlxRef.available() else "port"
+    cores = os.cpu_count() or 1
+    t_row = cpu_row_cost()
+    total_steps = args.steps + args.warmup
+    budget = 60.0  # seconds of kernel time over the whole run
+    rows = max(1, int(budget / max(1, total_steps) / t_row))
+    ctx = mp.get_context("spawn")
+    pools = [ctx.Pool(1, initializer=_ref_init, initargs=(i, rows)) for i in range(cores)]
+    try:
+        for _ in range(args.warmup):
+            [r.get() for r in [p.apply_async(_ref_run, (1,)) for p in pools]]
+        dt = 0.0
+        for _ in range(args.steps):
+            # a step ends when the slowest process has done its rows
+            dt += max(r.get() for r in [p.apply_async(_ref_run, (1,)) for p in pools])
+    finally:
+        for p in pools:
+            p.terminate()
+    tok = args.steps * cores * rows / decode_rows_per_token()
+    value = tok / dt
+    sample = (f"each step: {cores} processes x {rows} K=4096 rows of the reference MLX CPU 4-bit kernel "
+              f"(backend/cpu/quantized.cpp), throughput converted at {decode_rows_per_token()} row-equivalents "
+              "per decode token")
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * dt / max(1, args.steps), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 1: MoE layer decode, H4096 E128 top8 F1536 4-bit g64 (CPU sample)"},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# GPU arm
+# --------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=60000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="b2q", choices=["b2q", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+
+    import b2q
+    from b2q import synth
+    from b2q._lib import check, lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        pg = dist
+
+    hbm_peak, tc_peak, peak_kind = load_peaks()
+    L = lib()
+
+    # ---------------- decode (config 1) ----------------
+    layers = [synth.moe_layer(E, H, F, GS, device=dev, seed=100 + 7 * i) for i in range(N_LAYERS)]
+    routers = [synth.router_weight(E, H, device=dev, seed=200 + i) for i in range(N_LAYERS)]
+    xs = synth.activations((N_TOKENS, H), device=dev, seed=1)
+    out = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+    ws_bytes = L.b2q_moe_decode_workspace_size(1, H, E, F, TOPK)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+    fn = L.b2q_moe_decode
+    argsets = []
+    for i in range(N_LAYERS):
+        Ld = layers[i]
+        argsets.append([Ld[k].data_ptr() for k in ("wg", "sg", "bg", "wu", "su", "bu", "wd", "sd", "bd")])
+    xbase, xstride = xs.data_ptr(), H * 2
+    outp, wsp = out.data_ptr(), ws.data_ptr()
+
+    def step(i):
+        j = i % N_LAYERS
+        rc = fn(xbase + (i % N_TOKENS) * xstride, routers[j].data_ptr(), *argsets[j], outp, None, None, None,
+                1, H, E, F, TOPK, GS, 4, wsp, ws_bytes, sp)
+        if rc:
+            check(rc)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize(dev)
+    if pg:
+        pg.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms_total = ev0.elapsed_time(ev1)
+    if pg:
+        t = torch.tensor([ms_total], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms_total = float(t.item())
+    st = L.b2q_workspace_status(wsp, ws_bytes, sp)
+    if st != 0:
+        raise RuntimeError(f"device-side error {st} during the timed decode loop")
+    ms_step = ms_total / args.steps
+    tok_s = 1000.0 / ms_step  # one token per step for the whole job
+    achieved = DECODE_BYTES / (ms_step * 1e-3) / 1e9
+    clocks = clk.summary()
+
+    # ---------------- e2e through the public API ----------------
+    moe = [b2q.MoE(routers[i], layers[i], TOPK, GS) for i in range(N_LAYERS)]
+    n_e2e = min(args.steps, 3000)
+    host_x = torch.empty((n_e2e + args.warmup, 1, H), dtype=torch.bfloat16).pin_memory()
+    host_x.copy_(xs[: (n_e2e + args.warmup)].view(-1, 1, H).cpu())
+    host_out = torch.empty((1, H), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            dx.copy_(host_x[i], non_blocking=True)
+            y = moe[i % N_LAYERS](dx)
+            host_out.copy_(y, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n_e2e):
+            dx.copy_(host_x[args.warmup + i], non_blocking=True)
+            y = moe[i % N_LAYERS](dx)
+            host_out.copy_(y, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / n_e2e
+    if pg:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # ---------------- prefill (config 2) ----------------
+    prefill = None
+    if not args.no_prefill:
+        del moe
+        xp = synth.activations((PREFILL_T, H), device=dev, seed=3)
+        pws = b2q.Workspace(L.b2q_moe_prefill_workspace_size(PREFILL_T, H, E, F, TOPK), dev)
+        pout = torch.empty((PREFILL_T, H), dtype=torch.bfloat16, device=dev)
+
+        def pstep(i):
+            j = i % N_LAYERS
+            Ld = layers[j]
+            rc = L.b2q_moe_prefill(xp.data_ptr(), routers[j].data_ptr(),
+                                   *[Ld[k].data_ptr() for k in ("wg", "sg", "bg", "wu", "su", "bu", "wd", "sd", "bd")],
+                                   pout.data_ptr(), None, None, PREFILL_T, H, E, F, TOPK, GS, 4, pws.ptr(),
+                                   pws.buf.numel(), sp)
+            if rc:
+                check(rc)
+
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                pstep(i)
+        torch.cuda.synchronize(dev)
+        psteps = 10
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        for i in range(psteps):
+            pstep(i)
+        p1.record(stream)
+        torch.cuda.synchronize(dev)
+        pms = p0.elapsed_time(p1) / psteps
+        tflops = PREFILL_FLOP / (pms * 1e-3) / 1e12
+        prefill = {"workload": "config 2: MoE layer prefill, 2048 tokens", "tok_s": PREFILL_T * 1000.0 / pms,
+                   "ms_per_layer": pms, "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc_peak,
+                                                     "unit": "TFLOP/s", "frac": tflops / tc_peak,
+                                                     "peak_kind": peak_kind,
+                                                     "traffic": load_traffic("moe_prefill_c2.json")}}
+
+    if rank != 0:
+        if pg:
+            pg.destroy_process_group()
+        return
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        cpu = cpu_baseline_sample()
+    line = {
+        "metric": METRIC,
+        "value": tok_s,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded; random-init 4-bit experts)",
+        "config": {"workload": "config 1: one MoE layer decode, bs=1, H4096 E128 top8 F1536 4-bit g64",
+                   "parallelism": "single GPU" if world == 1 else f"ep{world}",
+                   "l2": f"cold: {N_LAYERS} rotating layers ({N_LAYERS * E * EXPERT_BYTES / 1e9:.1f} GB experts) "
+                         f"and a fresh token per step"},
+        "gather_qmv_hbm_gbs": achieved,
+        "hbm_frac_of_8tbs": achieved / 8000.0,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                     "bytes_per_launch": DECODE_BYTES,
+                     "traffic": load_traffic("moe_decode_c1.json")},
+        "e2e": {"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
+                "api": "b2q.MoE.__call__ (pinned host token in, pinned host output back each step)"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "prefill": prefill,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    if pg:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

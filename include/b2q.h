@@ -1,0 +1,204 @@
+/* b2q.h -- C ABI of the B200 affine 4-bit weight-product library (libb2q.so).
+ *
+ * The entry points replace the quantized-product surface of the reference
+ * engine (Layr-Labs/mlxfast-qwen38-125b-a6b-engine). Each declaration names the
+ * reference interface it stands in for; paths are relative to that project,
+ * with MLXC = Vendor/mlx-swift/Source/Cmlx/mlx/mlx and
+ * MLXCAPI = Vendor/mlx-swift/Source/Cmlx/mlx-c/mlx/c.
+ *
+ * Conventions (all entry points):
+ *  - Plain pointers and sizes. Tensors are row-major and live in device memory
+ *    unless a parameter says otherwise. bf16 values are 16-bit patterns
+ *    (uint16_t). Packed weights are uint32 words holding 32/bits values, value
+ *    8*i+j of a row in bits [4j, 4j+4) of word i (MLXC/backend/cpu/quantized.cpp:215-233);
+ *    scales and biases are bf16 [rows, K/group_size].
+ *  - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream) and is stream-ordered; nothing blocks the host unless stated.
+ *  - Return 0 on success, a negative B2Q_E* code on failure; no exception
+ *    crosses the ABI. b2q_last_error() gives a message for the calling thread
+ *    (mirrors mlx-c's status + error handler, MLXCAPI/ops.cpp:1505-1508).
+ *  - The library never allocates device memory. Entry points that need
+ *    scratch take a caller-owned `workspace` whose size comes from the matching
+ *    *_workspace_size() call; it must be zero-filled once before first use
+ *    (b2q_workspace_reset) and is left zero-filled by every call that
+ *    completes without a device-side error. Calls sharing one workspace must
+ *    be ordered on one stream.
+ *  - Only bits == 4 is implemented on the device (the packed format of the
+ *    path); group_size is 32, 64 or 128. Other values return B2Q_EUNSUPPORTED.
+ */
+#ifndef B2Q_H
+#define B2Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2Q_API __attribute__((visibility("default")))
+#else
+#define B2Q_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2Q_OK 0
+#define B2Q_EINVAL (-1)       /* invalid shape, pointer or argument */
+#define B2Q_EUNSUPPORTED (-2) /* valid for the reference, not implemented here */
+#define B2Q_ECUDA (-3)        /* a CUDA runtime / launch error */
+#define B2Q_ETIMEOUT (-4)     /* a bounded device-side wait ran out */
+#define B2Q_ENCCL (-5)        /* an NCCL error (expert-parallel mode) */
+
+/* Message of the last failing call on this thread ("" if none). */
+B2Q_API const char* b2q_last_error(void);
+/* ABI version: major*10000 + minor*100 + patch. */
+B2Q_API int b2q_version(void);
+/* Number of SMs of the current device (the persistent-grid size), or < 0. */
+B2Q_API int b2q_device_sm_count(void);
+
+/* ---- packing ------------------------------------------------------------ */
+
+/* Replaces mlx_dequantize (MLXCAPI/ops.h:359-369) -> affine_dequantize
+ * (MLXC/ops.cpp:5254-5346; Metal kernel MLXC/backend/metal/kernels/quantized.h:3314-3373).
+ * out[r, k] = bf16(fp32(s)*q + fp32(b)) for r < rows, k < K (bit-exact with the
+ * Metal dequantizer). */
+B2Q_API int b2q_dequantize(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                   uint16_t* out, int64_t rows, int K, int group_size, int bits,
+                   void* stream);
+
+/* Replaces mlx_quantize (MLXCAPI/ops.h:801-808) -> quantize
+ * (MLXC/ops.cpp:5214-5253; CPU kernel MLXC/backend/cpu/quantized.cpp:1158-1236).
+ * w bf16 [rows, K] -> packed w_q [rows, K*bits/32], scales/biases [rows, K/gs]. */
+B2Q_API int b2q_quantize(const uint16_t* w, uint32_t* w_q, uint16_t* scales, uint16_t* biases,
+                 int64_t rows, int K, int group_size, int bits, void* stream);
+
+/* ---- products ------------------------------------------------------------ */
+
+/* Replaces mlx_quantized_matmul (MLXCAPI/ops.h:809-818, MLXCAPI/ops.cpp:2585-2616)
+ * -> quantized_matmul (MLXC/ops.cpp:4784-4832), QuantizedMatmul::eval_gpu
+ * (MLXC/backend/metal/quantized.cpp:1982-2075).
+ * transpose != 0: y[M, N] = x[M, K] . dequant(w[N, K])^T (the only layout the
+ * engine uses; transpose == 0 returns B2Q_EUNSUPPORTED).
+ * Routing mirrors the reference's: M <= 8 -> the streaming qmv kernel
+ * (decode), larger M -> the tensor-core qmm kernel (prefill). */
+B2Q_API int b2q_qmm(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+            const uint16_t* biases, uint16_t* y, int M, int N, int K,
+            int group_size, int bits, int transpose, void* stream);
+
+/* Replaces mlx_gather_qmm (MLXCAPI/ops.h:475-488, MLXCAPI/ops.cpp:1471-1510)
+ * -> gather_qmm (MLXC/ops.cpp:5559-5643), GatherQMM::eval_gpu
+ * (MLXC/backend/metal/quantized.cpp:2089-2205).
+ * For i < batch: y[i] (M x N) = x[lhs[i]] (M x K) . dequant(w[rhs[i]])^T, with
+ * x [n_x, M, K], w [n_w, N, K*bits/32], scales/biases [n_w, N, K/gs],
+ * y [batch, M, N]. lhs_indices/rhs_indices may be NULL (identity). Indices are
+ * checked on the device: an item whose lhs >= n_x or rhs >= n_w is not read and
+ * its y rows are written as zeros (the reference reads out of bounds instead).
+ * sorted_indices is the reference's hint that rhs is non-decreasing. */
+B2Q_API int b2q_gather_qmm(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+                   const uint16_t* biases, const uint32_t* lhs_indices,
+                   const uint32_t* rhs_indices, uint16_t* y, int batch, int M,
+                   int N, int K, int n_x, int n_w, int group_size, int bits,
+                   int transpose, int sorted_indices, void* stream);
+
+/* ---- MoE operators (the Runner's fused-operator surface) ------------------ */
+
+/* Replaces TrackFastMoEKernels.routerGemv (Runner/FastModel/TrackFastMoE.swift:2246-2310)
+ * and the generic matmul(x_f32, W_f32^T) (Runner/FastModel/TrackFastModel.swift:884-903):
+ * logits f32 [T, E] = f32(x[T, H]) . f32(wr[E, H])^T. */
+B2Q_API int b2q_moe_router_logits(const uint16_t* x, const uint16_t* wr, float* logits,
+                          int T, int E, int H, void* stream);
+
+/* Replaces TrackFastMoEKernels.route (Runner/FastModel/TrackFastMoE.swift:767-911):
+ * top-k (largest first, ties to the lower index) + softmax over the k selected.
+ * logits f32 [T, E] -> idx u32 [T, k], w f32 [T, k]. k <= 32, E <= 1024. */
+B2Q_API int b2q_moe_route(const float* logits, uint32_t* idx, float* w, int T, int E, int k,
+                  void* stream);
+
+/* Replaces TrackFastMoEKernels.gateUpAct (Runner/FastModel/TrackFastMoE.swift:1192-1410)
+ * for routed slots: for slot z < n_slots with expert idx[z] and token xrow[z]:
+ * act[z, f] = silu(bf16(g)) * bf16(u) in bf16, g/u the gate/up qmv of x[xrow[z]].
+ * x [S, H]; wg/wu [E, F, H/8]; act [n_slots, F]. xrow may be NULL (slot z -> token z / k
+ * is then NOT assumed: NULL means token 0 for every slot). */
+B2Q_API int b2q_moe_gate_up_act(const uint16_t* x, const uint32_t* wg, const uint16_t* sg,
+                        const uint16_t* bg, const uint32_t* wu, const uint16_t* su,
+                        const uint16_t* bu, const uint32_t* idx, const uint32_t* xrow,
+                        uint16_t* act, int n_slots, int S, int H, int E, int F,
+                        int group_size, int bits, void* stream);
+
+/* Replaces TrackFastMoEKernels.downCombine (Runner/FastModel/TrackFastMoE.swift:1412-1590)
+ * without the shared expert: out[t, h] = bf16(colsum_j f32(bf16(y_j[h])) * w[t, j]),
+ * y_j = qmv(wd[idx[t*k+j]], act[t*k+j]). act [S*k, F], idx/w [S, k], out [S, H].
+ * k <= 8. */
+B2Q_API int b2q_moe_down_combine(const uint16_t* act, const uint32_t* wd, const uint16_t* sd,
+                         const uint16_t* bd, const uint32_t* idx, const float* w,
+                         uint16_t* out, int S, int H, int E, int F, int k,
+                         int group_size, int bits, void* stream);
+
+/* One decode MoE layer for S tokens (S <= 8): router logits, route,
+ * gate|up + SwiGLU, down + weighted combine. S == 1 runs as ONE persistent
+ * launch (grid barrier after the router, in-CTA combine); S > 1 chains the
+ * four operators above. Replaces the
+ * decode branch of moeForwardShared (Runner/FastModel/TrackFastModel.swift:867-955)
+ * minus the shared expert. Outputs: out [S, H] bf16; idx/w [S, k] (may be
+ * NULL); logits [S, E] f32 (may be NULL). k <= 8. The workspace holds the
+ * grid barrier counters, the slot activations and the error word. */
+B2Q_API size_t b2q_moe_decode_workspace_size(int S, int H, int E, int F, int k);
+B2Q_API int b2q_moe_decode(const uint16_t* x, const uint16_t* wr,
+                   const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                   const uint32_t* wd, const uint16_t* sd, const uint16_t* bd,
+                   uint16_t* out, uint32_t* idx, float* w, float* logits,
+                   int S, int H, int E, int F, int k, int group_size, int bits,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* One prefill MoE layer over T tokens: router logits, route, stable sort of the
+ * T*k assignments by expert (TrackPrefillSort.swift:84-201), gate|up + SwiGLU
+ * gather GEMM and down gather GEMM on the tensor cores over expert-aligned row
+ * tiles (TrackPrefillIndirect.swift:40-227), and the weighted combine through
+ * the inverse permutation (TrackP12Prefill.swift:180-237).
+ * out [T, H] bf16; idx/w [T, k] may be NULL. */
+B2Q_API size_t b2q_moe_prefill_workspace_size(int T, int H, int E, int F, int k);
+B2Q_API int b2q_moe_prefill(const uint16_t* x, const uint16_t* wr,
+                    const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                    const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                    const uint32_t* wd, const uint16_t* sd, const uint16_t* bd,
+                    uint16_t* out, uint32_t* idx, float* w,
+                    int T, int H, int E, int F, int k, int group_size, int bits,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces TrackFastKernels.swiglu2 (Runner/FastModel/TrackFastKernels2.swift:575-600):
+ * act[i] = silu(g[i]) * u[i] with the bf16 Sigmoid functor, n elements. */
+B2Q_API int b2q_swiglu(const uint16_t* g, const uint16_t* u, uint16_t* act, int64_t n, void* stream);
+
+/* Replaces track_p12_moe_sorted_combine (Runner/FastModel/TrackP12Prefill.swift:180-197)
+ * without the shared expert: out[t, h] = bf16(colsum_j f32(y[inverse[t*k+j], h]) * w[t, j]),
+ * y [T*k, H] in sorted-row order. k <= 32. */
+B2Q_API int b2q_moe_sorted_combine(const uint16_t* y, const uint32_t* inverse, const float* w, uint16_t* out,
+                           int T, int H, int k, void* stream);
+
+/* Stable counting sort of R expert ids (the first stage of b2q_moe_prefill):
+ * sorted_ids[p], token_rows[p] = order[p] / k, inverse[order[p]] = p,
+ * offsets[E + 1]. Replaces TrackPrefillSort.apply (TrackPrefillSort.swift:84-105). */
+B2Q_API size_t b2q_sort_workspace_size(int R, int E);
+B2Q_API int b2q_moe_sort(const uint32_t* ids, uint32_t* sorted_ids, uint32_t* token_rows,
+                 uint32_t* inverse, uint32_t* offsets, int R, int E, int k,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- workspace / status -------------------------------------------------- */
+
+/* Zero-fills a workspace (cudaMemsetAsync on `stream`). */
+B2Q_API int b2q_workspace_reset(void* workspace, size_t workspace_bytes, void* stream);
+/* Reads (synchronously) and clears the device error word a workspace carries:
+ * returns B2Q_OK or the B2Q_E* code a kernel recorded (e.g. B2Q_ETIMEOUT). */
+B2Q_API int b2q_workspace_status(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Test hook for the failure path: launches one kernel that waits, with a
+ * bound of timeout_ns, on a flag in `workspace` that nothing sets, and returns
+ * (after a stream sync) B2Q_ETIMEOUT when the bound ran out as designed. */
+B2Q_API int b2q_selftest_wait_timeout(void* workspace, size_t workspace_bytes,
+                              long long timeout_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2Q_H */

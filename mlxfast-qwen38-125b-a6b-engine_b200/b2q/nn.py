@@ -1,0 +1,104 @@
+"""Module-level call sites of the path, mirroring the reference's surface.
+
+* ``QuantizedLinear``  -- MLXNN QuantizedLinear.callAsFunction
+  (Vendor/mlx-swift/Source/MLXNN/Quantized.swift:238-350) and the Runner's
+  TrackQuantWeight.apply (Runner/FastModel/TrackFastWeights.swift:43-53).
+* ``SwitchLinear`` / ``SwitchGLU`` -- mlx-swift-lm's stacked-expert layers
+  (behaviour per docs/qwen38-125b-a6b-port-notes.md:628-735 and
+  Runner/FastModel/TrackP12Prefill.swift:198-237): gate/up/down projections of
+  E experts, ``act = silu(gate) * up``, computed through gather_qmm.
+* ``MoE``              -- the Runner's TrackMoE bundle and moeForwardShared
+  (Runner/FastModel/TrackFastModel.swift:225-248, :867-1009) without the
+  shared expert: router logits, top-k routing, experts, weighted combine;
+  decode windows (<= 8 tokens) take the fused decode operator, larger windows
+  the sorted prefill operator.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+class QuantizedLinear:
+    def __init__(self, weight, scales, biases, group_size: int = 64, bits: int = 4, bias=None):
+        self.weight, self.scales, self.biases = weight, scales, biases
+        self.group_size, self.bits = group_size, bits
+        self.bias = bias
+
+    @property
+    def rows(self) -> int:
+        return self.weight.shape[0]
+
+    @classmethod
+    def from_linear(cls, w_bf16: torch.Tensor, group_size: int = 64, bits: int = 4):
+        wq, s, b = ops.quantize(w_bf16.contiguous(), group_size, bits)
+        return cls(wq, s, b, group_size, bits)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        y = ops.quantized_matmul(x.contiguous(), self.weight, self.scales, self.biases, True, self.group_size, self.bits)
+        if self.bias is not None:
+            y = y + self.bias
+        return y
+
+
+class SwitchLinear:
+    """Stacked expert projection: weight [E, N, K/8], scales/biases [E, N, K/gs]."""
+
+    def __init__(self, weight, scales, biases, group_size: int = 64, bits: int = 4):
+        self.weight, self.scales, self.biases = weight, scales, biases
+        self.group_size, self.bits = group_size, bits
+
+    def __call__(self, x, indices, sorted_indices: bool = False):
+        # x [..., 1, K] per index (expanded), indices of x's leading shape
+        return ops.gather_qmm(x, self.weight, self.scales, self.biases, None, indices.contiguous(), True,
+                              self.group_size, self.bits, sorted_indices)
+
+
+class SwitchGLU:
+    def __init__(self, gate_proj: SwitchLinear, up_proj: SwitchLinear, down_proj: SwitchLinear):
+        self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        """x [T, H], indices [T, k] -> [T, k, H] (per-expert outputs, not combined)."""
+        T, H = x.shape
+        k = indices.shape[-1]
+        E = self.gate_proj.weight.shape[0]
+        sorted_ids, token_rows, inverse, _ = ops.moe_sort(indices.contiguous().view(-1), E, k)
+        x3 = x.contiguous().view(T, 1, H)
+        lhs = token_rows.view(-1)
+        g = ops.gather_qmm(x3, self.gate_proj.weight, self.gate_proj.scales, self.gate_proj.biases, lhs, sorted_ids,
+                           True, self.gate_proj.group_size, self.gate_proj.bits, True)
+        u = ops.gather_qmm(x3, self.up_proj.weight, self.up_proj.scales, self.up_proj.biases, lhs, sorted_ids,
+                           True, self.up_proj.group_size, self.up_proj.bits, True)
+        act = ops.swiglu(g, u)
+        y = ops.gather_qmm(act, self.down_proj.weight, self.down_proj.scales, self.down_proj.biases, None, sorted_ids,
+                           True, self.down_proj.group_size, self.down_proj.bits, True)
+        # unsort: row p of y belongs to flat slot order[p]; inverse[slot] = p
+        return y.view(T * k, -1)[inverse.long()].view(T, k, -1)
+
+
+class MoE:
+    """Router + routed experts + weighted combine (no shared expert)."""
+
+    def __init__(self, router_weight: torch.Tensor, experts: dict, top_k: int, group_size: int = 64, bits: int = 4):
+        self.router_weight = router_weight  # bf16 [E, H]
+        self.experts = experts  # wg/sg/bg, wu/su/bu, wd/sd/bd
+        self.top_k = top_k
+        self.group_size, self.bits = group_size, bits
+
+    @property
+    def num_experts(self) -> int:
+        return self.router_weight.shape[0]
+
+    def __call__(self, x: torch.Tensor, return_routing: bool = False):
+        x2 = x.contiguous().view(-1, x.shape[-1])
+        if x2.shape[0] <= 8:
+            r = ops.moe_decode(x2, self.router_weight, self.experts, self.top_k, self.group_size, self.bits,
+                               return_routing=return_routing)
+        else:
+            r = ops.moe_prefill(x2, self.router_weight, self.experts, self.top_k, self.group_size, self.bits,
+                                return_routing=return_routing)
+        if return_routing:
+            return (r[0].view(x.shape),) + tuple(r[1:])
+        return r.view(x.shape)

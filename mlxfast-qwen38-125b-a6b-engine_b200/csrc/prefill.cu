@@ -1,0 +1,216 @@
+// prefill.cu -- the prefill MoE layer: router, route, expert sort, expert
+// products over the sorted rows, SwiGLU, and the weighted combine through the
+// inverse permutation.
+//
+// Reference flow (paths relative to the reference project):
+//   TrackP12Prefill.sortedMoE            Runner/FastModel/TrackP12Prefill.swift:198-237
+//   TrackPrefillIndirect.apply / .down   Runner/FastModel/TrackPrefillIndirect.swift:83-227
+//   track_p12_moe_sorted_combine         Runner/FastModel/TrackP12Prefill.swift:180-197
+//   compiled silu * up                   Runner/FastModel/TrackFastKernels2.swift:547-600
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "engine.cuh"
+#include "host.hpp"
+#include "misc.cuh"
+#include "prefill.cuh"
+
+namespace b2q {
+
+// act[p, f] = silu(bf16 g) * bf16 u, all in bf16 (compiledSiluProduct).
+__global__ void swiglu_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u,
+                              uint16_t* __restrict__ act, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) act[i] = swiglu_bf16(g[i], u[i]);
+}
+
+// out[t, h] = bf16(colsum_j f32(y[inverse[t*k + j], h]) * w[t, j]) with the
+// mlx_colsum_small_f32 association (TrackFastKernels2.swift:36-47).
+__global__ void sorted_combine_kernel(const uint16_t* __restrict__ y, const uint32_t* __restrict__ inverse,
+                                      const float* __restrict__ w, uint16_t* __restrict__ out, int T, int H,
+                                      int k) {
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t = blockIdx.y;
+  if (h >= H || t >= T) return;
+  float prod[32];
+  for (int j = 0; j < k; ++j) {
+    const uint32_t pj = __ldg(inverse + (size_t)t * k + j);
+    prod[j] = bf2f(y[(size_t)pj * H + h]) * __ldg(w + (size_t)t * k + j);
+  }
+  const int TY = k < 8 ? k : 8;
+  float tt[8];
+  for (int q = 0; q < TY; ++q) {
+    float a = 0.0f;
+    for (int r = q; r < k; r += TY) a = prod[r] + a;
+    tt[q] = a;
+  }
+  float total = tt[0];
+  for (int q = 1; q < TY; ++q) total = tt[q] + total;
+  out[(size_t)t * H + h] = f2bf(total);
+}
+
+bool prefill_qmm_eligible(int, int, int, int, int, const void*, const void*, const void*, const void*,
+                          const void*) {
+  return false;  // the tensor-core gather GEMM is selected in prefill_tc.cu when built
+}
+
+int launch_prefill_gather_qmm(const uint16_t*, const uint32_t*, const uint16_t*, const uint16_t*, const uint32_t*,
+                              const uint32_t*, uint16_t*, int, int, int, int, int, int, int, int, cudaStream_t) {
+  return set_error(B2Q_EUNSUPPORTED, "tensor-core gather GEMM not built");
+}
+
+struct PrefillWs {
+  int* err;
+  float* logits;
+  uint32_t* idx;
+  float* w;
+  uint32_t* sorted_ids;
+  uint32_t* token_rows;
+  uint32_t* inverse;
+  uint32_t* offsets;
+  uint16_t* g;
+  uint16_t* u;
+  uint16_t* act;
+  uint16_t* y;
+  size_t bytes;
+};
+
+static size_t a256(size_t v) { return (v + 255) / 256 * 256; }
+
+static PrefillWs prefill_ws_layout(void* base, int T, int H, int E, int F, int k) {
+  PrefillWs d{};
+  char* b = static_cast<char*>(base);
+  const size_t R = (size_t)T * k;
+  size_t off = 0;
+  d.err = reinterpret_cast<int*>(b);
+  off = 256;
+  d.logits = reinterpret_cast<float*>(b + off);
+  off = a256(off + 4 * (size_t)T * E);
+  d.idx = reinterpret_cast<uint32_t*>(b + off);
+  off = a256(off + 4 * R);
+  d.w = reinterpret_cast<float*>(b + off);
+  off = a256(off + 4 * R);
+  d.sorted_ids = reinterpret_cast<uint32_t*>(b + off);
+  off = a256(off + 4 * R);
+  d.token_rows = reinterpret_cast<uint32_t*>(b + off);
+  off = a256(off + 4 * R);
+  d.inverse = reinterpret_cast<uint32_t*>(b + off);
+  off = a256(off + 4 * R);
+  d.offsets = reinterpret_cast<uint32_t*>(b + off);
+  off = a256(off + 4 * ((size_t)E + 1));
+  d.g = reinterpret_cast<uint16_t*>(b + off);
+  off = a256(off + 2 * R * F);
+  d.u = reinterpret_cast<uint16_t*>(b + off);
+  off = a256(off + 2 * R * F);
+  d.act = reinterpret_cast<uint16_t*>(b + off);
+  off = a256(off + 2 * R * F);
+  d.y = reinterpret_cast<uint16_t*>(b + off);
+  off = a256(off + 2 * R * H);
+  d.bytes = off;
+  return d;
+}
+
+}  // namespace b2q
+
+using namespace b2q;
+
+extern "C" {
+
+int b2q_swiglu(const uint16_t* g, const uint16_t* u, uint16_t* act, int64_t n, void* stream) {
+  clear_error();
+  if (n < 0) return set_error(B2Q_EINVAL, "swiglu: n < 0");
+  if (n == 0) return B2Q_OK;
+  if (!g || !u || !act) return set_error(B2Q_EINVAL, "swiglu: null pointer");
+  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, act, n);
+  B2Q_TRY_CUDA(cudaGetLastError());
+  return B2Q_OK;
+}
+
+int b2q_moe_sorted_combine(const uint16_t* y, const uint32_t* inverse, const float* w, uint16_t* out, int T, int H,
+                           int k, void* stream) {
+  clear_error();
+  if (T < 0 || H <= 0 || k < 1 || k > 32) return set_error(B2Q_EINVAL, "sorted_combine: bad shape");
+  if (T == 0) return B2Q_OK;
+  if (!y || !inverse || !w || !out) return set_error(B2Q_EINVAL, "sorted_combine: null pointer");
+  dim3 grid((H + 255) / 256, T);
+  sorted_combine_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, inverse, w, out, T, H, k);
+  B2Q_TRY_CUDA(cudaGetLastError());
+  return B2Q_OK;
+}
+
+size_t b2q_sort_workspace_size(int R, int E) {
+  (void)R;
+  (void)E;
+  return 256;  // the error word; the sort itself keeps its state in shared memory
+}
+
+int b2q_moe_sort(const uint32_t* ids, uint32_t* sorted_ids, uint32_t* token_rows, uint32_t* inverse,
+                 uint32_t* offsets, int R, int E, int k, void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (R < 0 || E < 1 || E > 1024 || k < 1) return set_error(B2Q_EINVAL, "moe_sort: bad shape");
+  if (!ids || !workspace || workspace_bytes < 256) return set_error(B2Q_EINVAL, "moe_sort: null pointer/workspace");
+  if (R == 0) return B2Q_OK;
+  return launch_expert_sort(ids, sorted_ids, token_rows, inverse, offsets, R, E, k, static_cast<int*>(workspace),
+                            static_cast<cudaStream_t>(stream));
+}
+
+size_t b2q_moe_prefill_workspace_size(int T, int H, int E, int F, int k) {
+  if (T < 1 || H < 1 || E < 1 || F < 1 || k < 1) return 0;
+  return prefill_ws_layout(nullptr, T, H, E, F, k).bytes;
+}
+
+int b2q_moe_prefill(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg,
+                    const uint16_t* bg, const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                    const uint32_t* wd, const uint16_t* sd, const uint16_t* bd, uint16_t* out, uint32_t* idx,
+                    float* w, int T, int H, int E, int F, int k, int group_size, int bits, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (bits != 4) return set_error(B2Q_EUNSUPPORTED, "moe_prefill: bits=%d", bits);
+  if (!(group_size == 32 || group_size == 64 || group_size == 128))
+    return set_error(B2Q_EUNSUPPORTED, "moe_prefill: group_size=%d", group_size);
+  if (T < 0 || H <= 0 || E < 1 || E > 1024 || F <= 0 || k < 1 || k > 32 || k > E || H % group_size ||
+      F % group_size || H % 8 || F % 8)
+    return set_error(B2Q_EINVAL, "moe_prefill: bad shape");
+  if (T == 0) return B2Q_OK;
+  if (!x || !wr || !wg || !sg || !bg || !wu || !su || !bu || !wd || !sd || !bd || !out)
+    return set_error(B2Q_EINVAL, "moe_prefill: null pointer");
+  const PrefillWs ws = prefill_ws_layout(workspace, T, H, E, F, k);
+  if (!workspace || workspace_bytes < ws.bytes || !aligned16(workspace))
+    return set_error(B2Q_EINVAL, "moe_prefill: workspace of %zu bytes needed", ws.bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int R = T * k;
+  uint32_t* ix = idx ? idx : ws.idx;
+  float* ww = w ? w : ws.w;
+  int rc = eng::launch_router_logits(x, wr, ws.logits, T, E, H, st);
+  if (rc) return rc;
+  rc = eng::launch_route(ws.logits, ix, ww, T, E, k, st);
+  if (rc) return rc;
+  rc = launch_expert_sort(ix, ws.sorted_ids, ws.token_rows, ws.inverse, ws.offsets, R, E, k, ws.err, st);
+  if (rc) return rc;
+  // expert products over the sorted rows: gate, up (x rows through token_rows)
+  rc = b2q_gather_qmm(x, wg, sg, bg, ws.token_rows, ws.sorted_ids, ws.g, R, 1, F, H, T, E, group_size, bits, 1, 1,
+                      stream);
+  if (rc) return rc;
+  rc = b2q_gather_qmm(x, wu, su, bu, ws.token_rows, ws.sorted_ids, ws.u, R, 1, F, H, T, E, group_size, bits, 1, 1,
+                      stream);
+  if (rc) return rc;
+  {
+    const int64_t n = (int64_t)R * F;
+    swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ws.g, ws.u, ws.act, n);
+    B2Q_TRY_CUDA(cudaGetLastError());
+  }
+  rc = b2q_gather_qmm(ws.act, wd, sd, bd, nullptr, ws.sorted_ids, ws.y, R, 1, H, F, R, E, group_size, bits, 1, 1,
+                      stream);
+  if (rc) return rc;
+  {
+    dim3 grid((H + 255) / 256, T);
+    sorted_combine_kernel<<<grid, 256, 0, st>>>(ws.y, ws.inverse, ww, out, T, H, k);
+    B2Q_TRY_CUDA(cudaGetLastError());
+  }
+  return B2Q_OK;
+}
+
+}  // extern "C"

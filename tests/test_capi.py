@@ -1,0 +1,77 @@
+"""The C-ABI library loads, exports every declared entry point, and its host
+side rejects bad arguments before touching the device (CPU-only checks)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "b2q.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^B2Q_API\s+[\w\s\*]+?\b(b2q_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_surface():
+    syms = declared_symbols()
+    for must in ("b2q_qmm", "b2q_gather_qmm", "b2q_dequantize", "b2q_quantize", "b2q_moe_route",
+                 "b2q_moe_gate_up_act", "b2q_moe_down_combine", "b2q_moe_decode", "b2q_moe_prefill",
+                 "b2q_moe_sort", "b2q_last_error"):
+        assert must in syms
+
+
+def test_library_exports_every_declared_symbol(b2q_mod):
+    from b2q._lib import LIB_PATH, SIGNATURES
+
+    lib = ctypes.CDLL(LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+        assert name in SIGNATURES, f"{name} missing from the Python binding"
+
+
+def test_host_side_argument_errors(b2q_mod):
+    lib = b2q_mod.lib()
+    # unsupported bit width / group size: refused before any CUDA call
+    assert lib.b2q_qmm(None, None, None, None, None, 1, 16, 512, 64, 3, 1, None) == -2
+    assert b"bits=3" in lib.b2q_last_error()
+    assert lib.b2q_qmm(None, None, None, None, None, 1, 16, 512, 48, 4, 1, None) == -2
+    # transpose=false is not implemented for the path
+    assert lib.b2q_gather_qmm(None, None, None, None, None, None, None, 1, 1, 16, 512, 1, 1, 64, 4, 0, 0,
+                              None) == -2
+    # bad shapes
+    assert lib.b2q_dequantize(None, None, None, None, 4, 100, 64, 4, None) == -1
+    assert lib.b2q_moe_route(None, None, None, 1, 16, 40, None) == -1
+    assert lib.b2q_moe_decode(*([None] * 15), 1, 4096, 128, 1536, 9, 64, 4, None, 0, None) == -2
+    # empty work is a no-op success
+    assert lib.b2q_qmm(None, None, None, None, None, 0, 16, 512, 64, 4, 1, None) == 0
+    # a null workspace is refused
+    assert lib.b2q_workspace_status(None, 0, None) == -1
+
+
+def test_workspace_sizes(b2q_mod):
+    lib = b2q_mod.lib()
+    d = lib.b2q_moe_decode_workspace_size(1, 4096, 128, 1536, 8)
+    assert d >= 256 + 8 * 1536 * 2 + 128 * 4
+    p = lib.b2q_moe_prefill_workspace_size(2048, 4096, 128, 1536, 8)
+    assert p >= 16384 * (3 * 1536 * 2 + 4096 * 2)
+    assert lib.b2q_moe_decode_workspace_size(0, 4096, 128, 1536, 8) == 0
+
+
+def test_python_ops_validate_inputs(b2q_mod):
+    import torch
+
+    x = torch.zeros(1, 512, dtype=torch.bfloat16)
+    w = torch.zeros(16, 64, dtype=torch.int32)
+    s = torch.zeros(16, 8, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA device"):
+        b2q_mod.quantized_matmul(x, w, s, s)
+    with pytest.raises(ValueError):
+        b2q_mod.ops._check_quant(w, s, s[:, :4], 64, 4)
+    with pytest.raises(ValueError, match="only 4-bit"):
+        b2q_mod.ops._check_quant(w, s, s, 64, 8)
