@@ -229,6 +229,8 @@ def main():
     ap.add_argument("--impl", default="b2q", choices=["b2q", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="rotating layers (cold-L2 decode)")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -260,8 +262,9 @@ def main():
     L = lib()
 
     # ---------------- decode (config 1) ----------------
-    layers = [synth.moe_layer(E, H, F, GS, device=dev, seed=100 + 7 * i) for i in range(N_LAYERS)]
-    routers = [synth.router_weight(E, H, device=dev, seed=200 + i) for i in range(N_LAYERS)]
+    n_layers = max(1, args.layers)
+    layers = [synth.moe_layer(E, H, F, GS, device=dev, seed=100 + 7 * i) for i in range(n_layers)]
+    routers = [synth.router_weight(E, H, device=dev, seed=200 + i) for i in range(n_layers)]
     xs = synth.activations((N_TOKENS, H), device=dev, seed=1)
     out = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
     ws_bytes = L.b2q_moe_decode_workspace_size(1, H, E, F, TOPK)
@@ -270,14 +273,14 @@ def main():
     sp = stream.cuda_stream
     fn = L.b2q_moe_decode
     argsets = []
-    for i in range(N_LAYERS):
+    for i in range(n_layers):
         Ld = layers[i]
         argsets.append([Ld[k].data_ptr() for k in ("wg", "sg", "bg", "wu", "su", "bu", "wd", "sd", "bd")])
     xbase, xstride = xs.data_ptr(), H * 2
     outp, wsp = out.data_ptr(), ws.data_ptr()
 
     def step(i):
-        j = i % N_LAYERS
+        j = i % n_layers
         rc = fn(xbase + (i % N_TOKENS) * xstride, routers[j].data_ptr(), *argsets[j], outp, None, None, None,
                 1, H, E, F, TOPK, GS, 4, wsp, ws_bytes, sp)
         if rc:
@@ -311,8 +314,8 @@ def main():
     clocks = clk.summary()
 
     # ---------------- e2e through the public API ----------------
-    moe = [b2q.MoE(routers[i], layers[i], TOPK, GS) for i in range(N_LAYERS)]
-    n_e2e = min(args.steps, 3000)
+    moe = [b2q.MoE(routers[i], layers[i], TOPK, GS) for i in range(n_layers)]
+    n_e2e = 0 if args.no_e2e else min(args.steps, 3000)
     host_x = torch.empty((n_e2e + args.warmup, 1, H), dtype=torch.bfloat16).pin_memory()
     host_x.copy_(xs[: (n_e2e + args.warmup)].view(-1, 1, H).cpu())
     host_out = torch.empty((1, H), dtype=torch.bfloat16).pin_memory()
@@ -320,18 +323,18 @@ def main():
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             dx.copy_(host_x[i], non_blocking=True)
-            y = moe[i % N_LAYERS](dx)
+            y = moe[i % n_layers](dx)
             host_out.copy_(y, non_blocking=True)
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(n_e2e):
             dx.copy_(host_x[args.warmup + i], non_blocking=True)
-            y = moe[i % N_LAYERS](dx)
+            y = moe[i % n_layers](dx)
             host_out.copy_(y, non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1) / n_e2e
+    e2e_ms = e0.elapsed_time(e1) / max(1, n_e2e) if n_e2e else float("nan")
     if pg:
         t = torch.tensor([e2e_ms], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -346,7 +349,7 @@ def main():
         pout = torch.empty((PREFILL_T, H), dtype=torch.bfloat16, device=dev)
 
         def pstep(i):
-            j = i % N_LAYERS
+            j = i % n_layers
             Ld = layers[j]
             rc = L.b2q_moe_prefill(xp.data_ptr(), routers[j].data_ptr(),
                                    *[Ld[k].data_ptr() for k in ("wg", "sg", "bg", "wu", "su", "bu", "wd", "sd", "bd")],
@@ -396,7 +399,7 @@ def main():
         "data": "synthetic (seeded; random-init 4-bit experts)",
         "config": {"workload": "config 1: one MoE layer decode, bs=1, H4096 E128 top8 F1536 4-bit g64",
                    "parallelism": "single GPU" if world == 1 else f"ep{world}",
-                   "l2": f"cold: {N_LAYERS} rotating layers ({N_LAYERS * E * EXPERT_BYTES / 1e9:.1f} GB experts) "
+                   "l2": f"cold: {n_layers} rotating layers ({n_layers * E * EXPERT_BYTES / 1e9:.1f} GB experts) "
                          f"and a fresh token per step"},
         "gather_qmv_hbm_gbs": achieved,
         "hbm_frac_of_8tbs": achieved / 8000.0,
@@ -404,8 +407,9 @@ def main():
                      "frac": achieved / hbm_peak, "peak_kind": peak_kind,
                      "bytes_per_launch": DECODE_BYTES,
                      "traffic": load_traffic("moe_decode_c1.json")},
-        "e2e": {"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
-                "api": "b2q.MoE.__call__ (pinned host token in, pinned host output back each step)"},
+        "e2e": ({"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
+                 "steps": n_e2e, "api": "b2q.MoE.__call__ (pinned host token in, pinned host output back each step)"}
+                if n_e2e else None),
         "gpu_launches": args.steps,
         "clocks": clocks,
         "prefill": prefill,

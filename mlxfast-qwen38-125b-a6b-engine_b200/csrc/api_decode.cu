@@ -125,9 +125,6 @@ static int gather_impl(const char* fn, const uint16_t* x, const uint32_t* w, con
     eng::Params p;
     base_params(p, eng::MODE_QMV, gs);
     p.x = x;
-    p.w = w;
-    p.s = s;
-    p.b = b;
     p.lhs = lhs;
     p.rhs = rhs;
     p.y = y;
@@ -138,7 +135,9 @@ static int gather_impl(const char* fn, const uint16_t* x, const uint32_t* w, con
     p.n_w = n_w;
     p.g1.K = K;
     rc = eng::plan(p);
+    if (rc == B2Q_OK) rc = eng::set_maps_qmv(p, w, s, b);
     if (rc == B2Q_OK) return eng::launch(p, stream, false);
+    if (rc != B2Q_EUNSUPPORTED) return rc;
   }
   if (M > eng::MAX_COLS && prefill_qmm_eligible(batch, M, N, K, gs, x, w, s, b, y)) {
     return launch_prefill_gather_qmm(x, w, s, b, lhs, rhs, y, batch, M, N, K, n_x, n_w, gs, sorted, st);
@@ -196,8 +195,6 @@ static int gate_up_impl(const uint16_t* x, const uint32_t* wg, const uint16_t* s
   eng::Params p;
   base_params(p, eng::MODE_GU, gs);
   p.x = x;
-  p.wg = wg; p.sg = sg; p.bg = bg;
-  p.wu = wu; p.su = su; p.bu = bu;
   p.idx_in = idx;
   p.xrow_in = xrow;
   p.k = tok_div;
@@ -208,6 +205,8 @@ static int gate_up_impl(const uint16_t* x, const uint32_t* wg, const uint16_t* s
   p.E = E;
   p.F = F;
   rc = eng::plan(p);
+  if (rc) return rc;
+  rc = eng::set_maps_gu(p, wg, sg, bg, wu, su, bu);
   if (rc) return rc;
   return eng::launch(p, stream, false);
 }
@@ -235,7 +234,6 @@ int b2q_moe_down_combine(const uint16_t* act, const uint32_t* wd, const uint16_t
   eng::Params p;
   base_params(p, eng::MODE_DOWN, group_size);
   p.act_in = act;
-  p.wd = wd; p.sd = sd; p.bd = bd;
   p.idx_in = idx;
   p.w_in = w;
   p.out = out;
@@ -245,6 +243,8 @@ int b2q_moe_down_combine(const uint16_t* act, const uint32_t* wd, const uint16_t
   p.F = F;
   p.k = k;
   rc = eng::plan(p);
+  if (rc) return rc;
+  rc = eng::set_maps_down(p, wd, sd, bd);
   if (rc) return rc;
   return eng::launch(p, stream, false);
 }
@@ -277,9 +277,6 @@ int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, co
     base_params(p, eng::MODE_FUSED, group_size);
     p.x = x;
     p.wr = wr;
-    p.wg = wg; p.sg = sg; p.bg = bg;
-    p.wu = wu; p.su = su; p.bu = bu;
-    p.wd = wd; p.sd = sd; p.bd = bd;
     p.out = out;
     p.idx_out = idx;
     p.w_out = w;
@@ -295,6 +292,10 @@ int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, co
     p.ws_logits = ws.logits;
     p.ws_act = ws.act;
     rc = eng::plan(p);
+    if (rc) return rc;
+    rc = eng::set_maps_gu(p, wg, sg, bg, wu, su, bu);
+    if (rc) return rc;
+    rc = eng::set_maps_down(p, wd, sd, bd);
     if (rc) return rc;
     return eng::launch(p, stream, true);
   }

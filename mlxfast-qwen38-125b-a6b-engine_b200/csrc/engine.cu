@@ -7,30 +7,76 @@
 //   track_moe_gate_up_act          Runner/FastModel/TrackFastMoE.swift:1192-1410
 //   track_moe_down_combine         Runner/FastModel/TrackFastMoE.swift:1412-1590
 //   track_moe_route                Runner/FastModel/TrackFastMoE.swift:767-911
-// The design is this file's own: bulk-copy producer, MMA consumers, static
-// persistent schedule, fixed-order cross-warp reduction.
+// The design is this file's own: TMA tensor-copy producer, MMA consumers,
+// static persistent schedule, fixed-order cross-warp reduction.
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 
 #include "common.cuh"
 #include "engine.cuh"
 #include "host.hpp"
+#include "tmap.hpp"
 
 namespace b2q {
 namespace eng {
 
 // ---------------------------------------------------------------------------
+// PTX: 3-D tiled TMA load into shared memory, completion on an mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Wait with a suspend-time hint so a waiting warp sleeps instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline, volatile int* abort) {
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (abort && *abort) return false;
+    if (globaltimer() > deadline) return false;
+  }
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ float lo_bf(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float hi_bf(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// ---------------------------------------------------------------------------
 // unit / pass enumeration (shared by producer and consumers)
 // ---------------------------------------------------------------------------
 struct Sched {
-  int U;       // total units
-  int U_gu;    // FUSED: gate|up units before the down units
-  int RB;      // QMV: row blocks per item
-  int FB;      // gate|up row blocks per slot (F / 8)
-  int HB;      // down row blocks per token (H / 8)
-  int npair;   // down slot pairs (ceil(k / 2))
+  int U;      // total units
+  int U_gu;   // FUSED: gate|up units before the down units
+  int RB;     // QMV: row blocks per item
+  int FB;     // gate|up row blocks per slot (F / 8)
+  int HB;     // down row blocks per token (H / 8)
+  int npair;  // down slot pairs (ceil(k / 2))
 };
 
 __device__ __forceinline__ Sched make_sched(const Params& p) {
@@ -65,19 +111,6 @@ __device__ __forceinline__ int unit_passes(const Params& p, const Sched& s, int 
   return unit_is_down(p, s, u) ? s.npair * p.g2.nkc : p.g1.nkc;
 }
 
-// Where one pass's rows come from.
-struct LoadDesc {
-  const uint8_t* wP;
-  const uint8_t* wQ;
-  const uint8_t* sP;
-  const uint8_t* bP;
-  const uint8_t* sQ;
-  const uint8_t* bQ;
-  int nP, nQ;
-  int row_bytes, meta_bytes;  // per row in this pass
-  int wstride, mstride;       // global row strides (bytes)
-};
-
 __device__ __forceinline__ uint32_t clamp_expert(uint32_t e, int E, int* err) {
   if (e >= (uint32_t)E) {
     record_error(err, B2Q_EINVAL);
@@ -86,65 +119,47 @@ __device__ __forceinline__ uint32_t clamp_expert(uint32_t e, int E, int* err) {
   return e;
 }
 
-// expert ids of the current CTA's routed slots (FUSED) live in shared memory
-__device__ __forceinline__ LoadDesc describe(const Params& p, const Sched& s, int u, int pass,
-                                             const uint32_t* sidx, int* err) {
+// Which maps and rows one pass reads.
+struct LoadDesc {
+  int mwP, msP, mbP, mwQ, msQ, mbQ;  // tensor-map slots
+  int rowP, rowQ;                    // first row of each 8-row block (in the map's row space)
+  int kc;                            // reduction chunk index
+  bool valid;
+};
+
+__device__ __forceinline__ LoadDesc describe(const Params& p, const Sched& s, int u, int pass, const uint32_t* sidx,
+                                             int* err) {
   LoadDesc d{};
-  if (!unit_is_down(p, s, u) && p.mode != MODE_QMV) {
-    // gate|up: P = gate rows, Q = up rows of expert e
-    const int z = u / s.FB, rb = u % s.FB;
-    const uint32_t e = (p.mode == MODE_FUSED) ? sidx[z] : clamp_expert(__ldg(p.idx_in + z), p.E, err);
-    const Geo& g = p.g1;
-    const int c = pass;
-    const size_t row0 = (size_t)e * p.F + (size_t)rb * 8;
-    d.wstride = g.K / 2;
-    d.mstride = g.G * 2;
-    d.row_bytes = min(g.KC, g.K - c * g.KC) / 2;
-    d.meta_bytes = d.row_bytes * 2 / p.gs * 2;
-    const size_t wo = row0 * d.wstride + (size_t)c * g.KC / 2;
-    const size_t mo = row0 * d.mstride + (size_t)c * (g.KC / p.gs) * 2;
-    d.wP = reinterpret_cast<const uint8_t*>(p.wg) + wo;
-    d.wQ = reinterpret_cast<const uint8_t*>(p.wu) + wo;
-    d.sP = reinterpret_cast<const uint8_t*>(p.sg) + mo;
-    d.bP = reinterpret_cast<const uint8_t*>(p.bg) + mo;
-    d.sQ = reinterpret_cast<const uint8_t*>(p.su) + mo;
-    d.bQ = reinterpret_cast<const uint8_t*>(p.bu) + mo;
-    d.nP = d.nQ = 8;
-    return d;
-  }
+  d.valid = true;
   if (p.mode == MODE_QMV) {
     const int item = u / s.RB, rb = u % s.RB;
     const uint32_t e = p.rhs ? __ldg(p.rhs + item) : (uint32_t)item;
     const uint32_t xi = p.lhs ? __ldg(p.lhs + item) : (uint32_t)item;
-    const Geo& g = p.g1;
-    const int c = pass;
-    d.wstride = g.K / 2;
-    d.mstride = g.G * 2;
-    d.row_bytes = min(g.KC, g.K - c * g.KC) / 2;
-    d.meta_bytes = d.row_bytes * 2 / p.gs * 2;
-    if (e >= (uint32_t)p.n_w || xi >= (uint32_t)p.n_x) {
-      d.nP = d.nQ = 0;  // the finisher writes zeros for this item
-      return d;
-    }
-    const int r0 = rb * 16;
-    d.nP = max(0, min(8, p.N - r0));
-    d.nQ = max(0, min(8, p.N - r0 - 8));
-    const size_t base = (size_t)e * p.N + r0;
-    const size_t wo = base * d.wstride + (size_t)c * g.KC / 2;
-    const size_t mo = base * d.mstride + (size_t)c * (g.KC / p.gs) * 2;
-    d.wP = reinterpret_cast<const uint8_t*>(p.w) + wo;
-    d.wQ = d.wP + (size_t)8 * d.wstride;
-    d.sP = reinterpret_cast<const uint8_t*>(p.s) + mo;
-    d.bP = reinterpret_cast<const uint8_t*>(p.b) + mo;
-    d.sQ = d.sP + (size_t)8 * d.mstride;
-    d.bQ = d.bP + (size_t)8 * d.mstride;
+    d.valid = e < (uint32_t)p.n_w && xi < (uint32_t)p.n_x;
+    d.mwP = d.mwQ = M_W;
+    d.msP = d.msQ = M_S;
+    d.mbP = d.mbQ = M_B;
+    d.rowP = (int)(e * (uint32_t)p.N) + rb * 16;
+    d.rowQ = d.rowP + 8;
+    d.kc = pass;
     return d;
   }
-  // down: unit = (token t, 8 output rows hb); pass = (slot pair, reduction chunk)
+  if (!unit_is_down(p, s, u)) {
+    const int z = u / s.FB, rb = u % s.FB;
+    const uint32_t e = (p.mode == MODE_FUSED) ? sidx[z] : clamp_expert(__ldg(p.idx_in + z), p.E, err);
+    d.mwP = M_WG;
+    d.msP = M_SG;
+    d.mbP = M_BG;
+    d.mwQ = M_WU;
+    d.msQ = M_SU;
+    d.mbQ = M_BU;
+    d.rowP = d.rowQ = (int)(e * (uint32_t)p.F) + rb * 8;
+    d.kc = pass;
+    return d;
+  }
   const int ud = (p.mode == MODE_FUSED) ? u - s.U_gu : u;
   const int t = ud / s.HB, hb = ud % s.HB;
-  const Geo& g = p.g2;
-  const int pair = pass / g.nkc, c = pass % g.nkc;
+  const int pair = pass / p.g2.nkc;
   const int j0 = 2 * pair, j1 = 2 * pair + 1;
   uint32_t e0, e1;
   if (p.mode == MODE_FUSED) {
@@ -154,28 +169,19 @@ __device__ __forceinline__ LoadDesc describe(const Params& p, const Sched& s, in
     e0 = clamp_expert(__ldg(p.idx_in + (size_t)t * p.k + j0), p.E, err);
     e1 = (j1 < p.k) ? clamp_expert(__ldg(p.idx_in + (size_t)t * p.k + j1), p.E, err) : e0;
   }
-  d.wstride = g.K / 2;
-  d.mstride = g.G * 2;
-  d.row_bytes = min(g.KC, g.K - c * g.KC) / 2;
-  d.meta_bytes = d.row_bytes * 2 / p.gs * 2;
-  const size_t r0P = (size_t)e0 * p.H + (size_t)hb * 8;
-  const size_t r0Q = (size_t)e1 * p.H + (size_t)hb * 8;
-  const size_t cw = (size_t)c * g.KC / 2, cm = (size_t)c * (g.KC / p.gs) * 2;
-  d.wP = reinterpret_cast<const uint8_t*>(p.wd) + r0P * d.wstride + cw;
-  d.wQ = reinterpret_cast<const uint8_t*>(p.wd) + r0Q * d.wstride + cw;
-  d.sP = reinterpret_cast<const uint8_t*>(p.sd) + r0P * d.mstride + cm;
-  d.bP = reinterpret_cast<const uint8_t*>(p.bd) + r0P * d.mstride + cm;
-  d.sQ = reinterpret_cast<const uint8_t*>(p.sd) + r0Q * d.mstride + cm;
-  d.bQ = reinterpret_cast<const uint8_t*>(p.bd) + r0Q * d.mstride + cm;
-  d.nP = 8;
-  d.nQ = (j1 < p.k) ? 8 : 0;
+  d.mwP = d.mwQ = M_WD;
+  d.msP = d.msQ = M_SD;
+  d.mbP = d.mbQ = M_BD;
+  d.rowP = (int)(e0 * (uint32_t)p.H) + hb * 8;
+  d.rowQ = (int)(e1 * (uint32_t)p.H) + hb * 8;
+  d.kc = pass % p.g2.nkc;
   return d;
 }
 
 // ---------------------------------------------------------------------------
 // activation staging: bf16 rows -> permuted chunks + fp32 group sums
 // ---------------------------------------------------------------------------
-// col c of `dst` (stride XS bytes) receives row src_rows[c]; sums[c * G + g].
+// column c of `dst` (stride XS bytes) receives row src_rows[c]; sums[c * G + g].
 __device__ void stage_columns(uint8_t* dst, float* sums, int XS, const uint16_t* const* src_rows, int ncols,
                               int K, int gs, bool coherent) {
   const int tid = threadIdx.x;
@@ -195,11 +201,8 @@ __device__ void stage_columns(uint8_t* dst, float* sums, int XS, const uint16_t*
     for (int ch = 0; ch < gs / 8; ++ch) {
       const uint4 v = *reinterpret_cast<const uint4*>(base + ch * 16);
       // permuted (x0,x4)(x1,x5)(x2,x6)(x3,x7): sum in k order x0..x7
-      const float x0 = __uint_as_float(v.x << 16), x4 = __uint_as_float(v.x & 0xffff0000u);
-      const float x1 = __uint_as_float(v.y << 16), x5 = __uint_as_float(v.y & 0xffff0000u);
-      const float x2 = __uint_as_float(v.z << 16), x6 = __uint_as_float(v.z & 0xffff0000u);
-      const float x3 = __uint_as_float(v.w << 16), x7 = __uint_as_float(v.w & 0xffff0000u);
-      acc += ((((((x0 + x1) + x2) + x3) + x4) + x5) + x6) + x7;
+      acc += ((((((lo_bf(v.x) + lo_bf(v.y)) + lo_bf(v.z)) + lo_bf(v.w)) + hi_bf(v.x)) + hi_bf(v.y)) + hi_bf(v.z)) +
+             hi_bf(v.w);
     }
     sums[(size_t)col * G + g] = acc;
   }
@@ -207,57 +210,100 @@ __device__ void stage_columns(uint8_t* dst, float* sums, int XS, const uint16_t*
 }
 
 // ---------------------------------------------------------------------------
-// one pass of MMAs over this warp's share of the groups
+// one pass of MMAs over this warp's share of the 128-byte row pieces
 // ---------------------------------------------------------------------------
-struct LaneCols {
-  const uint8_t* xcol;  // this lane's B column (permuted chunks) at the pass start
-  const float* xs0;     // group sums of column 2c (absolute group index)
-  const float* xs1;     // group sums of column 2c+1
-  bool a00, a01, a10, a11;
-};
-
-template <int WPT>
-__device__ __forceinline__ void consume_pass(const uint8_t* __restrict__ st, const Geo& g, int gs, int g_lo,
-                                             int g_hi, int gabs0, const LaneCols& lc, float (&acc)[4]) {
+// Stage layout: [P weights][Q weights][sP][bP][sQ][bQ]. A weight block is one
+// 1024-byte atom per 128-byte piece of the 8 rows, 16-byte unit u of row r at
+// unit position u ^ r (TMA 128-byte swizzle). Lane (r = lane/4, c = lane%4)
+// takes packed word 4*u + c of row r of P and of Q -> MMA rows r and r + 8.
+// A piece holds 256 values = 8 / WPT quantization groups; the unrolled loop
+// over its 8 units keeps every swizzle offset a per-lane constant.
+//
+// KIND 0: one activation column matters for every lane (gate|up, qmv M = 1):
+//         elements 0 (row r) and 2 (row r + 8) against column sums xs0.
+// KIND 1: two columns per lane (qmv M >= 2): elements 0..3, xs0 / xs1.
+// KIND 2: down pass of slot pair `pair`: lanes c == pair own element 0
+//         (P slot, column 2c) and element 3 (Q slot, column 2c + 1).
+template <int WPT, int KIND>
+__device__ __forceinline__ void consume_pass(const uint8_t* __restrict__ st, const Geo& g, int pc_lo, int pc_hi,
+                                             int gabs0, const uint8_t* __restrict__ xcol,
+                                             const float* __restrict__ xs0, const float* __restrict__ xs1,
+                                             bool on, float (&acc)[4]) {
+  constexpr int GPC = 8 / WPT;  // groups per 128-byte piece
   const int lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
-  const uint8_t* wrow0 = st + r * g.RS + c * 4;
-  const uint8_t* wrow8 = st + (r + 8) * g.RS + c * 4;
-  const uint8_t* meta = st + 16 * g.RS;
-  const uint16_t* sPm = reinterpret_cast<const uint16_t*>(meta + (0 + r) * g.MS);
-  const uint16_t* bPm = reinterpret_cast<const uint16_t*>(meta + (8 + r) * g.MS);
-  const uint16_t* sQm = reinterpret_cast<const uint16_t*>(meta + (16 + r) * g.MS);
-  const uint16_t* bQm = reinterpret_cast<const uint16_t*>(meta + (24 + r) * g.MS);
-  const bool actP = lc.a00 || lc.a01, actQ = lc.a10 || lc.a11;
-#pragma unroll 2
-  for (int gi = g_lo; gi < g_hi; ++gi) {
-    float dA[4] = {0.f, 0.f, 0.f, 0.f};
-    float dB[4] = {0.f, 0.f, 0.f, 0.f};
-    const int wbase = gi * (gs / 8);  // first packed word of the group within the pass
+  const uint8_t* wP = st + r * 128 + c * 4;
+  const uint8_t* wQ = wP + g.blkw;
+  const uint8_t* mP = st + 2 * g.blkw;  // sP; bP at +blkm
+  const uint8_t* mQ = mP + 2 * g.blkm;  // sQ; bQ at +blkm
+  const uint8_t* xl = xcol + c * 16;
+  int sw[8];
 #pragma unroll
-    for (int j = 0; j < WPT; ++j) {
-      const int wi = wbase + j * 4;  // lane c takes word wi + c
-      const uint32_t W0 = *reinterpret_cast<const uint32_t*>(wrow0 + wi * 4);
-      const uint32_t W8 = *reinterpret_cast<const uint32_t*>(wrow8 + wi * 4);
-      const uint4 xv = *reinterpret_cast<const uint4*>(lc.xcol + (size_t)(wi + c) * 16);
-      uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
-      decode_word(W0, p0, p1, p2, p3);
-      decode_word(W8, q0, q1, q2, q3);
-      mma_bf16_16816(dA, p0, q0, p1, q1, xv.x, xv.y);
-      mma_bf16_16816(dB, p2, q2, p3, q3, xv.z, xv.w);
-    }
-    const int ga = gabs0 + gi;
-    if (actP) {
-      const float sv = bf2f(sPm[gi]);
-      const float bv = bf2f(bPm[gi]) - 128.0f * sv;
-      if (lc.a00) acc[0] += sv * (dA[0] + dB[0]) + bv * lc.xs0[ga];
-      if (lc.a01) acc[1] += sv * (dA[1] + dB[1]) + bv * lc.xs1[ga];
-    }
-    if (actQ) {
-      const float sv = bf2f(sQm[gi]);
-      const float bv = bf2f(bQm[gi]) - 128.0f * sv;
-      if (lc.a10) acc[2] += sv * (dA[2] + dB[2]) + bv * lc.xs0[ga];
-      if (lc.a11) acc[3] += sv * (dA[3] + dB[3]) + bv * lc.xs1[ga];
+  for (int u = 0; u < 8; ++u) sw[u] = (u ^ r) << 4;
+  for (int pc = pc_lo; pc < pc_hi; ++pc) {
+    const uint8_t* pw = wP + pc * 1024;
+    const uint8_t* pq = wQ + pc * 1024;
+    const uint8_t* px = xl + pc * 512;
+#pragma unroll
+    for (int pp = 0; pp < GPC / 2; ++pp) {
+      float D[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float dA[4] = {0.f, 0.f, 0.f, 0.f};
+        float dB[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < WPT; ++j) {
+          const int u = (2 * pp + h) * WPT + j;  // 16-byte unit within the piece
+          const uint32_t W0 = lds32(pw + sw[u]);
+          const uint32_t W8 = lds32(pq + sw[u]);
+          const uint4 xv = lds128(px + u * 64);
+          uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
+          decode_word(W0, p0, p1, p2, p3);
+          decode_word(W8, q0, q1, q2, q3);
+          mma_bf16_16816(dA, p0, q0, p1, q1, xv.x, xv.y);
+          mma_bf16_16816(dB, p2, q2, p3, q3, xv.z, xv.w);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) D[h][i] = dA[i] + dB[i];
+      }
+      // scales / biases of groups (g0, g0 + 1) for rows r and r + 8: one 32-bit word each
+      const int g0 = pc * GPC + 2 * pp;
+      int moff;
+      if (g.mswz) {
+        const int gg = g0 & 63;
+        moff = (g0 >> 6) * 1024 + r * 128 + ((((gg >> 3) ^ r)) << 4) + (gg & 7) * 2;
+      } else {
+        moff = r * g.mrow + g0 * 2;
+      }
+      const uint32_t sPv = lds32(mP + moff), bPv = lds32(mP + g.blkm + moff);
+      const uint32_t sQv = lds32(mQ + moff), bQv = lds32(mQ + g.blkm + moff);
+      const float2 x0 = *reinterpret_cast<const float2*>(xs0 + gabs0 + g0);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float sP = h ? hi_bf(sPv) : lo_bf(sPv);
+        const float sQ = h ? hi_bf(sQv) : lo_bf(sQv);
+        const float bP = fmaf(-128.0f, sP, h ? hi_bf(bPv) : lo_bf(bPv));
+        const float bQ = fmaf(-128.0f, sQ, h ? hi_bf(bQv) : lo_bf(bQv));
+        const float xa = h ? x0.y : x0.x;
+        if (KIND == 0) {
+          acc[0] = fmaf(bP, xa, fmaf(sP, D[h][0], acc[0]));
+          acc[2] = fmaf(bQ, xa, fmaf(sQ, D[h][2], acc[2]));
+        } else if (KIND == 1) {
+          const float2 x1 = *reinterpret_cast<const float2*>(xs1 + gabs0 + g0);
+          const float xb = h ? x1.y : x1.x;
+          acc[0] = fmaf(bP, xa, fmaf(sP, D[h][0], acc[0]));
+          acc[1] = fmaf(bP, xb, fmaf(sP, D[h][1], acc[1]));
+          acc[2] = fmaf(bQ, xa, fmaf(sQ, D[h][2], acc[2]));
+          acc[3] = fmaf(bQ, xb, fmaf(sQ, D[h][3], acc[3]));
+        } else {
+          const float2 x1 = *reinterpret_cast<const float2*>(xs1 + gabs0 + g0);
+          const float xb = h ? x1.y : x1.x;
+          const float e0 = fmaf(bP, xa, sP * D[h][0]);
+          const float e3 = fmaf(bQ, xb, sQ * D[h][3]);
+          acc[0] += on ? e0 : 0.0f;
+          acc[3] += on ? e3 : 0.0f;
+        }
+      }
     }
   }
 }
@@ -265,8 +311,6 @@ __device__ __forceinline__ void consume_pass(const uint8_t* __restrict__ st, con
 // ---------------------------------------------------------------------------
 // routing (one warp): top-k, ties to the lower index, softmax over the k
 // ---------------------------------------------------------------------------
-// lr: logits row (global, read with ld.cg when `coherent`); results to
-// sidx/sw (lane j < k writes slot j).
 __device__ void warp_route(const float* lr, int E, int k, bool coherent, uint32_t* sidx, float* sw) {
   const int lane = threadIdx.x & 31;
   float v[32];
@@ -329,7 +373,9 @@ __device__ void warp_route(const float* lr, int E, int k, bool coherent, uint32_
 // ---------------------------------------------------------------------------
 template <int WPT>
 __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // swizzled TMA destinations need 1024-byte alignment
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_misc);
@@ -340,8 +386,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
   float* rsum = sw + MAX_COLS;  // [NC_WARPS] router partials
   int* err = p.err;
   const Sched sch = make_sched(p);
-  const uint64_t t0 = globaltimer();
-  const uint64_t deadline = t0 + (uint64_t)p.timeout_ns;
+  const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
 
   if (tid == 0) {
     for (int i = 0; i < NSTAGE; ++i) {
@@ -359,41 +404,55 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
     // ------------------------------- producer -------------------------------
     if (fused) named_bar_sync(2, NTHREADS);  // wait for the routing
     if (lane == 0) {
+      for (int i = 0; i < N_MAPS; ++i)
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.map[i])) : "memory");
       const uint64_t pol = policy_evict_first();
       int L = 0;
       bool ok = !*abort_flag;
       for (int u = blockIdx.x; ok && u < sch.U; u += gridDim.x) {
         const int np = unit_passes(p, sch, u);
+        const Geo& g = unit_is_down(p, sch, u) ? p.g2 : p.g1;
         for (int pass = 0; pass < np; ++pass, ++L) {
-          const int sidx_s = L % NSTAGE;
-          if (L >= NSTAGE && !mbar_wait(&empty[sidx_s], ((L / NSTAGE) - 1) & 1, deadline, abort_flag)) {
+          const int si = L % NSTAGE;
+          if (L >= NSTAGE && !bar_wait(&empty[si], ((L / NSTAGE) - 1) & 1, deadline, abort_flag)) {
             if (!*abort_flag) record_error(err, B2Q_ETIMEOUT);
             *abort_flag = 1;
             ok = false;
             break;
           }
-          const bool down = unit_is_down(p, sch, u);
-          const Geo& g = down ? p.g2 : p.g1;
           const LoadDesc d = describe(p, sch, u, pass, sidx, err);
-          uint8_t* st = stages + (size_t)sidx_s * p.stage_bytes;
-          const uint32_t bytes = (uint32_t)(d.nP + d.nQ) * (d.row_bytes + 2 * d.meta_bytes);
-          mbar_arrive_expect_tx(&full[sidx_s], bytes);
-          for (int r = 0; r < d.nP; ++r) {
-            bulk_g2s(st + r * g.RS, d.wP + (size_t)r * d.wstride, d.row_bytes, &full[sidx_s], pol);
-            bulk_g2s(st + 16 * g.RS + (0 + r) * g.MS, d.sP + (size_t)r * d.mstride, d.meta_bytes, &full[sidx_s], pol);
-            bulk_g2s(st + 16 * g.RS + (8 + r) * g.MS, d.bP + (size_t)r * d.mstride, d.meta_bytes, &full[sidx_s], pol);
+          uint8_t* st = stages + (size_t)si * p.stage_bytes;
+          if (!d.valid) {
+            mbar_arrive_expect_tx(&full[si], 0u);
+            continue;
           }
-          for (int r = 0; r < d.nQ; ++r) {
-            bulk_g2s(st + (8 + r) * g.RS, d.wQ + (size_t)r * d.wstride, d.row_bytes, &full[sidx_s], pol);
-            bulk_g2s(st + 16 * g.RS + (16 + r) * g.MS, d.sQ + (size_t)r * d.mstride, d.meta_bytes, &full[sidx_s], pol);
-            bulk_g2s(st + 16 * g.RS + (24 + r) * g.MS, d.bQ + (size_t)r * d.mstride, d.meta_bytes, &full[sidx_s], pol);
+          // a box always delivers its full size (out-of-range parts of a last,
+          // shorter chunk are zero-filled), so the byte count is per box
+          const uint32_t mbox = g.mswz ? (uint32_t)(g.GC / 64) * 1024u : 8u * (uint32_t)g.GC * 2u;
+          mbar_arrive_expect_tx(&full[si], 2u * (uint32_t)g.blkw + 4u * mbox);
+          const int cw = d.kc * (g.KC / 256);  // 128-byte piece index of the chunk start
+          tma_load_3d(st, &p.map[d.mwP], 0, d.rowP, cw, &full[si], pol);
+          tma_load_3d(st + g.blkw, &p.map[d.mwQ], 0, d.rowQ, cw, &full[si], pol);
+          uint8_t* mb = st + 2 * g.blkw;
+          if (g.mswz) {
+            const int cm = d.kc * (g.GC / 64);
+            tma_load_3d(mb, &p.map[d.msP], 0, d.rowP, cm, &full[si], pol);
+            tma_load_3d(mb + g.blkm, &p.map[d.mbP], 0, d.rowP, cm, &full[si], pol);
+            tma_load_3d(mb + 2 * g.blkm, &p.map[d.msQ], 0, d.rowQ, cm, &full[si], pol);
+            tma_load_3d(mb + 3 * g.blkm, &p.map[d.mbQ], 0, d.rowQ, cm, &full[si], pol);
+          } else {
+            const int cm = d.kc * g.GC;  // element index along the meta row
+            tma_load_2d(mb, &p.map[d.msP], cm, d.rowP, &full[si], pol);
+            tma_load_2d(mb + g.blkm, &p.map[d.mbP], cm, d.rowP, &full[si], pol);
+            tma_load_2d(mb + 2 * g.blkm, &p.map[d.msQ], cm, d.rowQ, &full[si], pol);
+            tma_load_2d(mb + 3 * g.blkm, &p.map[d.mbQ], cm, d.rowQ, &full[si], pol);
           }
         }
       }
-      // Drain: no bulk copy may still be landing when the CTA exits.
+      // Drain: no copy may still be landing when the CTA exits.
       const uint64_t dl2 = globaltimer() + 200000000ull;
       for (int l = max(0, L - NSTAGE); l < L; ++l) {
-        if (!mbar_wait(&full[l % NSTAGE], (l / NSTAGE) & 1, dl2, nullptr)) record_error(err, B2Q_ETIMEOUT);
+        if (!bar_wait(&full[l % NSTAGE], (l / NSTAGE) & 1, dl2, nullptr)) record_error(err, B2Q_ETIMEOUT);
       }
     }
     __syncwarp();
@@ -418,12 +477,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
         for (int v = tid; v < nvec; v += NCT) {
           const uint4 xv = __ldg(reinterpret_cast<const uint4*>(p.x) + v);
           const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.wr + (size_t)e * p.H) + v);
-          const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            part += __uint_as_float(xa[i] << 16) * __uint_as_float(wa[i] << 16);
-            part += __uint_as_float(xa[i] & 0xffff0000u) * __uint_as_float(wa[i] & 0xffff0000u);
-          }
+          part += lo_bf(xv.x) * lo_bf(wv.x) + hi_bf(xv.x) * hi_bf(wv.x);
+          part += lo_bf(xv.y) * lo_bf(wv.y) + hi_bf(xv.y) * hi_bf(wv.y);
+          part += lo_bf(xv.z) * lo_bf(wv.z) + hi_bf(xv.z) * hi_bf(wv.z);
+          part += lo_bf(xv.w) * lo_bf(wv.w) + hi_bf(xv.w) * hi_bf(wv.w);
         }
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
@@ -471,7 +528,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
       }
       named_bar_sync(2, NTHREADS);  // releases the producer
     } else if (p.mode == MODE_GU) {
-      // stage all S tokens once
       const uint16_t* rows[MAX_COLS];
       for (int t = 0; t < p.S; ++t) rows[t] = p.x + (size_t)t * p.H;
       stage_columns(xbuf, xsum, p.g1.XS, rows, p.S, p.H, p.gs, false);
@@ -482,7 +538,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
       const bool down = unit_is_down(p, sch, u);
       const Geo& g = down ? p.g2 : p.g1;
       // ---- per-unit activation setup ----
-      LaneCols lc{};
+      const uint8_t* xcol;
+      const float* xs0;
+      const float* xs1;
       int item = 0, zslot = 0, tok = 0, rb = 0, hb = 0;
       bool item_ok = true;
       if (p.mode == MODE_QMV) {
@@ -500,14 +558,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           }
           cur_item = xkey;
         }
-        const int n = r;  // B column of this lane = token n
-        const int ncol = (n < p.M) ? n : 0;
-        lc.xcol = xbuf + (size_t)ncol * g.XS;
-        const int c0 = min(2 * c, p.M - 1), c1 = min(2 * c + 1, p.M - 1);
-        lc.xs0 = xsum + (size_t)c0 * g.G;
-        lc.xs1 = xsum + (size_t)c1 * g.G;
-        lc.a00 = lc.a10 = (2 * c < p.M);
-        lc.a01 = lc.a11 = (2 * c + 1 < p.M);
+        xcol = xbuf + (size_t)((r < p.M) ? r : 0) * g.XS;
+        xs0 = xsum + (size_t)min(2 * c, p.M - 1) * g.G;
+        xs1 = xsum + (size_t)min(2 * c + 1, p.M - 1) * g.G;
       } else if (!down) {
         zslot = u / sch.FB;
         rb = u % sch.FB;
@@ -518,10 +571,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           record_error(err, B2Q_EINVAL);
           tok = 0;
         }
-        lc.xcol = xbuf + (size_t)tok * g.XS;
-        lc.xs0 = lc.xs1 = xsum + (size_t)tok * g.G;
-        lc.a00 = lc.a10 = (c == 0);
-        lc.a01 = lc.a11 = false;
+        xcol = xbuf + (size_t)tok * g.XS;
+        xs0 = xs1 = xsum + (size_t)tok * g.G;
       } else {
         const int ud = (p.mode == MODE_FUSED) ? u - sch.U_gu : u;
         tok = ud / sch.HB;
@@ -548,42 +599,41 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           stage_columns(abuf, asum, g.XS, rows, p.k, p.F, p.gs, false);
           cur_tok = tok;
         }
-        const int n = r;
-        const int ncol = (n < p.k) ? n : 0;
-        lc.xcol = abuf + (size_t)ncol * g.XS;
-        const int c0 = min(2 * c, p.k - 1), c1 = min(2 * c + 1, p.k - 1);
-        lc.xs0 = asum + (size_t)c0 * g.G;
-        lc.xs1 = asum + (size_t)c1 * g.G;
+        xcol = abuf + (size_t)((r < p.k) ? r : 0) * g.XS;
+        xs0 = asum + (size_t)min(2 * c, p.k - 1) * g.G;
+        xs1 = asum + (size_t)min(2 * c + 1, p.k - 1) * g.G;
       }
 
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       const int np = unit_passes(p, sch, u);
       for (int pass = 0; pass < np; ++pass, ++L) {
         const int si = L % NSTAGE;
-        const bool ok = mbar_wait(&full[si], (L / NSTAGE) & 1, deadline, abort_flag);
+        const bool ok = bar_wait(&full[si], (L / NSTAGE) & 1, deadline, abort_flag);
         if (!ok && !*abort_flag) {
           record_error(err, B2Q_ETIMEOUT);
           *abort_flag = 1;
         }
         if (ok && !*abort_flag) {
-          int kc = pass;
-          LaneCols lcp = lc;
+          const int kc = down ? pass % g.nkc : pass;
+          const int pair = down ? pass / g.nkc : 0;
+          const int kcw = min(g.KC, g.K - kc * g.KC);
+          const int npieces = kcw / 256;  // 128-byte pieces of each row in this chunk
+          const int plo = (warp * npieces) / NC_WARPS, phi = ((warp + 1) * npieces) / NC_WARPS;
+          const uint8_t* st = stages + (size_t)si * p.stage_bytes;
+          const uint8_t* xc = xcol + (size_t)kc * (g.KC / 8) * 16;
+          const int gabs0 = kc * g.GC;  // blocks keep the full-pass box layout, also for a shorter last chunk
           if (down) {
-            const int pair = pass / g.nkc;
-            kc = pass % g.nkc;
-            lcp.a00 = (c == pair) && (2 * pair < p.k);
-            lcp.a11 = (c == pair) && (2 * pair + 1 < p.k);
-            lcp.a01 = lcp.a10 = false;
+            consume_pass<WPT, 2>(st, g, plo, phi, gabs0, xc, xs0, xs1, c == pair, acc);
+          } else if (p.mode == MODE_QMV && p.M > 1) {
+            consume_pass<WPT, 1>(st, g, plo, phi, gabs0, xc, xs0, xs1, true, acc);
+          } else {
+            consume_pass<WPT, 0>(st, g, plo, phi, gabs0, xc, xs0, xs1, true, acc);
           }
-          const int Gc = min(g.KC, g.K - kc * g.KC) / p.gs;
-          const int glo = (warp * Gc) / NC_WARPS, ghi = ((warp + 1) * Gc) / NC_WARPS;
-          lcp.xcol += (size_t)kc * (g.KC / 8) * 16;
-          consume_pass<WPT>(stages + (size_t)si * p.stage_bytes, g, p.gs, glo, ghi, kc * (g.KC / p.gs), lcp, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[si]);
       }
-      // ---- unit epilogue: fixed-order reduction over the 8 warps ----
+      // ---- unit epilogue: fixed-order reduction over the warps ----
       float* rw = red + ((size_t)buf * NC_WARPS + warp) * 128;
       rw[r * 8 + 2 * c] = acc[0];
       rw[r * 8 + 2 * c + 1] = acc[1];
@@ -675,12 +725,10 @@ __global__ void router_logits_kernel(const uint16_t* __restrict__ x, const uint1
   float part = 0.0f;
   for (int v = lane; v < H / 8; v += 32) {
     const uint4 a = __ldg(xv + v), b = __ldg(wv + v);
-    const uint32_t xa[4] = {a.x, a.y, a.z, a.w}, wa[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      part += __uint_as_float(xa[i] << 16) * __uint_as_float(wa[i] << 16);
-      part += __uint_as_float(xa[i] & 0xffff0000u) * __uint_as_float(wa[i] & 0xffff0000u);
-    }
+    part += lo_bf(a.x) * lo_bf(b.x) + hi_bf(a.x) * hi_bf(b.x);
+    part += lo_bf(a.y) * lo_bf(b.y) + hi_bf(a.y) * hi_bf(b.y);
+    part += lo_bf(a.z) * lo_bf(b.z) + hi_bf(a.z) * hi_bf(b.z);
+    part += lo_bf(a.w) * lo_bf(b.w) + hi_bf(a.w) * hi_bf(b.w);
   }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
@@ -716,28 +764,30 @@ int launch_route(const float* logits, uint32_t* idx, float* w, int T, int E, int
 }
 
 // ---------------------------------------------------------------------------
-// host: geometry, shared-memory plan, launch
+// host: geometry, shared-memory plan, tensor maps, launch
 // ---------------------------------------------------------------------------
 static int round_up(int v, int a) { return (v + a - 1) / a * a; }
 
-// Reduction-chunk geometry for one product family (K elements per row).
+// Reduction-chunk geometry for one product family (K elements per row);
+// returns the stage bytes one full pass needs.
 static int make_geo(Geo& g, int K, int gs) {
   g.K = K;
   g.G = K / gs;
-  const int unit = 8 * gs;  // chunk granularity keeps meta rows 16-byte sized and aligned
-  // largest chunk whose 16 rows + 32 meta rows fit one stage
+  // chunk granularity: whole 128-byte row pieces and whole 16-byte meta units
+  const int unit = std::max(256, 8 * gs);
   int kc = (K <= 4096) ? K : 4096;
   kc = std::max(unit, kc / unit * unit);
   g.KC = kc;
   g.nkc = (K + kc - 1) / kc;
-  const int row_bytes = kc / 2;
-  g.RS = row_bytes + ((16 - row_bytes % 128) + 128) % 128;  // RS % 128 == 16
-  int ms = round_up((kc / gs) * 2, 16);
-  if ((ms / 16) % 2 == 0) ms += 16;  // odd multiple of 16: 8 meta rows hit 8 bank quads
-  g.MS = ms;
+  g.GC = kc / gs;
+  g.blkw = 8 * (kc / 2);
+  // meta rows take the swizzled 128-byte layout when every chunk is whole 128-byte pieces
+  g.mswz = (g.GC % 64 == 0 && g.G % 64 == 0) ? 1 : 0;
+  g.mrow = g.GC * 2;
+  g.blkm = g.mswz ? (g.GC / 64) * 1024 : round_up(8 * g.GC * 2, 128);
   const int xb = (K / 8) * 16;
-  g.XS = xb + ((64 - xb % 128) + 128) % 128;  // XS % 128 == 64
-  return 16 * g.RS + 32 * g.MS;
+  g.XS = xb + ((64 - xb % 128) + 128) % 128;  // XS % 128 == 64: 8 columns hit distinct bank quads
+  return 2 * g.blkw + 4 * g.blkm;
 }
 
 int plan(Params& p) {
@@ -749,23 +799,23 @@ int plan(Params& p) {
   const bool uses_g1 = p.mode != MODE_DOWN;
   if (uses_g1) st1 = make_geo(p.g1, p.mode == MODE_QMV ? p.g1.K : p.H, p.gs);
   if (uses_down) st2 = make_geo(p.g2, p.F, p.gs);
-  p.stage_bytes = round_up(std::max(st1, st2), 128);
+  p.stage_bytes = round_up(std::max(st1, st2), 1024);
   if (p.stage_bytes > STAGE_MAX) return set_error(B2Q_EUNSUPPORTED, "engine: stage of %d bytes", p.stage_bytes);
   int off = NSTAGE * p.stage_bytes;
   p.xcols = (p.mode == MODE_QMV) ? p.M : (p.mode == MODE_GU ? p.S : (p.mode == MODE_FUSED ? 1 : 0));
   p.off_x = off;
   off += round_up(p.xcols * (uses_g1 ? p.g1.XS : 0), 128);
   p.off_xs = off;
-  off += round_up(p.xcols * (uses_g1 ? p.g1.G : 0) * 4, 128);
+  off += round_up(p.xcols * (uses_g1 ? p.g1.G : 0) * 4 + 16, 128);
   p.off_act = off;
   off += round_up(uses_down ? p.k * p.g2.XS : 0, 128);
   p.off_acts = off;
-  off += round_up(uses_down ? p.k * p.g2.G * 4 : 0, 128);
+  off += round_up(uses_down ? p.k * p.g2.G * 4 + 16 : 0, 128);
   p.off_red = off;
   off += 2 * NC_WARPS * 128 * 4;
   p.off_misc = off;
   off += 2 * NSTAGE * 8 + 16 + MAX_COLS * 8 + NC_WARPS * 4;
-  p.smem_bytes = round_up(off, 128);
+  p.smem_bytes = round_up(off, 128) + 1024;  // + alignment slack of the 1024-byte base
   if (p.smem_bytes > di.smem_optin)
     return set_error(B2Q_EUNSUPPORTED, "engine: needs %d bytes of shared memory, device allows %d", p.smem_bytes,
                      di.smem_optin);
@@ -773,10 +823,42 @@ int plan(Params& p) {
   return B2Q_OK;
 }
 
+// maps for a weight tensor [rows, K/8] and its scales / biases [rows, K/gs]
+static int set_triplet(Params& p, int slot_w, int slot_s, int slot_b, const uint32_t* w, const uint16_t* s,
+                       const uint16_t* b, uint64_t rows, const Geo& g) {
+  int rc = make_row_block_map(&p.map[slot_w], w, rows, (uint64_t)g.K / 2, (uint32_t)g.KC / 2, true);
+  if (rc) return rc;
+  rc = make_row_block_map(&p.map[slot_s], s, rows, (uint64_t)g.G * 2, (uint32_t)g.GC * 2, g.mswz != 0);
+  if (rc) return rc;
+  return make_row_block_map(&p.map[slot_b], b, rows, (uint64_t)g.G * 2, (uint32_t)g.GC * 2, g.mswz != 0);
+}
+
+int set_maps_qmv(Params& p, const uint32_t* w, const uint16_t* s, const uint16_t* b) {
+  return set_triplet(p, M_W, M_S, M_B, w, s, b, (uint64_t)p.n_w * p.N, p.g1);
+}
+int set_maps_gu(Params& p, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg, const uint32_t* wu,
+                const uint16_t* su, const uint16_t* bu) {
+  int rc = set_triplet(p, M_WG, M_SG, M_BG, wg, sg, bg, (uint64_t)p.E * p.F, p.g1);
+  if (rc) return rc;
+  return set_triplet(p, M_WU, M_SU, M_BU, wu, su, bu, (uint64_t)p.E * p.F, p.g1);
+}
+int set_maps_down(Params& p, const uint32_t* wd, const uint16_t* sd, const uint16_t* bd) {
+  return set_triplet(p, M_WD, M_SD, M_BD, wd, sd, bd, (uint64_t)p.E * p.H, p.g2);
+}
+
 template <int WPT>
 static int launch_t(const Params& p, cudaStream_t stream, bool cooperative, int grid) {
   auto kern = engine_kernel<WPT>;
-  B2Q_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem_bytes));
+  // The shared-memory opt-in is a per-device function attribute: raise it to
+  // the device maximum once instead of on every launch.
+  static int opted[64] = {0};
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (!opted[di.device]) {
+    B2Q_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, di.smem_optin));
+    opted[di.device] = 1;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(NTHREADS);

@@ -1,18 +1,20 @@
 // engine.cuh -- the streaming (decode) product engine: shared declarations.
 //
-// One persistent CTA per SM. Warp 8 is the producer: its lane 0 walks the
-// CTA's static list of units and, per pass, issues 1-D bulk copies (TMA) of 16
-// weight rows (two 8-row blocks P and Q) plus their scale/bias rows into a
-// 4-stage shared-memory ring, completion counted on an mbarrier. Warps 0-7 are
-// consumers: each takes an equal share of the pass's quantization groups,
-// decodes nibbles to bf16 pairs and runs m16n8k16 MMAs whose A operand is the
-// 16 weight rows and whose B operand is up to 8 activation columns (tokens or
-// routed slots); the per-group affine epilogue s*D + (b - 128 s)*sum(x) is
+// One persistent CTA per SM. Warp NC_WARPS is the producer: its lane 0 walks
+// the CTA's static list of units and, per pass, issues six TMA tensor copies
+// (an 8-row weight block P, an 8-row weight block Q, and their scale / bias
+// blocks) into a 4-stage shared-memory ring; completion is counted on an
+// mbarrier per stage. Warps 0..NC_WARPS-1 are consumers: each takes an equal
+// share of the pass's quantization groups (in pairs), decodes nibbles to bf16
+// pairs and runs m16n8k16 MMAs whose A operand is the 16 weight rows (P rows
+// 0-7, Q rows 8-15) and whose B operand is up to 8 activation columns (tokens
+// or routed slots); the per-group affine epilogue s*D + (b - 128 s)*sum(x) is
 // applied in fp32. A unit's warp partials are reduced in a fixed order in
 // shared memory and finished by a mode-specific epilogue (bf16 store, SwiGLU,
 // or the weighted expert combine).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -27,35 +29,37 @@ constexpr int MAX_COLS = 8;
 constexpr int STAGE_MAX = 40 * 1024;
 
 enum Mode : int { MODE_QMV = 0, MODE_GU = 1, MODE_DOWN = 2, MODE_FUSED = 3 };
+// tensor-map slots
+enum Map : int { M_W = 0, M_S = 1, M_B = 2, M_WG = 0, M_SG = 1, M_BG = 2, M_WU = 3, M_SU = 4, M_BU = 5, M_WD = 6,
+                 M_SD = 7, M_BD = 8, N_MAPS = 9 };
 
 // Geometry of one product family (reduction length K).
 struct Geo {
-  int K;    // reduction length
-  int G;    // groups per row (K / gs)
-  int KC;   // reduction chunk per pass
-  int nkc;  // passes per row block
-  int RS;   // shared-memory weight-row stride (bytes)
-  int MS;   // shared-memory meta-row stride (bytes)
-  int XS;   // shared-memory activation-column stride (bytes)
+  int K;      // reduction length
+  int G;      // groups per row (K / gs)
+  int KC;     // reduction chunk per pass (elements, a multiple of 256)
+  int nkc;    // passes per row block
+  int GC;     // groups per full pass (KC / gs)
+  int blkw;   // bytes of an 8-row weight block of a full pass (8 * KC / 2, 1024-aligned)
+  int blkm;   // bytes reserved per 8-row scale (or bias) block
+  int mswz;   // 1: meta blocks use the 128-byte swizzled layout, 0: plain [row][GC]
+  int mrow;   // plain meta: bytes per row in shared memory (GC * 2)
+  int XS;     // shared-memory activation-column stride (bytes)
 };
 
-struct Params {
+struct alignas(64) Params {
+  CUtensorMap map[N_MAPS];
   int mode;
   int gs;
   int wpt;  // packed words per lane per group = gs / 32
   // QMV / gather
   const uint16_t* x;
-  const uint32_t* w;
-  const uint16_t* s;
-  const uint16_t* b;
+  uint16_t* y;
   const uint32_t* lhs;
   const uint32_t* rhs;
-  uint16_t* y;
   int batch, M, N, n_x, n_w;
   // MoE
   const uint16_t* wr;
-  const uint32_t *wg, *wu, *wd;
-  const uint16_t *sg, *bg, *su, *bu, *sd, *bd;
   const uint32_t* idx_in;
   const uint32_t* xrow_in;
   const float* w_in;
@@ -80,8 +84,12 @@ struct Params {
   long long timeout_ns;
 };
 
-// Host side: fill geometry / shared-memory plan; returns B2Q_OK or an error.
+// Host side: geometry / shared-memory plan and tensor maps; launch.
 int plan(Params& p);
+int set_maps_qmv(Params& p, const uint32_t* w, const uint16_t* s, const uint16_t* b);
+int set_maps_gu(Params& p, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg, const uint32_t* wu,
+                const uint16_t* su, const uint16_t* bu);
+int set_maps_down(Params& p, const uint32_t* wd, const uint16_t* sd, const uint16_t* bd);
 int launch(const Params& p, void* stream, bool cooperative);
 
 int launch_router_logits(const uint16_t* x, const uint16_t* wr, float* logits, int T, int E, int H,

@@ -170,7 +170,9 @@ def test_moe_prefill_small(cuda, b2q_mod, oracle):
     ridx, rw = oracle.route(_np(b2q_mod.router_logits(x, wr)), k)
     assert np.array_equal(_np(idx), ridx)
     ref = oracle.moe_experts_prefill(_np(x), ridx, rw, _layer_np(L), k)
-    assert rel_l2(_bf(_np(out)), _bf(ref)) < TIGHT
+    # the prefill reference rounds dequantized weights to bf16 before the
+    # product (tile-loader arithmetic); the parity bound is the spec's
+    assert rel_l2(_bf(_np(out)), _bf(ref)) < REL_L2
     assert lg.shape == (T, E)
 
 
