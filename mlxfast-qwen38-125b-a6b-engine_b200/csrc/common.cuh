@@ -6,6 +6,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -76,6 +77,20 @@ __device__ __forceinline__ void decode_word(uint32_t W, uint32_t& p0, uint32_t& 
   p3 = lop_or_and(W >> 12, m, mg);
 }
 
+// fp16 variant: OR-ing into fp16 1024.0 (0x6400; unit spacing on [1024, 2048))
+// holds a nibble in bits 0-3 as 1024 + q and one in bits 4-7 as 1024 + 16 q,
+// so one shift serves the four pairs (e0,e4) (16e1,16e5) (e2,e6) (16e3,16e7);
+// the activation side carries the matching 1/16 on the odd slots.
+__device__ __forceinline__ void decode_word_h(uint32_t W, uint32_t& p0, uint32_t& p1, uint32_t& p2,
+                                              uint32_t& p3) {
+  const uint32_t mg = 0x64006400u;
+  p0 = lop_or_and(W, 0x000F000Fu, mg);
+  p1 = lop_or_and(W, 0x00F000F0u, mg);
+  const uint32_t t = W >> 8;
+  p2 = lop_or_and(t, 0x000F000Fu, mg);
+  p3 = lop_or_and(t, 0x00F000F0u, mg);
+}
+
 // x chunk of 8 bf16 (x0..x7 as 4 packed pairs) -> (x0,x4) (x1,x5) (x2,x6) (x3,x7)
 __device__ __forceinline__ uint4 perm_x8(uint4 v) {
   uint4 o;
@@ -88,13 +103,43 @@ __device__ __forceinline__ uint4 perm_x8(uint4 v) {
 
 // ---- legacy MMA (decode streaming kernels) -------------------------------------
 // D(16x8, f32) += A(16x16, bf16, row) * B(16x8, bf16, col).
+// Not volatile: the MMA is a pure function of its registers, so the compiler
+// may interleave independent accumulator chains.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                                uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D(16x8, f32) = A * B (accumulator starts at zero).
+__device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                    uint32_t a3, uint32_t b0, uint32_t b1) {
+  const float z = 0.0f;
+  asm(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+// fp16 operands, fp32 accumulation: D += A * B, and D = A * B.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_f16_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                   uint32_t a3, uint32_t b0, uint32_t b1) {
+  const float z = 0.0f;
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
 }
 
 // ---- shared memory / mbarrier / bulk copy ----------------------------------------

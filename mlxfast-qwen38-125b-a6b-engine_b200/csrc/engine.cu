@@ -179,32 +179,100 @@ __device__ __forceinline__ LoadDesc describe(const Params& p, const Sched& s, in
 }
 
 // ---------------------------------------------------------------------------
-// activation staging: bf16 rows -> permuted chunks + fp32 group sums
+// activation staging: bf16 rows -> scaled, permuted fp16 chunks + group sums
 // ---------------------------------------------------------------------------
-// column c of `dst` (stride XS bytes) receives row src_rows[c]; sums[c * G + g].
-__device__ void stage_columns(uint8_t* dst, float* sums, int XS, const uint16_t* const* src_rows, int ncols,
+// The MMA B operand is fp16. Column c is scaled by S_c = 2^e_c chosen so that
+// max|x| * S_c lies in [1024, 2048): every bf16 value converts to fp16
+// exactly (bf16 has 8 significant bits, fp16 11) without overflow, and only
+// values below 2^-24 of the column's maximum lose bits. The 16-byte chunk of
+// values x0..x7 is stored as fp16 pairs
+//   (x0 S, x4 S) (x1 S/16, x5 S/16) (x2 S, x6 S) (x3 S/16, x7 S/16)
+// to meet the decoded weight pairs (1024+q0, 1024+q4) (1024+16q1, 1024+16q5)
+// (1024+q2, 1024+q6) (1024+16q3, 1024+16q7). Per group g:
+//   xs[c][g]   = sum of x S
+//   xoff[c][g] = 1024 * sum_even x S + 64 * sum_odd x S  (the offset the decode adds)
+// and inv[c] = 1 / S_c. Region layout: xs [cap][G], xoff [cap][G], inv [MAX_COLS],
+// colmax [MAX_COLS] (scratch).
+__device__ __forceinline__ float* cols_xs(float* sums, int G, int col) { return sums + (size_t)col * G; }
+__device__ __forceinline__ float* cols_xo(float* sums, int cap, int G, int col) {
+  return sums + (size_t)(cap + col) * G;
+}
+__device__ __forceinline__ float* cols_inv(float* sums, int cap, int G) { return sums + (size_t)2 * cap * G; }
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ void stage_columns(uint8_t* dst, float* sums, int cap, int XS, const uint16_t* const* src_rows, int ncols,
                               int K, int gs, bool coherent) {
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   const int nch = K / 8;
+  const int G = K / gs;
+  float* inv = cols_inv(sums, cap, G);
+  unsigned* colmax = reinterpret_cast<unsigned*>(inv + MAX_COLS);
+  if (tid < MAX_COLS) colmax[tid] = 0u;
+  named_bar_sync(1, NCT);
+  // pass 1: max |x| per column (non-negative floats order like their bits)
+  for (int q0 = 0; q0 < ncols * nch; q0 += NCT) {
+    const int q = q0 + tid;
+    unsigned m = 0u;
+    int col = q0 / nch;  // warp-uniform when a warp stays inside one column
+    if (q < ncols * nch) {
+      col = q / nch;
+      const int ch = q % nch;
+      const uint4* src = reinterpret_cast<const uint4*>(src_rows[col] + (size_t)ch * 8);
+      const uint4 v = coherent ? __ldcg(src) : __ldg(src);
+      m = max(max(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), max(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
+      m = max(m & 0xffffu, m >> 16) << 16;  // largest |bf16| of the chunk as float bits
+      if (m > 0x7f800000u) m = 0x7f800000u;  // NaN never sets the scale
+      atomicMax(&colmax[col], m);
+    }
+  }
+  named_bar_sync(1, NCT);
+  if (tid < ncols) {
+    const float mx = __uint_as_float(colmax[tid]);
+    int e = 0;
+    if (mx > 0.0f && mx < INFINITY) {
+      int E;
+      frexpf(mx, &E);  // mx = m * 2^E, m in [0.5, 1)
+      e = 11 - E;      // mx * 2^e in [1024, 2048)
+    }
+    inv[tid] = ldexpf(1.0f, -e);
+    colmax[tid] = (unsigned)(e + 1000);  // the exponent for pass 2
+  }
+  named_bar_sync(1, NCT);
+  // pass 2: scaled fp16 pairs
   for (int q = tid; q < ncols * nch; q += NCT) {
     const int col = q / nch, ch = q % nch;
     const uint4* src = reinterpret_cast<const uint4*>(src_rows[col] + (size_t)ch * 8);
-    uint4 v = coherent ? __ldcg(src) : __ldg(src);
-    *reinterpret_cast<uint4*>(dst + (size_t)col * XS + (size_t)ch * 16) = perm_x8(v);
+    const uint4 v = coherent ? __ldcg(src) : __ldg(src);
+    const int e = (int)colmax[col] - 1000;
+    const float S = ldexpf(1.0f, e), S16 = ldexpf(1.0f, e - 4);
+    uint4 o;
+    o.x = pack_h2(lo_bf(v.x) * S, lo_bf(v.z) * S);      // (x0, x4)
+    o.y = pack_h2(hi_bf(v.x) * S16, hi_bf(v.z) * S16);  // (x1/16, x5/16)
+    o.z = pack_h2(lo_bf(v.y) * S, lo_bf(v.w) * S);      // (x2, x6)
+    o.w = pack_h2(hi_bf(v.y) * S16, hi_bf(v.w) * S16);  // (x3/16, x7/16)
+    *reinterpret_cast<uint4*>(dst + (size_t)col * XS + (size_t)ch * 16) = o;
   }
   named_bar_sync(1, NCT);
-  const int G = K / gs;
+  // pass 3: group sums of the scaled values (k order within a chunk)
   for (int q = tid; q < ncols * G; q += NCT) {
     const int col = q / G, g = q % G;
     const uint8_t* base = dst + (size_t)col * XS + (size_t)g * (gs / 8) * 16;
-    float acc = 0.0f;
+    float se = 0.0f, so = 0.0f;
     for (int ch = 0; ch < gs / 8; ++ch) {
       const uint4 v = *reinterpret_cast<const uint4*>(base + ch * 16);
-      // permuted (x0,x4)(x1,x5)(x2,x6)(x3,x7): sum in k order x0..x7
-      acc += ((((((lo_bf(v.x) + lo_bf(v.y)) + lo_bf(v.z)) + lo_bf(v.w)) + hi_bf(v.x)) + hi_bf(v.y)) + hi_bf(v.z)) +
-             hi_bf(v.w);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+      se += ((a.x + c.x) + a.y) + c.y;              // x0 + x2 + x4 + x6
+      so += ((b.x + d.x) + b.y) + d.y;              // (x1 + x3 + x5 + x7) / 16
     }
-    sums[(size_t)col * G + g] = acc;
+    cols_xs(sums, G, col)[g] = se + 16.0f * so;
+    cols_xo(sums, cap, G, col)[g] = 1024.0f * se + 1024.0f * so;  // 64 * (16 * so)
   }
   named_bar_sync(1, NCT);
 }
@@ -226,85 +294,105 @@ __device__ void stage_columns(uint8_t* dst, float* sums, int XS, const uint16_t*
 //         (P slot, column 2c) and element 3 (Q slot, column 2c + 1).
 template <int WPT, int KIND>
 __device__ __forceinline__ void consume_pass(const uint8_t* __restrict__ st, const Geo& g, int pc_lo, int pc_hi,
-                                             int gabs0, const uint8_t* __restrict__ xcol,
+                                             int g_lo, int g_hi, int gabs0, const uint8_t* __restrict__ xcol,
                                              const float* __restrict__ xs0, const float* __restrict__ xs1,
+                                             const float* __restrict__ xo0, const float* __restrict__ xo1,
                                              bool on, float (&acc)[4]) {
   constexpr int GPC = 8 / WPT;  // groups per 128-byte piece
   const int lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
-  const uint8_t* wP = st + r * 128 + c * 4;
-  const uint8_t* wQ = wP + g.blkw;
-  const uint8_t* mP = st + 2 * g.blkw;  // sP; bP at +blkm
-  const uint8_t* mQ = mP + 2 * g.blkm;  // sQ; bQ at +blkm
-  const uint8_t* xl = xcol + c * 16;
-  int sw[8];
+  const int blkw = g.blkw, blkm = g.blkm, mswz = g.mswz, mrow = g.mrow;
+  const uint8_t* mP = st + 2 * blkw;  // sP; bP at +blkm
+  const uint8_t* mQ = mP + 2 * blkm;  // sQ; bQ at +blkm
+  // per-unit pointers of this lane's word (swizzle resolved once)
+  const uint8_t* wu[8];
 #pragma unroll
-  for (int u = 0; u < 8; ++u) sw[u] = (u ^ r) << 4;
+  for (int u = 0; u < 8; ++u) wu[u] = st + r * 128 + (((u ^ r)) << 4) + c * 4 + pc_lo * 1024;
+  const uint8_t* px = xcol + c * 16 + pc_lo * 512;
+  // byte offset of the 16-bit scale / bias of group gl (within the pass) for row r
+  auto meta_off = [&](int gl) -> int {
+    if (mswz) {
+      const int gg = gl & 63;
+      return (gl >> 6) * 1024 + r * 128 + ((((gg >> 3) ^ r)) << 4) + (gg & 7) * 2;
+    }
+    return r * mrow + gl * 2;
+  };
+  // one word-pair step of group gi of the current piece into D
+  auto step = [&](int u, bool first, float (&d)[4]) {
+    const uint32_t W0 = lds32(wu[u]);
+    const uint32_t W8 = lds32(wu[u] + blkw);
+    const uint4 xv = lds128(px + u * 64);
+    uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
+    decode_word_h(W0, p0, p1, p2, p3);
+    decode_word_h(W8, q0, q1, q2, q3);
+    if (first)
+      mma_f16_16816_zero(d, p0, q0, p1, q1, xv.x, xv.y);
+    else
+      mma_f16_16816(d, p0, q0, p1, q1, xv.x, xv.y);
+    mma_f16_16816(d, p2, q2, p3, q3, xv.z, xv.w);
+  };
   for (int pc = pc_lo; pc < pc_hi; ++pc) {
-    const uint8_t* pw = wP + pc * 1024;
-    const uint8_t* pq = wQ + pc * 1024;
-    const uint8_t* px = xl + pc * 512;
+    if (KIND == 0) {
+      // Every column holds the same activation, so the four lanes of a quad
+      // hold identical D: lane c finishes group c of each batch of NB groups.
+      constexpr int NB = GPC < 4 ? GPC : 4;
 #pragma unroll
-    for (int pp = 0; pp < GPC / 2; ++pp) {
-      float D[2][4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float dA[4] = {0.f, 0.f, 0.f, 0.f};
-        float dB[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int b0 = 0; b0 < GPC; b0 += NB) {
+        float D[NB][4];
 #pragma unroll
         for (int j = 0; j < WPT; ++j) {
-          const int u = (2 * pp + h) * WPT + j;  // 16-byte unit within the piece
-          const uint32_t W0 = lds32(pw + sw[u]);
-          const uint32_t W8 = lds32(pq + sw[u]);
-          const uint4 xv = lds128(px + u * 64);
-          uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
-          decode_word(W0, p0, p1, p2, p3);
-          decode_word(W8, q0, q1, q2, q3);
-          mma_bf16_16816(dA, p0, q0, p1, q1, xv.x, xv.y);
-          mma_bf16_16816(dB, p2, q2, p3, q3, xv.z, xv.w);
+#pragma unroll
+          for (int gi = 0; gi < NB; ++gi) step((b0 + gi) * WPT + j, j == 0, D[gi]);
         }
+        float e0 = D[0][0], e2 = D[0][2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) D[h][i] = dA[i] + dB[i];
+        for (int gi = 1; gi < NB; ++gi) {
+          e0 = (c == gi) ? D[gi][0] : e0;
+          e2 = (c == gi) ? D[gi][2] : e2;
+        }
+        const int gl = pc * GPC + b0 + (c < NB ? c : NB - 1);
+        const int mo = meta_off(gl);
+        const float sP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mo));
+        const float bP = bf2f(*reinterpret_cast<const uint16_t*>(mP + blkm + mo));
+        const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(mQ + mo));
+        const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(mQ + blkm + mo));
+        const float xa = xs0[gabs0 + gl], xoa = xo0[gabs0 + gl];
+        if (c < NB) {
+          acc[0] = fmaf(sP, e0 - xoa, fmaf(bP, xa, acc[0]));
+          acc[2] = fmaf(sQ, e2 - xoa, fmaf(bQ, xa, acc[2]));
+        }
       }
-      // scales / biases of groups (g0, g0 + 1) for rows r and r + 8: one 32-bit word each
-      const int g0 = pc * GPC + 2 * pp;
-      int moff;
-      if (g.mswz) {
-        const int gg = g0 & 63;
-        moff = (g0 >> 6) * 1024 + r * 128 + ((((gg >> 3) ^ r)) << 4) + (gg & 7) * 2;
-      } else {
-        moff = r * g.mrow + g0 * 2;
-      }
-      const uint32_t sPv = lds32(mP + moff), bPv = lds32(mP + g.blkm + moff);
-      const uint32_t sQv = lds32(mQ + moff), bQv = lds32(mQ + g.blkm + moff);
-      const float2 x0 = *reinterpret_cast<const float2*>(xs0 + gabs0 + g0);
+    } else {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float sP = h ? hi_bf(sPv) : lo_bf(sPv);
-        const float sQ = h ? hi_bf(sQv) : lo_bf(sQv);
-        const float bP = fmaf(-128.0f, sP, h ? hi_bf(bPv) : lo_bf(bPv));
-        const float bQ = fmaf(-128.0f, sQ, h ? hi_bf(bQv) : lo_bf(bQv));
-        const float xa = h ? x0.y : x0.x;
-        if (KIND == 0) {
-          acc[0] = fmaf(bP, xa, fmaf(sP, D[h][0], acc[0]));
-          acc[2] = fmaf(bQ, xa, fmaf(sQ, D[h][2], acc[2]));
-        } else if (KIND == 1) {
-          const float2 x1 = *reinterpret_cast<const float2*>(xs1 + gabs0 + g0);
-          const float xb = h ? x1.y : x1.x;
-          acc[0] = fmaf(bP, xa, fmaf(sP, D[h][0], acc[0]));
-          acc[1] = fmaf(bP, xb, fmaf(sP, D[h][1], acc[1]));
-          acc[2] = fmaf(bQ, xa, fmaf(sQ, D[h][2], acc[2]));
-          acc[3] = fmaf(bQ, xb, fmaf(sQ, D[h][3], acc[3]));
+      for (int gi = 0; gi < GPC; ++gi) {
+        const int gl = pc * GPC + gi;
+        if (gl < g_lo || gl >= g_hi) continue;
+        float D[4];
+#pragma unroll
+        for (int j = 0; j < WPT; ++j) step(gi * WPT + j, j == 0, D);
+        const int mo = meta_off(gl);
+        const float sP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mo));
+        const float bP = bf2f(*reinterpret_cast<const uint16_t*>(mP + blkm + mo));
+        const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(mQ + mo));
+        const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(mQ + blkm + mo));
+        const float xa = xs0[gabs0 + gl], xb = xs1[gabs0 + gl];
+        const float xoa = xo0[gabs0 + gl], xob = xo1[gabs0 + gl];
+        if (KIND == 1) {
+          acc[0] = fmaf(sP, D[0] - xoa, fmaf(bP, xa, acc[0]));
+          acc[1] = fmaf(sP, D[1] - xob, fmaf(bP, xb, acc[1]));
+          acc[2] = fmaf(sQ, D[2] - xoa, fmaf(bQ, xa, acc[2]));
+          acc[3] = fmaf(sQ, D[3] - xob, fmaf(bQ, xb, acc[3]));
         } else {
-          const float2 x1 = *reinterpret_cast<const float2*>(xs1 + gabs0 + g0);
-          const float xb = h ? x1.y : x1.x;
-          const float e0 = fmaf(bP, xa, sP * D[h][0]);
-          const float e3 = fmaf(bQ, xb, sQ * D[h][3]);
+          const float e0 = fmaf(sP, D[0] - xoa, bP * xa);
+          const float e3 = fmaf(sQ, D[3] - xob, bQ * xb);
           acc[0] += on ? e0 : 0.0f;
           acc[3] += on ? e3 : 0.0f;
         }
       }
     }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) wu[u] += 1024;
+    px += 512;
   }
 }
 
@@ -371,7 +459,11 @@ __device__ void warp_route(const float* lr, int E, int k, bool coherent, uint32_
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int WPT>
+// KMODE: MODE_QMV (one token), MODE_GU, MODE_DOWN, MODE_FUSED, or KMODE_QMVM
+// (qmv with 2..8 tokens); one instance per mode keeps each kernel's code small.
+constexpr int KMODE_QMVM = 4;
+
+template <int WPT, int KMODE>
 __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // swizzled TMA destinations need 1024-byte alignment
@@ -384,6 +476,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
   uint32_t* sidx = reinterpret_cast<uint32_t*>(smem + p.off_misc + 2 * NSTAGE * 8 + 16);
   float* sw = reinterpret_cast<float*>(sidx + MAX_COLS);
   float* rsum = sw + MAX_COLS;  // [NC_WARPS] router partials
+  float* fin = rsum + NC_WARPS;   // [8][8] down finisher products
   int* err = p.err;
   const Sched sch = make_sched(p);
   const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
@@ -501,7 +594,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
       // stage x (token 0) while the other CTAs finish their router rows
       {
         const uint16_t* rows[1] = {p.x};
-        stage_columns(xbuf, xsum, p.g1.XS, rows, 1, p.H, p.gs, false);
+        stage_columns(xbuf, xsum, p.xcols, p.g1.XS, rows, 1, p.H, p.gs, false);
       }
       if (tid == 0) {
         if (!wait_counter_geq(&p.counters[0], (unsigned)p.E, deadline, abort_flag)) {
@@ -530,7 +623,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
     } else if (p.mode == MODE_GU) {
       const uint16_t* rows[MAX_COLS];
       for (int t = 0; t < p.S; ++t) rows[t] = p.x + (size_t)t * p.H;
-      stage_columns(xbuf, xsum, p.g1.XS, rows, p.S, p.H, p.gs, false);
+      stage_columns(xbuf, xsum, p.xcols, p.g1.XS, rows, p.S, p.H, p.gs, false);
     }
 
     int L = 0, buf = 0;
@@ -541,6 +634,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
       const uint8_t* xcol;
       const float* xs0;
       const float* xs1;
+      const float* xo0;
+      const float* xo1;
+      float inv0, inv1;  // 1 / S of the columns of acc[0|2] and acc[1|3]
       int item = 0, zslot = 0, tok = 0, rb = 0, hb = 0;
       bool item_ok = true;
       if (p.mode == MODE_QMV) {
@@ -554,13 +650,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           if (item_ok) {
             const uint16_t* rows[MAX_COLS];
             for (int m = 0; m < p.M; ++m) rows[m] = p.x + ((size_t)xi * p.M + m) * g.K;
-            stage_columns(xbuf, xsum, g.XS, rows, p.M, g.K, p.gs, false);
+            stage_columns(xbuf, xsum, p.xcols, g.XS, rows, p.M, g.K, p.gs, false);
           }
           cur_item = xkey;
         }
         xcol = xbuf + (size_t)((r < p.M) ? r : 0) * g.XS;
-        xs0 = xsum + (size_t)min(2 * c, p.M - 1) * g.G;
-        xs1 = xsum + (size_t)min(2 * c + 1, p.M - 1) * g.G;
+        const int c0 = min(2 * c, p.M - 1), c1 = min(2 * c + 1, p.M - 1);
+        xs0 = cols_xs(xsum, g.G, c0);
+        xs1 = cols_xs(xsum, g.G, c1);
+        xo0 = cols_xo(xsum, p.xcols, g.G, c0);
+        xo1 = cols_xo(xsum, p.xcols, g.G, c1);
+        inv0 = cols_inv(xsum, p.xcols, g.G)[c0];
+        inv1 = cols_inv(xsum, p.xcols, g.G)[c1];
       } else if (!down) {
         zslot = u / sch.FB;
         rb = u % sch.FB;
@@ -572,7 +673,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           tok = 0;
         }
         xcol = xbuf + (size_t)tok * g.XS;
-        xs0 = xs1 = xsum + (size_t)tok * g.G;
+        xs0 = xs1 = cols_xs(xsum, g.G, tok);
+        xo0 = xo1 = cols_xo(xsum, p.xcols, g.G, tok);
+        inv0 = inv1 = cols_inv(xsum, p.xcols, g.G)[tok];
       } else {
         const int ud = (p.mode == MODE_FUSED) ? u - sch.U_gu : u;
         tok = ud / sch.HB;
@@ -590,18 +693,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
             named_bar_sync(1, NCT);
             const uint16_t* rows[MAX_COLS];
             for (int j = 0; j < p.k; ++j) rows[j] = p.ws_act + (size_t)j * p.F;
-            stage_columns(abuf, asum, g.XS, rows, p.k, p.F, p.gs, true);
+            stage_columns(abuf, asum, p.k, g.XS, rows, p.k, p.F, p.gs, true);
             act_ready = true;
           }
         } else if (tok != cur_tok) {
           const uint16_t* rows[MAX_COLS];
           for (int j = 0; j < p.k; ++j) rows[j] = p.act_in + ((size_t)tok * p.k + j) * p.F;
-          stage_columns(abuf, asum, g.XS, rows, p.k, p.F, p.gs, false);
+          stage_columns(abuf, asum, p.k, g.XS, rows, p.k, p.F, p.gs, false);
           cur_tok = tok;
         }
         xcol = abuf + (size_t)((r < p.k) ? r : 0) * g.XS;
-        xs0 = asum + (size_t)min(2 * c, p.k - 1) * g.G;
-        xs1 = asum + (size_t)min(2 * c + 1, p.k - 1) * g.G;
+        const int c0 = min(2 * c, p.k - 1), c1 = min(2 * c + 1, p.k - 1);
+        xs0 = cols_xs(asum, g.G, c0);
+        xs1 = cols_xs(asum, g.G, c1);
+        xo0 = cols_xo(asum, p.k, g.G, c0);
+        xo1 = cols_xo(asum, p.k, g.G, c1);
+        inv0 = cols_inv(asum, p.k, g.G)[c0];
+        inv1 = cols_inv(asum, p.k, g.G)[c1];
       }
 
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -618,22 +726,52 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           const int pair = down ? pass / g.nkc : 0;
           const int kcw = min(g.KC, g.K - kc * g.KC);
           const int npieces = kcw / 256;  // 128-byte pieces of each row in this chunk
-          const int plo = (warp * npieces) / NC_WARPS, phi = ((warp + 1) * npieces) / NC_WARPS;
+          // single-column passes split by whole pieces; the others by groups
+          // (pieces [plo, phi) cover groups [glo, ghi), partial at the ends)
+          int plo, phi, glo = 0, ghi = 1 << 30;
+          if (down || KMODE == KMODE_QMVM) {
+            const int ng = kcw / p.gs, gpc = 8 / WPT;
+            glo = (warp * ng) / NC_WARPS;
+            ghi = ((warp + 1) * ng) / NC_WARPS;
+            plo = glo / gpc;
+            phi = (ghi + gpc - 1) / gpc;
+          } else {
+            plo = (warp * npieces) / NC_WARPS;
+            phi = ((warp + 1) * npieces) / NC_WARPS;
+          }
           const uint8_t* st = stages + (size_t)si * p.stage_bytes;
           const uint8_t* xc = xcol + (size_t)kc * (g.KC / 8) * 16;
           const int gabs0 = kc * g.GC;  // blocks keep the full-pass box layout, also for a shorter last chunk
-          if (down) {
-            consume_pass<WPT, 2>(st, g, plo, phi, gabs0, xc, xs0, xs1, c == pair, acc);
-          } else if (p.mode == MODE_QMV && p.M > 1) {
-            consume_pass<WPT, 1>(st, g, plo, phi, gabs0, xc, xs0, xs1, true, acc);
+          if constexpr (KMODE == MODE_DOWN) {
+            consume_pass<WPT, 2>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, c == pair, acc);
+          } else if constexpr (KMODE == MODE_FUSED) {
+            if (down)
+              consume_pass<WPT, 2>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, c == pair, acc);
+            else
+              consume_pass<WPT, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, acc);
+          } else if constexpr (KMODE == KMODE_QMVM) {
+            consume_pass<WPT, 1>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, acc);
           } else {
-            consume_pass<WPT, 0>(st, g, plo, phi, gabs0, xc, xs0, xs1, true, acc);
+            consume_pass<WPT, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, acc);
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[si]);
       }
       // ---- unit epilogue: fixed-order reduction over the warps ----
+      // undo the activation scaling (a power of two: exact)
+      acc[0] *= inv0;
+      acc[1] *= inv1;
+      acc[2] *= inv0;
+      acc[3] *= inv1;
+      // single-column units: the four lanes of a quad hold different groups
+      const bool quad_groups = (KMODE == MODE_QMV || KMODE == MODE_GU || (KMODE == MODE_FUSED && !down));
+      if (quad_groups) {
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
+        acc[2] += __shfl_xor_sync(0xffffffffu, acc[2], 1);
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 2);
+        acc[2] += __shfl_xor_sync(0xffffffffu, acc[2], 2);
+      }
       float* rw = red + ((size_t)buf * NC_WARPS + warp) * 128;
       rw[r * 8 + 2 * c] = acc[0];
       rw[r * 8 + 2 * c + 1] = acc[1];
@@ -641,56 +779,77 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
       rw[(r + 8) * 8 + 2 * c + 1] = acc[3];
       named_bar_sync(1, NCT);
       const float* rr = red + (size_t)buf * NC_WARPS * 128;
-      if (p.mode == MODE_QMV) {
-        if (tid < 16 * p.M) {
-          const int i = tid & 15, n = tid >> 4;
+      // Sum of the NC_WARPS partials of element (i, n) by NC_WARPS consecutive
+      // lanes (xor tree, fixed order); every lane of the group gets the total.
+      constexpr int PW = NC_WARPS;
+      static_assert(PW == 8 || PW == 16, "finisher lane groups");
+      auto red16 = [&](int i, int n, bool valid) -> float {
+        float v = valid ? rr[(tid & (PW - 1)) * 128 + i * 8 + n] : 0.0f;
+#pragma unroll
+        for (int off = PW / 2; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        return v;
+      };
+      if constexpr (KMODE == MODE_QMV || KMODE == KMODE_QMVM) {
+        const int n_out = 16 * p.M;
+        for (int ob = 0; ob < n_out; ob += NCT / PW) {
+          const int o = ob + tid / PW;
+          const bool valid = o < n_out;
+          const int i = o & 15, n = o >> 4;
+          const float v = red16(i, valid ? n : 0, valid);
           const int row = rb * 16 + i;
-          if (row < p.N) {
-            float v = 0.0f;
-            for (int w = 0; w < NC_WARPS; ++w) v += rr[w * 128 + i * 8 + n];
+          if ((tid & (PW - 1)) == 0 && valid && row < p.N)
             p.y[((size_t)item * p.M + n) * p.N + row] = (item_ok && !*abort_flag) ? f2bf(v) : (uint16_t)0;
-          }
-        }
-      } else if (!down) {
-        if (tid < 8) {
-          float gv = 0.0f, uv = 0.0f;
-          for (int w = 0; w < NC_WARPS; ++w) {
-            gv += rr[w * 128 + tid * 8];
-            uv += rr[w * 128 + (tid + 8) * 8];
-          }
-          uint16_t* dst = (p.mode == MODE_FUSED) ? p.ws_act : p.act_out;
-          dst[(size_t)zslot * p.F + rb * 8 + tid] = swiglu_bf16(f2bf(gv), f2bf(uv));
-          if (p.mode == MODE_FUSED) __threadfence();
-        }
-        if (p.mode == MODE_FUSED) {
-          named_bar_sync(1, NCT);
-          if (tid == 0) {
-            __threadfence();
-            atomicAdd(&p.counters[1], 1u);
-          }
         }
       } else {
-        if (tid < 8) {
-          const float* wts = (p.mode == MODE_FUSED) ? sw : nullptr;
-          float prod[MAX_COLS];
-          for (int j = 0; j < p.k; ++j) {
-            const int i = (j & 1) ? tid + 8 : tid;
-            float v = 0.0f;
-            for (int w = 0; w < NC_WARPS; ++w) v += rr[w * 128 + i * 8 + j];
-            const float wj = wts ? wts[j] : __ldg(p.w_in + (size_t)tok * p.k + j);
-            prod[j] = b2q::rb(v) * wj;  // f32(bf16(y_j)) * w_j
+        if (!down) {
+          // output o = tid / PW: row o / 2, gate (o even) or up (o odd); the
+          // two lane groups of a row sit side by side in one warp
+          if (tid < 16 * PW) {
+            const int o = tid / PW, row = o >> 1;
+            const float v = red16((o & 1) ? row + 8 : row, 0, true);
+            const float gv = __shfl_sync(0xffffffffu, v, lane & ~PW), uv = __shfl_sync(0xffffffffu, v, lane | PW);
+            if ((tid & (2 * PW - 1)) == 0) {
+              uint16_t* dst = (KMODE == MODE_FUSED) ? p.ws_act : p.act_out;
+              dst[(size_t)zslot * p.F + rb * 8 + row] = swiglu_bf16(f2bf(gv), f2bf(uv));
+              if (KMODE == MODE_FUSED) __threadfence();
+            }
           }
-          // mlx_colsum_small_f32<K>: TY = min(8, K) chains, then folded in order
-          const int TY = p.k < 8 ? p.k : 8;
-          float t[MAX_COLS];
-          for (int y = 0; y < TY; ++y) {
-            float a = 0.0f;
-            for (int q = y; q < p.k; q += TY) a = prod[q] + a;
-            t[y] = a;
+          if (KMODE == MODE_FUSED) {
+            named_bar_sync(1, NCT);
+            if (tid == 0) {
+              __threadfence();
+              atomicAdd(&p.counters[1], 1u);
+            }
           }
-          float total = t[0];
-          for (int j = 1; j < TY; ++j) total = t[j] + total;
-          p.out[(size_t)tok * p.H + hb * 8 + tid] = f2bf(total);
+        } else {
+          // 8 rows x k slots: reduce, round to bf16, weight, then fold per row
+          const float* wts = (KMODE == MODE_FUSED) ? sw : nullptr;
+#pragma unroll
+          for (int q = 0; q < 64 / (NCT / PW); ++q) {
+            const int o = q * (NCT / PW) + tid / PW;
+            const int row = o >> 3, j = o & 7;
+            const bool valid = j < p.k;
+            const float v = red16((j & 1) ? row + 8 : row, j, valid);
+            if ((tid & (PW - 1)) == 0 && valid) {
+              const float wj = wts ? wts[j] : __ldg(p.w_in + (size_t)tok * p.k + j);
+              fin[row * 8 + j] = b2q::rb(v) * wj;  // f32(bf16(y_j)) * w_j
+            }
+          }
+          named_bar_sync(1, NCT);
+          if (tid < 8) {
+            // mlx_colsum_small_f32<K>: TY = min(8, K) chains, then folded in order
+            const float* prod = fin + tid * 8;
+            const int TY = p.k < 8 ? p.k : 8;
+            float t[MAX_COLS];
+            for (int y = 0; y < TY; ++y) {
+              float a = 0.0f;
+              for (int qq = y; qq < p.k; qq += TY) a = prod[qq] + a;
+              t[y] = a;
+            }
+            float total = t[0];
+            for (int j = 1; j < TY; ++j) total = t[j] + total;
+            p.out[(size_t)tok * p.H + hb * 8 + tid] = f2bf(total);
+          }
         }
       }
       buf ^= 1;
@@ -806,15 +965,15 @@ int plan(Params& p) {
   p.off_x = off;
   off += round_up(p.xcols * (uses_g1 ? p.g1.XS : 0), 128);
   p.off_xs = off;
-  off += round_up(p.xcols * (uses_g1 ? p.g1.G : 0) * 4 + 16, 128);
+  off += round_up((2 * p.xcols * (uses_g1 ? p.g1.G : 0) + 2 * MAX_COLS) * 4, 128);
   p.off_act = off;
   off += round_up(uses_down ? p.k * p.g2.XS : 0, 128);
   p.off_acts = off;
-  off += round_up(uses_down ? p.k * p.g2.G * 4 + 16 : 0, 128);
+  off += round_up(uses_down ? (2 * p.k * p.g2.G + 2 * MAX_COLS) * 4 : 0, 128);
   p.off_red = off;
   off += 2 * NC_WARPS * 128 * 4;
   p.off_misc = off;
-  off += 2 * NSTAGE * 8 + 16 + MAX_COLS * 8 + NC_WARPS * 4;
+  off += 2 * NSTAGE * 8 + 16 + MAX_COLS * 8 + NC_WARPS * 4 + 64 * 4;
   p.smem_bytes = round_up(off, 128) + 1024;  // + alignment slack of the 1024-byte base
   if (p.smem_bytes > di.smem_optin)
     return set_error(B2Q_EUNSUPPORTED, "engine: needs %d bytes of shared memory, device allows %d", p.smem_bytes,
@@ -846,9 +1005,9 @@ int set_maps_down(Params& p, const uint32_t* wd, const uint16_t* sd, const uint1
   return set_triplet(p, M_WD, M_SD, M_BD, wd, sd, bd, (uint64_t)p.E * p.H, p.g2);
 }
 
-template <int WPT>
+template <int WPT, int KMODE>
 static int launch_t(const Params& p, cudaStream_t stream, bool cooperative, int grid) {
-  auto kern = engine_kernel<WPT>;
+  auto kern = engine_kernel<WPT, KMODE>;
   // The shared-memory opt-in is a per-device function attribute: raise it to
   // the device maximum once instead of on every launch.
   static int opted[64] = {0};
@@ -887,11 +1046,20 @@ int launch(const Params& p, void* stream, bool cooperative) {
   if (U <= 0) return B2Q_OK;
   const int grid = (p.mode == MODE_FUSED) ? di.sm_count : std::min(U, di.sm_count);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (p.wpt) {
-    case 1: return launch_t<1>(p, s, cooperative, grid);
-    case 2: return launch_t<2>(p, s, cooperative, grid);
-    case 4: return launch_t<4>(p, s, cooperative, grid);
-    default: return set_error(B2Q_EUNSUPPORTED, "engine: group size %d", p.gs);
+  const int km = (p.mode == MODE_QMV && p.M > 1) ? KMODE_QMVM : p.mode;
+  switch (p.wpt * 8 + km) {
+#define B2Q_ENGINE_CASE(W, KM) \
+  case W * 8 + KM:             \
+    return launch_t<W, KM>(p, s, cooperative, grid);
+    B2Q_ENGINE_CASE(1, MODE_QMV) B2Q_ENGINE_CASE(1, MODE_GU) B2Q_ENGINE_CASE(1, MODE_DOWN)
+    B2Q_ENGINE_CASE(1, MODE_FUSED) B2Q_ENGINE_CASE(1, KMODE_QMVM)
+    B2Q_ENGINE_CASE(2, MODE_QMV) B2Q_ENGINE_CASE(2, MODE_GU) B2Q_ENGINE_CASE(2, MODE_DOWN)
+    B2Q_ENGINE_CASE(2, MODE_FUSED) B2Q_ENGINE_CASE(2, KMODE_QMVM)
+    B2Q_ENGINE_CASE(4, MODE_QMV) B2Q_ENGINE_CASE(4, MODE_GU) B2Q_ENGINE_CASE(4, MODE_DOWN)
+    B2Q_ENGINE_CASE(4, MODE_FUSED) B2Q_ENGINE_CASE(4, KMODE_QMVM)
+#undef B2Q_ENGINE_CASE
+    default:
+      return set_error(B2Q_EUNSUPPORTED, "engine: group size %d / mode %d", p.gs, p.mode);
   }
 }
 
