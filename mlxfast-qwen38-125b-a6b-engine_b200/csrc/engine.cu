@@ -35,6 +35,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// L2 prefetch of a tensor-map box (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
                                             uint64_t policy) {
   asm volatile(
@@ -292,107 +305,158 @@ __device__ void stage_columns(uint8_t* dst, float* sums, int cap, int XS, const 
 // KIND 1: two columns per lane (qmv M >= 2): elements 0..3, xs0 / xs1.
 // KIND 2: down pass of slot pair `pair`: lanes c == pair own element 0
 //         (P slot, column 2c) and element 3 (Q slot, column 2c + 1).
-template <int WPT, int KIND>
+// Shared per-pass lane context (plain values, so everything stays in registers).
+struct PassCtx {
+  const uint8_t* st;
+  const uint8_t* mP;  // sP; bP at +blkm
+  const uint8_t* mQ;  // sQ; bQ at +blkm
+  int blkw, blkm, mswz, mrow;
+  int r, c;
+};
+
+// byte offset of the 16-bit scale / bias of group gl (within the pass) for row r
+__device__ __forceinline__ int meta_off(const PassCtx& x, int gl) {
+  if (x.mswz) {
+    const int gg = gl & 63;
+    return (gl >> 6) * 1024 + x.r * 128 + (((gg >> 3) ^ x.r) << 4) + (gg & 7) * 2;
+  }
+  return x.r * x.mrow + gl * 2;
+}
+
+// One word step: P word at wp, Q word at wp + blkw, activation chunk xv.
+__device__ __forceinline__ void word_step(const uint8_t* wp, int blkw, const uint4 xv, bool first, float (&d)[4]) {
+  const uint32_t W0 = lds32(wp);
+  const uint32_t W8 = lds32(wp + blkw);
+  uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
+  decode_word_h(W0, p0, p1, p2, p3);
+  decode_word_h(W8, q0, q1, q2, q3);
+  if (first)
+    mma_f16_16816_zero(d, p0, q0, p1, q1, xv.x, xv.y);
+  else
+    mma_f16_16816(d, p0, q0, p1, q1, xv.x, xv.y);
+  mma_f16_16816(d, p2, q2, p3, q3, xv.z, xv.w);
+}
+
+// A single-column (KIND 0) piece: every column of B holds the same activation,
+// so the four lanes of a quad hold identical D: lane c finishes group c of
+// each batch of NB groups. `pw` points at this lane's word of unit 0 of the
+// piece before swizzling; unit u lives at pw + ((u ^ r) << 4). The activation
+// chunks come from xv (registers) when XREG, else from px (shared memory).
+template <int WPT, bool XREG>
+__device__ __forceinline__ void piece_kind0(const PassCtx& x, const uint8_t* pw, const uint8_t* px,
+                                            const uint4 (&xv)[8], int pc, int gabs0,
+                                            const float* __restrict__ xs0, const float* __restrict__ xo0,
+                                            float (&acc)[4]) {
+  constexpr int GPC = 8 / WPT;
+  constexpr int NB = GPC < 4 ? GPC : 4;
+#pragma unroll
+  for (int b0 = 0; b0 < GPC; b0 += NB) {
+    float D[NB][4];
+#pragma unroll
+    for (int j = 0; j < WPT; ++j) {
+#pragma unroll
+      for (int gi = 0; gi < NB; ++gi) {
+        const int u = (b0 + gi) * WPT + j;
+        const uint4 xu = XREG ? xv[u] : lds128(px + u * 64);
+        word_step(pw + ((u ^ x.r) << 4), x.blkw, xu, j == 0, D[gi]);
+      }
+    }
+    float e0 = D[0][0], e2 = D[0][2];
+#pragma unroll
+    for (int gi = 1; gi < NB; ++gi) {
+      e0 = (x.c == gi) ? D[gi][0] : e0;
+      e2 = (x.c == gi) ? D[gi][2] : e2;
+    }
+    const int gl = pc * GPC + b0 + (x.c < NB ? x.c : NB - 1);
+    const int mo = meta_off(x, gl);
+    const float sP = bf2f(*reinterpret_cast<const uint16_t*>(x.mP + mo));
+    const float bP = bf2f(*reinterpret_cast<const uint16_t*>(x.mP + x.blkm + mo));
+    const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(x.mQ + mo));
+    const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(x.mQ + x.blkm + mo));
+    const float xa = xs0[gabs0 + gl], xoa = xo0[gabs0 + gl];
+    if (x.c < NB) {
+      acc[0] = fmaf(sP, e0 - xoa, fmaf(bP, xa, acc[0]));
+      acc[2] = fmaf(sQ, e2 - xoa, fmaf(bQ, xa, acc[2]));
+    }
+  }
+}
+
+// One pass of MMAs over this warp's share of the pass's 128-byte row pieces.
+//
+// Stage layout: [P weights][Q weights][sP][bP][sQ][bQ]. A weight block is one
+// 1024-byte atom per 128-byte piece of the 8 rows, 16-byte unit u of row r at
+// unit position u ^ r (TMA 128-byte swizzle). Lane (r = lane/4, c = lane%4)
+// takes packed word 4*u + c of row r of P and of Q -> MMA rows r and r + 8.
+//
+// KIND 0: one activation column matters for every lane (gate|up, qmv M = 1):
+//         elements 0 (row r) and 2 (row r + 8) against column sums xs0.
+//         With XR = 2 the warp's (at most two) pieces take their activation
+//         chunks from registers (xr), loaded once per kernel.
+// KIND 1: two columns per lane (qmv M >= 2): elements 0..3, xs0 / xs1.
+// KIND 2: down pass of slot pair `pair`: lanes c == pair own element 0
+//         (P slot, column 2c) and element 3 (Q slot, column 2c + 1).
+template <int WPT, int KIND, int XR>
 __device__ __forceinline__ void consume_pass(const uint8_t* __restrict__ st, const Geo& g, int pc_lo, int pc_hi,
                                              int g_lo, int g_hi, int gabs0, const uint8_t* __restrict__ xcol,
                                              const float* __restrict__ xs0, const float* __restrict__ xs1,
                                              const float* __restrict__ xo0, const float* __restrict__ xo1,
-                                             bool on, float (&acc)[4]) {
+                                             bool on, const uint4 (&xr)[2][8], float (&acc)[4]) {
   constexpr int GPC = 8 / WPT;  // groups per 128-byte piece
   const int lane = threadIdx.x & 31;
-  const int r = lane >> 2, c = lane & 3;
-  const int blkw = g.blkw, blkm = g.blkm, mswz = g.mswz, mrow = g.mrow;
-  const uint8_t* mP = st + 2 * blkw;  // sP; bP at +blkm
-  const uint8_t* mQ = mP + 2 * blkm;  // sQ; bQ at +blkm
-  // per-unit pointers of this lane's word (swizzle resolved once)
-  const uint8_t* wu[8];
-#pragma unroll
-  for (int u = 0; u < 8; ++u) wu[u] = st + r * 128 + (((u ^ r)) << 4) + c * 4 + pc_lo * 1024;
-  const uint8_t* px = xcol + c * 16 + pc_lo * 512;
-  // byte offset of the 16-bit scale / bias of group gl (within the pass) for row r
-  auto meta_off = [&](int gl) -> int {
-    if (mswz) {
-      const int gg = gl & 63;
-      return (gl >> 6) * 1024 + r * 128 + ((((gg >> 3) ^ r)) << 4) + (gg & 7) * 2;
-    }
-    return r * mrow + gl * 2;
-  };
-  // one word-pair step of group gi of the current piece into D
-  auto step = [&](int u, bool first, float (&d)[4]) {
-    const uint32_t W0 = lds32(wu[u]);
-    const uint32_t W8 = lds32(wu[u] + blkw);
-    const uint4 xv = lds128(px + u * 64);
-    uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
-    decode_word_h(W0, p0, p1, p2, p3);
-    decode_word_h(W8, q0, q1, q2, q3);
-    if (first)
-      mma_f16_16816_zero(d, p0, q0, p1, q1, xv.x, xv.y);
-    else
-      mma_f16_16816(d, p0, q0, p1, q1, xv.x, xv.y);
-    mma_f16_16816(d, p2, q2, p3, q3, xv.z, xv.w);
-  };
+  PassCtx x;
+  x.st = st;
+  x.blkw = g.blkw;
+  x.blkm = g.blkm;
+  x.mswz = g.mswz;
+  x.mrow = g.mrow;
+  x.r = lane >> 2;
+  x.c = lane & 3;
+  x.mP = st + 2 * x.blkw;
+  x.mQ = x.mP + 2 * x.blkm;
+  const uint8_t* wbase = st + x.r * 128 + x.c * 4;
+  const uint8_t* xbase = xcol + x.c * 16;
+  if (KIND == 0 && XR > 0) {
+    if (pc_lo < pc_hi) piece_kind0<WPT, true>(x, wbase + pc_lo * 1024, nullptr, xr[0], pc_lo, gabs0, xs0, xo0, acc);
+    if (pc_lo + 1 < pc_hi)
+      piece_kind0<WPT, true>(x, wbase + (pc_lo + 1) * 1024, nullptr, xr[1], pc_lo + 1, gabs0, xs0, xo0, acc);
+    return;
+  }
   for (int pc = pc_lo; pc < pc_hi; ++pc) {
+    const uint8_t* pw = wbase + pc * 1024;
+    const uint8_t* px = xbase + pc * 512;
     if (KIND == 0) {
-      // Every column holds the same activation, so the four lanes of a quad
-      // hold identical D: lane c finishes group c of each batch of NB groups.
-      constexpr int NB = GPC < 4 ? GPC : 4;
-#pragma unroll
-      for (int b0 = 0; b0 < GPC; b0 += NB) {
-        float D[NB][4];
-#pragma unroll
-        for (int j = 0; j < WPT; ++j) {
-#pragma unroll
-          for (int gi = 0; gi < NB; ++gi) step((b0 + gi) * WPT + j, j == 0, D[gi]);
-        }
-        float e0 = D[0][0], e2 = D[0][2];
-#pragma unroll
-        for (int gi = 1; gi < NB; ++gi) {
-          e0 = (c == gi) ? D[gi][0] : e0;
-          e2 = (c == gi) ? D[gi][2] : e2;
-        }
-        const int gl = pc * GPC + b0 + (c < NB ? c : NB - 1);
-        const int mo = meta_off(gl);
-        const float sP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mo));
-        const float bP = bf2f(*reinterpret_cast<const uint16_t*>(mP + blkm + mo));
-        const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(mQ + mo));
-        const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(mQ + blkm + mo));
-        const float xa = xs0[gabs0 + gl], xoa = xo0[gabs0 + gl];
-        if (c < NB) {
-          acc[0] = fmaf(sP, e0 - xoa, fmaf(bP, xa, acc[0]));
-          acc[2] = fmaf(sQ, e2 - xoa, fmaf(bQ, xa, acc[2]));
-        }
-      }
-    } else {
-#pragma unroll
-      for (int gi = 0; gi < GPC; ++gi) {
-        const int gl = pc * GPC + gi;
-        if (gl < g_lo || gl >= g_hi) continue;
-        float D[4];
-#pragma unroll
-        for (int j = 0; j < WPT; ++j) step(gi * WPT + j, j == 0, D);
-        const int mo = meta_off(gl);
-        const float sP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mo));
-        const float bP = bf2f(*reinterpret_cast<const uint16_t*>(mP + blkm + mo));
-        const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(mQ + mo));
-        const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(mQ + blkm + mo));
-        const float xa = xs0[gabs0 + gl], xb = xs1[gabs0 + gl];
-        const float xoa = xo0[gabs0 + gl], xob = xo1[gabs0 + gl];
-        if (KIND == 1) {
-          acc[0] = fmaf(sP, D[0] - xoa, fmaf(bP, xa, acc[0]));
-          acc[1] = fmaf(sP, D[1] - xob, fmaf(bP, xb, acc[1]));
-          acc[2] = fmaf(sQ, D[2] - xoa, fmaf(bQ, xa, acc[2]));
-          acc[3] = fmaf(sQ, D[3] - xob, fmaf(bQ, xb, acc[3]));
-        } else {
-          const float e0 = fmaf(sP, D[0] - xoa, bP * xa);
-          const float e3 = fmaf(sQ, D[3] - xob, bQ * xb);
-          acc[0] += on ? e0 : 0.0f;
-          acc[3] += on ? e3 : 0.0f;
-        }
-      }
+      piece_kind0<WPT, false>(x, pw, px, xr[0], pc, gabs0, xs0, xo0, acc);
+      continue;
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) wu[u] += 1024;
-    px += 512;
+    for (int gi = 0; gi < GPC; ++gi) {
+      const int gl = pc * GPC + gi;
+      if (gl < g_lo || gl >= g_hi) continue;
+      float D[4];
+#pragma unroll
+      for (int j = 0; j < WPT; ++j) {
+        const int u = gi * WPT + j;
+        word_step(pw + ((u ^ x.r) << 4), x.blkw, lds128(px + u * 64), j == 0, D);
+      }
+      const int mo = meta_off(x, gl);
+      const float sP = bf2f(*reinterpret_cast<const uint16_t*>(x.mP + mo));
+      const float bP = bf2f(*reinterpret_cast<const uint16_t*>(x.mP + x.blkm + mo));
+      const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(x.mQ + mo));
+      const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(x.mQ + x.blkm + mo));
+      const float xa = xs0[gabs0 + gl], xb = xs1[gabs0 + gl];
+      const float xoa = xo0[gabs0 + gl], xob = xo1[gabs0 + gl];
+      if (KIND == 1) {
+        acc[0] = fmaf(sP, D[0] - xoa, fmaf(bP, xa, acc[0]));
+        acc[1] = fmaf(sP, D[1] - xob, fmaf(bP, xb, acc[1]));
+        acc[2] = fmaf(sQ, D[2] - xoa, fmaf(bQ, xa, acc[2]));
+        acc[3] = fmaf(sQ, D[3] - xob, fmaf(bQ, xb, acc[3]));
+      } else {
+        const float e0 = fmaf(sP, D[0] - xoa, bP * xa);
+        const float e3 = fmaf(sQ, D[3] - xob, bQ * xb);
+        acc[0] += on ? e0 : 0.0f;
+        acc[3] += on ? e3 : 0.0f;
+      }
+    }
   }
 }
 
@@ -471,20 +535,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_misc);
-  uint64_t* empty = full + NSTAGE;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NSTAGE);
-  uint32_t* sidx = reinterpret_cast<uint32_t*>(smem + p.off_misc + 2 * NSTAGE * 8 + 16);
+  uint64_t* empty = full + NSTAGE_MAX;
+  uint64_t* red_full = empty + NSTAGE_MAX;    // consumers -> finisher, per ring slot
+  uint64_t* red_free = red_full + NRED;   // finisher -> consumers
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red_free + NRED);
+  uint32_t* sidx = reinterpret_cast<uint32_t*>(smem + p.off_misc + (2 * NSTAGE_MAX + 2 * NRED) * 8 + 16);
   float* sw = reinterpret_cast<float*>(sidx + MAX_COLS);
   float* rsum = sw + MAX_COLS;  // [NC_WARPS] router partials
-  float* fin = rsum + NC_WARPS;   // [8][8] down finisher products
+  float* red = reinterpret_cast<float*>(smem + p.off_red);  // [NRED][NC_WARPS][16][8] partials
   int* err = p.err;
   const Sched sch = make_sched(p);
   const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
 
   if (tid == 0) {
-    for (int i = 0; i < NSTAGE; ++i) {
+    for (int i = 0; i < p.nstage; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NC_WARPS);
+    }
+    for (int i = 0; i < NRED; ++i) {
+      mbar_init(&red_full[i], NC_WARPS);
+      mbar_init(&red_free[i], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -500,20 +570,55 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
       for (int i = 0; i < N_MAPS; ++i)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.map[i])) : "memory");
       const uint64_t pol = policy_evict_first();
+      // L2 prefetch cursor, PF_AHEAD passes ahead of the shared-memory loads:
+      // it keeps more bytes in flight than the stage ring alone can hold.
+      const int PF_AHEAD = p.nstage + 2;
+      int pf_u = blockIdx.x, pf_pass = 0, pf_np = (pf_u < sch.U) ? unit_passes(p, sch, pf_u) : 0;
+      auto prefetch_next = [&]() {
+        if (pf_u >= sch.U) return;
+        const Geo& pg = unit_is_down(p, sch, pf_u) ? p.g2 : p.g1;
+        const LoadDesc d = describe(p, sch, pf_u, pf_pass, sidx, nullptr);
+        if (d.valid) {
+          const int cw = d.kc * (pg.KC / 256);
+          tma_prefetch_3d(&p.map[d.mwP], 0, d.rowP, cw);
+          tma_prefetch_3d(&p.map[d.mwQ], 0, d.rowQ, cw);
+          if (pg.mswz) {
+            const int cm = d.kc * (pg.GC / 64);
+            tma_prefetch_3d(&p.map[d.msP], 0, d.rowP, cm);
+            tma_prefetch_3d(&p.map[d.mbP], 0, d.rowP, cm);
+            tma_prefetch_3d(&p.map[d.msQ], 0, d.rowQ, cm);
+            tma_prefetch_3d(&p.map[d.mbQ], 0, d.rowQ, cm);
+          } else {
+            const int cm = d.kc * pg.GC;
+            tma_prefetch_2d(&p.map[d.msP], cm, d.rowP);
+            tma_prefetch_2d(&p.map[d.mbP], cm, d.rowP);
+            tma_prefetch_2d(&p.map[d.msQ], cm, d.rowQ);
+            tma_prefetch_2d(&p.map[d.mbQ], cm, d.rowQ);
+          }
+        }
+        if (++pf_pass >= pf_np) {
+          pf_pass = 0;
+          pf_u += gridDim.x;
+          pf_np = (pf_u < sch.U) ? unit_passes(p, sch, pf_u) : 0;
+        }
+      };
+      for (int i = 0; i < PF_AHEAD; ++i) prefetch_next();
       int L = 0;
       bool ok = !*abort_flag;
       for (int u = blockIdx.x; ok && u < sch.U; u += gridDim.x) {
         const int np = unit_passes(p, sch, u);
         const Geo& g = unit_is_down(p, sch, u) ? p.g2 : p.g1;
         for (int pass = 0; pass < np; ++pass, ++L) {
-          const int si = L % NSTAGE;
-          if (L >= NSTAGE && !bar_wait(&empty[si], ((L / NSTAGE) - 1) & 1, deadline, abort_flag)) {
+          const int NS = p.nstage;
+          const int si = L % NS;
+          if (L >= NS && !bar_wait(&empty[si], ((L / NS) - 1) & 1, deadline, abort_flag)) {
             if (!*abort_flag) record_error(err, B2Q_ETIMEOUT);
             *abort_flag = 1;
             ok = false;
             break;
           }
           const LoadDesc d = describe(p, sch, u, pass, sidx, err);
+          prefetch_next();
           uint8_t* st = stages + (size_t)si * p.stage_bytes;
           if (!d.valid) {
             mbar_arrive_expect_tx(&full[si], 0u);
@@ -544,20 +649,120 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
       }
       // Drain: no copy may still be landing when the CTA exits.
       const uint64_t dl2 = globaltimer() + 200000000ull;
-      for (int l = max(0, L - NSTAGE); l < L; ++l) {
-        if (!bar_wait(&full[l % NSTAGE], (l / NSTAGE) & 1, dl2, nullptr)) record_error(err, B2Q_ETIMEOUT);
+      for (int l = max(0, L - p.nstage); l < L; ++l) {
+        if (!bar_wait(&full[l % p.nstage], (l / p.nstage) & 1, dl2, nullptr)) record_error(err, B2Q_ETIMEOUT);
       }
     }
     __syncwarp();
+  } else if (warp == NC_WARPS + 1) {
+    // ------------------------------- finisher -------------------------------
+    // Per unit: wait for the NC_WARPS partials, sum them in warp order (a fixed
+    // association), write the unit's outputs, release the ring slot.
+    if (fused) named_bar_sync(2, NTHREADS);
+    int ui = 0;
+    for (int u = blockIdx.x; u < sch.U; u += gridDim.x, ++ui) {
+      const int rs = ui % NRED;
+      if (!bar_wait(&red_full[rs], (ui / NRED) & 1, deadline, abort_flag)) {
+        if (!*abort_flag) record_error(err, B2Q_ETIMEOUT);
+        *abort_flag = 1;
+      }
+      const float* rr = red + (size_t)rs * NC_WARPS * 128;
+      auto wsum = [&](int i, int n) -> float {
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NC_WARPS; ++w) v += rr[w * 128 + i * 8 + n];
+        return v;
+      };
+      const bool down = unit_is_down(p, sch, u);
+      if constexpr (KMODE == MODE_QMV || KMODE == KMODE_QMVM) {
+        const int item = u / sch.RB, rb = u % sch.RB;
+        const uint32_t xi = p.lhs ? __ldg(p.lhs + item) : (uint32_t)item;
+        const uint32_t e = p.rhs ? __ldg(p.rhs + item) : (uint32_t)item;
+        const bool item_ok = xi < (uint32_t)p.n_x && e < (uint32_t)p.n_w && !*abort_flag;
+        for (int o = lane; o < 16 * p.M; o += 32) {
+          const int i = o & 15, n = o >> 4;
+          const int row = rb * 16 + i;
+          if (row < p.N) p.y[((size_t)item * p.M + n) * p.N + row] = item_ok ? f2bf(wsum(i, n)) : (uint16_t)0;
+        }
+      } else if (!down) {
+        const int zslot = u / sch.FB, rb = u % sch.FB;
+        if (lane < 8) {
+          uint16_t* dst = (KMODE == MODE_FUSED) ? p.ws_act : p.act_out;
+          dst[(size_t)zslot * p.F + rb * 8 + lane] = swiglu_bf16(f2bf(wsum(lane, 0)), f2bf(wsum(lane + 8, 0)));
+          if (KMODE == MODE_FUSED) __threadfence();
+        }
+        if (KMODE == MODE_FUSED) {
+          __syncwarp();
+          if (lane == 0) {
+            __threadfence();
+            atomicAdd(&p.counters[1], 1u);
+          }
+        }
+      } else {
+        // 8 rows x k slots: lane (row = lane / 4, q = lane % 4) owns slots 2q (P
+        // rows) and 2q + 1 (Q rows); the products meet in lane 4 * row, which
+        // folds them in slot order (mlx_colsum_small_f32<K>).
+        const int ud = (KMODE == MODE_FUSED) ? u - sch.U_gu : u;
+        const int tok = ud / sch.HB, hb = ud % sch.HB;
+        const int row = lane >> 2, q = lane & 3;
+        const int j0 = 2 * q, j1 = 2 * q + 1;
+        float pr0 = 0.0f, pr1 = 0.0f;
+        if (j0 < p.k) {
+          const float wj = (KMODE == MODE_FUSED) ? sw[j0] : __ldg(p.w_in + (size_t)tok * p.k + j0);
+          pr0 = b2q::rb(wsum(row, j0)) * wj;  // f32(bf16(y_j)) * w_j
+        }
+        if (j1 < p.k) {
+          const float wj = (KMODE == MODE_FUSED) ? sw[j1] : __ldg(p.w_in + (size_t)tok * p.k + j1);
+          pr1 = b2q::rb(wsum(row + 8, j1)) * wj;
+        }
+        float prod[MAX_COLS];
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          prod[2 * qq] = __shfl_sync(0xffffffffu, pr0, (lane & ~3) | qq);
+          prod[2 * qq + 1] = __shfl_sync(0xffffffffu, pr1, (lane & ~3) | qq);
+        }
+        if (q == 0) {
+          const int TY = p.k < 8 ? p.k : 8;
+          float t[MAX_COLS];
+#pragma unroll
+          for (int y = 0; y < MAX_COLS; ++y) t[y] = 0.0f;
+          for (int y = 0; y < TY; ++y) {
+            float a = 0.0f;
+            for (int qq = y; qq < p.k; qq += TY) a = prod[qq] + a;
+            t[y] = a;
+          }
+          float total = t[0];
+          for (int j = 1; j < TY; ++j) total = t[j] + total;
+          p.out[(size_t)tok * p.H + hb * 8 + row] = f2bf(total);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_free[rs]);
+    }
   } else {
     // ------------------------------- consumers ------------------------------
     uint8_t* xbuf = smem + p.off_x;
     float* xsum = reinterpret_cast<float*>(smem + p.off_xs);
     uint8_t* abuf = smem + p.off_act;
     float* asum = reinterpret_cast<float*>(smem + p.off_acts);
-    float* red = reinterpret_cast<float*>(smem + p.off_red);  // [2][NC_WARPS][16][8]
     const int r = lane >> 2, c = lane & 3;
     int cur_item = -1;  // QMV gather: item whose activations are staged
+    // Register-resident activation chunks (single-column units): every pass
+    // of the gate|up / qmv family has one chunk, so a warp always takes pieces
+    // [xr_lo, xr_hi) and can keep their activations for the whole kernel.
+    uint4 xr[2][8];
+    const int np1 = p.g1.KC / 256;
+    const int xr_lo = (warp * np1) / NC_WARPS, xr_hi = ((warp + 1) * np1) / NC_WARPS;
+    const bool xreg = (KMODE == MODE_FUSED || KMODE == MODE_QMV || (KMODE == MODE_GU && p.S == 1)) &&
+                      p.mode != MODE_DOWN && p.g1.nkc == 1 && (xr_hi - xr_lo) <= 2;
+    auto load_xr = [&](const uint8_t* col) {
+#pragma unroll
+      for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          xr[pl][u] = (xr_lo + pl < xr_hi) ? lds128(col + c * 16 + (xr_lo + pl) * 512 + u * 64)
+                                           : make_uint4(0u, 0u, 0u, 0u);
+    };
     int cur_tok = -1;   // DOWN: token whose slot activations are staged
     bool act_ready = false;
 
@@ -591,11 +796,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
         __threadfence();
         atomicAdd(&p.counters[0], (unsigned)rows_done);
       }
-      // stage x (token 0) while the other CTAs finish their router rows
-      {
-        const uint16_t* rows[1] = {p.x};
-        stage_columns(xbuf, xsum, p.xcols, p.g1.XS, rows, 1, p.H, p.gs, false);
-      }
       if (tid == 0) {
         if (!wait_counter_geq(&p.counters[0], (unsigned)p.E, deadline, abort_flag)) {
           record_error(err, B2Q_ETIMEOUT);
@@ -620,13 +820,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
       }
       named_bar_sync(2, NTHREADS);  // releases the producer
+      // stage x (token 0) while the first expert tiles are in flight
+      {
+        const uint16_t* rows[1] = {p.x};
+        stage_columns(xbuf, xsum, p.xcols, p.g1.XS, rows, 1, p.H, p.gs, false);
+      }
+      if (xreg) load_xr(xbuf);
     } else if (p.mode == MODE_GU) {
       const uint16_t* rows[MAX_COLS];
       for (int t = 0; t < p.S; ++t) rows[t] = p.x + (size_t)t * p.H;
       stage_columns(xbuf, xsum, p.xcols, p.g1.XS, rows, p.S, p.H, p.gs, false);
+      if (xreg) load_xr(xbuf);
     }
 
-    int L = 0, buf = 0;
+    int L = 0;
     for (int u = blockIdx.x; u < sch.U; u += gridDim.x) {
       const bool down = unit_is_down(p, sch, u);
       const Geo& g = down ? p.g2 : p.g1;
@@ -651,6 +858,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
             const uint16_t* rows[MAX_COLS];
             for (int m = 0; m < p.M; ++m) rows[m] = p.x + ((size_t)xi * p.M + m) * g.K;
             stage_columns(xbuf, xsum, p.xcols, g.XS, rows, p.M, g.K, p.gs, false);
+            if (xreg) load_xr(xbuf);
           }
           cur_item = xkey;
         }
@@ -715,8 +923,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       const int np = unit_passes(p, sch, u);
       for (int pass = 0; pass < np; ++pass, ++L) {
-        const int si = L % NSTAGE;
-        const bool ok = bar_wait(&full[si], (L / NSTAGE) & 1, deadline, abort_flag);
+        const int si = L % p.nstage;
+        const bool ok = bar_wait(&full[si], (L / p.nstage) & 1, deadline, abort_flag);
         if (!ok && !*abort_flag) {
           record_error(err, B2Q_ETIMEOUT);
           *abort_flag = 1;
@@ -743,16 +951,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           const uint8_t* xc = xcol + (size_t)kc * (g.KC / 8) * 16;
           const int gabs0 = kc * g.GC;  // blocks keep the full-pass box layout, also for a shorter last chunk
           if constexpr (KMODE == MODE_DOWN) {
-            consume_pass<WPT, 2>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, c == pair, acc);
+            consume_pass<WPT, 2, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, c == pair, xr, acc);
           } else if constexpr (KMODE == MODE_FUSED) {
             if (down)
-              consume_pass<WPT, 2>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, c == pair, acc);
+              consume_pass<WPT, 2, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, c == pair, xr, acc);
             else
-              consume_pass<WPT, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, acc);
+              {
+              if (xreg)
+                consume_pass<WPT, 0, 2>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, xr, acc);
+              else
+                consume_pass<WPT, 0, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, xr, acc);
+            }
           } else if constexpr (KMODE == KMODE_QMVM) {
-            consume_pass<WPT, 1>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, acc);
+            consume_pass<WPT, 1, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, xr, acc);
           } else {
-            consume_pass<WPT, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, acc);
+            {
+              if (xreg)
+                consume_pass<WPT, 0, 2>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, xr, acc);
+              else
+                consume_pass<WPT, 0, 0>(st, g, plo, phi, glo, ghi, gabs0, xc, xs0, xs1, xo0, xo1, true, xr, acc);
+            }
           }
         }
         __syncwarp();
@@ -772,87 +990,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
         acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 2);
         acc[2] += __shfl_xor_sync(0xffffffffu, acc[2], 2);
       }
-      float* rw = red + ((size_t)buf * NC_WARPS + warp) * 128;
+      // hand the partials to the finisher warp through the ring
+      const int ui = (u - (int)blockIdx.x) / (int)gridDim.x;  // this CTA's unit ordinal
+      const int rs = ui % NRED;
+      if (ui >= NRED && !bar_wait(&red_free[rs], ((ui / NRED) - 1) & 1, deadline, abort_flag)) {
+        if (!*abort_flag) record_error(err, B2Q_ETIMEOUT);
+        *abort_flag = 1;
+      }
+      float* rw = red + ((size_t)rs * NC_WARPS + warp) * 128;
       rw[r * 8 + 2 * c] = acc[0];
       rw[r * 8 + 2 * c + 1] = acc[1];
       rw[(r + 8) * 8 + 2 * c] = acc[2];
       rw[(r + 8) * 8 + 2 * c + 1] = acc[3];
-      named_bar_sync(1, NCT);
-      const float* rr = red + (size_t)buf * NC_WARPS * 128;
-      // Sum of the NC_WARPS partials of element (i, n) by NC_WARPS consecutive
-      // lanes (xor tree, fixed order); every lane of the group gets the total.
-      constexpr int PW = NC_WARPS;
-      static_assert(PW == 8 || PW == 16, "finisher lane groups");
-      auto red16 = [&](int i, int n, bool valid) -> float {
-        float v = valid ? rr[(tid & (PW - 1)) * 128 + i * 8 + n] : 0.0f;
-#pragma unroll
-        for (int off = PW / 2; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        return v;
-      };
-      if constexpr (KMODE == MODE_QMV || KMODE == KMODE_QMVM) {
-        const int n_out = 16 * p.M;
-        for (int ob = 0; ob < n_out; ob += NCT / PW) {
-          const int o = ob + tid / PW;
-          const bool valid = o < n_out;
-          const int i = o & 15, n = o >> 4;
-          const float v = red16(i, valid ? n : 0, valid);
-          const int row = rb * 16 + i;
-          if ((tid & (PW - 1)) == 0 && valid && row < p.N)
-            p.y[((size_t)item * p.M + n) * p.N + row] = (item_ok && !*abort_flag) ? f2bf(v) : (uint16_t)0;
-        }
-      } else {
-        if (!down) {
-          // output o = tid / PW: row o / 2, gate (o even) or up (o odd); the
-          // two lane groups of a row sit side by side in one warp
-          if (tid < 16 * PW) {
-            const int o = tid / PW, row = o >> 1;
-            const float v = red16((o & 1) ? row + 8 : row, 0, true);
-            const float gv = __shfl_sync(0xffffffffu, v, lane & ~PW), uv = __shfl_sync(0xffffffffu, v, lane | PW);
-            if ((tid & (2 * PW - 1)) == 0) {
-              uint16_t* dst = (KMODE == MODE_FUSED) ? p.ws_act : p.act_out;
-              dst[(size_t)zslot * p.F + rb * 8 + row] = swiglu_bf16(f2bf(gv), f2bf(uv));
-              if (KMODE == MODE_FUSED) __threadfence();
-            }
-          }
-          if (KMODE == MODE_FUSED) {
-            named_bar_sync(1, NCT);
-            if (tid == 0) {
-              __threadfence();
-              atomicAdd(&p.counters[1], 1u);
-            }
-          }
-        } else {
-          // 8 rows x k slots: reduce, round to bf16, weight, then fold per row
-          const float* wts = (KMODE == MODE_FUSED) ? sw : nullptr;
-#pragma unroll
-          for (int q = 0; q < 64 / (NCT / PW); ++q) {
-            const int o = q * (NCT / PW) + tid / PW;
-            const int row = o >> 3, j = o & 7;
-            const bool valid = j < p.k;
-            const float v = red16((j & 1) ? row + 8 : row, j, valid);
-            if ((tid & (PW - 1)) == 0 && valid) {
-              const float wj = wts ? wts[j] : __ldg(p.w_in + (size_t)tok * p.k + j);
-              fin[row * 8 + j] = b2q::rb(v) * wj;  // f32(bf16(y_j)) * w_j
-            }
-          }
-          named_bar_sync(1, NCT);
-          if (tid < 8) {
-            // mlx_colsum_small_f32<K>: TY = min(8, K) chains, then folded in order
-            const float* prod = fin + tid * 8;
-            const int TY = p.k < 8 ? p.k : 8;
-            float t[MAX_COLS];
-            for (int y = 0; y < TY; ++y) {
-              float a = 0.0f;
-              for (int qq = y; qq < p.k; qq += TY) a = prod[qq] + a;
-              t[y] = a;
-            }
-            float total = t[0];
-            for (int j = 1; j < TY; ++j) total = t[j] + total;
-            p.out[(size_t)tok * p.H + hb * 8 + tid] = f2bf(total);
-          }
-        }
-      }
-      buf ^= 1;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_full[rs]);
     }
   }
 
@@ -960,8 +1111,21 @@ int plan(Params& p) {
   if (uses_down) st2 = make_geo(p.g2, p.F, p.gs);
   p.stage_bytes = round_up(std::max(st1, st2), 1024);
   if (p.stage_bytes > STAGE_MAX) return set_error(B2Q_EUNSUPPORTED, "engine: stage of %d bytes", p.stage_bytes);
-  int off = NSTAGE * p.stage_bytes;
+  // shared memory besides the stage ring
   p.xcols = (p.mode == MODE_QMV) ? p.M : (p.mode == MODE_GU ? p.S : (p.mode == MODE_FUSED ? 1 : 0));
+  int fixed = 0;
+  fixed += round_up(p.xcols * (uses_g1 ? p.g1.XS : 0), 128);
+  fixed += round_up((2 * p.xcols * (uses_g1 ? p.g1.G : 0) + 2 * MAX_COLS) * 4, 128);
+  fixed += round_up(uses_down ? p.k * p.g2.XS : 0, 128);
+  fixed += round_up(uses_down ? (2 * p.k * p.g2.G + 2 * MAX_COLS) * 4 : 0, 128);
+  fixed += NRED * NC_WARPS * 128 * 4;
+  fixed += round_up((2 * NSTAGE_MAX + 2 * NRED) * 8 + 16 + MAX_COLS * 8 + NC_WARPS * 4 + 64 * 4, 128);
+  fixed += 1024;  // alignment slack of the 1024-byte base
+  p.nstage = std::min(NSTAGE_MAX, (di.smem_optin - fixed) / p.stage_bytes);
+  if (p.nstage < 2)
+    return set_error(B2Q_EUNSUPPORTED, "engine: shared memory holds only %d stages of %d bytes", p.nstage,
+                     p.stage_bytes);
+  int off = p.nstage * p.stage_bytes;
   p.off_x = off;
   off += round_up(p.xcols * (uses_g1 ? p.g1.XS : 0), 128);
   p.off_xs = off;
@@ -971,9 +1135,9 @@ int plan(Params& p) {
   p.off_acts = off;
   off += round_up(uses_down ? (2 * p.k * p.g2.G + 2 * MAX_COLS) * 4 : 0, 128);
   p.off_red = off;
-  off += 2 * NC_WARPS * 128 * 4;
+  off += NRED * NC_WARPS * 128 * 4;
   p.off_misc = off;
-  off += 2 * NSTAGE * 8 + 16 + MAX_COLS * 8 + NC_WARPS * 4 + 64 * 4;
+  off += (2 * NSTAGE_MAX + 2 * NRED) * 8 + 16 + MAX_COLS * 8 + NC_WARPS * 4 + 64 * 4;
   p.smem_bytes = round_up(off, 128) + 1024;  // + alignment slack of the 1024-byte base
   if (p.smem_bytes > di.smem_optin)
     return set_error(B2Q_EUNSUPPORTED, "engine: needs %d bytes of shared memory, device allows %d", p.smem_bytes,

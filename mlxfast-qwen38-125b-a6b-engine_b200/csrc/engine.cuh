@@ -23,8 +23,9 @@ namespace eng {
 
 constexpr int NC_WARPS = 8;
 constexpr int NCT = NC_WARPS * 32;
-constexpr int NTHREADS = NCT + 32;
-constexpr int NSTAGE = 4;
+constexpr int NTHREADS = NCT + 64;  // + producer warp + finisher warp
+constexpr int NSTAGE_MAX = 8;  // stage ring size is planned per call from free shared memory
+constexpr int NRED = 4;  // ring of per-unit partial-sum slots handed to the finisher
 constexpr int MAX_COLS = 8;
 constexpr int STAGE_MAX = 40 * 1024;
 
@@ -79,6 +80,7 @@ struct alignas(64) Params {
   Geo g1;  // QMV: K; GU / FUSED gate|up: K = H
   Geo g2;  // DOWN / FUSED down: K = F
   int stage_bytes;
+  int nstage;  // stages in the ring (2..NSTAGE_MAX)
   int off_x, off_xs, off_act, off_acts, off_red, off_misc, smem_bytes;
   int xcols;  // activation columns staged at off_x
   long long timeout_ns;
