@@ -151,6 +151,30 @@ B2Q_API int b2q_moe_decode(const uint16_t* x, const uint16_t* wr,
                    int S, int H, int E, int F, int k, int group_size, int bits,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* b2q_moe_decode for one token (S == 1) that allocates nothing and takes no
+ * workspace. No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory when they decode (device memory owned by
+ * another allocator or a fixed arena, plugins handed only their input and
+ * output buffers, code that must avoid allocating CUDA calls). Its scratch is
+ * one file-scope device array of B2Q_NOALLOC_SCRATCH_BYTES per GPU that loads
+ * the library, held until exit; shapes whose decode workspace
+ * (b2q_moe_decode_workspace_size(1, H, E, F, k)) exceeds it are refused with
+ * B2Q_EINVAL. The first call on a device resolves the array's address and
+ * zeroes it with a blocking memset: make it before any stream capture. All
+ * calls on a device share the array; each clears its header on `stream`
+ * first, so calls in stream order are independent, but calls that overlap on
+ * the GPU race. `status` (device int, may be NULL) receives the call's
+ * device-side status in stream order: 0, or B2Q_ETIMEOUT if a bounded wait
+ * ran out. Other arguments as b2q_moe_decode. */
+#define B2Q_NOALLOC_SCRATCH_BYTES 65536
+B2Q_API int b2q_moe_decode_noalloc(const uint16_t* x, const uint16_t* wr,
+                   const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                   const uint32_t* wd, const uint16_t* sd, const uint16_t* bd,
+                   uint16_t* out, uint32_t* idx, float* w, float* logits,
+                   int H, int E, int F, int k, int group_size, int bits,
+                   int* status, void* stream);
+
 /* One prefill MoE layer over T tokens: router logits, route, stable sort of the
  * T*k assignments by expert (TrackPrefillSort.swift:84-201), gate|up + SwiGLU
  * gather GEMM and down gather GEMM on the tensor cores over expert-aligned row

@@ -12,72 +12,11 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "decode_ws.hpp"
 #include "engine.cuh"
 #include "host.hpp"
 #include "misc.cuh"
 #include "prefill.cuh"
-
-namespace b2q {
-
-// Every workspace starts with this 256-byte header.
-struct WsHeader {
-  int error;             // first device-side B2Q_E* code, 0 if none
-  unsigned counters[3];  // grid counters of the fused decode kernel
-  unsigned flag;         // self-test flag (never set)
-  unsigned pad[59];
-};
-static_assert(sizeof(WsHeader) == 256, "workspace header is 256 bytes");
-
-static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
-
-static bool gs_ok(int gs) { return gs == 32 || gs == 64 || gs == 128; }
-
-static int check_bits_gs(const char* fn, int bits, int gs) {
-  if (bits != 4) return set_error(B2Q_EUNSUPPORTED, "%s: bits=%d (only 4 is implemented)", fn, bits);
-  if (!gs_ok(gs)) return set_error(B2Q_EUNSUPPORTED, "%s: group_size=%d (32, 64 or 128)", fn, gs);
-  return B2Q_OK;
-}
-
-// Streaming-engine fast path: K a multiple of 8 groups (meta rows are whole
-// 16-byte units), 16-byte aligned bases.
-static bool engine_k_ok(int K, int gs) { return K > 0 && K % (8 * gs) == 0; }
-
-struct DecodeWs {
-  WsHeader* hdr;
-  float* logits;
-  uint32_t* idx;
-  float* w;
-  uint16_t* act;
-  size_t bytes;
-};
-
-static DecodeWs decode_ws_layout(void* base, int S, int E, int F, int k) {
-  DecodeWs d{};
-  size_t off = 0;
-  char* b = static_cast<char*>(base);
-  d.hdr = reinterpret_cast<WsHeader*>(b + off);
-  off += sizeof(WsHeader);
-  d.logits = reinterpret_cast<float*>(b + off);
-  off = align256(off + sizeof(float) * (size_t)S * E);
-  d.idx = reinterpret_cast<uint32_t*>(b + off);
-  off = align256(off + sizeof(uint32_t) * (size_t)S * k);
-  d.w = reinterpret_cast<float*>(b + off);
-  off = align256(off + sizeof(float) * (size_t)S * k);
-  d.act = reinterpret_cast<uint16_t*>(b + off);
-  off = align256(off + sizeof(uint16_t) * (size_t)S * k * F);
-  d.bytes = off;
-  return d;
-}
-
-static void base_params(eng::Params& p, int mode, int gs) {
-  std::memset(&p, 0, sizeof(p));
-  p.mode = mode;
-  p.gs = gs;
-  p.wpt = gs / 32;
-  p.timeout_ns = 2000000000ll;
-}
-
-}  // namespace b2q
 
 using namespace b2q;
 
