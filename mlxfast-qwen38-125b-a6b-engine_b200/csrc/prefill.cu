@@ -17,6 +17,7 @@
 #include "host.hpp"
 #include "misc.cuh"
 #include "prefill.cuh"
+#include "qmm_tc.cuh"
 
 namespace b2q {
 
@@ -71,8 +72,11 @@ struct PrefillWs {
   uint32_t* token_rows;
   uint32_t* inverse;
   uint32_t* offsets;
-  uint16_t* g;
+  uint32_t* prefix_gu;  // tensor-core unit ranges per expert (gate|up, down)
+  uint32_t* prefix_dn;
+  uint16_t* g;   // per-slot path: gate [R, F] and up [R, F] ...
   uint16_t* u;
+  uint16_t* xs;  // ... or, tensor-core path, the sorted token rows [R, H] (same region)
   uint16_t* act;
   uint16_t* y;
   size_t bytes;
@@ -101,16 +105,29 @@ static PrefillWs prefill_ws_layout(void* base, int T, int H, int E, int F, int k
   off = a256(off + 4 * R);
   d.offsets = reinterpret_cast<uint32_t*>(b + off);
   off = a256(off + 4 * ((size_t)E + 1));
+  d.prefix_gu = reinterpret_cast<uint32_t*>(b + off);
+  off = a256(off + 4 * ((size_t)E + 1));
+  d.prefix_dn = reinterpret_cast<uint32_t*>(b + off);
+  off = a256(off + 4 * ((size_t)E + 1));
   d.g = reinterpret_cast<uint16_t*>(b + off);
-  off = a256(off + 2 * R * F);
-  d.u = reinterpret_cast<uint16_t*>(b + off);
-  off = a256(off + 2 * R * F);
+  d.u = d.g + R * F;
+  d.xs = d.g;
+  off = a256(off + 2 * std::max(2 * R * F, R * (size_t)H));
   d.act = reinterpret_cast<uint16_t*>(b + off);
   off = a256(off + 2 * R * F);
   d.y = reinterpret_cast<uint16_t*>(b + off);
   off = a256(off + 2 * R * H);
   d.bytes = off;
   return d;
+}
+
+// The tensor-core path: both products fit the tcgen05 kernel's shape rules
+// and every operand is 16-byte aligned.
+static bool prefill_tc_ok(int H, int E, int F, int gs, const void* const* ptrs, int nptr) {
+  if (E > 1024 || !tc_shape_ok(F, H, gs, TC_GLU) || !tc_shape_ok(H, F, gs, TC_PLAIN)) return false;
+  for (int i = 0; i < nptr; ++i)
+    if (!aligned16(ptrs[i])) return false;
+  return true;
 }
 
 }  // namespace b2q
@@ -190,7 +207,55 @@ int b2q_moe_prefill(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, c
   if (rc) return rc;
   rc = launch_expert_sort(ix, ws.sorted_ids, ws.token_rows, ws.inverse, ws.offsets, R, E, k, ws.err, st);
   if (rc) return rc;
-  // expert products over the sorted rows: gate, up (x rows through token_rows)
+  const void* wptrs[9] = {wg, sg, bg, wu, su, bu, wd, sd, bd};
+  if (prefill_tc_ok(H, E, F, group_size, wptrs, 9)) {
+    // tensor cores: sorted token rows -> gate|up + SwiGLU -> down, per expert
+    rc = tc_unit_tables(ws.offsets, E, tc_m_tiles(F, TC_GLU), tc_m_tiles(H, TC_PLAIN), ws.prefix_gu, ws.prefix_dn, st);
+    if (rc) return rc;
+    rc = tc_gather_rows(x, ws.token_rows, ws.xs, R, H, T, st);
+    if (rc) return rc;
+    TcParams pg{};
+    pg.E = E;
+    pg.K = H;
+    pg.Nw = F;
+    pg.gs = group_size;
+    pg.s0 = sg;
+    pg.b0 = bg;
+    pg.s1 = su;
+    pg.b1 = bu;
+    pg.offsets = ws.offsets;
+    pg.prefix = ws.prefix_gu;
+    pg.out = ws.act;
+    pg.out_ld = F;
+    pg.err = ws.err;
+    pg.timeout_ns = 2000000000ll;
+    rc = tc_setup(pg, TC_GLU, ws.xs, R, wg, wu);
+    if (rc) return rc;
+    rc = tc_launch(pg, TC_GLU, st);
+    if (rc) return rc;
+    TcParams pd{};
+    pd.E = E;
+    pd.K = F;
+    pd.Nw = H;
+    pd.gs = group_size;
+    pd.s0 = sd;
+    pd.b0 = bd;
+    pd.offsets = ws.offsets;
+    pd.prefix = ws.prefix_dn;
+    pd.out = ws.y;
+    pd.out_ld = H;
+    pd.err = ws.err;
+    pd.timeout_ns = 2000000000ll;
+    rc = tc_setup(pd, TC_PLAIN, ws.act, R, wd, nullptr);
+    if (rc) return rc;
+    rc = tc_launch(pd, TC_PLAIN, st);
+    if (rc) return rc;
+    dim3 grid((H + 255) / 256, T);
+    sorted_combine_kernel<<<grid, 256, 0, st>>>(ws.y, ws.inverse, ww, out, T, H, k);
+    B2Q_TRY_CUDA(cudaGetLastError());
+    return B2Q_OK;
+  }
+  // per-slot products through the streaming engine: gate, up (x rows through token_rows)
   rc = b2q_gather_qmm(x, wg, sg, bg, ws.token_rows, ws.sorted_ids, ws.g, R, 1, F, H, T, E, group_size, bits, 1, 1,
                       stream);
   if (rc) return rc;

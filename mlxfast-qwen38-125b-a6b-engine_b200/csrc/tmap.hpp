@@ -26,4 +26,9 @@ namespace b2q {
 int make_row_block_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_bytes,
                        bool swizzled);
 
+// Plain 2-D map over a row-major matrix of 16-bit elements: box of
+// `box_bytes` per row x `box_rows` rows, swizzle 0, 32, 64 or 128 bytes.
+int make_2d_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_bytes,
+                uint32_t box_rows, int swizzle_bytes);
+
 }  // namespace b2q

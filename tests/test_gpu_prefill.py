@@ -1,0 +1,98 @@
+"""Prefill MoE layer on the tensor cores (tcgen05 grouped GEMM) vs the oracle.
+
+Config 2 at full size (2048 tokens, H 4096, 128 experts, top-8, F 1536, g64)
+checks sampled token rows against the CPU oracle's tile-loader arithmetic;
+smaller layers check every row, other group sizes, an expert whose token
+count needs several 256-row chunks, and experts with no tokens.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import REL_L2, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _np(t):
+    from b2q.synth import to_numpy_bits
+
+    return to_numpy_bits(t)
+
+
+def _bf(a):
+    from oracle.oracle import bf16_to_f32
+
+    return bf16_to_f32(a)
+
+
+def _layer_np(L):
+    return {k: _np(v) for k, v in L.items()}
+
+
+def _check_layer(b2q_mod, oracle, x, wr, L, k, gs, rows=None, bound=REL_L2):
+    out, idx, w = b2q_mod.moe_prefill(x, wr, L, k, group_size=gs, return_routing=True)
+    lg = b2q_mod.router_logits(x, wr)
+    ridx, rw = oracle.route(_np(lg), k)
+    assert np.array_equal(_np(idx), ridx)
+    assert np.allclose(_np(w), rw, rtol=2e-6, atol=1e-7)
+    ref = oracle.moe_experts_prefill(_np(x), ridx, rw, _layer_np(L), k, group_size=gs, rows=rows)
+    got = _bf(_np(out))
+    if rows is not None:
+        got = got[np.asarray(rows)]
+    assert np.isfinite(got).all()
+    e = rel_l2(got, _bf(ref))
+    assert e < bound, f"rel L2 {e}"
+    ws = b2q_mod.ops._ws_cache[("prefill", x.device)]
+    assert ws.status() == 0
+    return idx
+
+
+def test_prefill_c2_sampled_rows(cuda, b2q_mod, oracle):
+    from b2q import synth
+
+    E, H, F, k, T = 128, 4096, 1536, 8, 2048
+    L = synth.moe_layer(E, H, F, 64, seed=50)
+    wr = synth.router_weight(E, H, seed=51)
+    x = synth.activations((T, H), seed=52)
+    rows = [0, 1, 2, 511, 777, 1024, 1500, 2047]
+    idx = _check_layer(b2q_mod, oracle, x, wr, L, k, 64, rows=rows)
+    counts = np.bincount(_np(idx).ravel(), minlength=E)
+    assert counts.sum() == T * k
+
+
+@pytest.mark.parametrize("gs", [32, 128])
+def test_prefill_group_sizes(cuda, b2q_mod, oracle, gs):
+    from b2q import synth
+
+    E, H, F, k, T = 8, 1024, 1024, 2, 64
+    L = synth.moe_layer(E, H, F, gs, seed=60)
+    wr = synth.router_weight(E, H, seed=61)
+    x = synth.activations((T, H), seed=62)
+    _check_layer(b2q_mod, oracle, x, wr, L, k, gs)
+
+
+def test_prefill_skewed_and_empty_experts(cuda, b2q_mod, oracle):
+    """A common component in x and a router row along it send every token to
+    expert 0 (600 rows: three 200-row chunks); router rows pointing away
+    from it leave experts 12..15 without tokens."""
+    import torch
+
+    from b2q import synth
+
+    E, H, F, k, T = 16, 1024, 512, 2, 600
+    L = synth.moe_layer(E, H, F, 64, seed=70)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(71)
+    v = torch.randn(H, generator=g, device="cuda")
+    v = v / v.norm()
+    x = (torch.randn((T, H), generator=g, device="cuda") + 4.0 * v).to(torch.bfloat16)
+    wr = (0.02 * torch.randn((E, H), generator=g, device="cuda")).float()
+    wr[0] += 2.0 * v
+    wr[12:] -= 2.0 * v
+    wr = wr.to(torch.bfloat16)
+    rows = list(range(0, T, 37)) + [T - 1]
+    idx = _check_layer(b2q_mod, oracle, x, wr, L, k, 64, rows=rows)
+    counts = np.bincount(_np(idx).ravel(), minlength=E)
+    assert counts[0] == T and (counts[12:] == 0).all()
