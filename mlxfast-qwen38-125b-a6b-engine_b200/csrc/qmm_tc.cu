@@ -17,17 +17,26 @@
 //
 // Mapping onto tcgen05 (weights are the M side, tokens the N side, so an
 // expert's token count only has to be rounded to 16):
-//   * a work unit is (expert, chunk of <= 256 rows of that expert, 128-row
-//     weight tile); GLU tiles stack 64 gate rows over the same 64 up rows;
-//   * a producer warp streams, per 64-wide K step, the packed weight tile
-//     (TMA, 32-byte swizzle) and the token rows (TMA, 128-byte swizzle);
-//   * eight dequant warps turn packed nibbles into bf16 (mask into bf16 128.0,
-//     subtract 128, one bf16x2 fma with scale and bias: one rounding of
-//     s*q + b) and store them to TMEM as the MMA's A operand;
-//   * one thread issues tcgen05.mma (A from TMEM, B from shared memory) into a
-//     128 x N fp32 accumulator in TMEM;
+//   * a work unit is (expert, chunk of <= 192 rows of that expert, 128-row
+//     weight tile); a GLU tile holds 64 gate rows and the same 64 up rows,
+//     16 gate rows then their 16 up rows in every 32-lane quarter;
+//   * two producer warps stream the packed weight tile (TMA, 128 bytes of
+//     every row = 4 K steps per stage, 128-byte swizzle) and, per 64-wide K
+//     step, the token rows (TMA, 128-byte swizzle);
+//   * eight dequant warps (two groups of four taking alternate K steps) turn
+//     packed nibbles into bf16 (mask into bf16 128.0, subtract 128, one bf16x2
+//     fma with scale and bias: one rounding of s*q + b) and store them to
+//     TMEM as the MMA's A operand;
+//   * one warp issues tcgen05.mma (A from TMEM, B from shared memory) into
+//     one of two 128 x N fp32 accumulators in TMEM, so the epilogue of one
+//     unit overlaps the main loop of the next. Token rows and dequantized A
+//     of a K step complete ONE operand barrier (one wait, one commit per
+//     step), and the issuing warps stay converged with one elected lane per
+//     instruction: a single divergent lane issuing MMAs next to busy dequant
+//     warps reached well under half the tensor rate;
 //   * four epilogue warps read the accumulator back (tcgen05.ld) and write
-//     bf16 outputs; GLU pairs gate and up lanes through shared memory.
+//     bf16 outputs; GLU pairs a gate lane with its up lane by one shuffle,
+//     PLAIN transposes 32x32 tiles through shared memory for 16-byte stores.
 // K order: inside every 8-element block the token rows carry the order
 // (0,4,1,5,2,6,3,7), which is the order in which the nibble decode produces
 // weight pairs; both operands use it, so the dot products are unchanged.
@@ -49,29 +58,30 @@
 namespace b2q {
 namespace qtc {
 
-constexpr int KSTEP = 64;         // K elements per pipeline step
-constexpr int TILE_M = 128;       // weight rows per unit (TMEM lanes)
-constexpr int MAX_N = 256;        // token rows per unit
-constexpr int NB = 3;             // token-row stages
-constexpr int NP = 8;             // packed-weight stages
-constexpr int NA = 8;             // TMEM A stages (32 columns each)
-constexpr int B_STAGE = MAX_N * KSTEP * 2;   // 32 KB
-constexpr int P_STAGE = TILE_M * KSTEP / 2;  // 4 KB
-constexpr int EXCH_BYTES = 2 * MAX_N * 64 * 2;  // GLU gate/up bf16 exchange: 64 KB
+constexpr int KSTEP = 64;          // K elements per pipeline step
+constexpr int TILE_M = 128;        // weight rows per unit (TMEM lanes)
+constexpr int MAX_N = 192;         // token rows per unit (accumulator columns)
+constexpr int NS = 4;              // operand stages: token rows (smem) + dequantized A (TMEM), one K step each
+constexpr int NP = 4;              // packed-weight stages (4 K steps each)
+constexpr int PK = 4;              // K steps per packed-weight stage (128 bytes of every row)
+constexpr int B_STAGE = MAX_N * KSTEP * 2;   // 24 KB of token rows per operand stage
+constexpr int P_STAGE = TILE_M * PK * KSTEP / 2;  // 16 KB
 constexpr int TMEM_COLS = 512;
-constexpr int A_COL = 256;        // first TMEM column of the A ring
-constexpr int NWARPS = 14;        // 0 producer, 1 MMA, 2..9 dequant, 10..13 epilogue
+constexpr int D_COL1 = MAX_N;      // accumulators at columns [0, 192) and [192, 384)
+constexpr int A_COL = 2 * MAX_N;   // A ring at [384, 512)
+constexpr int NWARPS = 14;         // warps before the token-row producer (see the role list below)
 constexpr int NTHREADS = NWARPS * 32;
 constexpr int MAX_E = 1024;
+static_assert(A_COL + NS * 32 == TMEM_COLS, "TMEM plan");
 
 struct Smem {
-  uint8_t b[NB][B_STAGE];          // 1024-aligned (first member)
+  uint8_t b[NS][B_STAGE];          // 1024-aligned (first member)
   uint8_t p[NP][P_STAGE];
-  uint8_t exch[EXCH_BYTES];
+  uint16_t stg[4][32 * 32];        // PLAIN epilogue transpose, one 32x32 tile per warp
   uint32_t prefix[MAX_E + 1];
   uint32_t offs[MAX_E + 1];
-  uint64_t bfull[NB], bempty[NB], pfull[NP], pempty[NP], afull[NA], aempty[NA];
-  uint64_t dfull, dempty, drain;
+  uint64_t ofull[NS], oempty[NS], pfull[NP], pempty[NP];
+  uint64_t dfull[2], dempty[2], drain;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -116,8 +126,139 @@ __device__ __forceinline__ int kperm(int f) {
   return (f & ~7) | (j < 4 ? 2 * j : 2 * (j - 4) + 1);
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(NTHREADS, 1) qmm_tc_kernel(const __grid_constant__ TcParams p) {
+// SwiGLU with the bf16 rounding points of the decode path; exp through the
+// fast hardware exponential (results can differ from expf in the last bf16
+// place of the sigmoid, well inside the layer tolerance) and the reciprocal
+// through the correctly rounded rcp (identical to 1/x).
+// Round to bf16 (nearest even) with the conversion instruction; differs from
+// f2bf only in the NaN payload.
+__device__ __forceinline__ uint16_t f2bf_hw(float f) {
+  uint16_t h;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return h;
+}
+__device__ __forceinline__ float rb_hw(float f) { return __uint_as_float((uint32_t)f2bf_hw(f) << 16); }
+
+__device__ __forceinline__ uint16_t swiglu_bf16_fast(float g, float u) {
+  const float x = rb_hw(g);
+  const float e = rb_hw(__expf(rb_hw(fabsf(x))));
+  const float y = rb_hw(__frcp_rn(rb_hw(1.0f + e)));
+  const float sg = x < 0.0f ? y : rb_hw(1.0f - y);
+  const float si = rb_hw(x * sg);
+  return f2bf_hw(si * rb_hw(u));
+}
+
+// Scale or bias of group gi (0..7) of an 8-group block held as 16 bytes.
+template <int GI>
+__device__ __forceinline__ uint32_t meta_pair(const uint4& v) {
+  const uint32_t w = (GI >> 1) == 0 ? v.x : (GI >> 1) == 1 ? v.y : (GI >> 1) == 2 ? v.z : v.w;
+  // both halves of the result hold the group's bf16 value
+  return __byte_perm(w, 0, (GI & 1) ? 0x3232 : 0x1010);
+}
+
+// One dequant warp of group GROUP (0 or 1): the group handles every other K
+// step (the two groups keep two steps in flight); per step the warp turns the
+// 64 packed values of its A row into bf16 s*q + b and stores them to TMEM.
+// The group arithmetic is compile-time: GS / 8 K steps share one 16-byte
+// block of 8 scales / biases.
+template <int MODE, int GS, int GROUP>
+__device__ __forceinline__ void dequant_role(const TcParams& p, Smem& sm, uint32_t tbase, int warp, int lane, int E,
+                                             int MT, int nk, int U, uint64_t deadline, volatile int* abort_flag) {
+  constexpr int SPB = GS / 8;  // K steps per block of 8 groups (even)
+  static_assert(SPB % 2 == 0, "each block holds an even number of K steps");
+  const int quarter = warp & 3;
+  const int r = quarter * 32 + lane;  // A row = TMEM lane
+  // GLU rows: each 32-lane quarter holds 16 gate rows then the same 16 up rows
+  const int fo = quarter * 16 + (lane & 15);
+  const bool up_row = (MODE == TC_GLU) && (lane >= 16);
+  const int prow = (MODE == TC_GLU) ? (up_row ? 64 + fo : fo) : r;  // row in the packed stage
+  const uint32_t prow_off = prow * 128, sw = prow & 7;  // 128-byte swizzle: unit c at (c ^ row % 8)
+  const uint32_t t_col = tbase + ((uint32_t)(quarter * 32) << 16) + A_COL;
+  const int G = p.K / GS;
+  const int nblk = G / 8;
+  uint32_t ks = GROUP;  // running K-step index (stage counters), this group's steps only
+  for (int u = blockIdx.x; u < U && !__any_sync(0xffffffffu, *abort_flag != 0); u += gridDim.x) {
+    const Unit t = decode_unit(sm, E, MT, u);
+    const size_t row = (MODE == TC_GLU) ? (size_t)t.e * p.Nw + t.mt * 64 + fo : (size_t)t.e * p.Nw + t.mt * TILE_M + r;
+    const uint4* s4 = reinterpret_cast<const uint4*>((up_row ? p.s1 : p.s0) + row * G);
+    const uint4* b4 = reinterpret_cast<const uint4*>((up_row ? p.b1 : p.b0) + row * G);
+    uint4 s_nxt = __ldg(s4), b_nxt = __ldg(b4);
+    bool ok = true;
+    for (int blk = 0; blk < nblk && ok; ++blk) {
+      const uint4 sc = s_nxt, bc = b_nxt;
+      if (blk + 1 < nblk) {
+        s_nxt = __ldg(s4 + blk + 1);
+        b_nxt = __ldg(b4 + blk + 1);
+      }
+#pragma unroll
+      for (int j = GROUP; j < SPB; j += 2, ks += 2) {
+        const uint32_t pst = ks / PK, ps = pst % NP, as = ks % NS;
+        const uint32_t sub = j % PK;  // K step inside the packed stage (compile-time after unrolling)
+        if (!__all_sync(0xffffffffu, tc::wait(&sm.pfull[ps], (pst / NP) & 1, deadline, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const uint4 w0 = *reinterpret_cast<const uint4*>(sm.p[ps] + prow_off + (((2 * sub) ^ sw) << 4));
+        const uint4 w1 = *reinterpret_cast<const uint4*>(sm.p[ps] + prow_off + (((2 * sub + 1) ^ sw) << 4));
+        __syncwarp();
+        // each warp reads a packed stage in two of its K steps; it releases it after the second
+        if (sub >= 2 && lane == 0) mbar_arrive(&sm.pempty[ps]);
+        if (ks >= NS &&
+            !__all_sync(0xffffffffu, tc::wait(&sm.oempty[as], ((ks / NS) - 1) & 1, deadline, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc::fence_after();
+        // groups of the two 32-value halves of this K step inside the block
+        uint32_t s2[2], b2[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          switch ((j * 64 + h * 32) / GS) {
+            case 0: s2[h] = meta_pair<0>(sc); b2[h] = meta_pair<0>(bc); break;
+            case 1: s2[h] = meta_pair<1>(sc); b2[h] = meta_pair<1>(bc); break;
+            case 2: s2[h] = meta_pair<2>(sc); b2[h] = meta_pair<2>(bc); break;
+            case 3: s2[h] = meta_pair<3>(sc); b2[h] = meta_pair<3>(bc); break;
+            case 4: s2[h] = meta_pair<4>(sc); b2[h] = meta_pair<4>(bc); break;
+            case 5: s2[h] = meta_pair<5>(sc); b2[h] = meta_pair<5>(bc); break;
+            case 6: s2[h] = meta_pair<6>(sc); b2[h] = meta_pair<6>(bc); break;
+            default: s2[h] = meta_pair<7>(sc); b2[h] = meta_pair<7>(bc); break;
+          }
+        }
+        uint32_t a[32];
+        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t k128 = 0x43004300u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t w = words[i];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const uint32_t q = tc::bf2_sub(lop_or_and(w >> (4 * jj), 0x000F000Fu, k128), k128);
+            a[i * 4 + jj] = tc::bf2_fma(q, s2[i >> 2], b2[i >> 2]);
+          }
+        }
+        tc::tmem_st32(t_col + as * 32, a);
+        tc::tmem_wait_st();
+        tc::fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.ofull[as]);
+      }
+    }
+    if (!ok) {
+      if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
+      *abort_flag = 1;
+      break;
+    }
+  }
+}
+
+// Roles (warp: role). A warp may only touch TMEM lanes 32*(warp%4) ...+31.
+//   0      producer of packed weight tiles (elected lane)
+//   1      TMEM allocation; MMA issue (elected lane)
+//   2..9   dequant: A row = 32*(warp%4) + lane; warps 2..5 even K steps, 6..9 odd
+//   10..13 epilogue: accumulator lanes 32*(warp%4) ... +31
+//   14     producer of token-row tiles (elected lane)
+template <int MODE, int GS>
+__global__ void __launch_bounds__(NTHREADS + 32, 1) qmm_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -128,16 +269,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) qmm_tc_kernel(const __grid_consta
   const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
 
   if (tid == 0) {
-    for (int i = 0; i < NB; ++i) { mbar_init(&sm.bfull[i], 1); mbar_init(&sm.bempty[i], 1); }
+    // operand stage full: 4 dequant warps of one group + the token-row producer (with its bytes)
+    for (int i = 0; i < NS; ++i) { mbar_init(&sm.ofull[i], 5); mbar_init(&sm.oempty[i], 1); }
     for (int i = 0; i < NP; ++i) { mbar_init(&sm.pfull[i], 1); mbar_init(&sm.pempty[i], 8); }
-    for (int i = 0; i < NA; ++i) { mbar_init(&sm.afull[i], 8); mbar_init(&sm.aempty[i], 1); }
-    mbar_init(&sm.dfull, 1);
-    mbar_init(&sm.dempty, 4);
+    for (int i = 0; i < 2; ++i) { mbar_init(&sm.dfull[i], 1); mbar_init(&sm.dempty[i], 4); }
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
     fence_barrier_init();
   }
-  for (int i = tid; i <= E; i += NTHREADS) {
+  for (int i = tid; i <= E; i += blockDim.x) {
     sm.prefix[i] = p.prefix[i];
     sm.offs[i] = p.offsets[i];
   }
@@ -151,245 +291,173 @@ __global__ void __launch_bounds__(NTHREADS, 1) qmm_tc_kernel(const __grid_consta
   const uint32_t tbase = sm.tmem_base;
   const int U = (int)sm.prefix[E];
 
-  if (warp == 0) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
-      uint32_t nbfill = 0, npfill = 0;
-      for (int u = blockIdx.x; u < U && !*abort_flag; u += gridDim.x) {
-        const Unit t = decode_unit(sm, E, MT, u);
-        const int nbox = (t.len + 31) / 32;
-        for (int s = 0; s < nk; ++s) {
-          {
-            const uint32_t ps = npfill % NP;
-            if (npfill >= NP && !tc::wait(&sm.pempty[ps], ((npfill / NP) - 1) & 1, deadline, abort_flag)) {
-              record_error(p.err, B2Q_ETIMEOUT);
-              *abort_flag = 1;
-              break;
-            }
-            mbar_arrive_expect_tx(&sm.pfull[ps], P_STAGE);
-            uint8_t* dst = sm.p[ps];
-            if (MODE == TC_GLU) {
-              const int r0 = t.e * p.Nw + t.mt * 64;
-              tc::tma_load_2d(dst, &p.map_w0, s * 16, r0, &sm.pfull[ps], pol_w);
-              tc::tma_load_2d(dst + P_STAGE / 2, &p.map_w1, s * 16, r0, &sm.pfull[ps], pol_w);
-            } else {
-              tc::tma_load_2d(dst, &p.map_w0, s * 16, t.e * p.Nw + t.mt * TILE_M, &sm.pfull[ps], pol_w);
-            }
-            ++npfill;
-          }
-          {
-            const uint32_t bs = nbfill % NB;
-            if (nbfill >= NB && !tc::wait(&sm.bempty[bs], ((nbfill / NB) - 1) & 1, deadline, abort_flag)) {
-              record_error(p.err, B2Q_ETIMEOUT);
-              *abort_flag = 1;
-              break;
-            }
-            mbar_arrive_expect_tx(&sm.bfull[bs], nbox * 4096);
-            for (int b = 0; b < nbox; ++b)
-              tc::tma_load_2d(sm.b[bs] + b * 4096, &p.map_b, s * KSTEP, t.row0 + b * 32, &sm.bfull[bs], pol_x);
-            ++nbfill;
-          }
-        }
-      }
-      if (*abort_flag) {
-        // let every copy already issued land before the CTA can exit
-        const uint64_t dl = globaltimer() + 200000000ull;
-        for (uint32_t i = (npfill > NP ? npfill - NP : 0); i < npfill; ++i) tc::wait_until(&sm.pfull[i % NP], (i / NP) & 1, dl);
-        for (uint32_t i = (nbfill > NB ? nbfill - NB : 0); i < nbfill; ++i) tc::wait_until(&sm.bfull[i % NB], (i / NB) & 1, dl);
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      uint32_t nb = 0, na = 0, units = 0;
-      bool issued = false;
-      for (int u = blockIdx.x; u < U && !*abort_flag; u += gridDim.x, ++units) {
-        const Unit t = decode_unit(sm, E, MT, u);
-        const int N = ((t.len + 15) / 16) * 16;
-        const uint32_t idesc = tc::idesc_bf16_f32(TILE_M, N);
-        if (units > 0 && !tc::wait(&sm.dempty, (units - 1) & 1, deadline, abort_flag)) {
-          record_error(p.err, B2Q_ETIMEOUT);
-          *abort_flag = 1;
-          break;
-        }
-        tc::fence_after();
-        bool ok = true;
-        for (int s = 0; s < nk; ++s, ++nb, ++na) {
-          const uint32_t as = na % NA, bs = nb % NB;
-          if (!tc::wait(&sm.afull[as], (na / NA) & 1, deadline, abort_flag) ||
-              !tc::wait(&sm.bfull[bs], (nb / NB) & 1, deadline, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc::fence_after();
-          const uint64_t bdesc = tc::smem_desc_sw128(smem_u32(sm.b[bs]));
-#pragma unroll
-          for (int kk = 0; kk < KSTEP / 16; ++kk)
-            tc::mma_ts(tbase, tbase + A_COL + as * 32 + kk * 8, bdesc + 2 * kk, idesc, (s | kk) != 0);
-          issued = true;
-          tc::commit(&sm.aempty[as]);
-          tc::commit(&sm.bempty[bs]);
-        }
-        if (!ok) {
-          record_error(p.err, B2Q_ETIMEOUT);
-          *abort_flag = 1;
-          break;
-        }
-        tc::commit(&sm.dfull);
-      }
-      if (issued) {
-        // every MMA done before TMEM can be released
-        tc::commit(&sm.drain);
-        tc::wait_until(&sm.drain, 0, globaltimer() + 200000000ull);
-      }
-    }
-  } else if (warp < 10) {
-    // ---------------- dequant (8 warps: quarter = warp % 4, K half) ----------------
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int r = quarter * 32 + lane;  // A row = TMEM lane
-    const uint32_t t_lane = tbase + ((uint32_t)(quarter * 32) << 16);
-    const int G = p.K / p.gs;
-    uint32_t np = 0, na = 0;
+  if (warp == 0 || warp == NWARPS) {
+    // ---------------- producers (one converged warp each; an elected lane issues) ----------------
+    const bool weights = (warp == 0);
+    const uint64_t pol = weights ? policy_evict_first() : policy_evict_last();
+    uint32_t nfill = 0;
+    const uint32_t NSTG = weights ? NP : NS;
+    uint64_t* full = weights ? sm.pfull : sm.ofull;
+    uint64_t* empty = weights ? sm.pempty : sm.oempty;
     for (int u = blockIdx.x; u < U && !__any_sync(0xffffffffu, *abort_flag != 0); u += gridDim.x) {
       const Unit t = decode_unit(sm, E, MT, u);
-      // weight row of this thread and its metadata rows
-      const uint16_t* srow;
-      const uint16_t* brow;
-      if (MODE == TC_GLU) {
-        const int f = t.mt * 64 + (r & 63);
-        const size_t row = (size_t)t.e * p.Nw + f;
-        srow = (r < 64 ? p.s0 : p.s1) + row * G;
-        brow = (r < 64 ? p.b0 : p.b1) + row * G;
-      } else {
-        const size_t row = (size_t)t.e * p.Nw + t.mt * TILE_M + r;
-        srow = p.s0 + row * G;
-        brow = p.b0 + row * G;
-      }
-      // scales / biases in blocks of 8 groups (16 bytes), the next block in flight
-      int blk = -1;
-      uint4 s_cur = make_uint4(0, 0, 0, 0), b_cur = s_cur, s_nxt = s_cur, b_nxt = s_cur;
-      const uint4* s4 = reinterpret_cast<const uint4*>(srow);
-      const uint4* b4 = reinterpret_cast<const uint4*>(brow);
-      const int nblk = G / 8;
+      const int nbox = (t.len + 31) / 32;
       bool ok = true;
-      for (int s = 0; s < nk; ++s, ++np, ++na) {
-        const uint32_t ps = np % NP, as = na % NA;
-        // group of this thread's 32 K values
-        const int g = (s * KSTEP + half * 32) / p.gs;
-        if ((g >> 3) != blk) {
-          if (blk < 0) {
-            s_cur = __ldg(s4 + (g >> 3));
-            b_cur = __ldg(b4 + (g >> 3));
+      const int nfills = weights ? nk / PK : nk;
+      for (int s = 0; s < nfills; ++s, ++nfill) {
+        const uint32_t st = nfill % NSTG;
+        if (nfill >= NSTG &&
+            !__all_sync(0xffffffffu, tc::wait(&empty[st], ((nfill / NSTG) - 1) & 1, deadline, abort_flag))) {
+          ok = false;
+          break;
+        }
+        if (tc::elect_one()) {
+          if (weights) {
+            // 128 bytes (4 K steps) of each of the tile's weight rows
+            mbar_arrive_expect_tx(&full[st], P_STAGE);
+            uint8_t* dst = sm.p[st];
+            if (MODE == TC_GLU) {
+              const int r0 = t.e * p.Nw + t.mt * 64;
+              tc::tma_load_2d(dst, &p.map_w0, s * 64, r0, &full[st], pol);
+              tc::tma_load_2d(dst + P_STAGE / 2, &p.map_w1, s * 64, r0, &full[st], pol);
+            } else {
+              tc::tma_load_2d(dst, &p.map_w0, s * 64, t.e * p.Nw + t.mt * TILE_M, &full[st], pol);
+            }
           } else {
-            s_cur = s_nxt;
-            b_cur = b_nxt;
-          }
-          blk = g >> 3;
-          if (blk + 1 < nblk) {
-            s_nxt = __ldg(s4 + blk + 1);
-            b_nxt = __ldg(b4 + blk + 1);
+            // token rows of this K step; one of the five arrivals of the operand barrier
+            mbar_arrive_expect_tx(&full[st], nbox * 4096);
+            for (int b = 0; b < nbox; ++b)
+              tc::tma_load_2d(sm.b[st] + b * 4096, &p.map_b, s * KSTEP, t.row0 + b * 32, &full[st], pol);
           }
         }
-        const int gi = g & 7;
-        const uint32_t sw = (gi & 4) ? ((gi & 2) ? s_cur.w : s_cur.z) : ((gi & 2) ? s_cur.y : s_cur.x);
-        const uint32_t bw = (gi & 4) ? ((gi & 2) ? b_cur.w : b_cur.z) : ((gi & 2) ? b_cur.y : b_cur.x);
-        const uint32_t sv = (gi & 1) ? (sw >> 16) : (sw & 0xFFFFu);
-        const uint32_t bv = (gi & 1) ? (bw >> 16) : (bw & 0xFFFFu);
-        const uint32_t s2 = sv | (sv << 16), b2 = bv | (bv << 16);
-        if (!__all_sync(0xffffffffu, tc::wait(&sm.pfull[ps], (np / NP) & 1, deadline, abort_flag))) {
-          ok = false;
-          break;
-        }
-        const uint4 wv = *reinterpret_cast<const uint4*>(sm.p[ps] + r * 32 + ((half ^ ((r >> 2) & 1)) << 4));
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.pempty[ps]);
-        if (na >= NA &&
-            !__all_sync(0xffffffffu, tc::wait(&sm.aempty[as], ((na / NA) - 1) & 1, deadline, abort_flag))) {
-          ok = false;
-          break;
-        }
-        tc::fence_after();
-        uint32_t a[16];
-        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-        const uint32_t k128 = 0x43004300u;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t w = words[i];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t q = tc::bf2_sub(lop_or_and(w >> (4 * j), 0x000F000Fu, k128), k128);
-            a[i * 4 + j] = tc::bf2_fma(q, s2, b2);
-          }
-        }
-        tc::tmem_st16(t_lane + A_COL + as * 32 + half * 16, a);
-        tc::tmem_wait_st();
-        tc::fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.afull[as]);
       }
       if (!ok) {
-        record_error(p.err, B2Q_ETIMEOUT);
+        if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
         *abort_flag = 1;
         break;
       }
     }
-  } else {
+    if (*abort_flag) {
+      // let every copy already issued land before the CTA can exit
+      const uint64_t dl = globaltimer() + 200000000ull;
+      for (uint32_t i = (nfill > NSTG ? nfill - NSTG : 0); i < nfill; ++i)
+        tc::wait_until(&full[i % NSTG], (i / NSTG) & 1, dl);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (converged warp; an elected lane issues) ----------------
+    uint32_t ks = 0, units = 0;
+    bool issued = false;
+    for (int u = blockIdx.x; u < U && !__any_sync(0xffffffffu, *abort_flag != 0); u += gridDim.x, ++units) {
+      const Unit t = decode_unit(sm, E, MT, u);
+      const int N = ((t.len + 15) / 16) * 16;
+      const uint32_t idesc = tc::idesc_bf16_f32(TILE_M, N);
+      const uint32_t d = units & 1;
+      if (units >= 2 &&
+          !__all_sync(0xffffffffu, tc::wait(&sm.dempty[d], ((units >> 1) - 1) & 1, deadline, abort_flag))) {
+        if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      tc::fence_after();
+      const uint32_t dcol = tbase + (d ? D_COL1 : 0);
+      bool ok = true;
+      for (int s = 0; s < nk; ++s, ++ks) {
+        const uint32_t st = ks % NS;
+        if (!__all_sync(0xffffffffu, tc::wait(&sm.ofull[st], (ks / NS) & 1, deadline, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc::fence_after();
+        const uint64_t bdesc = tc::smem_desc_sw128(smem_u32(sm.b[st]));
+#pragma unroll
+        for (int kk = 0; kk < KSTEP / 16; ++kk)
+          tc::mma_ts_elect(dcol, tbase + A_COL + st * 32 + kk * 8, bdesc + 2 * kk, idesc, (s | kk) != 0);
+        issued = true;
+        tc::commit_elect(&sm.oempty[st]);
+      }
+      if (!ok) {
+        if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      tc::commit_elect(&sm.dfull[d]);
+    }
+    if (issued) {
+      // every MMA done before TMEM can be released
+      tc::commit_elect(&sm.drain);
+      tc::wait_until(&sm.drain, 0, globaltimer() + 200000000ull);
+    }
+  } else if (warp < 10) {
+    // ---------------- dequant (8 warps: quarter = warp % 4, K half) ----------------
+    if (warp < 6)
+      dequant_role<MODE, GS, 0>(p, sm, tbase, warp, lane, E, MT, nk, U, deadline, abort_flag);
+    else
+      dequant_role<MODE, GS, 1>(p, sm, tbase, warp, lane, E, MT, nk, U, deadline, abort_flag);
+  } else if (warp < NWARPS) {
     // ---------------- epilogue (4 warps, quarter = warp % 4) ----------------
     const int quarter = warp & 3;
-    const int etid = tid - 10 * 32;  // 0..127
     const uint32_t t_lane = tbase + ((uint32_t)(quarter * 32) << 16);
-    uint16_t* exg = reinterpret_cast<uint16_t*>(sm.exch);  // [MAX_N][64] gate
-    uint16_t* exu = exg + MAX_N * 64;                      // [MAX_N][64] up
+    uint16_t* stg = sm.stg[warp - 10];
     uint32_t units = 0;
     // the loop bound is uniform and every exit is decided by one barrier
-    // reduction over the four warps, so the named barriers below always see
-    // all 128 threads
+    // reduction over the four warps
     for (int u = blockIdx.x; u < U; u += gridDim.x, ++units) {
       const Unit t = decode_unit(sm, E, MT, u);
-      const bool got = tc::wait(&sm.dfull, units & 1, deadline, abort_flag);
+      const uint32_t d = units & 1;
+      const bool got = tc::wait(&sm.dfull[d], (units >> 1) & 1, deadline, abort_flag);
       if (!bar_red_and(1, 128, got)) {
         if (!got && !*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
         *abort_flag = 1;
         break;
       }
       tc::fence_after();
+      const uint32_t dcol = t_lane + (d ? D_COL1 : 0);
       const int nchunk = (t.len + 31) / 32;
       for (int c = 0; c < nchunk; ++c) {
         uint32_t v[32];
-        tc::tmem_ld32(t_lane + c * 32, v);
+        tc::tmem_ld32(dcol + c * 32, v);
         tc::tmem_wait_ld();
+        if (c == nchunk - 1) {
+          // accumulator fully read: hand it back to the MMA issuer
+          tc::fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.dempty[d]);
+        }
         if (MODE == TC_GLU) {
-          uint16_t* ex = (quarter < 2) ? exg : exu;
-          const int fl = (quarter & 1) * 32 + lane;
+          // lane l < 16: gate row f, lane l + 16: up row f; pair through a shuffle
+          const int f = t.mt * 64 + quarter * 16 + (lane & 15);
+          const int pf = kperm(f);
+          const bool lo = lane < 16;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ex[(c * 32 + i) * 64 + fl] = f2bf(__uint_as_float(v[i]));
+          for (int i = 0; i < 16; ++i) {
+            const uint32_t send = lo ? v[i + 16] : v[i];
+            const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            const float gv = __uint_as_float(lo ? v[i] : recv);
+            const float uv = __uint_as_float(lo ? recv : v[i + 16]);
+            const int tok = c * 32 + (lo ? i : 16 + i);
+            if (tok < t.len)
+              p.out[(size_t)(t.row0 + tok) * p.out_ld + pf] = swiglu_bf16_fast(gv, uv);
+          }
         } else {
-          const int h = t.mt * TILE_M + quarter * 32 + lane;
+          // transpose the 32 x 32 tile through shared memory for 16-byte row stores
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int tok = c * 32 + i;
+          for (int i = 0; i < 32; ++i) stg[i * 32 + lane] = f2bf_hw(__uint_as_float(v[i]));
+          __syncwarp();
+          const int h = t.mt * TILE_M + quarter * 32 + (lane & 3) * 8;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int tl = j * 8 + (lane >> 2);
+            const int tok = c * 32 + tl;
             if (tok < t.len) {
               const int row = t.row0 + tok;
               const size_t orow = p.out_rows ? p.out_rows[row] : (size_t)row;
-              p.out[orow * p.out_ld + h] = f2bf(__uint_as_float(v[i]));
+              *reinterpret_cast<uint4*>(p.out + orow * p.out_ld + h) =
+                  *reinterpret_cast<const uint4*>(stg + tl * 32 + (lane & 3) * 8);
             }
           }
+          __syncwarp();
         }
-      }
-      tc::fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.dempty);
-      if (MODE == TC_GLU) {
-        named_bar_sync(1, 128);
-        const int fl = etid & 63;
-        const int pf = kperm(t.mt * 64 + fl);
-        for (int tok = etid >> 6; tok < t.len; tok += 2) {
-          const uint16_t gv = exg[tok * 64 + fl], uv = exu[tok * 64 + fl];
-          p.out[(size_t)(t.row0 + tok) * p.out_ld + pf] = swiglu_bf16(gv, uv);
-        }
-        named_bar_sync(1, 128);
       }
     }
   }
@@ -400,7 +468,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) qmm_tc_kernel(const __grid_consta
   if (warp == 1) tc::tmem_dealloc(tbase, TMEM_COLS);
 }
 
-// Units per expert: ceil(R_e / 256) chunks times the weight tiles.
+// Units per expert: ceil(R_e / 192) chunks times the weight tiles.
 __global__ void unit_table_kernel(const uint32_t* __restrict__ offsets, int E, int MT0, int MT1,
                                   uint32_t* __restrict__ prefix0, uint32_t* __restrict__ prefix1) {
   __shared__ uint32_t c0[MAX_E + 1], c1[MAX_E + 1];
@@ -470,12 +538,13 @@ int tc_gather_rows(const uint16_t* x, const uint32_t* rows, uint16_t* xs, int R,
 }
 
 int tc_setup(TcParams& p, int mode, const uint16_t* xs, int R, const uint32_t* w0, const uint32_t* w1) {
-  // packed weights: uint16 view [E*Nw rows, K/4], boxes {16 (32 bytes), 64 or 128 rows}, 32-byte swizzle
+  // packed weights: uint16 view [E*Nw rows, K/4], boxes {64 (128 bytes = 4 K steps), 64 or 128 rows},
+  // 128-byte swizzle
   const int box_rows = (mode == TC_GLU) ? 64 : TILE_M;
-  int rc = make_2d_map(&p.map_w0, w0, (uint64_t)p.E * p.Nw, (uint64_t)p.K / 2, 32, box_rows, 32);
+  int rc = make_2d_map(&p.map_w0, w0, (uint64_t)p.E * p.Nw, (uint64_t)p.K / 2, 128, box_rows, 128);
   if (rc) return rc;
   if (mode == TC_GLU) {
-    rc = make_2d_map(&p.map_w1, w1, (uint64_t)p.E * p.Nw, (uint64_t)p.K / 2, 32, box_rows, 32);
+    rc = make_2d_map(&p.map_w1, w1, (uint64_t)p.E * p.Nw, (uint64_t)p.K / 2, 128, box_rows, 128);
     if (rc) return rc;
   }
   // token rows: bf16 [R, K], boxes {64 (128 bytes), 32 rows}, 128-byte swizzle
@@ -488,20 +557,21 @@ int tc_launch(const TcParams& p, int mode, cudaStream_t st) {
   if (rc) return rc;
   const size_t smem = tc_smem_bytes();
   if ((int)smem > di.smem_optin) return set_error(B2Q_EUNSUPPORTED, "tensor-core qmm: %zu bytes of shared memory", smem);
-  static int attr_done[64] = {};
-  const int slot = (di.device & 63);
-  if (!(attr_done[slot] & (1 << mode))) {
-    if (mode == TC_GLU)
-      B2Q_TRY_CUDA(cudaFuncSetAttribute(qmm_tc_kernel<TC_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    else
-      B2Q_TRY_CUDA(cudaFuncSetAttribute(qmm_tc_kernel<TC_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_done[slot] |= 1 << mode;
-  }
   const int grid = di.sm_count;
-  if (mode == TC_GLU)
-    qmm_tc_kernel<TC_GLU><<<grid, NTHREADS, smem, st>>>(p);
-  else
-    qmm_tc_kernel<TC_PLAIN><<<grid, NTHREADS, smem, st>>>(p);
+  const int threads = NTHREADS + 32;
+#define B2Q_TC_CASE(M, G)                                                                                   \
+  if (mode == M && p.gs == G) {                                                                             \
+    static int attr_done[64] = {};                                                                          \
+    if (!attr_done[di.device & 63]) {                                                                       \
+      B2Q_TRY_CUDA(cudaFuncSetAttribute(qmm_tc_kernel<M, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+      attr_done[di.device & 63] = 1;                                                                        \
+    }                                                                                                       \
+    qmm_tc_kernel<M, G><<<grid, threads, smem, st>>>(p);                                                    \
+  } else
+  B2Q_TC_CASE(TC_GLU, 32) B2Q_TC_CASE(TC_GLU, 64) B2Q_TC_CASE(TC_GLU, 128)
+  B2Q_TC_CASE(TC_PLAIN, 32) B2Q_TC_CASE(TC_PLAIN, 64) B2Q_TC_CASE(TC_PLAIN, 128)
+  return set_error(B2Q_EUNSUPPORTED, "tensor-core qmm: group size %d", p.gs);
+#undef B2Q_TC_CASE
   B2Q_TRY_CUDA(cudaGetLastError());
   return B2Q_OK;
 }
