@@ -1053,8 +1053,95 @@ __global__ void route_kernel(const float* __restrict__ logits, uint32_t* __restr
   warp_route(logits + (size_t)t * E, E, k, false, idx + (size_t)t * k, w + (size_t)t * k);
 }
 
+// Tiled router GEMM for token windows: CTA tile 32 tokens x 128 experts, K in
+// steps of 64 through double-buffered shared memory (cp.async), 8 warps each
+// 16 tokens x 32 experts with mma.sync m16n8k16 (bf16 products are exact in
+// fp32; fp32 accumulation).
+constexpr int RT_BM = 32, RT_BN = 128, RT_BK = 64, RT_LD = RT_BK + 8;  // padded rows: 144 bytes
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(pred ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+__global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __restrict__ x,
+                                                          const uint16_t* __restrict__ wr,
+                                                          float* __restrict__ logits, int T, int E, int H) {
+  __shared__ __align__(16) uint16_t xs[2][RT_BM * RT_LD];
+  __shared__ __align__(16) uint16_t ws[2][RT_BN * RT_LD];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = blockIdx.x * RT_BM, e0 = blockIdx.y * RT_BN;
+  const int wm = (warp & 1) * 16, wn = (warp >> 1) * 32;
+  auto load = [&](int buf, int k0) {
+    // x: 32 rows x 8 chunks of 16 bytes; wr: 128 rows x 8 chunks
+    for (int i = tid; i < RT_BM * 8; i += 256) {
+      const int r = i >> 3, c = i & 7;
+      const bool ok = t0 + r < T;
+      cp_async16(&xs[buf][r * RT_LD + c * 8], x + (size_t)(ok ? t0 + r : 0) * H + k0 + c * 8, ok);
+    }
+    for (int i = tid; i < RT_BN * 8; i += 256) {
+      const int r = i >> 3, c = i & 7;
+      const bool ok = e0 + r < E;
+      cp_async16(&ws[buf][r * RT_LD + c * 8], wr + (size_t)(ok ? e0 + r : 0) * H + k0 + c * 8, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float acc[4][4] = {};
+  const int nk = H / RT_BK;
+  load(0, 0);
+  for (int kt = 0; kt < nk; ++kt) {
+    if (kt + 1 < nk) {
+      load((kt + 1) & 1, (kt + 1) * RT_BK);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const uint16_t* xb = xs[kt & 1];
+    const uint16_t* wb = ws[kt & 1];
+#pragma unroll
+    for (int kk = 0; kk < RT_BK; kk += 16) {
+      uint32_t a[4];
+      ldmatrix_x4(a, xb + (wm + (lane & 15)) * RT_LD + kk + (lane >> 4) * 8);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t b[4];
+        const int m = lane >> 3, r = lane & 7;
+        ldmatrix_x4(b, wb + (wn + np * 16 + (m >> 1) * 8 + r) * RT_LD + kk + (m & 1) * 8);
+        mma_bf16_16816(acc[np * 2], a[0], a[1], a[2], a[3], b[0], b[1]);
+        mma_bf16_16816(acc[np * 2 + 1], a[0], a[1], a[2], a[3], b[2], b[3]);
+      }
+    }
+    __syncthreads();
+  }
+  const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    const int e = e0 + wn + nt * 8 + 2 * q;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = t0 + wm + g + h * 8;
+      if (t < T) {
+        if (e < E) logits[(size_t)t * E + e] = acc[nt][2 * h];
+        if (e + 1 < E) logits[(size_t)t * E + e + 1] = acc[nt][2 * h + 1];
+      }
+    }
+  }
+}
+
 int launch_router_logits(const uint16_t* x, const uint16_t* wr, float* logits, int T, int E, int H,
                          cudaStream_t s) {
+  if (T >= RT_BM && H % RT_BK == 0) {
+    dim3 grid((T + RT_BM - 1) / RT_BM, (E + RT_BN - 1) / RT_BN);
+    router_gemm_kernel<<<grid, 256, 0, s>>>(x, wr, logits, T, E, H);
+    B2Q_TRY_CUDA(cudaGetLastError());
+    return B2Q_OK;
+  }
   const long long warps = (long long)T * E;
   const int threads = 256;
   const long long blocks = (warps * 32 + threads - 1) / threads;

@@ -96,3 +96,17 @@ def test_prefill_skewed_and_empty_experts(cuda, b2q_mod, oracle):
     idx = _check_layer(b2q_mod, oracle, x, wr, L, k, 64, rows=rows)
     counts = np.bincount(_np(idx).ravel(), minlength=E)
     assert counts[0] == T and (counts[12:] == 0).all()
+
+
+@pytest.mark.parametrize("T,E,H", [(256, 128, 4096), (40, 16, 1024), (97, 200, 512)])
+def test_router_logits_windows(cuda, b2q_mod, oracle, T, E, H):
+    """Token windows go through the tiled tensor-core router GEMM (tails in both
+    tokens and experts); logits match the fp32 dot products up to summation
+    order: |diff| <= 1e-4 on logits of order one (sums of H products)."""
+    from b2q import synth
+
+    x = synth.activations((T, H), seed=80)
+    wr = synth.router_weight(E, H, seed=81)
+    lg = b2q_mod.router_logits(x, wr)
+    ref = oracle.router_logits(_np(x), _np(wr))
+    assert np.allclose(_np(lg), ref, rtol=1e-4, atol=1e-4)
