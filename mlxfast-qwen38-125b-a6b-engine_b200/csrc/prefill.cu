@@ -53,14 +53,113 @@ __global__ void sorted_combine_kernel(const uint16_t* __restrict__ y, const uint
   out[(size_t)t * H + h] = f2bf(total);
 }
 
-bool prefill_qmm_eligible(int, int, int, int, int, const void*, const void*, const void*, const void*,
-                          const void*) {
-  return false;  // the tensor-core gather GEMM is selected in prefill_tc.cu when built
+// ---------------------------------------------------------------------------
+// gather_qmm / quantized_matmul with many rows per weight matrix (M > 8): the
+// tcgen05 grouped GEMM over rows grouped by weight matrix.
+// Item i multiplies x[lhs[i]] (M rows; lhs null: x[i]) by w[rhs[i]] (rhs null:
+// w[i]) into y[i]; items whose indices are out of range produce zeros, as the
+// shape-general kernel does.
+// ---------------------------------------------------------------------------
+bool prefill_qmm_eligible(int batch, int M, int N, int K, int gs, const void* x, const void* w, const void* s,
+                          const void* b, const void* y) {
+  (void)batch;
+  return M > 8 && tc_shape_ok(N, K, gs, TC_PLAIN) && aligned16(x) && aligned16(w) && aligned16(s) &&
+         aligned16(b) && aligned16(y);
 }
 
-int launch_prefill_gather_qmm(const uint16_t*, const uint32_t*, const uint16_t*, const uint16_t*, const uint32_t*,
-                              const uint32_t*, uint16_t*, int, int, int, int, int, int, int, int, cudaStream_t) {
-  return set_error(B2Q_EUNSUPPORTED, "tensor-core gather GEMM not built");
+// ids[i] = rhs[i] (or i)
+__global__ void item_ids_kernel(const uint32_t* __restrict__ rhs, uint32_t* __restrict__ ids, int batch) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < batch) ids[i] = rhs ? rhs[i] : (uint32_t)i;
+}
+
+// Row tables of the sorted items: sorted row p*M + m reads x row
+// lhs[item]*M + m (0xFFFFFFFF when lhs is out of range: zeros) and is written
+// to y row item*M + m. Row offsets per weight matrix = item offsets * M.
+__global__ void item_rows_kernel(const uint32_t* __restrict__ item_of, const uint32_t* __restrict__ lhs,
+                                 const uint32_t* __restrict__ offsets, uint32_t* __restrict__ src_row,
+                                 uint32_t* __restrict__ out_row, uint32_t* __restrict__ row_offsets, int n_sorted,
+                                 int M, int n_x, int E) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t <= E && row_offsets) row_offsets[t] = offsets[t] * (uint32_t)M;
+  if (t >= n_sorted * M) return;
+  const int p = t / M, m = t % M;
+  const uint32_t item = item_of[p];
+  if (item >= (uint32_t)n_sorted) {  // a position past the valid items: never multiplied
+    src_row[t] = 0xFFFFFFFFu;
+    out_row[t] = 0;
+    return;
+  }
+  const uint32_t xi = lhs ? lhs[item] : item;
+  src_row[t] = xi < (uint32_t)n_x ? xi * (uint32_t)M + (uint32_t)m : 0xFFFFFFFFu;
+  out_row[t] = item * (uint32_t)M + (uint32_t)m;
+}
+
+int launch_prefill_gather_qmm(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                              const uint32_t* lhs, const uint32_t* rhs, uint16_t* y, int batch, int M, int N, int K,
+                              int n_x, int n_w, int gs, int sorted, cudaStream_t st) {
+  (void)sorted;  // the items are grouped by a stable sort either way
+  const int E = n_w;
+  if (E < 1 || E > 1024) return set_error(B2Q_EUNSUPPORTED, "gather_qmm: %d weight matrices on tensor cores", E);
+  const size_t R = (size_t)batch * M;
+  // temporaries (stream-ordered): ids, sorted ids, item order, inverse, offsets, row offsets,
+  // unit prefix, error word, source / output row tables, sorted x rows
+  auto a256 = [](size_t v) { return (v + 255) / 256 * 256; };
+  size_t off = 0;
+  const size_t o_ids = off; off = a256(off + 4 * (size_t)batch);
+  const size_t o_sid = off; off = a256(off + 4 * (size_t)batch);
+  const size_t o_item = off; off = a256(off + 4 * (size_t)batch);
+  const size_t o_inv = off; off = a256(off + 4 * (size_t)batch);
+  const size_t o_off = off; off = a256(off + 4 * ((size_t)E + 1));
+  const size_t o_roff = off; off = a256(off + 4 * ((size_t)E + 1));
+  const size_t o_pre = off; off = a256(off + 4 * ((size_t)E + 1));
+  const size_t o_err = off; off = a256(off + 4);
+  const size_t o_src = off; off = a256(off + 4 * R);
+  const size_t o_out = off; off = a256(off + 4 * R);
+  const size_t o_xs = off; off = a256(off + 2 * R * (size_t)K);
+  char* tmp = nullptr;
+  B2Q_TRY_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&tmp), off, st));
+  auto U32 = [&](size_t o) { return reinterpret_cast<uint32_t*>(tmp + o); };
+  int rc = B2Q_OK;
+  do {
+    if (cudaMemsetAsync(tmp + o_err, 0, 4, st) != cudaSuccess || cudaMemsetAsync(y, 0, R * (size_t)N * 2, st) != cudaSuccess) {
+      rc = cuda_check(cudaGetLastError(), "gather_qmm: memset");
+      break;
+    }
+    item_ids_kernel<<<(batch + 255) / 256, 256, 0, st>>>(rhs, U32(o_ids), batch);
+    // stable grouping of the items by weight matrix; out-of-range ids are left out
+    rc = launch_expert_sort(U32(o_ids), U32(o_sid), U32(o_item), U32(o_inv), U32(o_off), batch, E, 1,
+                            reinterpret_cast<int*>(tmp + o_err), st);
+    if (rc) break;
+    // row tables over every sorted position (positions of left-out items are never reached:
+    // the row offsets stop at the valid items)
+    const int nthreads = (int)std::max<size_t>(R, (size_t)E + 1);
+    item_rows_kernel<<<(nthreads + 255) / 256, 256, 0, st>>>(U32(o_item), lhs, U32(o_off), U32(o_src), U32(o_out),
+                                                              U32(o_roff), batch, M, n_x, E);
+    rc = tc_unit_tables(U32(o_roff), E, tc_m_tiles(N, TC_PLAIN), 0, U32(o_pre), nullptr, st);
+    if (rc) break;
+    rc = tc_gather_rows(x, U32(o_src), reinterpret_cast<uint16_t*>(tmp + o_xs), (int)R, K, n_x * M, st);
+    if (rc) break;
+    TcParams p{};
+    p.E = E;
+    p.K = K;
+    p.Nw = N;
+    p.gs = gs;
+    p.s0 = s;
+    p.b0 = b;
+    p.offsets = U32(o_roff);
+    p.prefix = U32(o_pre);
+    p.out = y;
+    p.out_rows = U32(o_out);
+    p.out_ld = N;
+    p.err = reinterpret_cast<int*>(tmp + o_err);
+    p.timeout_ns = 2000000000ll;
+    rc = tc_setup(p, TC_PLAIN, reinterpret_cast<uint16_t*>(tmp + o_xs), (int)R, w, nullptr);
+    if (rc) break;
+    rc = tc_launch(p, TC_PLAIN, st);
+  } while (0);
+  cudaFreeAsync(tmp, st);
+  return rc;
 }
 
 struct PrefillWs {

@@ -134,3 +134,45 @@ def test_gather_out_of_range_items_are_zero(cuda, b2q_mod):
     yy = _np(y)
     assert np.all(yy[1] == 0) and np.all(yy[2] == 0)
     assert np.any(yy[0] != 0)
+
+
+# ---- many rows per weight matrix (M > 8): the tcgen05 grouped GEMM ----------
+# The tensor-core path rounds the dequantized weight to bf16 before the product
+# (the reference's tile loader, quantized.h:485-530), so it is compared with the
+# oracle's tile-loader arithmetic.
+
+@pytest.mark.parametrize("M,N,K,gs", [(64, 256, 1024, 64), (200, 128, 2048, 32), (33, 384, 1024, 128)])
+def test_qmm_tensor_core(cuda, b2q_mod, oracle, M, N, K, gs):
+    from b2q import synth
+
+    w, s, b = synth.packed_weights((N,), K, gs, seed=11)
+    x = synth.activations((M, K), seed=12)
+    y = b2q_mod.quantized_matmul(x, w, s, b, True, gs, 4)
+    ref = oracle.qmm_tile_f32(_np(x), _np(w), _np(s), _np(b), gs, 4)
+    assert rel_l2(_bf(_np(y)), ref) < TIGHT
+
+
+def test_gather_qmm_tensor_core(cuda, b2q_mod, oracle):
+    """Unsorted items, repeated experts, an out-of-range expert and an
+    out-of-range x index (both give zeros)."""
+    import torch
+
+    from b2q import synth
+
+    E, N, K, M = 5, 256, 1024, 24
+    w, s, b = synth.packed_weights((E, N), K, 64, seed=13)
+    x = synth.activations((4, M, K), seed=14)
+    lhs_l = [3, 0, 2, 1, 0, 9, 2]
+    rhs_l = [4, 0, 4, 2, 7, 1, 0]
+    lhs = torch.tensor(lhs_l, dtype=torch.int32, device="cuda").view(torch.uint32)
+    rhs = torch.tensor(rhs_l, dtype=torch.int32, device="cuda").view(torch.uint32)
+    y = b2q_mod.gather_qmm(x, w, s, b, lhs, rhs)
+    assert tuple(y.shape) == (7, M, N)
+    xs, ws_, ss, bs = _np(x), _np(w), _np(s), _np(b)
+    yy = _np(y)
+    for i, (l, r) in enumerate(zip(lhs_l, rhs_l)):
+        if l >= 4 or r >= E:
+            assert np.all(yy[i] == 0), i
+            continue
+        ref = oracle.qmm_tile_f32(xs[l], ws_[r], ss[r], bs[r], 64, 4)
+        assert rel_l2(_bf(yy[i]), ref) < TIGHT, i
