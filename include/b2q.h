@@ -17,12 +17,14 @@
  *  - Return 0 on success, a negative B2Q_E* code on failure; no exception
  *    crosses the ABI. b2q_last_error() gives a message for the calling thread
  *    (mirrors mlx-c's status + error handler, MLXCAPI/ops.cpp:1505-1508).
- *  - The library never allocates device memory. Entry points that need
- *    scratch take a caller-owned `workspace` whose size comes from the matching
- *    *_workspace_size() call; it must be zero-filled once before first use
+ *  - Entry points that need scratch take a caller-owned `workspace` whose
+ *    size comes from the matching *_workspace_size() call and allocate
+ *    nothing; it must be zero-filled once before first use
  *    (b2q_workspace_reset) and is left zero-filled by every call that
  *    completes without a device-side error. Calls sharing one workspace must
- *    be ordered on one stream.
+ *    be ordered on one stream. b2q_qmm and b2q_gather_qmm keep mlx-c's
+ *    workspace-free signatures: with more than 8 rows per item they take
+ *    stream-ordered temporaries (cudaMallocAsync / cudaFreeAsync on `stream`).
  *  - Only bits == 4 is implemented on the device (the packed format of the
  *    path); group_size is 32, 64 or 128. Other values return B2Q_EUNSUPPORTED.
  */
@@ -174,6 +176,39 @@ B2Q_API int b2q_moe_decode_noalloc(const uint16_t* x, const uint16_t* wr,
                    uint16_t* out, uint32_t* idx, float* w, float* logits,
                    int H, int E, int F, int k, int group_size, int bits,
                    int* status, void* stream);
+
+/* Expert parallelism (experts sharded over ranks; one NCCL all-reduce per layer).
+ * The reference's expert-parallel configuration of its MoE layer
+ * (moeForwardShared, Runner/FastModel/TrackFastModel.swift:867-1009) with
+ * the expert stacks of each layer bound per rank (:470-540): every rank holds
+ * the router and the experts [e_lo, e_lo + e_local) as stacked tensors of its
+ * local experts only, computes the routing in full, multiplies the selected
+ * experts it holds and adds their weighted outputs into the fp32 `partial`
+ * [T, H]; the all-reduce (sum) runs on `stream`, then `out` (bf16, may be
+ * NULL) receives the rounded layer output. With comm == NULL (or one rank)
+ * there is no all-reduce and `partial` is this rank's share.
+ * b2q_ep_unique_id fills a 128-byte NCCL id on one rank; the caller sends it
+ * to the others (its own transport), then every rank calls b2q_ep_comm_init
+ * with its device current. NCCL is loaded at run time (libnccl.so.2). */
+B2Q_API int b2q_ep_unique_id(void* id_out, size_t id_bytes);
+B2Q_API int b2q_ep_comm_init(void** comm_out, int nranks, int rank, const void* id, size_t id_bytes);
+B2Q_API int b2q_ep_comm_destroy(void* comm);
+B2Q_API size_t b2q_ep_moe_decode_workspace_size(int S, int H, int E, int F, int k);
+B2Q_API int b2q_ep_moe_decode(void* comm, const uint16_t* x, const uint16_t* wr,
+                   const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                   const uint32_t* wd, const uint16_t* sd, const uint16_t* bd,
+                   float* partial, uint16_t* out, uint32_t* idx, float* w,
+                   int S, int H, int E, int F, int k, int e_lo, int e_local,
+                   int group_size, int bits, void* workspace, size_t workspace_bytes, void* stream);
+B2Q_API size_t b2q_ep_moe_prefill_workspace_size(int T, int H, int E, int F, int k);
+B2Q_API int b2q_ep_moe_prefill(void* comm, const uint16_t* x, const uint16_t* wr,
+                   const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                   const uint32_t* wd, const uint16_t* sd, const uint16_t* bd,
+                   float* partial, uint16_t* out, uint32_t* idx, float* w,
+                   int T, int H, int E, int F, int k, int e_lo, int e_local,
+                   int group_size, int bits, void* workspace, size_t workspace_bytes, void* stream);
 
 /* One prefill MoE layer over T tokens: router logits, route, stable sort of the
  * T*k assignments by expert (TrackPrefillSort.swift:84-201), gate|up + SwiGLU

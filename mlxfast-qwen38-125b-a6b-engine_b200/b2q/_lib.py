@@ -46,6 +46,13 @@ SIGNATURES = {
     "b2q_moe_sorted_combine": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
     "b2q_sort_workspace_size": (_SZ, [_I, _I]),
     "b2q_moe_sort": (_I, [_P] * 5 + [_I] * 3 + [_P, _SZ, _P]),
+    "b2q_ep_unique_id": (_I, [_P, _SZ]),
+    "b2q_ep_comm_init": (_I, [_P, _I, _I, _P, _SZ]),
+    "b2q_ep_comm_destroy": (_I, [_P]),
+    "b2q_ep_moe_decode_workspace_size": (_SZ, [_I] * 5),
+    "b2q_ep_moe_decode": (_I, [_P] * 16 + [_I] * 9 + [_P, _SZ, _P]),
+    "b2q_ep_moe_prefill_workspace_size": (_SZ, [_I] * 5),
+    "b2q_ep_moe_prefill": (_I, [_P] * 16 + [_I] * 9 + [_P, _SZ, _P]),
     "b2q_workspace_reset": (_I, [_P, _SZ, _P]),
     "b2q_workspace_status": (_I, [_P, _SZ, _P]),
     "b2q_selftest_wait_timeout": (_I, [_P, _SZ, _LL, _P]),

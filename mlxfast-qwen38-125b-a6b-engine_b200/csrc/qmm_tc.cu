@@ -492,11 +492,14 @@ __global__ void unit_table_kernel(const uint32_t* __restrict__ offsets, int E, i
   }
 }
 
-// xs[i, :] = x[rows[i], :] with every 8-block reordered (0,4,1,5,2,6,3,7).
+// xs[i, :] = x[rows[i], :] with every 8-block reordered (0,4,1,5,2,6,3,7);
+// with `range`, only rows in [range[0], range[range_n]) are written.
 __global__ void gather_rows_perm_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ rows,
-                                        uint16_t* __restrict__ xs, int R, int K, int n_src) {
+                                        uint16_t* __restrict__ xs, int R, int K, int n_src,
+                                        const uint32_t* __restrict__ range, int range_n) {
   const int i = blockIdx.x;
   if (i >= R) return;
+  if (range && ((uint32_t)i < range[0] || (uint32_t)i >= range[range_n])) return;
   const uint32_t src = rows ? rows[i] : (uint32_t)i;
   const int nv = K / 8;
   uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)i * K);
@@ -532,7 +535,15 @@ int tc_unit_tables(const uint32_t* offsets, int E, int mt0, int mt1, uint32_t* p
 int tc_gather_rows(const uint16_t* x, const uint32_t* rows, uint16_t* xs, int R, int K, int n_src,
                    cudaStream_t st) {
   if (R <= 0) return B2Q_OK;
-  gather_rows_perm_kernel<<<R, 128, 0, st>>>(x, rows, xs, R, K, n_src);
+  gather_rows_perm_kernel<<<R, 128, 0, st>>>(x, rows, xs, R, K, n_src, nullptr, 0);
+  B2Q_TRY_CUDA(cudaGetLastError());
+  return B2Q_OK;
+}
+
+int tc_gather_rows_range(const uint16_t* x, const uint32_t* rows, uint16_t* xs, int R, int K, int n_src,
+                         const uint32_t* offsets, int n_groups, cudaStream_t st) {
+  if (R <= 0) return B2Q_OK;
+  gather_rows_perm_kernel<<<R, 128, 0, st>>>(x, rows, xs, R, K, n_src, offsets, n_groups);
   B2Q_TRY_CUDA(cudaGetLastError());
   return B2Q_OK;
 }

@@ -35,6 +35,9 @@ int tc_unit_tables(const uint32_t* offsets, int E, int mt0, int mt1, uint32_t* p
 inline int tc_m_tiles(int Nw, int mode) { return mode == TC_GLU ? Nw / 64 : Nw / 128; }
 // xs[i] = x[rows[i]] (rows may be null: identity) with the 8-block K reorder; rows >= n_src give zeros.
 int tc_gather_rows(const uint16_t* x, const uint32_t* rows, uint16_t* xs, int R, int K, int n_src, cudaStream_t st);
+// The same for the rows [offsets[0], offsets[n_groups]) only (device-side bounds).
+int tc_gather_rows_range(const uint16_t* x, const uint32_t* rows, uint16_t* xs, int R, int K, int n_src,
+                         const uint32_t* offsets, int n_groups, cudaStream_t st);
 // Tensor maps for the weights (w1 only for GLU) and the token rows xs [R, K].
 int tc_setup(TcParams& p, int mode, const uint16_t* xs, int R, const uint32_t* w0, const uint32_t* w1);
 int tc_launch(const TcParams& p, int mode, cudaStream_t st);

@@ -13,7 +13,7 @@
 namespace b2q {
 namespace tc {
 
-// ---- TMA (tiled, no multicast) ------------------------------------------------
+// ---- TMA (tiled, one CTA destination) ------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
                                             uint64_t policy) {
   asm volatile(
