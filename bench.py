@@ -38,6 +38,7 @@ EXPERT_BYTES = 3 * (F * (H // 2 + 2 * 2 * H // GS))  # gate/up/down are the same
 DECODE_BYTES = TOPK * EXPERT_BYTES + E * H * 2 + 65_536
 PREFILL_FLOP = PREFILL_T * TOPK * (2 * 2 * F * H + 2 * H * F) + 2 * PREFILL_T * E * H
 METRIC = "decode tok/s (bs=1) + gather_qmv HBM GB/s and % of 8 TB/s; prefill tok/s"
+WORKLOAD = "config 1: one MoE layer decode, bs=1, H4096 E128 top8 F1536 4-bit g64"
 
 
 def load_peaks():
@@ -210,8 +211,8 @@ def run_reference(args, rank, world):
               "per decode token")
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * dt / max(1, args.steps), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config 1: MoE layer decode, H4096 E128 top8 F1536 4-bit g64 (CPU sample)"},
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": WORKLOAD, "parallelism": f"host CPU, {cores} processes of the reference kernel"},
             "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -272,6 +273,19 @@ def main():
     stream = torch.cuda.Stream(device=dev)
     sp = stream.cuda_stream
     fn = L.b2q_moe_decode
+    comm = None
+    e_lo, e_local = 0, E
+    if world > 1:
+        # expert parallelism: this rank holds experts [e_lo, e_lo + e_local) of every layer
+        from b2q.ep import EPComm, expert_range, shard_layer
+
+        e_lo, e_local = expert_range(E, world, rank)
+        layers = [shard_layer(Ld, e_lo, e_local) for Ld in layers]
+        torch.cuda.empty_cache()
+        comm = EPComm(world, rank, group=pg.group.WORLD)
+        ws_bytes = L.b2q_ep_moe_decode_workspace_size(1, H, E, F, TOPK)
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+        partial = torch.empty((1, H), dtype=torch.float32, device=dev)
     argsets = []
     for i in range(n_layers):
         Ld = layers[i]
@@ -279,12 +293,22 @@ def main():
     xbase, xstride = xs.data_ptr(), H * 2
     outp, wsp = out.data_ptr(), ws.data_ptr()
 
-    def step(i):
-        j = i % n_layers
-        rc = fn(xbase + (i % N_TOKENS) * xstride, routers[j].data_ptr(), *argsets[j], outp, None, None, None,
-                1, H, E, F, TOPK, GS, 4, wsp, ws_bytes, sp)
-        if rc:
-            check(rc)
+    if comm is None:
+        def step(i):
+            j = i % n_layers
+            rc = fn(xbase + (i % N_TOKENS) * xstride, routers[j].data_ptr(), *argsets[j], outp, None, None, None,
+                    1, H, E, F, TOPK, GS, 4, wsp, ws_bytes, sp)
+            if rc:
+                check(rc)
+    else:
+        epfn, commp, pp = L.b2q_ep_moe_decode, comm.ptr, partial.data_ptr()
+
+        def step(i):
+            j = i % n_layers
+            rc = epfn(commp, xbase + (i % N_TOKENS) * xstride, routers[j].data_ptr(), *argsets[j], pp, outp, None,
+                      None, 1, H, E, F, TOPK, e_lo, e_local, GS, 4, wsp, ws_bytes, sp)
+            if rc:
+                check(rc)
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -305,7 +329,7 @@ def main():
         t = torch.tensor([ms_total], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms_total = float(t.item())
-    st = L.b2q_workspace_status(wsp, ws_bytes, sp)
+    st = L.b2q_workspace_status(wsp, ws_bytes, sp) if comm is None else 0
     if st != 0:
         raise RuntimeError(f"device-side error {st} during the timed decode loop")
     ms_step = ms_total / args.steps
@@ -314,7 +338,12 @@ def main():
     clocks = clk.summary()
 
     # ---------------- e2e through the public API ----------------
-    moe = [b2q.MoE(routers[i], layers[i], TOPK, GS) for i in range(n_layers)]
+    if comm is None:
+        moe = [b2q.MoE(routers[i], layers[i], TOPK, GS) for i in range(n_layers)]
+    else:
+        from b2q.ep import EPMoE
+
+        moe = [EPMoE(routers[i], layers[i], E, e_lo, TOPK, comm, GS) for i in range(n_layers)]
     n_e2e = 0 if args.no_e2e else min(args.steps, 3000)
     host_x = torch.empty((n_e2e + args.warmup, 1, H), dtype=torch.bfloat16).pin_memory()
     host_x.copy_(xs[: (n_e2e + args.warmup)].view(-1, 1, H).cpu())
@@ -345,24 +374,35 @@ def main():
     if not args.no_prefill:
         del moe
         xp = synth.activations((PREFILL_T, H), device=dev, seed=3)
-        pws = b2q.Workspace(L.b2q_moe_prefill_workspace_size(PREFILL_T, H, E, F, TOPK), dev)
         pout = torch.empty((PREFILL_T, H), dtype=torch.bfloat16, device=dev)
+        if comm is None:
+            pws = b2q.Workspace(L.b2q_moe_prefill_workspace_size(PREFILL_T, H, E, F, TOPK), dev)
 
-        def pstep(i):
-            j = i % n_layers
-            Ld = layers[j]
-            rc = L.b2q_moe_prefill(xp.data_ptr(), routers[j].data_ptr(),
-                                   *[Ld[k].data_ptr() for k in ("wg", "sg", "bg", "wu", "su", "bu", "wd", "sd", "bd")],
-                                   pout.data_ptr(), None, None, PREFILL_T, H, E, F, TOPK, GS, 4, pws.ptr(),
-                                   pws.buf.numel(), sp)
-            if rc:
-                check(rc)
+            def pstep(i):
+                j = i % n_layers
+                rc = L.b2q_moe_prefill(xp.data_ptr(), routers[j].data_ptr(), *argsets[j], pout.data_ptr(), None,
+                                       None, PREFILL_T, H, E, F, TOPK, GS, 4, pws.ptr(), pws.buf.numel(), sp)
+                if rc:
+                    check(rc)
+        else:
+            pws = b2q.Workspace(L.b2q_ep_moe_prefill_workspace_size(PREFILL_T, H, E, F, TOPK), dev)
+            ppart = torch.empty((PREFILL_T, H), dtype=torch.float32, device=dev)
+
+            def pstep(i):
+                j = i % n_layers
+                rc = L.b2q_ep_moe_prefill(comm.ptr, xp.data_ptr(), routers[j].data_ptr(), *argsets[j],
+                                          ppart.data_ptr(), pout.data_ptr(), None, None, PREFILL_T, H, E, F, TOPK,
+                                          e_lo, e_local, GS, 4, pws.ptr(), pws.buf.numel(), sp)
+                if rc:
+                    check(rc)
 
         with torch.cuda.stream(stream):
             for i in range(3):
                 pstep(i)
         torch.cuda.synchronize(dev)
         psteps = 10
+        if pg:
+            pg.barrier()
         p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         p0.record(stream)
         for i in range(psteps):
@@ -370,6 +410,10 @@ def main():
         p1.record(stream)
         torch.cuda.synchronize(dev)
         pms = p0.elapsed_time(p1) / psteps
+        if pg:
+            t = torch.tensor([pms], device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            pms = float(t.item())
         tflops = PREFILL_FLOP / (pms * 1e-3) / 1e12
         prefill = {"workload": "config 2: MoE layer prefill, 2048 tokens", "tok_s": PREFILL_T * 1000.0 / pms,
                    "ms_per_layer": pms, "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc_peak,
@@ -377,6 +421,9 @@ def main():
                                                      "peak_kind": peak_kind,
                                                      "traffic": load_traffic("moe_prefill_c2.json")}}
 
+    if comm is not None:
+        torch.cuda.synchronize(dev)
+        comm.close()
     if rank != 0:
         if pg:
             pg.destroy_process_group()
@@ -397,8 +444,10 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded; random-init 4-bit experts)",
-        "config": {"workload": "config 1: one MoE layer decode, bs=1, H4096 E128 top8 F1536 4-bit g64",
-                   "parallelism": "single GPU" if world == 1 else f"ep{world}",
+        "config": {"workload": WORKLOAD,
+                   "parallelism": "single GPU" if world == 1 else
+                   f"ep{world}: experts sharded {E}/{world} per GPU, router replicated, one NCCL all-reduce of "
+                   f"the fp32 hidden vector per layer",
                    "l2": f"cold: {n_layers} rotating layers ({n_layers * E * EXPERT_BYTES / 1e9:.1f} GB experts) "
                          f"and a fresh token per step"},
         "gather_qmv_hbm_gbs": achieved,
@@ -408,9 +457,10 @@ def main():
                      "bytes_per_launch": DECODE_BYTES,
                      "traffic": load_traffic("moe_decode_c1.json")},
         "e2e": ({"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
-                 "steps": n_e2e, "api": "b2q.MoE.__call__ (pinned host token in, pinned host output back each step)"}
+                 "steps": n_e2e, "api": ("b2q.MoE.__call__" if comm is None else "b2q.ep.EPMoE.__call__")
+                 + " (pinned host token in, pinned host output back each step)"}
                 if n_e2e else None),
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (1 if world == 1 else 10),
         "clocks": clocks,
         "prefill": prefill,
         "cpu_baseline": cpu,
