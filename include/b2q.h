@@ -210,6 +210,25 @@ B2Q_API int b2q_ep_moe_prefill(void* comm, const uint16_t* x, const uint16_t* wr
                    int T, int H, int E, int F, int k, int e_lo, int e_local,
                    int group_size, int bits, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- checkpoint reading (per-layer packed-weight binding) ------------------ */
+
+/* Replaces the reference's safetensors header reader
+ * (Sources/MLXFastCore/Safetensors.swift:75-180) for binding a layer's
+ * stacked expert tensors (Runner/FastModel/TrackFastModel.swift:470-540).
+ * b2q_st_open maps the file read-only and checks the header (8-byte
+ * little-endian length, at most 100,000,000 bytes, a JSON object of
+ * {dtype, shape, data_offsets}, offsets ordered and inside the data section).
+ * b2q_st_read copies a tensor's stored bytes to host memory (to_device == 0)
+ * or to device memory (copy on `stream`, synchronised before returning). */
+B2Q_API int b2q_st_open(const char* path, void** handle);
+B2Q_API int b2q_st_close(void* handle);
+B2Q_API int b2q_st_count(void* handle);
+B2Q_API int b2q_st_name(void* handle, int i, char* buf, size_t buf_bytes);
+B2Q_API int b2q_st_info(void* handle, const char* name, char* dtype, size_t dtype_bytes,
+                int64_t* shape, int max_dims, int* ndim, uint64_t* nbytes);
+B2Q_API int b2q_st_read(void* handle, const char* name, void* dst, size_t dst_bytes,
+                int to_device, void* stream);
+
 /* One prefill MoE layer over T tokens: router logits, route, stable sort of the
  * T*k assignments by expert (TrackPrefillSort.swift:84-201), gate|up + SwiGLU
  * gather GEMM and down gather GEMM on the tensor cores over expert-aligned row

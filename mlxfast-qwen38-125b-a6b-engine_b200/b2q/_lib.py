@@ -53,6 +53,12 @@ SIGNATURES = {
     "b2q_ep_moe_decode": (_I, [_P] * 16 + [_I] * 9 + [_P, _SZ, _P]),
     "b2q_ep_moe_prefill_workspace_size": (_SZ, [_I] * 5),
     "b2q_ep_moe_prefill": (_I, [_P] * 16 + [_I] * 9 + [_P, _SZ, _P]),
+    "b2q_st_open": (_I, [ctypes.c_char_p, _P]),
+    "b2q_st_close": (_I, [_P]),
+    "b2q_st_count": (_I, [_P]),
+    "b2q_st_name": (_I, [_P, _I, ctypes.c_char_p, _SZ]),
+    "b2q_st_info": (_I, [_P, ctypes.c_char_p, ctypes.c_char_p, _SZ, _P, _I, _P, _P]),
+    "b2q_st_read": (_I, [_P, ctypes.c_char_p, _P, _SZ, _I, _P]),
     "b2q_workspace_reset": (_I, [_P, _SZ, _P]),
     "b2q_workspace_status": (_I, [_P, _SZ, _P]),
     "b2q_selftest_wait_timeout": (_I, [_P, _SZ, _LL, _P]),
