@@ -12,6 +12,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "decode1.cuh"
 #include "decode_ws.hpp"
 #include "engine.cuh"
 #include "host.hpp"
@@ -58,6 +59,10 @@ static int gather_impl(const char* fn, const uint16_t* x, const uint32_t* w, con
   if (!x || !w || !s || !b || !y) return set_error(B2Q_EINVAL, "%s: null pointer", fn);
   if (!aligned16(x)) return set_error(B2Q_EINVAL, "%s: x must be 16-byte aligned", fn);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // one row of x times one weight matrix: the single-column streaming kernel
+  if (M == 1 && batch == 1 && !lhs && !rhs && n_x >= 1 && n_w >= 1 && d1_qmv_eligible(N, K, gs, x, w, s, b) &&
+      aligned16(y))
+    return d1_qmv(x, w, s, b, y, N, K, gs, st);
   const bool engine_ok = M <= eng::MAX_COLS && engine_k_ok(K, gs) && aligned16(w) && aligned16(s) &&
                          aligned16(b);
   if (engine_ok) {
@@ -211,6 +216,12 @@ int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, co
   if (!workspace || workspace_bytes < ws.bytes || !aligned16(workspace))
     return set_error(B2Q_EINVAL, "moe_decode: workspace of %zu bytes needed", ws.bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const void* ptrs[] = {x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd};
+  bool all_aligned = true;
+  for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
+  if (S == 1 && all_aligned && d1_moe_eligible(H, E, F, k, group_size))
+    return d1_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size,
+                         &ws.hdr->error, ws.hdr->counters, ws.logits, ws.act, st);
   if (S == 1) {
     eng::Params p;
     base_params(p, eng::MODE_FUSED, group_size);

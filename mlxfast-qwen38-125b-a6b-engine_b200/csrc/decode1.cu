@@ -1,0 +1,914 @@
+// decode1.cu -- single-column streaming products: qmv for one row of x
+// (M = 1) and the fused one-token MoE decode layer.
+//
+// Reference operators (paths relative to the reference project):
+//   qmv_fast_impl / qdot       Vendor/mlx-swift/Source/Cmlx/mlx/mlx/backend/metal/kernels/quantized.h:28-105,191-290,757-822
+//   gateUpAct / downCombine    Runner/FastModel/TrackFastMoE.swift:1192-1590
+//   route (top-k + softmax)    Runner/FastModel/TrackFastMoE.swift:767-911
+//
+// Organisation (one persistent CTA per SM, 8 consumer warps + 1 producer warp):
+//  * A unit is 16 weight rows (P: 8 rows, Q: 8 rows; for gate|up P are gate
+//    rows and Q the up rows of the same 8 outputs) over the whole reduction
+//    length. It is split into T tasks of 1024 reduction values (4 x 128-byte
+//    row pieces); T consecutive consumer warps take the T tasks of a unit and
+//    the CTA runs 8 / T units side by side.
+//  * Every consumer warp owns two stage slots; the producer warp fills them in
+//    task order with TMA tensor copies (an 8-row weight block P, an 8-row
+//    block Q, and their scale / bias rows), one full / empty mbarrier pair
+//    per slot. A warp processes 4 pieces per wait.
+//  * A task's partial row sums go to shared memory; the last of the T warps
+//    (a shared-memory arrival count) adds them in task order and finishes
+//    the unit: bf16 store (qmv), SwiGLU into the activation rows (gate|up),
+//    or the weighted expert combine (down). No finisher warp, no per-unit
+//    handshake beyond that count.
+//  * Fused decode: router rows (CTA b takes experts b, b + grid, ...) -> a grid
+//    counter -> every CTA computes the same top-k -> gate|up units -> a grid
+//    counter of finished units -> activation staging -> down units (8 output
+//    rows x 8 slots: 4 slot pairs x 2 halves of F = 8 tasks). The producer
+//    starts the down weight copies before that counter completes; only the
+//    consumers wait for it. The last CTA out re-arms the counters.
+//  * The dot products use the engine's arithmetic: nibbles OR-ed into fp16
+//    1024.0 give 1024 + q (and 1024 + 16 q from the upper nibble of a byte);
+//    activations are staged as fp16 scaled by a power of two per column so
+//    that max |x| * 2^e lies in [1024, 2048); mma.sync m16n8k16 (fp16 x fp16
+//    -> fp32) per 16 weight rows; per group: s * (D - xoff) + b * sum(x),
+//    then the power of two is undone.
+// All waits are bounded; a wait that runs out records B2Q_ETIMEOUT and raises
+// an abort flag; every role then runs to the end of its loops without
+// waiting or computing, so all barriers still see every thread.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "decode1.cuh"
+#include "host.hpp"
+#include "tc.cuh"
+#include "tmap.hpp"
+
+namespace b2q {
+namespace d1 {
+
+constexpr int NCW = 8;                  // consumer warps
+constexpr int NCT = NCW * 32;
+constexpr int NTH = NCT + 32;           // + producer warp
+constexpr int SPW = 2;                  // stage slots per consumer warp
+constexpr int NSLOT = NCW * SPW;
+constexpr int SLOT = 10240;             // bytes per slot
+constexpr int TK = 1024;                // reduction values per gate|up / qmv task
+constexpr int RR = 4;                   // reduction-slot ring per warp group
+constexpr int MAXK = 8;                 // routed slots (fused decode)
+
+// tensor-map slots
+enum : int { MW = 0, MS = 1, MB = 2, MWG = 0, MSG = 1, MBG = 2, MWU = 3, MSU = 4, MBU = 5, MWD = 6, MSD = 7, MBD = 8 };
+
+// ---------------------------------------------------------------------------
+// shared-memory plan (byte offsets from the 1024-aligned base)
+// ---------------------------------------------------------------------------
+struct Plan {
+  int slots;     // NSLOT x SLOT
+  int x;         // staged activation column(s) of the gate|up / qmv family
+  int xs;        // its group sums
+  int act;       // staged activation columns of the down family (fused)
+  int acts;
+  int red;       // task partials
+  int misc;      // barriers, counters, routing
+  int bytes;
+  int XS1, XS2;  // activation column strides
+};
+
+// Activation staging: stage_cols writes `ncols` columns of K values as scaled,
+// permuted fp16 chunks (x0 S, x4 S) (x1 S/16, x5 S/16) (x2 S, x6 S)
+// (x3 S/16, x7 S/16) and per group: xs = sum of x S, xo = 1024 * sum_even +
+// 1024 * sum_odd / 16 (the offset the nibble decode adds), inv = 1 / S.
+// Region layout: xs [cap][G], xo [cap][G], inv [MAXK], colmax [MAXK].
+__device__ __forceinline__ float* c_xs(float* sums, int G, int col) { return sums + (size_t)col * G; }
+__device__ __forceinline__ float* c_xo(float* sums, int cap, int G, int col) { return sums + (size_t)(cap + col) * G; }
+__device__ __forceinline__ float* c_inv(float* sums, int cap, int G) { return sums + (size_t)2 * cap * G; }
+
+__device__ __forceinline__ uint32_t h2pack(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float lbf(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float hbf(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// All NCT consumer threads call this (named barrier 1).
+__device__ void stage_cols(uint8_t* dst, float* sums, int cap, int XS, const uint16_t* const* rows, int ncols, int K,
+                           int gs, bool coherent) {
+  const int tid = threadIdx.x;
+  const int nch = K / 8, G = K / gs;
+  float* inv = c_inv(sums, cap, G);
+  unsigned* colmax = reinterpret_cast<unsigned*>(inv + MAXK);
+  if (tid < MAXK) colmax[tid] = 0u;
+  named_bar_sync(1, NCT);
+  for (int q = tid; q < ncols * nch; q += NCT) {
+    const int col = q / nch, ch = q % nch;
+    const uint4* src = reinterpret_cast<const uint4*>(rows[col] + (size_t)ch * 8);
+    const uint4 v = coherent ? __ldcg(src) : __ldg(src);
+    unsigned m = max(max(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), max(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
+    m = max(m & 0xffffu, m >> 16) << 16;
+    if (m > 0x7f800000u) m = 0x7f800000u;
+    atomicMax(&colmax[col], m);
+  }
+  named_bar_sync(1, NCT);
+  if (tid < ncols) {
+    const float mx = __uint_as_float(colmax[tid]);
+    int e = 0;
+    if (mx > 0.0f && mx < INFINITY) {
+      int E2;
+      frexpf(mx, &E2);
+      e = 11 - E2;
+    }
+    inv[tid] = ldexpf(1.0f, -e);
+    colmax[tid] = (unsigned)(e + 1000);
+  }
+  named_bar_sync(1, NCT);
+  for (int q = tid; q < ncols * nch; q += NCT) {
+    const int col = q / nch, ch = q % nch;
+    const uint4* src = reinterpret_cast<const uint4*>(rows[col] + (size_t)ch * 8);
+    const uint4 v = coherent ? __ldcg(src) : __ldg(src);
+    const int e = (int)colmax[col] - 1000;
+    const float S = ldexpf(1.0f, e), S16 = ldexpf(1.0f, e - 4);
+    uint4 o;
+    o.x = h2pack(lbf(v.x) * S, lbf(v.z) * S);
+    o.y = h2pack(hbf(v.x) * S16, hbf(v.z) * S16);
+    o.z = h2pack(lbf(v.y) * S, lbf(v.w) * S);
+    o.w = h2pack(hbf(v.y) * S16, hbf(v.w) * S16);
+    *reinterpret_cast<uint4*>(dst + (size_t)col * XS + (size_t)ch * 16) = o;
+  }
+  named_bar_sync(1, NCT);
+  for (int q = tid; q < ncols * G; q += NCT) {
+    const int col = q / G, g = q % G;
+    const uint8_t* base = dst + (size_t)col * XS + (size_t)g * (gs / 8) * 16;
+    float se = 0.0f, so = 0.0f;
+    for (int ch = 0; ch < gs / 8; ++ch) {
+      const uint4 v = *reinterpret_cast<const uint4*>(base + ch * 16);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+      se += ((a.x + c.x) + a.y) + c.y;
+      so += ((b.x + d.x) + b.y) + d.y;
+    }
+    c_xs(sums, G, col)[g] = se + 16.0f * so;
+    c_xo(sums, cap, G, col)[g] = 1024.0f * se + 1024.0f * so;
+  }
+  named_bar_sync(1, NCT);
+}
+
+// ---------------------------------------------------------------------------
+// consumers: one task = npc 128-byte pieces of the 16 rows
+// ---------------------------------------------------------------------------
+// Slot layout: [P: npc atoms of 1024 bytes][Q: npc atoms][sP][bP][sQ][bQ], a
+// meta block = 8 rows x GB groups of bf16 (row stride GB * 2). Atom j holds
+// piece j of the 8 rows, 16-byte unit u of row r at unit position u ^ r.
+// Lane (r = lane / 4, c = lane % 4) takes word 4u + c of row r of P and of Q
+// (MMA rows r and r + 8).
+__device__ __forceinline__ void word_mma(const uint8_t* wp, int qoff, const uint4 xv, bool first, float (&d)[4]) {
+  const uint32_t W0 = *reinterpret_cast<const uint32_t*>(wp);
+  const uint32_t W8 = *reinterpret_cast<const uint32_t*>(wp + qoff);
+  uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
+  decode_word_h(W0, p0, p1, p2, p3);
+  decode_word_h(W8, q0, q1, q2, q3);
+  if (first)
+    mma_f16_16816_zero(d, p0, q0, p1, q1, xv.x, xv.y);
+  else
+    mma_f16_16816(d, p0, q0, p1, q1, xv.x, xv.y);
+  mma_f16_16816(d, p2, q2, p3, q3, xv.z, xv.w);
+}
+
+// Single activation column (qmv, gate|up): the quad lanes finish groups c of
+// each batch of NB groups; acc[0] row r (P), acc[2] row r + 8 (Q).
+// gb0: group index inside the slot's meta rows of the task's first group;
+// gabs0: absolute group index (for xs / xo) of the task's first group.
+template <int WPT>
+__device__ __forceinline__ void task_col(const uint8_t* st, int npc, int GB, int gb0, int gabs0,
+                                         const uint8_t* xc, const float* xs, const float* xo, float (&acc)[4]) {
+  constexpr int GPC = 8 / WPT;
+  constexpr int NB = GPC < 4 ? GPC : 4;
+  const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+  const int qoff = npc * 1024;
+  const uint8_t* mP = st + 2 * qoff;
+  const int mblk = 8 * GB * 2;
+  const uint8_t* wl = st + r * 128 + c * 4;
+  const uint8_t* xl = xc + c * 16;
+  for (int pc = 0; pc < npc; ++pc) {
+    const uint8_t* pw = wl + pc * 1024;
+    const uint8_t* px = xl + pc * 512;
+#pragma unroll
+    for (int b0 = 0; b0 < GPC; b0 += NB) {
+      float D[NB][4];
+#pragma unroll
+      for (int j = 0; j < WPT; ++j) {
+#pragma unroll
+        for (int gi = 0; gi < NB; ++gi) {
+          const int u = (b0 + gi) * WPT + j;
+          word_mma(pw + ((u ^ r) << 4), qoff, *reinterpret_cast<const uint4*>(px + u * 64), j == 0, D[gi]);
+        }
+      }
+      float e0 = D[0][0], e2 = D[0][2];
+#pragma unroll
+      for (int gi = 1; gi < NB; ++gi) {
+        e0 = (c == gi) ? D[gi][0] : e0;
+        e2 = (c == gi) ? D[gi][2] : e2;
+      }
+      const int gl = pc * GPC + b0 + (c < NB ? c : NB - 1);  // group inside the task
+      const int mo = r * GB * 2 + (gb0 + gl) * 2;
+      const float sP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mo));
+      const float bP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mblk + mo));
+      const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(mP + 2 * mblk + mo));
+      const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(mP + 3 * mblk + mo));
+      const float xa = xs[gabs0 + gl], xoa = xo[gabs0 + gl];
+      if (c < NB) {
+        acc[0] = fmaf(sP, e0 - xoa, fmaf(bP, xa, acc[0]));
+        acc[2] = fmaf(sQ, e2 - xoa, fmaf(bQ, xa, acc[2]));
+      }
+    }
+  }
+}
+
+// Down pair: P = slot 2 * pair, Q = slot 2 * pair + 1 against the 8 staged
+// activation columns (column n = slot n). Lanes c == pair own acc[0] (P) and
+// acc[3] (Q).
+template <int WPT>
+__device__ __forceinline__ void task_pair(const uint8_t* st, int npc, int GB, int gabs0, const uint8_t* acol0, int XS,
+                                          const float* xsP, const float* xoP, const float* xsQ, const float* xoQ,
+                                          int pair, float (&acc)[4]) {
+  constexpr int GPC = 8 / WPT;
+  const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+  const int qoff = npc * 1024;
+  const uint8_t* mP = st + 2 * qoff;
+  const int mblk = 8 * GB * 2;
+  const uint8_t* wl = st + r * 128 + c * 4;
+  const uint8_t* xl = acol0 + (size_t)r * XS + c * 16;  // column r = slot r
+  for (int pc = 0; pc < npc; ++pc) {
+    const uint8_t* pw = wl + pc * 1024;
+    const uint8_t* px = xl + pc * 512;
+#pragma unroll
+    for (int gi = 0; gi < GPC; ++gi) {
+      float D[4];
+#pragma unroll
+      for (int j = 0; j < WPT; ++j) {
+        const int u = gi * WPT + j;
+        word_mma(pw + ((u ^ r) << 4), qoff, *reinterpret_cast<const uint4*>(px + u * 64), j == 0, D);
+      }
+      const int gl = pc * GPC + gi;  // group inside the task
+      const int ga = gabs0 + gl;     // absolute group: the meta rows hold the full row
+      const int mo = r * GB * 2 + ga * 2;
+      const float sP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mo));
+      const float bP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mblk + mo));
+      const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(mP + 2 * mblk + mo));
+      const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(mP + 3 * mblk + mo));
+      if (c == pair) {
+        acc[0] = fmaf(sP, D[0] - xoP[ga], fmaf(bP, xsP[ga], acc[0]));
+        acc[3] = fmaf(sQ, D[3] - xoQ[ga], fmaf(bQ, xsQ[ga], acc[3]));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// routing: top-k (largest first, ties to the lower index) + softmax over k
+// (Runner/FastModel/TrackFastMoE.swift:767-911), one warp, logits read
+// coherently (other CTAs wrote them)
+// ---------------------------------------------------------------------------
+__device__ void warp_route_d1(const float* lr, int E, int k, uint32_t* sidx, float* sw) {
+  const int lane = threadIdx.x & 31;
+  float v[32];
+  bool taken[32];
+  const int EP = (E + 31) / 32;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int e = lane + 32 * j;
+    const bool ok = j < EP && e < E;
+    v[j] = ok ? __ldcg(lr + e) : -INFINITY;
+    taken[j] = !ok;
+  }
+  float selv = -INFINITY;
+  uint32_t seli = 0xffffffffu;
+  for (int kk = 0; kk < k; ++kk) {
+    float bv = -INFINITY;
+    int bj = -1;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (!taken[j] && v[j] > bv) {
+        bv = v[j];
+        bj = j;
+      }
+    float gmax = bv;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
+    uint32_t cand = (bj >= 0 && bv == gmax) ? (uint32_t)(lane + 32 * bj) : 0xffffffffu;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, off));
+    if (lane == kk) {
+      selv = gmax;
+      seli = cand;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j == bj && cand == (uint32_t)(lane + 32 * bj)) taken[j] = true;
+  }
+  // softmax over the k selected values, per-lane partials of 4 (slot order)
+  float mx = (lane < k) ? selv : -INFINITY;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float ex = (lane < k) ? expf(selv - mx) : 0.0f;
+  float part = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float t = __shfl_sync(0xffffffffu, ex, (4 * lane + i) & 31);
+    part += (lane < 8) ? t : 0.0f;
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+  const float inv = 1.0f / part;
+  if (lane < k) {
+    sidx[lane] = seli;
+    sw[lane] = ex * inv;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar,
+                                     uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+struct Shape {
+  int T;      // tasks per unit
+  int units;  // units of the phase (grid-wide)
+};
+
+template <int WPT, int MODE>
+__global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t* slots = smem + p.off_slots;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_misc);
+  uint64_t* empty = full + NSLOT;
+  unsigned* cnt = reinterpret_cast<unsigned*>(empty + NSLOT);  // [8 groups][RR] arrival counts
+  unsigned* gen = cnt + 8 * RR;                                // [8 groups][RR] consumed uses
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gen + 8 * RR);
+  uint32_t* sidx = reinterpret_cast<uint32_t*>(const_cast<int*>(abort_flag) + 4);
+  float* sw = reinterpret_cast<float*>(sidx + MAXK);
+  float* rsum = sw + MAXK;  // [NCW]
+  int* lastfill = reinterpret_cast<int*>(rsum + NCW);  // [NSLOT] ordinal of the last fill issued per slot
+  float* red = reinterpret_cast<float*>(smem + p.off_red);
+  const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
+  const bool fused = MODE == D1_FUSED;
+  const int G1 = p.K1 / p.gs, G2 = fused ? p.F / p.gs : 0;
+
+  if (tid == 0) {
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 8 * RR; ++i) cnt[i] = gen[i] = 0;
+    for (int i = 0; i < NSLOT; ++i) lastfill[i] = -1;
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // phase geometry
+  const Shape ph1{p.K1 / TK, fused ? p.k * (p.F / 8) : p.N / 16};
+  const Shape ph2{8, fused ? p.H / 8 : 0};
+  auto local_units = [&](int units) { return units > (int)blockIdx.x ? (units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0; };
+  const int nl1 = local_units(ph1.units), nl2 = local_units(ph2.units);
+  const int G1grp = NCW / ph1.T;  // units side by side in phase 1
+  const int rounds1 = (nl1 + G1grp - 1) / G1grp, rounds2 = nl2;
+
+  if (warp == NCW) {
+    // ------------------------------ producer ------------------------------
+    if (fused) named_bar_sync(2, NTH);  // routing done
+    const uint64_t pol = policy_evict_first();
+    if (tc::elect_one())
+      for (int i = 0; i < (fused ? 9 : 3); ++i)
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.map[i])) : "memory");
+    __syncwarp();
+    // n: the warp's task ordinal (its round in phase 1; then phase-1 count + round)
+    auto issue = [&](int w, int n, bool valid, int rowP, int rowQ, int pieceP, int npc, int mwP, int msP, int mbP,
+                     int mwQ, int msQ, int mbQ, int gcol, int GB) -> bool {
+      const int si = w * SPW + (n % SPW);
+      if (n >= SPW && !__all_sync(0xffffffffu, tc::wait(&empty[si], ((n / SPW) - 1) & 1, deadline, abort_flag))) {
+        if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
+      if (tc::elect_one()) {
+        uint8_t* st = slots + (size_t)si * SLOT;
+        lastfill[si] = n;
+        if (!valid || *abort_flag) {
+          mbar_arrive_expect_tx(&full[si], 0u);
+        } else {
+          const uint32_t mb = 8u * (uint32_t)GB * 2u;
+          mbar_arrive_expect_tx(&full[si], 2u * (uint32_t)npc * 1024u + 4u * mb);
+          tma3(st, &p.map[mwP], 0, rowP, pieceP, &full[si], pol);
+          tma3(st + npc * 1024, &p.map[mwQ], 0, rowQ, pieceP, &full[si], pol);
+          uint8_t* m = st + 2 * npc * 1024;
+          tc::tma_load_2d(m, &p.map[msP], gcol, rowP, &full[si], pol);
+          tc::tma_load_2d(m + mb, &p.map[mbP], gcol, rowP, &full[si], pol);
+          tc::tma_load_2d(m + 2 * mb, &p.map[msQ], gcol, rowQ, &full[si], pol);
+          tc::tma_load_2d(m + 3 * mb, &p.map[mbQ], gcol, rowQ, &full[si], pol);
+        }
+      }
+      __syncwarp();
+      return true;
+    };
+    auto p1_count = [&](int w) {  // phase-1 tasks of warp w
+      const int gi = w / ph1.T;
+      return nl1 > gi ? (nl1 - gi + G1grp - 1) / G1grp : 0;
+    };
+    bool ok = true;
+    // phase 1: qmv rows or gate|up rows, tasks of TK values (4 pieces)
+    const int GB1 = TK / p.gs;
+    for (int j = 0; ok && j < rounds1; ++j)
+      for (int gi = 0; ok && gi < G1grp; ++gi) {
+        const int li = j * G1grp + gi;
+        if (li >= nl1) break;
+        const int u = blockIdx.x + li * gridDim.x;
+        int rowP, rowQ;
+        if (fused) {
+          const int z = u / (p.F / 8), rb = u % (p.F / 8);
+          rowP = rowQ = (int)(sidx[z] * (uint32_t)p.F) + rb * 8;
+        } else {
+          rowP = u * 16;
+          rowQ = rowP + 8;
+        }
+        for (int t = 0; ok && t < ph1.T; ++t) {
+          const int w = gi * ph1.T + t;
+          ok = fused ? issue(w, j, true, rowP, rowQ, t * (TK / 256), TK / 256, MWG, MSG, MBG, MWU, MSU, MBU, t * GB1,
+                             GB1)
+                     : issue(w, j, true, rowP, rowQ, t * (TK / 256), TK / 256, MW, MS, MB, MW, MS, MB, t * GB1, GB1);
+        }
+      }
+    // phase 2 (fused): down rows, 4 slot pairs x 2 halves of F; meta rows are whole
+    if (fused) {
+      const int npc2 = p.F / 2 / 256;
+      for (int j = 0; ok && j < rounds2; ++j) {
+        const int u = blockIdx.x + j * gridDim.x;
+        for (int t = 0; ok && t < 8; ++t) {
+          const int pair = t >> 1, half = t & 1;
+          const int s0 = 2 * pair, s1 = 2 * pair + 1;
+          const bool v0 = s0 < p.k, v1 = s1 < p.k;
+          const uint32_t e0 = v0 ? sidx[s0] : 0u, e1 = v1 ? sidx[s1] : e0;
+          ok = issue(t, p1_count(t) + j, v0, (int)(e0 * (uint32_t)p.H) + u * 8, (int)(e1 * (uint32_t)p.H) + u * 8,
+                     half * npc2,
+                     npc2, MWD, MSD, MBD, MWD, MSD, MBD, 0, G2);
+        }
+      }
+    }
+    // let every copy issued land before the CTA may exit
+    const uint64_t dl = globaltimer() + 200000000ull;
+    __syncwarp();
+    if (lane < NSLOT && lastfill[lane] >= 0) tc::wait_until(&full[lane], (lastfill[lane] / SPW) & 1, dl);
+  } else {
+    // ------------------------------ consumers ------------------------------
+    uint8_t* xbuf = smem + p.off_x;
+    float* xsum = reinterpret_cast<float*>(smem + p.off_xs);
+    uint8_t* abuf = smem + p.off_act;
+    float* asum = reinterpret_cast<float*>(smem + p.off_acts);
+    const int r = lane >> 2, c = lane & 3;
+
+    if (fused) {
+      // router rows of this CTA, then a grid-wide count of finished rows
+      const int nvec = p.H / 8;
+      int rows_done = 0;
+      for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
+        float part = 0.0f;
+        for (int v = tid; v < nvec; v += NCT) {
+          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(p.x) + v);
+          const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.wr + (size_t)e * p.H) + v);
+          part += lbf(xv.x) * lbf(wv.x) + hbf(xv.x) * hbf(wv.x);
+          part += lbf(xv.y) * lbf(wv.y) + hbf(xv.y) * hbf(wv.y);
+          part += lbf(xv.z) * lbf(wv.z) + hbf(xv.z) * hbf(wv.z);
+          part += lbf(xv.w) * lbf(wv.w) + hbf(xv.w) * hbf(wv.w);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+        if (lane == 0) rsum[warp] = part;
+        named_bar_sync(1, NCT);
+        if (tid == 0) {
+          float lg = 0.0f;
+          for (int w = 0; w < NCW; ++w) lg += rsum[w];
+          p.ws_logits[e] = lg;
+        }
+        named_bar_sync(1, NCT);
+        ++rows_done;
+      }
+      if (tid == 0) {
+        if (rows_done) {
+          __threadfence();
+          atomicAdd(&p.counters[0], (unsigned)rows_done);
+        }
+        if (!wait_counter_geq(&p.counters[0], (unsigned)p.E, deadline, abort_flag)) {
+          record_error(p.err, B2Q_ETIMEOUT);
+          *abort_flag = 1;
+        }
+        __threadfence();
+      }
+      named_bar_sync(1, NCT);
+      if (warp == 0) {
+        if (!*abort_flag) {
+          warp_route_d1(p.ws_logits, p.E, p.k, sidx, sw);
+        } else if (lane < p.k) {
+          sidx[lane] = 0;
+          sw[lane] = 0.0f;
+        }
+        __syncwarp();
+        if (blockIdx.x == 0 && lane < p.k) {
+          if (p.idx_out) p.idx_out[lane] = sidx[lane];
+          if (p.w_out) p.w_out[lane] = sw[lane];
+        }
+        if (blockIdx.x == 0 && p.logits_out)
+          for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
+      }
+      named_bar_sync(2, NTH);  // releases the producer
+    }
+    {
+      const uint16_t* rows[1] = {p.x};
+      stage_cols(xbuf, xsum, 1, p.XS1, rows, 1, p.K1, p.gs, false);
+    }
+    const float* xs1 = c_xs(xsum, G1, 0);
+    const float* xo1 = c_xo(xsum, 1, G1, 0);
+    const float inv1 = c_inv(xsum, 1, G1)[0];
+
+    // this warp's slot ring
+    int n = 0;
+    auto take = [&](int& si) -> bool {
+      si = warp * SPW + (n % SPW);
+      const bool got = __all_sync(0xffffffffu, tc::wait(&full[si], (n / SPW) & 1, deadline, abort_flag));
+      if (!got && !*abort_flag) {
+        record_error(p.err, B2Q_ETIMEOUT);
+        *abort_flag = 1;
+      }
+      return got && !*abort_flag;
+    };
+    auto give = [&](int si) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[si]);
+      ++n;
+    };
+    // Reduction through shared memory: returns true in the warp that arrived last.
+    // slotf: the unit's partial rows [T][16] (or [8][16] for down).
+    auto arrive_last = [&](int grp, int use, int T) -> bool {
+      unsigned* cn = cnt + grp * RR + (use % RR);
+      unsigned old = 0;
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        old = atomicAdd(cn, 1u);
+      }
+      old = __shfl_sync(0xffffffffu, old, 0);
+      const bool last = old == (unsigned)(T - 1);
+      if (last) __threadfence_block();
+      return last;
+    };
+    auto release_use = [&](int grp, int use) {
+      __syncwarp();
+      if (lane == 0) {
+        cnt[grp * RR + (use % RR)] = 0;
+        __threadfence_block();
+        atomicAdd(&gen[grp * RR + (use % RR)], 1u);
+      }
+      __syncwarp();
+    };
+    // writers wait until the previous use of the reduction slot was consumed
+    auto slot_free = [&](int grp, int use) {
+      if (use < RR) return;
+      const unsigned want = (unsigned)(use / RR);
+      if (lane == 0) {
+        volatile unsigned* g = &gen[grp * RR + (use % RR)];
+        while (*g < want && !*abort_flag) {
+          if (globaltimer() > deadline) {
+            record_error(p.err, B2Q_ETIMEOUT);
+            *abort_flag = 1;
+          }
+        }
+      }
+      __syncwarp();
+    };
+
+    // ---------------- phase 1 ----------------
+    {
+      const int T = ph1.T, grp = warp / T, t = warp % T;
+      const int GB1 = TK / p.gs;
+      for (int j = 0; j < rounds1; ++j) {
+        const int li = j * G1grp + grp;
+        if (li >= nl1) break;
+        const int u = blockIdx.x + li * gridDim.x;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        int si;
+        if (take(si)) {
+          const uint8_t* st = slots + (size_t)si * SLOT;
+          task_col<WPT>(st, 4, GB1, 0, t * GB1, xbuf + (size_t)t * (TK / 8) * 16, xs1, xo1, acc);
+        }
+        give(si);
+        // the four lanes of a quad hold different groups: add them
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
+        acc[2] += __shfl_xor_sync(0xffffffffu, acc[2], 1);
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 2);
+        acc[2] += __shfl_xor_sync(0xffffffffu, acc[2], 2);
+        float* rp = red + ((size_t)(grp * RR + (j % RR)) * 8 + t) * 16;  // [grp][RR][T<=8][16]
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) continue;
+        slot_free(grp, j);
+        if (c == 0) {
+          rp[r] = acc[0];
+          rp[r + 8] = acc[2];
+        }
+        if (!arrive_last(grp, j, T)) continue;
+        // last warp of the unit: rows r (P) and r + 8 (Q) in task order
+        const float* rbuf = red + (size_t)(grp * RR + (j % RR)) * 8 * 16;
+        if (lane < 16) {
+          float tot = 0.0f;
+          for (int q = 0; q < T; ++q) tot += rbuf[q * 16 + lane];
+          tot *= inv1;
+          if (fused) {
+            // lanes 0..7: gate row f = rb*8 + lane and its up row (lane + 8)
+            const float up = __shfl_sync(0x0000ffffu, tot, lane + 8, 16);
+            if (lane < 8) {
+              const int z = u / (p.F / 8), rbk = u % (p.F / 8);
+              p.ws_act[(size_t)z * p.F + rbk * 8 + lane] = swiglu_bf16(f2bf(tot), f2bf(up));
+            }
+          } else {
+            p.y[(size_t)u * 16 + lane] = f2bf(tot);
+          }
+        }
+        release_use(grp, j);
+        if (fused && lane == 0) {
+          __threadfence();
+          atomicAdd(&p.counters[1], 1u);
+        }
+      }
+    }
+
+    // ---------------- phase 2 (fused): down + weighted combine ----------------
+    if (fused) {
+      // every gate|up unit of the grid must have published its activations
+      if (tid == 0) {
+        if (!*abort_flag && !wait_counter_geq(&p.counters[1], (unsigned)ph1.units, deadline, abort_flag)) {
+          record_error(p.err, B2Q_ETIMEOUT);
+          *abort_flag = 1;
+        }
+        __threadfence();
+      }
+      named_bar_sync(1, NCT);
+      {
+        const uint16_t* rows[MAXK];
+        for (int j = 0; j < p.k; ++j) rows[j] = p.ws_act + (size_t)j * p.F;
+        stage_cols(abuf, asum, p.k, p.XS2, rows, p.k, p.F, p.gs, true);
+      }
+      const int pair = warp >> 1, half = warp & 1;
+      const int s0 = min(2 * pair, p.k - 1), s1 = min(2 * pair + 1, p.k - 1);
+      const float* xsP = c_xs(asum, G2, s0);
+      const float* xoP = c_xo(asum, p.k, G2, s0);
+      const float* xsQ = c_xs(asum, G2, s1);
+      const float* xoQ = c_xo(asum, p.k, G2, s1);
+      const float* ainv = c_inv(asum, p.k, G2);
+      const int npc2 = p.F / 2 / 256;
+      const int gh = (p.F / 2) / p.gs;  // groups per half
+      for (int j = 0; j < rounds2; ++j) {
+        const int u = blockIdx.x + j * gridDim.x;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        int si;
+        if (take(si)) {
+          const uint8_t* st = slots + (size_t)si * SLOT;
+          if (2 * pair < p.k)
+            task_pair<WPT>(st, npc2, G2, half * gh, abuf + (size_t)half * (p.F / 2 / 8) * 16, p.XS2, xsP, xoP, xsQ,
+                           xoQ, pair, acc);
+        }
+        give(si);
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) continue;
+        const int use = rounds1 + j;  // reduction-slot uses continue from phase 1 (group 0)
+        float* rp = red + ((size_t)(0 * RR + (use % RR)) * 8 + warp) * 16;
+        slot_free(0, use);
+        if (c == pair) {  // lanes holding this pair's sums: row r of slot 2p (P), slot 2p+1 (Q)
+          rp[r] = acc[0];
+          rp[r + 8] = acc[3];
+        }
+        if (!arrive_last(0, use, 8)) continue;
+        const float* rbuf = red + (size_t)(0 * RR + (use % RR)) * 8 * 16;
+        if (lane < 8) {
+          // row h = u*8 + lane: y_j = (half 0 + half 1) / S_j, prod_j = rb(y_j) * w_j,
+          // combined in the mlx_colsum_small_f32 association
+          float prod[MAXK];
+#pragma unroll
+          for (int s = 0; s < MAXK; ++s) {
+            if (s < p.k) {
+              const int pr = s >> 1, q = s & 1;
+              const float y = (rbuf[(2 * pr) * 16 + q * 8 + lane] + rbuf[(2 * pr + 1) * 16 + q * 8 + lane]) * ainv[s];
+              prod[s] = b2q::rb(y) * sw[s];
+            } else {
+              prod[s] = 0.0f;
+            }
+          }
+          const int TY = p.k < 8 ? p.k : 8;
+          float total = 0.0f;
+#pragma unroll
+          for (int q = 0; q < MAXK; ++q) {
+            if (q < TY) {
+              float a = 0.0f;
+              for (int s = q; s < p.k; s += TY) a = prod[s] + a;
+              total = (q == 0) ? a : a + total;
+            }
+          }
+          p.out[(size_t)u * 8 + lane] = f2bf(total);
+        }
+        release_use(0, use);
+      }
+    }
+  }
+
+  // ---- exit: the last CTA out re-arms the grid counters for the next call ----
+  __syncthreads();
+  if (fused && tid == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(&p.counters[2], 1u);
+    if (prev == gridDim.x - 1) {
+      p.counters[0] = 0;
+      p.counters[1] = 0;
+      p.counters[2] = 0;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace d1
+}  // namespace b2q
+
+namespace b2q {
+namespace d1 {
+
+static int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+static int plan(D1Params& p, int mode) {
+  const int G1 = p.K1 / p.gs;
+  int off = 0;
+  p.off_slots = off;
+  off += NSLOT * SLOT;
+  p.XS1 = round_up(p.K1 * 2, 128) + 64;
+  p.off_x = off;
+  off = round_up(off + p.XS1, 128);
+  p.off_xs = off;
+  off = round_up(off + (2 * G1 + 2 * MAXK) * 4, 128);
+  if (mode == D1_FUSED) {
+    const int G2 = p.F / p.gs;
+    p.XS2 = round_up(p.F * 2, 128) + 64;
+    p.off_act = off;
+    off = round_up(off + MAXK * p.XS2, 128);
+    p.off_acts = off;
+    off = round_up(off + (2 * MAXK * G2 + 2 * MAXK) * 4, 128);
+  } else {
+    p.XS2 = 0;
+    p.off_act = p.off_acts = off;
+  }
+  p.off_red = off;
+  off = round_up(off + 8 * RR * 8 * 16 * 4, 128);
+  p.off_misc = off;
+  off = round_up(off + 2 * NSLOT * 8 + 2 * 8 * RR * 4 + 16 + (2 * MAXK + NCW + NSLOT) * 4 + 64, 128);
+  p.smem_bytes = off + 1024;
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (p.smem_bytes > di.smem_optin)
+    return set_error(B2Q_EUNSUPPORTED, "decode kernel: %d bytes of shared memory", p.smem_bytes);
+  return B2Q_OK;
+}
+
+template <int WPT, int MODE>
+static int launch_t(const D1Params& p, cudaStream_t st, int grid) {
+  static int attr_done[64] = {};
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (!attr_done[di.device & 63]) {
+    B2Q_TRY_CUDA(cudaFuncSetAttribute(d1_kernel<WPT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_done[di.device & 63] = 1;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NTH);
+  cfg.dynamicSmemBytes = p.smem_bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (MODE == D1_FUSED) ? 1 : 0;
+  B2Q_TRY_CUDA(cudaLaunchKernelEx(&cfg, d1_kernel<WPT, MODE>, p));
+  return B2Q_OK;
+}
+
+static int launch(const D1Params& p, int mode, cudaStream_t st) {
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int grid = di.sm_count;
+  const int wpt = p.gs / 32;
+  switch (wpt * 2 + mode) {
+    case 1 * 2 + D1_QMV: return launch_t<1, D1_QMV>(p, st, grid);
+    case 2 * 2 + D1_QMV: return launch_t<2, D1_QMV>(p, st, grid);
+    case 4 * 2 + D1_QMV: return launch_t<4, D1_QMV>(p, st, grid);
+    case 1 * 2 + D1_FUSED: return launch_t<1, D1_FUSED>(p, st, grid);
+    case 2 * 2 + D1_FUSED: return launch_t<2, D1_FUSED>(p, st, grid);
+    case 4 * 2 + D1_FUSED: return launch_t<4, D1_FUSED>(p, st, grid);
+    default: return set_error(B2Q_EUNSUPPORTED, "decode kernel: group size %d", p.gs);
+  }
+}
+
+// weights: 3-D 128-byte-swizzled map, box of 8 rows x `box_bytes` of each row;
+// scales / biases: 2-D map, box of 8 rows x `mbox_bytes`
+static int set_family(D1Params& p, int mw, int ms, int mb, const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                      uint64_t rows, int K, int box_bytes, int mbox_bytes) {
+  int rc = make_row_block_map(&p.map[mw], w, rows, (uint64_t)K / 2, box_bytes, true);
+  if (rc) return rc;
+  const uint64_t mrow = (uint64_t)(K / p.gs) * 2;
+  rc = make_row_block_map(&p.map[ms], s, rows, mrow, mbox_bytes, false);
+  if (rc) return rc;
+  return make_row_block_map(&p.map[mb], b, rows, mrow, mbox_bytes, false);
+}
+
+}  // namespace d1
+
+using namespace d1;
+
+bool d1_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const void* s, const void* b) {
+  return (gs == 32 || gs == 64 || gs == 128) && N > 0 && N % 16 == 0 && K % TK == 0 && K <= 8 * TK &&
+         aligned16(x) && aligned16(w) && aligned16(s) && aligned16(b);
+}
+
+int d1_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b, uint16_t* y, int N, int K,
+           int gs, cudaStream_t st) {
+  D1Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.gs = gs;
+  p.K1 = K;
+  p.N = N;
+  p.x = x;
+  p.y = y;
+  p.timeout_ns = 2000000000ll;
+  int rc = plan(p, D1_QMV);
+  if (rc) return rc;
+  rc = set_family(p, MW, MS, MB, w, s, b, (uint64_t)N, K, TK / 2, (TK / gs) * 2);
+  if (rc) return rc;
+  return launch(p, D1_QMV, st);
+}
+
+bool d1_moe_eligible(int H, int E, int F, int k, int gs) {
+  if (!((gs == 32 || gs == 64 || gs == 128) && H % TK == 0 && H <= 8 * TK && F % 512 == 0 && F <= 2048 &&
+        (F / gs) % 8 == 0 && k >= 1 && k <= MAXK && E >= k && E <= 1024))
+    return false;
+  // a down task (half of F for 16 rows) and a gate|up task with their scale / bias rows fit one slot
+  const int down_bytes = 2 * (F / 2 / 256) * 1024 + 4 * 8 * (F / gs) * 2;
+  const int gu_bytes = 2 * (TK / 256) * 1024 + 4 * 8 * (TK / gs) * 2;
+  return down_bytes <= SLOT && gu_bytes <= SLOT;
+}
+
+int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                  const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
+                  const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
+                  int k, int gs, int* err, unsigned* counters, float* ws_logits, uint16_t* ws_act, cudaStream_t st) {
+  D1Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.gs = gs;
+  p.K1 = H;
+  p.x = x;
+  p.wr = wr;
+  p.out = out;
+  p.idx_out = idx;
+  p.w_out = w;
+  p.logits_out = logits;
+  p.H = H;
+  p.E = E;
+  p.F = F;
+  p.k = k;
+  p.err = err;
+  p.counters = counters;
+  p.ws_logits = ws_logits;
+  p.ws_act = ws_act;
+  p.timeout_ns = 2000000000ll;
+  int rc = plan(p, D1_FUSED);
+  if (rc) return rc;
+  const uint64_t rgu = (uint64_t)E * F, rd = (uint64_t)E * H;
+  rc = set_family(p, MWG, MSG, MBG, wg, sg, bg, rgu, H, TK / 2, (TK / gs) * 2);
+  if (rc) return rc;
+  rc = set_family(p, MWU, MSU, MBU, wu, su, bu, rgu, H, TK / 2, (TK / gs) * 2);
+  if (rc) return rc;
+  rc = set_family(p, MWD, MSD, MBD, wd, sd, bd, rd, F, F / 4, (F / gs) * 2);
+  if (rc) return rc;
+  return launch(p, D1_FUSED, st);
+}
+
+}  // namespace b2q
