@@ -6,13 +6,13 @@
 //   gateUpAct / downCombine    Runner/FastModel/TrackFastMoE.swift:1192-1590
 //   route (top-k + softmax)    Runner/FastModel/TrackFastMoE.swift:767-911
 //
-// Organisation (one persistent CTA per SM, 8 consumer warps + 1 producer warp):
+// Organisation (one persistent CTA per SM, 8 consumer warps + 2 producer warps):
 //  * A unit is 16 weight rows (P: 8 rows, Q: 8 rows; for gate|up P are gate
 //    rows and Q the up rows of the same 8 outputs) over the whole reduction
 //    length. It is split into T tasks of 1024 reduction values (4 x 128-byte
 //    row pieces); T consecutive consumer warps take the T tasks of a unit and
 //    the CTA runs 8 / T units side by side.
-//  * Every consumer warp owns two stage slots; the producer warp fills them in
+//  * Every consumer warp owns two stage slots; two producer warps fill them in
 //    task order with TMA tensor copies (an 8-row weight block P, an 8-row
 //    block Q, and their scale / bias rows), one full / empty mbarrier pair
 //    per slot. A warp processes 4 pieces per wait.
@@ -25,8 +25,12 @@
 //    counter -> every CTA computes the same top-k -> gate|up units -> a grid
 //    counter of finished units -> activation staging -> down units (8 output
 //    rows x 8 slots: 4 slot pairs x 2 halves of F = 8 tasks). The producer
-//    starts the down weight copies before that counter completes; only the
-//    consumers wait for it. The last CTA out re-arms the counters.
+//    issues the copies of DOWN_AHEAD down units before that counter
+//    completes, the rest once the activations are staged (named barrier 3).
+//    Gate|up and down units are handed out by two grid-wide counters (the
+//    producer asks for its next round while it issues the current one) and
+//    published to the consumers with the slot fill. The last CTA out
+//    re-arms the counters.
 //  * The dot products use the engine's arithmetic: nibbles OR-ed into fp16
 //    1024.0 give 1024 + q (and 1024 + 16 q from the upper nibble of a byte);
 //    activations are staged as fp16 scaled by a power of two per column so
@@ -54,13 +58,17 @@ namespace d1 {
 
 constexpr int NCW = 8;                  // consumer warps
 constexpr int NCT = NCW * 32;
-constexpr int NTH = NCT + 32;           // + producer warp
+constexpr int NPW = 2;                  // producer warps
+constexpr int NTH = NCT + 32 * NPW;
 constexpr int SPW = 2;                  // stage slots per consumer warp
 constexpr int NSLOT = NCW * SPW;
 constexpr int SLOT = 10240;             // bytes per slot
 constexpr int TK = 1024;                // reduction values per gate|up / qmv task
 constexpr int RR = 4;                   // reduction-slot ring per warp group
 constexpr int MAXK = 8;                 // routed slots (fused decode)
+// Down units whose copies the producer issues before the activations are
+// staged: copies issued earlier queue in front of the staging loads.
+constexpr int DOWN_AHEAD = 1;
 
 // tensor-map slots
 enum : int { MW = 0, MS = 1, MB = 2, MWG = 0, MSG = 1, MBG = 2, MWU = 3, MSU = 4, MBU = 5, MWD = 6, MSD = 7, MBD = 8 };
@@ -84,7 +92,8 @@ struct Plan {
 // permuted fp16 chunks (x0 S, x4 S) (x1 S/16, x5 S/16) (x2 S, x6 S)
 // (x3 S/16, x7 S/16) and per group: xs = sum of x S, xo = 1024 * sum_even +
 // 1024 * sum_odd / 16 (the offset the nibble decode adds), inv = 1 / S.
-// Region layout: xs [cap][G], xo [cap][G], inv [MAXK], colmax [MAXK].
+// Region layout: xs [cap][G], xo [cap][G], inv [MAXK], colmax [MAXK],
+// S [MAXK], S / 16 [MAXK].
 __device__ __forceinline__ float* c_xs(float* sums, int G, int col) { return sums + (size_t)col * G; }
 __device__ __forceinline__ float* c_xo(float* sums, int cap, int G, int col) { return sums + (size_t)(cap + col) * G; }
 __device__ __forceinline__ float* c_inv(float* sums, int cap, int G) { return sums + (size_t)2 * cap * G; }
@@ -96,66 +105,137 @@ __device__ __forceinline__ uint32_t h2pack(float lo, float hi) {
 __device__ __forceinline__ float lbf(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float hbf(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
-// All NCT consumer threads call this (named barrier 1).
-__device__ void stage_cols(uint8_t* dst, float* sums, int cap, int XS, const uint16_t* const* rows, int ncols, int K,
-                           int gs, bool coherent) {
-  const int tid = threadIdx.x;
-  const int nch = K / 8, G = K / gs;
+// A 16-byte load issued where it stands (volatile: not sunk towards its use),
+// L2-coherent (.cg) or through the non-coherent path (.nc).
+__device__ __forceinline__ uint4 ld_v4_now(const void* ptr, bool coherent) {
+  uint4 v;
+  if (coherent)
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ptr));
+  else
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ptr));
+  return v;
+}
+
+// max |value| of 8 bf16 as bf16 bits << 16, NaN clamped to +inf's bits
+__device__ __forceinline__ unsigned chunk_max(uint4 v) {
+  unsigned m = max(max(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), max(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
+  m = max(m & 0xffffu, m >> 16) << 16;
+  return m > 0x7f800000u ? 0x7f800000u : m;
+}
+
+// Activation staging. All NCT consumer threads call this (named barrier 1).
+// Column j is the K values at base + j * rstride. A max pass finds each
+// column's max |value| (every CTA stages the same rows, so every CTA finds the
+// same scales); the store pass writes the scaled, permuted fp16 chunks and
+// forms the group sums by a shuffle reduction over the gs / 8 lanes that hold
+// a group's chunks. Up to SC_REG chunks per thread stay in registers between
+// the passes (their loads all issued first), else each pass loads them.
+constexpr int SC_REG = 8;
+__device__ void stage_cols(uint8_t* dst, float* sums, int cap, int XS, const uint16_t* base, size_t rstride, int ncols,
+                           int K, int gs, bool coherent) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nch = K / 8, G = K / gs, CPG = gs / 8;
+  const int total = ncols * nch;
   float* inv = c_inv(sums, cap, G);
   unsigned* colmax = reinterpret_cast<unsigned*>(inv + MAXK);
-  if (tid < MAXK) colmax[tid] = 0u;
-  named_bar_sync(1, NCT);
-  for (int q = tid; q < ncols * nch; q += NCT) {
-    const int col = q / nch, ch = q % nch;
-    const uint4* src = reinterpret_cast<const uint4*>(rows[col] + (size_t)ch * 8);
-    const uint4 v = coherent ? __ldcg(src) : __ldg(src);
-    unsigned m = max(max(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), max(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
-    m = max(m & 0xffffu, m >> 16) << 16;
-    if (m > 0x7f800000u) m = 0x7f800000u;
-    atomicMax(&colmax[col], m);
-  }
-  named_bar_sync(1, NCT);
-  if (tid < ncols) {
-    const float mx = __uint_as_float(colmax[tid]);
-    int e = 0;
-    if (mx > 0.0f && mx < INFINITY) {
-      int E2;
-      frexpf(mx, &E2);
-      e = 11 - E2;
+  float* colS = inv + 2 * MAXK;
+  float* colS16 = inv + 3 * MAXK;
+  // a warp's 32 consecutive chunks stay inside one column when nch is a multiple of 32
+  const bool warp_col = (nch % 32) == 0;
+  // q / nch by multiply-high: exact while q * nch < 2^32 / 8 (q < MAXK * nch)
+  const unsigned mdiv = 0xffffffffu / (unsigned)nch + 1u;
+  auto col_of = [&](int q) { return (int)__umulhi((unsigned)q, mdiv); };
+  auto src = [&](int q) {
+    const int col = col_of(q);
+    return base + (size_t)col * rstride + (size_t)(q - col * nch) * 8;
+  };
+  // max pass step over chunks q0 + [0, NCT) (q0 uniform)
+  auto max_step = [&](int q0, uint4 v) {
+    const int q = q0 + tid;
+    unsigned m = q < total ? chunk_max(v) : 0u;
+    const int col = col_of(q < total ? q : q0 + (tid & ~31));
+    if (warp_col) {
+      m = __reduce_max_sync(0xffffffffu, m);
+      if (lane == 0 && q0 + (tid & ~31) < total) atomicMax(&colmax[col], m);
+    } else if (q < total) {
+      atomicMax(&colmax[col], m);
     }
-    inv[tid] = ldexpf(1.0f, -e);
-    colmax[tid] = (unsigned)(e + 1000);
-  }
-  named_bar_sync(1, NCT);
-  for (int q = tid; q < ncols * nch; q += NCT) {
-    const int col = q / nch, ch = q % nch;
-    const uint4* src = reinterpret_cast<const uint4*>(rows[col] + (size_t)ch * 8);
-    const uint4 v = coherent ? __ldcg(src) : __ldg(src);
-    const int e = (int)colmax[col] - 1000;
-    const float S = ldexpf(1.0f, e), S16 = ldexpf(1.0f, e - 4);
+  };
+  // store pass step (q0 uniform; every lane takes part in the shuffles)
+  auto store_step = [&](int q0, uint4 v) {
+    const int q = q0 + tid;
+    const bool live = q < total;
+    const int col = live ? col_of(q) : 0, ch = live ? q - col * nch : 0;
+    const float S = colS[col], S16 = colS16[col];
     uint4 o;
     o.x = h2pack(lbf(v.x) * S, lbf(v.z) * S);
     o.y = h2pack(hbf(v.x) * S16, hbf(v.z) * S16);
     o.z = h2pack(lbf(v.y) * S, lbf(v.w) * S);
     o.w = h2pack(hbf(v.y) * S16, hbf(v.w) * S16);
-    *reinterpret_cast<uint4*>(dst + (size_t)col * XS + (size_t)ch * 16) = o;
-  }
-  named_bar_sync(1, NCT);
-  for (int q = tid; q < ncols * G; q += NCT) {
-    const int col = q / G, g = q % G;
-    const uint8_t* base = dst + (size_t)col * XS + (size_t)g * (gs / 8) * 16;
-    float se = 0.0f, so = 0.0f;
-    for (int ch = 0; ch < gs / 8; ++ch) {
-      const uint4 v = *reinterpret_cast<const uint4*>(base + ch * 16);
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
-      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
-      se += ((a.x + c.x) + a.y) + c.y;
-      so += ((b.x + d.x) + b.y) + d.y;
+    if (live) *reinterpret_cast<uint4*>(dst + (size_t)col * XS + (size_t)ch * 16) = o;
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&o.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&o.y));
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&o.z));
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&o.w));
+    float se = ((a.x + c.x) + a.y) + c.y;
+    float so = ((b.x + d.x) + b.y) + d.y;
+    for (int off = 1; off < CPG; off <<= 1) {
+      se += __shfl_xor_sync(0xffffffffu, se, off);
+      so += __shfl_xor_sync(0xffffffffu, so, off);
     }
-    c_xs(sums, G, col)[g] = se + 16.0f * so;
-    c_xo(sums, cap, G, col)[g] = 1024.0f * se + 1024.0f * so;
+    if (live && (ch % CPG) == 0) {
+      const int g = ch / CPG;
+      c_xs(sums, G, col)[g] = se + 16.0f * so;
+      c_xo(sums, cap, G, col)[g] = 1024.0f * se + 1024.0f * so;
+    }
+  };
+  // the power of two S = 2^e of each column from its max |value| bits: for a
+  // normal max with biased exponent x, max * 2^(137 - x) lies in [1024, 2048);
+  // e stays in [-100, 100] (0 for a zero, infinite or NaN max)
+  auto set_scales = [&]() {
+    if (tid < ncols) {
+      const unsigned mb = colmax[tid];
+      int e = 0;
+      if (mb != 0u && mb < 0x7f800000u) e = min(100, max(-100, 137 - (int)(mb >> 23)));
+      inv[tid] = __int_as_float((127 - e) << 23);
+      colS[tid] = __int_as_float((127 + e) << 23);
+      colS16[tid] = __int_as_float((123 + e) << 23);
+    }
+  };
+  if (tid < MAXK) colmax[tid] = 0u;
+  if (total <= SC_REG * NCT) {
+    uint4 keep[SC_REG];
+#pragma unroll
+    for (int i = 0; i < SC_REG; ++i) {
+      const int q = i * NCT + tid;
+      keep[i] = q < total ? ld_v4_now(src(q), coherent) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    named_bar_sync(1, NCT);
+#pragma unroll
+    for (int i = 0; i < SC_REG; ++i)
+      if (i * NCT < total) max_step(i * NCT, keep[i]);
+    named_bar_sync(1, NCT);
+    set_scales();
+    named_bar_sync(1, NCT);
+#pragma unroll
+    for (int i = 0; i < SC_REG; ++i)
+      if (i * NCT < total) store_step(i * NCT, keep[i]);
+  } else {
+    auto load = [&](int q) {
+      if (q >= total) return make_uint4(0u, 0u, 0u, 0u);
+      const uint4* sp = reinterpret_cast<const uint4*>(src(q));
+      return coherent ? __ldcg(sp) : __ldg(sp);
+    };
+    named_bar_sync(1, NCT);
+    for (int q0 = 0; q0 < total; q0 += NCT) max_step(q0, load(q0 + tid));
+    named_bar_sync(1, NCT);
+    set_scales();
+    named_bar_sync(1, NCT);
+    for (int q0 = 0; q0 < total; q0 += NCT) store_step(q0, load(q0 + tid));
   }
   named_bar_sync(1, NCT);
 }
@@ -231,89 +311,66 @@ __device__ __forceinline__ void task_col(const uint8_t* st, int npc, int GB, int
   }
 }
 
-// Down pair: P = slot 2 * pair, Q = slot 2 * pair + 1 against the 8 staged
-// activation columns (column n = slot n). Lanes c == pair own acc[0] (P) and
-// acc[3] (Q).
+// Down pair: P = slot 2 * pair, Q = slot 2 * pair + 1. The B operand's column
+// n is activation slot 2 * pair + (n & 1), so every lane (r, c) holds row r
+// against slot 2 * pair in D[0] and row r + 8 against slot 2 * pair + 1 in
+// D[3]; as in task_col, the quad lanes finish groups c of each batch of NB
+// groups (acc[0]: P, acc[3]: Q). gabs0: the task's first group inside the
+// full-length meta rows and staged sums.
 template <int WPT>
 __device__ __forceinline__ void task_pair(const uint8_t* st, int npc, int GB, int gabs0, const uint8_t* acol0, int XS,
                                           const float* xsP, const float* xoP, const float* xsQ, const float* xoQ,
                                           int pair, float (&acc)[4]) {
   constexpr int GPC = 8 / WPT;
+  constexpr int NB = GPC < 4 ? GPC : 4;
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
   const int qoff = npc * 1024;
   const uint8_t* mP = st + 2 * qoff;
   const int mblk = 8 * GB * 2;
   const uint8_t* wl = st + r * 128 + c * 4;
-  const uint8_t* xl = acol0 + (size_t)r * XS + c * 16;  // column r = slot r
+  const uint8_t* xl = acol0 + (size_t)(2 * pair + (r & 1)) * XS + c * 16;
   for (int pc = 0; pc < npc; ++pc) {
     const uint8_t* pw = wl + pc * 1024;
     const uint8_t* px = xl + pc * 512;
 #pragma unroll
-    for (int gi = 0; gi < GPC; ++gi) {
-      float D[4];
+    for (int b0 = 0; b0 < GPC; b0 += NB) {
+      float D[NB][4];
 #pragma unroll
       for (int j = 0; j < WPT; ++j) {
-        const int u = gi * WPT + j;
-        word_mma(pw + ((u ^ r) << 4), qoff, *reinterpret_cast<const uint4*>(px + u * 64), j == 0, D);
+#pragma unroll
+        for (int gi = 0; gi < NB; ++gi) {
+          const int u = (b0 + gi) * WPT + j;
+          word_mma(pw + ((u ^ r) << 4), qoff, *reinterpret_cast<const uint4*>(px + u * 64), j == 0, D[gi]);
+        }
       }
-      const int gl = pc * GPC + gi;  // group inside the task
-      const int ga = gabs0 + gl;     // absolute group: the meta rows hold the full row
+      float e0 = D[0][0], e3 = D[0][3];
+#pragma unroll
+      for (int gi = 1; gi < NB; ++gi) {
+        e0 = (c == gi) ? D[gi][0] : e0;
+        e3 = (c == gi) ? D[gi][3] : e3;
+      }
+      const int ga = gabs0 + pc * GPC + b0 + (c < NB ? c : NB - 1);
       const int mo = r * GB * 2 + ga * 2;
       const float sP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mo));
       const float bP = bf2f(*reinterpret_cast<const uint16_t*>(mP + mblk + mo));
       const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(mP + 2 * mblk + mo));
       const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(mP + 3 * mblk + mo));
-      if (c == pair) {
-        acc[0] = fmaf(sP, D[0] - xoP[ga], fmaf(bP, xsP[ga], acc[0]));
-        acc[3] = fmaf(sQ, D[3] - xoQ[ga], fmaf(bQ, xsQ[ga], acc[3]));
+      if (c < NB) {
+        acc[0] = fmaf(sP, e0 - xoP[ga], fmaf(bP, xsP[ga], acc[0]));
+        acc[3] = fmaf(sQ, e3 - xoQ[ga], fmaf(bQ, xsQ[ga], acc[3]));
       }
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// routing: top-k (largest first, ties to the lower index) + softmax over k
-// (Runner/FastModel/TrackFastMoE.swift:767-911), one warp, logits read
-// coherently (other CTAs wrote them)
+// routing (Runner/FastModel/TrackFastMoE.swift:767-911)
 // ---------------------------------------------------------------------------
-__device__ void warp_route_d1(const float* lr, int E, int k, uint32_t* sidx, float* sw) {
+// softmax over the k selected logits held by lanes 0..k-1 (slot order): max,
+// exp, per-lane partial sums of 4 then a butterfly, as the reference's
+// softmax over its k values (Runner/FastModel/TrackFastMoE.swift:846-880)
+__device__ void softmax_k(float selv, int k, float* sw) {
   const int lane = threadIdx.x & 31;
-  float v[32];
-  bool taken[32];
-  const int EP = (E + 31) / 32;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int e = lane + 32 * j;
-    const bool ok = j < EP && e < E;
-    v[j] = ok ? __ldcg(lr + e) : -INFINITY;
-    taken[j] = !ok;
-  }
-  float selv = -INFINITY;
-  uint32_t seli = 0xffffffffu;
-  for (int kk = 0; kk < k; ++kk) {
-    float bv = -INFINITY;
-    int bj = -1;
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (!taken[j] && v[j] > bv) {
-        bv = v[j];
-        bj = j;
-      }
-    float gmax = bv;
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
-    uint32_t cand = (bj >= 0 && bv == gmax) ? (uint32_t)(lane + 32 * bj) : 0xffffffffu;
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, off));
-    if (lane == kk) {
-      selv = gmax;
-      seli = cand;
-    }
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j == bj && cand == (uint32_t)(lane + 32 * bj)) taken[j] = true;
-  }
-  // softmax over the k selected values, per-lane partials of 4 (slot order)
   float mx = (lane < k) ? selv : -INFINITY;
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -327,10 +384,7 @@ __device__ void warp_route_d1(const float* lr, int E, int k, uint32_t* sidx, flo
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
   const float inv = 1.0f / part;
-  if (lane < k) {
-    sidx[lane] = seli;
-    sw[lane] = ex * inv;
-  }
+  if (lane < k) sw[lane] = ex * inv;
 }
 
 // ---------------------------------------------------------------------------
@@ -343,6 +397,18 @@ __device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int c0, 
       " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch3(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch2(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
 }
 
 struct Shape {
@@ -358,13 +424,16 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
   uint8_t* slots = smem + p.off_slots;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_misc);
   uint64_t* empty = full + NSLOT;
-  unsigned* cnt = reinterpret_cast<unsigned*>(empty + NSLOT);  // [8 groups][RR] arrival counts
-  unsigned* gen = cnt + 8 * RR;                                // [8 groups][RR] consumed uses
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(gen + 8 * RR);
+  unsigned* cnt = reinterpret_cast<unsigned*>(empty + NSLOT);  // [9 groups][RR] arrival counts
+  unsigned* gen = cnt + 9 * RR;                                // [9 groups][RR] consumed uses
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gen + 9 * RR);
   uint32_t* sidx = reinterpret_cast<uint32_t*>(const_cast<int*>(abort_flag) + 4);
   float* sw = reinterpret_cast<float*>(sidx + MAXK);
   float* rsum = sw + MAXK;  // [NCW]
   int* lastfill = reinterpret_cast<int*>(rsum + NCW);  // [NSLOT] ordinal of the last fill issued per slot
+  volatile int* slot_unit = lastfill + NSLOT;            // [NSLOT] unit of the task in the slot (-1: no more work)
+  int* p1n = lastfill + 2 * NSLOT;                       // [NCW] phase-1 task count of each consumer warp
+  unsigned* fin_cta = reinterpret_cast<unsigned*>(p1n + NCW);  // gate|up units this CTA finished
   float* red = reinterpret_cast<float*>(smem + p.off_red);
   const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
   const bool fused = MODE == D1_FUSED;
@@ -375,8 +444,9 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 8 * RR; ++i) cnt[i] = gen[i] = 0;
+    for (int i = 0; i < 9 * RR; ++i) cnt[i] = gen[i] = 0;
     for (int i = 0; i < NSLOT; ++i) lastfill[i] = -1;
+    *fin_cta = 0u;
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -386,12 +456,15 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
   const Shape ph1{p.K1 / TK, fused ? p.k * (p.F / 8) : p.N / 16};
   const Shape ph2{8, fused ? p.H / 8 : 0};
   auto local_units = [&](int units) { return units > (int)blockIdx.x ? (units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0; };
-  const int nl1 = local_units(ph1.units), nl2 = local_units(ph2.units);
+  const int nl1 = local_units(ph1.units);
   const int G1grp = NCW / ph1.T;  // units side by side in phase 1
-  const int rounds1 = (nl1 + G1grp - 1) / G1grp, rounds2 = nl2;
+  const int rounds1 = (nl1 + G1grp - 1) / G1grp;
 
-  if (warp == NCW) {
-    // ------------------------------ producer ------------------------------
+  if (warp >= NCW) {
+    // ------------------------------ producers ------------------------------
+    // Producer pw fills the slots of the phase-1 groups gi with gi % NPW == pw
+    // and, in the down phase, of consumer warps [4 pw, 4 pw + 4).
+    const int pw = warp - NCW;
     if (fused) named_bar_sync(2, NTH);  // routing done
     const uint64_t pol = policy_evict_first();
     if (tc::elect_one())
@@ -399,17 +472,24 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.map[i])) : "memory");
     __syncwarp();
     // n: the warp's task ordinal (its round in phase 1; then phase-1 count + round)
-    auto issue = [&](int w, int n, bool valid, int rowP, int rowQ, int pieceP, int npc, int mwP, int msP, int mbP,
-                     int mwQ, int msQ, int mbQ, int gcol, int GB) -> bool {
+    // waits until slot (w, n) is free: its fill of ordinal n - SPW was consumed
+    auto wait_empty = [&](int w, int n) -> bool {
       const int si = w * SPW + (n % SPW);
       if (n >= SPW && !__all_sync(0xffffffffu, tc::wait(&empty[si], ((n / SPW) - 1) & 1, deadline, abort_flag))) {
         if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
         *abort_flag = 1;
         return false;
       }
+      return true;
+    };
+    auto issue = [&](int w, int n, bool valid, int rowP, int rowQ, int pieceP, int npc, int mwP, int msP, int mbP,
+                     int mwQ, int msQ, int mbQ, int gcol, int GB, int unit) -> bool {
+      const int si = w * SPW + (n % SPW);
+      if (!wait_empty(w, n)) return false;
       if (tc::elect_one()) {
         uint8_t* st = slots + (size_t)si * SLOT;
         lastfill[si] = n;
+        slot_unit[si] = unit;  // published by the arrive below
         if (!valid || *abort_flag) {
           mbar_arrive_expect_tx(&full[si], 0u);
         } else {
@@ -427,53 +507,113 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       __syncwarp();
       return true;
     };
-    auto p1_count = [&](int w) {  // phase-1 tasks of warp w
-      const int gi = w / ph1.T;
-      return nl1 > gi ? (nl1 - gi + G1grp - 1) / G1grp : 0;
-    };
     bool ok = true;
-    // phase 1: qmv rows or gate|up rows, tasks of TK values (4 pieces)
     const int GB1 = TK / p.gs;
-    for (int j = 0; ok && j < rounds1; ++j)
-      for (int gi = 0; ok && gi < G1grp; ++gi) {
-        const int li = j * G1grp + gi;
-        if (li >= nl1) break;
-        const int u = blockIdx.x + li * gridDim.x;
-        int rowP, rowQ;
-        if (fused) {
-          const int z = u / (p.F / 8), rb = u % (p.F / 8);
-          rowP = rowQ = (int)(sidx[z] * (uint32_t)p.F) + rb * 8;
-        } else {
-          rowP = u * 16;
-          rowQ = rowP + 8;
+    if (!fused) {
+      // qmv: static round-robin units, T tasks of TK values (4 pieces) each
+      for (int j = 0; ok && j < rounds1; ++j)
+        for (int gi = 0; ok && gi < G1grp; ++gi) {
+          const int li = j * G1grp + gi;
+          if (li >= nl1) break;
+          if (gi % NPW != pw) continue;
+          const int u = blockIdx.x + li * gridDim.x;
+          // the issue order rotates with the round, so the warp whose data lands
+          // last (and that usually finishes the unit) changes from unit to unit
+          for (int i = 0; ok && i < ph1.T; ++i) {
+            const int t = (i + j) % ph1.T;
+            ok = issue(gi * ph1.T + t, j, true, u * 16, u * 16 + 8, t * (TK / 256), TK / 256, MW, MS, MB, MW, MS, MB,
+                       t * GB1, GB1, u);
+          }
         }
-        for (int t = 0; ok && t < ph1.T; ++t) {
-          const int w = gi * ph1.T + t;
-          ok = fused ? issue(w, j, true, rowP, rowQ, t * (TK / 256), TK / 256, MWG, MSG, MBG, MWU, MSU, MBU, t * GB1,
-                             GB1)
-                     : issue(w, j, true, rowP, rowQ, t * (TK / 256), TK / 256, MW, MS, MB, MW, MS, MB, t * GB1, GB1);
+    } else {
+      // fused, phase 1: units come from a grid-wide counter, so CTAs that
+      // stream faster take more. A round takes one unit per group of this
+      // producer with one atomic (unit base + k for its k-th group), and the
+      // next round's atomic is issued as soon as the current one is known, so
+      // its latency overlaps the round's copies. A unit past the end (a fill
+      // without copies, published as -1) ends a group's phase.
+      int jr[NCW];
+      bool gdone[NCW];
+      int ng = 0;
+      for (int gi = 0; gi < G1grp; ++gi) {
+        jr[gi] = 0;
+        gdone[gi] = gi % NPW != pw;
+        ng += gdone[gi] ? 0 : 1;
+      }
+      if (ng > 0) {
+        unsigned nxt = (lane == 0) ? atomicAdd(&p.sched[0], (unsigned)ng) : 0u;
+        int left = ng;
+        while (ok && left > 0) {
+          const unsigned base = __shfl_sync(0xffffffffu, nxt, 0);
+          if (lane == 0 && base < (unsigned)ph1.units) nxt = atomicAdd(&p.sched[0], (unsigned)ng);
+          for (int gi = pw, k = 0; ok && gi < G1grp; gi += NPW, ++k) {
+            if (gdone[gi]) continue;
+            const int u = base + k < (unsigned)ph1.units ? (int)(base + k) : -1;
+            if (u >= 0) {
+              const int z = u / (p.F / 8), rb = u % (p.F / 8);
+              const int row = (int)(sidx[z] * (uint32_t)p.F) + rb * 8;
+              for (int i = 0; ok && i < ph1.T; ++i) {  // rotated issue order, as in qmv
+                const int t = (i + jr[gi]) % ph1.T;
+                ok = issue(gi * ph1.T + t, jr[gi], true, row, row, t * (TK / 256), TK / 256, MWG, MSG, MBG, MWU,
+                           MSU, MBU, t * GB1, GB1, u);
+              }
+            } else {
+              for (int t = 0; ok && t < ph1.T; ++t)
+                ok = issue(gi * ph1.T + t, jr[gi], false, 0, 0, 0, 1, MWG, MSG, MBG, MWU, MSU, MBU, 0, GB1, -1);
+              gdone[gi] = true;
+              --left;
+            }
+            ++jr[gi];
+          }
         }
       }
-    // phase 2 (fused): down rows, 4 slot pairs x 2 halves of F; meta rows are whole
-    if (fused) {
+      // phase-1 fill counts of every consumer warp, for the down ordinals
+      if (lane == 0)
+        for (int gi = pw; gi < G1grp; gi += NPW)
+          for (int t = 0; t < ph1.T; ++t) p1n[gi * ph1.T + t] = jr[gi];
+      named_bar_sync(4, 32 * NPW);
+      // phase 2: down rows, 4 slot pairs x 2 halves of F (meta rows whole) for
+      // consumer warps 0..7; units round-robin over the CTAs (every CTA gets
+      // H / 8 / grid of them, within one); warp t's ordinals continue from its
+      // phase-1 count; a -1 unit ends the phase
       const int npc2 = p.F / 2 / 256;
-      for (int j = 0; ok && j < rounds2; ++j) {
-        const int u = blockIdx.x + j * gridDim.x;
-        for (int t = 0; ok && t < 8; ++t) {
+      const int nl2 = local_units(ph2.units);
+      uint32_t ex[MAXK];
+#pragma unroll
+      for (int s2 = 0; s2 < MAXK; ++s2) ex[s2] = s2 < p.k ? sidx[s2] : 0u;
+      int n0[8 / NPW];
+#pragma unroll
+      for (int i = 0; i < 8 / NPW; ++i) n0[i] = p1n[pw * (8 / NPW) + i];
+      bool staged = false;  // barrier 3: the consumers staged the activations
+      for (int j2 = 0; ok && j2 <= nl2; ++j2) {
+        if (j2 == DOWN_AHEAD) {
+          named_bar_sync(3, NTH);
+          staged = true;
+        }
+        const int u = j2 < nl2 ? (int)blockIdx.x + j2 * (int)gridDim.x : -1;
+#pragma unroll
+        for (int i0 = 0; i0 < 8 / NPW; ++i0) {
+          if (!ok) break;
+          const int i = (i0 + j2) % (8 / NPW);  // rotated issue order
+          const int t = pw * (8 / NPW) + i;
           const int pair = t >> 1, half = t & 1;
-          const int s0 = 2 * pair, s1 = 2 * pair + 1;
-          const bool v0 = s0 < p.k, v1 = s1 < p.k;
-          const uint32_t e0 = v0 ? sidx[s0] : 0u, e1 = v1 ? sidx[s1] : e0;
-          ok = issue(t, p1_count(t) + j, v0, (int)(e0 * (uint32_t)p.H) + u * 8, (int)(e1 * (uint32_t)p.H) + u * 8,
-                     half * npc2,
-                     npc2, MWD, MSD, MBD, MWD, MSD, MBD, 0, G2);
+          const bool v0 = 2 * pair < p.k, v1 = 2 * pair + 1 < p.k;
+          const uint32_t e0 = v0 ? ex[2 * pair] : 0u, e1 = v1 ? ex[2 * pair + 1] : e0;
+          const int n = n0[i] + j2;
+          ok = u >= 0 ? issue(t, n, v0, (int)(e0 * (uint32_t)p.H) + u * 8, (int)(e1 * (uint32_t)p.H) + u * 8,
+                              half * npc2, npc2, MWD, MSD, MBD, MWD, MSD, MBD, 0, G2, u)
+                      : issue(t, n, false, 0, 0, 0, 1, MWD, MSD, MBD, MWD, MSD, MBD, 0, G2, -1);
         }
       }
+      if (!staged) named_bar_sync(3, NTH);
     }
-    // let every copy issued land before the CTA may exit
+    // let every copy issued land before the CTA may exit: once both producers
+    // are done, a slot's last fill is the only one that can still be in
+    // flight (a fill is issued only after the previous one was consumed)
+    named_bar_sync(4, 32 * NPW);
     const uint64_t dl = globaltimer() + 200000000ull;
-    __syncwarp();
-    if (lane < NSLOT && lastfill[lane] >= 0) tc::wait_until(&full[lane], (lastfill[lane] / SPW) & 1, dl);
+    if (lane < NSLOT && lane % NPW == pw && lastfill[lane] >= 0)
+      tc::wait_until(&full[lane], (lastfill[lane] / SPW) & 1, dl);
   } else {
     // ------------------------------ consumers ------------------------------
     uint8_t* xbuf = smem + p.off_x;
@@ -508,25 +648,48 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         named_bar_sync(1, NCT);
         ++rows_done;
       }
+      if (tid == 0 && rows_done) {
+        __threadfence();
+        atomicAdd(&p.counters[0], (unsigned)rows_done);
+      }
+      {
+        // stage x while the other CTAs finish their router rows
+        stage_cols(xbuf, xsum, 1, p.XS1, p.x, 0, 1, p.K1, p.gs, false);
+      }
       if (tid == 0) {
-        if (rows_done) {
-          __threadfence();
-          atomicAdd(&p.counters[0], (unsigned)rows_done);
-        }
+        // acquire load of the count; the CTA barrier below orders the
+        // other threads' reads after it
         if (!wait_counter_geq(&p.counters[0], (unsigned)p.E, deadline, abort_flag)) {
           record_error(p.err, B2Q_ETIMEOUT);
           *abort_flag = 1;
         }
-        __threadfence();
+      }
+      named_bar_sync(1, NCT);
+      // top-k by rank: expert e is selected at slot rank(e) when rank(e) < k,
+      // rank(e) = #{j : v_j > v_e or (v_j == v_e and j < e)} (largest first, ties
+      // to the lower index, as the sequential selection); NaN ranks as -inf
+      float* lgs = reinterpret_cast<float*>(abuf);  // scratch before the down phase
+      float* sval = lgs + p.E;
+      for (int e = tid; e < p.E; e += NCT) {
+        const float v = *abort_flag ? 0.0f : __ldcg(p.ws_logits + e);
+        lgs[e] = (v != v) ? -INFINITY : v;
+      }
+      named_bar_sync(1, NCT);
+      for (int e = tid; e < p.E; e += NCT) {
+        const float v = lgs[e];
+        int rank = 0;
+        for (int j = 0; j < p.E; ++j) {
+          const float vj = lgs[j];
+          rank += (vj > v || (vj == v && j < e)) ? 1 : 0;
+        }
+        if (rank < p.k) {
+          sidx[rank] = (uint32_t)e;
+          sval[rank] = v;
+        }
       }
       named_bar_sync(1, NCT);
       if (warp == 0) {
-        if (!*abort_flag) {
-          warp_route_d1(p.ws_logits, p.E, p.k, sidx, sw);
-        } else if (lane < p.k) {
-          sidx[lane] = 0;
-          sw[lane] = 0.0f;
-        }
+        softmax_k(lane < p.k ? sval[lane] : -INFINITY, p.k, sw);
         __syncwarp();
         if (blockIdx.x == 0 && lane < p.k) {
           if (p.idx_out) p.idx_out[lane] = sidx[lane];
@@ -537,9 +700,8 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       }
       named_bar_sync(2, NTH);  // releases the producer
     }
-    {
-      const uint16_t* rows[1] = {p.x};
-      stage_cols(xbuf, xsum, 1, p.XS1, rows, 1, p.K1, p.gs, false);
+    if (!fused) {
+      stage_cols(xbuf, xsum, 1, p.XS1, p.x, 0, 1, p.K1, p.gs, false);
     }
     const float* xs1 = c_xs(xsum, G1, 0);
     const float* xo1 = c_xo(xsum, 1, G1, 0);
@@ -561,8 +723,8 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       if (lane == 0) mbar_arrive(&empty[si]);
       ++n;
     };
-    // Reduction through shared memory: returns true in the warp that arrived last.
-    // slotf: the unit's partial rows [T][16] (or [8][16] for down).
+    // Reduction through shared memory: returns true in the warp that arrived
+    // last. The unit's partial rows are [T][16] (or [8][16] for down).
     auto arrive_last = [&](int grp, int use, int T) -> bool {
       unsigned* cn = cnt + grp * RR + (use % RR);
       unsigned old = 0;
@@ -605,13 +767,26 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
     {
       const int T = ph1.T, grp = warp / T, t = warp % T;
       const int GB1 = TK / p.gs;
-      for (int j = 0; j < rounds1; ++j) {
-        const int li = j * G1grp + grp;
-        if (li >= nl1) break;
-        const int u = blockIdx.x + li * gridDim.x;
+      int finished = 0;  // gate|up units this warp finished (fused)
+      for (int j = 0;; ++j) {
+        int u = 0;
+        if (!fused) {
+          const int li = j * G1grp + grp;
+          if (li >= nl1) break;
+          u = blockIdx.x + li * gridDim.x;
+        }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int si;
-        if (take(si)) {
+        const bool got = take(si);
+        if (fused) {
+          // the producer publishes the unit with the fill; -1 ends the phase
+          u = got ? slot_unit[si] : -1;
+          if (u < 0) {
+            give(si);
+            break;
+          }
+        }
+        if (got) {
           const uint8_t* st = slots + (size_t)si * SLOT;
           task_col<WPT>(st, 4, GB1, 0, t * GB1, xbuf + (size_t)t * (TK / 8) * 16, xs1, xo1, acc);
         }
@@ -631,45 +806,49 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         if (!arrive_last(grp, j, T)) continue;
         // last warp of the unit: rows r (P) and r + 8 (Q) in task order
         const float* rbuf = red + (size_t)(grp * RR + (j % RR)) * 8 * 16;
+        float tot = 0.0f;
         if (lane < 16) {
-          float tot = 0.0f;
           for (int q = 0; q < T; ++q) tot += rbuf[q * 16 + lane];
           tot *= inv1;
-          if (fused) {
-            // lanes 0..7: gate row f = rb*8 + lane and its up row (lane + 8)
-            const float up = __shfl_sync(0x0000ffffu, tot, lane + 8, 16);
-            if (lane < 8) {
-              const int z = u / (p.F / 8), rbk = u % (p.F / 8);
-              p.ws_act[(size_t)z * p.F + rbk * 8 + lane] = swiglu_bf16(f2bf(tot), f2bf(up));
-            }
-          } else {
-            p.y[(size_t)u * 16 + lane] = f2bf(tot);
-          }
         }
+        // the reduction slot is free once read (its release fences shared
+        // memory only, so it goes before the global stores)
         release_use(grp, j);
-        if (fused && lane == 0) {
-          __threadfence();
-          atomicAdd(&p.counters[1], 1u);
+        if (fused) {
+          // lanes 0..7: gate row f = rb*8 + lane and its up row (lane + 8)
+          const float up = __shfl_sync(0xffffffffu, tot, (lane + 8) & 31);
+          const int z = u / (p.F / 8), rbk = u % (p.F / 8);
+          if (lane < 8) p.ws_act[(size_t)z * p.F + rbk * 8 + lane] = swiglu_bf16(f2bf(tot), f2bf(up));
+          ++finished;
+        } else {
+          if (lane < 16) p.y[(size_t)u * 16 + lane] = f2bf(tot);
         }
       }
+      if (fused && lane == 0 && finished) atomicAdd(fin_cta, (unsigned)finished);
     }
 
     // ---------------- phase 2 (fused): down + weighted combine ----------------
     if (fused) {
-      // every gate|up unit of the grid must have published its activations
+      // the CTA's finished units are published once (after the barrier, one
+      // fence covers every warp's activation rows); then every gate|up unit
+      // of the grid must have been published
+      named_bar_sync(1, NCT);
       if (tid == 0) {
+        const unsigned nfin = *fin_cta;
+        if (nfin) {
+          __threadfence();
+          atomicAdd(&p.counters[1], nfin);
+        }
         if (!*abort_flag && !wait_counter_geq(&p.counters[1], (unsigned)ph1.units, deadline, abort_flag)) {
           record_error(p.err, B2Q_ETIMEOUT);
           *abort_flag = 1;
         }
-        __threadfence();
       }
       named_bar_sync(1, NCT);
       {
-        const uint16_t* rows[MAXK];
-        for (int j = 0; j < p.k; ++j) rows[j] = p.ws_act + (size_t)j * p.F;
-        stage_cols(abuf, asum, p.k, p.XS2, rows, p.k, p.F, p.gs, true);
+        stage_cols(abuf, asum, p.k, p.XS2, p.ws_act, (size_t)p.F, p.k, p.F, p.gs, true);
       }
+      named_bar_arrive(3, NTH);  // the producer may issue the remaining down copies
       const int pair = warp >> 1, half = warp & 1;
       const int s0 = min(2 * pair, p.k - 1), s1 = min(2 * pair + 1, p.k - 1);
       const float* xsP = c_xs(asum, G2, s0);
@@ -679,11 +858,17 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       const float* ainv = c_inv(asum, p.k, G2);
       const int npc2 = p.F / 2 / 256;
       const int gh = (p.F / 2) / p.gs;  // groups per half
-      for (int j = 0; j < rounds2; ++j) {
-        const int u = blockIdx.x + j * gridDim.x;
+      constexpr int G_DOWN = 8;  // reduction group of the down units
+      for (int use = 0;; ++use) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int si;
-        if (take(si)) {
+        const bool got = take(si);
+        const int u = got ? slot_unit[si] : -1;
+        if (u < 0) {
+          give(si);
+          break;
+        }
+        {
           const uint8_t* st = slots + (size_t)si * SLOT;
           if (2 * pair < p.k)
             task_pair<WPT>(st, npc2, G2, half * gh, abuf + (size_t)half * (p.F / 2 / 8) * 16, p.XS2, xsP, xoP, xsQ,
@@ -691,29 +876,34 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         }
         give(si);
         if (__any_sync(0xffffffffu, *abort_flag != 0)) continue;
-        const int use = rounds1 + j;  // reduction-slot uses continue from phase 1 (group 0)
-        float* rp = red + ((size_t)(0 * RR + (use % RR)) * 8 + warp) * 16;
-        slot_free(0, use);
-        if (c == pair) {  // lanes holding this pair's sums: row r of slot 2p (P), slot 2p+1 (Q)
+        float* rp = red + ((size_t)(G_DOWN * RR + (use % RR)) * 8 + warp) * 16;
+        slot_free(G_DOWN, use);
+        // the four lanes of a quad hold different groups: add them
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
+        acc[3] += __shfl_xor_sync(0xffffffffu, acc[3], 1);
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 2);
+        acc[3] += __shfl_xor_sync(0xffffffffu, acc[3], 2);
+        if (c == 0) {  // row r against slot 2p (P), row r against slot 2p+1 (Q)
           rp[r] = acc[0];
           rp[r + 8] = acc[3];
         }
-        if (!arrive_last(0, use, 8)) continue;
-        const float* rbuf = red + (size_t)(0 * RR + (use % RR)) * 8 * 16;
-        if (lane < 8) {
-          // row h = u*8 + lane: y_j = (half 0 + half 1) / S_j, prod_j = rb(y_j) * w_j,
-          // combined in the mlx_colsum_small_f32 association
-          float prod[MAXK];
+        if (!arrive_last(G_DOWN, use, 8)) continue;
+        const float* rbuf = red + (size_t)(G_DOWN * RR + (use % RR)) * 8 * 16;
+        // row h = u*8 + lane: y_j = (half 0 + half 1) / S_j, prod_j = rb(y_j) * w_j,
+        // combined in the mlx_colsum_small_f32 association
+        float prod[MAXK];
 #pragma unroll
-          for (int s = 0; s < MAXK; ++s) {
-            if (s < p.k) {
-              const int pr = s >> 1, q = s & 1;
-              const float y = (rbuf[(2 * pr) * 16 + q * 8 + lane] + rbuf[(2 * pr + 1) * 16 + q * 8 + lane]) * ainv[s];
-              prod[s] = b2q::rb(y) * sw[s];
-            } else {
-              prod[s] = 0.0f;
-            }
+        for (int s = 0; s < MAXK; ++s) {
+          if (s < p.k && lane < 8) {
+            const int pr = s >> 1, q = s & 1;
+            const float y = (rbuf[(2 * pr) * 16 + q * 8 + lane] + rbuf[(2 * pr + 1) * 16 + q * 8 + lane]) * ainv[s];
+            prod[s] = b2q::rb(y) * sw[s];
+          } else {
+            prod[s] = 0.0f;
           }
+        }
+        release_use(G_DOWN, use);  // partials read; fences shared memory only
+        if (lane < 8) {
           const int TY = p.k < 8 ? p.k : 8;
           float total = 0.0f;
 #pragma unroll
@@ -726,7 +916,6 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
           }
           p.out[(size_t)u * 8 + lane] = f2bf(total);
         }
-        release_use(0, use);
       }
     }
   }
@@ -740,6 +929,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       p.counters[0] = 0;
       p.counters[1] = 0;
       p.counters[2] = 0;
+      p.sched[0] = p.sched[1] = 0;
       __threadfence();
     }
   }
@@ -762,22 +952,22 @@ static int plan(D1Params& p, int mode) {
   p.off_x = off;
   off = round_up(off + p.XS1, 128);
   p.off_xs = off;
-  off = round_up(off + (2 * G1 + 2 * MAXK) * 4, 128);
+  off = round_up(off + (2 * G1 + 4 * MAXK) * 4, 128);
   if (mode == D1_FUSED) {
     const int G2 = p.F / p.gs;
     p.XS2 = round_up(p.F * 2, 128) + 64;
     p.off_act = off;
     off = round_up(off + MAXK * p.XS2, 128);
     p.off_acts = off;
-    off = round_up(off + (2 * MAXK * G2 + 2 * MAXK) * 4, 128);
+    off = round_up(off + (2 * MAXK * G2 + 4 * MAXK) * 4, 128);
   } else {
     p.XS2 = 0;
     p.off_act = p.off_acts = off;
   }
   p.off_red = off;
-  off = round_up(off + 8 * RR * 8 * 16 * 4, 128);
+  off = round_up(off + 9 * RR * 8 * 16 * 4, 128);
   p.off_misc = off;
-  off = round_up(off + 2 * NSLOT * 8 + 2 * 8 * RR * 4 + 16 + (2 * MAXK + NCW + NSLOT) * 4 + 64, 128);
+  off = round_up(off + 2 * NSLOT * 8 + 2 * 9 * RR * 4 + 16 + (2 * MAXK + 2 * NCW + 2 * NSLOT) * 4 + 64, 128);
   p.smem_bytes = off + 1024;
   DeviceInfo di;
   int rc = device_info(&di);
@@ -879,7 +1069,8 @@ bool d1_moe_eligible(int H, int E, int F, int k, int gs) {
 int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
-                  int k, int gs, int* err, unsigned* counters, float* ws_logits, uint16_t* ws_act, cudaStream_t st) {
+                  int k, int gs, int* err, unsigned* counters, unsigned* sched, float* ws_logits,
+                  uint16_t* ws_act, cudaStream_t st) {
   D1Params p;
   std::memset(&p, 0, sizeof(p));
   p.gs = gs;
@@ -896,6 +1087,7 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
   p.k = k;
   p.err = err;
   p.counters = counters;
+  p.sched = sched;
   p.ws_logits = ws_logits;
   p.ws_act = ws_act;
   p.timeout_ns = 2000000000ll;

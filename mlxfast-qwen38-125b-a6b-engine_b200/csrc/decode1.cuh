@@ -24,6 +24,7 @@ struct alignas(64) D1Params {
   int H, E, F, k;
   int* err;
   unsigned* counters;
+  unsigned* sched;  // [2] dynamic unit counters (fused)
   float* ws_logits;
   uint16_t* ws_act;
   long long timeout_ns;
@@ -38,6 +39,7 @@ bool d1_moe_eligible(int H, int E, int F, int k, int gs);
 int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
-                  int k, int gs, int* err, unsigned* counters, float* ws_logits, uint16_t* ws_act, cudaStream_t st);
+                  int k, int gs, int* err, unsigned* counters, unsigned* sched, float* ws_logits,
+                  uint16_t* ws_act, cudaStream_t st);
 
 }  // namespace b2q

@@ -13,9 +13,10 @@ namespace b2q {
 // Every workspace starts with this 256-byte header.
 struct WsHeader {
   int error;             // first device-side B2Q_E* code, 0 if none
-  unsigned counters[3];  // grid counters of the fused decode kernel
+  unsigned counters[3];  // grid counters of the fused decode kernels
   unsigned flag;         // self-test flag (never set)
-  unsigned pad[59];
+  unsigned sched[2];     // single-column decode kernel: next gate|up unit, next down unit
+  unsigned pad[57];
 };
 static_assert(sizeof(WsHeader) == 256, "workspace header is 256 bytes");
 

@@ -16,6 +16,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "tc.cuh"
 #include "engine.cuh"
 #include "host.hpp"
 #include "tmap.hpp"
@@ -566,9 +567,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
   if (warp == NC_WARPS) {
     // ------------------------------- producer -------------------------------
     if (fused) named_bar_sync(2, NTHREADS);  // wait for the routing
-    if (lane == 0) {
-      for (int i = 0; i < N_MAPS; ++i)
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.map[i])) : "memory");
+    // The whole warp runs the schedule (its values stay warp-uniform) and one
+    // elected lane issues each group of copies.
+    {
+      if (tc::elect_one())
+        for (int i = 0; i < N_MAPS; ++i)
+          asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.map[i])) : "memory");
       const uint64_t pol = policy_evict_first();
       // L2 prefetch cursor, PF_AHEAD passes ahead of the shared-memory loads:
       // it keeps more bytes in flight than the stage ring alone can hold.
@@ -578,7 +582,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
         if (pf_u >= sch.U) return;
         const Geo& pg = unit_is_down(p, sch, pf_u) ? p.g2 : p.g1;
         const LoadDesc d = describe(p, sch, pf_u, pf_pass, sidx, nullptr);
-        if (d.valid) {
+        if (d.valid && tc::elect_one()) {
           const int cw = d.kc * (pg.KC / 256);
           tma_prefetch_3d(&p.map[d.mwP], 0, d.rowP, cw);
           tma_prefetch_3d(&p.map[d.mwQ], 0, d.rowQ, cw);
@@ -611,7 +615,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
         for (int pass = 0; pass < np; ++pass, ++L) {
           const int NS = p.nstage;
           const int si = L % NS;
-          if (L >= NS && !bar_wait(&empty[si], ((L / NS) - 1) & 1, deadline, abort_flag)) {
+          if (L >= NS && !__all_sync(0xffffffffu, bar_wait(&empty[si], ((L / NS) - 1) & 1, deadline, abort_flag))) {
             if (!*abort_flag) record_error(err, B2Q_ETIMEOUT);
             *abort_flag = 1;
             ok = false;
@@ -621,9 +625,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
           prefetch_next();
           uint8_t* st = stages + (size_t)si * p.stage_bytes;
           if (!d.valid) {
-            mbar_arrive_expect_tx(&full[si], 0u);
+            if (tc::elect_one()) mbar_arrive_expect_tx(&full[si], 0u);
+            __syncwarp();
             continue;
           }
+          if (tc::elect_one()) {
           // a box always delivers its full size (out-of-range parts of a last,
           // shorter chunk are zero-filled), so the byte count is per box
           const uint32_t mbox = g.mswz ? (uint32_t)(g.GC / 64) * 1024u : 8u * (uint32_t)g.GC * 2u;
@@ -645,12 +651,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) engine_kernel(const __grid_consta
             tma_load_2d(mb + 2 * g.blkm, &p.map[d.msQ], cm, d.rowQ, &full[si], pol);
             tma_load_2d(mb + 3 * g.blkm, &p.map[d.mbQ], cm, d.rowQ, &full[si], pol);
           }
+          }
+          __syncwarp();
         }
       }
       // Drain: no copy may still be landing when the CTA exits.
       const uint64_t dl2 = globaltimer() + 200000000ull;
       for (int l = max(0, L - p.nstage); l < L; ++l) {
-        if (!bar_wait(&full[l % p.nstage], (l / p.nstage) & 1, dl2, nullptr)) record_error(err, B2Q_ETIMEOUT);
+        if (!bar_wait(&full[l % p.nstage], (l / p.nstage) & 1, dl2, nullptr) && lane == 0) record_error(err, B2Q_ETIMEOUT);
       }
     }
     __syncwarp();
