@@ -221,7 +221,7 @@ int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, co
   for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
   if (S == 1 && all_aligned && d1_moe_eligible(H, E, F, k, group_size))
     return d1_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size,
-                         &ws.hdr->error, ws.hdr->counters, ws.hdr->sched, ws.tagged, ws.act, st);
+                         &ws.hdr->error, ws.hdr->counters, ws.hdr->sched, ws.logits, ws.act, st);
   if (S == 1) {
     eng::Params p;
     base_params(p, eng::MODE_FUSED, group_size);

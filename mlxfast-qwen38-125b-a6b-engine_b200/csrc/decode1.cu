@@ -45,20 +45,16 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
 #include "decode1.cuh"
 #include "host.hpp"
-#include "stream_util.cuh"
 #include "tc.cuh"
 #include "tmap.hpp"
 
 namespace b2q {
 namespace d1 {
-
-using namespace su;
 
 constexpr int NCW = 8;                  // consumer warps
 constexpr int NCT = NCW * 32;
@@ -70,6 +66,9 @@ constexpr int SLOT = 10240;             // bytes per slot
 constexpr int TK = 1024;                // reduction values per gate|up / qmv task
 constexpr int RR = 4;                   // reduction-slot ring per warp group
 constexpr int MAXK = 8;                 // routed slots (fused decode)
+// Down units whose copies the producer issues before the activations are
+// staged: copies issued earlier queue in front of the staging loads.
+constexpr int DOWN_AHEAD = 1;
 
 // tensor-map slots
 enum : int { MW = 0, MS = 1, MB = 2, MWG = 0, MSG = 1, MBG = 2, MWU = 3, MSU = 4, MBU = 5, MWD = 6, MSD = 7, MBD = 8 };
@@ -89,6 +88,157 @@ struct Plan {
   int XS1, XS2;  // activation column strides
 };
 
+// Activation staging: stage_cols writes `ncols` columns of K values as scaled,
+// permuted fp16 chunks (x0 S, x4 S) (x1 S/16, x5 S/16) (x2 S, x6 S)
+// (x3 S/16, x7 S/16) and per group: xs = sum of x S, xo = 1024 * sum_even +
+// 1024 * sum_odd / 16 (the offset the nibble decode adds), inv = 1 / S.
+// Region layout: xs [cap][G], xo [cap][G], inv [MAXK], colmax [MAXK],
+// S [MAXK], S / 16 [MAXK].
+__device__ __forceinline__ float* c_xs(float* sums, int G, int col) { return sums + (size_t)col * G; }
+__device__ __forceinline__ float* c_xo(float* sums, int cap, int G, int col) { return sums + (size_t)(cap + col) * G; }
+__device__ __forceinline__ float* c_inv(float* sums, int cap, int G) { return sums + (size_t)2 * cap * G; }
+
+__device__ __forceinline__ uint32_t h2pack(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float lbf(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float hbf(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// A 16-byte load issued where it stands (volatile: not sunk towards its use),
+// L2-coherent (.cg) or through the non-coherent path (.nc).
+__device__ __forceinline__ uint4 ld_v4_now(const void* ptr, bool coherent) {
+  uint4 v;
+  if (coherent)
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ptr));
+  else
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ptr));
+  return v;
+}
+
+// max |value| of 8 bf16 as bf16 bits << 16, NaN clamped to +inf's bits
+__device__ __forceinline__ unsigned chunk_max(uint4 v) {
+  unsigned m = max(max(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), max(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
+  m = max(m & 0xffffu, m >> 16) << 16;
+  return m > 0x7f800000u ? 0x7f800000u : m;
+}
+
+// Activation staging. All NCT consumer threads call this (named barrier 1).
+// Column j is the K values at base + j * rstride. A max pass finds each
+// column's max |value| (every CTA stages the same rows, so every CTA finds the
+// same scales); the store pass writes the scaled, permuted fp16 chunks and
+// forms the group sums by a shuffle reduction over the gs / 8 lanes that hold
+// a group's chunks. Up to SC_REG chunks per thread stay in registers between
+// the passes (their loads all issued first), else each pass loads them.
+constexpr int SC_REG = 8;
+__device__ void stage_cols(uint8_t* dst, float* sums, int cap, int XS, const uint16_t* base, size_t rstride, int ncols,
+                           int K, int gs, bool coherent) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nch = K / 8, G = K / gs, CPG = gs / 8;
+  const int total = ncols * nch;
+  float* inv = c_inv(sums, cap, G);
+  unsigned* colmax = reinterpret_cast<unsigned*>(inv + MAXK);
+  float* colS = inv + 2 * MAXK;
+  float* colS16 = inv + 3 * MAXK;
+  // a warp's 32 consecutive chunks stay inside one column when nch is a multiple of 32
+  const bool warp_col = (nch % 32) == 0;
+  // q / nch by multiply-high: exact while q * nch < 2^32 / 8 (q < MAXK * nch)
+  const unsigned mdiv = 0xffffffffu / (unsigned)nch + 1u;
+  auto col_of = [&](int q) { return (int)__umulhi((unsigned)q, mdiv); };
+  auto src = [&](int q) {
+    const int col = col_of(q);
+    return base + (size_t)col * rstride + (size_t)(q - col * nch) * 8;
+  };
+  // max pass step over chunks q0 + [0, NCT) (q0 uniform)
+  auto max_step = [&](int q0, uint4 v) {
+    const int q = q0 + tid;
+    unsigned m = q < total ? chunk_max(v) : 0u;
+    const int col = col_of(q < total ? q : q0 + (tid & ~31));
+    if (warp_col) {
+      m = __reduce_max_sync(0xffffffffu, m);
+      if (lane == 0 && q0 + (tid & ~31) < total) atomicMax(&colmax[col], m);
+    } else if (q < total) {
+      atomicMax(&colmax[col], m);
+    }
+  };
+  // store pass step (q0 uniform; every lane takes part in the shuffles)
+  auto store_step = [&](int q0, uint4 v) {
+    const int q = q0 + tid;
+    const bool live = q < total;
+    const int col = live ? col_of(q) : 0, ch = live ? q - col * nch : 0;
+    const float S = colS[col], S16 = colS16[col];
+    uint4 o;
+    o.x = h2pack(lbf(v.x) * S, lbf(v.z) * S);
+    o.y = h2pack(hbf(v.x) * S16, hbf(v.z) * S16);
+    o.z = h2pack(lbf(v.y) * S, lbf(v.w) * S);
+    o.w = h2pack(hbf(v.y) * S16, hbf(v.w) * S16);
+    if (live) *reinterpret_cast<uint4*>(dst + (size_t)col * XS + (size_t)ch * 16) = o;
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&o.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&o.y));
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&o.z));
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&o.w));
+    float se = ((a.x + c.x) + a.y) + c.y;
+    float so = ((b.x + d.x) + b.y) + d.y;
+    for (int off = 1; off < CPG; off <<= 1) {
+      se += __shfl_xor_sync(0xffffffffu, se, off);
+      so += __shfl_xor_sync(0xffffffffu, so, off);
+    }
+    if (live && (ch % CPG) == 0) {
+      const int g = ch / CPG;
+      c_xs(sums, G, col)[g] = se + 16.0f * so;
+      c_xo(sums, cap, G, col)[g] = 1024.0f * se + 1024.0f * so;
+    }
+  };
+  // the power of two S = 2^e of each column from its max |value| bits: for a
+  // normal max with biased exponent x, max * 2^(137 - x) lies in [1024, 2048);
+  // e stays in [-100, 100] (0 for a zero, infinite or NaN max)
+  auto set_scales = [&]() {
+    if (tid < ncols) {
+      const unsigned mb = colmax[tid];
+      int e = 0;
+      if (mb != 0u && mb < 0x7f800000u) e = min(100, max(-100, 137 - (int)(mb >> 23)));
+      inv[tid] = __int_as_float((127 - e) << 23);
+      colS[tid] = __int_as_float((127 + e) << 23);
+      colS16[tid] = __int_as_float((123 + e) << 23);
+    }
+  };
+  if (tid < MAXK) colmax[tid] = 0u;
+  if (total <= SC_REG * NCT) {
+    uint4 keep[SC_REG];
+#pragma unroll
+    for (int i = 0; i < SC_REG; ++i) {
+      const int q = i * NCT + tid;
+      keep[i] = q < total ? ld_v4_now(src(q), coherent) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    named_bar_sync(1, NCT);
+#pragma unroll
+    for (int i = 0; i < SC_REG; ++i)
+      if (i * NCT < total) max_step(i * NCT, keep[i]);
+    named_bar_sync(1, NCT);
+    set_scales();
+    named_bar_sync(1, NCT);
+#pragma unroll
+    for (int i = 0; i < SC_REG; ++i)
+      if (i * NCT < total) store_step(i * NCT, keep[i]);
+  } else {
+    auto load = [&](int q) {
+      if (q >= total) return make_uint4(0u, 0u, 0u, 0u);
+      const uint4* sp = reinterpret_cast<const uint4*>(src(q));
+      return coherent ? __ldcg(sp) : __ldg(sp);
+    };
+    named_bar_sync(1, NCT);
+    for (int q0 = 0; q0 < total; q0 += NCT) max_step(q0, load(q0 + tid));
+    named_bar_sync(1, NCT);
+    set_scales();
+    named_bar_sync(1, NCT);
+    for (int q0 = 0; q0 < total; q0 += NCT) store_step(q0, load(q0 + tid));
+  }
+  named_bar_sync(1, NCT);
+}
 
 // ---------------------------------------------------------------------------
 // consumers: one task = npc 128-byte pieces of the 16 rows
@@ -98,6 +248,18 @@ struct Plan {
 // piece j of the 8 rows, 16-byte unit u of row r at unit position u ^ r.
 // Lane (r = lane / 4, c = lane % 4) takes word 4u + c of row r of P and of Q
 // (MMA rows r and r + 8).
+__device__ __forceinline__ void word_mma(const uint8_t* wp, int qoff, const uint4 xv, bool first, float (&d)[4]) {
+  const uint32_t W0 = *reinterpret_cast<const uint32_t*>(wp);
+  const uint32_t W8 = *reinterpret_cast<const uint32_t*>(wp + qoff);
+  uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
+  decode_word_h(W0, p0, p1, p2, p3);
+  decode_word_h(W8, q0, q1, q2, q3);
+  if (first)
+    mma_f16_16816_zero(d, p0, q0, p1, q1, xv.x, xv.y);
+  else
+    mma_f16_16816(d, p0, q0, p1, q1, xv.x, xv.y);
+  mma_f16_16816(d, p2, q2, p3, q3, xv.z, xv.w);
+}
 
 // Single activation column (qmv, gate|up): the quad lanes finish groups c of
 // each batch of NB groups; acc[0] row r (P), acc[2] row r + 8 (Q).
@@ -204,6 +366,26 @@ __device__ __forceinline__ void task_pair(const uint8_t* st, int npc, int GB, in
 // ---------------------------------------------------------------------------
 // routing (Runner/FastModel/TrackFastMoE.swift:767-911)
 // ---------------------------------------------------------------------------
+// softmax over the k selected logits held by lanes 0..k-1 (slot order): max,
+// exp, per-lane partial sums of 4 then a butterfly, as the reference's
+// softmax over its k values (Runner/FastModel/TrackFastMoE.swift:846-880)
+__device__ void softmax_k(float selv, int k, float* sw) {
+  const int lane = threadIdx.x & 31;
+  float mx = (lane < k) ? selv : -INFINITY;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float ex = (lane < k) ? expf(selv - mx) : 0.0f;
+  float part = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float t = __shfl_sync(0xffffffffu, ex, (4 * lane + i) & 31);
+    part += (lane < 8) ? t : 0.0f;
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+  const float inv = 1.0f / part;
+  if (lane < k) sw[lane] = ex * inv;
+}
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -325,22 +507,6 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       __syncwarp();
       return true;
     };
-    // L2 prefetch of this CTA's down rows (the routed experts' rows of its
-    // static down units): 8 contiguous weight rows and their scale / bias rows
-    // per (unit, slot), split over the producer warps
-    const int pf_mode = fused ? p.pf_mode : 0;
-    auto prefetch_down = [&]() {
-      const int nl2 = local_units(fused ? p.H / 8 : 0);
-      const size_t wrow = (size_t)p.F / 2, mrow = (size_t)(p.F / p.gs) * 2;
-      for (int q = lane; q < nl2 * p.k; q += 32) {
-        const int j2 = q / p.k, s2 = q - j2 * p.k;
-        if (j2 % NPW != pw) continue;
-        const size_t row0 = (size_t)sidx[s2] * p.H + (size_t)(blockIdx.x + j2 * gridDim.x) * 8;
-        bulk_prefetch_l2(p.wd_raw + row0 * wrow, (uint32_t)(8 * wrow));
-        bulk_prefetch_l2(p.sd_raw + row0 * mrow, (uint32_t)(8 * mrow));
-        bulk_prefetch_l2(p.bd_raw + row0 * mrow, (uint32_t)(8 * mrow));
-      }
-    };
     bool ok = true;
     const int GB1 = TK / p.gs;
     if (!fused) {
@@ -374,25 +540,15 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         gdone[gi] = gi % NPW != pw;
         ng += gdone[gi] ? 0 : 1;
       }
-      if (pf_mode == 1) prefetch_down();
       if (ng > 0) {
-        // the first round is static (unit b * G1grp + gi for group gi of CTA
-        // b), so its copies go out without waiting for an atomic; the counter
-        // hands out the units after those
-        const unsigned nstatic = gridDim.x * (unsigned)G1grp;
         unsigned nxt = (lane == 0) ? atomicAdd(&p.sched[0], (unsigned)ng) : 0u;
         int left = ng;
-        bool first = true;
         while (ok && left > 0) {
-          unsigned base = 0;
-          if (!first) {
-            base = __shfl_sync(0xffffffffu, nxt, 0) + nstatic;
-            if (lane == 0 && base < (unsigned)ph1.units) nxt = atomicAdd(&p.sched[0], (unsigned)ng);
-          }
+          const unsigned base = __shfl_sync(0xffffffffu, nxt, 0);
+          if (lane == 0 && base < (unsigned)ph1.units) nxt = atomicAdd(&p.sched[0], (unsigned)ng);
           for (int gi = pw, k = 0; ok && gi < G1grp; gi += NPW, ++k) {
             if (gdone[gi]) continue;
-            const unsigned uu = first ? blockIdx.x * (unsigned)G1grp + gi : base + k;
-            const int u = uu < (unsigned)ph1.units ? (int)uu : -1;
+            const int u = base + k < (unsigned)ph1.units ? (int)(base + k) : -1;
             if (u >= 0) {
               const int z = u / (p.F / 8), rb = u % (p.F / 8);
               const int row = (int)(sidx[z] * (uint32_t)p.F) + rb * 8;
@@ -409,10 +565,8 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
             }
             ++jr[gi];
           }
-          first = false;
         }
       }
-      if (pf_mode == 2) prefetch_down();
       // phase-1 fill counts of every consumer warp, for the down ordinals
       if (lane == 0)
         for (int gi = pw; gi < G1grp; gi += NPW)
@@ -432,7 +586,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       for (int i = 0; i < 8 / NPW; ++i) n0[i] = p1n[pw * (8 / NPW) + i];
       bool staged = false;  // barrier 3: the consumers staged the activations
       for (int j2 = 0; ok && j2 <= nl2; ++j2) {
-        if (j2 == p.down_ahead) {
+        if (j2 == DOWN_AHEAD) {
           named_bar_sync(3, NTH);
           staged = true;
         }
@@ -469,29 +623,18 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
     const int r = lane >> 2, c = lane & 3;
 
     if (fused) {
-      // router rows of this CTA (all of a thread's loads issued first); each
-      // logit is published as one 64-bit store of (value bits | 1 << 32), so
-      // a reader that sees the tag also sees the value
+      // router rows of this CTA, then a grid-wide count of finished rows
       const int nvec = p.H / 8;
-      constexpr int RV = 4;  // 16-byte loads of x and of the row per thread and pass
+      int rows_done = 0;
       for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
         float part = 0.0f;
-        for (int v0 = 0; v0 < nvec; v0 += RV * NCT) {
-          uint4 xv[RV], wv[RV];
-#pragma unroll
-          for (int i = 0; i < RV; ++i) {
-            const int v = v0 + i * NCT + tid;
-            const bool in = v < nvec;
-            xv[i] = in ? __ldg(reinterpret_cast<const uint4*>(p.x) + v) : make_uint4(0u, 0u, 0u, 0u);
-            wv[i] = in ? __ldg(reinterpret_cast<const uint4*>(p.wr + (size_t)e * p.H) + v) : make_uint4(0u, 0u, 0u, 0u);
-          }
-#pragma unroll
-          for (int i = 0; i < RV; ++i) {
-            part += lbf(xv[i].x) * lbf(wv[i].x) + hbf(xv[i].x) * hbf(wv[i].x);
-            part += lbf(xv[i].y) * lbf(wv[i].y) + hbf(xv[i].y) * hbf(wv[i].y);
-            part += lbf(xv[i].z) * lbf(wv[i].z) + hbf(xv[i].z) * hbf(wv[i].z);
-            part += lbf(xv[i].w) * lbf(wv[i].w) + hbf(xv[i].w) * hbf(wv[i].w);
-          }
+        for (int v = tid; v < nvec; v += NCT) {
+          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(p.x) + v);
+          const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.wr + (size_t)e * p.H) + v);
+          part += lbf(xv.x) * lbf(wv.x) + hbf(xv.x) * hbf(wv.x);
+          part += lbf(xv.y) * lbf(wv.y) + hbf(xv.y) * hbf(wv.y);
+          part += lbf(xv.z) * lbf(wv.z) + hbf(xv.z) * hbf(wv.z);
+          part += lbf(xv.w) * lbf(wv.w) + hbf(xv.w) * hbf(wv.w);
         }
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
@@ -500,89 +643,65 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         if (tid == 0) {
           float lg = 0.0f;
           for (int w = 0; w < NCW; ++w) lg += rsum[w];
-          st_relaxed_u64(p.ws_tagged + e, (1ull << 32) | __float_as_uint(lg));
+          p.ws_logits[e] = lg;
         }
         named_bar_sync(1, NCT);
+        ++rows_done;
+      }
+      if (tid == 0 && rows_done) {
+        __threadfence();
+        atomicAdd(&p.counters[0], (unsigned)rows_done);
       }
       {
         // stage x while the other CTAs finish their router rows
-        stage_cols<NCT>(xbuf, xsum, 1, p.XS1, p.x, 0, 1, p.K1, p.gs, false);
+        stage_cols(xbuf, xsum, 1, p.XS1, p.x, 0, 1, p.K1, p.gs, false);
       }
-      // top-k by rank: expert e is selected at slot rank(e) when rank(e) < k,
-      // rank(e) = #{j : v_j > v_e or (v_j == v_e and j < e)} (largest first, ties
-      // to the lower index, as the sequential selection); NaN ranks as -inf.
-      // Keys: order-preserving bits of the value above ~e, so one unsigned
-      // 64-bit compare decides "j before e".
-      unsigned long long* keys = reinterpret_cast<unsigned long long*>(red);  // free until phase 1
-      for (int e = tid; e < p.E; e += NCT) {
-        unsigned long long t = 0;
-        bool got = false;
-        while (!*abort_flag) {
-          t = ld_relaxed_u64(p.ws_tagged + e);
-          if ((t >> 32) == 1ull) {
-            got = true;
-            break;
-          }
-          if (globaltimer() > deadline) {
-            record_error(p.err, B2Q_ETIMEOUT);
-            *abort_flag = 1;
-          }
+      if (tid == 0) {
+        // acquire load of the count; the CTA barrier below orders the
+        // other threads' reads after it
+        if (!wait_counter_geq(&p.counters[0], (unsigned)p.E, deadline, abort_flag)) {
+          record_error(p.err, B2Q_ETIMEOUT);
+          *abort_flag = 1;
         }
-        float v = got ? __uint_as_float((uint32_t)t) : 0.0f;
-        if (blockIdx.x == 0 && p.logits_out) p.logits_out[e] = v;
-        v = (v != v) ? -INFINITY : v;
-        v = (v == 0.0f) ? 0.0f : v;  // -0 and +0 compare equal
-        const uint32_t u = __float_as_uint(v);
-        const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-        keys[e] = ((unsigned long long)ord << 32) | (0xffffffffu - (uint32_t)e);
       }
       named_bar_sync(1, NCT);
-      auto key_value = [](unsigned long long key) {
-        const uint32_t ord = (uint32_t)(key >> 32);
-        return __uint_as_float((ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord);
-      };
-      if (2 * p.E <= NCT) {
-        // two adjacent lanes per expert, each counting half of the keys
-        const int e = tid >> 1, h = tid & 1;
+      // top-k by rank: expert e is selected at slot rank(e) when rank(e) < k,
+      // rank(e) = #{j : v_j > v_e or (v_j == v_e and j < e)} (largest first, ties
+      // to the lower index, as the sequential selection); NaN ranks as -inf
+      float* lgs = reinterpret_cast<float*>(abuf);  // scratch before the down phase
+      float* sval = lgs + p.E;
+      for (int e = tid; e < p.E; e += NCT) {
+        const float v = *abort_flag ? 0.0f : __ldcg(p.ws_logits + e);
+        lgs[e] = (v != v) ? -INFINITY : v;
+      }
+      named_bar_sync(1, NCT);
+      for (int e = tid; e < p.E; e += NCT) {
+        const float v = lgs[e];
         int rank = 0;
-        unsigned long long ke = 0;
-        if (e < p.E) {
-          ke = keys[e];
-          const int lo = h ? p.E / 2 : 0, hi = h ? p.E : p.E / 2;
-          for (int j = lo; j < hi; ++j) rank += keys[j] > ke ? 1 : 0;
+        for (int j = 0; j < p.E; ++j) {
+          const float vj = lgs[j];
+          rank += (vj > v || (vj == v && j < e)) ? 1 : 0;
         }
-        rank += __shfl_xor_sync(0xffffffffu, rank, 1);
-        if (e < p.E && h == 0 && rank < p.k) {
+        if (rank < p.k) {
           sidx[rank] = (uint32_t)e;
-          sw[rank] = key_value(ke);
-        }
-      } else {
-        for (int e = tid; e < p.E; e += NCT) {
-          const unsigned long long ke = keys[e];
-          int rank = 0;
-          for (int j = 0; j < p.E; ++j) rank += keys[j] > ke ? 1 : 0;
-          if (rank < p.k) {
-            sidx[rank] = (uint32_t)e;
-            sw[rank] = key_value(ke);
-          }
+          sval[rank] = v;
         }
       }
       named_bar_sync(1, NCT);
       if (warp == 0) {
-        // sw holds the selected logits until softmax_k overwrites them
-        const float sv = lane < p.k ? sw[lane] : -INFINITY;
-        __syncwarp();
-        softmax_k(sv, p.k, sw);
+        softmax_k(lane < p.k ? sval[lane] : -INFINITY, p.k, sw);
         __syncwarp();
         if (blockIdx.x == 0 && lane < p.k) {
           if (p.idx_out) p.idx_out[lane] = sidx[lane];
           if (p.w_out) p.w_out[lane] = sw[lane];
         }
+        if (blockIdx.x == 0 && p.logits_out)
+          for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
       }
       named_bar_sync(2, NTH);  // releases the producer
     }
     if (!fused) {
-      stage_cols<NCT>(xbuf, xsum, 1, p.XS1, p.x, 0, 1, p.K1, p.gs, false);
+      stage_cols(xbuf, xsum, 1, p.XS1, p.x, 0, 1, p.K1, p.gs, false);
     }
     const float* xs1 = c_xs(xsum, G1, 0);
     const float* xo1 = c_xo(xsum, 1, G1, 0);
@@ -727,7 +846,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       }
       named_bar_sync(1, NCT);
       {
-        stage_cols<NCT>(abuf, asum, p.k, p.XS2, p.ws_act, (size_t)p.F, p.k, p.F, p.gs, true);
+        stage_cols(abuf, asum, p.k, p.XS2, p.ws_act, (size_t)p.F, p.k, p.F, p.gs, true);
       }
       named_bar_arrive(3, NTH);  // the producer may issue the remaining down copies
       const int pair = warp >> 1, half = warp & 1;
@@ -807,8 +926,6 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
     __threadfence();
     const unsigned prev = atomicAdd(&p.counters[2], 1u);
     if (prev == gridDim.x - 1) {
-      // every CTA has read the logits: clear their tags for the next call
-      for (int e = 0; e < p.E; ++e) p.ws_tagged[e] = 0ull;
       p.counters[0] = 0;
       p.counters[1] = 0;
       p.counters[2] = 0;
@@ -825,11 +942,6 @@ namespace b2q {
 namespace d1 {
 
 static int round_up(int v, int a) { return (v + a - 1) / a * a; }
-
-static int env_int(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return v ? atoi(v) : dflt;
-}
 
 static int plan(D1Params& p, int mode) {
   const int G1 = p.K1 / p.gs;
@@ -957,7 +1069,7 @@ bool d1_moe_eligible(int H, int E, int F, int k, int gs) {
 int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
-                  int k, int gs, int* err, unsigned* counters, unsigned* sched, unsigned long long* ws_tagged,
+                  int k, int gs, int* err, unsigned* counters, unsigned* sched, float* ws_logits,
                   uint16_t* ws_act, cudaStream_t st) {
   D1Params p;
   std::memset(&p, 0, sizeof(p));
@@ -976,13 +1088,8 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
   p.err = err;
   p.counters = counters;
   p.sched = sched;
-  p.ws_tagged = ws_tagged;
+  p.ws_logits = ws_logits;
   p.ws_act = ws_act;
-  p.wd_raw = reinterpret_cast<const uint8_t*>(wd);
-  p.sd_raw = reinterpret_cast<const uint8_t*>(sd);
-  p.bd_raw = reinterpret_cast<const uint8_t*>(bd);
-  p.pf_mode = env_int("B2Q_D1_PF", 2);
-  p.down_ahead = env_int("B2Q_D1_AHEAD", 1);
   p.timeout_ns = 2000000000ll;
   int rc = plan(p, D1_FUSED);
   if (rc) return rc;

@@ -25,13 +25,8 @@ struct alignas(64) D1Params {
   int* err;
   unsigned* counters;
   unsigned* sched;  // [2] dynamic unit counters (fused)
-  unsigned long long* ws_tagged;  // [E] router logits tagged for publication (zero between calls)
+  float* ws_logits;
   uint16_t* ws_act;
-  const uint8_t* wd_raw;  // down weights / scales / biases (L2 prefetch of the down rows)
-  const uint8_t* sd_raw;
-  const uint8_t* bd_raw;
-  int pf_mode;     // when the down rows are prefetched into L2: 0 never, 1 after routing, 2 after the gate|up issue
-  int down_ahead;  // down units whose copies are issued before the activations are staged
   long long timeout_ns;
   int off_slots, off_x, off_xs, off_act, off_acts, off_red, off_misc, smem_bytes;
   int XS1, XS2;
@@ -44,7 +39,7 @@ bool d1_moe_eligible(int H, int E, int F, int k, int gs);
 int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
-                  int k, int gs, int* err, unsigned* counters, unsigned* sched, unsigned long long* ws_tagged,
+                  int k, int gs, int* err, unsigned* counters, unsigned* sched, float* ws_logits,
                   uint16_t* ws_act, cudaStream_t st);
 
 }  // namespace b2q

@@ -40,9 +40,6 @@ struct DecodeWs {
   uint32_t* idx;
   float* w;
   uint16_t* act;
-  // router logits of the one-token decode kernel, each tagged for
-  // publication (value bits | 1 << 32); all zero between calls
-  unsigned long long* tagged;
   size_t bytes;
 };
 
@@ -60,8 +57,6 @@ static inline DecodeWs decode_ws_layout(void* base, int S, int E, int F, int k) 
   off = align256(off + sizeof(float) * (size_t)S * k);
   d.act = reinterpret_cast<uint16_t*>(b + off);
   off = align256(off + sizeof(uint16_t) * (size_t)S * k * F);
-  d.tagged = reinterpret_cast<unsigned long long*>(b + off);
-  off = align256(off + sizeof(unsigned long long) * (size_t)E);
   d.bytes = off;
   return d;
 }
