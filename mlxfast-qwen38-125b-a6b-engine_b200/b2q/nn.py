@@ -86,13 +86,38 @@ class MoE:
         self.experts = experts  # wg/sg/bg, wu/su/bu, wd/sd/bd
         self.top_k = top_k
         self.group_size, self.bits = group_size, bits
+        # The one-token call is host-latency bound: its weight pointers and
+        # shape arguments are fixed per layer, so they are prepared once.
+        ops._dev(router_weight, "router_weight", ops._BF16)
+        for n in ("wg", "sg", "bg", "wu", "su", "bu", "wd", "sd", "bd"):
+            ops._dev(experts[n], n, ops._PACK if n.startswith("w") else ops._BF16)
+        self._E, self._H = router_weight.shape
+        self._F = experts["wg"].shape[1]
+        self._wptrs = (router_weight.data_ptr(),) + tuple(
+            experts[n].data_ptr() for n in ("wg", "sg", "bg", "wu", "su", "bu", "wd", "sd", "bd"))
+        self._ws1 = None
 
     @property
     def num_experts(self) -> int:
         return self.router_weight.shape[0]
 
+    def _decode_one(self, x2: torch.Tensor) -> torch.Tensor:
+        """One token through the fused decode operator with the prepared arguments."""
+        if x2.dtype != torch.bfloat16 or x2.device.type != "cuda" or x2.shape[1] != self._H:
+            raise ValueError("x: expected a CUDA bf16 tensor [1, H] matching the router weight")
+        if self._ws1 is None or self._ws1.buf.device != x2.device:
+            size = ops.lib().b2q_moe_decode_workspace_size(1, self._H, self._E, self._F, self.top_k)
+            self._ws1 = ops.Workspace(size, x2.device)
+        out = torch.empty((1, self._H), dtype=torch.bfloat16, device=x2.device)
+        ops.check(ops.lib().b2q_moe_decode(x2.data_ptr(), *self._wptrs, out.data_ptr(), None, None, None, 1, self._H,
+                                           self._E, self._F, self.top_k, self.group_size, self.bits, self._ws1.ptr(),
+                                           self._ws1.buf.numel(), ops._stream(x2.device)))
+        return out
+
     def __call__(self, x: torch.Tensor, return_routing: bool = False):
         x2 = x.contiguous().view(-1, x.shape[-1])
+        if x2.shape[0] == 1 and not return_routing:
+            return self._decode_one(x2).view(x.shape)
         if x2.shape[0] <= 8:
             r = ops.moe_decode(x2, self.router_weight, self.experts, self.top_k, self.group_size, self.bits,
                                return_routing=return_routing)

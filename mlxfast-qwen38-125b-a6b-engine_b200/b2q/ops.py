@@ -27,8 +27,17 @@ __all__ = [
 ]
 
 
-def _stream():
-    return torch.cuda.current_stream().cuda_stream
+try:  # the raw handle without building a torch.cuda.Stream object (a per-call cost)
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
+def _stream(device=None):
+    if _raw_stream is not None:
+        idx = device.index if device is not None and device.index is not None else torch.cuda.current_device()
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 def _dev(t: torch.Tensor, name: str, dtypes) -> torch.Tensor:

@@ -46,6 +46,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "decode1.cuh"
@@ -1018,6 +1019,58 @@ static int launch(const D1Params& p, int mode, cudaStream_t st) {
   }
 }
 
+// Tensor maps of recently used weight sets. Encoding the (up to nine) maps of
+// a call costs microseconds of host time, while a model calls the same layers
+// over and over; maps depend only on addresses, shapes and boxes, so an entry
+// keyed by those stays valid whatever the buffers hold. Least recently used
+// entries are replaced.
+struct MapKey {
+  const void* ptr[9];
+  int device, mode, a, b, c, gs;
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map[9];
+  uint64_t stamp;
+};
+constexpr int MAP_CACHE = 128;
+static std::mutex g_map_mu;
+static MapEntry g_maps[MAP_CACHE];
+static uint64_t g_map_clock = 0;
+
+static MapKey map_key(int mode, const void* const* ptrs, int n, int a, int b, int c, int gs) {
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));  // padding included: keys compare bytewise
+  for (int i = 0; i < n; ++i) k.ptr[i] = ptrs[i];
+  cudaGetDevice(&k.device);
+  k.mode = mode;
+  k.a = a;
+  k.b = b;
+  k.c = c;
+  k.gs = gs;
+  return k;
+}
+static bool find_maps(const MapKey& k, CUtensorMap* out, int n) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  for (MapEntry& e : g_maps) {
+    if (e.stamp && std::memcmp(&e.key, &k, sizeof(k)) == 0) {
+      std::memcpy(out, e.map, sizeof(CUtensorMap) * n);
+      e.stamp = ++g_map_clock;
+      return true;
+    }
+  }
+  return false;
+}
+static void put_maps(const MapKey& k, const CUtensorMap* m, int n) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  MapEntry* victim = &g_maps[0];
+  for (MapEntry& e : g_maps)
+    if (e.stamp < victim->stamp) victim = &e;
+  victim->key = k;
+  std::memcpy(victim->map, m, sizeof(CUtensorMap) * n);
+  victim->stamp = ++g_map_clock;
+}
+
 // weights: 3-D 128-byte-swizzled map, box of 8 rows x `box_bytes` of each row;
 // scales / biases: 2-D map, box of 8 rows x `mbox_bytes`
 static int set_family(D1Params& p, int mw, int ms, int mb, const uint32_t* w, const uint16_t* s, const uint16_t* b,
@@ -1051,8 +1104,13 @@ int d1_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16
   p.timeout_ns = 2000000000ll;
   int rc = plan(p, D1_QMV);
   if (rc) return rc;
-  rc = set_family(p, MW, MS, MB, w, s, b, (uint64_t)N, K, TK / 2, (TK / gs) * 2);
-  if (rc) return rc;
+  const void* ptrs[3] = {w, s, b};
+  const MapKey key = map_key(D1_QMV, ptrs, 3, N, K, 0, gs);
+  if (!find_maps(key, p.map, 3)) {
+    rc = set_family(p, MW, MS, MB, w, s, b, (uint64_t)N, K, TK / 2, (TK / gs) * 2);
+    if (rc) return rc;
+    put_maps(key, p.map, 3);
+  }
   return launch(p, D1_QMV, st);
 }
 
@@ -1093,13 +1151,18 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
   p.timeout_ns = 2000000000ll;
   int rc = plan(p, D1_FUSED);
   if (rc) return rc;
-  const uint64_t rgu = (uint64_t)E * F, rd = (uint64_t)E * H;
-  rc = set_family(p, MWG, MSG, MBG, wg, sg, bg, rgu, H, TK / 2, (TK / gs) * 2);
-  if (rc) return rc;
-  rc = set_family(p, MWU, MSU, MBU, wu, su, bu, rgu, H, TK / 2, (TK / gs) * 2);
-  if (rc) return rc;
-  rc = set_family(p, MWD, MSD, MBD, wd, sd, bd, rd, F, F / 4, (F / gs) * 2);
-  if (rc) return rc;
+  const void* ptrs[9] = {wg, sg, bg, wu, su, bu, wd, sd, bd};
+  const MapKey key = map_key(D1_FUSED, ptrs, 9, H, E, F, gs);
+  if (!find_maps(key, p.map, 9)) {
+    const uint64_t rgu = (uint64_t)E * F, rd = (uint64_t)E * H;
+    rc = set_family(p, MWG, MSG, MBG, wg, sg, bg, rgu, H, TK / 2, (TK / gs) * 2);
+    if (rc) return rc;
+    rc = set_family(p, MWU, MSU, MBU, wu, su, bu, rgu, H, TK / 2, (TK / gs) * 2);
+    if (rc) return rc;
+    rc = set_family(p, MWD, MSD, MBD, wd, sd, bd, rd, F, F / 4, (F / gs) * 2);
+    if (rc) return rc;
+    put_maps(key, p.map, 9);
+  }
   return launch(p, D1_FUSED, st);
 }
 
