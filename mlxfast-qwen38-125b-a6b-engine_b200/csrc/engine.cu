@@ -1065,7 +1065,8 @@ __global__ void route_kernel(const float* __restrict__ logits, uint32_t* __restr
 // steps of 64 through double-buffered shared memory (cp.async), 8 warps each
 // 16 tokens x 32 experts with mma.sync m16n8k16 (bf16 products are exact in
 // fp32; fp32 accumulation).
-constexpr int RT_BM = 32, RT_BN = 128, RT_BK = 64, RT_LD = RT_BK + 8;  // padded rows: 144 bytes
+// 16 tokens x 128 experts per CTA (2048 tokens: 128 CTAs); padded rows: 144 bytes
+constexpr int RT_BM = 16, RT_BN = 128, RT_BK = 64, RT_LD = RT_BK + 8;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(pred ? 16 : 0)
@@ -1084,7 +1085,7 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
   __shared__ __align__(16) uint16_t ws[2][RT_BN * RT_LD];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * RT_BM, e0 = blockIdx.y * RT_BN;
-  const int wm = (warp & 1) * 16, wn = (warp >> 1) * 32;
+  const int wn = warp * 16;  // 8 warps x 16 experts
   auto load = [&](int buf, int k0) {
     // x: 32 rows x 8 chunks of 16 bytes; wr: 128 rows x 8 chunks
     for (int i = tid; i < RT_BM * 8; i += 256) {
@@ -1099,7 +1100,7 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  float acc[4][4] = {};
+  float acc[2][4] = {};
   const int nk = H / RT_BK;
   load(0, 0);
   for (int kt = 0; kt < nk; ++kt) {
@@ -1115,25 +1116,22 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
 #pragma unroll
     for (int kk = 0; kk < RT_BK; kk += 16) {
       uint32_t a[4];
-      ldmatrix_x4(a, xb + (wm + (lane & 15)) * RT_LD + kk + (lane >> 4) * 8);
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t b[4];
-        const int m = lane >> 3, r = lane & 7;
-        ldmatrix_x4(b, wb + (wn + np * 16 + (m >> 1) * 8 + r) * RT_LD + kk + (m & 1) * 8);
-        mma_bf16_16816(acc[np * 2], a[0], a[1], a[2], a[3], b[0], b[1]);
-        mma_bf16_16816(acc[np * 2 + 1], a[0], a[1], a[2], a[3], b[2], b[3]);
-      }
+      ldmatrix_x4(a, xb + (lane & 15) * RT_LD + kk + (lane >> 4) * 8);
+      uint32_t b[4];
+      const int m = lane >> 3, r = lane & 7;
+      ldmatrix_x4(b, wb + (wn + (m >> 1) * 8 + r) * RT_LD + kk + (m & 1) * 8);
+      mma_bf16_16816(acc[0], a[0], a[1], a[2], a[3], b[0], b[1]);
+      mma_bf16_16816(acc[1], a[0], a[1], a[2], a[3], b[2], b[3]);
     }
     __syncthreads();
   }
   const int g = lane >> 2, q = lane & 3;
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
+  for (int nt = 0; nt < 2; ++nt) {
     const int e = e0 + wn + nt * 8 + 2 * q;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int t = t0 + wm + g + h * 8;
+      const int t = t0 + g + h * 8;
       if (t < T) {
         if (e < E) logits[(size_t)t * E + e] = acc[nt][2 * h];
         if (e + 1 < E) logits[(size_t)t * E + e + 1] = acc[nt][2 * h + 1];

@@ -53,6 +53,61 @@ __global__ void sorted_combine_kernel(const uint16_t* __restrict__ y, const uint
   out[(size_t)t * H + h] = f2bf(total);
 }
 
+// The same combine for 8 consecutive outputs per thread (16-byte loads of the
+// k rows and one 16-byte store); H % 8 == 0, 16-byte aligned rows.
+__global__ void sorted_combine8_kernel(const uint16_t* __restrict__ y, const uint32_t* __restrict__ inverse,
+                                       const float* __restrict__ w, uint16_t* __restrict__ out, int T, int H,
+                                       int k) {
+  const int h0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int t = blockIdx.y;
+  if (h0 >= H || t >= T) return;
+  const int TY = k < 8 ? k : 8;
+  float tt[8][8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+#pragma unroll
+    for (int v = 0; v < 8; ++v) tt[q][v] = 0.0f;
+  for (int j = 0; j < k; ++j) {
+    const uint32_t pj = __ldg(inverse + (size_t)t * k + j);
+    const float wj = __ldg(w + (size_t)t * k + j);
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(y + (size_t)pj * H + h0));
+    const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+    const int q = j % TY;
+#pragma unroll
+    for (int qq = 0; qq < 8; ++qq) {
+      if (qq != q) continue;
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const uint32_t word = rw[v >> 1];
+        const float yv = __uint_as_float((v & 1) ? (word & 0xffff0000u) : (word << 16));
+        tt[qq][v] = __fmul_rn(yv, wj) + tt[qq][v];  // product rounded, then added
+      }
+    }
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int v = 0; v < 8; v += 2) {
+    float t0 = tt[0][v], t1 = tt[0][v + 1];
+    for (int q = 1; q < TY; ++q) {
+      t0 = tt[q][v] + t0;
+      t1 = tt[q][v + 1] + t1;
+    }
+    o[v >> 1] = (uint32_t)f2bf(t0) | ((uint32_t)f2bf(t1) << 16);
+  }
+  *reinterpret_cast<uint4*>(out + (size_t)t * H + h0) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+static void launch_sorted_combine(const uint16_t* y, const uint32_t* inverse, const float* w, uint16_t* out, int T,
+                                  int H, int k, cudaStream_t st) {
+  if (H % 8 == 0 && aligned16(y) && aligned16(out)) {
+    dim3 grid((H / 8 + 255) / 256, T);
+    sorted_combine8_kernel<<<grid, 256, 0, st>>>(y, inverse, w, out, T, H, k);
+  } else {
+    dim3 grid((H + 255) / 256, T);
+    sorted_combine_kernel<<<grid, 256, 0, st>>>(y, inverse, w, out, T, H, k);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // gather_qmm / quantized_matmul with many rows per weight matrix (M > 8): the
 // tcgen05 grouped GEMM over rows grouped by weight matrix.
@@ -251,8 +306,7 @@ int b2q_moe_sorted_combine(const uint16_t* y, const uint32_t* inverse, const flo
   if (T < 0 || H <= 0 || k < 1 || k > 32) return set_error(B2Q_EINVAL, "sorted_combine: bad shape");
   if (T == 0) return B2Q_OK;
   if (!y || !inverse || !w || !out) return set_error(B2Q_EINVAL, "sorted_combine: null pointer");
-  dim3 grid((H + 255) / 256, T);
-  sorted_combine_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, inverse, w, out, T, H, k);
+  launch_sorted_combine(y, inverse, w, out, T, H, k, static_cast<cudaStream_t>(stream));
   B2Q_TRY_CUDA(cudaGetLastError());
   return B2Q_OK;
 }
@@ -349,8 +403,7 @@ int b2q_moe_prefill(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, c
     if (rc) return rc;
     rc = tc_launch(pd, TC_PLAIN, st);
     if (rc) return rc;
-    dim3 grid((H + 255) / 256, T);
-    sorted_combine_kernel<<<grid, 256, 0, st>>>(ws.y, ws.inverse, ww, out, T, H, k);
+    launch_sorted_combine(ws.y, ws.inverse, ww, out, T, H, k, st);
     B2Q_TRY_CUDA(cudaGetLastError());
     return B2Q_OK;
   }
@@ -370,8 +423,7 @@ int b2q_moe_prefill(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, c
                       stream);
   if (rc) return rc;
   {
-    dim3 grid((H + 255) / 256, T);
-    sorted_combine_kernel<<<grid, 256, 0, st>>>(ws.y, ws.inverse, ww, out, T, H, k);
+    launch_sorted_combine(ws.y, ws.inverse, ww, out, T, H, k, st);
     B2Q_TRY_CUDA(cudaGetLastError());
   }
   return B2Q_OK;
