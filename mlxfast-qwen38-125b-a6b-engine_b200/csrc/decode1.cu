@@ -435,6 +435,8 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
   volatile int* slot_unit = lastfill + NSLOT;            // [NSLOT] unit of the task in the slot (-1: no more work)
   int* p1n = lastfill + 2 * NSLOT;                       // [NCW] phase-1 task count of each consumer warp
   unsigned* fin_cta = reinterpret_cast<unsigned*>(p1n + NCW);  // gate|up units this CTA finished
+  int* lslot = reinterpret_cast<int*>(fin_cta + 1);  // [MAXK] routed slots whose expert this rank holds, in slot order
+  int* nloc_sm = lslot + MAXK;                      // their count
   float* red = reinterpret_cast<float*>(smem + p.off_red);
   const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
   const bool fused = MODE == D1_FUSED;
@@ -542,17 +544,18 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         ng += gdone[gi] ? 0 : 1;
       }
       if (ng > 0) {
+        const unsigned U1 = (unsigned)(*nloc_sm * (p.F / 8));  // units of the local slots
         unsigned nxt = (lane == 0) ? atomicAdd(&p.sched[0], (unsigned)ng) : 0u;
         int left = ng;
         while (ok && left > 0) {
           const unsigned base = __shfl_sync(0xffffffffu, nxt, 0);
-          if (lane == 0 && base < (unsigned)ph1.units) nxt = atomicAdd(&p.sched[0], (unsigned)ng);
+          if (lane == 0 && base < U1) nxt = atomicAdd(&p.sched[0], (unsigned)ng);
           for (int gi = pw, k = 0; ok && gi < G1grp; gi += NPW, ++k) {
             if (gdone[gi]) continue;
-            const int u = base + k < (unsigned)ph1.units ? (int)(base + k) : -1;
+            const int u = base + k < U1 ? (int)(base + k) : -1;
             if (u >= 0) {
               const int z = u / (p.F / 8), rb = u % (p.F / 8);
-              const int row = (int)(sidx[z] * (uint32_t)p.F) + rb * 8;
+              const int row = (int)((sidx[lslot[z]] - (uint32_t)p.e_lo) * (uint32_t)p.F) + rb * 8;
               for (int i = 0; ok && i < ph1.T; ++i) {  // rotated issue order, as in qmv
                 const int t = (i + jr[gi]) % ph1.T;
                 ok = issue(gi * ph1.T + t, jr[gi], true, row, row, t * (TK / 256), TK / 256, MWG, MSG, MBG, MWU,
@@ -581,7 +584,8 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       const int nl2 = local_units(ph2.units);
       uint32_t ex[MAXK];
 #pragma unroll
-      for (int s2 = 0; s2 < MAXK; ++s2) ex[s2] = s2 < p.k ? sidx[s2] : 0u;
+      const int nloc = *nloc_sm;
+      for (int s2 = 0; s2 < MAXK; ++s2) ex[s2] = s2 < nloc ? sidx[lslot[s2]] - (uint32_t)p.e_lo : 0u;
       int n0[8 / NPW];
 #pragma unroll
       for (int i = 0; i < 8 / NPW; ++i) n0[i] = p1n[pw * (8 / NPW) + i];
@@ -598,7 +602,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
           const int i = (i0 + j2) % (8 / NPW);  // rotated issue order
           const int t = pw * (8 / NPW) + i;
           const int pair = t >> 1, half = t & 1;
-          const bool v0 = 2 * pair < p.k, v1 = 2 * pair + 1 < p.k;
+          const bool v0 = 2 * pair < nloc, v1 = 2 * pair + 1 < nloc;
           const uint32_t e0 = v0 ? ex[2 * pair] : 0u, e1 = v1 ? ex[2 * pair + 1] : e0;
           const int n = n0[i] + j2;
           ok = u >= 0 ? issue(t, n, v0, (int)(e0 * (uint32_t)p.H) + u * 8, (int)(e1 * (uint32_t)p.H) + u * 8,
@@ -698,6 +702,16 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         }
         if (blockIdx.x == 0 && p.logits_out)
           for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
+        // the slots this rank computes: all of them, or (expert parallel) those
+        // whose expert lies in [e_lo, e_lo + e_local)
+        if (lane == 0) {
+          int n = 0;
+          for (int s = 0; s < p.k; ++s) {
+            const int e = (int)sidx[s];
+            if (p.e_local == 0 || (e >= p.e_lo && e < p.e_lo + p.e_local)) lslot[n++] = s;
+          }
+          *nloc_sm = n;
+        }
       }
       named_bar_sync(2, NTH);  // releases the producer
     }
@@ -830,6 +844,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
 
     // ---------------- phase 2 (fused): down + weighted combine ----------------
     if (fused) {
+      const int nloc = *nloc_sm;
       // the CTA's finished units are published once (after the barrier, one
       // fence covers every warp's activation rows); then every gate|up unit
       // of the grid must have been published
@@ -840,18 +855,20 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
           __threadfence();
           atomicAdd(&p.counters[1], nfin);
         }
-        if (!*abort_flag && !wait_counter_geq(&p.counters[1], (unsigned)ph1.units, deadline, abort_flag)) {
+        if (!*abort_flag &&
+            !wait_counter_geq(&p.counters[1], (unsigned)(*nloc_sm * (p.F / 8)), deadline, abort_flag)) {
           record_error(p.err, B2Q_ETIMEOUT);
           *abort_flag = 1;
         }
       }
       named_bar_sync(1, NCT);
       {
-        stage_cols(abuf, asum, p.k, p.XS2, p.ws_act, (size_t)p.F, p.k, p.F, p.gs, true);
+        // the activation rows of the local slots (compact, local order)
+        if (nloc > 0) stage_cols(abuf, asum, p.k, p.XS2, p.ws_act, (size_t)p.F, nloc, p.F, p.gs, true);
       }
       named_bar_arrive(3, NTH);  // the producer may issue the remaining down copies
       const int pair = warp >> 1, half = warp & 1;
-      const int s0 = min(2 * pair, p.k - 1), s1 = min(2 * pair + 1, p.k - 1);
+      const int s0 = max(0, min(2 * pair, nloc - 1)), s1 = max(0, min(2 * pair + 1, nloc - 1));
       const float* xsP = c_xs(asum, G2, s0);
       const float* xoP = c_xo(asum, p.k, G2, s0);
       const float* xsQ = c_xs(asum, G2, s1);
@@ -871,7 +888,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         }
         {
           const uint8_t* st = slots + (size_t)si * SLOT;
-          if (2 * pair < p.k)
+          if (2 * pair < nloc)
             task_pair<WPT>(st, npc2, G2, half * gh, abuf + (size_t)half * (p.F / 2 / 8) * 16, p.XS2, xsP, xoP, xsQ,
                            xoQ, pair, acc);
         }
@@ -895,27 +912,30 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         float prod[MAXK];
 #pragma unroll
         for (int s = 0; s < MAXK; ++s) {
-          if (s < p.k && lane < 8) {
+          if (s < nloc && lane < 8) {
             const int pr = s >> 1, q = s & 1;
             const float y = (rbuf[(2 * pr) * 16 + q * 8 + lane] + rbuf[(2 * pr + 1) * 16 + q * 8 + lane]) * ainv[s];
-            prod[s] = b2q::rb(y) * sw[s];
+            prod[s] = b2q::rb(y) * sw[lslot[s]];
           } else {
             prod[s] = 0.0f;
           }
         }
         release_use(G_DOWN, use);  // partials read; fences shared memory only
         if (lane < 8) {
-          const int TY = p.k < 8 ? p.k : 8;
+          const int TY = nloc < 8 ? nloc : 8;
           float total = 0.0f;
 #pragma unroll
           for (int q = 0; q < MAXK; ++q) {
             if (q < TY) {
               float a = 0.0f;
-              for (int s = q; s < p.k; s += TY) a = prod[s] + a;
+              for (int s = q; s < nloc; s += TY) a = prod[s] + a;
               total = (q == 0) ? a : a + total;
             }
           }
-          p.out[(size_t)u * 8 + lane] = f2bf(total);
+          if (p.out_f32)
+            p.out_f32[(size_t)u * 8 + lane] = total;  // this rank's partial (expert parallel)
+          else
+            p.out[(size_t)u * 8 + lane] = f2bf(total);
         }
       }
     }
@@ -1128,7 +1148,7 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
                   int k, int gs, int* err, unsigned* counters, unsigned* sched, float* ws_logits,
-                  uint16_t* ws_act, cudaStream_t st) {
+                  uint16_t* ws_act, cudaStream_t st, int e_lo, int e_local, float* out_f32) {
   D1Params p;
   std::memset(&p, 0, sizeof(p));
   p.gs = gs;
@@ -1148,13 +1168,17 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
   p.sched = sched;
   p.ws_logits = ws_logits;
   p.ws_act = ws_act;
+  p.e_lo = e_lo;
+  p.e_local = e_local;
+  p.out_f32 = out_f32;
   p.timeout_ns = 2000000000ll;
   int rc = plan(p, D1_FUSED);
   if (rc) return rc;
   const void* ptrs[9] = {wg, sg, bg, wu, su, bu, wd, sd, bd};
-  const MapKey key = map_key(D1_FUSED, ptrs, 9, H, E, F, gs);
+  const int Eh = e_local > 0 ? e_local : E;  // experts in the stacks this call reads
+  const MapKey key = map_key(D1_FUSED, ptrs, 9, H, Eh, F, gs);
   if (!find_maps(key, p.map, 9)) {
-    const uint64_t rgu = (uint64_t)E * F, rd = (uint64_t)E * H;
+    const uint64_t rgu = (uint64_t)Eh * F, rd = (uint64_t)Eh * H;
     rc = set_family(p, MWG, MSG, MBG, wg, sg, bg, rgu, H, TK / 2, (TK / gs) * 2);
     if (rc) return rc;
     rc = set_family(p, MWU, MSU, MBU, wu, su, bu, rgu, H, TK / 2, (TK / gs) * 2);

@@ -28,6 +28,8 @@ struct alignas(64) D1Params {
   float* ws_logits;
   uint16_t* ws_act;
   long long timeout_ns;
+  int e_lo, e_local;  // expert parallel: this rank holds experts [e_lo, e_lo + e_local) (e_local 0: all)
+  float* out_f32;     // expert parallel: fp32 partial output instead of bf16 `out`
   int off_slots, off_x, off_xs, off_act, off_acts, off_red, off_misc, smem_bytes;
   int XS1, XS2;
 };
@@ -40,6 +42,6 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
                   int k, int gs, int* err, unsigned* counters, unsigned* sched, float* ws_logits,
-                  uint16_t* ws_act, cudaStream_t st);
+                  uint16_t* ws_act, cudaStream_t st, int e_lo = 0, int e_local = 0, float* out_f32 = nullptr);
 
 }  // namespace b2q

@@ -30,6 +30,8 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "decode1.cuh"
+#include "decode_ws.hpp"
 #include "engine.cuh"
 #include "host.hpp"
 #include "prefill.cuh"
@@ -329,6 +331,21 @@ int b2q_ep_moe_decode(void* comm, const uint16_t* x, const uint16_t* wr, const u
     return set_error(B2Q_EINVAL, "ep_moe_decode: workspace of %zu bytes needed", ws.bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int R = S * k;
+  if (S == 1) {
+    // one token: the fused single-column kernel over the local slots only,
+    // writing this rank's fp32 partial (the workspace header doubles as its
+    // error word and grid counters)
+    const void* ptrs[] = {x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, partial};
+    bool all_aligned = true;
+    for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
+    if (all_aligned && d1_moe_eligible(H, E, F, k, group_size)) {
+      WsHeader* hdr = static_cast<WsHeader*>(workspace);
+      rc = d1_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, nullptr, idx, w, nullptr, H, E, F, k, group_size,
+                         &hdr->error, hdr->counters, hdr->sched, ws.logits, ws.act, st, e_lo, e_local, partial);
+      if (rc) return rc;
+      return ep_finish(static_cast<EpComm*>(comm), partial, out, (size_t)S * H, st);
+    }
+  }
   uint32_t* ix = idx ? idx : ws.idx;
   float* ww = w ? w : ws.w;
   rc = eng::launch_router_logits(x, wr, ws.logits, S, E, H, st);
