@@ -439,7 +439,8 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
   int* nloc_sm = lslot + MAXK;                      // their count
   float* red = reinterpret_cast<float*>(smem + p.off_red);
   const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
-  const bool fused = MODE == D1_FUSED;
+  const bool fused = MODE != D1_QMV;
+  constexpr bool EP = MODE == D1_FUSED_EP;  // local slots only, fp32 partial out
   const int G1 = p.K1 / p.gs, G2 = fused ? p.F / p.gs : 0;
 
   if (tid == 0) {
@@ -544,7 +545,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         ng += gdone[gi] ? 0 : 1;
       }
       if (ng > 0) {
-        const unsigned U1 = (unsigned)(*nloc_sm * (p.F / 8));  // units of the local slots
+        const unsigned U1 = (unsigned)((EP ? *nloc_sm : p.k) * (p.F / 8));  // units of the (local) slots
         unsigned nxt = (lane == 0) ? atomicAdd(&p.sched[0], (unsigned)ng) : 0u;
         int left = ng;
         while (ok && left > 0) {
@@ -555,7 +556,8 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
             const int u = base + k < U1 ? (int)(base + k) : -1;
             if (u >= 0) {
               const int z = u / (p.F / 8), rb = u % (p.F / 8);
-              const int row = (int)((sidx[lslot[z]] - (uint32_t)p.e_lo) * (uint32_t)p.F) + rb * 8;
+              const int row = EP ? (int)((sidx[lslot[z]] - (uint32_t)p.e_lo) * (uint32_t)p.F) + rb * 8
+                                 : (int)(sidx[z] * (uint32_t)p.F) + rb * 8;
               for (int i = 0; ok && i < ph1.T; ++i) {  // rotated issue order, as in qmv
                 const int t = (i + jr[gi]) % ph1.T;
                 ok = issue(gi * ph1.T + t, jr[gi], true, row, row, t * (TK / 256), TK / 256, MWG, MSG, MBG, MWU,
@@ -584,8 +586,9 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
       const int nl2 = local_units(ph2.units);
       uint32_t ex[MAXK];
 #pragma unroll
-      const int nloc = *nloc_sm;
-      for (int s2 = 0; s2 < MAXK; ++s2) ex[s2] = s2 < nloc ? sidx[lslot[s2]] - (uint32_t)p.e_lo : 0u;
+      const int nloc = EP ? *nloc_sm : p.k;
+      for (int s2 = 0; s2 < MAXK; ++s2)
+        ex[s2] = s2 < nloc ? (EP ? sidx[lslot[s2]] - (uint32_t)p.e_lo : sidx[s2]) : 0u;
       int n0[8 / NPW];
 #pragma unroll
       for (int i = 0; i < 8 / NPW; ++i) n0[i] = p1n[pw * (8 / NPW) + i];
@@ -704,11 +707,11 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
           for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
         // the slots this rank computes: all of them, or (expert parallel) those
         // whose expert lies in [e_lo, e_lo + e_local)
-        if (lane == 0) {
+        if (EP && lane == 0) {
           int n = 0;
           for (int s = 0; s < p.k; ++s) {
             const int e = (int)sidx[s];
-            if (p.e_local == 0 || (e >= p.e_lo && e < p.e_lo + p.e_local)) lslot[n++] = s;
+            if (e >= p.e_lo && e < p.e_lo + p.e_local) lslot[n++] = s;
           }
           *nloc_sm = n;
         }
@@ -844,7 +847,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
 
     // ---------------- phase 2 (fused): down + weighted combine ----------------
     if (fused) {
-      const int nloc = *nloc_sm;
+      const int nloc = EP ? *nloc_sm : p.k;
       // the CTA's finished units are published once (after the barrier, one
       // fence covers every warp's activation rows); then every gate|up unit
       // of the grid must have been published
@@ -856,7 +859,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
           atomicAdd(&p.counters[1], nfin);
         }
         if (!*abort_flag &&
-            !wait_counter_geq(&p.counters[1], (unsigned)(*nloc_sm * (p.F / 8)), deadline, abort_flag)) {
+            !wait_counter_geq(&p.counters[1], (unsigned)(nloc * (p.F / 8)), deadline, abort_flag)) {
           record_error(p.err, B2Q_ETIMEOUT);
           *abort_flag = 1;
         }
@@ -915,7 +918,7 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
           if (s < nloc && lane < 8) {
             const int pr = s >> 1, q = s & 1;
             const float y = (rbuf[(2 * pr) * 16 + q * 8 + lane] + rbuf[(2 * pr + 1) * 16 + q * 8 + lane]) * ainv[s];
-            prod[s] = b2q::rb(y) * sw[lslot[s]];
+            prod[s] = b2q::rb(y) * sw[EP ? lslot[s] : s];
           } else {
             prod[s] = 0.0f;
           }
@@ -932,8 +935,8 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
               total = (q == 0) ? a : a + total;
             }
           }
-          if (p.out_f32)
-            p.out_f32[(size_t)u * 8 + lane] = total;  // this rank's partial (expert parallel)
+          if (EP)
+            p.out_f32[(size_t)u * 8 + lane] = total;  // this rank's partial
           else
             p.out[(size_t)u * 8 + lane] = f2bf(total);
         }
@@ -974,7 +977,7 @@ static int plan(D1Params& p, int mode) {
   off = round_up(off + p.XS1, 128);
   p.off_xs = off;
   off = round_up(off + (2 * G1 + 4 * MAXK) * 4, 128);
-  if (mode == D1_FUSED) {
+  if (mode != D1_QMV) {
     const int G2 = p.F / p.gs;
     p.XS2 = round_up(p.F * 2, 128) + 64;
     p.off_act = off;
@@ -1017,7 +1020,7 @@ static int launch_t(const D1Params& p, cudaStream_t st, int grid) {
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = (MODE == D1_FUSED) ? 1 : 0;
+  cfg.numAttrs = (MODE != D1_QMV) ? 1 : 0;
   B2Q_TRY_CUDA(cudaLaunchKernelEx(&cfg, d1_kernel<WPT, MODE>, p));
   return B2Q_OK;
 }
@@ -1028,13 +1031,16 @@ static int launch(const D1Params& p, int mode, cudaStream_t st) {
   if (rc) return rc;
   const int grid = di.sm_count;
   const int wpt = p.gs / 32;
-  switch (wpt * 2 + mode) {
-    case 1 * 2 + D1_QMV: return launch_t<1, D1_QMV>(p, st, grid);
-    case 2 * 2 + D1_QMV: return launch_t<2, D1_QMV>(p, st, grid);
-    case 4 * 2 + D1_QMV: return launch_t<4, D1_QMV>(p, st, grid);
-    case 1 * 2 + D1_FUSED: return launch_t<1, D1_FUSED>(p, st, grid);
-    case 2 * 2 + D1_FUSED: return launch_t<2, D1_FUSED>(p, st, grid);
-    case 4 * 2 + D1_FUSED: return launch_t<4, D1_FUSED>(p, st, grid);
+  switch (wpt * 4 + mode) {
+    case 1 * 4 + D1_QMV: return launch_t<1, D1_QMV>(p, st, grid);
+    case 2 * 4 + D1_QMV: return launch_t<2, D1_QMV>(p, st, grid);
+    case 4 * 4 + D1_QMV: return launch_t<4, D1_QMV>(p, st, grid);
+    case 1 * 4 + D1_FUSED: return launch_t<1, D1_FUSED>(p, st, grid);
+    case 2 * 4 + D1_FUSED: return launch_t<2, D1_FUSED>(p, st, grid);
+    case 4 * 4 + D1_FUSED: return launch_t<4, D1_FUSED>(p, st, grid);
+    case 1 * 4 + D1_FUSED_EP: return launch_t<1, D1_FUSED_EP>(p, st, grid);
+    case 2 * 4 + D1_FUSED_EP: return launch_t<2, D1_FUSED_EP>(p, st, grid);
+    case 4 * 4 + D1_FUSED_EP: return launch_t<4, D1_FUSED_EP>(p, st, grid);
     default: return set_error(B2Q_EUNSUPPORTED, "decode kernel: group size %d", p.gs);
   }
 }
@@ -1172,7 +1178,8 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
   p.e_local = e_local;
   p.out_f32 = out_f32;
   p.timeout_ns = 2000000000ll;
-  int rc = plan(p, D1_FUSED);
+  const int mode = out_f32 ? D1_FUSED_EP : D1_FUSED;
+  int rc = plan(p, mode);
   if (rc) return rc;
   const void* ptrs[9] = {wg, sg, bg, wu, su, bu, wd, sd, bd};
   const int Eh = e_local > 0 ? e_local : E;  // experts in the stacks this call reads
@@ -1187,7 +1194,7 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
     if (rc) return rc;
     put_maps(key, p.map, 9);
   }
-  return launch(p, D1_FUSED, st);
+  return launch(p, mode, st);
 }
 
 }  // namespace b2q

@@ -7,7 +7,7 @@
 
 namespace b2q {
 
-enum { D1_QMV = 0, D1_FUSED = 1 };
+enum { D1_QMV = 0, D1_FUSED = 1, D1_FUSED_EP = 2 };
 
 struct alignas(64) D1Params {
   CUtensorMap map[9];  // qmv: W, S, B; fused: gate W/S/B, up W/S/B, down W/S/B
