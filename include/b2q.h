@@ -210,6 +210,77 @@ B2Q_API int b2q_ep_moe_prefill(void* comm, const uint16_t* x, const uint16_t* wr
                    int T, int H, int E, int F, int k, int e_lo, int e_local,
                    int group_size, int bits, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Expert-parallel prefill over an all-to-all token exchange (dispatch /
+ * combine). No counterpart in the reference, which keeps all experts of a
+ * layer on one Apple GPU: this is its MoE layer (moeForwardShared,
+ * Runner/FastModel/TrackFastModel.swift:867-1009, sorted prefill
+ * Runner/FastModel/TrackP12Prefill.swift:180-237) with tokens owned by ranks
+ * and experts sharded by b2q_ep_expert_range (contiguous blocks, the first
+ * E % nranks ranks one expert more). Up to B2Q_EP_MAX_RANKS ranks.
+ *
+ * b2q_ep_a2a_dispatch (token owner): routes its T tokens and, for every rank d
+ *   holding one of a token's k experts, copies the token row once into block d
+ *   of send_x [nranks, T, H] (bf16) and its k expert ids and k fp32 weight bits
+ *   into send_meta [nranks, T, 2k] (u32); send_counts [nranks] (int32) = rows
+ *   in each block, pos [T, nranks] (int32) = a token's row in block d or -1.
+ *   idx / w (may be NULL) receive the routing [T, k].
+ * b2q_ep_a2a_experts (expert rank): for R received rows (recv_x [R, H],
+ *   recv_meta [R, 2k], blocks of all senders concatenated) multiplies the slots
+ *   whose expert lies in [e_lo, e_lo + e_local) by the local stacks
+ *   (tensor cores, gate|up + SwiGLU, down) and writes each row's weighted sum
+ *   of its local slots to partial [R, H] (fp32).
+ * b2q_ep_a2a_combine (token owner): ret [nranks, T, H] (fp32) holds in block d
+ *   the partial rows rank d returned, in the order they were sent;
+ *   out[t] = bf16(sum over d in rank order of ret[d, pos[t, d]]).
+ * b2q_ep_moe_prefill_a2a chains the three over the library's communicator
+ *   (comm == NULL: one rank): all-gather of the counts, grouped NCCL send /
+ *   recv of the blocks, the experts, the partial rows back, the combine. Every
+ *   rank calls it (T may be 0, T <= T_max); it reads the counts on the host,
+ *   so it returns after the dispatch has run. */
+#define B2Q_EP_MAX_RANKS 8
+B2Q_API int b2q_ep_expert_range(int E, int nranks, int rank, int* e_lo, int* e_local);
+B2Q_API size_t b2q_ep_a2a_dispatch_workspace_size(int T, int H, int E, int k, int nranks);
+B2Q_API int b2q_ep_a2a_dispatch(const uint16_t* x, const uint16_t* wr, uint16_t* send_x, uint32_t* send_meta,
+                   int32_t* send_counts, int32_t* pos, uint32_t* idx, float* w,
+                   int T, int H, int E, int k, int nranks,
+                   void* workspace, size_t workspace_bytes, void* stream);
+B2Q_API size_t b2q_ep_a2a_experts_workspace_size(int R, int H, int E, int F, int k);
+B2Q_API int b2q_ep_a2a_experts(const uint16_t* recv_x, const uint32_t* recv_meta,
+                   const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                   const uint32_t* wd, const uint16_t* sd, const uint16_t* bd,
+                   float* partial, int R, int H, int E, int F, int k, int e_lo, int e_local,
+                   int group_size, int bits, void* workspace, size_t workspace_bytes, void* stream);
+B2Q_API int b2q_ep_a2a_combine(const float* ret, const int32_t* pos, uint16_t* out,
+                   int T, int H, int nranks, void* stream);
+B2Q_API size_t b2q_ep_moe_prefill_a2a_workspace_size(int T_max, int H, int E, int F, int k, int nranks);
+B2Q_API int b2q_ep_moe_prefill_a2a(void* comm, const uint16_t* x, const uint16_t* wr,
+                   const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                   const uint32_t* wd, const uint16_t* sd, const uint16_t* bd,
+                   uint16_t* out, uint32_t* idx, float* w,
+                   int T, int T_max, int H, int E, int F, int k,
+                   int group_size, int bits, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- decoder around the path (configs with a full model) -------------------
+ * b2q_embed_gather: out[t] (bf16 [T, K]) = dequantize(table row ids[t]) of a
+ *   4-bit table w [V, K/8], scales / biases [V, K/gs] -- MLXNN
+ *   QuantizedEmbedding.callAsFunction (Vendor/mlx-swift/Source/MLXNN/
+ *   Quantized.swift:238-300) with the Metal dequantizer's arithmetic. An id
+ *   outside [0, V) gives a zero row and B2Q_EINVAL in *status (may be NULL).
+ * b2q_rms_norm: out [T, H] = bf16(weight * x * rsqrt(mean(x^2) + eps)), fp32
+ *   inside (MLX fast::rms_norm, which the reference's norms call).
+ * b2q_rope: x [T, heads, head_dim] in place, non-interleaved rotary embedding
+ *   (MLX fast::rope, traditional = false, scale 1) at positions[t] or, when
+ *   positions is NULL, pos0 + t. */
+B2Q_API int b2q_embed_gather(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                   const int32_t* ids, uint16_t* out, int T, int V, int K, int group_size, int bits,
+                   int* status, void* stream);
+B2Q_API int b2q_rms_norm(const uint16_t* x, const uint16_t* weight, uint16_t* out, int T, int H, float eps,
+                   void* stream);
+B2Q_API int b2q_rope(uint16_t* x, int T, int heads, int head_dim, const int32_t* positions, int pos0,
+                   float theta, void* stream);
+
 /* ---- checkpoint reading (per-layer packed-weight binding) ------------------ */
 
 /* Replaces the reference's safetensors header reader

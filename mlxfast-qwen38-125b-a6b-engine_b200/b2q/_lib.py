@@ -53,6 +53,17 @@ SIGNATURES = {
     "b2q_ep_moe_decode": (_I, [_P] * 16 + [_I] * 9 + [_P, _SZ, _P]),
     "b2q_ep_moe_prefill_workspace_size": (_SZ, [_I] * 5),
     "b2q_ep_moe_prefill": (_I, [_P] * 16 + [_I] * 9 + [_P, _SZ, _P]),
+    "b2q_ep_expert_range": (_I, [_I, _I, _I, _P, _P]),
+    "b2q_ep_a2a_dispatch_workspace_size": (_SZ, [_I] * 5),
+    "b2q_ep_a2a_dispatch": (_I, [_P] * 8 + [_I] * 5 + [_P, _SZ, _P]),
+    "b2q_ep_a2a_experts_workspace_size": (_SZ, [_I] * 5),
+    "b2q_ep_a2a_experts": (_I, [_P] * 12 + [_I] * 9 + [_P, _SZ, _P]),
+    "b2q_ep_a2a_combine": (_I, [_P] * 3 + [_I] * 3 + [_P]),
+    "b2q_ep_moe_prefill_a2a_workspace_size": (_SZ, [_I] * 6),
+    "b2q_ep_moe_prefill_a2a": (_I, [_P] * 15 + [_I] * 8 + [_P, _SZ, _P]),
+    "b2q_embed_gather": (_I, [_P] * 5 + [_I] * 5 + [_P, _P]),
+    "b2q_rms_norm": (_I, [_P] * 3 + [_I, _I, ctypes.c_float, _P]),
+    "b2q_rope": (_I, [_P, _I, _I, _I, _P, _I, ctypes.c_float, _P]),
     "b2q_st_open": (_I, [ctypes.c_char_p, _P]),
     "b2q_st_close": (_I, [_P]),
     "b2q_st_count": (_I, [_P]),

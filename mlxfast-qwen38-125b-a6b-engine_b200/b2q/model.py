@@ -1,0 +1,334 @@
+"""A generic 4-bit MoE decoder built around the path (the full-model configs).
+
+The reference's model (Qwen3.8-class, mlx-swift-lm's Qwen4ExpModel) has
+attention variants, hyper-connections and other blocks that are outside the
+path; this decoder is the generic shape the benchmark configuration names:
+
+    h = embed(tokens)                                  4-bit tied table
+    per layer:
+        a   = rms_norm(h) ; q|k|v = QuantizedLinear(a)  one fused 4-bit product
+        q,k = rope(q, k)   (non-interleaved, theta)     ; k, v -> bf16 KV cache
+        h  += QuantizedLinear_o(attention(q, K, V))     GQA, causal
+        h  += MoE(rms_norm(h))                          router top-k, SwiGLU experts
+    logits = lm_head(rms_norm(h))                       the tied table as a 4-bit product
+    MTP draft (one extra block, DeepSeek-style): x = eh_proj([norm(embed(t+1)) ; norm(h_t)]),
+        one block, the shared final norm and lm_head -> the token after next
+
+Every weight product and the MoE layers run through the library (qmv / qmm,
+the fused decode MoE, the sorted prefill MoE); RMSNorm, RoPE and the token
+embedding are library kernels too. Attention itself is PyTorch's SDPA on the
+GPU (outside the path). A greedy decode step can be captured in a CUDA graph
+(`Decoder.decode_graph`): token id and position live in device buffers that
+the graph updates itself, and attention runs over a fixed window with a mask,
+so one replay is one token.
+
+Random-init weights follow the synthetic distributions of the benchmark
+(packed nibbles uniform, scales U(0.002, 0.02), biases -8*scale + N(0, 1e-3)).
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+import torch.nn.functional as Fnn
+
+from . import ops, synth
+from ._lib import check, lib
+from .nn import MoE, QuantizedLinear
+
+
+@dataclasses.dataclass
+class DecoderConfig:
+    n_layers: int = 48
+    hidden: int = 4096
+    n_heads: int = 32
+    n_kv_heads: int = 4
+    head_dim: int = 128
+    n_experts: int = 128
+    top_k: int = 8
+    expert_ffn: int = 1536
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+    group_size: int = 64
+    mtp: bool = True
+    max_seq: int = 2048
+
+    def validate(self):
+        if self.n_heads % self.n_kv_heads:
+            raise ValueError("n_heads must be a multiple of n_kv_heads")
+        if self.head_dim % 2 or self.hidden % 8:
+            raise ValueError("head_dim must be even and hidden a multiple of 8")
+        if self.top_k > self.n_experts:
+            raise ValueError("top_k > n_experts")
+        return self
+
+    @property
+    def qkv_rows(self) -> int:
+        return (self.n_heads + 2 * self.n_kv_heads) * self.head_dim
+
+    def packed_bytes(self, rows: int, K: int) -> int:
+        """Bytes of a 4-bit matrix: packed nibbles + bf16 scale and bias per group."""
+        return rows * (K // 2 + 2 * 2 * (K // self.group_size))
+
+    def decode_bytes_per_token(self, position: int) -> int:
+        """Weight + KV bytes one greedy decode step reads (no MTP): per layer the
+        attention projections, the router, k experts, the KV cache up to `position`;
+        then the lm_head."""
+        H, hd = self.hidden, self.head_dim
+        attn = self.packed_bytes(self.qkv_rows, H) + self.packed_bytes(H, self.n_heads * hd)
+        expert = 2 * self.packed_bytes(self.expert_ffn, H) + self.packed_bytes(H, self.expert_ffn)
+        router = self.n_experts * H * 2
+        kv = 2 * self.n_kv_heads * hd * 2 * (position + 1)
+        return self.n_layers * (attn + router + self.top_k * expert + kv) + self.packed_bytes(self.vocab, H)
+
+
+def _ql(rows, K, gs, dev, seed):
+    w, s, b = synth.packed_weights((rows,), K, gs, dev, seed)
+    return QuantizedLinear(w, s, b, gs, 4)
+
+
+def _norm_weight(H, dev, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return (1.0 + 0.05 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+
+
+class Block:
+    """One decoder block: attention (fused q|k|v product, RoPE, GQA) then the MoE."""
+
+    def __init__(self, cfg: DecoderConfig, dev, seed: int):
+        H, hd = cfg.hidden, cfg.head_dim
+        self.cfg = cfg
+        self.attn_norm = _norm_weight(H, dev, seed)
+        self.qkv = _ql(cfg.qkv_rows, H, cfg.group_size, dev, seed + 1)
+        self.o = _ql(H, cfg.n_heads * hd, cfg.group_size, dev, seed + 2)
+        self.mlp_norm = _norm_weight(H, dev, seed + 3)
+        router = synth.router_weight(cfg.n_experts, H, dev, seed + 4)
+        experts = synth.moe_layer(cfg.n_experts, H, cfg.expert_ffn, cfg.group_size, dev, seed + 5)
+        self.moe = MoE(router, experts, cfg.top_k, cfg.group_size)
+        self.k_cache = torch.zeros((cfg.max_seq, cfg.n_kv_heads, hd), dtype=torch.bfloat16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+
+    def attention(self, a: torch.Tensor, positions: torch.Tensor, pos0: int | None, window: int | None,
+                  mask: torch.Tensor | None) -> torch.Tensor:
+        """a [T, H] normed -> attention output [T, n_heads * hd] (bf16).
+
+        positions: int32 [T] device tensor of the rows' positions. With `window`
+        (graph-safe decode) attention covers cache rows [0, window) under `mask`;
+        otherwise rows [0, pos0 + T) with a causal mask (prefill / windows)."""
+        cfg = self.cfg
+        T = a.shape[0]
+        nq, nk, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        qkv = self.qkv(a)  # [T, (nq + 2 nk) hd]
+        q = qkv[:, :nq * hd].contiguous()
+        k = qkv[:, nq * hd:(nq + nk) * hd].contiguous()
+        v = qkv[:, (nq + nk) * hd:].view(T, nk, hd)
+        st = ops._stream(a.device)
+        check(lib().b2q_rope(q.data_ptr(), T, nq, hd, positions.data_ptr(), 0, cfg.rope_theta, st))
+        check(lib().b2q_rope(k.data_ptr(), T, nk, hd, positions.data_ptr(), 0, cfg.rope_theta, st))
+        pl = positions.long()
+        self.k_cache.index_copy_(0, pl, k.view(T, nk, hd))
+        self.v_cache.index_copy_(0, pl, v)
+        g = nq // nk
+        if window is not None:
+            L = window
+            # one query row per (kv head, group member): q [1, nk, T*g, hd]
+            qh = q.view(T, nk, g, hd).permute(1, 0, 2, 3).reshape(1, nk, T * g, hd)
+            kh = self.k_cache[:L].permute(1, 0, 2).unsqueeze(0)
+            vh = self.v_cache[:L].permute(1, 0, 2).unsqueeze(0)
+            o = Fnn.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask)
+            o = o.view(nk, T, g, hd).permute(1, 0, 2, 3).reshape(T, nq * hd)
+        else:
+            L = pos0 + T
+            qh = q.view(T, nq, hd).permute(1, 0, 2).unsqueeze(0)
+            kh = self.k_cache[:L].permute(1, 0, 2).unsqueeze(0)
+            vh = self.v_cache[:L].permute(1, 0, 2).unsqueeze(0)
+            if pos0 == 0:
+                o = Fnn.scaled_dot_product_attention(qh, kh, vh, is_causal=True, enable_gqa=True)
+            else:
+                qi = torch.arange(pos0, pos0 + T, device=a.device).view(T, 1)
+                ki = torch.arange(L, device=a.device).view(1, L)
+                m = torch.zeros((T, L), dtype=torch.bfloat16, device=a.device).masked_fill(ki > qi, float("-inf"))
+                o = Fnn.scaled_dot_product_attention(qh, kh, vh, attn_mask=m, enable_gqa=True)
+            o = o.squeeze(0).permute(1, 0, 2).reshape(T, nq * hd)
+        return o.contiguous()
+
+    def __call__(self, h: torch.Tensor, positions, pos0=None, window=None, mask=None) -> torch.Tensor:
+        cfg = self.cfg
+        a = rms_norm(h, self.attn_norm, cfg.rms_eps)
+        h = h + self.o(self.attention(a, positions, pos0, window, mask))
+        m = rms_norm(h, self.mlp_norm, cfg.rms_eps)
+        return h + self.moe(m)
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    x = x.contiguous()
+    T, H = x.shape
+    out = torch.empty_like(x)
+    check(lib().b2q_rms_norm(x.data_ptr(), w.data_ptr(), out.data_ptr(), T, H, eps, ops._stream(x.device)))
+    return out
+
+
+class Decoder:
+    """Random-init decoder of `cfg` on `device` (seeded), with a bf16 KV cache of cfg.max_seq rows per layer."""
+
+    def __init__(self, cfg: DecoderConfig, device="cuda", seed: int = 0):
+        self.cfg = cfg.validate()
+        dev = torch.device(device)
+        self.device = dev
+        H = cfg.hidden
+        ew, es, eb = synth.packed_weights((cfg.vocab,), H, cfg.group_size, dev, seed)
+        self.embed_w, self.embed_s, self.embed_b = ew, es, eb
+        self.lm_head = QuantizedLinear(ew, es, eb, cfg.group_size, 4)  # tied
+        self.blocks = [Block(cfg, dev, seed + 100 * (i + 1)) for i in range(cfg.n_layers)]
+        self.final_norm = _norm_weight(H, dev, seed + 7)
+        self.mtp = None
+        if cfg.mtp:
+            base = seed + 100 * (cfg.n_layers + 1)
+            self.mtp = {"enorm": _norm_weight(H, dev, base), "hnorm": _norm_weight(H, dev, base + 1),
+                        "eh_proj": _ql(H, 2 * H, cfg.group_size, dev, base + 2),
+                        "block": Block(cfg, dev, base + 10)}
+        self._status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._graph = None
+
+    # ---- pieces --------------------------------------------------------------
+    def embed(self, ids: torch.Tensor) -> torch.Tensor:
+        ids = ids.to(torch.int32).contiguous().view(-1)
+        T = ids.numel()
+        out = torch.empty((T, self.cfg.hidden), dtype=torch.bfloat16, device=self.device)
+        check(lib().b2q_embed_gather(self.embed_w.data_ptr(), self.embed_s.data_ptr(), self.embed_b.data_ptr(),
+                                     ids.data_ptr(), out.data_ptr(), T, self.cfg.vocab, self.cfg.hidden,
+                                     self.cfg.group_size, 4, self._status.data_ptr(), ops._stream(self.device)))
+        return out
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        return self.lm_head(rms_norm(h, self.final_norm, self.cfg.rms_eps))
+
+    def status(self) -> int:
+        """Device-side error recorded by the embedding lookup (B2Q_EINVAL for a bad token id), then cleared."""
+        v = int(self._status.item())
+        self._status.zero_()
+        return v
+
+    # ---- eager forward ---------------------------------------------------------
+    def forward(self, ids: torch.Tensor, pos0: int = 0):
+        """Tokens ids [T] at positions pos0.. -> (hidden [T, H] after the last block, logits of the last row)."""
+        T = ids.numel()
+        if pos0 + T > self.cfg.max_seq:
+            raise ValueError("sequence longer than max_seq")
+        positions = torch.arange(pos0, pos0 + T, dtype=torch.int32, device=self.device)
+        h = self.embed(ids)
+        for blk in self.blocks:
+            h = blk(h, positions, pos0=pos0)
+        return h, self.logits(h[-1:])
+
+    def mtp_draft(self, h_prev: torch.Tensor, ids: torch.Tensor, pos0: int) -> torch.Tensor:
+        """The draft head over rows pos0..: row p takes the main model's hidden of
+        position p - 1 (h_prev[i]) and the token at p (ids[i]); it appends row p to
+        the head's own KV cache and returns the logits of the last row, a guess of
+        the token at p + 1."""
+        m = self.mtp
+        e = rms_norm(self.embed(ids), m["enorm"], self.cfg.rms_eps)
+        hh = rms_norm(h_prev.contiguous(), m["hnorm"], self.cfg.rms_eps)
+        x = m["eh_proj"](torch.cat([e, hh], dim=-1))
+        positions = torch.arange(pos0, pos0 + x.shape[0], dtype=torch.int32, device=self.device)
+        x = m["block"](x, positions, pos0=pos0)
+        return self.logits(x[-1:])
+
+    def generate(self, prompt: torch.Tensor, n_new: int, use_mtp: bool = False):
+        """Greedy decode (eager). With use_mtp the draft head proposes the token after
+        next and a two-row window verifies it (accepted when the main model agrees).
+        Returns (tokens [n_new] on the host, accepted draft count)."""
+        prompt = prompt.to(self.device).view(-1)
+        T = prompt.numel()
+        h, lg = self.forward(prompt, 0)
+        out = [int(lg.argmax(-1).item())]
+        pos = T  # position of out[-1]
+        h_last = h[-1:]
+        accepted = 0
+        use_mtp = use_mtp and self.mtp is not None
+        if use_mtp:
+            # the head's cache over the prompt: row p from (h_{p-1}, token p), h_{-1} = 0
+            hp = torch.cat([torch.zeros_like(h[:1]), h[:-1]])
+            self.mtp_draft(hp, prompt, 0)
+        while len(out) < n_new:
+            tok = torch.tensor([out[-1]], dtype=torch.int32, device=self.device)
+            if use_mtp and pos + 2 <= self.cfg.max_seq:
+                draft = int(self.mtp_draft(h_last, tok, pos).argmax(-1).item())
+                ids = torch.tensor([out[-1], draft], dtype=torch.int32, device=self.device)
+                hw = self._window(ids, pos)
+                lw = self.logits(hw)
+                a0 = int(lw[0].argmax(-1).item())
+                if a0 == draft:
+                    accepted += 1
+                    out += [draft, int(lw[1].argmax(-1).item())]
+                    # the head's row pos + 1 (the accepted draft) before it drafts from pos + 2
+                    self.mtp_draft(hw[0:1], ids[1:2], pos + 1)
+                    h_last = hw[1:2]
+                    pos += 2
+                else:
+                    out.append(a0)
+                    h_last = hw[0:1]
+                    pos += 1
+            else:
+                hw = self._window(tok, pos)
+                out.append(int(self.logits(hw).argmax(-1).item()))
+                h_last = hw
+                pos += 1
+        return out[:n_new], accepted
+
+    def _window(self, ids: torch.Tensor, pos0: int) -> torch.Tensor:
+        positions = torch.arange(pos0, pos0 + ids.numel(), dtype=torch.int32, device=self.device)
+        h = self.embed(ids)
+        for blk in self.blocks:
+            h = blk(h, positions, pos0=pos0)
+        return h
+
+    # ---- CUDA-graph decode ----------------------------------------------------------
+    def decode_graph(self, window: int):
+        """Capture one greedy decode step over attention window [0, window): the graph
+        reads the token and position from device buffers, appends to the KV cache,
+        writes the argmax back as the next token and advances the position.
+        Returns (replay_fn, token_buf, pos_buf, logits_buf); logits_buf holds the
+        last replayed step's logits [1, vocab]."""
+        cfg = self.cfg
+        if window > cfg.max_seq:
+            raise ValueError("window > max_seq")
+        dev = self.device
+        tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        ar = torch.arange(window, dtype=torch.int32, device=dev)
+        g = cfg.n_heads // cfg.n_kv_heads
+        lg_buf = torch.zeros((1, cfg.vocab), dtype=torch.bfloat16, device=dev)
+        stream = torch.cuda.Stream(device=dev)
+
+        def step():
+            mask = torch.where(ar <= pos, 0.0, float("-inf")).to(torch.bfloat16).view(1, 1, 1, window)
+            mask = mask.expand(1, 1, g, window)
+            h = self.embed(tok)
+            for blk in self.blocks:
+                h = blk(h, pos, window=window, mask=mask)
+            lg = self.logits(h)
+            lg_buf.copy_(lg)
+            tok.copy_(lg.argmax(-1).to(torch.int32).view(1))
+            pos.add_(1)
+
+        # warm the library's per-shape state (tensor maps, attributes) outside the
+        # capture; the warm-up writes KV row `window - 1`, which no caller has yet
+        tok.zero_()
+        pos.fill_(window - 1)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            step()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        torch.cuda.synchronize(dev)
+        self._graph = graph
+
+        def replay():
+            graph.replay()
+
+        return replay, tok, pos, lg_buf

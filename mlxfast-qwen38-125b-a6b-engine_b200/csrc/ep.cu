@@ -33,34 +33,12 @@
 #include "decode1.cuh"
 #include "decode_ws.hpp"
 #include "engine.cuh"
+#include "ep.cuh"
 #include "host.hpp"
 #include "prefill.cuh"
 #include "qmm_tc.cuh"
 
 namespace b2q {
-namespace {
-
-// ---- the few NCCL entry points used, resolved with dlsym --------------------
-struct NcclUid {
-  char internal[128];
-};
-typedef void* NcclComm;
-typedef int (*FnGetUniqueId)(NcclUid*);
-typedef int (*FnCommInitRank)(NcclComm*, int, NcclUid, int);
-typedef int (*FnCommDestroy)(NcclComm);
-typedef int (*FnAllReduce)(const void*, void*, size_t, int, int, NcclComm, cudaStream_t);
-typedef const char* (*FnGetErrorString)(int);
-constexpr int kNcclFloat32 = 7;  // ncclFloat32 / ncclFloat
-constexpr int kNcclSum = 0;      // ncclSum
-
-struct Nccl {
-  FnGetUniqueId get_unique_id = nullptr;
-  FnCommInitRank comm_init_rank = nullptr;
-  FnCommDestroy comm_destroy = nullptr;
-  FnAllReduce all_reduce = nullptr;
-  FnGetErrorString error_string = nullptr;
-  bool ok = false;
-};
 
 const Nccl& nccl() {
   static Nccl n;
@@ -72,8 +50,14 @@ const Nccl& nccl() {
     n.comm_init_rank = reinterpret_cast<FnCommInitRank>(dlsym(h, "ncclCommInitRank"));
     n.comm_destroy = reinterpret_cast<FnCommDestroy>(dlsym(h, "ncclCommDestroy"));
     n.all_reduce = reinterpret_cast<FnAllReduce>(dlsym(h, "ncclAllReduce"));
+    n.all_gather = reinterpret_cast<FnAllGather>(dlsym(h, "ncclAllGather"));
+    n.send = reinterpret_cast<FnSend>(dlsym(h, "ncclSend"));
+    n.recv = reinterpret_cast<FnRecv>(dlsym(h, "ncclRecv"));
+    n.group_start = reinterpret_cast<FnGroup>(dlsym(h, "ncclGroupStart"));
+    n.group_end = reinterpret_cast<FnGroup>(dlsym(h, "ncclGroupEnd"));
     n.error_string = reinterpret_cast<FnGetErrorString>(dlsym(h, "ncclGetErrorString"));
     n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce && n.error_string;
+    n.p2p_ok = n.ok && n.all_gather && n.send && n.recv && n.group_start && n.group_end;
   });
   return n;
 }
@@ -84,10 +68,7 @@ int nccl_check(int r, const char* what) {
   return set_error(B2Q_ENCCL, "%s: %s (%d)", what, n.error_string ? n.error_string(r) : "NCCL error", r);
 }
 
-struct EpComm {
-  NcclComm comm;
-  int nranks, rank;
-};
+namespace {
 
 size_t a256(size_t v) { return (v + 255) / 256 * 256; }
 
@@ -251,6 +232,8 @@ int ep_finish(EpComm* c, float* partial, uint16_t* out, size_t n, cudaStream_t s
   return B2Q_OK;
 }
 
+}  // namespace
+
 int ep_check_common(const char* fn, int T, int H, int E, int F, int k, int e_lo, int e_local, int gs, int bits) {
   if (bits != 4) return set_error(B2Q_EUNSUPPORTED, "%s: bits=%d", fn, bits);
   if (!(gs == 32 || gs == 64 || gs == 128)) return set_error(B2Q_EUNSUPPORTED, "%s: group_size=%d", fn, gs);
@@ -260,7 +243,19 @@ int ep_check_common(const char* fn, int T, int H, int E, int F, int k, int e_lo,
   return B2Q_OK;
 }
 
-}  // namespace
+int launch_ep_sorted_combine(const uint16_t* y, const uint32_t* inverse, const float* w, const uint32_t* offsets,
+                             int e_lo, int e_local, float* partial, int T, int H, int k, cudaStream_t st) {
+  // rows in chunks of at most 65535 (the grid's y limit)
+  for (int t0 = 0; t0 < T; t0 += 65535) {
+    const int n = T - t0 < 65535 ? T - t0 : 65535;
+    dim3 grid((H + 255) / 256, n);
+    ep_sorted_combine_kernel<<<grid, 256, 0, st>>>(y, inverse + (size_t)t0 * k, w + (size_t)t0 * k, offsets, e_lo,
+                                                   e_local, partial + (size_t)t0 * H, n, H, k);
+    B2Q_TRY_CUDA(cudaGetLastError());
+  }
+  return B2Q_OK;
+}
+
 }  // namespace b2q
 
 using namespace b2q;
@@ -446,9 +441,8 @@ int b2q_ep_moe_prefill(void* comm, const uint16_t* x, const uint16_t* wr, const 
   if (rc) return rc;
   rc = tc_launch(pd, TC_PLAIN, st);
   if (rc) return rc;
-  dim3 grid((H + 255) / 256, T);
-  ep_sorted_combine_kernel<<<grid, 256, 0, st>>>(ws.y, ws.inverse, ww, ws.offsets, e_lo, e_local, partial, T, H, k);
-  B2Q_TRY_CUDA(cudaGetLastError());
+  rc = launch_ep_sorted_combine(ws.y, ws.inverse, ww, ws.offsets, e_lo, e_local, partial, T, H, k, st);
+  if (rc) return rc;
   return ep_finish(static_cast<EpComm*>(comm), partial, out, (size_t)T * H, st);
 }
 

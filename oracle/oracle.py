@@ -57,6 +57,30 @@ def f32_to_bf16(a: np.ndarray) -> np.ndarray:
     return r
 
 
+def ep_owner(e: int, E: int, nranks: int) -> int:
+    """Rank holding expert e when E experts are split into contiguous blocks over
+    nranks ranks, the first E % nranks ranks one expert more."""
+    base, extra = divmod(E, nranks)
+    split = extra * (base + 1)
+    return e // (base + 1) if e < split else extra + (e - split) // base
+
+
+def ep_a2a_plan(idx: np.ndarray, E: int, nranks: int):
+    """Dispatch plan of the expert-parallel all-to-all prefill, restated in plain
+    Python. The reference has no expert parallelism (its experts share one GPU),
+    so this pins the build's own rule: token t goes to rank d once if d holds
+    any of its k experts; pos[t, d] = number of earlier tokens sent to d, or -1;
+    counts[d] = tokens sent to d."""
+    T = idx.shape[0]
+    pos = np.full((T, nranks), -1, np.int32)
+    counts = np.zeros(nranks, np.int32)
+    for t in range(T):
+        for d in sorted({ep_owner(int(e), E, nranks) for e in idx[t]}):
+            pos[t, d] = counts[d]
+            counts[d] += 1
+    return pos, counts
+
+
 class Oracle:
     def __init__(self, path: str = ORACLE_SO):
         if not os.path.exists(path):

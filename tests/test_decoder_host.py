@@ -1,0 +1,41 @@
+"""Host-side arithmetic of the decoder around the path (no GPU): its shape
+rules and the bytes one decode step reads (the roofline basis of the
+full-decoder benchmark leg)."""
+from __future__ import annotations
+
+import pytest
+
+
+def test_decode_bytes_of_the_config3_model():
+    from b2q.model import DecoderConfig
+
+    c = DecoderConfig()
+    H = 4096
+    attn = (c.qkv_rows + H) * (H // 2 + 4 * (H // 64))
+    assert attn == 21_233_664  # q|k|v [5120, 4096] + o [4096, 4096], 4-bit g64
+    expert = 3 * 1536 * (H // 2 + 4 * (H // 64))
+    assert expert == 10_616_832
+    lm_head = 151936 * (H // 2 + 4 * (H // 64))
+    kv = 2 * 4 * 128 * 2 * 1025
+    total = 48 * (attn + 128 * H * 2 + 8 * expert + kv) + lm_head
+    assert c.decode_bytes_per_token(1024) == total
+    assert 5.4e9 < total < 5.7e9
+
+
+def test_config_rules():
+    from b2q.model import DecoderConfig
+
+    with pytest.raises(ValueError):
+        DecoderConfig(n_heads=30, n_kv_heads=4).validate()
+    with pytest.raises(ValueError):
+        DecoderConfig(top_k=200).validate()
+    assert DecoderConfig(n_layers=2).validate().qkv_rows == (32 + 8) * 128
+
+
+def test_decoder_kernels_refuse_bad_shapes(b2q_mod):
+    lib = b2q_mod.lib()
+    assert lib.b2q_rms_norm(None, None, None, 2, 1001, 1e-6, None) == -1
+    assert lib.b2q_rms_norm(None, None, None, 0, 1024, 1e-6, None) == 0
+    assert lib.b2q_rope(None, 1, 4, 127, None, 0, 1e6, None) == -1
+    assert lib.b2q_embed_gather(None, None, None, None, None, 1, 10, 1024, 48, 4, None, None) == -2
+    assert lib.b2q_embed_gather(None, None, None, None, None, 0, 10, 1024, 64, 4, None, None) == 0

@@ -126,3 +126,148 @@ def test_sharded_layer_on_two_gloo_ranks(tmp_path):
     from oracle.oracle import f32_to_bf16
 
     assert np.array_equal(f32_to_bf16(one), full)
+
+
+def test_expert_range_matches_the_library_rule(b2q_mod):
+    """The Python rule, the C-ABI rule (b2q_ep_expert_range, host arithmetic only)
+    and the oracle's owner function agree, so the dispatch routes to the rank that
+    holds the expert."""
+    import ctypes
+
+    from b2q.ep import expert_range, token_range
+    from oracle.oracle import ep_owner
+
+    lib = b2q_mod.lib()
+    for E in (16, 128, 13, 8):
+        for world in range(1, 9):
+            if world > E:
+                continue
+            for r in range(world):
+                lo, n = ctypes.c_int(), ctypes.c_int()
+                assert lib.b2q_ep_expert_range(E, world, r, ctypes.byref(lo), ctypes.byref(n)) == 0
+                assert (lo.value, n.value) == expert_range(E, world, r)
+                assert all(ep_owner(e, E, world) == r for e in range(lo.value, lo.value + n.value))
+    lo, n = ctypes.c_int(), ctypes.c_int()
+    assert lib.b2q_ep_expert_range(4, 8, 0, ctypes.byref(lo), ctypes.byref(n)) == -1
+    for T, world in ((96, 2), (7, 3), (0, 2), (5, 8)):
+        blocks = [token_range(T, world, r) for r in range(world)]
+        assert sum(n for _, n in blocks) == T
+        assert [lo for lo, _ in blocks] == [sum(n for _, n in blocks[:r]) for r in range(world)]
+
+
+def test_a2a_plan_dedups_per_rank():
+    from oracle.oracle import ep_a2a_plan
+
+    idx = np.array([[0, 1, 8], [9, 10, 15], [2, 3, 4], [0, 15, 7]], np.uint32)
+    pos, counts = ep_a2a_plan(idx, 16, 2)
+    assert counts.tolist() == [3, 3]
+    assert pos.tolist() == [[0, 0], [-1, 1], [1, -1], [2, 2]]
+
+
+def test_a2a_argument_checks(b2q_mod):
+    lib = b2q_mod.lib()
+    # more ranks than the exchange supports, or than experts: refused on the host
+    assert lib.b2q_ep_a2a_dispatch(*([None] * 8), 4, 256, 16, 2, 9, None, 0, None) == -1
+    assert lib.b2q_ep_a2a_dispatch_workspace_size(4, 256, 4, 2, 8) == 0
+    assert lib.b2q_ep_moe_prefill_a2a_workspace_size(64, 1024, 16, 512, 4, 9) == 0
+    assert lib.b2q_ep_moe_prefill_a2a_workspace_size(64, 1024, 16, 512, 4, 2) > 2 * 64 * 1024 * (2 + 2 + 4 + 4)
+    # T above T_max, and shapes the tensor cores do not take
+    assert lib.b2q_ep_moe_prefill_a2a(*([None] * 15), 65, 64, 1024, 16, 512, 4, 64, 4, None, 0, None) == -1
+    assert lib.b2q_ep_moe_prefill_a2a(*([None] * 15), 8, 64, 1000, 16, 512, 4, 64, 4, None, 0, None) in (-1, -2)
+    assert lib.b2q_ep_a2a_combine(None, None, None, 4, 1026, 2, None) == -1
+    assert lib.b2q_ep_a2a_combine(None, None, None, 0, 1024, 2, None) == 0
+
+
+def _a2a_rank_main(rank, world, port, T, result_path):
+    """The all-to-all protocol over gloo with the oracle as the products: own
+    tokens -> plan -> rows and (expert, weight) pairs to their ranks -> local
+    partial rows -> back to the owner -> sum in rank order."""
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from b2q.ep import expert_range, token_range
+        from oracle.oracle import ep_a2a_plan
+
+        o, x, layer, idx, w, shp = _problem(S=T)
+        k, H = shp["k"], shp["H"]
+        t_lo, t_n = token_range(T, world, rank)
+        my_idx, my_w = idx[t_lo:t_lo + t_n], w[t_lo:t_lo + t_n]
+        pos, counts = ep_a2a_plan(my_idx, shp["E"], world)
+        # counts to everyone (the library all-gathers them)
+        allc = torch.zeros(world * world, dtype=torch.int32)
+        dist.all_gather(list(allc.view(world, world).unbind(0)), torch.from_numpy(counts))
+        cm = allc.view(world, world).numpy()
+        blocks = []
+        for d in range(world):
+            rows = [t for t in range(t_n) if pos[t, d] >= 0]
+            blocks.append((x[t_lo + np.array(rows, int)].reshape(-1, H) if rows else np.zeros((0, H), np.uint16),
+                           my_idx[rows].reshape(-1, k), my_w[rows].reshape(-1, k)))
+        recv = []
+        for s in range(world):
+            n = int(cm[s, rank])
+            if s == rank:
+                recv.append(blocks[rank])
+                continue
+            xb = torch.zeros((n, H), dtype=torch.int16)
+            ib = torch.zeros((n, k), dtype=torch.int64)
+            wb = torch.zeros((n, k), dtype=torch.float32)
+            # the lower rank of the pair sends first (gloo send blocks until received)
+            for turn in sorted(((rank, s), (s, rank))):
+                if turn[0] == rank and cm[rank, s]:
+                    bx, bi, bw = blocks[s]
+                    dist.send(torch.from_numpy(bx.view(np.int16).copy()), s)
+                    dist.send(torch.from_numpy(bi.astype(np.int64)), s)
+                    dist.send(torch.from_numpy(bw.astype(np.float32)), s)
+                elif turn[0] == s and n:
+                    dist.recv(xb, s)
+                    dist.recv(ib, s)
+                    dist.recv(wb, s)
+            recv.append((xb.numpy().view(np.uint16), ib.numpy().astype(np.uint32), wb.numpy()))
+        e_lo, e_local = expert_range(shp["E"], world, rank)
+        parts = []
+        for rx, ri, rw in recv:
+            sh = dict(shp, S=rx.shape[0])
+            parts.append(_partial(o, rx, layer, ri, rw, sh, e_lo, e_local) if rx.shape[0] else np.zeros((0, H), np.float32))
+        # partial rows back to the owners; the owner sums in rank order
+        ret = [None] * world
+        for s in range(world):
+            if s == rank:
+                ret[rank] = parts[rank]
+                continue
+            buf = torch.zeros((int(cm[rank, s]), H), dtype=torch.float32)
+            for turn in sorted(((rank, s), (s, rank))):
+                if turn[0] == rank and cm[s, rank]:
+                    dist.send(torch.from_numpy(np.ascontiguousarray(parts[s])), s)
+                elif turn[0] == s and cm[rank, s]:
+                    dist.recv(buf, s)
+            ret[s] = buf.numpy()
+        out = np.zeros((t_n, H), np.float32)
+        for t in range(t_n):
+            first = True
+            for d in range(world):
+                if pos[t, d] < 0:
+                    continue
+                v = ret[d][pos[t, d]]
+                out[t] = v if first else (out[t] + v).astype(np.float32)
+                first = False
+        np.save(result_path + f".{rank}.npy", out)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_a2a_layer_on_two_gloo_ranks(tmp_path):
+    import torch.multiprocessing as mp
+
+    from oracle.oracle import bf16_to_f32
+
+    T = 5
+    path = str(tmp_path / "a2a")
+    mp.start_processes(_a2a_rank_main, args=(2, _free_port(), T, path), nprocs=2, start_method="spawn", join=True)
+    got = np.concatenate([np.load(path + f".{r}.npy") for r in range(2)])
+    o, x, layer, idx, w, shp = _problem(S=T)
+    full = o.moe_experts_decode(x, idx, w, layer, shp["k"], group_size=shp["gs"])
+    e = rel_l2(got, bf16_to_f32(full))
+    assert e < REL_L2, e

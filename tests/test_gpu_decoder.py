@@ -1,0 +1,192 @@
+"""The decoder around the path on the GPU: its kernels (embedding lookup from
+the 4-bit table, RMSNorm, RoPE) against the oracle / fp32 math, the attention
+half of a block against an fp32 restatement, and the decoder's three decode
+forms (prefill, eager windows, the CUDA-graph step) against each other."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _np(t):
+    from b2q.synth import to_numpy_bits
+
+    return to_numpy_bits(t)
+
+
+def _bf(a):
+    from oracle.oracle import bf16_to_f32
+
+    return bf16_to_f32(a)
+
+
+def _tiny(**kw):
+    from b2q.model import DecoderConfig
+
+    c = dict(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=2, head_dim=128, n_experts=16, top_k=4,
+             expert_ffn=512, vocab=4096, max_seq=64, mtp=True)
+    c.update(kw)
+    return DecoderConfig(**c)
+
+
+def test_embed_gather_is_the_dequantized_rows(cuda, b2q_mod, oracle):
+    import torch
+
+    from b2q.model import Decoder
+
+    dec = Decoder(_tiny(n_layers=1, mtp=False), seed=3)
+    ids = torch.tensor([0, 4095, 17, 17, 2048], dtype=torch.int32, device="cuda")
+    got = _np(dec.embed(ids))
+    rows = ids.cpu().numpy()
+    ref = oracle.dequantize(_np(dec.embed_w)[rows], _np(dec.embed_s)[rows], _np(dec.embed_b)[rows], 64,
+                            variant="metal")
+    assert np.array_equal(got, ref)
+    assert dec.status() == 0
+    bad = torch.tensor([5, 4096], dtype=torch.int32, device="cuda")
+    out = _np(dec.embed(bad))
+    assert dec.status() == b2q_mod._lib.B2Q_EINVAL and not out[1].any()
+
+
+def test_rms_norm_and_rope(cuda, b2q_mod):
+    import torch
+
+    from b2q import synth
+    from b2q._lib import check, lib
+    from b2q.model import rms_norm
+
+    x = synth.activations((5, 1024), seed=40) * 3
+    w = (1.0 + 0.1 * synth.activations((1024,), seed=41)).to(torch.bfloat16)
+    got = _bf(_np(rms_norm(x, w, 1e-6)))
+    xf, wf = _bf(_np(x)).astype(np.float64), _bf(_np(w)).astype(np.float64)
+    ref = xf / np.sqrt((xf ** 2).mean(-1, keepdims=True) + 1e-6) * wf
+    assert np.abs(got - ref).max() <= np.abs(ref).max() * 2 ** -7
+    assert rel_l2(got, ref) < 3e-3
+    # rope over [T, heads, d] at given positions, theta 1e6
+    T, heads, d = 3, 4, 128
+    q = synth.activations((T, heads, d), seed=42)
+    pos = torch.tensor([0, 7, 1000], dtype=torch.int32, device="cuda")
+    qr = q.clone()
+    check(lib().b2q_rope(qr.data_ptr(), T, heads, d, pos.data_ptr(), 0, 1e6, torch.cuda.current_stream().cuda_stream))
+    a = _bf(_np(q)).astype(np.float64)
+    half = d // 2
+    inv = 1e6 ** (-np.arange(half) / half)
+    ang = pos.cpu().numpy()[:, None, None].astype(np.float64) * inv[None, None, :]
+    x1, x2 = a[..., :half], a[..., half:]
+    ref = np.concatenate([x1 * np.cos(ang) - x2 * np.sin(ang), x1 * np.sin(ang) + x2 * np.cos(ang)], -1)
+    assert rel_l2(_bf(_np(qr)), ref) < 5e-3
+    assert np.array_equal(_np(qr)[0], _bf16_round(ref[0]))
+
+
+def _bf16_round(a):
+    from oracle.oracle import f32_to_bf16
+
+    return f32_to_bf16(np.asarray(a, np.float32))
+
+
+def _attention_half_reference(blk, h, pos0, k_hist, v_hist):
+    """fp32 restatement of h + o(attention(rms_norm(h))) with dequantized weights,
+    rounding to bf16 where the device path stores bf16."""
+    import torch
+
+    from b2q import ops
+
+    cfg = blk.cfg
+    nq, nk, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    f = lambda t: torch.from_numpy(_bf(_np(t)).astype(np.float32))  # noqa: E731
+    rb = lambda t: t.to(torch.bfloat16).float()  # noqa: E731
+    wqkv = f(ops.dequantize(blk.qkv.weight, blk.qkv.scales, blk.qkv.biases))
+    wo = f(ops.dequantize(blk.o.weight, blk.o.scales, blk.o.biases))
+    x = f(h)
+    T = x.shape[0]
+    a = rb(x * torch.rsqrt((x * x).mean(-1, keepdim=True) + cfg.rms_eps) * f(blk.attn_norm))
+    qkv = rb(a @ wqkv.T)
+    q, k, v = qkv[:, :nq * hd], qkv[:, nq * hd:(nq + nk) * hd], qkv[:, (nq + nk) * hd:]
+    half = hd // 2
+    pos = torch.arange(pos0, pos0 + T, dtype=torch.float64)
+    inv = torch.tensor(cfg.rope_theta, dtype=torch.float64) ** (-torch.arange(half, dtype=torch.float64) / half)
+    ang = (pos[:, None] * inv[None, :])
+    cs, sn = torch.cos(ang).float()[:, None, :], torch.sin(ang).float()[:, None, :]
+
+    def rope(t, heads):
+        t = t.view(T, heads, hd)
+        x1, x2 = t[..., :half], t[..., half:]
+        return rb(torch.cat([x1 * cs - x2 * sn, x1 * sn + x2 * cs], -1))
+
+    q, k = rope(q, nq), rope(k, nk)
+    K = torch.cat([k_hist, k]) if k_hist is not None else k
+    V = torch.cat([v_hist, v.view(T, nk, hd)]) if v_hist is not None else v.view(T, nk, hd)
+    g = nq // nk
+    out = torch.zeros(T, nq, hd)
+    for t in range(T):
+        for hq in range(nq):
+            kv = hq // g
+            s = (K[:pos0 + t + 1, kv] @ q[t, hq]) / math.sqrt(hd)
+            p = torch.softmax(s, 0)
+            out[t, hq] = p @ V[:pos0 + t + 1, kv]
+    o = rb(rb(out.view(T, nq * hd)) @ wo.T)
+    return rb(x + o), K, V
+
+
+def test_attention_half_against_fp32(cuda, b2q_mod):
+    """Prefill of 12 rows, then a 2-row window at position 12 on the filled cache."""
+    import torch
+
+    from b2q import synth
+    from b2q.model import Block, rms_norm
+
+    cfg = _tiny()
+    blk = Block(cfg, torch.device("cuda"), seed=50)
+    h = synth.activations((12, cfg.hidden), seed=51)
+    pos = torch.arange(12, dtype=torch.int32, device="cuda")
+    got = h + blk.o(blk.attention(rms_norm(h, blk.attn_norm, cfg.rms_eps), pos, 0, None, None))
+    ref, K, V = _attention_half_reference(blk, h, 0, None, None)
+    assert rel_l2(_bf(_np(got)), ref.numpy()) < 1e-2
+    h2 = synth.activations((2, cfg.hidden), seed=52)
+    pos2 = torch.arange(12, 14, dtype=torch.int32, device="cuda")
+    got2 = h2 + blk.o(blk.attention(rms_norm(h2, blk.attn_norm, cfg.rms_eps), pos2, 12, None, None))
+    ref2, _, _ = _attention_half_reference(blk, h2, 12, K, V)
+    assert rel_l2(_bf(_np(got2)), ref2.numpy()) < 1e-2
+
+
+def test_decoder_decode_forms_agree(cuda, b2q_mod):
+    """The logits of position 9 from (a) a 10-token prefill, (b) a 9-token prefill
+    then a one-row window, (c) the CUDA-graph step; and greedy generation with and
+    without the draft head starts from the same token."""
+    import torch
+
+    from b2q.model import Decoder
+
+    cfg = _tiny()
+    dec = Decoder(cfg, seed=7)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(8)
+    ids = torch.randint(0, cfg.vocab, (10,), generator=g, device="cuda", dtype=torch.int32)
+    _, la = dec.forward(ids, 0)
+    la = _bf(_np(la)).reshape(-1)
+    _, _ = dec.forward(ids[:9], 0)
+    hb = dec._window(ids[9:10], 9)
+    lb = _bf(_np(dec.logits(hb))).reshape(-1)
+    assert rel_l2(lb, la) < 2e-2
+    replay, tok, pos, lg = dec.decode_graph(window=32)
+    _, _ = dec.forward(ids[:9], 0)
+    tok.fill_(int(ids[9]))
+    pos.fill_(9)
+    replay()
+    torch.cuda.synchronize()
+    lc = _bf(_np(lg)).reshape(-1)
+    assert rel_l2(lc, la) < 2e-2
+    assert int(pos.item()) == 10 and lc[int(tok.item())] == lc.max()
+    # a second replay continues from the graph's own token / position
+    replay()
+    torch.cuda.synchronize()
+    assert int(pos.item()) == 11
+    assert dec.status() == 0
+    t0, _ = dec.generate(ids, 4)
+    t1, acc = dec.generate(ids, 5, use_mtp=True)
+    assert len(t0) == 4 and len(t1) == 5 and t0[0] == t1[0] and 0 <= acc <= 2

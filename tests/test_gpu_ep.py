@@ -127,3 +127,150 @@ def test_two_ranks_nccl(cuda, b2q_mod, tmp_path, T):
     x = synth.activations((T, H), seed=92)
     ref = b2q_mod.moe_decode(x, wr, L, k) if T <= 8 else b2q_mod.moe_prefill(x, wr, L, k)
     assert rel_l2(_bf(o0), _bf(_np(ref))) < REL_L2
+
+
+# ---- all-to-all prefill ---------------------------------------------------------
+def _emulate_a2a(x, wr, L, E, k, sizes):
+    """Ranks emulated on one GPU through the three phase entry points: rank r owns
+    the next sizes[r] tokens; blocks move between ranks by tensor copies in the
+    order the NCCL exchange uses (senders in rank order)."""
+    import torch
+
+    from b2q.ep import a2a_combine, a2a_dispatch, a2a_experts, expert_range, shard_layer
+
+    N = len(sizes)
+    starts = np.cumsum([0] + list(sizes))
+    disp = [a2a_dispatch(x[starts[r]:starts[r + 1]], wr, E, k, N) for r in range(N)]
+    counts = [d[2].cpu().numpy() for d in disp]
+    parts = []
+    for d in range(N):
+        rx = torch.cat([disp[s][0][d, :counts[s][d]] for s in range(N)])
+        rm = torch.cat([disp[s][1][d, :counts[s][d]] for s in range(N)])
+        lo, n = expert_range(E, N, d)
+        parts.append(a2a_experts(rx, rm, shard_layer(L, lo, n), E, lo, k))
+    outs = []
+    for s in range(N):
+        T_s = int(sizes[s])
+        ret = torch.zeros((N, T_s, x.shape[1]), dtype=torch.float32, device=x.device)
+        for d in range(N):
+            off = int(sum(counts[q][d] for q in range(s)))
+            ret[d, :counts[s][d]] = parts[d][off:off + counts[s][d]]
+        outs.append(a2a_combine(ret, disp[s][3]))
+    return torch.cat(outs), disp
+
+
+def test_a2a_dispatch_plan_and_blocks(cuda, b2q_mod):
+    import torch
+
+    from b2q import synth
+    from b2q.ep import a2a_dispatch
+    from oracle.oracle import ep_a2a_plan
+
+    E, H, k, N, T = 16, 1024, 4, 3, 70
+    wr = synth.router_weight(E, H, seed=91)
+    x = synth.activations((T, H), seed=93)
+    send_x, send_meta, counts, pos, idx, w = a2a_dispatch(x, wr, E, k, N)
+    torch.cuda.synchronize()
+    _, ref_idx = b2q_mod.moe_prefill(x, wr, synth.moe_layer(E, H, 512, 64, seed=90), k, return_routing=True)[:2]
+    assert np.array_equal(_np(idx).astype(np.uint32), _np(ref_idx).astype(np.uint32))
+    rpos, rcounts = ep_a2a_plan(_np(idx).astype(np.uint32), E, N)
+    assert np.array_equal(_np(pos), rpos) and np.array_equal(_np(counts), rcounts)
+    xs, sx, sm = _np(x), _np(send_x), _np(send_meta).view(np.uint32)
+    for d in range(N):
+        rows = [t for t in range(T) if rpos[t, d] >= 0]
+        assert np.array_equal(sx[d, :len(rows)], xs[rows])
+        assert np.array_equal(sm[d, :len(rows), :k], _np(idx).view(np.uint32)[rows])
+        assert np.array_equal(sm[d, :len(rows), k:], _np(w).view(np.uint32)[rows])
+
+
+@pytest.mark.parametrize("sizes", [(48, 48), (40, 0, 56), (10, 30, 1, 55)])
+def test_a2a_emulated_ranks_match_the_layer(cuda, b2q_mod, oracle, sizes):
+    E, H, F, k = 16, 1024, 512, 4
+    L, wr = _layer(E, H, F, 90)
+    from b2q import synth
+
+    x = synth.activations((sum(sizes), H), seed=94)
+    out, _ = _emulate_a2a(x, wr, L, E, k, sizes)
+    ref = b2q_mod.moe_prefill(x, wr, L, k)
+    assert rel_l2(_bf(_np(out)), _bf(_np(ref))) < 5e-3
+    lg = b2q_mod.router_logits(x, wr)
+    ridx, rw = oracle.route(_np(lg), k)
+    rows = list(range(0, sum(sizes), 11))
+    ro = _bf(oracle.moe_experts_prefill(_np(x), ridx, rw, {kk: _np(v) for kk, v in L.items()}, k, rows=rows))
+    assert rel_l2(_bf(_np(out))[rows], ro) < REL_L2
+
+
+def test_a2a_single_rank_call(cuda, b2q_mod):
+    """One rank (no communicator): the chained call equals the phases bit for bit,
+    and a second call with the workspace reused gives the same output."""
+    from b2q import synth
+    from b2q.ep import EPMoE
+
+    E, H, F, k, T = 16, 1024, 512, 4, 80
+    L, wr = _layer(E, H, F, 90)
+    x = synth.activations((T, H), seed=95)
+    moe = EPMoE(wr, L, E, 0, k)
+    a = moe.prefill_a2a(x, T_max=96)
+    b = moe.prefill_a2a(x, T_max=96)
+    ref, _ = _emulate_a2a(x, wr, L, E, k, [T])
+    assert np.array_equal(_np(a), _np(ref)) and np.array_equal(_np(a), _np(b))
+
+
+def _rank_a2a(rank, world, port, T, path):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [root, os.path.join(root, "mlxfast-qwen38-125b-a6b-engine_b200")]
+        from b2q import synth
+        from b2q.ep import EPComm, EPMoE, expert_range, shard_layer, token_range
+
+        E, H, F, k = 16, 1024, 512, 4
+        L = synth.moe_layer(E, H, F, 64, device="cuda", seed=90)
+        wr = synth.router_weight(E, H, device="cuda", seed=91)
+        x = synth.activations((T, H), device="cuda", seed=96)
+        comm = EPComm(world, rank)
+        lo, n = expert_range(E, world, rank)
+        t_lo, t_n = token_range(T, world, rank)
+        moe = EPMoE(wr, shard_layer(L, lo, n), E, lo, k, comm)
+        T_max = max(token_range(T, world, r)[1] for r in range(world))
+        out = moe.prefill_a2a(x[t_lo:t_lo + t_n], T_max=T_max)
+        torch.cuda.synchronize()
+        np.save(path + f".{rank}.npy", _np(out))
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_nccl_a2a(cuda, b2q_mod, tmp_path):
+    """Two GPUs over NCCL: the same bits as the one-GPU emulation of the two ranks."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    from b2q import synth
+    from b2q.ep import token_range
+
+    T = 97
+    path = str(tmp_path / "a2a")
+    env = dict(os.environ)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        mp.start_processes(_rank_a2a, args=(2, _free_port(), T, path), nprocs=2, start_method="spawn", join=True)
+    finally:
+        os.environ.clear()
+        os.environ.update(env)
+    got = np.concatenate([np.load(path + f".{r}.npy") for r in range(2)])
+    E, H, F, k = 16, 1024, 512, 4
+    L, wr = synth.moe_layer(E, H, F, 64, seed=90), synth.router_weight(E, H, seed=91)
+    x = synth.activations((T, H), seed=96)
+    ref, _ = _emulate_a2a(x, wr, L, E, k, [token_range(T, 2, r)[1] for r in range(2)])
+    assert np.array_equal(got, _np(ref))
