@@ -225,25 +225,23 @@ def run_reference(args, rank, world):
 DEC_PROMPT, DEC_NEW = 1024, 256
 
 
-def run_decoder(dev, hbm_peak, peak_kind):
+def run_decoder(dev, hbm_peak, peak_kind, n_new=DEC_NEW, prefill_warmup=2, n_layers=48):
     """Config 3: random-init 48-layer decoder; prefill 1024 random ids, then 256 greedy
-    tokens, each one replay of the captured decode step (attention over a fixed
-    1280-row window under a mask)."""
+    tokens, each one replay of the captured decode step."""
     import torch
 
     from b2q.model import Decoder, DecoderConfig
 
-    window = DEC_PROMPT + DEC_NEW
-    cfg = DecoderConfig(max_seq=window)
+    cfg = DecoderConfig(max_seq=DEC_PROMPT + DEC_NEW, n_layers=n_layers)
     dec = Decoder(cfg, device=dev, seed=11)
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (DEC_PROMPT,), generator=g, device=dev, dtype=torch.int32)
     try:
-        replay, tok, pos, lg = dec.decode_graph(window)
+        replay, tok, pos, lg = dec.decode_graph()
     except Exception as ex:  # reported, not hidden: the leg then has no decode number
         return {"workload": "config 3", "error": f"decode step capture failed: {ex!r}"[:300]}
-    for _ in range(2):  # warm-up prefill
+    for _ in range(prefill_warmup):
         dec.forward(prompt, 0)
     torch.cuda.synchronize(dev)
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -254,23 +252,23 @@ def run_decoder(dev, hbm_peak, peak_kind):
     prefill_ms = p0.elapsed_time(p1)
     tok.copy_(logits.argmax(-1).to(torch.int32).view(1))
     pos.fill_(DEC_PROMPT)
-    tokens = torch.empty(DEC_NEW, dtype=torch.int32, device=dev)
+    tokens = torch.empty(n_new, dtype=torch.int32, device=dev)
     tokens[0].copy_(tok[0])
     torch.cuda.synchronize(dev)
     d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d0.record()
-    for i in range(1, DEC_NEW):
+    for i in range(1, n_new):
         replay()
         tokens[i].copy_(tok[0])
     d1.record()
     torch.cuda.synchronize(dev)
-    steps = DEC_NEW - 1
+    steps = n_new - 1
     ms_tok = d0.elapsed_time(d1) / steps
     status = dec.status()
-    bytes_tok = cfg.decode_bytes_per_token(DEC_PROMPT + DEC_NEW // 2)
+    bytes_tok = cfg.decode_bytes_per_token(DEC_PROMPT + n_new // 2)
     gbs = bytes_tok / (ms_tok * 1e-3) / 1e9
-    out = {"workload": "config 3: 48-layer 4-bit MoE decoder (H4096, GQA 32/4 x 128, E128 top8 F1536, vocab 151936 "
-                       "tied 4-bit), random init, prompt 1024 random ids then 256 greedy tokens",
+    out = {"workload": f"config 3: {n_layers}-layer 4-bit MoE decoder (H4096, GQA 32/4 x 128, E128 top8 F1536, vocab 151936 "
+                       f"tied 4-bit), random init, prompt {DEC_PROMPT} random ids then {n_new} greedy tokens",
            "decode_tok_s": 1000.0 / ms_tok, "ms_per_token": ms_tok, "prefill_tok_s": DEC_PROMPT * 1000.0 / prefill_ms,
            "prefill_ms": prefill_ms, "bytes_per_token": bytes_tok,
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
@@ -294,6 +292,9 @@ def main():
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="rotating layers (cold-L2 decode)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the config-3 full-decoder leg")
+    ap.add_argument("--decoder-only", type=int, default=0, metavar="TOKENS",
+                    help="run only the config-3 leg with this many generated tokens (a short case for profiling)")
+    ap.add_argument("--decoder-layers", type=int, default=48, help="layers of the config-3 model (48 in the spec)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -313,6 +314,13 @@ def main():
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    if args.decoder_only:
+        hbm_peak, _, peak_kind = load_peaks()
+        d = run_decoder(dev, hbm_peak, peak_kind, n_new=max(2, args.decoder_only), prefill_warmup=1,
+                        n_layers=args.decoder_layers)
+        print(json.dumps({"metric": "config 3 decode tok/s (bs=1)", "value": d.get("decode_tok_s"), "unit": "tok/s",
+                          "n_gpus": 1, "decoder": d}), flush=True)
+        return
     pg = None
     if world > 1:
         import torch.distributed as dist
@@ -379,11 +387,43 @@ def main():
     if pg:
         pg.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
-        torch.cuda.synchronize(dev)
+    graphs = None
+    if comm is None:
+        # One GPU: the K steps replay from CUDA graphs of G captured steps (step i reads
+        # token i mod 4096 and layer i mod 8, as in the launch loop). The launch loop is
+        # timed too and reported beside it.
         ev0.record(stream)
         for i in range(args.steps):
             step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        loop_ms = ev0.elapsed_time(ev1) / args.steps
+        G = min(args.steps, 240)
+        reps, rem = divmod(args.steps, G)
+
+        def capture(first, count):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(count):
+                    step(first + i)
+            return g
+
+        graphs = [capture(args.warmup, G)] * reps
+        if rem:
+            graphs.append(capture(args.warmup + reps * G, rem))
+        with torch.cuda.stream(stream):
+            graphs[0].replay()  # untimed warm replay
+        torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        if graphs is not None:
+            with torch.cuda.stream(stream):
+                for g in graphs:
+                    g.replay()
+        else:
+            for i in range(args.steps):
+                step(args.warmup + i)
         ev1.record(stream)
         torch.cuda.synchronize(dev)
     ms_total = ev0.elapsed_time(ev1)
@@ -556,6 +596,8 @@ def main():
                    f"the fp32 hidden vector per layer",
                    "l2": f"cold: {n_layers} rotating layers ({n_layers * E * EXPERT_BYTES / 1e9:.1f} GB experts) "
                          f"and a fresh token per step"},
+        "decode_form": ("CUDA-graph replays of the captured steps (launch loop: "
+                        f"{loop_ms * 1000.0:.2f} us per step)" if graphs is not None else "launch loop"),
         "gather_qmv_hbm_gbs": achieved,
         "hbm_frac_of_8tbs": achieved / 8000.0,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",

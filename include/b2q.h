@@ -280,6 +280,29 @@ B2Q_API int b2q_rms_norm(const uint16_t* x, const uint16_t* weight, uint16_t* ou
                    void* stream);
 B2Q_API int b2q_rope(uint16_t* x, int T, int heads, int head_dim, const int32_t* positions, int pos0,
                    float theta, void* stream);
+/* b2q_add_rms_norm: h_out = bf16(h + delta) (delta may be NULL: no add, h_out
+ *   unused; h_out may be h), out = rms_norm(h_out) as b2q_rms_norm -- the
+ *   residual add of one block fused into the next norm.
+ * b2q_rope_kv: qkv [T, (nq + 2 nk) * head_dim] (a fused q|k|v product): rope
+ *   on its q and k heads in place at positions[t], then the k and v heads
+ *   written to k_cache / v_cache [max_seq, nk, head_dim] at row positions[t]
+ *   (a position outside [0, max_seq) writes nothing and sets B2Q_EINVAL in
+ *   *status).
+ * b2q_gqa_decode: attention of T query rows (q row t at q + t * q_ld, nq heads)
+ *   over cache rows [0, positions[t]] with nq / nk query heads per kv head,
+ *   softmax(q.k / sqrt(d)) v in fp32, out [T, nq * head_dim] bf16. `window`
+ *   bounds the positions (and must not exceed the cache rows); the workspace
+ *   (b2q_gqa_decode_workspace_size) holds the per-chunk partial sums. For
+ *   decode steps and short verify windows; prefill uses a causal attention
+ *   kernel of the framework (off the path). */
+B2Q_API int b2q_add_rms_norm(const uint16_t* h, const uint16_t* delta, const uint16_t* weight, uint16_t* h_out,
+                   uint16_t* out, int T, int H, float eps, void* stream);
+B2Q_API int b2q_rope_kv(uint16_t* qkv, int T, int nq, int nk, int head_dim, const int32_t* positions, float theta,
+                   uint16_t* k_cache, uint16_t* v_cache, int max_seq, int* status, void* stream);
+B2Q_API size_t b2q_gqa_decode_workspace_size(int T, int nq, int nk, int head_dim, int window);
+B2Q_API int b2q_gqa_decode(const uint16_t* q, int q_ld, const uint16_t* k_cache, const uint16_t* v_cache,
+                   const int32_t* positions, uint16_t* out, int T, int nq, int nk, int head_dim, int window,
+                   int* status, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- checkpoint reading (per-layer packed-weight binding) ------------------ */
 

@@ -64,6 +64,10 @@ SIGNATURES = {
     "b2q_embed_gather": (_I, [_P] * 5 + [_I] * 5 + [_P, _P]),
     "b2q_rms_norm": (_I, [_P] * 3 + [_I, _I, ctypes.c_float, _P]),
     "b2q_rope": (_I, [_P, _I, _I, _I, _P, _I, ctypes.c_float, _P]),
+    "b2q_add_rms_norm": (_I, [_P] * 5 + [_I, _I, ctypes.c_float, _P]),
+    "b2q_rope_kv": (_I, [_P, _I, _I, _I, _I, _P, ctypes.c_float, _P, _P, _I, _P, _P]),
+    "b2q_gqa_decode_workspace_size": (_SZ, [_I] * 5),
+    "b2q_gqa_decode": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "b2q_st_open": (_I, [ctypes.c_char_p, _P]),
     "b2q_st_close": (_I, [_P]),
     "b2q_st_count": (_I, [_P]),

@@ -17,9 +17,11 @@ path; this decoder is the generic shape the benchmark configuration names:
 Every weight product and the MoE layers run through the library (qmv / qmm,
 the fused decode MoE, the sorted prefill MoE); RMSNorm, RoPE and the token
 embedding are library kernels too. Attention itself is PyTorch's SDPA on the
-GPU (outside the path). A greedy decode step can be captured in a CUDA graph
-(`Decoder.decode_graph`): token id and position live in device buffers that
-the graph updates itself, and attention runs over a fixed window with a mask,
+GPU for prefill (outside the path); windows of up to 8 rows (decode, MTP
+verify) use the library's GQA decode attention, which reads the rows'
+positions on the device. The residual add is fused into the following norm.
+A greedy decode step can be captured in a CUDA graph (`Decoder.decode_graph`):
+token id and position live in device buffers that the graph updates itself,
 so one replay is one token.
 
 Random-init weights follow the synthetic distributions of the benchmark
@@ -95,9 +97,13 @@ def _norm_weight(H, dev, seed):
 
 
 class Block:
-    """One decoder block: attention (fused q|k|v product, RoPE, GQA) then the MoE."""
+    """One decoder block: attention (fused q|k|v product, RoPE, GQA) then the MoE.
 
-    def __init__(self, cfg: DecoderConfig, dev, seed: int):
+    The residual stream is carried as (h, delta): a block adds the previous
+    block's MoE output into h inside its first norm (b2q_add_rms_norm) and
+    returns its own MoE output as the next delta."""
+
+    def __init__(self, cfg: DecoderConfig, dev, seed: int, status: torch.Tensor, attn_ws: torch.Tensor):
         H, hd = cfg.hidden, cfg.head_dim
         self.cfg = cfg
         self.attn_norm = _norm_weight(H, dev, seed)
@@ -109,57 +115,52 @@ class Block:
         self.moe = MoE(router, experts, cfg.top_k, cfg.group_size)
         self.k_cache = torch.zeros((cfg.max_seq, cfg.n_kv_heads, hd), dtype=torch.bfloat16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
+        self.status, self.attn_ws = status, attn_ws
 
-    def attention(self, a: torch.Tensor, positions: torch.Tensor, pos0: int | None, window: int | None,
-                  mask: torch.Tensor | None) -> torch.Tensor:
+    def attention(self, a: torch.Tensor, positions: torch.Tensor, pos0: int | None = None) -> torch.Tensor:
         """a [T, H] normed -> attention output [T, n_heads * hd] (bf16).
 
-        positions: int32 [T] device tensor of the rows' positions. With `window`
-        (graph-safe decode) attention covers cache rows [0, window) under `mask`;
-        otherwise rows [0, pos0 + T) with a causal mask (prefill / windows)."""
+        positions: int32 [T] device tensor of the rows' positions (consecutive).
+        Windows of up to 8 rows (decode, verify) attend through b2q_gqa_decode,
+        which reads the positions on the device (graph-safe); longer windows
+        (prefill) use the framework's causal attention from row pos0 on."""
         cfg = self.cfg
         T = a.shape[0]
         nq, nk, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         qkv = self.qkv(a)  # [T, (nq + 2 nk) hd]
-        q = qkv[:, :nq * hd].contiguous()
-        k = qkv[:, nq * hd:(nq + nk) * hd].contiguous()
-        v = qkv[:, (nq + nk) * hd:].view(T, nk, hd)
         st = ops._stream(a.device)
-        check(lib().b2q_rope(q.data_ptr(), T, nq, hd, positions.data_ptr(), 0, cfg.rope_theta, st))
-        check(lib().b2q_rope(k.data_ptr(), T, nk, hd, positions.data_ptr(), 0, cfg.rope_theta, st))
-        pl = positions.long()
-        self.k_cache.index_copy_(0, pl, k.view(T, nk, hd))
-        self.v_cache.index_copy_(0, pl, v)
-        g = nq // nk
-        if window is not None:
-            L = window
-            # one query row per (kv head, group member): q [1, nk, T*g, hd]
-            qh = q.view(T, nk, g, hd).permute(1, 0, 2, 3).reshape(1, nk, T * g, hd)
-            kh = self.k_cache[:L].permute(1, 0, 2).unsqueeze(0)
-            vh = self.v_cache[:L].permute(1, 0, 2).unsqueeze(0)
-            o = Fnn.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask)
-            o = o.view(nk, T, g, hd).permute(1, 0, 2, 3).reshape(T, nq * hd)
+        check(lib().b2q_rope_kv(qkv.data_ptr(), T, nq, nk, hd, positions.data_ptr(), cfg.rope_theta,
+                                self.k_cache.data_ptr(), self.v_cache.data_ptr(), cfg.max_seq,
+                                self.status.data_ptr(), st))
+        if T <= 8:
+            out = torch.empty((T, nq * hd), dtype=torch.bfloat16, device=a.device)
+            check(lib().b2q_gqa_decode(qkv.data_ptr(), cfg.qkv_rows, self.k_cache.data_ptr(),
+                                       self.v_cache.data_ptr(), positions.data_ptr(), out.data_ptr(), T, nq, nk, hd,
+                                       cfg.max_seq, self.status.data_ptr(), self.attn_ws.data_ptr(),
+                                       self.attn_ws.numel(), st))
+            return out
+        if pos0 is None:
+            raise ValueError("a window of more than 8 rows needs its first position on the host")
+        L = pos0 + T
+        qh = qkv[:, :nq * hd].view(T, nq, hd).permute(1, 0, 2).unsqueeze(0)
+        kh = self.k_cache[:L].permute(1, 0, 2).unsqueeze(0)
+        vh = self.v_cache[:L].permute(1, 0, 2).unsqueeze(0)
+        if pos0 == 0:
+            o = Fnn.scaled_dot_product_attention(qh, kh, vh, is_causal=True, enable_gqa=True)
         else:
-            L = pos0 + T
-            qh = q.view(T, nq, hd).permute(1, 0, 2).unsqueeze(0)
-            kh = self.k_cache[:L].permute(1, 0, 2).unsqueeze(0)
-            vh = self.v_cache[:L].permute(1, 0, 2).unsqueeze(0)
-            if pos0 == 0:
-                o = Fnn.scaled_dot_product_attention(qh, kh, vh, is_causal=True, enable_gqa=True)
-            else:
-                qi = torch.arange(pos0, pos0 + T, device=a.device).view(T, 1)
-                ki = torch.arange(L, device=a.device).view(1, L)
-                m = torch.zeros((T, L), dtype=torch.bfloat16, device=a.device).masked_fill(ki > qi, float("-inf"))
-                o = Fnn.scaled_dot_product_attention(qh, kh, vh, attn_mask=m, enable_gqa=True)
-            o = o.squeeze(0).permute(1, 0, 2).reshape(T, nq * hd)
-        return o.contiguous()
+            qi = torch.arange(pos0, pos0 + T, device=a.device).view(T, 1)
+            ki = torch.arange(L, device=a.device).view(1, L)
+            m = torch.zeros((T, L), dtype=torch.bfloat16, device=a.device).masked_fill(ki > qi, float("-inf"))
+            o = Fnn.scaled_dot_product_attention(qh, kh, vh, attn_mask=m, enable_gqa=True)
+        return o.squeeze(0).permute(1, 0, 2).reshape(T, nq * hd).contiguous()
 
-    def __call__(self, h: torch.Tensor, positions, pos0=None, window=None, mask=None) -> torch.Tensor:
+    def __call__(self, h: torch.Tensor, delta, positions, pos0=None):
+        """(h, delta) -> (h + delta + attention, MoE output): h is updated in place."""
         cfg = self.cfg
-        a = rms_norm(h, self.attn_norm, cfg.rms_eps)
-        h = h + self.o(self.attention(a, positions, pos0, window, mask))
-        m = rms_norm(h, self.mlp_norm, cfg.rms_eps)
-        return h + self.moe(m)
+        a = add_rms_norm(h, delta, self.attn_norm, cfg.rms_eps)
+        o = self.o(self.attention(a, positions, pos0))
+        m = add_rms_norm(h, o, self.mlp_norm, cfg.rms_eps)
+        return h, self.moe(m)
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -167,6 +168,15 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     T, H = x.shape
     out = torch.empty_like(x)
     check(lib().b2q_rms_norm(x.data_ptr(), w.data_ptr(), out.data_ptr(), T, H, eps, ops._stream(x.device)))
+    return out
+
+
+def add_rms_norm(h: torch.Tensor, delta, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """h += delta (bf16, in place; skipped when delta is None), then rms_norm(h)."""
+    T, H = h.shape
+    out = torch.empty_like(h)
+    check(lib().b2q_add_rms_norm(h.data_ptr(), None if delta is None else delta.data_ptr(), w.data_ptr(),
+                                 h.data_ptr(), out.data_ptr(), T, H, eps, ops._stream(h.device)))
     return out
 
 
@@ -181,15 +191,18 @@ class Decoder:
         ew, es, eb = synth.packed_weights((cfg.vocab,), H, cfg.group_size, dev, seed)
         self.embed_w, self.embed_s, self.embed_b = ew, es, eb
         self.lm_head = QuantizedLinear(ew, es, eb, cfg.group_size, 4)  # tied
-        self.blocks = [Block(cfg, dev, seed + 100 * (i + 1)) for i in range(cfg.n_layers)]
+        self._status = torch.zeros(1, dtype=torch.int32, device=dev)
+        ws = lib().b2q_gqa_decode_workspace_size(8, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.max_seq)
+        self._attn_ws = torch.empty(ws, dtype=torch.uint8, device=dev)
+        self.blocks = [Block(cfg, dev, seed + 100 * (i + 1), self._status, self._attn_ws)
+                       for i in range(cfg.n_layers)]
         self.final_norm = _norm_weight(H, dev, seed + 7)
         self.mtp = None
         if cfg.mtp:
             base = seed + 100 * (cfg.n_layers + 1)
             self.mtp = {"enorm": _norm_weight(H, dev, base), "hnorm": _norm_weight(H, dev, base + 1),
                         "eh_proj": _ql(H, 2 * H, cfg.group_size, dev, base + 2),
-                        "block": Block(cfg, dev, base + 10)}
-        self._status = torch.zeros(1, dtype=torch.int32, device=dev)
+                        "block": Block(cfg, dev, base + 10, self._status, self._attn_ws)}
         self._graph = None
 
     # ---- pieces --------------------------------------------------------------
@@ -218,10 +231,16 @@ class Decoder:
         if pos0 + T > self.cfg.max_seq:
             raise ValueError("sequence longer than max_seq")
         positions = torch.arange(pos0, pos0 + T, dtype=torch.int32, device=self.device)
-        h = self.embed(ids)
-        for blk in self.blocks:
-            h = blk(h, positions, pos0=pos0)
-        return h, self.logits(h[-1:])
+        h, normed = self._blocks(self.embed(ids), positions, pos0)
+        return h, self.lm_head(normed[-1:])
+
+    def _blocks(self, h, positions, pos0=None, blocks=None):
+        """Rows through the blocks; returns (final residual h, final-normed h)."""
+        delta = None
+        for blk in (self.blocks if blocks is None else blocks):
+            h, delta = blk(h, delta, positions, pos0)
+        normed = add_rms_norm(h, delta, self.final_norm, self.cfg.rms_eps)
+        return h, normed
 
     def mtp_draft(self, h_prev: torch.Tensor, ids: torch.Tensor, pos0: int) -> torch.Tensor:
         """The draft head over rows pos0..: row p takes the main model's hidden of
@@ -233,8 +252,8 @@ class Decoder:
         hh = rms_norm(h_prev.contiguous(), m["hnorm"], self.cfg.rms_eps)
         x = m["eh_proj"](torch.cat([e, hh], dim=-1))
         positions = torch.arange(pos0, pos0 + x.shape[0], dtype=torch.int32, device=self.device)
-        x = m["block"](x, positions, pos0=pos0)
-        return self.logits(x[-1:])
+        _, normed = self._blocks(x, positions, pos0, blocks=[m["block"]])
+        return self.lm_head(normed[-1:])
 
     def generate(self, prompt: torch.Tensor, n_new: int, use_mtp: bool = False):
         """Greedy decode (eager). With use_mtp the draft head proposes the token after
@@ -280,44 +299,34 @@ class Decoder:
 
     def _window(self, ids: torch.Tensor, pos0: int) -> torch.Tensor:
         positions = torch.arange(pos0, pos0 + ids.numel(), dtype=torch.int32, device=self.device)
-        h = self.embed(ids)
-        for blk in self.blocks:
-            h = blk(h, positions, pos0=pos0)
+        h, _ = self._blocks(self.embed(ids), positions, pos0)
         return h
 
     # ---- CUDA-graph decode ----------------------------------------------------------
-    def decode_graph(self, window: int):
-        """Capture one greedy decode step over attention window [0, window): the graph
-        reads the token and position from device buffers, appends to the KV cache,
-        writes the argmax back as the next token and advances the position.
+    def decode_graph(self):
+        """Capture one greedy decode step: the graph reads the token and position
+        from device buffers, appends to the KV cache, writes the argmax back as the
+        next token and advances the position (positions up to max_seq - 1).
         Returns (replay_fn, token_buf, pos_buf, logits_buf); logits_buf holds the
         last replayed step's logits [1, vocab]."""
         cfg = self.cfg
-        if window > cfg.max_seq:
-            raise ValueError("window > max_seq")
         dev = self.device
         tok = torch.zeros(1, dtype=torch.int32, device=dev)
         pos = torch.zeros(1, dtype=torch.int32, device=dev)
-        ar = torch.arange(window, dtype=torch.int32, device=dev)
-        g = cfg.n_heads // cfg.n_kv_heads
         lg_buf = torch.zeros((1, cfg.vocab), dtype=torch.bfloat16, device=dev)
         stream = torch.cuda.Stream(device=dev)
 
         def step():
-            mask = torch.where(ar <= pos, 0.0, float("-inf")).to(torch.bfloat16).view(1, 1, 1, window)
-            mask = mask.expand(1, 1, g, window)
-            h = self.embed(tok)
-            for blk in self.blocks:
-                h = blk(h, pos, window=window, mask=mask)
-            lg = self.logits(h)
+            _, normed = self._blocks(self.embed(tok), pos)
+            lg = self.lm_head(normed)
             lg_buf.copy_(lg)
             tok.copy_(lg.argmax(-1).to(torch.int32).view(1))
             pos.add_(1)
 
         # warm the library's per-shape state (tensor maps, attributes) outside the
-        # capture; the warm-up writes KV row `window - 1`, which no caller has yet
+        # capture; the warm-up writes KV row max_seq - 1, which no caller has yet
         tok.zero_()
-        pos.fill_(window - 1)
+        pos.fill_(cfg.max_seq - 1)
         stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(stream):
             step()

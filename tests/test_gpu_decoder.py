@@ -141,17 +141,21 @@ def test_attention_half_against_fp32(cuda, b2q_mod):
     from b2q.model import Block, rms_norm
 
     cfg = _tiny()
-    blk = Block(cfg, torch.device("cuda"), seed=50)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws = torch.empty(b2q_mod.lib().b2q_gqa_decode_workspace_size(8, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+                                                                  cfg.max_seq), dtype=torch.uint8, device="cuda")
+    blk = Block(cfg, torch.device("cuda"), 50, status, ws)
     h = synth.activations((12, cfg.hidden), seed=51)
     pos = torch.arange(12, dtype=torch.int32, device="cuda")
-    got = h + blk.o(blk.attention(rms_norm(h, blk.attn_norm, cfg.rms_eps), pos, 0, None, None))
+    got = h + blk.o(blk.attention(rms_norm(h, blk.attn_norm, cfg.rms_eps), pos, 0))
     ref, K, V = _attention_half_reference(blk, h, 0, None, None)
     assert rel_l2(_bf(_np(got)), ref.numpy()) < 1e-2
     h2 = synth.activations((2, cfg.hidden), seed=52)
     pos2 = torch.arange(12, 14, dtype=torch.int32, device="cuda")
-    got2 = h2 + blk.o(blk.attention(rms_norm(h2, blk.attn_norm, cfg.rms_eps), pos2, 12, None, None))
+    got2 = h2 + blk.o(blk.attention(rms_norm(h2, blk.attn_norm, cfg.rms_eps), pos2))
     ref2, _, _ = _attention_half_reference(blk, h2, 12, K, V)
     assert rel_l2(_bf(_np(got2)), ref2.numpy()) < 1e-2
+    assert int(status.item()) == 0
 
 
 def test_decoder_decode_forms_agree(cuda, b2q_mod):
@@ -173,7 +177,7 @@ def test_decoder_decode_forms_agree(cuda, b2q_mod):
     hb = dec._window(ids[9:10], 9)
     lb = _bf(_np(dec.logits(hb))).reshape(-1)
     assert rel_l2(lb, la) < 2e-2
-    replay, tok, pos, lg = dec.decode_graph(window=32)
+    replay, tok, pos, lg = dec.decode_graph()
     _, _ = dec.forward(ids[:9], 0)
     tok.fill_(int(ids[9]))
     pos.fill_(9)
@@ -190,3 +194,61 @@ def test_decoder_decode_forms_agree(cuda, b2q_mod):
     t0, _ = dec.generate(ids, 4)
     t1, acc = dec.generate(ids, 5, use_mtp=True)
     assert len(t0) == 4 and len(t1) == 5 and t0[0] == t1[0] and 0 <= acc <= 2
+
+
+def test_fused_norm_rope_kv_and_gqa_decode(cuda, b2q_mod):
+    """add_rms_norm = bf16 add then the norm; rope_kv = rope in place + cache rows;
+    gqa_decode over 3 key chunks (positions 5, 130, 299) against fp32 softmax attention."""
+    import torch
+
+    from b2q import synth
+    from b2q._lib import check, lib
+    from b2q.model import add_rms_norm, rms_norm
+
+    st = torch.cuda.current_stream().cuda_stream
+    h = synth.activations((3, 1024), seed=60) * 4
+    d = synth.activations((3, 1024), seed=61)
+    w = (1.0 + 0.1 * synth.activations((1024,), seed=62)).to(torch.bfloat16)
+    h_ref = (h.float() + d.float()).to(torch.bfloat16)
+    out = add_rms_norm(h, d, w, 1e-6)
+    assert torch.equal(h, h_ref)  # in place, one bf16 rounding
+    assert torch.equal(out, rms_norm(h_ref, w, 1e-6))
+
+    nq, nk, hd, S = 8, 2, 128, 300
+    T = 3
+    qkv = synth.activations((T, (nq + 2 * nk) * hd), seed=63)
+    pos = torch.tensor([5, 130, 299], dtype=torch.int32, device="cuda")
+    kc = synth.activations((S, nk, hd), seed=64)
+    vc = synth.activations((S, nk, hd), seed=65)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    q_ref = qkv[:, :nq * hd].clone().contiguous()
+    k_ref = qkv[:, nq * hd:(nq + nk) * hd].clone().contiguous()
+    check(lib().b2q_rope(q_ref.data_ptr(), T, nq, hd, pos.data_ptr(), 0, 1e6, st))
+    check(lib().b2q_rope(k_ref.data_ptr(), T, nk, hd, pos.data_ptr(), 0, 1e6, st))
+    x = qkv.clone()
+    check(lib().b2q_rope_kv(x.data_ptr(), T, nq, nk, hd, pos.data_ptr(), 1e6, kc.data_ptr(), vc.data_ptr(), S,
+                            status.data_ptr(), st))
+    assert torch.equal(x[:, :nq * hd], q_ref) and torch.equal(x[:, nq * hd:(nq + nk) * hd], k_ref)
+    pl = pos.long()
+    assert torch.equal(kc[pl].reshape(T, -1), k_ref)
+    assert torch.equal(vc[pl].reshape(T, -1), qkv[:, (nq + nk) * hd:])
+    ws = torch.empty(lib().b2q_gqa_decode_workspace_size(T, nq, nk, hd, S), dtype=torch.uint8, device="cuda")
+    out = torch.empty((T, nq * hd), dtype=torch.bfloat16, device="cuda")
+    check(lib().b2q_gqa_decode(x.data_ptr(), (nq + 2 * nk) * hd, kc.data_ptr(), vc.data_ptr(), pos.data_ptr(),
+                               out.data_ptr(), T, nq, nk, hd, S, status.data_ptr(), ws.data_ptr(), ws.numel(), st))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    qf, kf, vf = x[:, :nq * hd].float().view(T, nq, hd), kc.float(), vc.float()
+    ref = torch.empty(T, nq, hd, device="cuda")
+    for t in range(T):
+        p = int(pos[t])
+        for j in range(nq):
+            s = (kf[:p + 1, j // (nq // nk)] @ qf[t, j]) / hd ** 0.5
+            ref[t, j] = torch.softmax(s, 0) @ vf[:p + 1, j // (nq // nk)]
+    assert rel_l2(_bf(_np(out)), ref.view(T, -1).cpu().numpy()) < 4e-3
+    # a position outside the window is recorded
+    bad = torch.tensor([300], dtype=torch.int32, device="cuda")
+    check(lib().b2q_gqa_decode(x.data_ptr(), (nq + 2 * nk) * hd, kc.data_ptr(), vc.data_ptr(), bad.data_ptr(),
+                               out.data_ptr(), 1, nq, nk, hd, S, status.data_ptr(), ws.data_ptr(), ws.numel(), st))
+    torch.cuda.synchronize()
+    assert int(status.item()) == b2q_mod._lib.B2Q_EINVAL
