@@ -717,33 +717,6 @@ __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Pa
         }
       }
       named_bar_sync(2, NTH);  // releases the producer
-#ifdef B2Q_D1_PREFETCH_DOWN
-      {
-        // L2 prefetch of this CTA's down rows (its units are static: u = b, b + grid,
-        // ...) while the gate|up phase streams: per unit and routed slot, 8 rows of
-        // packed weights and their scale / bias rows, one 128-byte line per request
-        const int nl2p = local_units(ph2.units);
-        const int nlp = EP ? *nloc_sm : p.k;
-        const int wrow = p.F / 2, mrow = (p.F / p.gs) * 2;
-        const int wl = 8 * wrow / 128, ml = (8 * mrow + 127) / 128;
-        const int per = wl + 2 * ml;
-        const int total = nl2p * nlp * per;
-        for (int i = tid; i < total; i += NCT) {
-          const int j2 = i / (nlp * per), rem = i % (nlp * per), sl = rem / per, l = rem % per;
-          const size_t u = (size_t)blockIdx.x + (size_t)j2 * gridDim.x;
-          const uint32_t e = EP ? sidx[lslot[sl]] - (uint32_t)p.e_lo : sidx[sl];
-          const size_t row0 = (size_t)e * p.H + u * 8;
-          const char* a;
-          if (l < wl)
-            a = static_cast<const char*>(p.down_w) + row0 * wrow + (size_t)l * 128;
-          else if (l < wl + ml)
-            a = static_cast<const char*>(p.down_s) + row0 * mrow + (size_t)min((l - wl) * 128, 8 * mrow - 1);
-          else
-            a = static_cast<const char*>(p.down_b) + row0 * mrow + (size_t)min((l - wl - ml) * 128, 8 * mrow - 1);
-          asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(a));
-        }
-      }
-#endif
     }
     if (!fused) {
       stage_cols(xbuf, xsum, 1, p.XS1, p.x, 0, 1, p.K1, p.gs, false);
@@ -1204,9 +1177,6 @@ int d1_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
   p.e_lo = e_lo;
   p.e_local = e_local;
   p.out_f32 = out_f32;
-  p.down_w = wd;
-  p.down_s = sd;
-  p.down_b = bd;
   p.timeout_ns = 2000000000ll;
   const int mode = out_f32 ? D1_FUSED_EP : D1_FUSED;
   int rc = plan(p, mode);

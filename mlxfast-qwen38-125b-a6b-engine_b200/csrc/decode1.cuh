@@ -30,9 +30,6 @@ struct alignas(64) D1Params {
   long long timeout_ns;
   int e_lo, e_local;  // expert parallel: this rank holds experts [e_lo, e_lo + e_local) (e_local 0: all)
   float* out_f32;     // expert parallel: fp32 partial output instead of bf16 `out`
-  const void* down_w;  // fused: the down stacks (raw, for the L2 prefetch of the routed rows)
-  const void* down_s;
-  const void* down_b;
   int off_slots, off_x, off_xs, off_act, off_acts, off_red, off_misc, smem_bytes;
   int XS1, XS2;
 };

@@ -330,7 +330,9 @@ __global__ void __launch_bounds__(ATT_CHUNK)
       for (int j = 0; j < ATT_MAXG; ++j)
         if (j < g) acc[j] = fmaf(ps[j][key], vv, acc[j]);
     }
-    for (int j = 0; j < g; ++j) out[2 * g + (size_t)j * d + e] = acc[j];
+#pragma unroll
+    for (int j = 0; j < ATT_MAXG; ++j)  // static indices keep acc in registers
+      if (j < g) out[2 * g + (size_t)j * d + e] = acc[j];
   }
 }
 
