@@ -230,13 +230,26 @@ constexpr int ATT_CHUNK = 128;  // keys per CTA (one per thread in the score pha
 constexpr int ATT_MAXG = 16;    // query heads per kv head
 constexpr int ATT_MAXD = 256;   // head_dim
 
+// Shared memory of one chunk CTA: K rows padded by 8 values (16-byte reads of
+// consecutive rows fall in distinct banks), V rows, the g query rows (fp32) and
+// the g x 128 probabilities.
+__host__ __device__ inline int gqa_kld(int d) { return d + 8; }
+__host__ __device__ inline size_t gqa_smem_bytes(int g, int d) {
+  return (size_t)ATT_CHUNK * gqa_kld(d) * 2 + (size_t)ATT_CHUNK * d * 2 + (size_t)g * d * 4 +
+         (size_t)g * ATT_CHUNK * 4;
+}
+
 // partial layout per (t, kv head, chunk): [g] max, [g] sum, [g][d] weighted values
 __global__ void __launch_bounds__(ATT_CHUNK)
     gqa_chunk_kernel(const uint16_t* __restrict__ q, int q_ld, const uint16_t* __restrict__ kc,
                      const uint16_t* __restrict__ vc, const int32_t* __restrict__ positions, int nk, int g, int d,
                      int n_chunks, int window, float scale_log2, float* __restrict__ part, int* err) {
-  __shared__ float qs[ATT_MAXG][ATT_MAXD];
-  __shared__ float ps[ATT_MAXG][ATT_CHUNK];
+  extern __shared__ __align__(16) unsigned char gsm[];
+  const int kld = gqa_kld(d);
+  uint16_t* ks = reinterpret_cast<uint16_t*>(gsm);
+  uint16_t* vs = ks + (size_t)ATT_CHUNK * kld;
+  float* qs = reinterpret_cast<float*>(vs + (size_t)ATT_CHUNK * d);
+  float* ps = qs + (size_t)g * d;
   __shared__ float red[ATT_MAXG][ATT_CHUNK / 32];
   __shared__ float stat[ATT_MAXG];
   const int kh = blockIdx.x, chunk = blockIdx.y, t = blockIdx.z;
@@ -256,9 +269,21 @@ __global__ void __launch_bounds__(ATT_CHUNK)
     }
     return;
   }
+  // stage the chunk's K and V rows (16-byte loads, many in flight per thread) and q
+  const int vpr = d / 8;  // 16-byte vectors per row
+  const int nvec = nkeys * vpr;
+#pragma unroll 4
+  for (int i = tid; i < nvec; i += ATT_CHUNK) {
+    const int key = i / vpr, c = i % vpr;
+    const size_t src = ((size_t)(k0 + key) * nk + kh) * d + (size_t)c * 8;
+    const uint4 kv = __ldg(reinterpret_cast<const uint4*>(kc + src));
+    const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vc + src));
+    *reinterpret_cast<uint4*>(ks + (size_t)key * kld + c * 8) = kv;
+    *reinterpret_cast<uint4*>(vs + (size_t)key * d + c * 8) = vv;
+  }
   for (int idx = tid; idx < g * d; idx += ATT_CHUNK) {
     const int j = idx / d, e = idx % d;
-    qs[j][e] = bf2f(q[(size_t)t * q_ld + (size_t)(kh * g + j) * d + e]);
+    qs[idx] = bf2f(q[(size_t)t * q_ld + (size_t)(kh * g + j) * d + e]);
   }
   __syncthreads();
   // scores: thread = key
@@ -266,11 +291,11 @@ __global__ void __launch_bounds__(ATT_CHUNK)
 #pragma unroll
   for (int j = 0; j < ATT_MAXG; ++j) s[j] = -INFINITY;
   if (tid < nkeys) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kc + ((size_t)(k0 + tid) * nk + kh) * d);
 #pragma unroll
     for (int j = 0; j < ATT_MAXG; ++j) s[j] = 0.0f;
-    for (int v = 0; v < d / 8; ++v) {
-      const uint4 kv = __ldg(kr + v);
+    const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)tid * kld);
+    for (int v = 0; v < vpr; ++v) {
+      const uint4 kv = kr[v];
       const uint32_t u[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
@@ -278,7 +303,7 @@ __global__ void __launch_bounds__(ATT_CHUNK)
         const int e = v * 8 + 2 * m;
 #pragma unroll
         for (int j = 0; j < ATT_MAXG; ++j)
-          if (j < g) s[j] = fmaf(c, qs[j][e + 1], fmaf(a, qs[j][e], s[j]));
+          if (j < g) s[j] = fmaf(c, qs[j * d + e + 1], fmaf(a, qs[j * d + e], s[j]));
       }
     }
 #pragma unroll
@@ -305,7 +330,7 @@ __global__ void __launch_bounds__(ATT_CHUNK)
   for (int j = 0; j < ATT_MAXG; ++j) {
     if (j < g) {
       const float pj = (tid < nkeys) ? exp2f(s[j] - stat[j]) : 0.0f;
-      ps[j][tid] = pj;
+      ps[j * ATT_CHUNK + tid] = pj;
       float l = pj;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
@@ -319,16 +344,17 @@ __global__ void __launch_bounds__(ATT_CHUNK)
     out[tid] = stat[tid];
     out[g + tid] = l;
   }
-  // weighted values: thread = dimension
+  // weighted values from shared memory: thread = dimension
   for (int e = tid; e < d; e += ATT_CHUNK) {
     float acc[ATT_MAXG];
 #pragma unroll
     for (int j = 0; j < ATT_MAXG; ++j) acc[j] = 0.0f;
+#pragma unroll 4
     for (int key = 0; key < nkeys; ++key) {
-      const float vv = bf2f(vc[((size_t)(k0 + key) * nk + kh) * d + e]);
+      const float vv = bf2f(vs[(size_t)key * d + e]);
 #pragma unroll
       for (int j = 0; j < ATT_MAXG; ++j)
-        if (j < g) acc[j] = fmaf(ps[j][key], vv, acc[j]);
+        if (j < g) acc[j] = fmaf(ps[j * ATT_CHUNK + key], vv, acc[j]);
     }
 #pragma unroll
     for (int j = 0; j < ATT_MAXG; ++j)  // static indices keep acc in registers
@@ -457,7 +483,8 @@ int b2q_gqa_decode(const uint16_t* q, int q_ld, const uint16_t* k_cache, const u
                      window);
   if (T == 0) return B2Q_OK;
   if (!q || !k_cache || !v_cache || !positions || !out) return set_error(B2Q_EINVAL, "gqa_decode: null pointer");
-  if (!aligned16(k_cache)) return set_error(B2Q_EINVAL, "gqa_decode: k_cache must be 16-byte aligned");
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return set_error(B2Q_EINVAL, "gqa_decode: k_cache and v_cache must be 16-byte aligned");
   const size_t need = b2q_gqa_decode_workspace_size(T, nq, nk, head_dim, window);
   if (!workspace || workspace_bytes < need)
     return set_error(B2Q_EINVAL, "gqa_decode: workspace of %zu bytes needed", need);
@@ -468,8 +495,19 @@ int b2q_gqa_decode(const uint16_t* q, int q_ld, const uint16_t* k_cache, const u
   float* part = static_cast<float*>(workspace);
   // scores in the log2 domain: q.k / sqrt(d) * log2(e)
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
-  gqa_chunk_kernel<<<dim3(nk, chunks, T), ATT_CHUNK, 0, st>>>(q, q_ld, k_cache, v_cache, positions, nk, g, head_dim,
-                                                             chunks, window, scale_log2, part, status);
+  const size_t smem = gqa_smem_bytes(g, head_dim);
+  static int attr_done[64] = {};
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if ((int)smem > di.smem_optin) return set_error(B2Q_EUNSUPPORTED, "gqa_decode: %zu bytes of shared memory", smem);
+  if (!attr_done[di.device & 63]) {  // the largest shape's need, once per device
+    B2Q_TRY_CUDA(cudaFuncSetAttribute(gqa_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)gqa_smem_bytes(ATT_MAXG, ATT_MAXD)));
+    attr_done[di.device & 63] = 1;
+  }
+  gqa_chunk_kernel<<<dim3(nk, chunks, T), ATT_CHUNK, smem, st>>>(q, q_ld, k_cache, v_cache, positions, nk, g,
+                                                                head_dim, chunks, window, scale_log2, part, status);
   B2Q_TRY_CUDA(cudaGetLastError());
   gqa_merge_kernel<<<dim3(nk, g, T), 128, 0, st>>>(part, out, nk, g, head_dim, chunks);
   B2Q_TRY_CUDA(cudaGetLastError());
