@@ -22,7 +22,7 @@
 //                  scatters).
 //   gqa_decode   : attention of a few query rows over the KV cache rows
 //                  [0, position] (decode and short windows): split over key
-//                  chunks of 64, each CTA one kv head and chunk with the g
+//                  chunks of 128, each CTA one kv head and chunk with the g
 //                  query heads that share it, fp32 scores / exp / sums; a second
 //                  kernel merges the chunks (max-rescaled sums) and rounds once.
 #include <cuda_runtime.h>
@@ -227,7 +227,7 @@ __global__ void rope_kv_kernel(uint16_t* __restrict__ qkv, int T, int nq, int nk
 
 // ---- GQA attention of a few query rows over the cache ------------------------------
 #ifndef B2Q_ATT_CHUNK
-#define B2Q_ATT_CHUNK 64
+#define B2Q_ATT_CHUNK 128
 #endif
 constexpr int ATT_CHUNK = B2Q_ATT_CHUNK;  // keys per CTA (one per thread in the score phase)
 constexpr int ATT_MAXG = 16;    // query heads per kv head

@@ -39,7 +39,7 @@ def test_decoder_kernels_refuse_bad_shapes(b2q_mod):
     assert lib.b2q_rope(None, 1, 4, 127, None, 0, 1e6, None) == -1
     assert lib.b2q_embed_gather(None, None, None, None, None, 1, 10, 1024, 48, 4, None, None) == -2
     assert lib.b2q_embed_gather(None, None, None, None, None, 0, 10, 1024, 64, 4, None, None) == 0
-    assert lib.b2q_gqa_decode_workspace_size(1, 32, 4, 128, 1280) == 4 * 4 * 20 * 8 * 130  # 64-key chunks
+    assert lib.b2q_gqa_decode_workspace_size(1, 32, 4, 128, 1280) == 4 * 4 * 10 * 8 * 130  # 128-key chunks
     assert lib.b2q_gqa_decode(None, 4096, None, None, None, None, 1, 30, 4, 128, 64, None, None, 0, None) == -1
     assert lib.b2q_rope_kv(None, 0, 8, 2, 128, None, 1e6, None, None, 64, None, None) == 0
     assert lib.b2q_add_rms_norm(None, None, None, None, None, 1, 1001, 1e-6, None) == -1
