@@ -281,6 +281,66 @@ def run_decoder(dev, hbm_peak, peak_kind, n_new=DEC_NEW, prefill_warmup=2, n_lay
     return out
 
 
+EP_PROMPT, EP_NEW = 8192, 512
+
+
+def run_ep_decoder(dev, world, rank, comm, pg, hbm_peak, peak_kind, n_new=EP_NEW, n_layers=48):
+    """Config 4: the config-3 model with every MoE layer's experts sharded over the
+    ranks (attention replicated); prefill 8192 random ids, then greedy tokens, each
+    one replay of the captured step (NCCL all-reduce per layer inside the graph).
+    Times are the max over ranks."""
+    import torch
+
+    from b2q.model import Decoder, DecoderConfig
+
+    cfg = DecoderConfig(max_seq=EP_PROMPT + n_new, n_layers=n_layers, mtp=False)
+    dec = Decoder(cfg, device=dev, seed=11, expert_parallel=(comm, world, rank))
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (EP_PROMPT,), generator=g, device=dev, dtype=torch.int32)
+    replay, tok, pos, lg = dec.decode_graph()
+    dec.forward(prompt, 0)  # warm-up prefill
+    torch.cuda.synchronize(dev)
+
+    def max_over_ranks(ms):
+        if pg is None:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    if pg is not None:
+        pg.barrier()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    _, logits = dec.forward(prompt, 0)
+    p1.record()
+    torch.cuda.synchronize(dev)
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1))
+    tok.copy_(logits.argmax(-1).to(torch.int32).view(1))
+    pos.fill_(EP_PROMPT)
+    torch.cuda.synchronize(dev)
+    if pg is not None:
+        pg.barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for _ in range(1, n_new):
+        replay()
+    d1.record()
+    torch.cuda.synchronize(dev)
+    ms_tok = max_over_ranks(d0.elapsed_time(d1) / (n_new - 1))
+    status = dec.status()
+    del replay, dec
+    torch.cuda.empty_cache()
+    return {"workload": f"config 4: the config-3 model ({n_layers} layers) expert-parallel over {world} GPU(s), "
+                        f"experts {cfg.n_experts}/{world} per GPU, attention replicated; prompt {EP_PROMPT} random "
+                        f"ids then {n_new} greedy tokens",
+            "decode_tok_s": 1000.0 / ms_tok, "ms_per_token": ms_tok, "prefill_tok_s": EP_PROMPT * 1000.0 / prefill_ms,
+            "prefill_ms": prefill_ms, "device_status": status,
+            "decode_form": "one CUDA-graph replay per token; one NCCL all-reduce of the fp32 hidden partial per "
+                           "layer inside the graph; prefill MoE layers through the all-reduce form"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -295,6 +355,8 @@ def main():
     ap.add_argument("--decoder-only", type=int, default=0, metavar="TOKENS",
                     help="run only the config-3 leg with this many generated tokens (a short case for profiling)")
     ap.add_argument("--decoder-layers", type=int, default=48, help="layers of the config-3 model (48 in the spec)")
+    ap.add_argument("--ep-decoder", type=int, default=0, metavar="TOKENS",
+                    help="run only the config-4 leg (expert-parallel full model over the launched ranks)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -331,6 +393,21 @@ def main():
 
     hbm_peak, tc_peak, peak_kind = load_peaks()
     L = lib()
+    if args.ep_decoder:
+        from b2q.ep import EPComm
+
+        comm4 = EPComm(world, rank, group=pg.group.WORLD) if world > 1 else None
+        d = run_ep_decoder(dev, world, rank, comm4, pg, hbm_peak, peak_kind, n_new=max(2, args.ep_decoder),
+                           n_layers=args.decoder_layers)
+        if comm4 is not None:
+            torch.cuda.synchronize(dev)
+            comm4.close()
+        if rank == 0:
+            print(json.dumps({"metric": "config 4 decode tok/s (bs=1)", "value": d["decode_tok_s"], "unit": "tok/s",
+                              "n_gpus": world, "decoder": d}), flush=True)
+        if pg:
+            pg.destroy_process_group()
+        return
 
     # ---------------- decode (config 1) ----------------
     n_layers = max(1, args.layers)

@@ -36,6 +36,7 @@ import torch.nn.functional as Fnn
 
 from . import ops, synth
 from ._lib import check, lib
+from .ep import EPMoE, expert_range, shard_layer
 from .nn import MoE, QuantizedLinear
 
 
@@ -103,7 +104,8 @@ class Block:
     block's MoE output into h inside its first norm (b2q_add_rms_norm) and
     returns its own MoE output as the next delta."""
 
-    def __init__(self, cfg: DecoderConfig, dev, seed: int, status: torch.Tensor, attn_ws: torch.Tensor):
+    def __init__(self, cfg: DecoderConfig, dev, seed: int, status: torch.Tensor, attn_ws: torch.Tensor,
+                 ep: tuple | None = None):
         H, hd = cfg.hidden, cfg.head_dim
         self.cfg = cfg
         self.attn_norm = _norm_weight(H, dev, seed)
@@ -112,7 +114,16 @@ class Block:
         self.mlp_norm = _norm_weight(H, dev, seed + 3)
         router = synth.router_weight(cfg.n_experts, H, dev, seed + 4)
         experts = synth.moe_layer(cfg.n_experts, H, cfg.expert_ffn, cfg.group_size, dev, seed + 5)
-        self.moe = MoE(router, experts, cfg.top_k, cfg.group_size)
+        if ep is None:
+            self.moe = MoE(router, experts, cfg.top_k, cfg.group_size)
+        else:
+            # expert parallel: this rank keeps its contiguous block of experts; the
+            # layer output is the NCCL all-reduce of the ranks' fp32 partials
+            comm, world, rank = ep
+            lo, n = expert_range(cfg.n_experts, world, rank)
+            local = shard_layer(experts, lo, n)
+            del experts
+            self.moe = EPMoE(router, local, cfg.n_experts, lo, cfg.top_k, comm, cfg.group_size)
         self.k_cache = torch.zeros((cfg.max_seq, cfg.n_kv_heads, hd), dtype=torch.bfloat16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.status, self.attn_ws = status, attn_ws
@@ -181,9 +192,16 @@ def add_rms_norm(h: torch.Tensor, delta, w: torch.Tensor, eps: float) -> torch.T
 
 
 class Decoder:
-    """Random-init decoder of `cfg` on `device` (seeded), with a bf16 KV cache of cfg.max_seq rows per layer."""
+    """Random-init decoder of `cfg` on `device` (seeded), with a bf16 KV cache of cfg.max_seq rows per layer.
 
-    def __init__(self, cfg: DecoderConfig, device="cuda", seed: int = 0):
+    expert_parallel=(comm, world, rank) shards every MoE layer's experts over the
+    ranks of `comm` (an EPComm, or None for one rank): attention, norms, router
+    and embeddings stay replicated, every rank runs the same token stream, and
+    each MoE layer ends in one NCCL all-reduce of the fp32 layer partial (the
+    expert-parallel full-model configuration). All ranks must call the same
+    methods in the same order."""
+
+    def __init__(self, cfg: DecoderConfig, device="cuda", seed: int = 0, expert_parallel: tuple | None = None):
         self.cfg = cfg.validate()
         dev = torch.device(device)
         self.device = dev
@@ -194,7 +212,7 @@ class Decoder:
         self._status = torch.zeros(1, dtype=torch.int32, device=dev)
         ws = lib().b2q_gqa_decode_workspace_size(8, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.max_seq)
         self._attn_ws = torch.empty(ws, dtype=torch.uint8, device=dev)
-        self.blocks = [Block(cfg, dev, seed + 100 * (i + 1), self._status, self._attn_ws)
+        self.blocks = [Block(cfg, dev, seed + 100 * (i + 1), self._status, self._attn_ws, expert_parallel)
                        for i in range(cfg.n_layers)]
         self.final_norm = _norm_weight(H, dev, seed + 7)
         self.mtp = None
@@ -202,7 +220,7 @@ class Decoder:
             base = seed + 100 * (cfg.n_layers + 1)
             self.mtp = {"enorm": _norm_weight(H, dev, base), "hnorm": _norm_weight(H, dev, base + 1),
                         "eh_proj": _ql(H, 2 * H, cfg.group_size, dev, base + 2),
-                        "block": Block(cfg, dev, base + 10, self._status, self._attn_ws)}
+                        "block": Block(cfg, dev, base + 10, self._status, self._attn_ws, expert_parallel)}
         self._graph = None
 
     # ---- pieces --------------------------------------------------------------

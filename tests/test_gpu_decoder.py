@@ -252,3 +252,30 @@ def test_fused_norm_rope_kv_and_gqa_decode(cuda, b2q_mod):
                                out.data_ptr(), 1, nq, nk, hd, S, status.data_ptr(), ws.data_ptr(), ws.numel(), st))
     torch.cuda.synchronize()
     assert int(status.item()) == b2q_mod._lib.B2Q_EINVAL
+
+
+def test_expert_parallel_decoder_one_rank(cuda, b2q_mod):
+    """The expert-parallel decoder on one rank (all experts local, the EP decode and
+    prefill operators with their fp32 partials) agrees with the plain decoder built
+    from the same seeds, in prefill and in the CUDA-graph step."""
+    import torch
+
+    from b2q.model import Decoder
+
+    cfg = _tiny(mtp=False)
+    ref = Decoder(cfg, seed=21)
+    dec = Decoder(cfg, seed=21, expert_parallel=(None, 1, 0))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(22)
+    ids = torch.randint(0, cfg.vocab, (12,), generator=g, device="cuda", dtype=torch.int32)
+    _, la = ref.forward(ids, 0)
+    _, lb = dec.forward(ids, 0)
+    assert rel_l2(_bf(_np(lb)), _bf(_np(la))) < 2e-2
+    replay, tok, pos, lg = dec.decode_graph()
+    dec.forward(ids[:11], 0)
+    tok.fill_(int(ids[11]))
+    pos.fill_(11)
+    replay()
+    torch.cuda.synchronize()
+    assert rel_l2(_bf(_np(lg)).reshape(-1), _bf(_np(la)).reshape(-1)) < 2e-2
+    assert dec.status() == 0
