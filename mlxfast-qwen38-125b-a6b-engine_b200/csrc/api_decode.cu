@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "decode1.cuh"
+#include "decode2.cuh"
 #include "decode_ws.hpp"
 #include "engine.cuh"
 #include "host.hpp"
@@ -60,9 +61,10 @@ static int gather_impl(const char* fn, const uint16_t* x, const uint32_t* w, con
   if (!aligned16(x)) return set_error(B2Q_EINVAL, "%s: x must be 16-byte aligned", fn);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // one row of x times one weight matrix: the single-column streaming kernel
-  if (M == 1 && batch == 1 && !lhs && !rhs && n_x >= 1 && n_w >= 1 && d1_qmv_eligible(N, K, gs, x, w, s, b) &&
-      aligned16(y))
-    return d1_qmv(x, w, s, b, y, N, K, gs, st);
+  if (M == 1 && batch == 1 && !lhs && !rhs && n_x >= 1 && n_w >= 1 && aligned16(y)) {
+    if (!decode_v1() && d2_qmv_eligible(N, K, gs, x, w, s, b)) return d2_qmv(x, w, s, b, y, N, K, gs, st);
+    if (decode_v1() && d1_qmv_eligible(N, K, gs, x, w, s, b)) return d1_qmv(x, w, s, b, y, N, K, gs, st);
+  }
   const bool engine_ok = M <= eng::MAX_COLS && engine_k_ok(K, gs) && aligned16(w) && aligned16(s) &&
                          aligned16(b);
   if (engine_ok) {
@@ -196,7 +198,7 @@ int b2q_moe_down_combine(const uint16_t* act, const uint32_t* wd, const uint16_t
 size_t b2q_moe_decode_workspace_size(int S, int H, int E, int F, int k) {
   (void)H;
   if (S < 1 || E < 1 || F < 1 || k < 1) return 0;
-  return decode_ws_layout(nullptr, S, E, F, k).bytes;
+  return decode_ws_layout(nullptr, S, H, E, F, k).bytes;
 }
 
 int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
@@ -212,14 +214,19 @@ int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, co
                      "moe_decode: shape outside the kernel (S<=8, k<=8, E<=1024, H,F multiples of 8*group_size)");
   if (!x || !wr || !wg || !sg || !bg || !wu || !su || !bu || !wd || !sd || !bd || !out)
     return set_error(B2Q_EINVAL, "moe_decode: null pointer");
-  const DecodeWs ws = decode_ws_layout(workspace, S, E, F, k);
+  const DecodeWs ws = decode_ws_layout(workspace, S, H, E, F, k);
   if (!workspace || workspace_bytes < ws.bytes || !aligned16(workspace))
     return set_error(B2Q_EINVAL, "moe_decode: workspace of %zu bytes needed", ws.bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const void* ptrs[] = {x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd};
   bool all_aligned = true;
   for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
-  if (S == 1 && all_aligned && d1_moe_eligible(H, E, F, k, group_size))
+  if (S == 1 && all_aligned && !decode_v1() && d2_moe_eligible(H, E, F, k, group_size)) {
+    const D2Scratch scr{&ws.hdr->error, ws.ctr, ws.logits, ws.act, ws.asum, ws.y};
+    return d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size, scr,
+                         st);
+  }
+  if (S == 1 && all_aligned && decode_v1() && d1_moe_eligible(H, E, F, k, group_size))
     return d1_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size,
                          &ws.hdr->error, ws.hdr->counters, ws.hdr->sched, ws.logits, ws.act, st);
   if (S == 1) {

@@ -4,6 +4,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -25,6 +26,14 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 void clear_error() { g_last_error.clear(); }
+
+bool decode_v1() {
+  static const bool v = [] {
+    const char* e = std::getenv("B2Q_DECODE_V1");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
 
 int device_info(DeviceInfo* out) {
   static std::mutex mu;

@@ -1,0 +1,956 @@
+// decode2.cu -- single-column streaming products on a unit queue: qmv for one
+// row of x (M = 1) and the fused one-token MoE decode layer.
+//
+// Reference operators (paths relative to the reference project):
+//   qmv_fast_impl / qdot       Vendor/mlx-swift/Source/Cmlx/mlx/mlx/backend/metal/kernels/quantized.h:28-105,191-290,757-822
+//   gateUpAct / downCombine    Runner/FastModel/TrackFastMoE.swift:1192-1590
+//   route (top-k + softmax)    Runner/FastModel/TrackFastMoE.swift:767-911
+//   combine association        Runner/FastModel/TrackFastKernels2.swift:36-47
+//
+// Organisation: one CTA per SM, one producer warp and 8 consumer warps.
+//  * The work of a call is a sequence of units, each one TMA fill of a stage:
+//      gate|up unit  16 outputs of one routed expert: its 16 gate rows and 16
+//                    up rows over the whole hidden size (two copies of 16 rows
+//                    x the whole row) plus their 4 scale / bias blocks;
+//      down unit     64 rows of one routed expert's down matrix over the whole
+//                    expert width, their scales / biases, and the expert's
+//                    SwiGLU activations (with their chunk sums);
+//      qmv unit      16 rows of the matrix over the whole reduction.
+//    Fused calls hand units out from a grid-wide counter in the order: all
+//    gate|up units slot by slot, then all down units slot by slot, so the down
+//    units of slot j start as soon as slot j's activations are final (a
+//    per-slot count of finished gate|up units), with no grid-wide barrier
+//    between the two phases. qmv units go round-robin over the CTAs.
+//  * Large copies (32 KB boxes of whole rows) keep the per-copy issue cost of
+//    the TMA small against the bytes moved.
+//  * The producer fills a ring of stages (full / empty mbarrier per stage) with
+//    whole-row TMA boxes in the 128-byte swizzle (16-byte unit u of row r at
+//    position u ^ (r % 8)); the consumer warps split the unit's reduction (or
+//    its row blocks and reduction) between them and hand their row partials
+//    to shared memory; the last warp to arrive finishes the unit: bf16 store
+//    (qmv), SwiGLU into the activations (gate|up) or the per-slot down
+//    products, and the last down unit of a 64-row block folds the k slots in
+//    the reference's combine order.
+//  * Dot products: nibbles OR-ed into bf16 128.0 give exactly 128 + q; the
+//    legacy mma.sync m16n8k16 (bf16 x bf16 -> fp32) multiplies 16 weight rows
+//    (P: 8 rows, Q: 8 rows) by the activation chunk, each product exact in
+//    fp32; per group: s * (D - 128 * sum(x)) + b * sum(x) (the Metal qdot
+//    factorisation, quantized.h:191-290). For gate|up and qmv units the
+//    activation chunks of a warp's reduction slice stay in registers.
+//  * Launches use programmatic dependent launch: barrier set-up, tensor-map
+//    prefetch and L2 prefetches (router rows; the first qmv units) run while
+//    the previous kernel in the stream finishes; nothing is read into the CTA
+//    before griddepcontrol.wait.
+// All waits are bounded; a wait that runs out records B2Q_ETIMEOUT and raises
+// an abort flag that ends every loop; the producer lets its copies land
+// before the CTA exits.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "decode2.cuh"
+#include "host.hpp"
+#include "tc.cuh"
+#include "tmap.hpp"
+
+namespace b2q {
+namespace d2 {
+
+constexpr int NCW = 8;               // consumer warps
+constexpr int NTH = (NCW + 1) * 32;  // + the producer warp
+constexpr int MAXK = 8;              // routed slots
+constexpr int MAXST = 6;             // stages at most
+constexpr int ROWS_QMV = 16;         // rows of a qmv unit
+constexpr int ROWS_GU = 16;          // outputs of a gate|up unit (16 gate + 16 up rows)
+constexpr int ROWS_DOWN = 64;        // rows of a down unit
+constexpr int MISC_BYTES = 512;
+constexpr int XR = 16;               // activation chunks a consumer lane holds in registers
+
+enum : int { U_END = -1, U_GU = 0, U_DOWN = 1, U_QMV = 2 };
+enum : int { MW = 0, MS = 1, MB = 2, MWG = 0, MSG = 1, MBG = 2, MWU = 3, MSU = 4, MBU = 5, MWD = 6, MSD = 7, MBD = 8 };
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+__device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar,
+                                     uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+__device__ __forceinline__ float lbf(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float hbf(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// Byte offset of metadata (row, group) in a block whose rows are `mb` bytes,
+// stored plain or in the 128-byte swizzle (then mb == 128).
+__device__ __forceinline__ int moff(int row, int g, int mb, bool sw) {
+  const int b = 2 * g;
+  return sw ? row * 128 + ((((b >> 4) ^ row) & 7) << 4) + (b & 15) : row * mb + b;
+}
+
+// ---------------------------------------------------------------------------
+// Consumer warp arithmetic. A warp multiplies 16-row blocks (P: 8 rows, Q: 8
+// rows; lane (r = lane / 4, c = lane % 4) owns P row r and Q row r) by the
+// activation over chunk columns [cc0, cc0 + ncc); a chunk column is 32
+// reduction values, 16 bytes of every row. Word c of 16-byte unit u of a row
+// sits at  piece * PS + row * 128 + ((u ^ (row % 8)) << 4) + 4 c  (the TMA
+// 128-byte swizzle); P0 / Q0 are the byte offsets of P row 0 / Q row 0. The
+// quad lanes finish groups c of each batch of 4 groups.
+// ---------------------------------------------------------------------------
+struct Meta {
+  const uint8_t *sP, *bP, *sQ, *bQ;
+  int rowP, rowQ, mb;
+  bool sw;
+};
+
+__device__ __forceinline__ void group_epilogue(const Meta& m, int ga, float xa, float eP, float eQ, float& accP,
+                                               float& accQ) {
+  const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m.sP + moff(m.rowP, ga, m.mb, m.sw)));
+  const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m.bP + moff(m.rowP, ga, m.mb, m.sw)));
+  const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(m.sQ + moff(m.rowQ, ga, m.mb, m.sw)));
+  const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(m.bQ + moff(m.rowQ, ga, m.mb, m.sw)));
+  const float xo = 128.0f * xa;
+  accP = fmaf(sP, eP - xo, fmaf(bP, xa, accP));
+  accQ = fmaf(sQ, eQ - xo, fmaf(bQ, xa, accQ));
+}
+
+__device__ __forceinline__ void mma_word_pair(float (&d)[4], uint32_t W0, uint32_t W8, const uint4& xv, bool first) {
+  uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
+  decode_word(W0, p0, p1, p2, p3);
+  decode_word(W8, q0, q1, q2, q3);
+  if (first)
+    mma_bf16_16816_zero(d, p0, q0, p1, q1, xv.x, xv.y);
+  else
+    mma_bf16_16816(d, p0, q0, p1, q1, xv.x, xv.y);
+  mma_bf16_16816(d, p2, q2, p3, q3, xv.z, xv.w);
+}
+
+// Activation held in registers (gate|up and qmv units): xr[i] is the chunk of
+// chunk column cc0 + i for this lane's c (i < ncc <= XR); NRB row blocks per
+// warp share each activation chunk.
+template <int CPG, int NRB>
+__device__ __forceinline__ void dot_xreg(const uint8_t* wbase, int PS, const int (&P0)[NRB], const int (&Q0)[NRB],
+                                         int cc0, int ncc, const uint4 (&xr)[XR], const float* gsum,
+                                         const Meta (&m)[NRB], float (&accP)[NRB], float (&accQ)[NRB]) {
+  constexpr int NGMAX = XR / CPG;
+  const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+  const int ng = ncc / CPG;
+  const int g0 = cc0 / CPG;
+  const uint8_t* wl = wbase + r * 128 + c * 4;
+#pragma unroll
+  for (int gb = 0; gb < NGMAX; gb += 4) {
+    if (gb < ng) {
+      float D[NRB][4][4];
+#pragma unroll
+      for (int gi = 0; gi < 4; ++gi) {
+        if (gb + gi < ng) {
+#pragma unroll
+          for (int j = 0; j < CPG; ++j) {
+            const int i = (gb + gi) * CPG + j;
+            const int cc = cc0 + i;
+            const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4);
+#pragma unroll
+            for (int b = 0; b < NRB; ++b) {
+              const uint32_t W0 = *reinterpret_cast<const uint32_t*>(wp + P0[b]);
+              const uint32_t W8 = *reinterpret_cast<const uint32_t*>(wp + Q0[b]);
+              mma_word_pair(D[b][gi], W0, W8, xr[i < XR ? i : 0], j == 0);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int b = 0; b < NRB; ++b) D[b][gi][0] = D[b][gi][1] = D[b][gi][2] = D[b][gi][3] = 0.0f;
+        }
+      }
+      const int gl = gb + c;
+      const float xa = gsum[gl < ng ? gl : 0];
+#pragma unroll
+      for (int b = 0; b < NRB; ++b) {
+        float eP = D[b][0][0], eQ = D[b][0][2];
+#pragma unroll
+        for (int gi = 1; gi < 4; ++gi) {
+          eP = (c == gi) ? D[b][gi][0] : eP;
+          eQ = (c == gi) ? D[b][gi][2] : eQ;
+        }
+        if (gl < ng) group_epilogue(m[b], g0 + gl, xa, eP, eQ, accP[b], accQ[b]);
+      }
+    }
+  }
+}
+
+// Activation chunks in shared memory (down units: the slot's activations are
+// part of the stage); gsum_lane: lane l < ng holds the sum over group l.
+template <int CPG>
+__device__ __forceinline__ void dot_xsmem(const uint8_t* wbase, int PS, int P0, int Q0, int cc0, int ncc,
+                                          const uint8_t* xch, float gsum_lane, const Meta& m, float& accP,
+                                          float& accQ) {
+  const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+  const int ng = ncc / CPG;
+  const int g0 = cc0 / CPG;
+  const uint8_t* wl = wbase + r * 128 + c * 4;
+  const uint8_t* xl = xch + c * 16;
+  for (int gb = 0; gb < ng; gb += 4) {
+    float D[4][4];
+#pragma unroll
+    for (int gi = 0; gi < 4; ++gi) {
+      if (gb + gi < ng) {
+#pragma unroll
+        for (int j = 0; j < CPG; ++j) {
+          const int cc = cc0 + (gb + gi) * CPG + j;
+          const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4);
+          const uint32_t W0 = *reinterpret_cast<const uint32_t*>(wp + P0);
+          const uint32_t W8 = *reinterpret_cast<const uint32_t*>(wp + Q0);
+          const uint4 xv = *reinterpret_cast<const uint4*>(xl + (size_t)cc * 64);
+          mma_word_pair(D[gi], W0, W8, xv, j == 0);
+        }
+      } else {
+        D[gi][0] = D[gi][1] = D[gi][2] = D[gi][3] = 0.0f;
+      }
+    }
+    float eP = D[0][0], eQ = D[0][2];
+#pragma unroll
+    for (int gi = 1; gi < 4; ++gi) {
+      eP = (c == gi) ? D[gi][0] : eP;
+      eQ = (c == gi) ? D[gi][2] : eQ;
+    }
+    const int gl = gb + c;
+    const float xa = __shfl_sync(0xffffffffu, gsum_lane, gl & 31);
+    if (gl < ng) group_epilogue(m, g0 + gl, xa, eP, eQ, accP, accQ);
+  }
+}
+
+// softmax over the k selected logits held by lanes 0..k-1 (slot order): max,
+// exp, per-lane partial sums of 4 then a butterfly, as the reference's softmax
+// over its k values (Runner/FastModel/TrackFastMoE.swift:846-880)
+__device__ void softmax_k(float selv, int k, float* sw) {
+  const int lane = threadIdx.x & 31;
+  float mx = (lane < k) ? selv : -INFINITY;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float ex = (lane < k) ? expf(selv - mx) : 0.0f;
+  float part = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float t = __shfl_sync(0xffffffffu, ex, (4 * lane + i) & 31);
+    part += (lane < 8) ? t : 0.0f;
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+  const float inv = 1.0f / part;
+  if (lane < k) sw[lane] = ex * inv;
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int CPG, int MODE>
+__global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr bool FUSED = MODE != D2_QMV;
+  constexpr bool EP = MODE == D2_FUSED_EP;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int NS = p.nstage;
+
+  uint8_t* misc = smem + p.off_misc;
+  uint64_t* full = reinterpret_cast<uint64_t*>(misc);
+  uint64_t* empty = full + MAXST;
+  int4* info = reinterpret_cast<int4*>(empty + MAXST);          // [MAXST] unit of each stage fill
+  unsigned* arr = reinterpret_cast<unsigned*>(info + MAXST);     // [MAXST] warps done with a unit
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(arr + MAXST);
+  int* nloc_sm = const_cast<int*>(abort_flag) + 1;
+  uint32_t* sidx = reinterpret_cast<uint32_t*>(nloc_sm + 3);     // [MAXK] selected experts, slot order
+  float* sw = reinterpret_cast<float*>(sidx + MAXK);             // [MAXK] their weights
+  int* lslot = reinterpret_cast<int*>(sw + MAXK);                // [MAXK] routed slots held here (EP)
+  float* rsum = reinterpret_cast<float*>(lslot + MAXK);          // [NCW + 1]
+  float* red = reinterpret_cast<float*>(smem + p.off_red);       // [nstage][NCW][32]
+  float* xsum = reinterpret_cast<float*>(smem + p.off_xs);
+  unsigned* done = p.ctr + 4;
+  unsigned* comb = p.ctr + D2_CTR_FIXED;
+
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NCW);
+      arr[i] = 0u;
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == NCW && lane == 0) {
+    for (int i = 0; i < (FUSED ? 9 : 3); ++i)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.map[i])) : "memory");
+    if (FUSED)
+      for (int e = blockIdx.x; e < p.E; e += gridDim.x) prefetch_l2(p.wr + (size_t)e * p.H, (uint32_t)p.H * 2u);
+    if (!FUSED) {
+      // the first units' weight rows go to L2 only: a prefetch reads nothing
+      // into the CTA, and the stage loads after the wait see whatever the
+      // previous kernel wrote (L2 is the point of coherence)
+      for (int i = 0; i < NS; ++i) {
+        const unsigned u = blockIdx.x + (unsigned)i * gridDim.x;
+        if (u >= (unsigned)(p.N / ROWS_QMV)) break;
+        asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                         reinterpret_cast<uint64_t>(&p.map[MW])),
+                     "r"(0), "r"((int)u * ROWS_QMV), "r"(0)
+                     : "memory");
+      }
+    }
+  }
+  // everything below may read what the previous kernel in the stream wrote
+  griddep_wait();
+  griddep_launch();
+  const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
+  unsigned nxt = 0u;  // producer lane 0: the next unit from the queue
+  if (FUSED && warp == NCW && lane == 0) nxt = atomicAdd(&p.ctr[1], 1u);
+  __syncthreads();
+
+  const int K1 = p.K1;
+  constexpr int CPC = CPG * 4;  // 8-value chunks per group
+  // ---- router rows of this CTA (fused) ----
+  if (FUSED) {
+    int rows = 0;
+    for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
+      float part = 0.0f;
+      const uint4* xr4 = reinterpret_cast<const uint4*>(p.x);
+      const uint4* wrow = reinterpret_cast<const uint4*>(p.wr + (size_t)e * p.H);
+      for (int v = tid; v < p.H / 8; v += NTH) {
+        const uint4 xv = __ldg(xr4 + v), wv = __ldg(wrow + v);
+        part += lbf(xv.x) * lbf(wv.x) + hbf(xv.x) * hbf(wv.x);
+        part += lbf(xv.y) * lbf(wv.y) + hbf(xv.y) * hbf(wv.y);
+        part += lbf(xv.z) * lbf(wv.z) + hbf(xv.z) * hbf(wv.z);
+        part += lbf(xv.w) * lbf(wv.w) + hbf(xv.w) * hbf(wv.w);
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+      if (lane == 0) rsum[warp] = part;
+      __syncthreads();
+      if (tid == 0) {
+        float lg = 0.0f;
+        for (int w = 0; w < NCW + 1; ++w) lg += rsum[w];
+        p.ws_logits[e] = lg;
+      }
+      __syncthreads();
+      ++rows;
+    }
+    if (tid == 0 && rows) {
+      __threadfence();
+      atomicAdd(&p.ctr[0], (unsigned)rows);
+    }
+  }
+  // ---- per-group sums of x ----
+  {
+    const int nch = K1 / 8;
+    for (int q0 = 0; q0 < nch; q0 += NTH) {
+      const int q = q0 + tid;
+      const bool live = q < nch;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (live) v = __ldg(reinterpret_cast<const uint4*>(p.x) + q);
+      float s = ((lbf(v.x) + hbf(v.x)) + (lbf(v.y) + hbf(v.y))) + ((lbf(v.z) + hbf(v.z)) + (lbf(v.w) + hbf(v.w)));
+#pragma unroll
+      for (int off = 1; off < CPC; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      if (live && (q % CPC) == 0) xsum[q / CPC] = s;
+    }
+  }
+  // ---- the consumer warp's activation chunks, pair-permuted, in registers ----
+  uint4 xr[XR];
+  const int ncc1 = K1 / 32 / NCW, cc01 = (warp < NCW ? warp : 0) * ncc1;
+  {
+    const int c = lane & 3;
+#pragma unroll
+    for (int i = 0; i < XR; ++i) {
+      xr[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (warp < NCW && i < ncc1) xr[i] = perm_x8(__ldg(reinterpret_cast<const uint4*>(p.x) + 4 * (cc01 + i) + c));
+    }
+  }
+  // ---- routing (fused): every CTA ranks the same logits ----
+  if (FUSED) {
+    if (tid == 0 && !wait_counter_geq(&p.ctr[0], (unsigned)p.E, deadline, abort_flag)) {
+      record_error(p.err, B2Q_ETIMEOUT);
+      *abort_flag = 1;
+    }
+    __syncthreads();
+    float* lgs = reinterpret_cast<float*>(smem);  // stage 0 is free until the producer starts
+    float* sval = lgs + p.E;
+    for (int e = tid; e < p.E; e += NTH) {
+      const float v = *abort_flag ? 0.0f : __ldcg(p.ws_logits + e);
+      lgs[e] = (v != v) ? -INFINITY : v;
+    }
+    __syncthreads();
+    // expert e takes slot rank(e) when rank(e) < k, rank(e) = #{j : v_j > v_e or
+    // (v_j == v_e and j < e)}: largest first, ties to the lower index
+    for (int e = tid; e < p.E; e += NTH) {
+      const float v = lgs[e];
+      int rank = 0;
+      for (int j = 0; j < p.E; ++j) {
+        const float vj = lgs[j];
+        rank += (vj > v || (vj == v && j < e)) ? 1 : 0;
+      }
+      if (rank < p.k) {
+        sidx[rank] = (uint32_t)e;
+        sval[rank] = v;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      softmax_k(lane < p.k ? sval[lane] : -INFINITY, p.k, sw);
+      __syncwarp();
+      if (blockIdx.x == 0 && lane < p.k) {
+        if (p.idx_out) p.idx_out[lane] = sidx[lane];
+        if (p.w_out) p.w_out[lane] = sw[lane];
+      }
+      if (blockIdx.x == 0 && p.logits_out)
+        for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
+      if (lane == 0) {
+        int n = 0;
+        for (int s = 0; s < p.k; ++s) {
+          const int e = (int)sidx[s];
+          if (!EP || (e >= p.e_lo && e < p.e_lo + p.e_local)) lslot[n++] = s;
+        }
+        *nloc_sm = n;
+      }
+    }
+  }
+  __syncthreads();
+
+  const int nloc = FUSED ? *nloc_sm : 0;
+  const int F = p.F, H = p.H;
+  const unsigned U1 = FUSED ? (unsigned)(nloc * (F / ROWS_GU)) : (unsigned)(p.N / ROWS_QMV);
+  const unsigned U2 = FUSED ? (unsigned)(nloc * (H / ROWS_DOWN)) : 0u;
+  const unsigned UT = U1 + U2;
+
+  if (warp == NCW) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const uint64_t pol_keep = policy_evict_last();
+      int lastf[MAXST];
+      for (int i = 0; i < MAXST; ++i) lastf[i] = -1;
+      for (int it = 0;; ++it) {
+        const int s = it % NS;
+        unsigned u;
+        if (FUSED) {
+          u = nxt;
+          if (u < UT) nxt = atomicAdd(&p.ctr[1], 1u);
+        } else {
+          u = blockIdx.x + (unsigned)it * gridDim.x;
+        }
+        if (it >= NS && !tc::wait(&empty[s], ((it / NS) - 1) & 1, deadline, abort_flag)) {
+          if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
+          *abort_flag = 1;
+        }
+        if (u >= UT || *abort_flag) {
+          info[s] = make_int4(U_END, 0, 0, 0);
+          mbar_arrive(&full[s]);
+          lastf[s] = it;
+          break;
+        }
+        uint8_t* st = smem + (size_t)s * p.stage_bytes;
+        if (!FUSED) {
+          const int row = (int)u * ROWS_QMV;
+          info[s] = make_int4(U_QMV, 0, (int)u, 0);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(ROWS_QMV * K1 / 2 + 2 * ROWS_QMV * p.mb1));
+          tma3(st, &p.map[MW], 0, row, 0, &full[s], pol);
+          tc::tma_load_2d(st + p.st_meta1, &p.map[MS], 0, row, &full[s], pol);
+          tc::tma_load_2d(st + p.st_meta1 + p.st_mstep1, &p.map[MB], 0, row, &full[s], pol);
+        } else if (u < U1) {
+          const int z = (int)u / (F / ROWS_GU), rb = (int)u % (F / ROWS_GU);
+          const uint32_t e = EP ? sidx[lslot[z]] - (uint32_t)p.e_lo : sidx[z];
+          const int row = (int)(e * (uint32_t)F) + rb * ROWS_GU;
+          info[s] = make_int4(U_GU, z, rb, 0);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * ROWS_GU * K1 / 2 + 4 * ROWS_GU * p.mb1));
+          tma3(st, &p.map[MWG], 0, row, 0, &full[s], pol);
+          tma3(st + ROWS_GU * K1 / 2, &p.map[MWU], 0, row, 0, &full[s], pol);
+          uint8_t* m = st + p.st_meta1;
+          tc::tma_load_2d(m, &p.map[MSG], 0, row, &full[s], pol);
+          tc::tma_load_2d(m + p.st_mstep1, &p.map[MBG], 0, row, &full[s], pol);
+          tc::tma_load_2d(m + 2 * p.st_mstep1, &p.map[MSU], 0, row, &full[s], pol);
+          tc::tma_load_2d(m + 3 * p.st_mstep1, &p.map[MBU], 0, row, &full[s], pol);
+        } else {
+          const unsigned v = u - U1;
+          const int z = (int)v / (H / ROWS_DOWN), hb = (int)v % (H / ROWS_DOWN);
+          const uint32_t e = EP ? sidx[lslot[z]] - (uint32_t)p.e_lo : sidx[z];
+          const int row = (int)(e * (uint32_t)H) + hb * ROWS_DOWN;
+          // the slot's activations must be final: every gate|up unit of it finished
+          if (!wait_counter_geq(&done[z], (unsigned)(F / ROWS_GU), deadline, abort_flag)) {
+            if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
+            *abort_flag = 1;
+            info[s] = make_int4(U_END, 0, 0, 0);
+            mbar_arrive(&full[s]);
+            lastf[s] = it;
+            break;
+          }
+          fence_proxy_async_global();  // the copies below read what generic stores wrote
+          info[s] = make_int4(U_DOWN, z, hb, 0);
+          mbar_arrive_expect_tx(&full[s],
+                                (uint32_t)(ROWS_DOWN * F / 2 + 2 * ROWS_DOWN * p.mb2 + F * 2 + F / 2));
+          tma3(st, &p.map[MWD], 0, row, 0, &full[s], pol);
+          tc::tma_load_2d(st + p.st_meta2, &p.map[MSD], 0, row, &full[s], pol);
+          tc::tma_load_2d(st + p.st_meta2 + p.st_mstep2, &p.map[MBD], 0, row, &full[s], pol);
+          bulk_g2s(st + p.st_act, p.ws_act + (size_t)z * F, (uint32_t)F * 2u, &full[s], pol_keep);
+          bulk_g2s(st + p.st_asum, p.ws_asum + (size_t)z * (F / 8), (uint32_t)F / 2u, &full[s], pol_keep);
+        }
+        lastf[s] = it;
+      }
+      // let every copy issued land before the CTA exits (after an abort some
+      // fills may never have been consumed): wait for the latest phase of
+      // every stage used, end markers included
+      const uint64_t dl = globaltimer() + 200000000ull;
+      for (int i = 0; i < NS; ++i)
+        if (lastf[i] >= 0) tc::wait_until(&full[i], (lastf[i] / NS) & 1, dl);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ consumers ------------------------------
+    const int r = lane >> 2, c = lane & 3;
+    for (int it = 0;; ++it) {
+      const int s = it % NS;
+      if (!__all_sync(0xffffffffu, tc::wait(&full[s], (it / NS) & 1, deadline, abort_flag))) {
+        if (!*abort_flag && lane == 0) record_error(p.err, B2Q_ETIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      const int4 inf = info[s];
+      if (inf.x == U_END) break;
+      const uint8_t* st = smem + (size_t)s * p.stage_bytes;
+      float* rp = red + ((size_t)s * NCW + warp) * 32;
+      if (FUSED && inf.x == U_DOWN) {
+        // 4 row blocks of 16 x 2 reduction halves
+        const int b = warp >> 1, qw = warp & 1;
+        const int ncc = F / 32 / 2, cc0 = qw * ncc, ng = ncc / CPG;
+        const float* as = reinterpret_cast<const float*>(st + p.st_asum);
+        float gl_sum = 0.0f;
+        if (lane < ng) {
+          const int q0 = (cc0 / CPG + lane) * CPC;
+#pragma unroll
+          for (int i = 0; i < CPC; ++i) gl_sum += as[q0 + i];
+        }
+        const Meta m{st + p.st_meta2, st + p.st_meta2 + p.st_mstep2, st + p.st_meta2,
+                     st + p.st_meta2 + p.st_mstep2, 16 * b + r, 16 * b + 8 + r, p.mb2, p.sw2 != 0};
+        float accP = 0.0f, accQ = 0.0f;
+        dot_xsmem<CPG>(st, ROWS_DOWN * 128, b * 2048, b * 2048 + 1024, cc0, ncc, st + p.st_act, gl_sum, m, accP,
+                       accQ);
+        accP += __shfl_xor_sync(0xffffffffu, accP, 1);
+        accQ += __shfl_xor_sync(0xffffffffu, accQ, 1);
+        accP += __shfl_xor_sync(0xffffffffu, accP, 2);
+        accQ += __shfl_xor_sync(0xffffffffu, accQ, 2);
+        if (c == 0) {
+          rp[r] = accP;
+          rp[r + 8] = accQ;
+        }
+      } else if (FUSED) {
+        // gate|up: both row blocks of the 16 outputs, the warp's eighth of the reduction
+        const uint8_t* mb = st + p.st_meta1;
+        const Meta m[2] = {
+            {mb, mb + p.st_mstep1, mb + 2 * p.st_mstep1, mb + 3 * p.st_mstep1, r, r, p.mb1, p.sw1 != 0},
+            {mb, mb + p.st_mstep1, mb + 2 * p.st_mstep1, mb + 3 * p.st_mstep1, 8 + r, 8 + r, p.mb1, p.sw1 != 0}};
+        const int ub = ROWS_GU * K1 / 2;  // the up rows' box
+        const int P0[2] = {0, 1024}, Q0[2] = {ub, ub + 1024};
+        float accP[2] = {0.0f, 0.0f}, accQ[2] = {0.0f, 0.0f};
+        dot_xreg<CPG, 2>(st, ROWS_GU * 128, P0, Q0, cc01, ncc1, xr, xsum + cc01 / CPG, m, accP, accQ);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 1);
+          accQ[b] += __shfl_xor_sync(0xffffffffu, accQ[b], 1);
+          accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 2);
+          accQ[b] += __shfl_xor_sync(0xffffffffu, accQ[b], 2);
+          if (c == 0) {
+            rp[16 * b + r] = accP[b];
+            rp[16 * b + 8 + r] = accQ[b];
+          }
+        }
+      } else {
+        const uint8_t* mb = st + p.st_meta1;
+        const Meta m[1] = {{mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, r, 8 + r, p.mb1, p.sw1 != 0}};
+        const int P0[1] = {0}, Q0[1] = {1024};
+        float accP[1] = {0.0f}, accQ[1] = {0.0f};
+        dot_xreg<CPG, 1>(st, ROWS_QMV * 128, P0, Q0, cc01, ncc1, xr, xsum + cc01 / CPG, m, accP, accQ);
+        accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 1);
+        accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 1);
+        accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 2);
+        accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 2);
+        if (c == 0) {
+          rp[r] = accP[0];
+          rp[r + 8] = accQ[0];
+        }
+      }
+      __syncwarp();
+      unsigned old = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        old = atomicAdd(&arr[s], 1u);
+      }
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == NCW - 1) {
+        // the last warp of the unit finishes it
+        __threadfence_block();
+        const float* rb = red + (size_t)s * NCW * 32;
+        if (FUSED && inf.x == U_GU) {
+          // lane l: total of row l of the warp partials ([gate 0..7][up 0..7][gate 8..15][up 8..15])
+          const int z = inf.y, blk = inf.z;
+          float tot = 0.0f;
+          for (int w = 0; w < NCW; ++w) tot += rb[w * 32 + lane];
+          const int f = lane & 15;  // output of lanes 0..15
+          const float g = __shfl_sync(0xffffffffu, tot, 16 * (f >> 3) + (f & 7));
+          const float up = __shfl_sync(0xffffffffu, tot, 16 * (f >> 3) + 8 + (f & 7));
+          uint16_t a = 0;
+          if (lane < 16) {
+            a = swiglu_bf16(f2bf(g), f2bf(up));
+            const int j = f & 7, pos = j < 4 ? 2 * j : 2 * (j - 4) + 1;
+            p.ws_act[(size_t)z * F + blk * ROWS_GU + (f >> 3) * 8 + pos] = a;
+          }
+          float af = lane < 16 ? bf2f(a) : 0.0f;
+          af += __shfl_xor_sync(0xffffffffu, af, 1);
+          af += __shfl_xor_sync(0xffffffffu, af, 2);
+          af += __shfl_xor_sync(0xffffffffu, af, 4);
+          if (lane == 0 || lane == 8) p.ws_asum[(size_t)z * (F / 8) + blk * 2 + (lane >> 3)] = af;
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) red_release_add_u32(&done[z], 1u);
+        } else if (FUSED) {
+          const int z = inf.y, hb = inf.z;
+          // rows lane and lane + 32 of the unit: row i is block i / 16, partial row i % 16
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int i = lane + 32 * h2, b = i >> 4, j = i & 15;
+            const float y2 = rb[(2 * b) * 32 + j] + rb[(2 * b + 1) * 32 + j];
+            p.ws_y[(size_t)z * H + hb * ROWS_DOWN + i] = f2bf(y2);
+          }
+          __threadfence();
+          __syncwarp();
+          unsigned prev = 0;
+          if (lane == 0) prev = atomicAdd(&comb[hb], 1u);
+          prev = __shfl_sync(0xffffffffu, prev, 0);
+          if (prev == (unsigned)(nloc - 1)) {
+            // every slot's rows of this block are in: y_j = bf16 product,
+            // prod_j = y_j * w_j, folded in the mlx_colsum_small_f32 order
+            __threadfence();
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int h = hb * ROWS_DOWN + lane + 32 * h2;
+              float prod[MAXK];
+#pragma unroll
+              for (int s2 = 0; s2 < MAXK; ++s2)
+                prod[s2] = s2 < nloc ? bf2f(__ldcg(p.ws_y + (size_t)s2 * H + h)) * sw[EP ? lslot[s2] : s2] : 0.0f;
+              const int TY = nloc < 8 ? nloc : 8;
+              float total = 0.0f;
+#pragma unroll
+              for (int q = 0; q < MAXK; ++q) {
+                if (q < TY) {
+                  float a2 = 0.0f;
+                  for (int s2 = q; s2 < nloc; s2 += TY) a2 = prod[s2] + a2;
+                  total = (q == 0) ? a2 : a2 + total;
+                }
+              }
+              if (EP)
+                p.out_f32[h] = total;
+              else
+                p.out[h] = f2bf(total);
+            }
+            if (lane == 0) comb[hb] = 0u;
+          }
+        } else {
+          if (lane < 16) {
+            float tot = 0.0f;
+            for (int w = 0; w < NCW; ++w) tot += rb[w * 32 + lane];
+            p.y[(size_t)inf.z * ROWS_QMV + lane] = f2bf(tot);
+          }
+        }
+        if (lane == 0) arr[s] = 0u;
+        __syncwarp();
+      }
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+
+  // expert parallel with no routed slot here: the partial is zero
+  if (EP && nloc == 0)
+    for (int h = blockIdx.x * NTH + tid; h < H; h += gridDim.x * NTH) p.out_f32[h] = 0.0f;
+
+  // ---- exit: the last CTA out re-arms the grid counters for the next call ----
+  __syncthreads();
+  if (FUSED && tid == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(&p.ctr[2], 1u);
+    if (prev == gridDim.x - 1) {
+      p.ctr[0] = 0u;
+      p.ctr[1] = 0u;
+      p.ctr[2] = 0u;
+      for (int i = 0; i < MAXK; ++i) done[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace d2
+}  // namespace b2q
+
+namespace b2q {
+namespace d2 {
+
+static int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+static int plan(D2Params& p, int mode) {
+  const int K1 = p.K1;
+  p.mb1 = K1 / p.gs * 2;
+  p.sw1 = p.mb1 == 128;
+  int st;
+  if (mode == D2_QMV) {
+    p.st_meta1 = ROWS_QMV * K1 / 2;
+    p.st_mstep1 = round_up(ROWS_QMV * p.mb1, p.sw1 ? 1024 : 128);
+    st = p.st_meta1 + 2 * p.st_mstep1;
+    p.mb2 = p.sw2 = p.st_meta2 = p.st_mstep2 = p.st_act = p.st_asum = 0;
+  } else {
+    p.st_meta1 = 2 * ROWS_GU * K1 / 2;
+    p.st_mstep1 = round_up(ROWS_GU * p.mb1, p.sw1 ? 1024 : 128);
+    const int gu = p.st_meta1 + 4 * p.st_mstep1;
+    p.mb2 = p.F / p.gs * 2;
+    p.sw2 = p.mb2 == 128;
+    p.st_meta2 = ROWS_DOWN * p.F / 2;
+    p.st_mstep2 = round_up(ROWS_DOWN * p.mb2, p.sw2 ? 1024 : 128);
+    p.st_act = p.st_meta2 + 2 * p.st_mstep2;
+    p.st_asum = p.st_act + p.F * 2;
+    const int dn = p.st_asum + p.F / 2;
+    st = std::max(gu, dn);
+  }
+  p.stage_bytes = round_up(st, 1024);
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  // stages first (1024-aligned), then the group sums of x, the warp partials
+  // of every stage and the barriers / routing state
+  const int xs_bytes = round_up(K1 / p.gs * 4, 128);
+  int ns = MAXST;
+  for (; ns >= 2; --ns) {
+    const int total = ns * p.stage_bytes + xs_bytes + ns * NCW * 32 * 4 + MISC_BYTES + 1024;
+    if (total <= di.smem_optin) break;
+  }
+  if (ns < 2) return set_error(B2Q_EUNSUPPORTED, "decode kernel: stages of %d bytes do not fit", p.stage_bytes);
+  p.nstage = ns;
+  int off = ns * p.stage_bytes;
+  p.off_xs = off;
+  off += xs_bytes;
+  p.off_red = off;
+  off += ns * NCW * 32 * 4;
+  p.off_misc = off;
+  off += MISC_BYTES;
+  p.smem_bytes = off + 1024;
+  return B2Q_OK;
+}
+
+template <int CPG, int MODE>
+static int launch_t(const D2Params& p, cudaStream_t st, int grid) {
+  static bool attr_done[64] = {};
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (!attr_done[di.device & 63]) {
+    B2Q_TRY_CUDA(cudaFuncSetAttribute(d2_kernel<CPG, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      di.smem_optin));
+    attr_done[di.device & 63] = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NTH);
+  cfg.dynamicSmemBytes = p.smem_bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2Q_TRY_CUDA(cudaLaunchKernelEx(&cfg, d2_kernel<CPG, MODE>, p));
+  return B2Q_OK;
+}
+
+static int launch(const D2Params& p, int mode, cudaStream_t st) {
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int grid = di.sm_count;
+  const int cpg = p.gs / 32;
+  switch (cpg * 4 + mode) {
+    case 1 * 4 + D2_QMV: return launch_t<1, D2_QMV>(p, st, grid);
+    case 2 * 4 + D2_QMV: return launch_t<2, D2_QMV>(p, st, grid);
+    case 4 * 4 + D2_QMV: return launch_t<4, D2_QMV>(p, st, grid);
+    case 1 * 4 + D2_FUSED: return launch_t<1, D2_FUSED>(p, st, grid);
+    case 2 * 4 + D2_FUSED: return launch_t<2, D2_FUSED>(p, st, grid);
+    case 4 * 4 + D2_FUSED: return launch_t<4, D2_FUSED>(p, st, grid);
+    case 1 * 4 + D2_FUSED_EP: return launch_t<1, D2_FUSED_EP>(p, st, grid);
+    case 2 * 4 + D2_FUSED_EP: return launch_t<2, D2_FUSED_EP>(p, st, grid);
+    case 4 * 4 + D2_FUSED_EP: return launch_t<4, D2_FUSED_EP>(p, st, grid);
+    default: return set_error(B2Q_EUNSUPPORTED, "decode kernel: group size %d", p.gs);
+  }
+}
+
+// Tensor maps of recently used weight sets. Encoding the (up to nine) maps of
+// a call costs microseconds of host time, while a model calls the same layers
+// over and over; maps depend only on addresses, shapes and boxes, so an entry
+// keyed by those stays valid whatever the buffers hold. Least recently used
+// entries are replaced.
+struct MapKey {
+  const void* ptr[9];
+  int device, mode, a, b, c, gs;
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map[9];
+  uint64_t stamp;
+};
+constexpr int MAP_CACHE = 128;
+static std::mutex g_map_mu;
+static MapEntry g_maps[MAP_CACHE];
+static uint64_t g_map_clock = 0;
+
+static MapKey map_key(int mode, const void* const* ptrs, int n, int a, int b, int c, int gs) {
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));  // padding included: keys compare bytewise
+  for (int i = 0; i < n; ++i) k.ptr[i] = ptrs[i];
+  cudaGetDevice(&k.device);
+  k.mode = mode;
+  k.a = a;
+  k.b = b;
+  k.c = c;
+  k.gs = gs;
+  return k;
+}
+static bool find_maps(const MapKey& k, CUtensorMap* out, int n) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  for (MapEntry& e : g_maps) {
+    if (e.stamp && std::memcmp(&e.key, &k, sizeof(k)) == 0) {
+      std::memcpy(out, e.map, sizeof(CUtensorMap) * n);
+      e.stamp = ++g_map_clock;
+      return true;
+    }
+  }
+  return false;
+}
+static void put_maps(const MapKey& k, const CUtensorMap* m, int n) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  MapEntry* victim = &g_maps[0];
+  for (MapEntry& e : g_maps)
+    if (e.stamp < victim->stamp) victim = &e;
+  victim->key = k;
+  std::memcpy(victim->map, m, sizeof(CUtensorMap) * n);
+  victim->stamp = ++g_map_clock;
+}
+
+// weights: 3-D swizzled map, box of `box_rows` rows x the whole row;
+// scales / biases: 2-D map, box of `box_rows` rows x the whole metadata row
+static int set_family(D2Params& p, int mw, int ms, int mb, const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                      uint64_t rows, int K, int box_rows) {
+  int rc = make_row_tile_map(&p.map[mw], w, rows, (uint64_t)K / 2, (uint32_t)box_rows);
+  if (rc) return rc;
+  const int mrow = K / p.gs * 2;
+  const int swz = mrow == 128 ? 128 : 0;
+  rc = make_2d_map(&p.map[ms], s, rows, (uint64_t)mrow, (uint32_t)mrow, (uint32_t)box_rows, swz);
+  if (rc) return rc;
+  return make_2d_map(&p.map[mb], b, rows, (uint64_t)mrow, (uint32_t)mrow, (uint32_t)box_rows, swz);
+}
+
+static bool gs_ok(int gs) { return gs == 32 || gs == 64 || gs == 128; }
+
+}  // namespace d2
+
+using namespace d2;
+
+bool d2_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const void* s, const void* b) {
+  return gs_ok(gs) && N > 0 && N % ROWS_QMV == 0 && K > 0 && K % (8 * gs) == 0 && K % 256 == 0 &&
+         K / 256 <= XR && aligned16(x) && aligned16(w) && aligned16(s) && aligned16(b);
+}
+
+int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b, uint16_t* y, int N, int K,
+           int gs, cudaStream_t st) {
+  D2Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.gs = gs;
+  p.K1 = K;
+  p.N = N;
+  p.x = x;
+  p.y = y;
+  p.timeout_ns = 2000000000ll;
+  int rc = plan(p, D2_QMV);
+  if (rc) return rc;
+  const void* ptrs[3] = {w, s, b};
+  const MapKey key = map_key(D2_QMV, ptrs, 3, N, K, 0, gs);
+  if (!find_maps(key, p.map, 3)) {
+    rc = set_family(p, MW, MS, MB, w, s, b, (uint64_t)N, K, ROWS_QMV);
+    if (rc) return rc;
+    put_maps(key, p.map, 3);
+  }
+  return launch(p, D2_QMV, st);
+}
+
+bool d2_moe_eligible(int H, int E, int F, int k, int gs) {
+  if (!(gs_ok(gs) && H > 0 && F > 0 && H % (8 * gs) == 0 && H % 256 == 0 && H / 256 <= XR &&
+        F % (8 * gs) == 0 && F % 256 == 0 && F % ROWS_GU == 0 && H % ROWS_DOWN == 0 && F / gs * 2 <= 512 &&
+        k >= 1 && k <= MAXK && E >= k && E <= 1024 && d2_counter_words(H) * 4 <= 2048))
+    return false;
+  D2Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.gs = gs;
+  p.K1 = H;
+  p.H = H;
+  p.F = F;
+  const bool fits = plan(p, D2_FUSED) == B2Q_OK;
+  clear_error();
+  return fits;
+}
+
+int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                  const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
+                  const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
+                  int k, int gs, const D2Scratch& scr, cudaStream_t st, int e_lo, int e_local, float* out_f32) {
+  D2Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.gs = gs;
+  p.K1 = H;
+  p.x = x;
+  p.wr = wr;
+  p.out = out;
+  p.idx_out = idx;
+  p.w_out = w;
+  p.logits_out = logits;
+  p.H = H;
+  p.E = E;
+  p.F = F;
+  p.k = k;
+  p.err = scr.err;
+  p.ctr = scr.ctr;
+  p.ws_logits = scr.logits;
+  p.ws_act = scr.act;
+  p.ws_asum = scr.asum;
+  p.ws_y = scr.y;
+  p.e_lo = e_lo;
+  p.e_local = e_local;
+  p.out_f32 = out_f32;
+  p.timeout_ns = 2000000000ll;
+  const int mode = out_f32 ? D2_FUSED_EP : D2_FUSED;
+  int rc = plan(p, mode);
+  if (rc) return rc;
+  const void* ptrs[9] = {wg, sg, bg, wu, su, bu, wd, sd, bd};
+  const int Eh = e_local > 0 ? e_local : E;  // experts in the stacks this call reads
+  const MapKey key = map_key(D2_FUSED, ptrs, 9, H, Eh, F, gs);
+  if (!find_maps(key, p.map, 9)) {
+    const uint64_t rgu = (uint64_t)Eh * F, rd = (uint64_t)Eh * H;
+    rc = set_family(p, MWG, MSG, MBG, wg, sg, bg, rgu, H, ROWS_GU);
+    if (rc) return rc;
+    rc = set_family(p, MWU, MSU, MBU, wu, su, bu, rgu, H, ROWS_GU);
+    if (rc) return rc;
+    rc = set_family(p, MWD, MSD, MBD, wd, sd, bd, rd, F, ROWS_DOWN);
+    if (rc) return rc;
+    put_maps(key, p.map, 9);
+  }
+  return launch(p, mode, st);
+}
+
+}  // namespace b2q

@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <cstring>
 
+#include "decode2.cuh"
 #include "engine.cuh"
 #include "host.hpp"
 
@@ -36,19 +37,30 @@ static inline bool engine_k_ok(int K, int gs) { return K > 0 && K % (8 * gs) == 
 
 struct DecodeWs {
   WsHeader* hdr;
+  unsigned* ctr;  // one-token fused kernel: grid counters (d2_counter_words(H))
   float* logits;
   uint32_t* idx;
   float* w;
   uint16_t* act;
+  float* asum;    // one-token fused kernel: chunk sums of the activations [k][F / 8]
+  uint16_t* y;    // one-token fused kernel: per-slot down products [k][H]
   size_t bytes;
 };
 
-static inline DecodeWs decode_ws_layout(void* base, int S, int E, int F, int k) {
+// The one-token fused kernel's grid counters sit at a fixed offset right after
+// the header, whatever the shapes: a workspace reused for another shape keeps
+// them where the last call left them (zero).
+constexpr size_t D2_CTR_BYTES = 2048;
+static_assert(D2_CTR_FIXED * 4 < (int)D2_CTR_BYTES, "counter block");
+
+static inline DecodeWs decode_ws_layout(void* base, int S, int H, int E, int F, int k) {
   DecodeWs d{};
   size_t off = 0;
   char* b = static_cast<char*>(base);
   d.hdr = reinterpret_cast<WsHeader*>(b + off);
   off += sizeof(WsHeader);
+  d.ctr = reinterpret_cast<unsigned*>(b + off);
+  off += D2_CTR_BYTES;
   d.logits = reinterpret_cast<float*>(b + off);
   off = align256(off + sizeof(float) * (size_t)S * E);
   d.idx = reinterpret_cast<uint32_t*>(b + off);
@@ -57,6 +69,10 @@ static inline DecodeWs decode_ws_layout(void* base, int S, int E, int F, int k) 
   off = align256(off + sizeof(float) * (size_t)S * k);
   d.act = reinterpret_cast<uint16_t*>(b + off);
   off = align256(off + sizeof(uint16_t) * (size_t)S * k * F);
+  d.asum = reinterpret_cast<float*>(b + off);
+  off = align256(off + sizeof(float) * (size_t)k * (F / 8));
+  d.y = reinterpret_cast<uint16_t*>(b + off);
+  off = align256(off + sizeof(uint16_t) * (size_t)k * H);
   d.bytes = off;
   return d;
 }

@@ -31,6 +31,7 @@
 
 #include "common.cuh"
 #include "decode1.cuh"
+#include "decode2.cuh"
 #include "decode_ws.hpp"
 #include "engine.cuh"
 #include "ep.cuh"
@@ -81,6 +82,8 @@ struct EpDecodeWs {
   uint32_t* rhs;  // local expert of each slot, 0xFFFFFFFF when not held here
   uint32_t* tok;  // token of each slot
   uint16_t *g, *u, *act, *y;
+  float* asum;    // one-token fused kernel: activation chunk sums
+  unsigned* ctr;  // one-token fused kernel: grid counters (fixed offset)
   size_t bytes;
 };
 
@@ -91,6 +94,8 @@ EpDecodeWs ep_decode_layout(void* base, int S, int H, int E, int F, int k) {
   size_t off = 0;
   d.err = reinterpret_cast<int*>(b);
   off = 256;
+  d.ctr = reinterpret_cast<unsigned*>(b + off);  // fixed offset, as in decode_ws_layout
+  off += D2_CTR_BYTES;
   d.logits = reinterpret_cast<float*>(b + off);
   off = a256(off + 4 * (size_t)S * E);
   d.idx = reinterpret_cast<uint32_t*>(b + off);
@@ -109,6 +114,8 @@ EpDecodeWs ep_decode_layout(void* base, int S, int H, int E, int F, int k) {
   off = a256(off + 2 * R * F);
   d.y = reinterpret_cast<uint16_t*>(b + off);
   off = a256(off + 2 * R * H);
+  d.asum = reinterpret_cast<float*>(b + off);
+  off = a256(off + 4 * R * (F / 8));
   d.bytes = off;
   return d;
 }
@@ -333,7 +340,14 @@ int b2q_ep_moe_decode(void* comm, const uint16_t* x, const uint16_t* wr, const u
     const void* ptrs[] = {x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, partial};
     bool all_aligned = true;
     for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
-    if (all_aligned && d1_moe_eligible(H, E, F, k, group_size)) {
+    if (all_aligned && !decode_v1() && d2_moe_eligible(H, E, F, k, group_size)) {
+      const D2Scratch scr{ws.err, ws.ctr, ws.logits, ws.act, ws.asum, ws.y};
+      rc = d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, nullptr, idx, w, nullptr, H, E, F, k, group_size,
+                         scr, st, e_lo, e_local, partial);
+      if (rc) return rc;
+      return ep_finish(static_cast<EpComm*>(comm), partial, out, (size_t)S * H, st);
+    }
+    if (all_aligned && decode_v1() && d1_moe_eligible(H, E, F, k, group_size)) {
       WsHeader* hdr = static_cast<WsHeader*>(workspace);
       rc = d1_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, nullptr, idx, w, nullptr, H, E, F, k, group_size,
                          &hdr->error, hdr->counters, hdr->sched, ws.logits, ws.act, st, e_lo, e_local, partial);

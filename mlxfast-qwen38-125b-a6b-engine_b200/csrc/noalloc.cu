@@ -78,7 +78,7 @@ extern "C" int b2q_moe_decode_noalloc(const uint16_t* x, const uint16_t* wr, con
       !engine_k_ok(F, group_size))
     return set_error(B2Q_EUNSUPPORTED,
                      "moe_decode_noalloc: shape outside the kernel (k<=8, E<=1024, H,F multiples of 8*group_size)");
-  const size_t need = decode_ws_layout(nullptr, 1, E, F, k).bytes;
+  const size_t need = decode_ws_layout(nullptr, 1, H, E, F, k).bytes;
   if (need > (size_t)B2Q_NOALLOC_SCRATCH_BYTES)
     return set_error(B2Q_EINVAL,
                      "moe_decode_noalloc: E=%d, k=%d, F=%d need %zu bytes of scratch, above the fixed %d "
@@ -89,7 +89,7 @@ extern "C" int b2q_moe_decode_noalloc(const uint16_t* x, const uint16_t* wr, con
   void* scratch = nullptr;
   rc = scratch_on_current_device(&scratch);
   if (rc) return rc;
-  const DecodeWs ws = decode_ws_layout(scratch, 1, E, F, k);
+  const DecodeWs ws = decode_ws_layout(scratch, 1, H, E, F, k);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // what must start at zero: the error word and the grid counters
   B2Q_TRY_CUDA(cudaMemsetAsync(ws.hdr, 0, sizeof(WsHeader), st));

@@ -56,6 +56,26 @@ int make_row_block_map(CUtensorMap* map, const void* base, uint64_t rows, uint64
   return B2Q_OK;
 }
 
+int make_row_tile_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(B2Q_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (row_bytes % 128 || row_bytes / 128 > 256 || box_rows < 1 || box_rows > 256 || rows < box_rows ||
+      (reinterpret_cast<uintptr_t>(base) & 15))
+    return set_error(B2Q_EINVAL, "tensor map: rows of %llu bytes in boxes of %u rows not encodable",
+                     (unsigned long long)row_bytes, box_rows);
+  cuuint64_t dims[3] = {64, rows, row_bytes / 128};
+  cuuint64_t strides[2] = {row_bytes, 128};
+  cuuint32_t box[3] = {64, box_rows, (cuuint32_t)(row_bytes / 128)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(B2Q_ECUDA, "cuTensorMapEncodeTiled failed (%d) for rows=%llu row_bytes=%llu box_rows=%u", (int)r,
+                     (unsigned long long)rows, (unsigned long long)row_bytes, box_rows);
+  return B2Q_OK;
+}
+
 int make_2d_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_bytes,
                 uint32_t box_rows, int swizzle_bytes) {
   auto fn = encode_fn();

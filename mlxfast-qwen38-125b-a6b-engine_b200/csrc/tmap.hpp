@@ -26,6 +26,11 @@ namespace b2q {
 int make_row_block_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_bytes,
                        bool swizzled);
 
+// Same 3-D swizzled form with a box of `box_rows` rows x the whole row
+// (row_bytes / 128 pieces): one copy brings every reduction value of a block
+// of rows, landing as [piece][box_rows][128 bytes].
+int make_row_tile_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows);
+
 // Plain 2-D map over a row-major matrix of 16-bit elements: box of
 // `box_bytes` per row x `box_rows` rows, swizzle 0, 32, 64 or 128 bytes.
 int make_2d_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_bytes,
