@@ -6,8 +6,10 @@ path never does.
 
 * ``Oracle``   -- liboracle.so, the C restatement in b2q_oracle.c.
 * ``MlxRef``   -- _ref/libmlxref.so, the reference's own MLX CPU quantized
-                 kernels (backend/cpu/quantized.cpp:155-419, :1158-1236)
-                 compiled from the reference tree.
+                 kernels (backend/cpu/quantized.cpp:155-419, :701-747,
+                 :1158-1236) compiled from the reference tree: the bf16 kernel,
+                 the same kernel over fp32 operands (fp32 accumulation) and the
+                 gather loop over index pairs.
 
 bf16 arrays are numpy ``uint16`` bit patterns; packed weights are ``uint32``.
 """
@@ -245,6 +247,11 @@ class MlxRef:
         self.L = L
         L.mlxref_qmm_bf16.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I]
         L.mlxref_quantize_bf16.argtypes = [_P, _P, _P, _P, _I, _I, ctypes.c_longlong]
+        self.has_f32 = hasattr(L, "mlxref_qmm_f32")
+        if self.has_f32:
+            L.mlxref_qmm_f32.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I]
+            for fn in (L.mlxref_gather_qmm_bf16, L.mlxref_gather_qmm_f32):
+                fn.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I]
 
     @staticmethod
     def available(path: str = REF_SO) -> bool:
@@ -259,6 +266,46 @@ class MlxRef:
         rc = self.L.mlxref_qmm_bf16(_ptr(y), _ptr(x), _ptr(w), _ptr(s), _ptr(b), M, N, K, group_size, bits, 1)
         if rc:
             raise ValueError("mlx reference qmm failed")
+        return y
+
+    def qmm_f32(self, x, w, s, b, group_size=64, bits=4):
+        """The reference kernel over fp32 operands (fp32 products and running sum):
+        x, s, b are bf16 bit patterns, widened exactly to fp32; returns fp32 [M, N]."""
+        xf, sf, bf = (_c(bf16_to_f32(a), np.float32) for a in (x, s, b))
+        w = _c(w, np.uint32)
+        K = xf.shape[-1]
+        M = xf.size // K
+        N = w.shape[-2]
+        y = np.zeros((M, N), np.float32)
+        rc = self.L.mlxref_qmm_f32(_ptr(y), _ptr(xf), _ptr(w), _ptr(sf), _ptr(bf), M, N, K, group_size, bits, 1)
+        if rc:
+            raise ValueError("mlx reference qmm (fp32) failed")
+        return y
+
+    def gather_qmm(self, x, w, s, b, lhs, rhs, group_size=64, bits=4, fp32=True):
+        """gather_qmm as the reference's CPU loop: y[i] = x[lhs[i]] . dequant(w[rhs[i]])^T.
+        x [n_x, M, K], w [n_w, N, K/8], s/b [n_w, N, K/gs]; lhs/rhs uint32 [pairs] or None
+        (identity modulo n_x / n_w). fp32=True widens x, s, b exactly and returns fp32
+        [pairs, M, N]; otherwise the bf16 kernel's bf16 bits."""
+        w = _c(w, np.uint32)
+        n_w, N = w.shape[0], w.shape[1]
+        x = np.asarray(x)
+        n_x, M, K = x.shape
+        lhs_a = None if lhs is None else _c(lhs, np.uint32)
+        rhs_a = None if rhs is None else _c(rhs, np.uint32)
+        pairs = len(lhs_a) if lhs_a is not None else len(rhs_a)
+        if fp32:
+            xf, sf, bf = (_c(bf16_to_f32(a), np.float32) for a in (x, s, b))
+            y = np.zeros((pairs, M, N), np.float32)
+            fn = self.L.mlxref_gather_qmm_f32
+        else:
+            xf, sf, bf = _c(x, np.uint16), _c(s, np.uint16), _c(b, np.uint16)
+            y = np.zeros((pairs, M, N), np.uint16)
+            fn = self.L.mlxref_gather_qmm_bf16
+        rc = fn(_ptr(y), _ptr(xf), _ptr(w), _ptr(sf), _ptr(bf), _ptr(lhs_a), _ptr(rhs_a), pairs, M, N, K, n_x, n_w,
+                group_size, bits)
+        if rc:
+            raise ValueError(f"mlx reference gather_qmm failed ({rc})")
         return y
 
     def quantize(self, w_bf16, group_size=64, bits=4):

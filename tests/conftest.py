@@ -64,3 +64,31 @@ def cuda():
         pytest.fail("gpu test selected but no CUDA device is visible")
     torch.cuda.init()
     return torch.device("cuda:0")
+
+
+def moe_layer_reference_products(ref, orc, x, idx, wts, layer, k, group_size=64):
+    """One MoE layer whose every product is the reference's own MLX CPU kernel
+    over fp32 operands (fp32 products and running sum, backend/cpu/quantized.cpp:155,
+    :341), composed the way the Runner's decode operators compose them: gate and
+    up rounded to bf16, SwiGLU with the Runner's bf16 rounding points
+    (TrackFastKernels2.swift:22-31), the down product rounded to bf16, times the
+    routing weight, folded in the mlx_colsum_small_f32 order
+    (TrackFastKernels2.swift:36-47), rounded to bf16. x bf16 bits [T, H];
+    idx / wts [T, k]; returns bf16 bits [T, H]."""
+    from oracle.oracle import bf16_to_f32, f32_to_bf16
+
+    T = x.shape[0]
+    H = x.shape[1]
+    out = np.zeros((T, H), np.uint16)
+    for t in range(T):
+        prods = []
+        for j in range(k):
+            e = int(idx[t, j])
+            g = ref.qmm_f32(x[t:t + 1], layer["wg"][e], layer["sg"][e], layer["bg"][e], group_size)
+            u = ref.qmm_f32(x[t:t + 1], layer["wu"][e], layer["su"][e], layer["bu"][e], group_size)
+            act = orc.swiglu(f32_to_bf16(g), f32_to_bf16(u)).reshape(1, -1)
+            y = ref.qmm_f32(act, layer["wd"][e], layer["sd"][e], layer["bd"][e], group_size)
+            prods.append(bf16_to_f32(f32_to_bf16(y[0])) * np.float32(wts[t, j]))
+        P = np.stack(prods).astype(np.float32)  # [k, H]
+        out[t] = f32_to_bf16(np.array([orc.colsum_small(P[:, h]) for h in range(H)], np.float32))
+    return out
