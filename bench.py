@@ -165,6 +165,24 @@ def decode_rows_per_token():
     return TOPK * (2 * F + H * F // H)
 
 
+def prefill_rows_per_assignment():
+    # gate + up: 2 x 1536 rows of K = 4096; down: 4096 rows of K = 1536 = 1536 rows of K = 4096 equivalent
+    return 2 * F + H * F // H
+
+
+def prefill_cpu_baseline(t_row, kind):
+    """Config 2 on one core, extrapolated from the measured row cost of the reference
+    kernel: the reference's CPU gather runs one qmm call per (token, expert) pair
+    (backend/cpu/quantized.cpp:701-747), so a prefill layer is 2048 x 8 assignments
+    of 4608 K=4096 row-equivalents plus the router (128 rows per token)."""
+    rows = PREFILL_T * TOPK * prefill_rows_per_assignment() + PREFILL_T * E
+    sec = rows * t_row
+    return {"value": PREFILL_T / sec, "unit": "tok/s", "cores": 1, "kind": kind,
+            "sample": (f"extrapolated: measured per-row time of the reference's MLX CPU kernel (K=4096 4-bit g64, "
+                       f"bf16 sum) x {rows} row-equivalents per 2048-token layer (16384 assignments x "
+                       f"{prefill_rows_per_assignment()} + router); SwiGLU, sort and combine omitted")}
+
+
 def cpu_baseline_sample(budget_s=12.0):
     """Single core, the reference CPU kernel, bounded sample of config 1."""
     from oracle.oracle import MlxRef
@@ -178,7 +196,7 @@ def cpu_baseline_sample(budget_s=12.0):
     sample = (f"{3 * rows} rows of K=4096 4-bit g64 qmv through the reference's MLX CPU kernel "
               f"(backend/cpu/quantized.cpp _qmm_t, bf16 sum) on 1 core; tok/s = 1/(row time x "
               f"{decode_rows_per_token()} row-equivalents per token); router/SwiGLU/combine (<2% of work) omitted")
-    return {"value": tok_s, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample}
+    return {"value": tok_s, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample, "row_s": per_row}
 
 
 def run_reference(args, rank, world):
@@ -281,6 +299,85 @@ def run_decoder(dev, hbm_peak, peak_kind, n_new=DEC_NEW, prefill_warmup=2, n_lay
     return out
 
 
+C0_COPIES, C0_CALLS = 32, 256
+C0_BYTES = 4096 * (4096 // 2 + 2 * 2 * 4096 // GS) + 2 * 4096 + 2 * 4096  # 9,453,568 B per call
+
+
+def run_c0(dev, stream, hbm_peak, peak_kind):
+    """Config 0: one 4-bit qmv, x [1, 4096], W [4096, 4096] g64. A CUDA graph of 256
+    back-to-back calls over 32 weight copies (302 MB, larger than L2), timed with
+    CUDA events; plus the same calls through b2q.quantized_matmul from pinned host
+    memory (e2e)."""
+    import torch
+
+    import b2q
+    from b2q import synth
+    from b2q._lib import check, lib
+
+    L = lib()
+    sp = stream.cuda_stream
+    copies = [synth.packed_weights((4096,), 4096, GS, device=dev, seed=500 + i) for i in range(C0_COPIES)]
+    xs = synth.activations((C0_CALLS, 4096), device=dev, seed=501)
+    y = torch.empty((C0_CALLS, 4096), dtype=torch.bfloat16, device=dev)
+    ptrs = [(w.data_ptr(), s_.data_ptr(), b.data_ptr()) for (w, s_, b) in copies]
+
+    def call(i):
+        w, s_, b = ptrs[i % C0_COPIES]
+        rc = L.b2q_qmm(xs[i].data_ptr(), w, s_, b, y[i].data_ptr(), 1, 4096, 4096, GS, 4, 1, sp)
+        if rc:
+            check(rc)
+
+    with torch.cuda.stream(stream):
+        for i in range(8):
+            call(i)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(C0_CALLS):
+            call(i)
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    reps = 8
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * C0_CALLS)
+    gbs = C0_BYTES / (us * 1e-6) / 1e9
+    # e2e: through the public op, x copied in from pinned host memory and y read back per call
+    hx = torch.empty((64, 1, 4096), dtype=torch.bfloat16).pin_memory()
+    hx.copy_(xs[:64].view(64, 1, 4096).cpu())
+    hy = torch.empty((1, 4096), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty((1, 4096), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(8):
+            dx.copy_(hx[i], non_blocking=True)
+            hy.copy_(b2q.quantized_matmul(dx, *copies[i % C0_COPIES]), non_blocking=True)
+        torch.cuda.synchronize(dev)
+        n = 512
+        e0.record(stream)
+        for i in range(n):
+            dx.copy_(hx[i % 64], non_blocking=True)
+            hy.copy_(b2q.quantized_matmul(dx, *copies[i % C0_COPIES]), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    e2e_us = e0.elapsed_time(e1) * 1000.0 / n
+    del g, copies
+    torch.cuda.empty_cache()
+    return {"workload": "config 0: qmv x [1,4096] . W[4096,4096]^T, 4-bit g64",
+            "us_per_call": us, "calls_per_s": 1e6 / us,
+            "form": f"CUDA graph of {C0_CALLS} calls over {C0_COPIES} weight copies "
+                    f"({C0_COPIES * C0_BYTES / 1e6:.0f} MB, cold in L2)",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "peak_kind": peak_kind, "bytes_per_launch": C0_BYTES},
+            "e2e": {"value": 1e6 / e2e_us, "unit": "calls/s", "us_per_call": e2e_us, "h2d_bytes_per_step": 8192,
+                    "d2h_bytes_per_step": 8192, "api": "b2q.quantized_matmul (pinned host x in, y back each call)"}}
+
+
 EP_PROMPT, EP_NEW = 8192, 512
 
 
@@ -352,6 +449,7 @@ def main():
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="rotating layers (cold-L2 decode)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the config-3 full-decoder leg")
+    ap.add_argument("--no-c0", action="store_true", help="skip the config-0 single-qmv leg")
     ap.add_argument("--decoder-only", type=int, default=0, metavar="TOKENS",
                     help="run only the config-3 leg with this many generated tokens (a short case for profiling)")
     ap.add_argument("--decoder-layers", type=int, default=48, help="layers of the config-3 model (48 in the spec)")
@@ -639,6 +737,11 @@ def main():
                                                      "peak_kind": peak_kind,
                                                      "traffic": load_traffic("moe_prefill_c2.json")}}
 
+    # ---------------- single qmv (config 0), one GPU ----------------
+    c0 = None
+    if world == 1 and not args.no_c0:
+        c0 = run_c0(dev, stream, hbm_peak, peak_kind)
+
     # ---------------- full decoder (config 3), one GPU ----------------
     decoder = None
     if not args.no_decoder and world == 1:
@@ -654,6 +757,13 @@ def main():
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         cpu = cpu_baseline_sample()
+        if prefill is not None:
+            prefill["cpu_baseline"] = prefill_cpu_baseline(cpu["row_s"], cpu["kind"])
+        if c0 is not None:
+            c0["cpu_baseline"] = {"value": 1.0 / (cpu["row_s"] * 4096), "unit": "calls/s", "cores": 1,
+                                  "kind": cpu["kind"],
+                                  "sample": "measured per-row time of the reference's MLX CPU kernel (K=4096 4-bit "
+                                            "g64, bf16 sum) x 4096 rows"}
     line = {
         "metric": METRIC,
         "value": tok_s,
@@ -689,6 +799,7 @@ def main():
         "clocks": clocks,
         "prefill": prefill,
         "decoder": decoder,
+        "c0": c0,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
