@@ -161,14 +161,15 @@ B2Q_API int b2q_moe_decode(const uint16_t* x, const uint16_t* wr,
  * one file-scope device array of B2Q_NOALLOC_SCRATCH_BYTES per GPU that loads
  * the library, held until exit; shapes whose decode workspace
  * (b2q_moe_decode_workspace_size(1, H, E, F, k)) exceeds it are refused with
- * B2Q_EINVAL. The first call on a device resolves the array's address and
- * zeroes it with a blocking memset: make it before any stream capture. All
- * calls on a device share the array; each clears its header on `stream`
- * first, so calls in stream order are independent, but calls that overlap on
- * the GPU race. `status` (device int, may be NULL) receives the call's
- * device-side status in stream order: 0, or B2Q_ETIMEOUT if a bounded wait
- * ran out. Other arguments as b2q_moe_decode. */
-#define B2Q_NOALLOC_SCRATCH_BYTES 65536
+ * B2Q_EINVAL. The first call on a device resolves the array's address
+ * (cudaGetSymbolAddress): make it before any stream capture. All calls on a
+ * device share the array; each clears its error word and grid counters with
+ * an asynchronous memset on `stream` first, so calls in stream order are
+ * independent, but calls that overlap on the GPU race. It runs the same kernel
+ * as b2q_moe_decode for the shape. `status` (device int, may be NULL)
+ * receives the call's device-side status in stream order: 0, or B2Q_ETIMEOUT
+ * if a bounded wait ran out. Other arguments as b2q_moe_decode. */
+#define B2Q_NOALLOC_SCRATCH_BYTES 131072
 B2Q_API int b2q_moe_decode_noalloc(const uint16_t* x, const uint16_t* wr,
                    const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
                    const uint32_t* wu, const uint16_t* su, const uint16_t* bu,

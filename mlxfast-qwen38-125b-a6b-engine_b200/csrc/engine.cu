@@ -1140,6 +1140,121 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
   }
 }
 
+// Split-K router GEMM for long token windows (prefill): a CTA computes 64
+// tokens x 128 experts over one of S slices of the hidden size through a
+// 4-stage cp.async ring; 8 warps each 64 tokens x 16 experts (mma.sync
+// m16n8k16, bf16 products exact in fp32, fp32 accumulation). Every CTA writes
+// its fp32 partial tile; router_reduce_kernel adds the S partials in slice
+// order. Fewer re-reads of the router matrix per token than the 16-token
+// tiles, and a deeper pipeline.
+constexpr int RS_BM = 64, RS_BN = 128, RS_BK = 64, RS_LD = RS_BK + 8, RS_ST = 4;
+constexpr int RS_SMEM = RS_ST * (RS_BM + RS_BN) * RS_LD * 2;
+
+__global__ void __launch_bounds__(256) router_gemm_sk_kernel(const uint16_t* __restrict__ x,
+                                                             const uint16_t* __restrict__ wr,
+                                                             float* __restrict__ partial, int T, int E, int H,
+                                                             int S) {
+  extern __shared__ __align__(16) uint16_t rsm[];
+  uint16_t* xs = rsm;                           // [RS_ST][RS_BM * RS_LD]
+  uint16_t* wsm = rsm + RS_ST * RS_BM * RS_LD;  // [RS_ST][RS_BN * RS_LD]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = blockIdx.x * RS_BM, e0 = blockIdx.y * RS_BN, sl = blockIdx.z;
+  const int kslice = H / S, kbase = sl * kslice, nk = kslice / RS_BK;
+  const int wn = warp * 16;
+  auto load = [&](int buf, int kt) {
+    const int k0 = kbase + kt * RS_BK;
+    for (int i = tid; i < RS_BM * 8; i += 256) {
+      const int r = i >> 3, c = i & 7;
+      const bool ok = t0 + r < T;
+      cp_async16(&xs[buf * RS_BM * RS_LD + r * RS_LD + c * 8], x + (size_t)(ok ? t0 + r : 0) * H + k0 + c * 8, ok);
+    }
+    for (int i = tid; i < RS_BN * 8; i += 256) {
+      const int r = i >> 3, c = i & 7;
+      const bool ok = e0 + r < E;
+      cp_async16(&wsm[buf * RS_BN * RS_LD + r * RS_LD + c * 8], wr + (size_t)(ok ? e0 + r : 0) * H + k0 + c * 8,
+                 ok);
+    }
+  };
+  float acc[4][2][4] = {};
+#pragma unroll
+  for (int st = 0; st < RS_ST - 1; ++st) {
+    if (st < nk) load(st, st);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (int kt = 0; kt < nk; ++kt) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(RS_ST - 2) : "memory");
+    __syncthreads();
+    if (kt + RS_ST - 1 < nk) load((kt + RS_ST - 1) % RS_ST, kt + RS_ST - 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint16_t* xb = xs + (kt % RS_ST) * RS_BM * RS_LD;
+    const uint16_t* wb = wsm + (kt % RS_ST) * RS_BN * RS_LD;
+#pragma unroll
+    for (int kk = 0; kk < RS_BK; kk += 16) {
+      uint32_t b[4];
+      const int m = lane >> 3, r = lane & 7;
+      ldmatrix_x4(b, wb + (wn + (m >> 1) * 8 + r) * RS_LD + kk + (m & 1) * 8);
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi) {
+        uint32_t a[4];
+        ldmatrix_x4(a, xb + (mi * 16 + (lane & 15)) * RS_LD + kk + (lane >> 4) * 8);
+        mma_bf16_16816(acc[mi][0], a[0], a[1], a[2], a[3], b[0], b[1]);
+        mma_bf16_16816(acc[mi][1], a[0], a[1], a[2], a[3], b[2], b[3]);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  const int g = lane >> 2, q = lane & 3;
+  float* part = partial + (size_t)sl * T * E;
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int e = e0 + wn + nt * 8 + 2 * q;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int t = t0 + mi * 16 + g + h * 8;
+        if (t < T) {
+          if (e < E) part[(size_t)t * E + e] = acc[mi][nt][2 * h];
+          if (e + 1 < E) part[(size_t)t * E + e + 1] = acc[mi][nt][2 * h + 1];
+        }
+      }
+    }
+}
+
+__global__ void router_reduce_kernel(const float* __restrict__ partial, float* __restrict__ logits, long long n,
+                                     int S) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float a = partial[i];
+  for (int s = 1; s < S; ++s) a += partial[(size_t)s * n + i];
+  logits[i] = a;
+}
+
+int launch_router_logits_sk(const uint16_t* x, const uint16_t* wr, float* logits, float* scratch,
+                            size_t scratch_bytes, int T, int E, int H, cudaStream_t s) {
+  const int mt = (T + RS_BM - 1) / RS_BM, nt = (E + RS_BN - 1) / RS_BN;
+  int S = 1;
+  // slices until the grid fills the GPU about twice (two CTAs fit per SM)
+  while (S < 8 && mt * nt * S * 2 <= 296 && H % (RS_BK * S * 2) == 0) S *= 2;
+  if (T < RS_BM || H % (RS_BK * S) || !scratch || scratch_bytes < (size_t)S * T * E * sizeof(float))
+    return launch_router_logits(x, wr, logits, T, E, H, s);
+  static bool attr_done[64] = {};
+  int dev = 0;
+  B2Q_TRY_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev & 63]) {
+    B2Q_TRY_CUDA(cudaFuncSetAttribute(router_gemm_sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RS_SMEM));
+    attr_done[dev & 63] = true;
+  }
+  router_gemm_sk_kernel<<<dim3(mt, nt, S), 256, RS_SMEM, s>>>(x, wr, S > 1 ? scratch : logits, T, E, H, S);
+  B2Q_TRY_CUDA(cudaGetLastError());
+  if (S > 1) {
+    const long long n = (long long)T * E;
+    router_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(scratch, logits, n, S);
+    B2Q_TRY_CUDA(cudaGetLastError());
+  }
+  return B2Q_OK;
+}
+
 int launch_router_logits(const uint16_t* x, const uint16_t* wr, float* logits, int T, int E, int H,
                          cudaStream_t s) {
   if (T >= RT_BM && H % RT_BK == 0) {

@@ -97,6 +97,10 @@ int launch(const Params& p, void* stream, bool cooperative);
 int launch_router_logits(const uint16_t* x, const uint16_t* wr, float* logits, int T, int E, int H,
                          cudaStream_t s);
 int launch_route(const float* logits, uint32_t* idx, float* w, int T, int E, int k, cudaStream_t s);
+// Long windows with fp32 scratch of at least 8 * T * E floats: the split-K
+// router GEMM (falls back to launch_router_logits otherwise).
+int launch_router_logits_sk(const uint16_t* x, const uint16_t* wr, float* logits, float* scratch,
+                            size_t scratch_bytes, int T, int E, int H, cudaStream_t s);
 
 }  // namespace eng
 }  // namespace b2q

@@ -13,17 +13,22 @@
 //  * every GPU that loads the library holds B2Q_NOALLOC_SCRATCH_BYTES of it
 //    until the process exits;
 //  * the first call on a device looks up the array's address there
-//    (cudaGetSymbolAddress) and zeroes its header with a blocking cudaMemset;
-//    make that first call before any stream capture on that device;
+//    (cudaGetSymbolAddress); make that first call before any stream capture
+//    on that device;
 //  * all calls on a device share the array and it keeps the last call's
-//    contents; each call clears the header (error word, grid counters) on its
-//    stream before the kernel, so calls in stream order are independent, but
-//    calls whose kernels overlap on the GPU (two streams, two threads) race
-//    on the counters and the activations and give wrong results.
+//    contents; each call clears what must start at zero (the error word and
+//    the grid counters) with an asynchronous memset on its own stream before
+//    the kernel, so calls in stream order are independent, but calls whose
+//    kernels overlap on the GPU (two streams, two threads) race on the
+//    counters and the activations and give wrong results.
+// The kernel is the one b2q_moe_decode runs for the same shape (the
+// single-column fused kernel where its shape rules hold, else the streaming
+// engine's fused mode).
 #include <cuda_runtime.h>
 
 #include <mutex>
 
+#include "decode2.cuh"
 #include "decode_ws.hpp"
 #include "engine.cuh"
 #include "host.hpp"
@@ -42,7 +47,7 @@ std::mutex g_setup_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
 
 // Address of the scratch array on the current device; the first request per
-// device resolves it and zeroes the header.
+// device resolves it.
 int scratch_on_current_device(void** out) {
   int dev = -1;
   B2Q_TRY_CUDA(cudaGetDevice(&dev));
@@ -54,7 +59,6 @@ int scratch_on_current_device(void** out) {
     if (e != cudaSuccess || !ptr)
       return set_error(B2Q_ECUDA, "moe_decode_noalloc: cudaGetSymbolAddress of the scratch array: %s",
                        cudaGetErrorString(e));
-    B2Q_TRY_CUDA(cudaMemset(ptr, 0, sizeof(WsHeader)));
     g_scratch_ptr[dev] = ptr;
   }
   *out = g_scratch_ptr[dev];
@@ -91,9 +95,18 @@ extern "C" int b2q_moe_decode_noalloc(const uint16_t* x, const uint16_t* wr, con
   if (rc) return rc;
   const DecodeWs ws = decode_ws_layout(scratch, 1, H, E, F, k);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // what must start at zero: the error word and the grid counters
-  B2Q_TRY_CUDA(cudaMemsetAsync(ws.hdr, 0, sizeof(WsHeader), st));
+  // what must start at zero: the error word and the grid counters (header and
+  // the counter block that follows it)
+  B2Q_TRY_CUDA(cudaMemsetAsync(ws.hdr, 0, sizeof(WsHeader) + D2_CTR_BYTES, st));
   if (status) B2Q_TRY_CUDA(cudaMemsetAsync(status, 0, sizeof(int), st));
+  const void* ptrs[] = {x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd};
+  bool all_aligned = true;
+  for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
+  if (all_aligned && d2_moe_eligible(H, E, F, k, group_size)) {
+    const D2Scratch scr{status ? status : &ws.hdr->error, ws.ctr, ws.logits, ws.act, ws.asum, ws.y};
+    return d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size, scr,
+                         st);
+  }
   eng::Params p;
   base_params(p, eng::MODE_FUSED, group_size);
   p.x = x;

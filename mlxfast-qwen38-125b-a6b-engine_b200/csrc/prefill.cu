@@ -54,43 +54,41 @@ __global__ void sorted_combine_kernel(const uint16_t* __restrict__ y, const uint
 }
 
 // The same combine for 8 consecutive outputs per thread (16-byte loads of the
-// k rows and one 16-byte store); H % 8 == 0, 16-byte aligned rows.
+// k rows and one 16-byte store); H % 8 == 0, 16-byte aligned rows, k <= 8.
+// All k row loads are issued before any is used (up to 8 x 16 bytes in flight
+// per thread); with k <= 8 each slot is its own chain of the colsum
+// association, and the chains fold in slot order.
 __global__ void sorted_combine8_kernel(const uint16_t* __restrict__ y, const uint32_t* __restrict__ inverse,
                                        const float* __restrict__ w, uint16_t* __restrict__ out, int T, int H,
                                        int k) {
   const int h0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   const int t = blockIdx.y;
   if (h0 >= H || t >= T) return;
-  const int TY = k < 8 ? k : 8;
-  float tt[8][8];
+  uint4 r[8];
+  float wj[8];
 #pragma unroll
-  for (int q = 0; q < 8; ++q)
-#pragma unroll
-    for (int v = 0; v < 8; ++v) tt[q][v] = 0.0f;
-  for (int j = 0; j < k; ++j) {
-    const uint32_t pj = __ldg(inverse + (size_t)t * k + j);
-    const float wj = __ldg(w + (size_t)t * k + j);
-    const uint4 r = __ldg(reinterpret_cast<const uint4*>(y + (size_t)pj * H + h0));
-    const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
-    const int q = j % TY;
-#pragma unroll
-    for (int qq = 0; qq < 8; ++qq) {
-      if (qq != q) continue;
-#pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        const uint32_t word = rw[v >> 1];
-        const float yv = __uint_as_float((v & 1) ? (word & 0xffff0000u) : (word << 16));
-        tt[qq][v] = __fmul_rn(yv, wj) + tt[qq][v];  // product rounded, then added
-      }
+  for (int j = 0; j < 8; ++j) {
+    if (j < k) {
+      const uint32_t pj = __ldg(inverse + (size_t)t * k + j);
+      wj[j] = __ldg(w + (size_t)t * k + j);
+      r[j] = __ldg(reinterpret_cast<const uint4*>(y + (size_t)pj * H + h0));
     }
   }
   uint32_t o[4];
 #pragma unroll
   for (int v = 0; v < 8; v += 2) {
-    float t0 = tt[0][v], t1 = tt[0][v + 1];
-    for (int q = 1; q < TY; ++q) {
-      t0 = tt[q][v] + t0;
-      t1 = tt[q][v + 1] + t1;
+    float t0 = 0.0f, t1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < k) {
+        const uint32_t word = (v >> 1) == 0 ? r[j].x : (v >> 1) == 1 ? r[j].y : (v >> 1) == 2 ? r[j].z : r[j].w;
+        // product rounded, then a chain starting from 0 (c = p + 0, as the
+        // colsum's running sums do), chains folded in slot order
+        const float c0 = __fmul_rn(__uint_as_float(word << 16), wj[j]) + 0.0f;
+        const float c1 = __fmul_rn(__uint_as_float(word & 0xffff0000u), wj[j]) + 0.0f;
+        t0 = (j == 0) ? c0 : c0 + t0;
+        t1 = (j == 0) ? c1 : c1 + t1;
+      }
     }
     o[v >> 1] = (uint32_t)f2bf(t0) | ((uint32_t)f2bf(t1) << 16);
   }
@@ -99,7 +97,7 @@ __global__ void sorted_combine8_kernel(const uint16_t* __restrict__ y, const uin
 
 static void launch_sorted_combine(const uint16_t* y, const uint32_t* inverse, const float* w, uint16_t* out, int T,
                                   int H, int k, cudaStream_t st) {
-  if (H % 8 == 0 && aligned16(y) && aligned16(out)) {
+  if (k <= 8 && H % 8 == 0 && aligned16(y) && aligned16(out)) {
     dim3 grid((H / 8 + 255) / 256, T);
     sorted_combine8_kernel<<<grid, 256, 0, st>>>(y, inverse, w, out, T, H, k);
   } else {
@@ -354,7 +352,10 @@ int b2q_moe_prefill(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, c
   const int R = T * k;
   uint32_t* ix = idx ? idx : ws.idx;
   float* ww = w ? w : ws.w;
-  int rc = eng::launch_router_logits(x, wr, ws.logits, T, E, H, st);
+  // the split-K router GEMM keeps its partials in the down-output region,
+  // which is not in use before the expert products
+  int rc = eng::launch_router_logits_sk(x, wr, ws.logits, reinterpret_cast<float*>(ws.y), 2 * (size_t)T * k * H, T,
+                                        E, H, st);
   if (rc) return rc;
   rc = eng::launch_route(ws.logits, ix, ww, T, E, k, st);
   if (rc) return rc;

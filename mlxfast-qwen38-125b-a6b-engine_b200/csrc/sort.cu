@@ -4,10 +4,16 @@
 // expert id (Runner/FastModel/TrackPrefillSort.swift:17-44 argues MLX's
 // argsort is stable, so this permutation equals argSort(flatIDs)); outputs
 // sorted_ids[p], token_rows[p] = order[p] / k, inverse[order[p]] = p and the
-// per-expert offsets [E + 1]. One CTA of 1024 threads walks the slots in
-// chunks of 1024; inside a chunk, ranks among equal ids come from
-// __match_any_sync within a warp plus per-warp counts of earlier warps, so the
-// order among equal ids is slot order.
+// per-expert offsets [E + 1].
+//
+// One CTA of 32 warps; warp w owns the contiguous slot range
+// [w * R / 32, (w + 1) * R / 32), so slot order is (warp, position in the
+// warp's range). Pass 1: every warp counts its range per expert (ranks inside
+// 32 consecutive slots from __match_any_sync, the lowest lane of each peer set
+// adds the set's size). Scan: base[w][e] = the counts of e in warps before w;
+// offsets = exclusive scan of the per-expert totals. Pass 2: every warp walks
+// its range again, placing slot i at offsets[e] + base[w][e] + (earlier slots
+// of e in the warp's range). Three block barriers in all.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -24,26 +30,45 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
                        uint32_t* __restrict__ token_rows, uint32_t* __restrict__ inverse,
                        uint32_t* __restrict__ offsets, int R, int E, int k, int* err) {
   extern __shared__ unsigned sm[];
-  unsigned* base = sm;         // [E] running bucket start
-  unsigned* wcnt = sm + E;     // [SORT_WARPS][E] counts of the current chunk
+  unsigned* cnt = sm;                   // [SORT_WARPS][E] counts, then running positions
+  unsigned* tot = sm + SORT_WARPS * E;  // [E] per-expert totals, then offsets
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int e = tid; e < E; e += SORT_THREADS) base[e] = 0;
-  for (int i = tid; i < SORT_WARPS * E; i += SORT_THREADS) wcnt[i] = 0;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int i = tid; i < SORT_WARPS * E; i += SORT_THREADS) cnt[i] = 0;
   __syncthreads();
-  for (int i = tid; i < R; i += SORT_THREADS) {
-    const uint32_t e = __ldg(ids + i);
-    if (e < (uint32_t)E)
-      atomicAdd(&base[e], 1u);
-    else
+  // this warp's slot range
+  const int per = (R + SORT_WARPS - 1) / SORT_WARPS;
+  const int i0 = min(R, warp * per), i1 = min(R, i0 + per);
+  unsigned* wc = cnt + warp * E;
+  // ---- pass 1: counts per expert of the warp's range ----
+  for (int c0 = i0; c0 < i1; c0 += 32) {
+    const int i = c0 + lane;
+    uint32_t e = (i < i1) ? __ldg(ids + i) : 0xffffffffu;
+    if (i < i1 && e >= (uint32_t)E) {
       record_error(err, B2Q_EINVAL);
+      e = 0xffffffffu;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e != 0xffffffffu && (peers & lt_mask) == 0) wc[e] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  // ---- scan: base[w][e] over warps, offsets over experts ----
+  for (int e = tid; e < E; e += SORT_THREADS) {
+    unsigned run = 0;
+    for (int w = 0; w < SORT_WARPS; ++w) {
+      const unsigned c = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += c;
+    }
+    tot[e] = run;
   }
   __syncthreads();
   if (warp == 0) {
-    // exclusive scan of the E bucket sizes: each lane owns a contiguous run
-    const int per = (E + 31) / 32;
-    const int e0 = lane * per, e1 = min(E, e0 + per);
+    const int pe = (E + 31) / 32;
+    const int e0 = lane * pe, e1 = min(E, e0 + pe);
     unsigned run = 0;
-    for (int e = e0; e < e1; ++e) run += base[e];
+    for (int e = e0; e < e1; ++e) run += tot[e];
     unsigned incl = run;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -52,48 +77,35 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
     }
     unsigned acc = incl - run;
     for (int e = e0; e < e1; ++e) {
-      const unsigned c = base[e];
-      base[e] = acc;
+      const unsigned c = tot[e];
+      tot[e] = acc;
       if (offsets) offsets[e] = acc;
       acc += c;
     }
     if (lane == 31 && offsets) offsets[E] = incl;
   }
   __syncthreads();
-  const unsigned lt_mask = (1u << lane) - 1u;
-  for (int c0 = 0; c0 < R; c0 += SORT_THREADS) {
-    const int i = c0 + tid;
-    uint32_t e = (i < R) ? __ldg(ids + i) : 0xffffffffu;
+  // ---- pass 2: place the warp's range in slot order ----
+  for (int c0 = i0; c0 < i1; c0 += 32) {
+    const int i = c0 + lane;
+    uint32_t e = (i < i1) ? __ldg(ids + i) : 0xffffffffu;
     if (e >= (uint32_t)E) e = 0xffffffffu;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const unsigned rank = __popc(peers & lt_mask);
-    const bool valid = e != 0xffffffffu;
-    if (valid && rank == 0) wcnt[warp * E + e] = __popc(peers);
-    __syncthreads();
-    if (valid) {
-      unsigned pre = 0;
-      for (int w = 0; w < warp; ++w) pre += wcnt[w * E + e];
-      const unsigned pos = base[e] + pre + rank;
+    if (e != 0xffffffffu) {
+      const unsigned pos = tot[e] + wc[e] + __popc(peers & lt_mask);
       if (sorted_ids) sorted_ids[pos] = e;
       if (token_rows) token_rows[pos] = (uint32_t)(i / k);
       if (inverse) inverse[i] = pos;
     }
-    __syncthreads();
-    for (int ee = tid; ee < E; ee += SORT_THREADS) {
-      unsigned tot = 0;
-      for (int w = 0; w < SORT_WARPS; ++w) {
-        tot += wcnt[w * E + ee];
-        wcnt[w * E + ee] = 0;
-      }
-      base[ee] += tot;
-    }
-    __syncthreads();
+    __syncwarp();
+    if (e != 0xffffffffu && (peers & lt_mask) == 0) wc[e] += __popc(peers);
+    __syncwarp();
   }
 }
 
 int launch_expert_sort(const uint32_t* ids, uint32_t* sorted_ids, uint32_t* token_rows, uint32_t* inverse,
                        uint32_t* offsets, int R, int E, int k, int* err, cudaStream_t st) {
-  const size_t smem = sizeof(unsigned) * (size_t)E * (1 + SORT_WARPS);
+  const size_t smem = sizeof(unsigned) * (size_t)E * (SORT_WARPS + 1);
   B2Q_TRY_CUDA(cudaFuncSetAttribute(expert_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   expert_sort_kernel<<<1, SORT_THREADS, smem, st>>>(ids, sorted_ids, token_rows, inverse, offsets, R, E, k, err);
   B2Q_TRY_CUDA(cudaGetLastError());

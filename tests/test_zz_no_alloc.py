@@ -14,7 +14,7 @@ import pytest
 from conftest import rel_l2
 
 TIGHT = 5e-3
-SCRATCH_BYTES = 65536  # B2Q_NOALLOC_SCRATCH_BYTES in include/b2q.h
+SCRATCH_BYTES = 131072  # B2Q_NOALLOC_SCRATCH_BYTES in include/b2q.h
 
 
 def _bf(t):
