@@ -7,7 +7,7 @@
 //   route (top-k + softmax)    Runner/FastModel/TrackFastMoE.swift:767-911
 //   combine association        Runner/FastModel/TrackFastKernels2.swift:36-47
 //
-// Organisation: one CTA per SM, one producer warp and 8 consumer warps.
+// Organisation: one CTA per SM, one producer warp and 16 consumer warps.
 //  * The work of a call is a sequence of units, each one TMA fill of a stage:
 //      gate|up unit  16 outputs of one routed expert: its 16 gate rows and 16
 //                    up rows over the whole hidden size (two copies of 16 rows
@@ -60,7 +60,7 @@
 namespace b2q {
 namespace d2 {
 
-constexpr int NCW = 8;               // consumer warps
+constexpr int NCW = 16;              // consumer warps
 constexpr int NTH = (NCW + 1) * 32;  // + the producer warp
 constexpr int MAXK = 8;              // routed slots
 constexpr int MAXST = 6;             // stages at most
@@ -68,7 +68,7 @@ constexpr int ROWS_QMV = 16;         // rows of a qmv unit
 constexpr int ROWS_GU = 16;          // outputs of a gate|up unit (16 gate + 16 up rows)
 constexpr int ROWS_DOWN = 64;        // rows of a down unit
 constexpr int MISC_BYTES = 512;
-constexpr int XR = 16;               // activation chunks a consumer lane holds in registers
+constexpr int XR = 8;                // activation chunks a consumer lane holds in registers
 
 enum : int { U_END = -1, U_GU = 0, U_DOWN = 1, U_QMV = 2 };
 enum : int { MW = 0, MS = 1, MB = 2, MWG = 0, MSG = 1, MBG = 2, MWU = 3, MSU = 4, MBU = 5, MWD = 6, MSD = 7, MBD = 8 };
@@ -144,33 +144,40 @@ __device__ __forceinline__ void dot_xreg(const uint8_t* wbase, int PS, const int
                                          int cc0, int ncc, const uint4 (&xr)[XR], const float* gsum,
                                          const Meta (&m)[NRB], float (&accP)[NRB], float (&accQ)[NRB]) {
   constexpr int NGMAX = XR / CPG;
+  constexpr int NBW = NRB == 1 ? 4 : 2;       // groups per batch (fewer live accumulators with two row blocks)
+  constexpr int NB = NGMAX < NBW ? NGMAX : NBW;
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
   const int ng = ncc / CPG;
   const int g0 = cc0 / CPG;
   const uint8_t* wl = wbase + r * 128 + c * 4;
 #pragma unroll
-  for (int gb = 0; gb < NGMAX; gb += 4) {
+  for (int gb = 0; gb < NGMAX; gb += NB) {
     if (gb < ng) {
-      float D[NRB][4][4];
+      float D[NRB][NB][4];
 #pragma unroll
-      for (int gi = 0; gi < 4; ++gi) {
-        if (gb + gi < ng) {
+      for (int j = 0; j < CPG; ++j) {
+        // every word of this step first, then the MMAs, consecutive ones on
+        // independent accumulators
+        uint32_t W0[NB][NRB], W8[NB][NRB];
 #pragma unroll
-          for (int j = 0; j < CPG; ++j) {
-            const int i = (gb + gi) * CPG + j;
-            const int cc = cc0 + i;
-            const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4);
+        for (int gi = 0; gi < NB; ++gi) {
+          const int i = (gb + gi) * CPG + j;
+          const int cc = cc0 + i;
+          const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4);
 #pragma unroll
-            for (int b = 0; b < NRB; ++b) {
-              const uint32_t W0 = *reinterpret_cast<const uint32_t*>(wp + P0[b]);
-              const uint32_t W8 = *reinterpret_cast<const uint32_t*>(wp + Q0[b]);
-              mma_word_pair(D[b][gi], W0, W8, xr[i < XR ? i : 0], j == 0);
-            }
+          for (int b = 0; b < NRB; ++b) {
+            const bool live = gb + gi < ng;
+            W0[gi][b] = live ? *reinterpret_cast<const uint32_t*>(wp + P0[b]) : 0u;
+            W8[gi][b] = live ? *reinterpret_cast<const uint32_t*>(wp + Q0[b]) : 0u;
           }
-        } else {
-#pragma unroll
-          for (int b = 0; b < NRB; ++b) D[b][gi][0] = D[b][gi][1] = D[b][gi][2] = D[b][gi][3] = 0.0f;
         }
+#pragma unroll
+        for (int b = 0; b < NRB; ++b)
+#pragma unroll
+          for (int gi = 0; gi < NB; ++gi) {
+            const int i = (gb + gi) * CPG + j;
+            mma_word_pair(D[b][gi], W0[gi][b], W8[gi][b], xr[i < XR ? i : 0], j == 0);
+          }
       }
       const int gl = gb + c;
       const float xa = gsum[gl < ng ? gl : 0];
@@ -178,11 +185,11 @@ __device__ __forceinline__ void dot_xreg(const uint8_t* wbase, int PS, const int
       for (int b = 0; b < NRB; ++b) {
         float eP = D[b][0][0], eQ = D[b][0][2];
 #pragma unroll
-        for (int gi = 1; gi < 4; ++gi) {
+        for (int gi = 1; gi < NB; ++gi) {
           eP = (c == gi) ? D[b][gi][0] : eP;
           eQ = (c == gi) ? D[b][gi][2] : eQ;
         }
-        if (gl < ng) group_epilogue(m[b], g0 + gl, xa, eP, eQ, accP[b], accQ[b]);
+        if (c < NB && gl < ng) group_epilogue(m[b], g0 + gl, xa, eP, eQ, accP[b], accQ[b]);
       }
     }
   }
@@ -202,19 +209,21 @@ __device__ __forceinline__ void dot_xsmem(const uint8_t* wbase, int PS, int P0, 
   for (int gb = 0; gb < ng; gb += 4) {
     float D[4][4];
 #pragma unroll
-    for (int gi = 0; gi < 4; ++gi) {
-      if (gb + gi < ng) {
+    for (int j = 0; j < CPG; ++j) {
+      uint32_t W0[4], W8[4];
 #pragma unroll
-        for (int j = 0; j < CPG; ++j) {
-          const int cc = cc0 + (gb + gi) * CPG + j;
-          const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4);
-          const uint32_t W0 = *reinterpret_cast<const uint32_t*>(wp + P0);
-          const uint32_t W8 = *reinterpret_cast<const uint32_t*>(wp + Q0);
-          const uint4 xv = *reinterpret_cast<const uint4*>(xl + (size_t)cc * 64);
-          mma_word_pair(D[gi], W0, W8, xv, j == 0);
-        }
-      } else {
-        D[gi][0] = D[gi][1] = D[gi][2] = D[gi][3] = 0.0f;
+      for (int gi = 0; gi < 4; ++gi) {
+        const bool live = gb + gi < ng;
+        const int cc = cc0 + (gb + gi) * CPG + j;
+        const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4);
+        W0[gi] = live ? *reinterpret_cast<const uint32_t*>(wp + P0) : 0u;
+        W8[gi] = live ? *reinterpret_cast<const uint32_t*>(wp + Q0) : 0u;
+      }
+#pragma unroll
+      for (int gi = 0; gi < 4; ++gi) {
+        const int cc = cc0 + (gb + gi) * CPG + j;
+        const uint4 xv = gb + gi < ng ? *reinterpret_cast<const uint4*>(xl + (size_t)cc * 64) : make_uint4(0u, 0u, 0u, 0u);
+        mma_word_pair(D[gi], W0[gi], W8[gi], xv, j == 0);
       }
     }
     float eP = D[0][0], eQ = D[0][2];
@@ -511,78 +520,22 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
     __syncwarp();
   } else {
     // ------------------------------ consumers ------------------------------
+    // A CTA's queue hands out all its gate|up units before any down unit, so
+    // the consumers run two phases: units whose activation is in registers
+    // (gate|up, qmv), then down units (their activation is in the stage).
     const int r = lane >> 2, c = lane & 3;
-    for (int it = 0;; ++it) {
+    auto wait_full = [&](int it) -> bool {
       const int s = it % NS;
       if (!__all_sync(0xffffffffu, tc::wait(&full[s], (it / NS) & 1, deadline, abort_flag))) {
         if (!*abort_flag && lane == 0) record_error(p.err, B2Q_ETIMEOUT);
         *abort_flag = 1;
-        break;
+        return false;
       }
-      const int4 inf = info[s];
-      if (inf.x == U_END) break;
-      const uint8_t* st = smem + (size_t)s * p.stage_bytes;
-      float* rp = red + ((size_t)s * NCW + warp) * 32;
-      if (FUSED && inf.x == U_DOWN) {
-        // 4 row blocks of 16 x 2 reduction halves
-        const int b = warp >> 1, qw = warp & 1;
-        const int ncc = F / 32 / 2, cc0 = qw * ncc, ng = ncc / CPG;
-        const float* as = reinterpret_cast<const float*>(st + p.st_asum);
-        float gl_sum = 0.0f;
-        if (lane < ng) {
-          const int q0 = (cc0 / CPG + lane) * CPC;
-#pragma unroll
-          for (int i = 0; i < CPC; ++i) gl_sum += as[q0 + i];
-        }
-        const Meta m{st + p.st_meta2, st + p.st_meta2 + p.st_mstep2, st + p.st_meta2,
-                     st + p.st_meta2 + p.st_mstep2, 16 * b + r, 16 * b + 8 + r, p.mb2, p.sw2 != 0};
-        float accP = 0.0f, accQ = 0.0f;
-        dot_xsmem<CPG>(st, ROWS_DOWN * 128, b * 2048, b * 2048 + 1024, cc0, ncc, st + p.st_act, gl_sum, m, accP,
-                       accQ);
-        accP += __shfl_xor_sync(0xffffffffu, accP, 1);
-        accQ += __shfl_xor_sync(0xffffffffu, accQ, 1);
-        accP += __shfl_xor_sync(0xffffffffu, accP, 2);
-        accQ += __shfl_xor_sync(0xffffffffu, accQ, 2);
-        if (c == 0) {
-          rp[r] = accP;
-          rp[r + 8] = accQ;
-        }
-      } else if (FUSED) {
-        // gate|up: both row blocks of the 16 outputs, the warp's eighth of the reduction
-        const uint8_t* mb = st + p.st_meta1;
-        const Meta m[2] = {
-            {mb, mb + p.st_mstep1, mb + 2 * p.st_mstep1, mb + 3 * p.st_mstep1, r, r, p.mb1, p.sw1 != 0},
-            {mb, mb + p.st_mstep1, mb + 2 * p.st_mstep1, mb + 3 * p.st_mstep1, 8 + r, 8 + r, p.mb1, p.sw1 != 0}};
-        const int ub = ROWS_GU * K1 / 2;  // the up rows' box
-        const int P0[2] = {0, 1024}, Q0[2] = {ub, ub + 1024};
-        float accP[2] = {0.0f, 0.0f}, accQ[2] = {0.0f, 0.0f};
-        dot_xreg<CPG, 2>(st, ROWS_GU * 128, P0, Q0, cc01, ncc1, xr, xsum + cc01 / CPG, m, accP, accQ);
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 1);
-          accQ[b] += __shfl_xor_sync(0xffffffffu, accQ[b], 1);
-          accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 2);
-          accQ[b] += __shfl_xor_sync(0xffffffffu, accQ[b], 2);
-          if (c == 0) {
-            rp[16 * b + r] = accP[b];
-            rp[16 * b + 8 + r] = accQ[b];
-          }
-        }
-      } else {
-        const uint8_t* mb = st + p.st_meta1;
-        const Meta m[1] = {{mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, r, 8 + r, p.mb1, p.sw1 != 0}};
-        const int P0[1] = {0}, Q0[1] = {1024};
-        float accP[1] = {0.0f}, accQ[1] = {0.0f};
-        dot_xreg<CPG, 1>(st, ROWS_QMV * 128, P0, Q0, cc01, ncc1, xr, xsum + cc01 / CPG, m, accP, accQ);
-        accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 1);
-        accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 1);
-        accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 2);
-        accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 2);
-        if (c == 0) {
-          rp[r] = accP[0];
-          rp[r + 8] = accQ[0];
-        }
-      }
+      return true;
+    };
+    // after a warp's partials are in `red`: the last warp of the unit
+    // finishes it; every warp then releases the stage
+    auto hand_in = [&](int s, const int4& inf) {
       __syncwarp();
       unsigned old = 0;
       if (lane == 0) {
@@ -591,7 +544,6 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       }
       old = __shfl_sync(0xffffffffu, old, 0);
       if (old == NCW - 1) {
-        // the last warp of the unit finishes it
         __threadfence_block();
         const float* rb = red + (size_t)s * NCW * 32;
         if (FUSED && inf.x == U_GU) {
@@ -622,7 +574,8 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             const int i = lane + 32 * h2, b = i >> 4, j = i & 15;
-            const float y2 = rb[(2 * b) * 32 + j] + rb[(2 * b + 1) * 32 + j];
+            const float y2 = (rb[(4 * b) * 32 + j] + rb[(4 * b + 1) * 32 + j]) +
+                             (rb[(4 * b + 2) * 32 + j] + rb[(4 * b + 3) * 32 + j]);
             p.ws_y[(size_t)z * H + hb * ROWS_DOWN + i] = f2bf(y2);
           }
           __threadfence();
@@ -669,6 +622,93 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         __syncwarp();
       }
       if (lane == 0) mbar_arrive(&empty[s]);
+    };
+
+    int it = 0;
+    int4 inf = make_int4(U_END, 0, 0, 0);
+    bool live = true;
+    // ---- phase 1: gate|up (fused) or qmv units ----
+    for (;; ++it) {
+      if (!wait_full(it)) {
+        live = false;
+        break;
+      }
+      const int s = it % NS;
+      inf = info[s];
+      if (inf.x == U_END || inf.x == U_DOWN) break;
+      const uint8_t* st = smem + (size_t)s * p.stage_bytes;
+      float* rp = red + ((size_t)s * NCW + warp) * 32;
+      const uint8_t* mb = st + p.st_meta1;
+      if (FUSED) {
+        // both row blocks of the 16 outputs, the warp's slice of the reduction
+        const Meta m[2] = {
+            {mb, mb + p.st_mstep1, mb + 2 * p.st_mstep1, mb + 3 * p.st_mstep1, r, r, p.mb1, p.sw1 != 0},
+            {mb, mb + p.st_mstep1, mb + 2 * p.st_mstep1, mb + 3 * p.st_mstep1, 8 + r, 8 + r, p.mb1, p.sw1 != 0}};
+        const int ub = ROWS_GU * K1 / 2;  // the up rows' box
+        const int P0[2] = {0, 1024}, Q0[2] = {ub, ub + 1024};
+        float accP[2] = {0.0f, 0.0f}, accQ[2] = {0.0f, 0.0f};
+        dot_xreg<CPG, 2>(st, ROWS_GU * 128, P0, Q0, cc01, ncc1, xr, xsum + cc01 / CPG, m, accP, accQ);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 1);
+          accQ[b] += __shfl_xor_sync(0xffffffffu, accQ[b], 1);
+          accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 2);
+          accQ[b] += __shfl_xor_sync(0xffffffffu, accQ[b], 2);
+          if (c == 0) {
+            rp[16 * b + r] = accP[b];
+            rp[16 * b + 8 + r] = accQ[b];
+          }
+        }
+      } else {
+        const Meta m[1] = {{mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, r, 8 + r, p.mb1, p.sw1 != 0}};
+        const int P0[1] = {0}, Q0[1] = {1024};
+        float accP[1] = {0.0f}, accQ[1] = {0.0f};
+        dot_xreg<CPG, 1>(st, ROWS_QMV * 128, P0, Q0, cc01, ncc1, xr, xsum + cc01 / CPG, m, accP, accQ);
+        accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 1);
+        accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 1);
+        accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 2);
+        accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 2);
+        if (c == 0) {
+          rp[r] = accP[0];
+          rp[r + 8] = accQ[0];
+        }
+      }
+      hand_in(s, inf);
+    }
+    // ---- phase 2 (fused): down units; the unit at `it` has already been waited for ----
+    if (FUSED && live) {
+      for (;; ++it) {
+        const int s = it % NS;
+        if (inf.x != U_DOWN) break;
+        const uint8_t* st = smem + (size_t)s * p.stage_bytes;
+        float* rp = red + ((size_t)s * NCW + warp) * 32;
+        // 4 row blocks of 16 x 4 reduction quarters
+        const int b = warp >> 2, qw = warp & 3;
+        const int ncc = F / 32 / 4, cc0 = qw * ncc, ng = ncc / CPG;
+        const float* as = reinterpret_cast<const float*>(st + p.st_asum);
+        float gl_sum = 0.0f;
+        if (lane < ng) {
+          const int q0 = (cc0 / CPG + lane) * CPC;
+#pragma unroll
+          for (int i = 0; i < CPC; ++i) gl_sum += as[q0 + i];
+        }
+        const Meta m{st + p.st_meta2, st + p.st_meta2 + p.st_mstep2, st + p.st_meta2,
+                     st + p.st_meta2 + p.st_mstep2, 16 * b + r, 16 * b + 8 + r, p.mb2, p.sw2 != 0};
+        float accP = 0.0f, accQ = 0.0f;
+        dot_xsmem<CPG>(st, ROWS_DOWN * 128, b * 2048, b * 2048 + 1024, cc0, ncc, st + p.st_act, gl_sum, m, accP,
+                       accQ);
+        accP += __shfl_xor_sync(0xffffffffu, accP, 1);
+        accQ += __shfl_xor_sync(0xffffffffu, accQ, 1);
+        accP += __shfl_xor_sync(0xffffffffu, accP, 2);
+        accQ += __shfl_xor_sync(0xffffffffu, accQ, 2);
+        if (c == 0) {
+          rp[r] = accP;
+          rp[r + 8] = accQ;
+        }
+        hand_in(s, inf);
+        if (!wait_full(it + 1)) break;
+        inf = info[(it + 1) % NS];
+      }
     }
   }
 
@@ -859,13 +899,20 @@ static int set_family(D2Params& p, int mw, int ms, int mb, const uint32_t* w, co
 
 static bool gs_ok(int gs) { return gs == 32 || gs == 64 || gs == 128; }
 
+// The gate|up / qmv reduction splits into NCW equal slices of whole groups of
+// at most XR chunk columns each (a chunk column is 32 values).
+static bool xreg_split_ok(int K, int gs) {
+  const int ncc = K / (32 * NCW);
+  return K > 0 && K % (32 * NCW) == 0 && K % (8 * gs) == 0 && ncc % (gs / 32) == 0 && ncc <= XR;
+}
+
 }  // namespace d2
 
 using namespace d2;
 
 bool d2_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const void* s, const void* b) {
-  return gs_ok(gs) && N > 0 && N % ROWS_QMV == 0 && K > 0 && K % (8 * gs) == 0 && K % 256 == 0 &&
-         K / 256 <= XR && aligned16(x) && aligned16(w) && aligned16(s) && aligned16(b);
+  return gs_ok(gs) && N > 0 && N % ROWS_QMV == 0 && xreg_split_ok(K, gs) && aligned16(x) && aligned16(w) &&
+         aligned16(s) && aligned16(b);
 }
 
 int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b, uint16_t* y, int N, int K,
@@ -891,8 +938,8 @@ int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16
 }
 
 bool d2_moe_eligible(int H, int E, int F, int k, int gs) {
-  if (!(gs_ok(gs) && H > 0 && F > 0 && H % (8 * gs) == 0 && H % 256 == 0 && H / 256 <= XR &&
-        F % (8 * gs) == 0 && F % 256 == 0 && F % ROWS_GU == 0 && H % ROWS_DOWN == 0 && F / gs * 2 <= 512 &&
+  if (!(gs_ok(gs) && H > 0 && F > 0 && xreg_split_ok(H, gs) && F % (8 * gs) == 0 && F % 256 == 0 &&
+        (F / 128) % (gs / 32) == 0 && F % ROWS_GU == 0 && H % ROWS_DOWN == 0 && F / gs * 2 <= 512 &&
         k >= 1 && k <= MAXK && E >= k && E <= 1024 && d2_counter_words(H) * 4 <= 2048))
     return false;
   D2Params p;
