@@ -35,8 +35,9 @@
 //    legacy mma.sync m16n8k16 (bf16 x bf16 -> fp32) multiplies 16 weight rows
 //    (P: 8 rows, Q: 8 rows) by the activation chunk, each product exact in
 //    fp32; per group: s * (D - 128 * sum(x)) + b * sum(x) (the Metal qdot
-//    factorisation, quantized.h:191-290). For gate|up and qmv units the
-//    activation chunks of a warp's reduction slice stay in registers.
+//    factorisation, quantized.h:191-290) for down units; gate|up and qmv units
+//    (whose activation is the call's x) use integer MMAs on raw nibbles and
+//    an exact int8 split of x (see dot_i8).
 //  * Launches use programmatic dependent launch: barrier set-up, tensor-map
 //    prefetch and L2 prefetches (router rows; the first qmv units) run while
 //    the previous kernel in the stream finishes; nothing is read into the CTA
@@ -68,7 +69,6 @@ constexpr int ROWS_QMV = 16;         // rows of a qmv unit
 constexpr int ROWS_GU = 16;          // outputs of a gate|up unit (16 gate + 16 up rows)
 constexpr int ROWS_DOWN = 64;        // rows of a down unit
 constexpr int MISC_BYTES = 512;
-constexpr int XR = 8;                // activation chunks a consumer lane holds in registers
 
 enum : int { U_END = -1, U_GU = 0, U_DOWN = 1, U_QMV = 2 };
 enum : int { MW = 0, MS = 1, MB = 2, MWG = 0, MSG = 1, MBG = 2, MWU = 3, MSU = 4, MBU = 5, MWD = 6, MSD = 7, MBD = 8 };
@@ -136,60 +136,132 @@ __device__ __forceinline__ void mma_word_pair(float (&d)[4], uint32_t W0, uint32
   mma_bf16_16816(d, p2, q2, p3, q3, xv.z, xv.w);
 }
 
-// Activation held in registers (gate|up and qmv units): xr[i] is the chunk of
-// chunk column cc0 + i for this lane's c (i < ncc <= XR); NRB row blocks per
-// warp share each activation chunk.
-template <int CPG, int NRB>
-__device__ __forceinline__ void dot_xreg(const uint8_t* wbase, int PS, const int (&P0)[NRB], const int (&Q0)[NRB],
-                                         int cc0, int ncc, const uint4 (&xr)[XR], const float* gsum,
-                                         const Meta (&m)[NRB], float (&accP)[NRB], float (&accQ)[NRB]) {
-  constexpr int NGMAX = XR / CPG;
-  constexpr int NBW = NRB == 1 ? 4 : 2;       // groups per batch (fewer live accumulators with two row blocks)
-  constexpr int NB = NGMAX < NBW ? NGMAX : NBW;
+// ---------------------------------------------------------------------------
+// Units whose activation is the call's x (gate|up, qmv): integer MMAs.
+// x is held per group g as 16-bit fixed point X = round(x * 2^(14 - E_g))
+// (E_g: exponent of the group's max |x|; exact for every value within 2^7 of
+// the max, |X| < 2^15), split into int8 pieces hi = (X + 128) >> 8 and
+// lo = X - 256 hi. Weights go in as raw u8 nibbles (two masks per word), so
+// mma.sync m16n8k32 u8 x s8 -> s32 sums q * hi and q * lo exactly.
+// A "slot" is min(gs, 64) reduction values; in one MMA lane c of a quad
+// carries a word of slot 4t + c (rotated so the four lanes of a 16-byte unit
+// read different banks), and the B operand is zero except in columns 2c (hi
+// pieces) and 2c + 1 (lo pieces) at lane c's k-slots, so D[row][2c] and
+// D[row][2c + 1] -- registers d0, d1 of lane c -- are slot 4t + c's sums.
+// Per group: q.x = 2^(E_g - 14) * (256 * hi_sum + lo_sum), then
+// s * q.x + b * sum(x).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+constexpr int XB = 16;  // activation piece registers per lane (8 MMA steps x 2)
+
+// word of slot `slot` a lane c reads at step j (rotated inside each 4-word chunk)
+template <int WS>
+__device__ __forceinline__ int slot_word(int j, int c) {
+  return (j & ~3) + ((j + c) & 3);
+}
+
+// Builds this lane's B registers for the warp's slice [cc0, cc0 + ncc) chunk
+// columns of x (global, bf16); gsc[g].x = 2^(E_g - 14).
+template <int SLOT>
+__device__ __forceinline__ void build_pieces(const uint16_t* x, int cc0, int ncc, int gs, const float2* gsc,
+                                             uint32_t (&xb)[XB]) {
+  constexpr int WS = SLOT / 8, CPS = SLOT / 32;
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
-  const int ng = ncc / CPG;
-  const int g0 = cc0 / CPG;
-  const uint8_t* wl = wbase + r * 128 + c * 4;
+  const int nslot = ncc / CPS;
 #pragma unroll
-  for (int gb = 0; gb < NGMAX; gb += NB) {
-    if (gb < ng) {
-      float D[NRB][NB][4];
+  for (int i = 0; i < XB; ++i) xb[i] = 0u;
+  if ((r >> 1) != c) return;
 #pragma unroll
-      for (int j = 0; j < CPG; ++j) {
-        // every word of this step first, then the MMAs, consecutive ones on
-        // independent accumulators
-        uint32_t W0[NB][NRB], W8[NB][NRB];
+  for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int gi = 0; gi < NB; ++gi) {
-          const int i = (gb + gi) * CPG + j;
-          const int cc = cc0 + i;
-          const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4);
+    for (int j = 0; j < WS; ++j) {
+      const int st = t * WS + j;
+      const int slot = 4 * t + c;
+      if (st >= XB / 2 || slot >= nslot) continue;
+      const int w = slot_word<WS>(j, c);
+      const int k0 = (cc0 + slot * CPS) * 32 + w * 8;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + k0));
+      const float f = 1.0f / gsc[k0 / gs].x;  // a power of two
+      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+      uint32_t ev = 0u, od = 0u;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t h = (e & 1) ? (vw[e >> 1] & 0xffff0000u) : (vw[e >> 1] << 16);
+        const int X = __float2int_rn(__uint_as_float(h) * f);
+        const int hi = (X + 128) >> 8;
+        const int piece = (r & 1) ? X - (hi << 8) : hi;
+        const uint32_t byte = (uint32_t)piece & 0xffu;
+        if (e & 1)
+          od |= byte << (8 * (e >> 1));
+        else
+          ev |= byte << (8 * (e >> 1));
+      }
+      xb[2 * st] = ev;
+      xb[2 * st + 1] = od;
+    }
+}
+
+template <int SLOT, int NRB>
+__device__ __forceinline__ void dot_i8(const uint8_t* wbase, int PS, const int (&P0)[NRB], const int (&Q0)[NRB],
+                                       int cc0, int ncc, int gs, const uint32_t (&xb)[XB], const float2* gsc,
+                                       const Meta (&m)[NRB], float (&accP)[NRB], float (&accQ)[NRB]) {
+  constexpr int WS = SLOT / 8, CPS = SLOT / 32;
+  const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+  const int nslot = ncc / CPS;
+  const uint8_t* wl = wbase + r * 128;
+  const int spg = gs / SLOT;  // slots per group (1 or 2)
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    if (4 * t < nslot) {
+      const int slot = 4 * t + c;
+      const bool live = slot < nslot;
+      int D[NRB][2][4];
+#pragma unroll
+      for (int b = 0; b < NRB; ++b)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) D[b][h][0] = D[b][h][1] = D[b][h][2] = D[b][h][3] = 0;
+#pragma unroll
+      for (int j = 0; j < WS; ++j) {
+        const int st = t * WS + j;
+        if (st < XB / 2) {
+          const int w = slot_word<WS>(j, c);
+          const int cc = cc0 + slot * CPS + (w >> 2);
+          const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4) + 4 * (w & 3);
 #pragma unroll
           for (int b = 0; b < NRB; ++b) {
-            const bool live = gb + gi < ng;
-            W0[gi][b] = live ? *reinterpret_cast<const uint32_t*>(wp + P0[b]) : 0u;
-            W8[gi][b] = live ? *reinterpret_cast<const uint32_t*>(wp + Q0[b]) : 0u;
+            const uint32_t W0 = live ? *reinterpret_cast<const uint32_t*>(wp + P0[b]) : 0u;
+            const uint32_t W8 = live ? *reinterpret_cast<const uint32_t*>(wp + Q0[b]) : 0u;
+            imma_u8s8(D[b][j & 1], W0 & 0x0F0F0F0Fu, W8 & 0x0F0F0F0Fu, (W0 >> 4) & 0x0F0F0F0Fu,
+                      (W8 >> 4) & 0x0F0F0F0Fu, xb[2 * st], xb[2 * st + 1]);
           }
         }
-#pragma unroll
-        for (int b = 0; b < NRB; ++b)
-#pragma unroll
-          for (int gi = 0; gi < NB; ++gi) {
-            const int i = (gb + gi) * CPG + j;
-            mma_word_pair(D[b][gi], W0[gi][b], W8[gi][b], xr[i < XR ? i : 0], j == 0);
-          }
       }
-      const int gl = gb + c;
-      const float xa = gsum[gl < ng ? gl : 0];
+      // lane c: slot 4t + c of P row r (d0 hi, d1 lo) and Q row r (d2, d3)
+      const int sa = cc0 / CPS + slot;  // slot index in the whole reduction
 #pragma unroll
       for (int b = 0; b < NRB; ++b) {
-        float eP = D[b][0][0], eQ = D[b][0][2];
-#pragma unroll
-        for (int gi = 1; gi < NB; ++gi) {
-          eP = (c == gi) ? D[b][gi][0] : eP;
-          eQ = (c == gi) ? D[b][gi][2] : eQ;
+        int vP = 256 * (D[b][0][0] + D[b][1][0]) + (D[b][0][1] + D[b][1][1]);
+        int vQ = 256 * (D[b][0][2] + D[b][1][2]) + (D[b][0][3] + D[b][1][3]);
+        if (spg == 2) {  // two slots per group: lanes c and c ^ 1 hold one group
+          vP += __shfl_xor_sync(0xffffffffu, vP, 1);
+          vQ += __shfl_xor_sync(0xffffffffu, vQ, 1);
         }
-        if (c < NB && gl < ng) group_epilogue(m[b], g0 + gl, xa, eP, eQ, accP[b], accQ[b]);
+        if (live && (spg == 1 || (c & 1) == 0)) {
+          const int g = sa / spg;
+          const float2 sc = gsc[g];
+          const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
+          const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
+          const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw)));
+          const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw)));
+          accP[b] = fmaf(sP, (float)vP * sc.x, fmaf(bP, sc.y, accP[b]));
+          accQ[b] = fmaf(sQ, (float)vQ * sc.x, fmaf(bQ, sc.y, accQ[b]));
+        }
       }
     }
   }
@@ -264,6 +336,7 @@ __device__ void softmax_k(float selv, int k, float* sw) {
 // ---------------------------------------------------------------------------
 template <int CPG, int MODE>
 __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Params p) {
+  constexpr int SLOT = CPG == 1 ? 32 : 64;  // reduction values per column slot of the integer MMAs
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr bool FUSED = MODE != D2_QMV;
@@ -283,7 +356,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   int* lslot = reinterpret_cast<int*>(sw + MAXK);                // [MAXK] routed slots held here (EP)
   float* rsum = reinterpret_cast<float*>(lslot + MAXK);          // [NCW + 1]
   float* red = reinterpret_cast<float*>(smem + p.off_red);       // [nstage][NCW][32]
-  float* xsum = reinterpret_cast<float*>(smem + p.off_xs);
+  float2* gsc = reinterpret_cast<float2*>(smem + p.off_xs);     // per group: 2^(E_g - 14), sum(x)
   unsigned* done = p.ctr + 4;
   unsigned* comb = p.ctr + D2_CTR_FIXED;
 
@@ -356,7 +429,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       atomicAdd(&p.ctr[0], (unsigned)rows);
     }
   }
-  // ---- per-group sums of x ----
+  // ---- per group of x: the fixed-point scale 2^(E_g - 14) and sum(x) ----
   {
     const int nch = K1 / 8;
     for (int q0 = 0; q0 < nch; q0 += NTH) {
@@ -365,22 +438,32 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (live) v = __ldg(reinterpret_cast<const uint4*>(p.x) + q);
       float s = ((lbf(v.x) + hbf(v.x)) + (lbf(v.y) + hbf(v.y))) + ((lbf(v.z) + hbf(v.z)) + (lbf(v.w) + hbf(v.w)));
+      unsigned mx = max(max(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), max(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
+      mx = max(mx & 0xffffu, mx >> 16);  // bf16 bits of the chunk's max |x|
 #pragma unroll
-      for (int off = 1; off < CPC; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      if (live && (q % CPC) == 0) xsum[q / CPC] = s;
+      for (int off = 1; off < CPC; off <<= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, off);
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      }
+      if (live && (q % CPC) == 0) {
+        // exponent of the max; zero, infinite or NaN maxima take 0 (values
+        // then saturate: no defined result for non-finite inputs)
+        int e = (int)((mx >> 7) & 0xffu) - 127;
+        if (mx == 0u || mx >= 0x7f80u) e = 0;
+        e = max(-110, min(120, e));
+        gsc[q / CPC] = make_float2(__int_as_float((127 + e - 14) << 23), s);
+      }
     }
   }
-  // ---- the consumer warp's activation chunks, pair-permuted, in registers ----
-  uint4 xr[XR];
+  __syncthreads();
+  // ---- the consumer lane's activation pieces (B operands) in registers ----
+  uint32_t xb[XB];
   const int ncc1 = K1 / 32 / NCW, cc01 = (warp < NCW ? warp : 0) * ncc1;
-  {
-    const int c = lane & 3;
+  if (warp < NCW)
+    build_pieces<SLOT>(p.x, cc01, ncc1, p.gs, gsc, xb);
+  else
 #pragma unroll
-    for (int i = 0; i < XR; ++i) {
-      xr[i] = make_uint4(0u, 0u, 0u, 0u);
-      if (warp < NCW && i < ncc1) xr[i] = perm_x8(__ldg(reinterpret_cast<const uint4*>(p.x) + 4 * (cc01 + i) + c));
-    }
-  }
+    for (int i = 0; i < XB; ++i) xb[i] = 0u;
   // ---- routing (fused): every CTA ranks the same logits ----
   if (FUSED) {
     if (tid == 0 && !wait_counter_geq(&p.ctr[0], (unsigned)p.E, deadline, abort_flag)) {
@@ -647,7 +730,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         const int ub = ROWS_GU * K1 / 2;  // the up rows' box
         const int P0[2] = {0, 1024}, Q0[2] = {ub, ub + 1024};
         float accP[2] = {0.0f, 0.0f}, accQ[2] = {0.0f, 0.0f};
-        dot_xreg<CPG, 2>(st, ROWS_GU * 128, P0, Q0, cc01, ncc1, xr, xsum + cc01 / CPG, m, accP, accQ);
+        dot_i8<SLOT, 2>(st, ROWS_GU * 128, P0, Q0, cc01, ncc1, p.gs, xb, gsc, m, accP, accQ);
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
           accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 1);
@@ -663,7 +746,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         const Meta m[1] = {{mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, r, 8 + r, p.mb1, p.sw1 != 0}};
         const int P0[1] = {0}, Q0[1] = {1024};
         float accP[1] = {0.0f}, accQ[1] = {0.0f};
-        dot_xreg<CPG, 1>(st, ROWS_QMV * 128, P0, Q0, cc01, ncc1, xr, xsum + cc01 / CPG, m, accP, accQ);
+        dot_i8<SLOT, 1>(st, ROWS_QMV * 128, P0, Q0, cc01, ncc1, p.gs, xb, gsc, m, accP, accQ);
         accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 1);
         accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 1);
         accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 2);
@@ -768,7 +851,7 @@ static int plan(D2Params& p, int mode) {
   if (rc) return rc;
   // stages first (1024-aligned), then the group sums of x, the warp partials
   // of every stage and the barriers / routing state
-  const int xs_bytes = round_up(K1 / p.gs * 4, 128);
+  const int xs_bytes = round_up(K1 / p.gs * 8, 128);
   int ns = MAXST;
   for (; ns >= 2; --ns) {
     const int total = ns * p.stage_bytes + xs_bytes + ns * NCW * 32 * 4 + MISC_BYTES + 1024;
@@ -902,8 +985,12 @@ static bool gs_ok(int gs) { return gs == 32 || gs == 64 || gs == 128; }
 // The gate|up / qmv reduction splits into NCW equal slices of whole groups of
 // at most XR chunk columns each (a chunk column is 32 values).
 static bool xreg_split_ok(int K, int gs) {
-  const int ncc = K / (32 * NCW);
-  return K > 0 && K % (32 * NCW) == 0 && K % (8 * gs) == 0 && ncc % (gs / 32) == 0 && ncc <= XR;
+  const int ncc = K / (32 * NCW);  // chunk columns per consumer warp
+  const int cps = gs == 32 ? 1 : 2;  // chunk columns per column slot
+  // whole groups per warp, at most two batches of four slots, at most XB / 2 MMA steps
+  const int nslot = ncc / cps, steps = ((nslot + 3) / 4) * (cps * 4);
+  return K > 0 && K % (32 * NCW) == 0 && K % (8 * gs) == 0 && ncc % (gs / 32) == 0 && ncc % cps == 0 &&
+         nslot <= 8 && steps <= XB / 2;
 }
 
 }  // namespace d2

@@ -33,11 +33,18 @@ def _layer_np(L):
 
 def _check_layer(b2q_mod, oracle, x, wr, L, k, gs, rows=None, bound=REL_L2):
     out, idx, w = b2q_mod.moe_prefill(x, wr, L, k, group_size=gs, return_routing=True)
-    lg = b2q_mod.router_logits(x, wr)
-    ridx, rw = oracle.route(_np(lg), k)
-    assert np.array_equal(_np(idx), ridx)
-    assert np.allclose(_np(w), rw, rtol=2e-6, atol=1e-7)
-    ref = oracle.moe_experts_prefill(_np(x), ridx, rw, _layer_np(L), k, group_size=gs, rows=rows)
+    # routing: the prefill's router GEMM sums in another fp32 order than the
+    # oracle's dot products, so the softmax weights agree to a few fp32 ulps
+    rl = oracle.router_logits(_np(x), _np(wr))
+    ridx, rw = oracle.route(rl, k)
+    # tokens whose k-th and (k+1)-th logits are not within fp32 summation noise
+    srt = -np.sort(-rl, axis=1)
+    clear = (srt[:, k - 1] - srt[:, k]) > 1e-4 * np.maximum(1.0, np.abs(srt[:, k - 1]))
+    assert clear.mean() > 0.95
+    assert np.array_equal(_np(idx)[clear], ridx[clear])
+    assert np.allclose(_np(w)[clear], rw[clear], rtol=2e-5, atol=1e-7)
+    # the expert products and combine, given the layer's own routing
+    ref = oracle.moe_experts_prefill(_np(x), _np(idx), _np(w), _layer_np(L), k, group_size=gs, rows=rows)
     got = _bf(_np(out))
     if rows is not None:
         got = got[np.asarray(rows)]
