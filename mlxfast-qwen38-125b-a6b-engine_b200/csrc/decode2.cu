@@ -527,8 +527,13 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       const uint64_t pol_keep = policy_evict_last();
       int lastf[MAXST];
       for (int i = 0; i < MAXST; ++i) lastf[i] = -1;
+      int s = -1;
+      uint32_t eph = 1u;  // parity of the empty phase the next reuse of stage s waits for
       for (int it = 0;; ++it) {
-        const int s = it % NS;
+        if (++s == NS) {
+          s = 0;
+          eph ^= 1u;
+        }
         unsigned u;
         if (FUSED) {
           u = nxt;
@@ -536,14 +541,14 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         } else {
           u = blockIdx.x + (unsigned)it * gridDim.x;
         }
-        if (it >= NS && !tc::wait(&empty[s], ((it / NS) - 1) & 1, deadline, abort_flag)) {
+        if (it >= NS && !tc::wait(&empty[s], eph, deadline, abort_flag)) {
           if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
           *abort_flag = 1;
         }
         if (u >= UT || *abort_flag) {
           info[s] = make_int4(U_END, 0, 0, 0);
           mbar_arrive(&full[s]);
-          lastf[s] = it;
+          lastf[s] = (int)(eph ^ 1u);
           break;
         }
         uint8_t* st = smem + (size_t)s * p.stage_bytes;
@@ -578,7 +583,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
             *abort_flag = 1;
             info[s] = make_int4(U_END, 0, 0, 0);
             mbar_arrive(&full[s]);
-            lastf[s] = it;
+            lastf[s] = (int)(eph ^ 1u);
             break;
           }
           fence_proxy_async_global();  // the copies below read what generic stores wrote
@@ -591,14 +596,14 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           bulk_g2s(st + p.st_act, p.ws_act + (size_t)z * F, (uint32_t)F * 2u, &full[s], pol_keep);
           bulk_g2s(st + p.st_asum, p.ws_asum + (size_t)z * (F / 8), (uint32_t)F / 2u, &full[s], pol_keep);
         }
-        lastf[s] = it;
+        lastf[s] = (int)(eph ^ 1u);
       }
       // let every copy issued land before the CTA exits (after an abort some
       // fills may never have been consumed): wait for the latest phase of
-      // every stage used, end markers included
+      // every stage used, end markers included (lastf: that fill's parity)
       const uint64_t dl = globaltimer() + 200000000ull;
       for (int i = 0; i < NS; ++i)
-        if (lastf[i] >= 0) tc::wait_until(&full[i], (lastf[i] / NS) & 1, dl);
+        if (lastf[i] >= 0) tc::wait_until(&full[i], (uint32_t)lastf[i], dl);
     }
     __syncwarp();
   } else {
@@ -607,9 +612,18 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
     // the consumers run two phases: units whose activation is in registers
     // (gate|up, qmv), then down units (their activation is in the stage).
     const int r = lane >> 2, c = lane & 3;
-    auto wait_full = [&](int it) -> bool {
-      const int s = it % NS;
-      if (!__all_sync(0xffffffffu, tc::wait(&full[s], (it / NS) & 1, deadline, abort_flag))) {
+    // stage and phase of the consumers' current unit
+    int cs = 0;
+    uint32_t cph = 0u;
+    auto advance = [&]() {
+      if (++cs == NS) {
+        cs = 0;
+        cph ^= 1u;
+      }
+    };
+    auto wait_full = [&]() -> bool {
+      const int s = cs;
+      if (!__all_sync(0xffffffffu, tc::wait(&full[s], cph, deadline, abort_flag))) {
         if (!*abort_flag && lane == 0) record_error(p.err, B2Q_ETIMEOUT);
         *abort_flag = 1;
         return false;
@@ -707,16 +721,15 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       if (lane == 0) mbar_arrive(&empty[s]);
     };
 
-    int it = 0;
     int4 inf = make_int4(U_END, 0, 0, 0);
     bool live = true;
     // ---- phase 1: gate|up (fused) or qmv units ----
-    for (;; ++it) {
-      if (!wait_full(it)) {
+    for (;; advance()) {
+      if (!wait_full()) {
         live = false;
         break;
       }
-      const int s = it % NS;
+      const int s = cs;
       inf = info[s];
       if (inf.x == U_END || inf.x == U_DOWN) break;
       const uint8_t* st = smem + (size_t)s * p.stage_bytes;
@@ -758,10 +771,10 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       }
       hand_in(s, inf);
     }
-    // ---- phase 2 (fused): down units; the unit at `it` has already been waited for ----
+    // ---- phase 2 (fused): down units; the current unit has already been waited for ----
     if (FUSED && live) {
-      for (;; ++it) {
-        const int s = it % NS;
+      for (;;) {
+        const int s = cs;
         if (inf.x != U_DOWN) break;
         const uint8_t* st = smem + (size_t)s * p.stage_bytes;
         float* rp = red + ((size_t)s * NCW + warp) * 32;
@@ -789,8 +802,9 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           rp[r + 8] = accQ;
         }
         hand_in(s, inf);
-        if (!wait_full(it + 1)) break;
-        inf = info[(it + 1) % NS];
+        advance();
+        if (!wait_full()) break;
+        inf = info[cs];
       }
     }
   }

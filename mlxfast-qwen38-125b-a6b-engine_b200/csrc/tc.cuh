@@ -43,13 +43,15 @@ __device__ __forceinline__ bool test_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded: false when the deadline passed or *abort became non-zero.
+// Bounded: false when the deadline passed or *abort became non-zero. The
+// clock is read once per 64 polls: many warps polling at once would otherwise
+// keep the special-register pipe busy.
 __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, uint64_t deadline, volatile int* abort) {
   if (test_wait(bar, parity)) return true;
-  for (;;) {
+  for (uint32_t n = 1;; ++n) {
     if (try_wait_sleep(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() > deadline) return false;
+    if ((n & 63u) == 0u && globaltimer() > deadline) return false;
   }
 }
 
