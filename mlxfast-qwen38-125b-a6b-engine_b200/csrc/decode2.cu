@@ -15,7 +15,7 @@
 //      down unit     64 rows of one routed expert's down matrix over the whole
 //                    expert width, their scales / biases, and the expert's
 //                    SwiGLU activations (with their chunk sums);
-//      qmv unit      16 rows of the matrix over the whole reduction.
+//      qmv unit      32 rows of the matrix over the whole reduction.
 //    Fused calls hand units out from a grid-wide counter in the order: all
 //    gate|up units slot by slot, then all down units slot by slot, so the down
 //    units of slot j start as soon as slot j's activations are final (a
@@ -65,7 +65,7 @@ constexpr int NCW = 16;              // consumer warps
 constexpr int NTH = (NCW + 1) * 32;  // + the producer warp
 constexpr int MAXK = 8;              // routed slots
 constexpr int MAXST = 6;             // stages at most
-constexpr int ROWS_QMV = 16;         // rows of a qmv unit
+constexpr int ROWS_QMV = 32;         // rows of a qmv unit (two 16-row MMA blocks)
 constexpr int ROWS_GU = 16;          // outputs of a gate|up unit (16 gate + 16 up rows)
 constexpr int ROWS_DOWN = 64;        // rows of a down unit
 constexpr int MISC_BYTES = 512;
@@ -166,11 +166,12 @@ __device__ __forceinline__ int slot_word(int j, int c) {
   return (j & ~3) + ((j + c) & 3);
 }
 
-// Builds this lane's B registers for the warp's slice [cc0, cc0 + ncc) chunk
-// columns of x (global, bf16); gsc[g].x = 2^(E_g - 14).
+// Staged activation pieces in shared memory: 16 bytes per word of 8 values,
+// [hi of values 0,2,4,6][hi of 1,3,5,7][lo of 0,2,4,6][lo of 1,3,5,7].
+// Builds this lane's B registers for the warp's slice of chunk columns
+// [cc0, cc0 + ncc): nonzero only in the two lanes of each quad column pair.
 template <int SLOT>
-__device__ __forceinline__ void build_pieces(const uint16_t* x, int cc0, int ncc, int gs, const float2* gsc,
-                                             uint32_t (&xb)[XB]) {
+__device__ __forceinline__ void load_pieces(const uint8_t* pieces, int cc0, int ncc, uint32_t (&xb)[XB]) {
   constexpr int WS = SLOT / 8, CPS = SLOT / 32;
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
   const int nslot = ncc / CPS;
@@ -185,36 +186,39 @@ __device__ __forceinline__ void build_pieces(const uint16_t* x, int cc0, int ncc
       const int slot = 4 * t + c;
       if (st >= XB / 2 || slot >= nslot) continue;
       const int w = slot_word<WS>(j, c);
-      const int k0 = (cc0 + slot * CPS) * 32 + w * 8;
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + k0));
-      const float f = 1.0f / gsc[k0 / gs].x;  // a power of two
-      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
-      uint32_t ev = 0u, od = 0u;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const uint32_t h = (e & 1) ? (vw[e >> 1] & 0xffff0000u) : (vw[e >> 1] << 16);
-        const int X = __float2int_rn(__uint_as_float(h) * f);
-        const int hi = (X + 128) >> 8;
-        const int piece = (r & 1) ? X - (hi << 8) : hi;
-        const uint32_t byte = (uint32_t)piece & 0xffu;
-        if (e & 1)
-          od |= byte << (8 * (e >> 1));
-        else
-          ev |= byte << (8 * (e >> 1));
-      }
-      xb[2 * st] = ev;
-      xb[2 * st + 1] = od;
+      const int wi = (cc0 + slot * CPS) * 4 + w;  // word of x
+      const uint2 v = *reinterpret_cast<const uint2*>(pieces + wi * 16 + (r & 1) * 8);
+      xb[2 * st] = v.x;
+      xb[2 * st + 1] = v.y;
     }
 }
 
-template <int SLOT, int NRB>
-__device__ __forceinline__ void dot_i8(const uint8_t* wbase, int PS, const int (&P0)[NRB], const int (&Q0)[NRB],
-                                       int cc0, int ncc, int gs, const uint32_t (&xb)[XB], const float2* gsc,
-                                       const Meta (&m)[NRB], float (&accP)[NRB], float (&accQ)[NRB]) {
+// Byte offset, inside a stage, of the word lane (r, c) reads at each step, for
+// P row r of row block 0 (boxes of `rows` rows: piece stride rows * 128).
+template <int SLOT>
+__device__ __forceinline__ void word_offsets(int cc0, int rows, uint32_t (&woff)[XB / 2]) {
   constexpr int WS = SLOT / 8, CPS = SLOT / 32;
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
-  const int nslot = ncc / CPS;
-  const uint8_t* wl = wbase + r * 128;
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int j = 0; j < WS; ++j) {
+      const int st = t * WS + j;
+      if (st >= XB / 2) continue;
+      const int slot = 4 * t + c;
+      const int w = slot_word<WS>(j, c);
+      const int cc = cc0 + slot * CPS + (w >> 2);
+      woff[st] = (uint32_t)((cc >> 3) * rows * 128 + r * 128 + (((cc & 7) ^ r) << 4) + 4 * (w & 3));
+    }
+}
+
+// Row block b's P rows start at b * bstride, its Q rows qoff further.
+template <int SLOT, int NRB>
+__device__ __forceinline__ void dot_i8(const uint8_t* st_base, const uint32_t (&woff)[XB / 2], int bstride, int qoff,
+                                       int slot0, int nslot, int gs, const uint32_t (&xb)[XB], const float2* gsc,
+                                       const Meta (&m)[NRB], float (&accP)[NRB], float (&accQ)[NRB]) {
+  constexpr int WS = SLOT / 8;
+  const int c = threadIdx.x & 3;
   const int spg = gs / SLOT;  // slots per group (1 or 2)
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
@@ -230,20 +234,18 @@ __device__ __forceinline__ void dot_i8(const uint8_t* wbase, int PS, const int (
       for (int j = 0; j < WS; ++j) {
         const int st = t * WS + j;
         if (st < XB / 2) {
-          const int w = slot_word<WS>(j, c);
-          const int cc = cc0 + slot * CPS + (w >> 2);
-          const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4) + 4 * (w & 3);
+          const uint8_t* wp = st_base + woff[st];
 #pragma unroll
           for (int b = 0; b < NRB; ++b) {
-            const uint32_t W0 = live ? *reinterpret_cast<const uint32_t*>(wp + P0[b]) : 0u;
-            const uint32_t W8 = live ? *reinterpret_cast<const uint32_t*>(wp + Q0[b]) : 0u;
+            const uint32_t W0 = live ? *reinterpret_cast<const uint32_t*>(wp + b * bstride) : 0u;
+            const uint32_t W8 = live ? *reinterpret_cast<const uint32_t*>(wp + b * bstride + qoff) : 0u;
             imma_u8s8(D[b][j & 1], W0 & 0x0F0F0F0Fu, W8 & 0x0F0F0F0Fu, (W0 >> 4) & 0x0F0F0F0Fu,
                       (W8 >> 4) & 0x0F0F0F0Fu, xb[2 * st], xb[2 * st + 1]);
           }
         }
       }
       // lane c: slot 4t + c of P row r (d0 hi, d1 lo) and Q row r (d2, d3)
-      const int sa = cc0 / CPS + slot;  // slot index in the whole reduction
+      const int g = (slot0 + slot) / spg;
 #pragma unroll
       for (int b = 0; b < NRB; ++b) {
         int vP = 256 * (D[b][0][0] + D[b][1][0]) + (D[b][0][1] + D[b][1][1]);
@@ -253,7 +255,6 @@ __device__ __forceinline__ void dot_i8(const uint8_t* wbase, int PS, const int (
           vQ += __shfl_xor_sync(0xffffffffu, vQ, 1);
         }
         if (live && (spg == 1 || (c & 1) == 0)) {
-          const int g = sa / spg;
           const float2 sc = gsc[g];
           const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
           const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
@@ -380,7 +381,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       // previous kernel wrote (L2 is the point of coherence)
       for (int i = 0; i < NS; ++i) {
         const unsigned u = blockIdx.x + (unsigned)i * gridDim.x;
-        if (u >= (unsigned)(p.N / ROWS_QMV)) break;
+        if (u >= (unsigned)((p.N + ROWS_QMV - 1) / ROWS_QMV)) break;
         asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
                          reinterpret_cast<uint64_t>(&p.map[MW])),
                      "r"(0), "r"((int)u * ROWS_QMV), "r"(0)
@@ -429,7 +430,10 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       atomicAdd(&p.ctr[0], (unsigned)rows);
     }
   }
-  // ---- per group of x: the fixed-point scale 2^(E_g - 14) and sum(x) ----
+  // ---- per group of x: the fixed-point scale 2^(E_g - 14), sum(x), and the
+  // int8 pieces of every word (staged at the end of the stage ring, which the
+  // producer does not fill before the block barrier after routing) ----
+  uint8_t* pieces = smem + (size_t)NS * p.stage_bytes - (size_t)K1 * 2;
   {
     const int nch = K1 / 8;
     for (int q0 = 0; q0 < nch; q0 += NTH) {
@@ -445,25 +449,42 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         s += __shfl_xor_sync(0xffffffffu, s, off);
         mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       }
-      if (live && (q % CPC) == 0) {
-        // exponent of the max; zero, infinite or NaN maxima take 0 (values
-        // then saturate: no defined result for non-finite inputs)
-        int e = (int)((mx >> 7) & 0xffu) - 127;
-        if (mx == 0u || mx >= 0x7f80u) e = 0;
-        e = max(-110, min(120, e));
-        gsc[q / CPC] = make_float2(__int_as_float((127 + e - 14) << 23), s);
+      // exponent of the group's max; zero, infinite or NaN maxima take 0 (values
+      // then saturate: no defined result for non-finite inputs)
+      int e = (int)((mx >> 7) & 0xffu) - 127;
+      if (mx == 0u || mx >= 0x7f80u) e = 0;
+      e = max(-110, min(120, e));
+      if (live && (q % CPC) == 0) gsc[q / CPC] = make_float2(__int_as_float((127 + e - 14) << 23), s);
+      if (live) {
+        const float f = __int_as_float((127 + 14 - e) << 23);  // 2^(14 - E_g)
+        const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+        uint32_t he = 0u, ho = 0u, le = 0u, lo = 0u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t h = (i & 1) ? (vw[i >> 1] & 0xffff0000u) : (vw[i >> 1] << 16);
+          const int X = __float2int_rn(__uint_as_float(h) * f);
+          const int hi = (X + 128) >> 8;
+          const uint32_t hb = (uint32_t)hi & 0xffu, lb = (uint32_t)(X - (hi << 8)) & 0xffu;
+          const int sh = 8 * (i >> 1);
+          if (i & 1) {
+            ho |= hb << sh;
+            lo |= lb << sh;
+          } else {
+            he |= hb << sh;
+            le |= lb << sh;
+          }
+        }
+        *reinterpret_cast<uint4*>(pieces + (size_t)q * 16) = make_uint4(he, ho, le, lo);
       }
     }
   }
   __syncthreads();
-  // ---- the consumer lane's activation pieces (B operands) in registers ----
-  uint32_t xb[XB];
+  // ---- the consumer lane's activation pieces (B operands) and word offsets ----
+  uint32_t xb[XB], woff[XB / 2];
   const int ncc1 = K1 / 32 / NCW, cc01 = (warp < NCW ? warp : 0) * ncc1;
-  if (warp < NCW)
-    build_pieces<SLOT>(p.x, cc01, ncc1, p.gs, gsc, xb);
-  else
-#pragma unroll
-    for (int i = 0; i < XB; ++i) xb[i] = 0u;
+  load_pieces<SLOT>(pieces, cc01, warp < NCW ? ncc1 : 0, xb);
+  word_offsets<SLOT>(cc01, FUSED ? ROWS_GU : ROWS_QMV, woff);
+  const int nslot1 = ncc1 / (SLOT / 32), slot01 = cc01 / (SLOT / 32);
   // ---- routing (fused): every CTA ranks the same logits ----
   if (FUSED) {
     if (tid == 0 && !wait_counter_geq(&p.ctr[0], (unsigned)p.E, deadline, abort_flag)) {
@@ -516,7 +537,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
 
   const int nloc = FUSED ? *nloc_sm : 0;
   const int F = p.F, H = p.H;
-  const unsigned U1 = FUSED ? (unsigned)(nloc * (F / ROWS_GU)) : (unsigned)(p.N / ROWS_QMV);
+  const unsigned U1 = FUSED ? (unsigned)(nloc * (F / ROWS_GU)) : (unsigned)((p.N + ROWS_QMV - 1) / ROWS_QMV);
   const unsigned U2 = FUSED ? (unsigned)(nloc * (H / ROWS_DOWN)) : 0u;
   const unsigned UT = U1 + U2;
 
@@ -709,11 +730,11 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
             if (lane == 0) comb[hb] = 0u;
           }
         } else {
-          if (lane < 16) {
-            float tot = 0.0f;
-            for (int w = 0; w < NCW; ++w) tot += rb[w * 32 + lane];
-            p.y[(size_t)inf.z * ROWS_QMV + lane] = f2bf(tot);
-          }
+          // row lane of the unit: partial slot lane ([P 0..7][Q 8..15][P 16..23][Q 24..31])
+          float tot = 0.0f;
+          for (int w = 0; w < NCW; ++w) tot += rb[w * 32 + lane];
+          const int row = inf.z * ROWS_QMV + lane;
+          if (row < p.N) p.y[row] = f2bf(tot);
         }
         if (lane == 0) arr[s] = 0u;
         __syncwarp();
@@ -741,9 +762,8 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
             {mb, mb + p.st_mstep1, mb + 2 * p.st_mstep1, mb + 3 * p.st_mstep1, r, r, p.mb1, p.sw1 != 0},
             {mb, mb + p.st_mstep1, mb + 2 * p.st_mstep1, mb + 3 * p.st_mstep1, 8 + r, 8 + r, p.mb1, p.sw1 != 0}};
         const int ub = ROWS_GU * K1 / 2;  // the up rows' box
-        const int P0[2] = {0, 1024}, Q0[2] = {ub, ub + 1024};
         float accP[2] = {0.0f, 0.0f}, accQ[2] = {0.0f, 0.0f};
-        dot_i8<SLOT, 2>(st, ROWS_GU * 128, P0, Q0, cc01, ncc1, p.gs, xb, gsc, m, accP, accQ);
+        dot_i8<SLOT, 2>(st, woff, 1024, ub, slot01, nslot1, p.gs, xb, gsc, m, accP, accQ);
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
           accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 1);
@@ -756,17 +776,21 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           }
         }
       } else {
-        const Meta m[1] = {{mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, r, 8 + r, p.mb1, p.sw1 != 0}};
-        const int P0[1] = {0}, Q0[1] = {1024};
-        float accP[1] = {0.0f}, accQ[1] = {0.0f};
-        dot_i8<SLOT, 1>(st, ROWS_QMV * 128, P0, Q0, cc01, ncc1, p.gs, xb, gsc, m, accP, accQ);
-        accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 1);
-        accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 1);
-        accP[0] += __shfl_xor_sync(0xffffffffu, accP[0], 2);
-        accQ[0] += __shfl_xor_sync(0xffffffffu, accQ[0], 2);
-        if (c == 0) {
-          rp[r] = accP[0];
-          rp[r + 8] = accQ[0];
+        // two row blocks of 16 rows (P: rows 16b..16b+7, Q: rows 16b+8..16b+15)
+        const Meta m[2] = {{mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, r, 8 + r, p.mb1, p.sw1 != 0},
+                           {mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, 16 + r, 24 + r, p.mb1, p.sw1 != 0}};
+        float accP[2] = {0.0f, 0.0f}, accQ[2] = {0.0f, 0.0f};
+        dot_i8<SLOT, 2>(st, woff, 2048, 1024, slot01, nslot1, p.gs, xb, gsc, m, accP, accQ);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 1);
+          accQ[b] += __shfl_xor_sync(0xffffffffu, accQ[b], 1);
+          accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 2);
+          accQ[b] += __shfl_xor_sync(0xffffffffu, accQ[b], 2);
+          if (c == 0) {
+            rp[16 * b + r] = accP[b];
+            rp[16 * b + 8 + r] = accQ[b];
+          }
         }
       }
       hand_in(s, inf);
@@ -1012,7 +1036,7 @@ static bool xreg_split_ok(int K, int gs) {
 using namespace d2;
 
 bool d2_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const void* s, const void* b) {
-  return gs_ok(gs) && N > 0 && N % ROWS_QMV == 0 && xreg_split_ok(K, gs) && aligned16(x) && aligned16(w) &&
+  return gs_ok(gs) && N >= ROWS_QMV && N % 16 == 0 && xreg_split_ok(K, gs) && aligned16(x) && aligned16(w) &&
          aligned16(s) && aligned16(b);
 }
 
