@@ -442,8 +442,9 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (live) v = __ldg(reinterpret_cast<const uint4*>(p.x) + q);
       float s = ((lbf(v.x) + hbf(v.x)) + (lbf(v.y) + hbf(v.y))) + ((lbf(v.z) + hbf(v.z)) + (lbf(v.w) + hbf(v.w)));
-      unsigned mx = max(max(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), max(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
-      mx = max(mx & 0xffffu, mx >> 16);  // bf16 bits of the chunk's max |x|
+      // bf16 bits of the chunk's max |x| (per-halfword maxima, then the two halves)
+      unsigned mx = __vmaxu2(__vmaxu2(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), __vmaxu2(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
+      mx = max(mx & 0xffffu, mx >> 16);
 #pragma unroll
       for (int off = 1; off < CPC; off <<= 1) {
         s += __shfl_xor_sync(0xffffffffu, s, off);

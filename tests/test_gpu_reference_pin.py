@@ -122,7 +122,9 @@ def test_fused_decode_c1_against_reference_products(cuda, b2q_mod, oracle, ref):
 def test_dequantize_against_both_rounding_variants(cuda, b2q_mod, oracle, gs):
     """A2: the CUDA dequantize is bit-exact with the tile-loader variant (ii),
     bf16(fp32(s) * q + fp32(b)); against the CPU-op variant (i), bf16(bf16(q * s) + b)
-    (ops.cpp:5322-5325), the mismatches are counted and each is one bf16 ulp."""
+    (ops.cpp:5322-5325), the mismatches are counted, and each differs by at most
+    the rounding of the intermediate q * s (one bf16 ulp of q * s) plus one ulp of
+    the result: where q * s and b nearly cancel, that is many ulps of the result."""
     from b2q import synth
 
     w, s, b = synth.packed_weights((64,), 2048, gs, seed=70 + gs)
@@ -134,6 +136,10 @@ def test_dequantize_against_both_rounding_variants(cuda, b2q_mod, oracle, gs):
     n = int(diff.sum())
     print(f"gs={gs}: {n} of {out.size} values differ from the CPU-op rounding variant (i)")
     if n:
-        ulp = np.abs(out[diff].astype(np.int32) - v1[diff].astype(np.int32))
-        same_sign = (out[diff] & 0x8000) == (v1[diff] & 0x8000)
-        assert np.all(ulp[same_sign] <= 1)
+        wq, sq = _np(w), _bf(_np(s))
+        q = ((wq[..., None] >> (4 * np.arange(8, dtype=np.uint32))) & 0xF).reshape(wq.shape[0], -1)
+        qs = np.abs(q * np.repeat(sq, gs, axis=1)).astype(np.float32)
+        ulp_of = lambda a: np.exp2(np.floor(np.log2(np.maximum(np.abs(a), 1e-30))) - 7)
+        a2, a1 = _bf(out), _bf(v1)
+        bound = ulp_of(qs) + ulp_of(a2)
+        assert np.all(np.abs(a2 - a1)[diff] <= bound[diff])
