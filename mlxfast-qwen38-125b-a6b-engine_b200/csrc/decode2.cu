@@ -399,40 +399,10 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
 
   const int K1 = p.K1;
   constexpr int CPC = CPG * 4;  // 8-value chunks per group
-  // ---- router rows of this CTA (fused) ----
-  if (FUSED) {
-    int rows = 0;
-    for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
-      float part = 0.0f;
-      const uint4* xr4 = reinterpret_cast<const uint4*>(p.x);
-      const uint4* wrow = reinterpret_cast<const uint4*>(p.wr + (size_t)e * p.H);
-      for (int v = tid; v < p.H / 8; v += NTH) {
-        const uint4 xv = __ldg(xr4 + v), wv = __ldg(wrow + v);
-        part += lbf(xv.x) * lbf(wv.x) + hbf(xv.x) * hbf(wv.x);
-        part += lbf(xv.y) * lbf(wv.y) + hbf(xv.y) * hbf(wv.y);
-        part += lbf(xv.z) * lbf(wv.z) + hbf(xv.z) * hbf(wv.z);
-        part += lbf(xv.w) * lbf(wv.w) + hbf(xv.w) * hbf(wv.w);
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-      if (lane == 0) rsum[warp] = part;
-      __syncthreads();
-      if (tid == 0) {
-        float lg = 0.0f;
-        for (int w = 0; w < NCW + 1; ++w) lg += rsum[w];
-        p.ws_logits[e] = lg;
-      }
-      __syncthreads();
-      ++rows;
-    }
-    if (tid == 0 && rows) {
-      __threadfence();
-      atomicAdd(&p.ctr[0], (unsigned)rows);
-    }
-  }
-  // ---- per group of x: the fixed-point scale 2^(E_g - 14), sum(x), and the
-  // int8 pieces of every word (staged at the end of the stage ring, which the
-  // producer does not fill before the block barrier after routing) ----
+  // ---- one pass over x: this CTA's router rows (fused), and per group of x
+  // the fixed-point scale 2^(E_g - 14), sum(x) and the int8 pieces of every
+  // word (staged at the end of the stage ring, which the producer does not
+  // fill before the block barrier after routing) ----
   uint8_t* pieces = smem + (size_t)NS * p.stage_bytes - (size_t)K1 * 2;
   {
     const int nch = K1 / 8;
@@ -441,6 +411,35 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       const bool live = q < nch;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (live) v = __ldg(reinterpret_cast<const uint4*>(p.x) + q);
+      if (FUSED && q0 == 0 && nch <= NTH) {
+        // router rows e = blockIdx.x + i * grid (x word q of each)
+        int rows = 0;
+        for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
+          float part = 0.0f;
+          if (live) {
+            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.wr + (size_t)e * p.H) + q);
+            part = lbf(v.x) * lbf(wv.x) + hbf(v.x) * hbf(wv.x);
+            part += lbf(v.y) * lbf(wv.y) + hbf(v.y) * hbf(wv.y);
+            part += lbf(v.z) * lbf(wv.z) + hbf(v.z) * hbf(wv.z);
+            part += lbf(v.w) * lbf(wv.w) + hbf(v.w) * hbf(wv.w);
+          }
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+          if (lane == 0) rsum[warp] = part;
+          __syncthreads();
+          if (tid == 0) {
+            float lg = 0.0f;
+            for (int w = 0; w < NCW + 1; ++w) lg += rsum[w];
+            p.ws_logits[e] = lg;
+          }
+          __syncthreads();
+          ++rows;
+        }
+        if (tid == 0 && rows) {
+          __threadfence();
+          atomicAdd(&p.ctr[0], (unsigned)rows);
+        }
+      }
       float s = ((lbf(v.x) + hbf(v.x)) + (lbf(v.y) + hbf(v.y))) + ((lbf(v.z) + hbf(v.z)) + (lbf(v.w) + hbf(v.w)));
       // bf16 bits of the chunk's max |x| (per-halfword maxima, then the two halves)
       unsigned mx = __vmaxu2(__vmaxu2(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), __vmaxu2(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
@@ -486,52 +485,66 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   load_pieces<SLOT>(pieces, cc01, warp < NCW ? ncc1 : 0, xb);
   word_offsets<SLOT>(cc01, FUSED ? ROWS_GU : ROWS_QMV, woff);
   const int nslot1 = ncc1 / (SLOT / 32), slot01 = cc01 / (SLOT / 32);
-  // ---- routing (fused): every CTA ranks the same logits ----
-  if (FUSED) {
-    if (tid == 0 && !wait_counter_geq(&p.ctr[0], (unsigned)p.E, deadline, abort_flag)) {
-      record_error(p.err, B2Q_ETIMEOUT);
+  // ---- routing (fused): every CTA selects the same top-k in warp 0 ----
+  if (FUSED && warp == 0) {
+    bool ok = true;
+    if (lane == 0) ok = wait_counter_geq(&p.ctr[0], (unsigned)p.E, deadline, abort_flag);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) {
+      if (lane == 0) record_error(p.err, B2Q_ETIMEOUT);
       *abort_flag = 1;
     }
-    __syncthreads();
-    float* lgs = reinterpret_cast<float*>(smem);  // stage 0 is free until the producer starts
-    float* sval = lgs + p.E;
-    for (int e = tid; e < p.E; e += NTH) {
-      const float v = *abort_flag ? 0.0f : __ldcg(p.ws_logits + e);
-      lgs[e] = (v != v) ? -INFINITY : v;
-    }
-    __syncthreads();
-    // expert e takes slot rank(e) when rank(e) < k, rank(e) = #{j : v_j > v_e or
-    // (v_j == v_e and j < e)}: largest first, ties to the lower index
-    for (int e = tid; e < p.E; e += NTH) {
-      const float v = lgs[e];
-      int rank = 0;
-      for (int j = 0; j < p.E; ++j) {
-        const float vj = lgs[j];
-        rank += (vj > v || (vj == v && j < e)) ? 1 : 0;
-      }
-      if (rank < p.k) {
-        sidx[rank] = (uint32_t)e;
-        sval[rank] = v;
+    // lane l holds experts l, l + 32, ... as orderable keys: larger value first,
+    // ties to the lower index (the reference's stable selection), NaN as -inf
+    constexpr int EPL = 8;  // experts per lane at most (E <= 256)
+    unsigned long long key[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      key[i] = 0ull;
+      if (e < p.E) {
+        float v = ok ? __ldcg(p.ws_logits + e) : 0.0f;
+        if (v != v) v = -INFINITY;
+        uint32_t u = __float_as_uint(v);
+        u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving map
+        key[i] = ((unsigned long long)u << 32) | (0xffffffffu - (uint32_t)e);
       }
     }
-    __syncthreads();
-    if (warp == 0) {
-      softmax_k(lane < p.k ? sval[lane] : -INFINITY, p.k, sw);
-      __syncwarp();
-      if (blockIdx.x == 0 && lane < p.k) {
-        if (p.idx_out) p.idx_out[lane] = sidx[lane];
-        if (p.w_out) p.w_out[lane] = sw[lane];
+    float selv = -INFINITY;
+    for (int slot = 0; slot < p.k; ++slot) {
+      unsigned long long best = 0ull;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) best = key[i] > best ? key[i] : best;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+        best = o > best ? o : best;
       }
-      if (blockIdx.x == 0 && p.logits_out)
-        for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
-      if (lane == 0) {
-        int n = 0;
-        for (int s = 0; s < p.k; ++s) {
-          const int e = (int)sidx[s];
-          if (!EP || (e >= p.e_lo && e < p.e_lo + p.e_local)) lslot[n++] = s;
-        }
-        *nloc_sm = n;
+      const int e = (int)(0xffffffffu - (uint32_t)best);
+      uint32_t u = (uint32_t)(best >> 32);
+      u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+      if (lane == slot) selv = __uint_as_float(u);
+      if (lane == 0) sidx[slot] = (uint32_t)e;
+      if ((e & 31) == lane)
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+          if (i == (e >> 5)) key[i] = 0ull;  // taken
+    }
+    softmax_k(selv, p.k, sw);
+    __syncwarp();
+    if (blockIdx.x == 0 && lane < p.k) {
+      if (p.idx_out) p.idx_out[lane] = sidx[lane];
+      if (p.w_out) p.w_out[lane] = sw[lane];
+    }
+    if (blockIdx.x == 0 && p.logits_out)
+      for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
+    if (lane == 0) {
+      int n = 0;
+      for (int s2 = 0; s2 < p.k; ++s2) {
+        const int e = (int)sidx[s2];
+        if (!EP || (e >= p.e_lo && e < p.e_lo + p.e_local)) lslot[n++] = s2;
       }
+      *nloc_sm = n;
     }
   }
   __syncthreads();
@@ -662,85 +675,93 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         old = atomicAdd(&arr[s], 1u);
       }
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == NCW - 1) {
+      const bool finisher = old == NCW - 1;
+      // the finisher takes what it needs from the partials into registers and
+      // releases the stage before its global stores, fences and atomics
+      float t0 = 0.0f, t1 = 0.0f;
+      if (finisher) {
         __threadfence_block();
         const float* rb = red + (size_t)s * NCW * 32;
-        if (FUSED && inf.x == U_GU) {
-          // lane l: total of row l of the warp partials ([gate 0..7][up 0..7][gate 8..15][up 8..15])
-          const int z = inf.y, blk = inf.z;
-          float tot = 0.0f;
-          for (int w = 0; w < NCW; ++w) tot += rb[w * 32 + lane];
-          const int f = lane & 15;  // output of lanes 0..15
-          const float g = __shfl_sync(0xffffffffu, tot, 16 * (f >> 3) + (f & 7));
-          const float up = __shfl_sync(0xffffffffu, tot, 16 * (f >> 3) + 8 + (f & 7));
-          uint16_t a = 0;
-          if (lane < 16) {
-            a = swiglu_bf16(f2bf(g), f2bf(up));
-            const int j = f & 7, pos = j < 4 ? 2 * j : 2 * (j - 4) + 1;
-            p.ws_act[(size_t)z * F + blk * ROWS_GU + (f >> 3) * 8 + pos] = a;
-          }
-          float af = lane < 16 ? bf2f(a) : 0.0f;
-          af += __shfl_xor_sync(0xffffffffu, af, 1);
-          af += __shfl_xor_sync(0xffffffffu, af, 2);
-          af += __shfl_xor_sync(0xffffffffu, af, 4);
-          if (lane == 0 || lane == 8) p.ws_asum[(size_t)z * (F / 8) + blk * 2 + (lane >> 3)] = af;
-          __threadfence();
-          __syncwarp();
-          if (lane == 0) red_release_add_u32(&done[z], 1u);
-        } else if (FUSED) {
-          const int z = inf.y, hb = inf.z;
+        if (FUSED && inf.x == U_DOWN) {
           // rows lane and lane + 32 of the unit: row i is block i / 16, partial row i % 16
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             const int i = lane + 32 * h2, b = i >> 4, j = i & 15;
             const float y2 = (rb[(4 * b) * 32 + j] + rb[(4 * b + 1) * 32 + j]) +
                              (rb[(4 * b + 2) * 32 + j] + rb[(4 * b + 3) * 32 + j]);
-            p.ws_y[(size_t)z * H + hb * ROWS_DOWN + i] = f2bf(y2);
-          }
-          __threadfence();
-          __syncwarp();
-          unsigned prev = 0;
-          if (lane == 0) prev = atomicAdd(&comb[hb], 1u);
-          prev = __shfl_sync(0xffffffffu, prev, 0);
-          if (prev == (unsigned)(nloc - 1)) {
-            // every slot's rows of this block are in: y_j = bf16 product,
-            // prod_j = y_j * w_j, folded in the mlx_colsum_small_f32 order
-            __threadfence();
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-              const int h = hb * ROWS_DOWN + lane + 32 * h2;
-              float prod[MAXK];
-#pragma unroll
-              for (int s2 = 0; s2 < MAXK; ++s2)
-                prod[s2] = s2 < nloc ? bf2f(__ldcg(p.ws_y + (size_t)s2 * H + h)) * sw[EP ? lslot[s2] : s2] : 0.0f;
-              const int TY = nloc < 8 ? nloc : 8;
-              float total = 0.0f;
-#pragma unroll
-              for (int q = 0; q < MAXK; ++q) {
-                if (q < TY) {
-                  float a2 = 0.0f;
-                  for (int s2 = q; s2 < nloc; s2 += TY) a2 = prod[s2] + a2;
-                  total = (q == 0) ? a2 : a2 + total;
-                }
-              }
-              if (EP)
-                p.out_f32[h] = total;
-              else
-                p.out[h] = f2bf(total);
-            }
-            if (lane == 0) comb[hb] = 0u;
+            if (h2 == 0) t0 = y2; else t1 = y2;
           }
         } else {
-          // row lane of the unit: partial slot lane ([P 0..7][Q 8..15][P 16..23][Q 24..31])
-          float tot = 0.0f;
-          for (int w = 0; w < NCW; ++w) tot += rb[w * 32 + lane];
-          const int row = inf.z * ROWS_QMV + lane;
-          if (row < p.N) p.y[row] = f2bf(tot);
+          // lane l: total of partial row l over the warps
+          for (int w = 0; w < NCW; ++w) t0 += rb[w * 32 + lane];
         }
         if (lane == 0) arr[s] = 0u;
         __syncwarp();
       }
       if (lane == 0) mbar_arrive(&empty[s]);
+      if (!finisher) return;
+      if (FUSED && inf.x == U_GU) {
+        // t0 at lane l: row l of [gate 0..7][up 0..7][gate 8..15][up 8..15]
+        const int z = inf.y, blk = inf.z;
+        const int f = lane & 15;  // output of lanes 0..15
+        const float g = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + (f & 7));
+        const float up = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + 8 + (f & 7));
+        uint16_t a = 0;
+        if (lane < 16) {
+          a = swiglu_bf16(f2bf(g), f2bf(up));
+          const int j = f & 7, pos = j < 4 ? 2 * j : 2 * (j - 4) + 1;
+          p.ws_act[(size_t)z * F + blk * ROWS_GU + (f >> 3) * 8 + pos] = a;
+        }
+        float af = lane < 16 ? bf2f(a) : 0.0f;
+        af += __shfl_xor_sync(0xffffffffu, af, 1);
+        af += __shfl_xor_sync(0xffffffffu, af, 2);
+        af += __shfl_xor_sync(0xffffffffu, af, 4);
+        if (lane == 0 || lane == 8) p.ws_asum[(size_t)z * (F / 8) + blk * 2 + (lane >> 3)] = af;
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) red_release_add_u32(&done[z], 1u);
+      } else if (FUSED) {
+        const int z = inf.y, hb = inf.z;
+        p.ws_y[(size_t)z * H + hb * ROWS_DOWN + lane] = f2bf(t0);
+        p.ws_y[(size_t)z * H + hb * ROWS_DOWN + lane + 32] = f2bf(t1);
+        __threadfence();
+        __syncwarp();
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(&comb[hb], 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == (unsigned)(nloc - 1)) {
+          // every slot's rows of this block are in: y_j = bf16 product,
+          // prod_j = y_j * w_j, folded in the mlx_colsum_small_f32 order
+          __threadfence();
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int h = hb * ROWS_DOWN + lane + 32 * h2;
+            float prod[MAXK];
+#pragma unroll
+            for (int s2 = 0; s2 < MAXK; ++s2)
+              prod[s2] = s2 < nloc ? bf2f(__ldcg(p.ws_y + (size_t)s2 * H + h)) * sw[EP ? lslot[s2] : s2] : 0.0f;
+            const int TY = nloc < 8 ? nloc : 8;
+            float total = 0.0f;
+#pragma unroll
+            for (int q = 0; q < MAXK; ++q) {
+              if (q < TY) {
+                float a2 = 0.0f;
+                for (int s2 = q; s2 < nloc; s2 += TY) a2 = prod[s2] + a2;
+                total = (q == 0) ? a2 : a2 + total;
+              }
+            }
+            if (EP)
+              p.out_f32[h] = total;
+            else
+              p.out[h] = f2bf(total);
+          }
+          if (lane == 0) comb[hb] = 0u;
+        }
+      } else {
+        // row lane of the unit: partial slot lane ([P 0..7][Q 8..15][P 16..23][Q 24..31])
+        const int row = inf.z * ROWS_QMV + lane;
+        if (row < p.N) p.y[row] = f2bf(t0);
+      }
     };
 
     int4 inf = make_int4(U_END, 0, 0, 0);
@@ -1066,7 +1087,7 @@ int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16
 bool d2_moe_eligible(int H, int E, int F, int k, int gs) {
   if (!(gs_ok(gs) && H > 0 && F > 0 && xreg_split_ok(H, gs) && F % (8 * gs) == 0 && F % 256 == 0 &&
         (F / 128) % (gs / 32) == 0 && F % ROWS_GU == 0 && H % ROWS_DOWN == 0 && F / gs * 2 <= 512 &&
-        k >= 1 && k <= MAXK && E >= k && E <= 1024 && d2_counter_words(H) * 4 <= 2048))
+        k >= 1 && k <= MAXK && E >= k && E <= 256 && H / 8 <= NTH && d2_counter_words(H) * 4 <= 2048))
     return false;
   D2Params p;
   std::memset(&p, 0, sizeof(p));
