@@ -356,6 +356,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   float* sw = reinterpret_cast<float*>(sidx + MAXK);             // [MAXK] their weights
   int* lslot = reinterpret_cast<int*>(sw + MAXK);                // [MAXK] routed slots held here (EP)
   float* rsum = reinterpret_cast<float*>(lslot + MAXK);          // [NCW + 1]
+  int* lastf_sm = reinterpret_cast<int*>(rsum + NCW + 1);        // [MAXST] producer bookkeeping
   float* red = reinterpret_cast<float*>(smem + p.off_red);       // [nstage][NCW][32]
   float2* gsc = reinterpret_cast<float2*>(smem + p.off_xs);     // per group: 2^(E_g - 14), sum(x)
   unsigned* done = p.ctr + 4;
@@ -494,41 +495,40 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       if (lane == 0) record_error(p.err, B2Q_ETIMEOUT);
       *abort_flag = 1;
     }
-    // lane l holds experts l, l + 32, ... as orderable keys: larger value first,
-    // ties to the lower index (the reference's stable selection), NaN as -inf
-    constexpr int EPL = 8;  // experts per lane at most (E <= 256)
-    unsigned long long key[EPL];
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-      const int e = lane + 32 * i;
-      key[i] = 0ull;
-      if (e < p.E) {
-        float v = ok ? __ldcg(p.ws_logits + e) : 0.0f;
-        if (v != v) v = -INFINITY;
-        uint32_t u = __float_as_uint(v);
-        u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving map
-        key[i] = ((unsigned long long)u << 32) | (0xffffffffu - (uint32_t)e);
-      }
+    // logits to shared memory (stage 0 is free until the producer starts), NaN as -inf
+    float* lgs = reinterpret_cast<float*>(smem);
+    for (int e = lane; e < p.E; e += 32) {
+      float v = ok ? __ldcg(p.ws_logits + e) : 0.0f;
+      lgs[e] = (v != v) ? -INFINITY : v;
     }
+    __syncwarp();
+    // k rounds of a warp arg-max over orderable keys (larger value first, ties
+    // to the lower index: the reference's stable selection); lane l scans
+    // experts l, l + 32, ... and remembers the ones taken in a bit mask
+    constexpr int EPL = 8;  // experts per lane at most (E <= 256)
+    uint32_t taken = 0u;
     float selv = -INFINITY;
     for (int slot = 0; slot < p.k; ++slot) {
       unsigned long long best = 0ull;
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) best = key[i] > best ? key[i] : best;
+      for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        if (e < p.E && !((taken >> i) & 1u)) {
+          uint32_t u = __float_as_uint(lgs[e]);
+          u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving map
+          const unsigned long long key = ((unsigned long long)u << 32) | (0xffffffffu - (uint32_t)e);
+          best = key > best ? key : best;
+        }
+      }
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) {
         const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
         best = o > best ? o : best;
       }
       const int e = (int)(0xffffffffu - (uint32_t)best);
-      uint32_t u = (uint32_t)(best >> 32);
-      u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
-      if (lane == slot) selv = __uint_as_float(u);
+      if (lane == slot) selv = lgs[e];
       if (lane == 0) sidx[slot] = (uint32_t)e;
-      if ((e & 31) == lane)
-#pragma unroll
-        for (int i = 0; i < EPL; ++i)
-          if (i == (e >> 5)) key[i] = 0ull;  // taken
+      if ((e & 31) == lane) taken |= 1u << (e >> 5);
     }
     softmax_k(selv, p.k, sw);
     __syncwarp();
@@ -560,7 +560,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       const uint64_t pol_keep = policy_evict_last();
-      int lastf[MAXST];
+      int* lastf = lastf_sm;  // parity of each stage's latest fill, -1 before the first
       for (int i = 0; i < MAXST; ++i) lastf[i] = -1;
       int s = -1;
       uint32_t eph = 1u;  // parity of the empty phase the next reuse of stage s waits for
@@ -736,17 +736,16 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             const int h = hb * ROWS_DOWN + lane + 32 * h2;
-            float prod[MAXK];
+            // with nloc <= 8 slots the colsum association has one product per
+            // chain (chain q = 0 + prod_q) and folds the chains in slot order
+            float yv[MAXK];
 #pragma unroll
-            for (int s2 = 0; s2 < MAXK; ++s2)
-              prod[s2] = s2 < nloc ? bf2f(__ldcg(p.ws_y + (size_t)s2 * H + h)) * sw[EP ? lslot[s2] : s2] : 0.0f;
-            const int TY = nloc < 8 ? nloc : 8;
+            for (int s2 = 0; s2 < MAXK; ++s2) yv[s2] = s2 < nloc ? bf2f(__ldcg(p.ws_y + (size_t)s2 * H + h)) : 0.0f;
             float total = 0.0f;
 #pragma unroll
             for (int q = 0; q < MAXK; ++q) {
-              if (q < TY) {
-                float a2 = 0.0f;
-                for (int s2 = q; s2 < nloc; s2 += TY) a2 = prod[s2] + a2;
+              if (q < nloc) {
+                const float a2 = yv[q] * sw[EP ? lslot[q] : q] + 0.0f;
                 total = (q == 0) ? a2 : a2 + total;
               }
             }
