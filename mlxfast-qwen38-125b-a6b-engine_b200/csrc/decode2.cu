@@ -16,11 +16,13 @@
 //                    expert width, their scales / biases, and the expert's
 //                    SwiGLU activations (with their chunk sums);
 //      qmv unit      32 rows of the matrix over the whole reduction.
-//    Fused calls hand units out from a grid-wide counter in the order: all
-//    gate|up units slot by slot, then all down units slot by slot, so the down
-//    units of slot j start as soon as slot j's activations are final (a
-//    per-slot count of finished gate|up units), with no grid-wide barrier
-//    between the two phases. qmv units go round-robin over the CTAs.
+//    Units go round-robin over the CTAs (unit u to CTA u mod grid); fused
+//    calls order them all gate|up units slot by slot, then all down units
+//    slot by slot, so the down units of slot j start as soon as slot j's
+//    activations are final (a per-slot count of finished gate|up units), with
+//    no grid-wide barrier between the two phases. The static order keeps
+//    global round trips out of the producer's loop: at full bandwidth a
+//    round trip waits behind the CTA's copies in flight for microseconds.
 //  * Large copies (32 KB boxes of whole rows) keep the per-copy issue cost of
 //    the TMA small against the bytes moved.
 //  * The producer fills a ring of stages (full / empty mbarrier per stage) with
@@ -67,8 +69,10 @@ constexpr int MAXK = 8;              // routed slots
 constexpr int MAXST = 6;             // stages at most
 constexpr int ROWS_QMV = 32;         // rows of a qmv unit (two 16-row MMA blocks)
 constexpr int ROWS_GU = 16;          // outputs of a gate|up unit (16 gate + 16 up rows)
-constexpr int ROWS_DOWN = 64;        // rows of a down unit
-constexpr int MISC_BYTES = 512;
+constexpr int ROWS_D = 16;           // rows of a down block (output rows h)
+constexpr int SLOTS_D = 4;           // routed slots of a down unit
+constexpr int MAXBLK = 16;           // down blocks of one CTA at most
+constexpr int MISC_BYTES = 1024;
 
 enum : int { U_END = -1, U_GU = 0, U_DOWN = 1, U_QMV = 2 };
 enum : int { MW = 0, MS = 1, MB = 2, MWG = 0, MSG = 1, MBG = 2, MWU = 3, MSU = 4, MBU = 5, MWD = 6, MSD = 7, MBD = 8 };
@@ -357,10 +361,11 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   int* lslot = reinterpret_cast<int*>(sw + MAXK);                // [MAXK] routed slots held here (EP)
   float* rsum = reinterpret_cast<float*>(lslot + MAXK);          // [NCW + 1]
   int* lastf_sm = reinterpret_cast<int*>(rsum + NCW + 1);        // [MAXST] producer bookkeeping
+  unsigned* ycnt = reinterpret_cast<unsigned*>(lastf_sm + MAXST); // [MAXBLK] down units finished per block
+  float* ysm = reinterpret_cast<float*>(smem + p.off_ysm);       // [MAXBLK][MAXK][ROWS_D] slot products
   float* red = reinterpret_cast<float*>(smem + p.off_red);       // [nstage][NCW][32]
   float2* gsc = reinterpret_cast<float2*>(smem + p.off_xs);     // per group: 2^(E_g - 14), sum(x)
   unsigned* done = p.ctr + 4;
-  unsigned* comb = p.ctr + D2_CTR_FIXED;
 
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
@@ -368,6 +373,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       mbar_init(&empty[i], NCW);
       arr[i] = 0u;
     }
+    for (int i = 0; i < MAXBLK; ++i) ycnt[i] = 0u;
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -394,8 +400,10 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   griddep_wait();
   griddep_launch();
   const uint64_t deadline = globaltimer() + (uint64_t)p.timeout_ns;
-  unsigned nxt = 0u;  // producer lane 0: the next unit from the queue
-  if (FUSED && warp == NCW && lane == 0) nxt = atomicAdd(&p.ctr[1], 1u);
+  // the call's tag: router logits carry it, so a value read is complete and
+  // of this call with no separate count (the last CTA out advances it)
+  const unsigned tag = FUSED ? __ldcg(p.ctr + D2_CTR_TAG) + 1u : 0u;
+  unsigned long long* tlg = reinterpret_cast<unsigned long long*>(p.ctr + D2_CTR_LOGITS);
   __syncthreads();
 
   const int K1 = p.K1;
@@ -414,7 +422,6 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       if (live) v = __ldg(reinterpret_cast<const uint4*>(p.x) + q);
       if (FUSED && q0 == 0 && nch <= NTH) {
         // router rows e = blockIdx.x + i * grid (x word q of each)
-        int rows = 0;
         for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
           float part = 0.0f;
           if (live) {
@@ -431,14 +438,9 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           if (tid == 0) {
             float lg = 0.0f;
             for (int w = 0; w < NCW + 1; ++w) lg += rsum[w];
-            p.ws_logits[e] = lg;
+            st_relaxed_u64(tlg + e, ((unsigned long long)tag << 32) | __float_as_uint(lg));
           }
           __syncthreads();
-          ++rows;
-        }
-        if (tid == 0 && rows) {
-          __threadfence();
-          atomicAdd(&p.ctr[0], (unsigned)rows);
         }
       }
       float s = ((lbf(v.x) + hbf(v.x)) + (lbf(v.y) + hbf(v.y))) + ((lbf(v.z) + hbf(v.z)) + (lbf(v.w) + hbf(v.w)));
@@ -488,47 +490,62 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   const int nslot1 = ncc1 / (SLOT / 32), slot01 = cc01 / (SLOT / 32);
   // ---- routing (fused): every CTA selects the same top-k in warp 0 ----
   if (FUSED && warp == 0) {
+    // lane l holds experts l, l + 32, ...: poll until every logit carries this
+    // call's tag (one read of the values, no separate count)
+    constexpr int EPL = 8;  // experts per lane at most (E <= 256)
+    uint32_t key[EPL];
     bool ok = true;
-    if (lane == 0) ok = wait_counter_geq(&p.ctr[0], (unsigned)p.E, deadline, abort_flag);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
+    for (int poll = 0;; ++poll) {
+      bool all = true;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        key[i] = 0u;
+        if (e < p.E) {
+          const unsigned long long v = ld_relaxed_u64(tlg + e);
+          all = all && (unsigned)(v >> 32) == tag;
+          key[i] = (uint32_t)v;
+        }
+      }
+      if (__all_sync(0xffffffffu, all)) break;
+      if ((poll & 7) == 7 && __shfl_sync(0xffffffffu, (globaltimer() > deadline || *abort_flag) ? 1 : 0, 0)) {
+        ok = false;
+        break;
+      }
+    }
     if (!ok) {
       if (lane == 0) record_error(p.err, B2Q_ETIMEOUT);
       *abort_flag = 1;
     }
-    // logits to shared memory (stage 0 is free until the producer starts), NaN as -inf
-    float* lgs = reinterpret_cast<float*>(smem);
-    for (int e = lane; e < p.E; e += 32) {
-      float v = ok ? __ldcg(p.ws_logits + e) : 0.0f;
-      lgs[e] = (v != v) ? -INFINITY : v;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      if (!ok) key[i] = 0u;  // routing on zero logits after a timeout (the call reports it)
+      if (blockIdx.x == 0 && p.logits_out && e < p.E) p.logits_out[e] = __uint_as_float(key[i]);
+      // order-preserving keys, NaN as -inf; 0 marks no expert (or one taken)
+      uint32_t u = key[i];
+      if ((u & 0x7fffffffu) > 0x7f800000u) u = 0xff800000u;
+      key[i] = e < p.E ? ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) : 0u;
     }
-    __syncwarp();
-    // k rounds of a warp arg-max over orderable keys (larger value first, ties
-    // to the lower index: the reference's stable selection); lane l scans
-    // experts l, l + 32, ... and remembers the ones taken in a bit mask
-    constexpr int EPL = 8;  // experts per lane at most (E <= 256)
-    uint32_t taken = 0u;
+    // k rounds of a warp arg-max: larger key first, ties to the lower index
+    // (the reference's stable selection)
     float selv = -INFINITY;
     for (int slot = 0; slot < p.k; ++slot) {
-      unsigned long long best = 0ull;
+      uint32_t bk = 0u;
+      unsigned be = 0xffffffffu;
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) {
-        const int e = lane + 32 * i;
-        if (e < p.E && !((taken >> i) & 1u)) {
-          uint32_t u = __float_as_uint(lgs[e]);
-          u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving map
-          const unsigned long long key = ((unsigned long long)u << 32) | (0xffffffffu - (uint32_t)e);
-          best = key > best ? key : best;
+      for (int i = 0; i < EPL; ++i)
+        if (key[i] > bk) {
+          bk = key[i];
+          be = (unsigned)(lane + 32 * i);
         }
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
-        best = o > best ? o : best;
-      }
-      const int e = (int)(0xffffffffu - (uint32_t)best);
-      if (lane == slot) selv = lgs[e];
+      const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
+      const int e = (int)__reduce_min_sync(0xffffffffu, bk == m ? be : 0xffffffffu);
+      if (lane == slot) selv = __uint_as_float((m & 0x80000000u) ? (m & 0x7fffffffu) : ~m);
       if (lane == 0) sidx[slot] = (uint32_t)e;
-      if ((e & 31) == lane) taken |= 1u << (e >> 5);
+#pragma unroll
+      for (int i = 0; i < EPL; ++i)
+        if (e == lane + 32 * i) key[i] = 0u;
     }
     softmax_k(selv, p.k, sw);
     __syncwarp();
@@ -536,8 +553,6 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       if (p.idx_out) p.idx_out[lane] = sidx[lane];
       if (p.w_out) p.w_out[lane] = sw[lane];
     }
-    if (blockIdx.x == 0 && p.logits_out)
-      for (int e = lane; e < p.E; e += 32) p.logits_out[e] = __ldcg(p.ws_logits + e);
     if (lane == 0) {
       int n = 0;
       for (int s2 = 0; s2 < p.k; ++s2) {
@@ -551,9 +566,17 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
 
   const int nloc = FUSED ? *nloc_sm : 0;
   const int F = p.F, H = p.H;
-  const unsigned U1 = FUSED ? (unsigned)(nloc * (F / ROWS_GU)) : (unsigned)((p.N + ROWS_QMV - 1) / ROWS_QMV);
-  const unsigned U2 = FUSED ? (unsigned)(nloc * (H / ROWS_DOWN)) : 0u;
-  const unsigned UT = U1 + U2;
+  // Static schedule. qmv: unit u to CTA u mod grid. Fused: gate|up unit u to
+  // CTA grid - 1 - (u mod grid); 16-row down block j to CTA j mod grid, each
+  // CTA streaming its blocks' rows of every routed slot (units of 4 slots,
+  // slots 0-3 of all its blocks first) and folding the slots locally; the
+  // CTAs with a block fewer take the extra gate|up units.
+  const int G = (int)gridDim.x, bx = (int)blockIdx.x;
+  const int U1 = FUSED ? nloc * (F / ROWS_GU) : (p.N + ROWS_QMV - 1) / ROWS_QMV;
+  const int nq = (nloc + SLOTS_D - 1) / SLOTS_D;     // down units per block
+  const int nblk = FUSED ? (H / ROWS_D + G - 1 - bx) / G : 0;
+  const int ngu = FUSED ? (U1 + bx) / G : (U1 - bx + G - 1) / G;  // first-family units of this CTA
+  const int UT = ngu + nblk * nq;
 
   if (warp == NCW) {
     // ------------------------------ producer ------------------------------
@@ -564,23 +587,17 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       for (int i = 0; i < MAXST; ++i) lastf[i] = -1;
       int s = -1;
       uint32_t eph = 1u;  // parity of the empty phase the next reuse of stage s waits for
+      uint32_t ready = 0u;  // slots whose activations this CTA has seen final
       for (int it = 0;; ++it) {
         if (++s == NS) {
           s = 0;
           eph ^= 1u;
         }
-        unsigned u;
-        if (FUSED) {
-          u = nxt;
-          if (u < UT) nxt = atomicAdd(&p.ctr[1], 1u);
-        } else {
-          u = blockIdx.x + (unsigned)it * gridDim.x;
-        }
         if (it >= NS && !tc::wait(&empty[s], eph, deadline, abort_flag)) {
           if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
           *abort_flag = 1;
         }
-        if (u >= UT || *abort_flag) {
+        if (it >= UT || *abort_flag) {
           info[s] = make_int4(U_END, 0, 0, 0);
           mbar_arrive(&full[s]);
           lastf[s] = (int)(eph ^ 1u);
@@ -588,14 +605,16 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         }
         uint8_t* st = smem + (size_t)s * p.stage_bytes;
         if (!FUSED) {
-          const int row = (int)u * ROWS_QMV;
-          info[s] = make_int4(U_QMV, 0, (int)u, 0);
+          const int u = bx + it * G;
+          const int row = u * ROWS_QMV;
+          info[s] = make_int4(U_QMV, 0, u, 0);
           mbar_arrive_expect_tx(&full[s], (uint32_t)(ROWS_QMV * K1 / 2 + 2 * ROWS_QMV * p.mb1));
           tma3(st, &p.map[MW], 0, row, 0, &full[s], pol);
           tc::tma_load_2d(st + p.st_meta1, &p.map[MS], 0, row, &full[s], pol);
           tc::tma_load_2d(st + p.st_meta1 + p.st_mstep1, &p.map[MB], 0, row, &full[s], pol);
-        } else if (u < U1) {
-          const int z = (int)u / (F / ROWS_GU), rb = (int)u % (F / ROWS_GU);
+        } else if (it < ngu) {
+          const int u = G - 1 - bx + it * G;
+          const int z = u / (F / ROWS_GU), rb = u % (F / ROWS_GU);
           const uint32_t e = EP ? sidx[lslot[z]] - (uint32_t)p.e_lo : sidx[z];
           const int row = (int)(e * (uint32_t)F) + rb * ROWS_GU;
           info[s] = make_int4(U_GU, z, rb, 0);
@@ -608,12 +627,18 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           tc::tma_load_2d(m + 2 * p.st_mstep1, &p.map[MSU], 0, row, &full[s], pol);
           tc::tma_load_2d(m + 3 * p.st_mstep1, &p.map[MBU], 0, row, &full[s], pol);
         } else {
-          const unsigned v = u - U1;
-          const int z = (int)v / (H / ROWS_DOWN), hb = (int)v % (H / ROWS_DOWN);
-          const uint32_t e = EP ? sidx[lslot[z]] - (uint32_t)p.e_lo : sidx[z];
-          const int row = (int)(e * (uint32_t)H) + hb * ROWS_DOWN;
-          // the slot's activations must be final: every gate|up unit of it finished
-          if (!wait_counter_geq(&done[z], (unsigned)(F / ROWS_GU), deadline, abort_flag)) {
+          const int d = it - ngu, nbk = max(nblk, 1), quad = d / nbk, lb = d % nbk, blk = bx + lb * G;
+          const int z0 = quad * SLOTS_D, nsl = min(SLOTS_D, nloc - z0);
+          // the slots' activations must be final: every gate|up unit of them
+          // finished (one acquire per slot and CTA)
+          bool ok = true;
+          for (int i = 0; i < nsl && ok; ++i) {
+            const int z = z0 + i;
+            if ((ready >> z) & 1u) continue;
+            ok = wait_counter_geq(&done[z], (unsigned)(F / ROWS_GU), deadline, abort_flag);
+            ready |= 1u << z;
+          }
+          if (!ok) {
             if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
             *abort_flag = 1;
             info[s] = make_int4(U_END, 0, 0, 0);
@@ -622,14 +647,21 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
             break;
           }
           fence_proxy_async_global();  // the copies below read what generic stores wrote
-          info[s] = make_int4(U_DOWN, z, hb, 0);
-          mbar_arrive_expect_tx(&full[s],
-                                (uint32_t)(ROWS_DOWN * F / 2 + 2 * ROWS_DOWN * p.mb2 + F * 2 + F / 2));
-          tma3(st, &p.map[MWD], 0, row, 0, &full[s], pol);
-          tc::tma_load_2d(st + p.st_meta2, &p.map[MSD], 0, row, &full[s], pol);
-          tc::tma_load_2d(st + p.st_meta2 + p.st_mstep2, &p.map[MBD], 0, row, &full[s], pol);
-          bulk_g2s(st + p.st_act, p.ws_act + (size_t)z * F, (uint32_t)F * 2u, &full[s], pol_keep);
-          bulk_g2s(st + p.st_asum, p.ws_asum + (size_t)z * (F / 8), (uint32_t)F / 2u, &full[s], pol_keep);
+          info[s] = make_int4(U_DOWN, quad, blk, lb | (nsl << 8));
+          const int wb = ROWS_D * F / 2;  // one slot's weight box
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(nsl * (wb + 2 * ROWS_D * p.mb2 + F * 2 + F / 2)));
+          for (int i = 0; i < nsl; ++i) {
+            const int z = z0 + i;
+            const uint32_t e = EP ? sidx[lslot[z]] - (uint32_t)p.e_lo : sidx[z];
+            const int row = (int)(e * (uint32_t)H) + blk * ROWS_D;
+            uint8_t* m = st + p.st_meta2 + i * 2 * p.st_mstep2;
+            tma3(st + i * wb, &p.map[MWD], 0, row, 0, &full[s], pol);
+            tc::tma_load_2d(m, &p.map[MSD], 0, row, &full[s], pol);
+            tc::tma_load_2d(m + p.st_mstep2, &p.map[MBD], 0, row, &full[s], pol);
+            bulk_g2s(st + p.st_act + i * F * 2, p.ws_act + (size_t)z * F, (uint32_t)F * 2u, &full[s], pol_keep);
+            bulk_g2s(st + p.st_asum + i * (F / 2), p.ws_asum + (size_t)z * (F / 8), (uint32_t)F / 2u, &full[s],
+                     pol_keep);
+          }
         }
         lastf[s] = (int)(eph ^ 1u);
       }
@@ -717,44 +749,45 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         af += __shfl_xor_sync(0xffffffffu, af, 2);
         af += __shfl_xor_sync(0xffffffffu, af, 4);
         if (lane == 0 || lane == 8) p.ws_asum[(size_t)z * (F / 8) + blk * 2 + (lane >> 3)] = af;
-        __threadfence();
+        // the warp barrier orders every lane's stores before lane 0's release
+        // (cumulative): no full fence, and the release does not stall the warp
         __syncwarp();
         if (lane == 0) red_release_add_u32(&done[z], 1u);
       } else if (FUSED) {
-        const int z = inf.y, hb = inf.z;
-        p.ws_y[(size_t)z * H + hb * ROWS_DOWN + lane] = f2bf(t0);
-        p.ws_y[(size_t)z * H + hb * ROWS_DOWN + lane + 32] = f2bf(t1);
-        __threadfence();
+        // rows lane, lane + 32 of the unit: slot quad * 4 + row / 16, block row row % 16;
+        // the bf16 products go to the block's slot table, and the unit that
+        // completes the block folds its slots in the reference's combine order
+        const int quad = inf.y, blk = inf.z, lb = inf.w & 0xff, nsl = inf.w >> 8;
+        float* yb = ysm + (size_t)lb * MAXK * ROWS_D;
+        if ((lane >> 4) < nsl) yb[(quad * SLOTS_D + (lane >> 4)) * ROWS_D + (lane & 15)] = bf2f(f2bf(t0));
+        if ((lane >> 4) + 2 < nsl) yb[(quad * SLOTS_D + 2 + (lane >> 4)) * ROWS_D + (lane & 15)] = bf2f(f2bf(t1));
         __syncwarp();
         unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(&comb[hb], 1u);
+        if (lane == 0) {
+          __threadfence_block();
+          prev = atomicAdd(&ycnt[lb], 1u);
+        }
         prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == (unsigned)(nloc - 1)) {
-          // every slot's rows of this block are in: y_j = bf16 product,
-          // prod_j = y_j * w_j, folded in the mlx_colsum_small_f32 order
-          __threadfence();
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int h = hb * ROWS_DOWN + lane + 32 * h2;
-            // with nloc <= 8 slots the colsum association has one product per
-            // chain (chain q = 0 + prod_q) and folds the chains in slot order
-            float yv[MAXK];
-#pragma unroll
-            for (int s2 = 0; s2 < MAXK; ++s2) yv[s2] = s2 < nloc ? bf2f(__ldcg(p.ws_y + (size_t)s2 * H + h)) : 0.0f;
+        if (prev == (unsigned)(nq - 1)) {
+          __threadfence_block();
+          if (lane < ROWS_D) {
+            // y_j = bf16 product, prod_j = y_j * w_j: with nloc <= 8 slots the
+            // colsum association has one product per chain (chain q = 0 +
+            // prod_q) and folds the chains in slot order
             float total = 0.0f;
 #pragma unroll
             for (int q = 0; q < MAXK; ++q) {
               if (q < nloc) {
-                const float a2 = yv[q] * sw[EP ? lslot[q] : q] + 0.0f;
+                const float a2 = yb[q * ROWS_D + lane] * sw[EP ? lslot[q] : q] + 0.0f;
                 total = (q == 0) ? a2 : a2 + total;
               }
             }
+            const int h = blk * ROWS_D + lane;
             if (EP)
               p.out_f32[h] = total;
             else
               p.out[h] = f2bf(total);
           }
-          if (lane == 0) comb[hb] = 0u;
         }
       } else {
         // row lane of the unit: partial slot lane ([P 0..7][Q 8..15][P 16..23][Q 24..31])
@@ -823,21 +856,23 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         if (inf.x != U_DOWN) break;
         const uint8_t* st = smem + (size_t)s * p.stage_bytes;
         float* rp = red + ((size_t)s * NCW + warp) * 32;
-        // 4 row blocks of 16 x 4 reduction quarters
-        const int b = warp >> 2, qw = warp & 3;
+        // 4 slots (16 rows each) x 4 reduction quarters
+        const int b = warp >> 2, qw = warp & 3, nsl = inf.w >> 8;
         const int ncc = F / 32 / 4, cc0 = qw * ncc, ng = ncc / CPG;
-        const float* as = reinterpret_cast<const float*>(st + p.st_asum);
-        float gl_sum = 0.0f;
-        if (lane < ng) {
-          const int q0 = (cc0 / CPG + lane) * CPC;
-#pragma unroll
-          for (int i = 0; i < CPC; ++i) gl_sum += as[q0 + i];
-        }
-        const Meta m{st + p.st_meta2, st + p.st_meta2 + p.st_mstep2, st + p.st_meta2,
-                     st + p.st_meta2 + p.st_mstep2, 16 * b + r, 16 * b + 8 + r, p.mb2, p.sw2 != 0};
         float accP = 0.0f, accQ = 0.0f;
-        dot_xsmem<CPG>(st, ROWS_DOWN * 128, b * 2048, b * 2048 + 1024, cc0, ncc, st + p.st_act, gl_sum, m, accP,
-                       accQ);
+        if (b < nsl) {
+          const float* as = reinterpret_cast<const float*>(st + p.st_asum + b * (F / 2));
+          float gl_sum = 0.0f;
+          if (lane < ng) {
+            const int q0 = (cc0 / CPG + lane) * CPC;
+#pragma unroll
+            for (int i = 0; i < CPC; ++i) gl_sum += as[q0 + i];
+          }
+          const uint8_t* mb = st + p.st_meta2 + b * 2 * p.st_mstep2;
+          const Meta m{mb, mb + p.st_mstep2, mb, mb + p.st_mstep2, r, 8 + r, p.mb2, p.sw2 != 0};
+          dot_xsmem<CPG>(st + b * (ROWS_D * F / 2), ROWS_D * 128, 0, 1024, cc0, ncc, st + p.st_act + b * F * 2,
+                         gl_sum, m, accP, accQ);
+        }
         accP += __shfl_xor_sync(0xffffffffu, accP, 1);
         accQ += __shfl_xor_sync(0xffffffffu, accQ, 1);
         accP += __shfl_xor_sync(0xffffffffu, accP, 2);
@@ -858,15 +893,14 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   if (EP && nloc == 0)
     for (int h = blockIdx.x * NTH + tid; h < H; h += gridDim.x * NTH) p.out_f32[h] = 0.0f;
 
-  // ---- exit: the last CTA out re-arms the grid counters for the next call ----
+  // ---- exit: the last CTA out re-arms the grid words for the next call ----
   __syncthreads();
   if (FUSED && tid == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(&p.ctr[2], 1u);
     if (prev == gridDim.x - 1) {
-      p.ctr[0] = 0u;
-      p.ctr[1] = 0u;
       p.ctr[2] = 0u;
+      p.ctr[D2_CTR_TAG] = tag;
       for (int i = 0; i < MAXK; ++i) done[i] = 0u;
       __threadfence();
     }
@@ -897,11 +931,12 @@ static int plan(D2Params& p, int mode) {
     const int gu = p.st_meta1 + 4 * p.st_mstep1;
     p.mb2 = p.F / p.gs * 2;
     p.sw2 = p.mb2 == 128;
-    p.st_meta2 = ROWS_DOWN * p.F / 2;
-    p.st_mstep2 = round_up(ROWS_DOWN * p.mb2, p.sw2 ? 1024 : 128);
-    p.st_act = p.st_meta2 + 2 * p.st_mstep2;
-    p.st_asum = p.st_act + p.F * 2;
-    const int dn = p.st_asum + p.F / 2;
+    // down unit: 4 slots' 16-row weight boxes, their scale / bias tiles, activations, chunk sums
+    p.st_meta2 = SLOTS_D * ROWS_D * p.F / 2;
+    p.st_mstep2 = round_up(ROWS_D * p.mb2, p.sw2 ? 1024 : 128);
+    p.st_act = p.st_meta2 + SLOTS_D * 2 * p.st_mstep2;
+    p.st_asum = p.st_act + SLOTS_D * p.F * 2;
+    const int dn = p.st_asum + SLOTS_D * p.F / 2;
     st = std::max(gu, dn);
   }
   p.stage_bytes = round_up(st, 1024);
@@ -911,9 +946,11 @@ static int plan(D2Params& p, int mode) {
   // stages first (1024-aligned), then the group sums of x, the warp partials
   // of every stage and the barriers / routing state
   const int xs_bytes = round_up(K1 / p.gs * 8, 128);
+  // down blocks' slot tables (fused)
+  const int ys_bytes = mode == D2_QMV ? 0 : (p.H / ROWS_D + di.sm_count - 1) / di.sm_count * MAXK * ROWS_D * 4;
   int ns = MAXST;
   for (; ns >= 2; --ns) {
-    const int total = ns * p.stage_bytes + xs_bytes + ns * NCW * 32 * 4 + MISC_BYTES + 1024;
+    const int total = ns * p.stage_bytes + xs_bytes + ys_bytes + ns * NCW * 32 * 4 + MISC_BYTES + 1024;
     if (total <= di.smem_optin) break;
   }
   if (ns < 2) return set_error(B2Q_EUNSUPPORTED, "decode kernel: stages of %d bytes do not fit", p.stage_bytes);
@@ -921,6 +958,8 @@ static int plan(D2Params& p, int mode) {
   int off = ns * p.stage_bytes;
   p.off_xs = off;
   off += xs_bytes;
+  p.off_ysm = off;
+  off += ys_bytes;
   p.off_red = off;
   off += ns * NCW * 32 * 4;
   p.off_misc = off;
@@ -1085,9 +1124,14 @@ int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16
 
 bool d2_moe_eligible(int H, int E, int F, int k, int gs) {
   if (!(gs_ok(gs) && H > 0 && F > 0 && xreg_split_ok(H, gs) && F % (8 * gs) == 0 && F % 256 == 0 &&
-        (F / 128) % (gs / 32) == 0 && F % ROWS_GU == 0 && H % ROWS_DOWN == 0 && F / gs * 2 <= 512 &&
-        k >= 1 && k <= MAXK && E >= k && E <= 256 && H / 8 <= NTH && d2_counter_words(H) * 4 <= 2048))
+        (F / 128) % (gs / 32) == 0 && F % ROWS_GU == 0 && H % ROWS_D == 0 && F / gs * 2 <= 512 &&
+        k >= 1 && k <= MAXK && E >= k && E <= 256 && H / 8 <= NTH))
     return false;
+  DeviceInfo di;
+  if (device_info(&di) || H / ROWS_D > MAXBLK * di.sm_count) {
+    clear_error();
+    return false;
+  }
   D2Params p;
   std::memset(&p, 0, sizeof(p));
   p.gs = gs;
@@ -1122,7 +1166,6 @@ int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
   p.ws_logits = scr.logits;
   p.ws_act = scr.act;
   p.ws_asum = scr.asum;
-  p.ws_y = scr.y;
   p.e_lo = e_lo;
   p.e_local = e_local;
   p.out_f32 = out_f32;
@@ -1139,7 +1182,7 @@ int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
     if (rc) return rc;
     rc = set_family(p, MWU, MSU, MBU, wu, su, bu, rgu, H, ROWS_GU);
     if (rc) return rc;
-    rc = set_family(p, MWD, MSD, MBD, wd, sd, bd, rd, F, ROWS_DOWN);
+    rc = set_family(p, MWD, MSD, MBD, wd, sd, bd, rd, F, ROWS_D);
     if (rc) return rc;
     put_maps(key, p.map, 9);
   }

@@ -10,13 +10,13 @@ namespace b2q {
 
 enum { D2_QMV = 0, D2_FUSED = 1, D2_FUSED_EP = 2 };
 
-// Grid counters of the fused kernel, zero between calls (the last CTA out
-// re-arms the fixed ones, each combine re-arms its own):
-//   [0] router rows published, [1] unit queue, [2] CTAs exited,
+// Grid words of the fused kernel (the last CTA out re-arms them):
+//   [2] CTAs exited, [3] tag of the last call,
 //   [4, 4 + 8) gate|up units finished per routed slot,
-//   [16, 16 + H / 64) down units finished per 64-row block.
-constexpr int D2_CTR_FIXED = 16;
-inline int d2_counter_words(int H) { return D2_CTR_FIXED + H / 64; }
+//   [512, 512 + 2 E) router logits, each 64-bit word (call tag << 32 | fp32 bits).
+// A zeroed block is a valid state (tag 0); it stays valid call to call.
+constexpr int D2_CTR_TAG = 3;
+constexpr int D2_CTR_LOGITS = 512;
 
 struct alignas(64) D2Params {
   CUtensorMap map[9];  // qmv: W, S, B; fused: gate W/S/B, up W/S/B, down W/S/B
@@ -36,13 +36,12 @@ struct alignas(64) D2Params {
   float* ws_logits;   // [E]
   uint16_t* ws_act;   // [k][F] SwiGLU activations, 8-value chunks stored as (a0,a4,a1,a5,a2,a6,a3,a7)
   float* ws_asum;     // [k][F / 8] chunk sums of the activations
-  uint16_t* ws_y;     // [k][H] per-slot down products (bf16)
   long long timeout_ns;
   int e_lo, e_local;  // expert parallel: this rank holds experts [e_lo, e_lo + e_local) (e_local 0: all)
   float* out_f32;     // expert parallel: fp32 partial output instead of bf16 `out`
   // launch plan (host)
   int nstage, stage_bytes, smem_bytes;
-  int off_xs, off_red, off_misc;
+  int off_xs, off_ysm, off_red, off_misc;
   int mb1, mb2;             // metadata row bytes: first family, down
   int sw1, sw2;             // metadata blocks in the 128-byte swizzle
   int st_meta1, st_mstep1;  // first family: metadata blocks inside a stage
@@ -53,14 +52,14 @@ bool d2_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const v
 int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b, uint16_t* y, int N, int K,
            int gs, cudaStream_t st);
 bool d2_moe_eligible(int H, int E, int F, int k, int gs);
-// Device scratch of one fused call (all caller-owned; ctr zeroed once).
+// Device scratch of one fused call (all caller-owned; ctr zeroed once: the
+// grid words and tagged router logits, 4096 bytes).
 struct D2Scratch {
   int* err;
   unsigned* ctr;      // d2_counter_words(H)
   float* logits;      // [E]
   uint16_t* act;      // [k][F]
   float* asum;        // [k][F / 8]
-  uint16_t* y;        // [k][H]
 };
 int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,

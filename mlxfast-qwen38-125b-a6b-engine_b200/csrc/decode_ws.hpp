@@ -43,15 +43,14 @@ struct DecodeWs {
   float* w;
   uint16_t* act;
   float* asum;    // one-token fused kernel: chunk sums of the activations [k][F / 8]
-  uint16_t* y;    // one-token fused kernel: per-slot down products [k][H]
   size_t bytes;
 };
 
 // The one-token fused kernel's grid counters sit at a fixed offset right after
 // the header, whatever the shapes: a workspace reused for another shape keeps
 // them where the last call left them (zero).
-constexpr size_t D2_CTR_BYTES = 2048;
-static_assert(D2_CTR_FIXED * 4 < (int)D2_CTR_BYTES, "counter block");
+constexpr size_t D2_CTR_BYTES = 4096;
+static_assert(D2_CTR_LOGITS * 4 + 256 * 8 <= (int)D2_CTR_BYTES, "counter block");
 
 static inline DecodeWs decode_ws_layout(void* base, int S, int H, int E, int F, int k) {
   DecodeWs d{};
@@ -71,8 +70,6 @@ static inline DecodeWs decode_ws_layout(void* base, int S, int H, int E, int F, 
   off = align256(off + sizeof(uint16_t) * (size_t)S * k * F);
   d.asum = reinterpret_cast<float*>(b + off);
   off = align256(off + sizeof(float) * (size_t)k * (F / 8));
-  d.y = reinterpret_cast<uint16_t*>(b + off);
-  off = align256(off + sizeof(uint16_t) * (size_t)k * H);
   d.bytes = off;
   return d;
 }

@@ -341,7 +341,7 @@ int b2q_ep_moe_decode(void* comm, const uint16_t* x, const uint16_t* wr, const u
     bool all_aligned = true;
     for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
     if (all_aligned && !decode_v1() && d2_moe_eligible(H, E, F, k, group_size)) {
-      const D2Scratch scr{ws.err, ws.ctr, ws.logits, ws.act, ws.asum, ws.y};
+      const D2Scratch scr{ws.err, ws.ctr, ws.logits, ws.act, ws.asum};
       rc = d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, nullptr, idx, w, nullptr, H, E, F, k, group_size,
                          scr, st, e_lo, e_local, partial);
       if (rc) return rc;

@@ -27,8 +27,8 @@ def _bf(t):
 def test_noalloc_refuses_oversized_shapes(b2q_mod):
     """Checked on the host before any CUDA call: the scratch has a fixed size."""
     lib = b2q_mod.lib()
-    assert lib.b2q_moe_decode_workspace_size(1, 4096, 1024, 4096, 8) > SCRATCH_BYTES
-    rc = lib.b2q_moe_decode_noalloc(*([None] * 15), 4096, 1024, 4096, 8, 64, 4, None, None)
+    assert lib.b2q_moe_decode_workspace_size(1, 4096, 1024, 16384, 8) > SCRATCH_BYTES
+    rc = lib.b2q_moe_decode_noalloc(*([None] * 15), 4096, 1024, 16384, 8, 64, 4, None, None)
     assert rc == -1
     assert b"scratch" in lib.b2q_last_error()
 
