@@ -64,7 +64,8 @@ namespace b2q {
 namespace d2 {
 
 constexpr int NCW = 16;              // consumer warps
-constexpr int NTH = (NCW + 1) * 32;  // + the producer warp
+constexpr int NWARP = NCW + 2;       // + the producer warp and the epilogue warp
+constexpr int NTH = NWARP * 32;
 constexpr int MAXK = 8;              // routed slots
 constexpr int MAXST = 6;             // stages at most
 constexpr int ROWS_QMV = 32;         // rows of a qmv unit (two 16-row MMA blocks)
@@ -144,8 +145,10 @@ __device__ __forceinline__ void mma_word_pair(float (&d)[4], uint32_t W0, uint32
 // Units whose activation is the call's x (gate|up, qmv): integer MMAs.
 // x is held per group g as 16-bit fixed point X = round(x * 2^(14 - E_g))
 // (E_g: exponent of the group's max |x|; exact for every value within 2^7 of
-// the max, |X| < 2^15), split into int8 pieces hi = (X + 128) >> 8 and
-// lo = X - 256 hi. Weights go in as raw u8 nibbles (two masks per word), so
+// the max, |X| <= 32640), split into int8 pieces hi = (X + 128) >> 8 and
+// lo = X - 256 hi. The pieces reach 256 hi + lo <= 32639: the one positive
+// value above it, 32640 (a max of mantissa 0x7f), is held as 32639, an error
+// of 2^-15 of the group's max. Weights go in as raw u8 nibbles (two masks per word), so
 // mma.sync m16n8k32 u8 x s8 -> s32 sums q * hi and q * lo exactly.
 // A "slot" is min(gs, 64) reduction values; in one MMA lane c of a quad
 // carries a word of slot 4t + c (rotated so the four lanes of a 16-byte unit
@@ -352,16 +355,15 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   uint8_t* misc = smem + p.off_misc;
   uint64_t* full = reinterpret_cast<uint64_t*>(misc);
   uint64_t* empty = full + MAXST;
-  int4* info = reinterpret_cast<int4*>(empty + MAXST);          // [MAXST] unit of each stage fill
-  unsigned* arr = reinterpret_cast<unsigned*>(info + MAXST);     // [MAXST] warps done with a unit
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(arr + MAXST);
+  uint64_t* rfull = empty + MAXST;                               // [MAXST] consumer partials of a unit posted
+  int4* info = reinterpret_cast<int4*>(rfull + MAXST);          // [MAXST] unit of each stage fill
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(info + MAXST);
   int* nloc_sm = const_cast<int*>(abort_flag) + 1;
   uint32_t* sidx = reinterpret_cast<uint32_t*>(nloc_sm + 3);     // [MAXK] selected experts, slot order
   float* sw = reinterpret_cast<float*>(sidx + MAXK);             // [MAXK] their weights
   int* lslot = reinterpret_cast<int*>(sw + MAXK);                // [MAXK] routed slots held here (EP)
-  float* rsum = reinterpret_cast<float*>(lslot + MAXK);          // [NCW + 1]
-  int* lastf_sm = reinterpret_cast<int*>(rsum + NCW + 1);        // [MAXST] producer bookkeeping
-  unsigned* ycnt = reinterpret_cast<unsigned*>(lastf_sm + MAXST); // [MAXBLK] down units finished per block
+  float* rsum = reinterpret_cast<float*>(lslot + MAXK);          // [NWARP]
+  int* lastf_sm = reinterpret_cast<int*>(rsum + NWARP);          // [MAXST] producer bookkeeping
   float* ysm = reinterpret_cast<float*>(smem + p.off_ysm);       // [MAXBLK][MAXK][ROWS_D] slot products
   float* red = reinterpret_cast<float*>(smem + p.off_red);       // [nstage][NCW][32]
   float2* gsc = reinterpret_cast<float2*>(smem + p.off_xs);     // per group: 2^(E_g - 14), sum(x)
@@ -370,10 +372,9 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], NCW);
-      arr[i] = 0u;
+      mbar_init(&empty[i], 1);
+      mbar_init(&rfull[i], NCW);
     }
-    for (int i = 0; i < MAXBLK; ++i) ycnt[i] = 0u;
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -437,7 +438,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           __syncthreads();
           if (tid == 0) {
             float lg = 0.0f;
-            for (int w = 0; w < NCW + 1; ++w) lg += rsum[w];
+            for (int w = 0; w < NWARP; ++w) lg += rsum[w];
             st_relaxed_u64(tlg + e, ((unsigned long long)tag << 32) | __float_as_uint(lg));
           }
           __syncthreads();
@@ -465,7 +466,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const uint32_t h = (i & 1) ? (vw[i >> 1] & 0xffff0000u) : (vw[i >> 1] << 16);
-          const int X = __float2int_rn(__uint_as_float(h) * f);
+          const int X = min(__float2int_rn(__uint_as_float(h) * f), 32639);
           const int hi = (X + 128) >> 8;
           const uint32_t hb = (uint32_t)hi & 0xffu, lb = (uint32_t)(X - (hi << 8)) & 0xffu;
           const int sh = 8 * (i >> 1);
@@ -673,10 +674,116 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         if (lastf[i] >= 0) tc::wait_until(&full[i], (uint32_t)lastf[i], dl);
     }
     __syncwarp();
+  } else if (warp == NCW + 1) {
+    // ------------------------------ epilogue ------------------------------
+    // Finishes the units in order once the consumers posted their partials:
+    // it releases the stage, then does the unit's global work (bf16 store,
+    // SwiGLU activations, or the down block's slot table and fold). Finished
+    // gate|up units are published (fence, then per-slot counts) only when the
+    // next unit's partials are not in yet: a fence waits for this warp's
+    // stores to be acknowledged, microseconds at full bandwidth, and stalls
+    // no other warp here.
+    uint64_t pend = 0ull;  // gate|up units finished and not yet published, 8 bits per slot
+    auto publish = [&]() {
+      __syncwarp();
+      if (lane == 0 && pend != 0ull) {
+        __threadfence();
+        for (int z = 0; z < MAXK; ++z) {
+          const unsigned cz = (unsigned)(pend >> (8 * z)) & 0xffu;
+          if (cz) atomicAdd(&done[z], cz);
+        }
+      }
+      pend = 0ull;
+    };
+    int s = 0;
+    uint32_t ph = 0u;
+    for (int n = 0; n < UT; ++n) {
+      if (!__shfl_sync(0xffffffffu, tc::test_wait(&rfull[s], ph) ? 1 : 0, 0)) {
+        if (FUSED) publish();
+        if (!__all_sync(0xffffffffu, tc::wait(&rfull[s], ph, deadline, abort_flag))) {
+          if (!*abort_flag && lane == 0) record_error(p.err, B2Q_ETIMEOUT);
+          *abort_flag = 1;
+          break;
+        }
+      }
+      const int4 inf = info[s];
+      const float* rb = red + (size_t)s * NCW * 32;
+      float t0 = 0.0f, t1 = 0.0f;
+      if (FUSED && inf.x == U_DOWN) {
+        // rows lane and lane + 32 of the unit: row i is slot block i / 16, partial row i % 16
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int i = lane + 32 * h2, b = i >> 4, j = i & 15;
+          const float y2 = (rb[(4 * b) * 32 + j] + rb[(4 * b + 1) * 32 + j]) +
+                           (rb[(4 * b + 2) * 32 + j] + rb[(4 * b + 3) * 32 + j]);
+          if (h2 == 0) t0 = y2; else t1 = y2;
+        }
+      } else {
+        // lane l: total of partial row l over the warps
+        for (int w = 0; w < NCW; ++w) t0 += rb[w * 32 + lane];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == NS) {
+        s = 0;
+        ph ^= 1u;
+      }
+      if (FUSED && inf.x == U_GU) {
+        // t0 at lane l: row l of [gate 0..7][up 0..7][gate 8..15][up 8..15]
+        const int z = inf.y, blk = inf.z;
+        const int f = lane & 15;  // output of lanes 0..15
+        const float g = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + (f & 7));
+        const float up = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + 8 + (f & 7));
+        uint16_t a = 0;
+        if (lane < 16) {
+          a = swiglu_bf16(f2bf(g), f2bf(up));
+          const int j = f & 7, pos = j < 4 ? 2 * j : 2 * (j - 4) + 1;
+          p.ws_act[(size_t)z * F + blk * ROWS_GU + (f >> 3) * 8 + pos] = a;
+        }
+        float af = lane < 16 ? bf2f(a) : 0.0f;
+        af += __shfl_xor_sync(0xffffffffu, af, 1);
+        af += __shfl_xor_sync(0xffffffffu, af, 2);
+        af += __shfl_xor_sync(0xffffffffu, af, 4);
+        if (lane == 0 || lane == 8) p.ws_asum[(size_t)z * (F / 8) + blk * 2 + (lane >> 3)] = af;
+        pend += 1ull << (8 * z);
+      } else if (FUSED) {
+        // rows lane, lane + 32: slot quad * 4 + row / 16, block row row % 16;
+        // the bf16 products go to the block's slot table, and the block's last
+        // unit folds its slots in the reference's combine order
+        const int quad = inf.y, blk = inf.z, lb = inf.w & 0xff, nsl = inf.w >> 8;
+        float* yb = ysm + (size_t)lb * MAXK * ROWS_D;
+        if ((lane >> 4) < nsl) yb[(quad * SLOTS_D + (lane >> 4)) * ROWS_D + (lane & 15)] = bf2f(f2bf(t0));
+        if ((lane >> 4) + 2 < nsl) yb[(quad * SLOTS_D + 2 + (lane >> 4)) * ROWS_D + (lane & 15)] = bf2f(f2bf(t1));
+        __syncwarp();
+        if (quad == nq - 1 && lane < ROWS_D) {
+          // y_j = bf16 product, prod_j = y_j * w_j: with nloc <= 8 slots the
+          // colsum association has one product per chain (chain q = 0 +
+          // prod_q) and folds the chains in slot order
+          float total = 0.0f;
+#pragma unroll
+          for (int q = 0; q < MAXK; ++q) {
+            if (q < nloc) {
+              const float a2 = yb[q * ROWS_D + lane] * sw[EP ? lslot[q] : q] + 0.0f;
+              total = (q == 0) ? a2 : a2 + total;
+            }
+          }
+          const int h = blk * ROWS_D + lane;
+          if (EP)
+            p.out_f32[h] = total;
+          else
+            p.out[h] = f2bf(total);
+        }
+      } else {
+        // row lane of the unit: partial slot lane ([P 0..7][Q 8..15][P 16..23][Q 24..31])
+        const int row = inf.z * ROWS_QMV + lane;
+        if (row < p.N) p.y[row] = f2bf(t0);
+      }
+    }
+    if (FUSED) publish();
   } else {
     // ------------------------------ consumers ------------------------------
-    // A CTA's queue hands out all its gate|up units before any down unit, so
-    // the consumers run two phases: units whose activation is in registers
+    // A CTA's units are all its gate|up units, then its down units, so the
+    // consumers run two phases: units whose activation is in registers
     // (gate|up, qmv), then down units (their activation is in the stage).
     const int r = lane >> 2, c = lane & 3;
     // stage and phase of the consumers' current unit
@@ -697,103 +804,10 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       }
       return true;
     };
-    // after a warp's partials are in `red`: the last warp of the unit
-    // finishes it; every warp then releases the stage
-    auto hand_in = [&](int s, const int4& inf) {
+    // the warp's partials are in `red`: post them to the epilogue warp
+    auto post = [&](int s) {
       __syncwarp();
-      unsigned old = 0;
-      if (lane == 0) {
-        __threadfence_block();
-        old = atomicAdd(&arr[s], 1u);
-      }
-      old = __shfl_sync(0xffffffffu, old, 0);
-      const bool finisher = old == NCW - 1;
-      // the finisher takes what it needs from the partials into registers and
-      // releases the stage before its global stores, fences and atomics
-      float t0 = 0.0f, t1 = 0.0f;
-      if (finisher) {
-        __threadfence_block();
-        const float* rb = red + (size_t)s * NCW * 32;
-        if (FUSED && inf.x == U_DOWN) {
-          // rows lane and lane + 32 of the unit: row i is block i / 16, partial row i % 16
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int i = lane + 32 * h2, b = i >> 4, j = i & 15;
-            const float y2 = (rb[(4 * b) * 32 + j] + rb[(4 * b + 1) * 32 + j]) +
-                             (rb[(4 * b + 2) * 32 + j] + rb[(4 * b + 3) * 32 + j]);
-            if (h2 == 0) t0 = y2; else t1 = y2;
-          }
-        } else {
-          // lane l: total of partial row l over the warps
-          for (int w = 0; w < NCW; ++w) t0 += rb[w * 32 + lane];
-        }
-        if (lane == 0) arr[s] = 0u;
-        __syncwarp();
-      }
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (!finisher) return;
-      if (FUSED && inf.x == U_GU) {
-        // t0 at lane l: row l of [gate 0..7][up 0..7][gate 8..15][up 8..15]
-        const int z = inf.y, blk = inf.z;
-        const int f = lane & 15;  // output of lanes 0..15
-        const float g = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + (f & 7));
-        const float up = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + 8 + (f & 7));
-        uint16_t a = 0;
-        if (lane < 16) {
-          a = swiglu_bf16(f2bf(g), f2bf(up));
-          const int j = f & 7, pos = j < 4 ? 2 * j : 2 * (j - 4) + 1;
-          p.ws_act[(size_t)z * F + blk * ROWS_GU + (f >> 3) * 8 + pos] = a;
-        }
-        float af = lane < 16 ? bf2f(a) : 0.0f;
-        af += __shfl_xor_sync(0xffffffffu, af, 1);
-        af += __shfl_xor_sync(0xffffffffu, af, 2);
-        af += __shfl_xor_sync(0xffffffffu, af, 4);
-        if (lane == 0 || lane == 8) p.ws_asum[(size_t)z * (F / 8) + blk * 2 + (lane >> 3)] = af;
-        // the warp barrier orders every lane's stores before lane 0's release
-        // (cumulative): no full fence, and the release does not stall the warp
-        __syncwarp();
-        if (lane == 0) red_release_add_u32(&done[z], 1u);
-      } else if (FUSED) {
-        // rows lane, lane + 32 of the unit: slot quad * 4 + row / 16, block row row % 16;
-        // the bf16 products go to the block's slot table, and the unit that
-        // completes the block folds its slots in the reference's combine order
-        const int quad = inf.y, blk = inf.z, lb = inf.w & 0xff, nsl = inf.w >> 8;
-        float* yb = ysm + (size_t)lb * MAXK * ROWS_D;
-        if ((lane >> 4) < nsl) yb[(quad * SLOTS_D + (lane >> 4)) * ROWS_D + (lane & 15)] = bf2f(f2bf(t0));
-        if ((lane >> 4) + 2 < nsl) yb[(quad * SLOTS_D + 2 + (lane >> 4)) * ROWS_D + (lane & 15)] = bf2f(f2bf(t1));
-        __syncwarp();
-        unsigned prev = 0;
-        if (lane == 0) {
-          __threadfence_block();
-          prev = atomicAdd(&ycnt[lb], 1u);
-        }
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == (unsigned)(nq - 1)) {
-          __threadfence_block();
-          if (lane < ROWS_D) {
-            // y_j = bf16 product, prod_j = y_j * w_j: with nloc <= 8 slots the
-            // colsum association has one product per chain (chain q = 0 +
-            // prod_q) and folds the chains in slot order
-            float total = 0.0f;
-#pragma unroll
-            for (int q = 0; q < MAXK; ++q) {
-              if (q < nloc) {
-                const float a2 = yb[q * ROWS_D + lane] * sw[EP ? lslot[q] : q] + 0.0f;
-                total = (q == 0) ? a2 : a2 + total;
-              }
-            }
-            const int h = blk * ROWS_D + lane;
-            if (EP)
-              p.out_f32[h] = total;
-            else
-              p.out[h] = f2bf(total);
-          }
-        }
-      } else {
-        // row lane of the unit: partial slot lane ([P 0..7][Q 8..15][P 16..23][Q 24..31])
-        const int row = inf.z * ROWS_QMV + lane;
-        if (row < p.N) p.y[row] = f2bf(t0);
-      }
+      if (lane == 0) mbar_arrive(&rfull[s]);
     };
 
     int4 inf = make_int4(U_END, 0, 0, 0);
@@ -847,7 +861,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           }
         }
       }
-      hand_in(s, inf);
+      post(s);
     }
     // ---- phase 2 (fused): down units; the current unit has already been waited for ----
     if (FUSED && live) {
@@ -881,7 +895,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           rp[r] = accP;
           rp[r + 8] = accQ;
         }
-        hand_in(s, inf);
+        post(s);
         advance();
         if (!wait_full()) break;
         inf = info[cs];

@@ -117,6 +117,18 @@ def test_moe_decode_fused_c1(c1, b2q_mod, oracle):
     assert ws.status() == 0
 
 
+def test_moe_decode_fused_group_max_at_top_mantissa(c1, b2q_mod, oracle):
+    """x whose groups peak at +-(2 - 2^-7), the edge of the integer split."""
+    from test_gpu_products import _top_mantissa_x
+
+    x = _top_mantissa_x(1, c1["H"], 64, seed=7)
+    out, idx, w, lg = b2q_mod.moe_decode(x, c1["wr"], c1["L"], c1["k"], return_routing=True)
+    ridx, rw = oracle.route(_np(lg), c1["k"])
+    assert np.array_equal(_np(idx), ridx)
+    ref = oracle.moe_experts_decode(_np(x), ridx, rw, c1["Lnp"], c1["k"])
+    assert rel_l2(_bf(_np(out)), _bf(ref)) < TIGHT
+
+
 def test_moe_decode_multi_token(c1, b2q_mod, oracle):
     from b2q import synth
 

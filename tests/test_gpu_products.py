@@ -64,6 +64,34 @@ def test_qmv_streaming(cuda, b2q_mod, oracle, M, gs):
     assert rel_l2(_bf(_np(y)), _bf(ref)) < TIGHT
 
 
+def _top_mantissa_x(M, K, gs, seed):
+    """Activations whose every group has its max |x| at +-(2 - 2^-7): the
+    largest fixed-point value of the integer split (positive: the edge of the
+    int8 pieces' range)."""
+    import torch
+
+    from b2q import synth
+
+    x = synth.activations((M, K), seed=seed).float() * 0.25
+    g = torch.arange(K // gs, device=x.device)
+    pos = g * gs + (g * 7) % gs
+    sign = torch.where(g % 3 == 2, -1.0, 1.0).to(x.device)
+    x[:, pos] = sign * 1.9921875
+    return x.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("gs", [32, 64, 128])
+def test_qmv_group_max_at_top_mantissa(cuda, b2q_mod, oracle, gs):
+    from b2q import synth
+
+    N, K = 272, 2048
+    w, s, b = synth.packed_weights((N,), K, gs, seed=5)
+    x = _top_mantissa_x(1, K, gs, seed=6)
+    y = b2q_mod.quantized_matmul(x, w, s, b, True, gs, 4)
+    ref = oracle.qmv_metal(_np(x), _np(w), _np(s), _np(b), gs, 4)
+    assert rel_l2(_bf(_np(y)), _bf(ref)) < TIGHT
+
+
 def test_qmv_c0_full_size(cuda, b2q_mod, oracle):
     """Config 0: x [1, 4096], W [4096, 4096] g64."""
     from b2q import synth
