@@ -222,7 +222,7 @@ int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, co
   bool all_aligned = true;
   for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
   if (S == 1 && all_aligned && !decode_v1() && d2_moe_eligible(H, E, F, k, group_size)) {
-    const D2Scratch scr{&ws.hdr->error, ws.ctr, ws.logits, ws.act, ws.asum};
+    const D2Scratch scr{&ws.hdr->error, ws.ctr, ws.logits, ws.act, ws.asc};
     return d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size, scr,
                          st);
   }

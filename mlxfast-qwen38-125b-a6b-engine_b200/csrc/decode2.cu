@@ -1,5 +1,5 @@
-// decode2.cu -- single-column streaming products on a unit queue: qmv for one
-// row of x (M = 1) and the fused one-token MoE decode layer.
+// decode2.cu -- single-column streaming products: qmv for one row of x
+// (M = 1) and the fused one-token MoE decode layer.
 //
 // Reference operators (paths relative to the reference project):
 //   qmv_fast_impl / qdot       Vendor/mlx-swift/Source/Cmlx/mlx/mlx/backend/metal/kernels/quantized.h:28-105,191-290,757-822
@@ -7,39 +7,38 @@
 //   route (top-k + softmax)    Runner/FastModel/TrackFastMoE.swift:767-911
 //   combine association        Runner/FastModel/TrackFastKernels2.swift:36-47
 //
-// Organisation: one CTA per SM, one producer warp and 16 consumer warps.
+// Organisation: one CTA per SM: 16 consumer warps, a producer warp and an
+// epilogue warp.
 //  * The work of a call is a sequence of units, each one TMA fill of a stage:
 //      gate|up unit  16 outputs of one routed expert: its 16 gate rows and 16
 //                    up rows over the whole hidden size (two copies of 16 rows
 //                    x the whole row) plus their 4 scale / bias blocks;
-//      down unit     64 rows of one routed expert's down matrix over the whole
-//                    expert width, their scales / biases, and the expert's
-//                    SwiGLU activations (with their chunk sums);
+//      down unit     one 16-row block of the output for 4 routed slots: each
+//                    slot's 16 down rows over the whole expert width, their
+//                    scales / biases, and the slot's activations;
 //      qmv unit      32 rows of the matrix over the whole reduction.
-//    Units go round-robin over the CTAs (unit u to CTA u mod grid); fused
-//    calls order them all gate|up units slot by slot, then all down units
-//    slot by slot, so the down units of slot j start as soon as slot j's
-//    activations are final (a per-slot count of finished gate|up units), with
-//    no grid-wide barrier between the two phases. The static order keeps
-//    global round trips out of the producer's loop: at full bandwidth a
-//    round trip waits behind the CTA's copies in flight for microseconds.
+//    Units are assigned statically: qmv unit u to CTA u mod grid; gate|up
+//    unit u to CTA grid - 1 - u mod grid; down block j to CTA j mod grid,
+//    which streams the block's rows of every routed slot and folds the slots
+//    itself. A down unit waits only for its slots' activations to be final
+//    (a per-slot count of finished gate|up units): no grid-wide barrier
+//    between the phases. The static order keeps global round trips out of
+//    the producer's loop: at full bandwidth a round trip waits behind the
+//    CTA's copies in flight for microseconds.
 //  * Large copies (32 KB boxes of whole rows) keep the per-copy issue cost of
 //    the TMA small against the bytes moved.
 //  * The producer fills a ring of stages (full / empty mbarrier per stage) with
 //    whole-row TMA boxes in the 128-byte swizzle (16-byte unit u of row r at
 //    position u ^ (r % 8)); the consumer warps split the unit's reduction (or
-//    its row blocks and reduction) between them and hand their row partials
-//    to shared memory; the last warp to arrive finishes the unit: bf16 store
-//    (qmv), SwiGLU into the activations (gate|up) or the per-slot down
-//    products, and the last down unit of a 64-row block folds the k slots in
-//    the reference's combine order.
-//  * Dot products: nibbles OR-ed into bf16 128.0 give exactly 128 + q; the
-//    legacy mma.sync m16n8k16 (bf16 x bf16 -> fp32) multiplies 16 weight rows
-//    (P: 8 rows, Q: 8 rows) by the activation chunk, each product exact in
-//    fp32; per group: s * (D - 128 * sum(x)) + b * sum(x) (the Metal qdot
-//    factorisation, quantized.h:191-290) for down units; gate|up and qmv units
-//    (whose activation is the call's x) use integer MMAs on raw nibbles and
-//    an exact int8 split of x (see dot_i8).
+//    its slots and reduction) between them and post their row partials to
+//    shared memory; the epilogue warp sums them, releases the stage and does
+//    the unit's global work: bf16 store (qmv), SwiGLU activations (gate|up)
+//    or the block's slot table, whose last unit folds the k slots in the
+//    reference's combine order (down).
+//  * Dot products: integer MMAs (mma.sync m16n8k32 u8 x s8 -> s32) on the
+//    raw weight nibbles and an int8 split of the activation (see dot_i8):
+//    per group of x a 16-bit fixed point, per block of 16 SwiGLU outputs
+//    (made by the epilogue) the same with its own scale (see dot_i8_act).
 //  * Launches use programmatic dependent launch: barrier set-up, tensor-map
 //    prefetch and L2 prefetches (router rows; the first qmv units) run while
 //    the previous kernel in the stream finishes; nothing is read into the CTA
@@ -107,39 +106,16 @@ __device__ __forceinline__ int moff(int row, int g, int mb, bool sw) {
 // ---------------------------------------------------------------------------
 // Consumer warp arithmetic. A warp multiplies 16-row blocks (P: 8 rows, Q: 8
 // rows; lane (r = lane / 4, c = lane % 4) owns P row r and Q row r) by the
-// activation over chunk columns [cc0, cc0 + ncc); a chunk column is 32
-// reduction values, 16 bytes of every row. Word c of 16-byte unit u of a row
-// sits at  piece * PS + row * 128 + ((u ^ (row % 8)) << 4) + 4 c  (the TMA
-// 128-byte swizzle); P0 / Q0 are the byte offsets of P row 0 / Q row 0. The
-// quad lanes finish groups c of each batch of 4 groups.
+// activation over a range of chunk columns; a chunk column is 32 reduction
+// values, 16 bytes of every row. Word w of 16-byte unit u of a row sits at
+// piece * (rows * 128) + row * 128 + ((u ^ (row % 8)) << 4) + 4 w  (the TMA
+// 128-byte swizzle over boxes of `rows` rows).
 // ---------------------------------------------------------------------------
 struct Meta {
   const uint8_t *sP, *bP, *sQ, *bQ;
   int rowP, rowQ, mb;
   bool sw;
 };
-
-__device__ __forceinline__ void group_epilogue(const Meta& m, int ga, float xa, float eP, float eQ, float& accP,
-                                               float& accQ) {
-  const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m.sP + moff(m.rowP, ga, m.mb, m.sw)));
-  const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m.bP + moff(m.rowP, ga, m.mb, m.sw)));
-  const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(m.sQ + moff(m.rowQ, ga, m.mb, m.sw)));
-  const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(m.bQ + moff(m.rowQ, ga, m.mb, m.sw)));
-  const float xo = 128.0f * xa;
-  accP = fmaf(sP, eP - xo, fmaf(bP, xa, accP));
-  accQ = fmaf(sQ, eQ - xo, fmaf(bQ, xa, accQ));
-}
-
-__device__ __forceinline__ void mma_word_pair(float (&d)[4], uint32_t W0, uint32_t W8, const uint4& xv, bool first) {
-  uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
-  decode_word(W0, p0, p1, p2, p3);
-  decode_word(W8, q0, q1, q2, q3);
-  if (first)
-    mma_bf16_16816_zero(d, p0, q0, p1, q1, xv.x, xv.y);
-  else
-    mma_bf16_16816(d, p0, q0, p1, q1, xv.x, xv.y);
-  mma_bf16_16816(d, p2, q2, p3, q3, xv.z, xv.w);
-}
 
 // ---------------------------------------------------------------------------
 // Units whose activation is the call's x (gate|up, qmv): integer MMAs.
@@ -275,46 +251,62 @@ __device__ __forceinline__ void dot_i8(const uint8_t* st_base, const uint32_t (&
   }
 }
 
-// Activation chunks in shared memory (down units: the slot's activations are
-// part of the stage); gsum_lane: lane l < ng holds the sum over group l.
-template <int CPG>
-__device__ __forceinline__ void dot_xsmem(const uint8_t* wbase, int PS, int P0, int Q0, int cc0, int ncc,
-                                          const uint8_t* xch, float gsum_lane, const Meta& m, float& accP,
-                                          float& accQ) {
+// Down units: the activations are int8 pieces too, made by the epilogue from
+// the bf16 SwiGLU outputs of each gate|up unit with one scale per block of 16
+// values (the unit's outputs), 16 bytes per word like x's pieces; asc holds
+// (2^(E_b - 14), sum of the block's values) per block. One 32-value chunk per
+// lane slot; at step j lane c takes word j ^ c of its chunk (the four lanes of
+// a quad read four different words: no bank conflict), so steps 0, 1 cover
+// words c, c ^ 1 (block c / 2) and steps 2, 3 the chunk's other block: two
+// accumulators, one scale each.
+__device__ __forceinline__ void dot_i8_act(const uint8_t* wbox, const uint8_t* pcs, const float2* asc, int cc0,
+                                           int nslot, int gs, const Meta& m, float& accP, float& accQ) {
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
-  const int ng = ncc / CPG;
-  const int g0 = cc0 / CPG;
-  const uint8_t* wl = wbase + r * 128 + c * 4;
-  const uint8_t* xl = xch + c * 16;
-  for (int gb = 0; gb < ng; gb += 4) {
-    float D[4][4];
+  const bool diag = (r >> 1) == c;  // B lanes of lane c's column pair
+  const int spg = gs / 32;          // chunks per group
+  for (int t = 0; 4 * t < nslot; ++t) {
+    const int cc = cc0 + 4 * t + c;
+    const bool live = 4 * t + c < nslot;
+    const uint8_t* wr = wbox + (cc >> 3) * (ROWS_D * 128) + r * 128 + (((cc & 7) ^ r) << 4);
+    const uint8_t* xp = pcs + (size_t)cc * 64 + (r & 1) * 8;
+    int A[4] = {0, 0, 0, 0}, B[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int j = 0; j < CPG; ++j) {
-      uint32_t W0[4], W8[4];
-#pragma unroll
-      for (int gi = 0; gi < 4; ++gi) {
-        const bool live = gb + gi < ng;
-        const int cc = cc0 + (gb + gi) * CPG + j;
-        const uint8_t* wp = wl + (cc >> 3) * PS + (((cc & 7) ^ r) << 4);
-        W0[gi] = live ? *reinterpret_cast<const uint32_t*>(wp + P0) : 0u;
-        W8[gi] = live ? *reinterpret_cast<const uint32_t*>(wp + Q0) : 0u;
-      }
-#pragma unroll
-      for (int gi = 0; gi < 4; ++gi) {
-        const int cc = cc0 + (gb + gi) * CPG + j;
-        const uint4 xv = gb + gi < ng ? *reinterpret_cast<const uint4*>(xl + (size_t)cc * 64) : make_uint4(0u, 0u, 0u, 0u);
-        mma_word_pair(D[gi], W0[gi], W8[gi], xv, j == 0);
-      }
+    for (int j = 0; j < 4; ++j) {
+      const int w = j ^ c;
+      const uint32_t W0 = live ? *reinterpret_cast<const uint32_t*>(wr + 4 * w) : 0u;
+      const uint32_t W8 = live ? *reinterpret_cast<const uint32_t*>(wr + 4 * w + 8 * 128) : 0u;
+      uint2 xv = make_uint2(0u, 0u);
+      if (live && diag) xv = *reinterpret_cast<const uint2*>(xp + w * 16);
+      if (j < 2)
+        imma_u8s8(A, W0 & 0x0F0F0F0Fu, W8 & 0x0F0F0F0Fu, (W0 >> 4) & 0x0F0F0F0Fu, (W8 >> 4) & 0x0F0F0F0Fu, xv.x,
+                  xv.y);
+      else
+        imma_u8s8(B, W0 & 0x0F0F0F0Fu, W8 & 0x0F0F0F0Fu, (W0 >> 4) & 0x0F0F0F0Fu, (W8 >> 4) & 0x0F0F0F0Fu, xv.x,
+                  xv.y);
     }
-    float eP = D[0][0], eQ = D[0][2];
-#pragma unroll
-    for (int gi = 1; gi < 4; ++gi) {
-      eP = (c == gi) ? D[gi][0] : eP;
-      eQ = (c == gi) ? D[gi][2] : eQ;
+    // lane c: chunk cc of P row r (d0 hi, d1 lo) and Q row r (d2, d3)
+    float fP = 0.0f, fQ = 0.0f, xs = 0.0f;
+    if (live) {
+      const float2 sa = asc[2 * cc + (c >> 1)], sb = asc[2 * cc + ((c >> 1) ^ 1)];
+      fP = (float)(256 * A[0] + A[1]) * sa.x + (float)(256 * B[0] + B[1]) * sb.x;
+      fQ = (float)(256 * A[2] + A[3]) * sa.x + (float)(256 * B[2] + B[3]) * sb.x;
+      xs = sa.y + sb.y;
     }
-    const int gl = gb + c;
-    const float xa = __shfl_sync(0xffffffffu, gsum_lane, gl & 31);
-    if (gl < ng) group_epilogue(m, g0 + gl, xa, eP, eQ, accP, accQ);
+    // groups of spg chunks: lanes c, c ^ 1 (, c ^ 2) hold one group
+    for (int o = 1; o < spg; o <<= 1) {
+      fP += __shfl_xor_sync(0xffffffffu, fP, o);
+      fQ += __shfl_xor_sync(0xffffffffu, fQ, o);
+      xs += __shfl_xor_sync(0xffffffffu, xs, o);
+    }
+    if (live && (c & (spg - 1)) == 0) {
+      const int g = cc / spg;
+      const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m.sP + moff(m.rowP, g, m.mb, m.sw)));
+      const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m.bP + moff(m.rowP, g, m.mb, m.sw)));
+      const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(m.sQ + moff(m.rowQ, g, m.mb, m.sw)));
+      const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(m.bQ + moff(m.rowQ, g, m.mb, m.sw)));
+      accP = fmaf(sP, fP, fmaf(bP, xs, accP));
+      accQ = fmaf(sQ, fQ, fmaf(bQ, xs, accQ));
+    }
   }
 }
 
@@ -660,7 +652,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
             tc::tma_load_2d(m, &p.map[MSD], 0, row, &full[s], pol);
             tc::tma_load_2d(m + p.st_mstep2, &p.map[MBD], 0, row, &full[s], pol);
             bulk_g2s(st + p.st_act + i * F * 2, p.ws_act + (size_t)z * F, (uint32_t)F * 2u, &full[s], pol_keep);
-            bulk_g2s(st + p.st_asum + i * (F / 2), p.ws_asum + (size_t)z * (F / 8), (uint32_t)F / 2u, &full[s],
+            bulk_g2s(st + p.st_asc + i * (F / 2), p.ws_asc + (size_t)z * (F / 16), (uint32_t)F / 2u, &full[s],
                      pol_keep);
           }
         }
@@ -731,20 +723,37 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       if (FUSED && inf.x == U_GU) {
         // t0 at lane l: row l of [gate 0..7][up 0..7][gate 8..15][up 8..15]
         const int z = inf.y, blk = inf.z;
-        const int f = lane & 15;  // output of lanes 0..15
+        const int f = lane & 15;  // output f of the unit (lanes 16..31 repeat lanes 0..15)
         const float g = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + (f & 7));
         const float up = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + 8 + (f & 7));
-        uint16_t a = 0;
-        if (lane < 16) {
-          a = swiglu_bf16(f2bf(g), f2bf(up));
-          const int j = f & 7, pos = j < 4 ? 2 * j : 2 * (j - 4) + 1;
-          p.ws_act[(size_t)z * F + blk * ROWS_GU + (f >> 3) * 8 + pos] = a;
+        const uint16_t a = swiglu_bf16(f2bf(g), f2bf(up));
+        // the block of 16 as int8 pieces: scale 2^(14 - E) from the max |a|,
+        // X = round(a * 2^(14 - E)) <= 32639 (as for x), hi = byte 1 of
+        // X + 128, lo = byte 0 of X
+        unsigned mx = a & 0x7fffu;
+        float sm = lane < 16 ? bf2f(a) : 0.0f;
+#pragma unroll
+        for (int off = 1; off < 16; off <<= 1) {
+          mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          sm += __shfl_xor_sync(0xffffffffu, sm, off);
         }
-        float af = lane < 16 ? bf2f(a) : 0.0f;
-        af += __shfl_xor_sync(0xffffffffu, af, 1);
-        af += __shfl_xor_sync(0xffffffffu, af, 2);
-        af += __shfl_xor_sync(0xffffffffu, af, 4);
-        if (lane == 0 || lane == 8) p.ws_asum[(size_t)z * (F / 8) + blk * 2 + (lane >> 3)] = af;
+        int e = (int)((mx >> 7) & 0xffu) - 127;
+        if (mx == 0u || mx >= 0x7f80u) e = 0;
+        e = max(-110, min(120, e));
+        const int X = min(__float2int_rn(bf2f(a) * __int_as_float((127 + 14 - e) << 23)), 32639);
+        const uint32_t hb = ((uint32_t)(X + 128) >> 8) & 0xffu, lb = (uint32_t)X & 0xffu;
+        // lane l < 8 builds 32-bit piece q = l % 4 of word l / 4: byte i is value
+        // 2 i (+1 for odd q) of the word, hi pieces for q < 2, lo for q >= 2
+        const int wq = (lane >> 2) & 1, q = lane & 3;
+        uint32_t pw = 0u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int src = 8 * wq + 2 * i + (q & 1);
+          const uint32_t hv = __shfl_sync(0xffffffffu, hb, src), lv = __shfl_sync(0xffffffffu, lb, src);
+          pw |= ((q & 2) ? lv : hv) << (8 * i);
+        }
+        if (lane < 8) reinterpret_cast<uint32_t*>(p.ws_act + (size_t)z * F + blk * ROWS_GU)[lane] = pw;
+        if (lane == 0) p.ws_asc[(size_t)z * (F / 16) + blk] = make_float2(__int_as_float((127 + e - 14) << 23), sm);
         pend += 1ull << (8 * z);
       } else if (FUSED) {
         // rows lane, lane + 32: slot quad * 4 + row / 16, block row row % 16;
@@ -872,20 +881,13 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         float* rp = red + ((size_t)s * NCW + warp) * 32;
         // 4 slots (16 rows each) x 4 reduction quarters
         const int b = warp >> 2, qw = warp & 3, nsl = inf.w >> 8;
-        const int ncc = F / 32 / 4, cc0 = qw * ncc, ng = ncc / CPG;
         float accP = 0.0f, accQ = 0.0f;
         if (b < nsl) {
-          const float* as = reinterpret_cast<const float*>(st + p.st_asum + b * (F / 2));
-          float gl_sum = 0.0f;
-          if (lane < ng) {
-            const int q0 = (cc0 / CPG + lane) * CPC;
-#pragma unroll
-            for (int i = 0; i < CPC; ++i) gl_sum += as[q0 + i];
-          }
           const uint8_t* mb = st + p.st_meta2 + b * 2 * p.st_mstep2;
           const Meta m{mb, mb + p.st_mstep2, mb, mb + p.st_mstep2, r, 8 + r, p.mb2, p.sw2 != 0};
-          dot_xsmem<CPG>(st + b * (ROWS_D * F / 2), ROWS_D * 128, 0, 1024, cc0, ncc, st + p.st_act + b * F * 2,
-                         gl_sum, m, accP, accQ);
+          dot_i8_act(st + b * (ROWS_D * F / 2), st + p.st_act + b * F * 2,
+                     reinterpret_cast<const float2*>(st + p.st_asc + b * (F / 2)), qw * (F / 128), F / 128, p.gs, m,
+                     accP, accQ);
         }
         accP += __shfl_xor_sync(0xffffffffu, accP, 1);
         accQ += __shfl_xor_sync(0xffffffffu, accQ, 1);
@@ -938,7 +940,7 @@ static int plan(D2Params& p, int mode) {
     p.st_meta1 = ROWS_QMV * K1 / 2;
     p.st_mstep1 = round_up(ROWS_QMV * p.mb1, p.sw1 ? 1024 : 128);
     st = p.st_meta1 + 2 * p.st_mstep1;
-    p.mb2 = p.sw2 = p.st_meta2 = p.st_mstep2 = p.st_act = p.st_asum = 0;
+    p.mb2 = p.sw2 = p.st_meta2 = p.st_mstep2 = p.st_act = p.st_asc = 0;
   } else {
     p.st_meta1 = 2 * ROWS_GU * K1 / 2;
     p.st_mstep1 = round_up(ROWS_GU * p.mb1, p.sw1 ? 1024 : 128);
@@ -949,8 +951,8 @@ static int plan(D2Params& p, int mode) {
     p.st_meta2 = SLOTS_D * ROWS_D * p.F / 2;
     p.st_mstep2 = round_up(ROWS_D * p.mb2, p.sw2 ? 1024 : 128);
     p.st_act = p.st_meta2 + SLOTS_D * 2 * p.st_mstep2;
-    p.st_asum = p.st_act + SLOTS_D * p.F * 2;
-    const int dn = p.st_asum + SLOTS_D * p.F / 2;
+    p.st_asc = p.st_act + SLOTS_D * p.F * 2;
+    const int dn = p.st_asc + SLOTS_D * p.F / 2;
     st = std::max(gu, dn);
   }
   p.stage_bytes = round_up(st, 1024);
@@ -1179,7 +1181,7 @@ int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
   p.ctr = scr.ctr;
   p.ws_logits = scr.logits;
   p.ws_act = scr.act;
-  p.ws_asum = scr.asum;
+  p.ws_asc = scr.asc;
   p.e_lo = e_lo;
   p.e_local = e_local;
   p.out_f32 = out_f32;

@@ -34,8 +34,8 @@ struct alignas(64) D2Params {
   int* err;
   unsigned* ctr;
   float* ws_logits;   // [E]
-  uint16_t* ws_act;   // [k][F] SwiGLU activations, 8-value chunks stored as (a0,a4,a1,a5,a2,a6,a3,a7)
-  float* ws_asum;     // [k][F / 8] chunk sums of the activations
+  uint16_t* ws_act;   // [k][F] SwiGLU activations as int8 pieces (16 bytes per word of 8 values)
+  float2* ws_asc;     // [k][F / 16] per block of 16 activations: (2^(E - 14), sum)
   long long timeout_ns;
   int e_lo, e_local;  // expert parallel: this rank holds experts [e_lo, e_lo + e_local) (e_local 0: all)
   float* out_f32;     // expert parallel: fp32 partial output instead of bf16 `out`
@@ -45,7 +45,7 @@ struct alignas(64) D2Params {
   int mb1, mb2;             // metadata row bytes: first family, down
   int sw1, sw2;             // metadata blocks in the 128-byte swizzle
   int st_meta1, st_mstep1;  // first family: metadata blocks inside a stage
-  int st_meta2, st_mstep2, st_act, st_asum;  // down units
+  int st_meta2, st_mstep2, st_act, st_asc;  // down units
 };
 
 bool d2_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const void* s, const void* b);
@@ -59,7 +59,7 @@ struct D2Scratch {
   unsigned* ctr;      // d2_counter_words(H)
   float* logits;      // [E]
   uint16_t* act;      // [k][F]
-  float* asum;        // [k][F / 8]
+  float2* asc;        // [k][F / 16]
 };
 int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,

@@ -42,7 +42,7 @@ struct DecodeWs {
   uint32_t* idx;
   float* w;
   uint16_t* act;
-  float* asum;    // one-token fused kernel: chunk sums of the activations [k][F / 8]
+  float2* asc;    // one-token fused kernel: per block of 16 activations (scale, sum) [k][F / 16]
   size_t bytes;
 };
 
@@ -68,8 +68,8 @@ static inline DecodeWs decode_ws_layout(void* base, int S, int H, int E, int F, 
   off = align256(off + sizeof(float) * (size_t)S * k);
   d.act = reinterpret_cast<uint16_t*>(b + off);
   off = align256(off + sizeof(uint16_t) * (size_t)S * k * F);
-  d.asum = reinterpret_cast<float*>(b + off);
-  off = align256(off + sizeof(float) * (size_t)k * (F / 8));
+  d.asc = reinterpret_cast<float2*>(b + off);
+  off = align256(off + sizeof(float2) * (size_t)k * (F / 16));
   d.bytes = off;
   return d;
 }

@@ -82,7 +82,7 @@ struct EpDecodeWs {
   uint32_t* rhs;  // local expert of each slot, 0xFFFFFFFF when not held here
   uint32_t* tok;  // token of each slot
   uint16_t *g, *u, *act, *y;
-  float* asum;    // one-token fused kernel: activation chunk sums
+  float2* asc;    // one-token fused kernel: per block of 16 activations (scale, sum)
   unsigned* ctr;  // one-token fused kernel: grid counters (fixed offset)
   size_t bytes;
 };
@@ -114,8 +114,8 @@ EpDecodeWs ep_decode_layout(void* base, int S, int H, int E, int F, int k) {
   off = a256(off + 2 * R * F);
   d.y = reinterpret_cast<uint16_t*>(b + off);
   off = a256(off + 2 * R * H);
-  d.asum = reinterpret_cast<float*>(b + off);
-  off = a256(off + 4 * R * (F / 8));
+  d.asc = reinterpret_cast<float2*>(b + off);
+  off = a256(off + 8 * R * (F / 16));
   d.bytes = off;
   return d;
 }
@@ -341,7 +341,7 @@ int b2q_ep_moe_decode(void* comm, const uint16_t* x, const uint16_t* wr, const u
     bool all_aligned = true;
     for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
     if (all_aligned && !decode_v1() && d2_moe_eligible(H, E, F, k, group_size)) {
-      const D2Scratch scr{ws.err, ws.ctr, ws.logits, ws.act, ws.asum};
+      const D2Scratch scr{ws.err, ws.ctr, ws.logits, ws.act, ws.asc};
       rc = d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, nullptr, idx, w, nullptr, H, E, F, k, group_size,
                          scr, st, e_lo, e_local, partial);
       if (rc) return rc;
