@@ -626,17 +626,20 @@ def main():
     host_x.copy_(xs[: (n_e2e + args.warmup)].view(-1, 1, H).cpu())
     host_out = torch.empty((1, H), dtype=torch.bfloat16).pin_memory()
     dx = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+    dy = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+    # the one-token call writes a persistent output buffer (no allocation per call)
+    call_kw = {"out": dy} if comm is None else {}
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             dx.copy_(host_x[i], non_blocking=True)
-            y = moe[i % n_layers](dx)
+            y = moe[i % n_layers](dx, **call_kw)
             host_out.copy_(y, non_blocking=True)
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(n_e2e):
             dx.copy_(host_x[args.warmup + i], non_blocking=True)
-            y = moe[i % n_layers](dx)
+            y = moe[i % n_layers](dx, **call_kw)
             host_out.copy_(y, non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize(dev)

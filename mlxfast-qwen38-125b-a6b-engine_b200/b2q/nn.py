@@ -101,23 +101,32 @@ class MoE:
     def num_experts(self) -> int:
         return self.router_weight.shape[0]
 
-    def _decode_one(self, x2: torch.Tensor) -> torch.Tensor:
-        """One token through the fused decode operator with the prepared arguments."""
+    def _decode_one(self, x2: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """One token through the fused decode operator with the prepared
+        arguments; ``out`` (CUDA bf16, H elements, contiguous) is written in place
+        of a new tensor, so a caller's decode loop allocates nothing."""
         if x2.dtype != torch.bfloat16 or x2.device.type != "cuda" or x2.shape[1] != self._H:
             raise ValueError("x: expected a CUDA bf16 tensor [1, H] matching the router weight")
         if self._ws1 is None or self._ws1.buf.device != x2.device:
             size = ops.lib().b2q_moe_decode_workspace_size(1, self._H, self._E, self._F, self.top_k)
             self._ws1 = ops.Workspace(size, x2.device)
-        out = torch.empty((1, self._H), dtype=torch.bfloat16, device=x2.device)
+        if out is None:
+            out = torch.empty((1, self._H), dtype=torch.bfloat16, device=x2.device)
+        elif (out.dtype != torch.bfloat16 or out.device != x2.device or out.numel() != self._H
+              or not out.is_contiguous()):
+            raise ValueError("out: expected a contiguous CUDA bf16 tensor of H elements on x's device")
         ops.check(ops.lib().b2q_moe_decode(x2.data_ptr(), *self._wptrs, out.data_ptr(), None, None, None, 1, self._H,
                                            self._E, self._F, self.top_k, self.group_size, self.bits, self._ws1.ptr(),
                                            self._ws1.buf.numel(), ops._stream(x2.device)))
         return out
 
-    def __call__(self, x: torch.Tensor, return_routing: bool = False):
+    def __call__(self, x: torch.Tensor, return_routing: bool = False, out: torch.Tensor | None = None):
+        """``out`` (one-token calls only): a persistent output buffer the call writes."""
         x2 = x.contiguous().view(-1, x.shape[-1])
         if x2.shape[0] == 1 and not return_routing:
-            return self._decode_one(x2).view(x.shape)
+            return self._decode_one(x2, out).view(x.shape)
+        if out is not None:
+            raise ValueError("out: only for one-token calls without routing outputs")
         if x2.shape[0] <= 8:
             r = ops.moe_decode(x2, self.router_weight, self.experts, self.top_k, self.group_size, self.bits,
                                return_routing=return_routing)

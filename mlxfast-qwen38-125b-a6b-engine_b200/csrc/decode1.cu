@@ -420,7 +420,9 @@ struct Shape {
 template <int WPT, int MODE>
 __global__ void __launch_bounds__(NTH, 1) d1_kernel(const __grid_constant__ D1Params p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // aligned by pointer arithmetic on the shared array (an integer round trip
+  // would hide the address space and turn every shared access generic)
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint8_t* slots = smem + p.off_slots;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_misc);

@@ -338,7 +338,9 @@ template <int CPG, int MODE>
 __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Params p) {
   constexpr int SLOT = CPG == 1 ? 32 : 64;  // reduction values per column slot of the integer MMAs
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // aligned by pointer arithmetic on the shared array (an integer round trip
+  // would hide the address space and turn every shared access generic)
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   constexpr bool FUSED = MODE != D2_QMV;
   constexpr bool EP = MODE == D2_FUSED_EP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

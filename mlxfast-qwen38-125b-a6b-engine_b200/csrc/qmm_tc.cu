@@ -260,7 +260,9 @@ __device__ __forceinline__ void dequant_role(const TcParams& p, Smem& sm, uint32
 template <int MODE, int GS>
 __global__ void __launch_bounds__(NTHREADS + 32, 1) qmm_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // aligned by pointer arithmetic on the shared array (an integer round trip
+  // would hide the address space and turn every shared access generic)
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = p.E;
   const int MT = (MODE == TC_GLU) ? p.Nw / 64 : p.Nw / TILE_M;
