@@ -63,7 +63,8 @@ namespace b2q {
 namespace d2 {
 
 constexpr int NCW = 16;              // consumer warps
-constexpr int NWARP = NCW + 2;       // + the producer warp and the epilogue warp
+constexpr int NEPI = 2;              // epilogue warps (unit n: warp n % NEPI)
+constexpr int NWARP = NCW + 1 + NEPI; // + the producer warp and the epilogue warps
 constexpr int NTH = NWARP * 32;
 constexpr int MAXK = 8;              // routed slots
 constexpr int MAXST = 6;             // stages at most
@@ -231,20 +232,20 @@ __device__ __forceinline__ void dot_i8(const uint8_t* st_base, const uint32_t (&
       const int g = (slot0 + slot) / spg;
 #pragma unroll
       for (int b = 0; b < NRB; ++b) {
-        int vP = 256 * (D[b][0][0] + D[b][1][0]) + (D[b][0][1] + D[b][1][1]);
-        int vQ = 256 * (D[b][0][2] + D[b][1][2]) + (D[b][0][3] + D[b][1][3]);
-        if (spg == 2) {  // two slots per group: lanes c and c ^ 1 hold one group
-          vP += __shfl_xor_sync(0xffffffffu, vP, 1);
-          vQ += __shfl_xor_sync(0xffffffffu, vQ, 1);
-        }
-        if (live && (spg == 1 || (c & 1) == 0)) {
+        const int vP = 256 * (D[b][0][0] + D[b][1][0]) + (D[b][0][1] + D[b][1][1]);
+        const int vQ = 256 * (D[b][0][2] + D[b][1][2]) + (D[b][0][3] + D[b][1][3]);
+        // each lane scales its slot; with two slots per group (spg 2) the bias
+        // term b * sum(x) goes with the group's first slot, and the quad sum at
+        // the end adds the slots
+        if (live) {
           const float2 sc = gsc[g];
+          const float xg = (spg == 1 || (c & 1) == 0) ? sc.y : 0.0f;
           const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
           const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
           const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw)));
           const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw)));
-          accP[b] = fmaf(sP, (float)vP * sc.x, fmaf(bP, sc.y, accP[b]));
-          accQ[b] = fmaf(sQ, (float)vQ * sc.x, fmaf(bQ, sc.y, accQ[b]));
+          accP[b] = fmaf(sP, (float)vP * sc.x, fmaf(bP, xg, accP[b]));
+          accQ[b] = fmaf(sQ, (float)vQ * sc.x, fmaf(bQ, xg, accQ[b]));
         }
       }
     }
@@ -259,53 +260,63 @@ __device__ __forceinline__ void dot_i8(const uint8_t* st_base, const uint32_t (&
 // a quad read four different words: no bank conflict), so steps 0, 1 cover
 // words c, c ^ 1 (block c / 2) and steps 2, 3 the chunk's other block: two
 // accumulators, one scale each.
+template <int U>
 __device__ __forceinline__ void dot_i8_act(const uint8_t* wbox, const uint8_t* pcs, const float2* asc, int cc0,
                                            int nslot, int gs, const Meta& m, float& accP, float& accQ) {
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
   const bool diag = (r >> 1) == c;  // B lanes of lane c's column pair
   const int spg = gs / 32;          // chunks per group
-  for (int t = 0; 4 * t < nslot; ++t) {
-    const int cc = cc0 + 4 * t + c;
-    const bool live = 4 * t + c < nslot;
-    const uint8_t* wr = wbox + (cc >> 3) * (ROWS_D * 128) + r * 128 + (((cc & 7) ^ r) << 4);
-    const uint8_t* xp = pcs + (size_t)cc * 64 + (r & 1) * 8;
-    int A[4] = {0, 0, 0, 0}, B[4] = {0, 0, 0, 0};
+  // U rounds of 4 chunks per pass, unrolled so that the loads and MMAs of a
+  // round overlap the epilogue of the one before (nslot is a multiple of 4 U
+  // for U > 1)
+  for (int t0 = 0; 4 * t0 < nslot; t0 += U) {
+    int A[U][4], B[U][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int w = j ^ c;
-      const uint32_t W0 = live ? *reinterpret_cast<const uint32_t*>(wr + 4 * w) : 0u;
-      const uint32_t W8 = live ? *reinterpret_cast<const uint32_t*>(wr + 4 * w + 8 * 128) : 0u;
-      uint2 xv = make_uint2(0u, 0u);
-      if (live && diag) xv = *reinterpret_cast<const uint2*>(xp + w * 16);
-      if (j < 2)
-        imma_u8s8(A, W0 & 0x0F0F0F0Fu, W8 & 0x0F0F0F0Fu, (W0 >> 4) & 0x0F0F0F0Fu, (W8 >> 4) & 0x0F0F0F0Fu, xv.x,
-                  xv.y);
-      else
-        imma_u8s8(B, W0 & 0x0F0F0F0Fu, W8 & 0x0F0F0F0Fu, (W0 >> 4) & 0x0F0F0F0Fu, (W8 >> 4) & 0x0F0F0F0Fu, xv.x,
-                  xv.y);
+    for (int u = 0; u < U; ++u) {
+      const int cc = cc0 + 4 * (t0 + u) + c;
+      const bool live = U > 1 || 4 * (t0 + u) + c < nslot;
+      const uint8_t* wr = wbox + (cc >> 3) * (ROWS_D * 128) + r * 128 + (((cc & 7) ^ r) << 4);
+      const uint8_t* xp = pcs + (size_t)cc * 64 + (r & 1) * 8;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) A[u][i] = B[u][i] = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int w = j ^ c;
+        const uint32_t W0 = live ? *reinterpret_cast<const uint32_t*>(wr + 4 * w) : 0u;
+        const uint32_t W8 = live ? *reinterpret_cast<const uint32_t*>(wr + 4 * w + 8 * 128) : 0u;
+        uint2 xv = make_uint2(0u, 0u);
+        if (live && diag) xv = *reinterpret_cast<const uint2*>(xp + w * 16);
+        if (j < 2)
+          imma_u8s8(A[u], W0 & 0x0F0F0F0Fu, W8 & 0x0F0F0F0Fu, (W0 >> 4) & 0x0F0F0F0Fu, (W8 >> 4) & 0x0F0F0F0Fu,
+                    xv.x, xv.y);
+        else
+          imma_u8s8(B[u], W0 & 0x0F0F0F0Fu, W8 & 0x0F0F0F0Fu, (W0 >> 4) & 0x0F0F0F0Fu, (W8 >> 4) & 0x0F0F0F0Fu,
+                    xv.x, xv.y);
+      }
     }
-    // lane c: chunk cc of P row r (d0 hi, d1 lo) and Q row r (d2, d3)
-    float fP = 0.0f, fQ = 0.0f, xs = 0.0f;
-    if (live) {
-      const float2 sa = asc[2 * cc + (c >> 1)], sb = asc[2 * cc + ((c >> 1) ^ 1)];
-      fP = (float)(256 * A[0] + A[1]) * sa.x + (float)(256 * B[0] + B[1]) * sb.x;
-      fQ = (float)(256 * A[2] + A[3]) * sa.x + (float)(256 * B[2] + B[3]) * sb.x;
-      xs = sa.y + sb.y;
-    }
-    // groups of spg chunks: lanes c, c ^ 1 (, c ^ 2) hold one group
-    for (int o = 1; o < spg; o <<= 1) {
-      fP += __shfl_xor_sync(0xffffffffu, fP, o);
-      fQ += __shfl_xor_sync(0xffffffffu, fQ, o);
-      xs += __shfl_xor_sync(0xffffffffu, xs, o);
-    }
-    if (live && (c & (spg - 1)) == 0) {
-      const int g = cc / spg;
-      const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m.sP + moff(m.rowP, g, m.mb, m.sw)));
-      const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m.bP + moff(m.rowP, g, m.mb, m.sw)));
-      const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(m.sQ + moff(m.rowQ, g, m.mb, m.sw)));
-      const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(m.bQ + moff(m.rowQ, g, m.mb, m.sw)));
-      accP = fmaf(sP, fP, fmaf(bP, xs, accP));
-      accQ = fmaf(sQ, fQ, fmaf(bQ, xs, accQ));
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      // lane c: chunk cc of P row r (d0 hi, d1 lo) and Q row r (d2, d3)
+      const int cc = cc0 + 4 * (t0 + u) + c;
+      const bool live = U > 1 || 4 * (t0 + u) + c < nslot;
+      float fP = 0.0f, fQ = 0.0f, xs = 0.0f;
+      if (live) {
+        const float2 sa = asc[2 * cc + (c >> 1)], sb = asc[2 * cc + ((c >> 1) ^ 1)];
+        fP = (float)(256 * A[u][0] + A[u][1]) * sa.x + (float)(256 * B[u][0] + B[u][1]) * sb.x;
+        fQ = (float)(256 * A[u][2] + A[u][3]) * sa.x + (float)(256 * B[u][2] + B[u][3]) * sb.x;
+        xs = sa.y + sb.y;
+      }
+      // each lane scales its chunk by its group's scale / bias; the quad sum at
+      // the end adds the chunks of a group (spg > 1) with the rest
+      if (live) {
+        const int g = cc / spg;
+        const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m.sP + moff(m.rowP, g, m.mb, m.sw)));
+        const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m.bP + moff(m.rowP, g, m.mb, m.sw)));
+        const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(m.sQ + moff(m.rowQ, g, m.mb, m.sw)));
+        const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(m.bQ + moff(m.rowQ, g, m.mb, m.sw)));
+        accP = fmaf(sP, fP, fmaf(bP, xs, accP));
+        accQ = fmaf(sQ, fQ, fmaf(bQ, xs, accQ));
+      }
     }
   }
 }
@@ -358,6 +369,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   int* lslot = reinterpret_cast<int*>(sw + MAXK);                // [MAXK] routed slots held here (EP)
   float* rsum = reinterpret_cast<float*>(lslot + MAXK);          // [NWARP]
   int* lastf_sm = reinterpret_cast<int*>(rsum + NWARP);          // [MAXST] producer bookkeeping
+  unsigned* ycnt = reinterpret_cast<unsigned*>(lastf_sm + MAXST); // [MAXBLK] down units finished per block
   float* ysm = reinterpret_cast<float*>(smem + p.off_ysm);       // [MAXBLK][MAXK][ROWS_D] slot products
   float* red = reinterpret_cast<float*>(smem + p.off_red);       // [nstage][NCW][32]
   float2* gsc = reinterpret_cast<float2*>(smem + p.off_xs);     // per group: 2^(E_g - 14), sum(x)
@@ -369,6 +381,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       mbar_init(&empty[i], 1);
       mbar_init(&rfull[i], NCW);
     }
+    for (int i = 0; i < MAXBLK; ++i) ycnt[i] = 0u;
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -625,13 +638,30 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           const int d = it - ngu, nbk = max(nblk, 1), quad = d / nbk, lb = d % nbk, blk = bx + lb * G;
           const int z0 = quad * SLOTS_D, nsl = min(SLOTS_D, nloc - z0);
           // the slots' activations must be final: every gate|up unit of them
-          // finished (one acquire per slot and CTA)
+          // finished. The counts of the unit's slots not yet seen final are
+          // read together (one round trip per poll, not one per slot).
           bool ok = true;
-          for (int i = 0; i < nsl && ok; ++i) {
-            const int z = z0 + i;
-            if ((ready >> z) & 1u) continue;
-            ok = wait_counter_geq(&done[z], (unsigned)(F / ROWS_GU), deadline, abort_flag);
-            ready |= 1u << z;
+          const uint32_t need = (((1u << nsl) - 1u) << z0) & ~ready;
+          if (need) {
+            for (uint32_t n = 0;; ++n) {
+              uint32_t seen = 0u;
+#pragma unroll
+              for (int i = 0; i < SLOTS_D; ++i) {
+                const int z = z0 + i;
+                if ((need >> z) & 1u)
+                  seen |= (ld_relaxed_u32(&done[z]) >= (unsigned)(F / ROWS_GU) ? 1u : 0u) << z;
+              }
+              if (seen == need) break;
+              if (*abort_flag || ((n & 15u) == 15u && globaltimer() > deadline)) {
+                ok = false;
+                break;
+              }
+              __nanosleep(32);
+            }
+            // relaxed reads that saw the counts, then one fence: the acquire
+            // side of the epilogues' release counts
+            fence_acq_rel_gpu();
+            ready |= need;
           }
           if (!ok) {
             if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
@@ -653,10 +683,11 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
             tma3(st + i * wb, &p.map[MWD], 0, row, 0, &full[s], pol);
             tc::tma_load_2d(m, &p.map[MSD], 0, row, &full[s], pol);
             tc::tma_load_2d(m + p.st_mstep2, &p.map[MBD], 0, row, &full[s], pol);
-            bulk_g2s(st + p.st_act + i * F * 2, p.ws_act + (size_t)z * F, (uint32_t)F * 2u, &full[s], pol_keep);
-            bulk_g2s(st + p.st_asc + i * (F / 2), p.ws_asc + (size_t)z * (F / 16), (uint32_t)F / 2u, &full[s],
-                     pol_keep);
           }
+          // the unit's slots are consecutive: their activations and block
+          // scales (written by the epilogues, in L2) are one copy each
+          bulk_g2s(st + p.st_act, p.ws_act + (size_t)z0 * F, (uint32_t)(nsl * F * 2), &full[s], pol_keep);
+          bulk_g2s(st + p.st_asc, p.ws_asc + (size_t)z0 * (F / 16), (uint32_t)(nsl * F / 2), &full[s], pol_keep);
         }
         lastf[s] = (int)(eph ^ 1u);
       }
@@ -668,37 +699,23 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         if (lastf[i] >= 0) tc::wait_until(&full[i], (uint32_t)lastf[i], dl);
     }
     __syncwarp();
-  } else if (warp == NCW + 1) {
+  } else if (warp > NCW) {
     // ------------------------------ epilogue ------------------------------
-    // Finishes the units in order once the consumers posted their partials:
-    // it releases the stage, then does the unit's global work (bf16 store,
-    // SwiGLU activations, or the down block's slot table and fold). Finished
-    // gate|up units are published (fence, then per-slot counts) only when the
-    // next unit's partials are not in yet: a fence waits for this warp's
-    // stores to be acknowledged, microseconds at full bandwidth, and stalls
-    // no other warp here.
-    uint64_t pend = 0ull;  // gate|up units finished and not yet published, 8 bits per slot
-    auto publish = [&]() {
-      __syncwarp();
-      if (lane == 0 && pend != 0ull) {
-        __threadfence();
-        for (int z = 0; z < MAXK; ++z) {
-          const unsigned cz = (unsigned)(pend >> (8 * z)) & 0xffu;
-          if (cz) atomicAdd(&done[z], cz);
-        }
-      }
-      pend = 0ull;
-    };
-    int s = 0;
-    uint32_t ph = 0u;
-    for (int n = 0; n < UT; ++n) {
-      if (!__shfl_sync(0xffffffffu, tc::test_wait(&rfull[s], ph) ? 1 : 0, 0)) {
-        if (FUSED) publish();
-        if (!__all_sync(0xffffffffu, tc::wait(&rfull[s], ph, deadline, abort_flag))) {
-          if (!*abort_flag && lane == 0) record_error(p.err, B2Q_ETIMEOUT);
-          *abort_flag = 1;
-          break;
-        }
+    // Epilogue warp e finishes units e, e + NEPI, ... once the consumers
+    // posted their partials: it releases the stage, then does the unit's
+    // global work (bf16 store, SwiGLU activations, or the down block's slot
+    // table and fold). A finished gate|up unit is published at once (fence,
+    // then the slot's count): the fence waits for this warp's stores to be
+    // acknowledged, which at full bandwidth takes about as long as a unit
+    // streams, so the units alternate between warps and no compute warp waits.
+    const int ew = warp - NCW - 1;
+    for (int n = ew; n < UT; n += NEPI) {
+      const int s = n % NS;
+      const uint32_t ph = (uint32_t)(n / NS) & 1u;
+      if (!__all_sync(0xffffffffu, tc::wait(&rfull[s], ph, deadline, abort_flag))) {
+        if (!*abort_flag && lane == 0) record_error(p.err, B2Q_ETIMEOUT);
+        *abort_flag = 1;
+        break;
       }
       const int4 inf = info[s];
       const float* rb = red + (size_t)s * NCW * 32;
@@ -713,15 +730,18 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           if (h2 == 0) t0 = y2; else t1 = y2;
         }
       } else {
-        // lane l: total of partial row l over the warps
-        for (int w = 0; w < NCW; ++w) t0 += rb[w * 32 + lane];
+        // lane l: total of partial row l over the warps (pairwise)
+        float v[NCW];
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) v[w] = rb[w * 32 + lane];
+#pragma unroll
+        for (int h = NCW / 2; h >= 1; h >>= 1)
+#pragma unroll
+          for (int w = 0; w < h; ++w) v[w] += v[w + h];
+        t0 = v[0];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      if (++s == NS) {
-        s = 0;
-        ph ^= 1u;
-      }
       if (FUSED && inf.x == U_GU) {
         // t0 at lane l: row l of [gate 0..7][up 0..7][gate 8..15][up 8..15]
         const int z = inf.y, blk = inf.z;
@@ -756,7 +776,10 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         }
         if (lane < 8) reinterpret_cast<uint32_t*>(p.ws_act + (size_t)z * F + blk * ROWS_GU)[lane] = pw;
         if (lane == 0) p.ws_asc[(size_t)z * (F / 16) + blk] = make_float2(__int_as_float((127 + e - 14) << 23), sm);
-        pend += 1ull << (8 * z);
+        // warp barrier, then one release count by lane 0 (cumulative over the
+        // lanes' stores)
+        __syncwarp();
+        if (lane == 0) red_release_add_u32(&done[z], 1u);
       } else if (FUSED) {
         // rows lane, lane + 32: slot quad * 4 + row / 16, block row row % 16;
         // the bf16 products go to the block's slot table, and the block's last
@@ -765,24 +788,35 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         float* yb = ysm + (size_t)lb * MAXK * ROWS_D;
         if ((lane >> 4) < nsl) yb[(quad * SLOTS_D + (lane >> 4)) * ROWS_D + (lane & 15)] = bf2f(f2bf(t0));
         if ((lane >> 4) + 2 < nsl) yb[(quad * SLOTS_D + 2 + (lane >> 4)) * ROWS_D + (lane & 15)] = bf2f(f2bf(t1));
+        // the block's units go to both epilogue warps: the one that finishes
+        // the block's last unit folds
         __syncwarp();
-        if (quad == nq - 1 && lane < ROWS_D) {
-          // y_j = bf16 product, prod_j = y_j * w_j: with nloc <= 8 slots the
-          // colsum association has one product per chain (chain q = 0 +
-          // prod_q) and folds the chains in slot order
-          float total = 0.0f;
+        unsigned prev = 0;
+        if (lane == 0) {
+          __threadfence_block();
+          prev = atomicAdd(&ycnt[lb], 1u);
+        }
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == (unsigned)(nq - 1)) {
+          __threadfence_block();
+          if (lane < ROWS_D) {
+            // y_j = bf16 product, prod_j = y_j * w_j: with nloc <= 8 slots the
+            // colsum association has one product per chain (chain q = 0 +
+            // prod_q) and folds the chains in slot order
+            float total = 0.0f;
 #pragma unroll
-          for (int q = 0; q < MAXK; ++q) {
-            if (q < nloc) {
-              const float a2 = yb[q * ROWS_D + lane] * sw[EP ? lslot[q] : q] + 0.0f;
-              total = (q == 0) ? a2 : a2 + total;
+            for (int q = 0; q < MAXK; ++q) {
+              if (q < nloc) {
+                const float a2 = yb[q * ROWS_D + lane] * sw[EP ? lslot[q] : q] + 0.0f;
+                total = (q == 0) ? a2 : a2 + total;
+              }
             }
+            const int h = blk * ROWS_D + lane;
+            if (EP)
+              p.out_f32[h] = total;
+            else
+              p.out[h] = f2bf(total);
           }
-          const int h = blk * ROWS_D + lane;
-          if (EP)
-            p.out_f32[h] = total;
-          else
-            p.out[h] = f2bf(total);
         }
       } else {
         // row lane of the unit: partial slot lane ([P 0..7][Q 8..15][P 16..23][Q 24..31])
@@ -790,7 +824,6 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         if (row < p.N) p.y[row] = f2bf(t0);
       }
     }
-    if (FUSED) publish();
   } else {
     // ------------------------------ consumers ------------------------------
     // A CTA's units are all its gate|up units, then its down units, so the
@@ -887,9 +920,16 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         if (b < nsl) {
           const uint8_t* mb = st + p.st_meta2 + b * 2 * p.st_mstep2;
           const Meta m{mb, mb + p.st_mstep2, mb, mb + p.st_mstep2, r, 8 + r, p.mb2, p.sw2 != 0};
-          dot_i8_act(st + b * (ROWS_D * F / 2), st + p.st_act + b * F * 2,
-                     reinterpret_cast<const float2*>(st + p.st_asc + b * (F / 2)), qw * (F / 128), F / 128, p.gs, m,
-                     accP, accQ);
+          const uint8_t* wbx = st + b * (ROWS_D * F / 2);
+          const uint8_t* pcs = st + p.st_act + b * F * 2;
+          const float2* asc = reinterpret_cast<const float2*>(st + p.st_asc + b * (F / 2));
+          const int ns = F / 128;  // chunks of the warp's quarter
+          if (ns % 12 == 0)
+            dot_i8_act<3>(wbx, pcs, asc, qw * ns, ns, p.gs, m, accP, accQ);
+          else if (ns % 8 == 0)
+            dot_i8_act<2>(wbx, pcs, asc, qw * ns, ns, p.gs, m, accP, accQ);
+          else
+            dot_i8_act<1>(wbx, pcs, asc, qw * ns, ns, p.gs, m, accP, accQ);
         }
         accP += __shfl_xor_sync(0xffffffffu, accP, 1);
         accQ += __shfl_xor_sync(0xffffffffu, accQ, 1);
