@@ -12,7 +12,6 @@
 #include <cstring>
 
 #include "common.cuh"
-#include "decode1.cuh"
 #include "decode2.cuh"
 #include "decode_ws.hpp"
 #include "engine.cuh"
@@ -62,8 +61,7 @@ static int gather_impl(const char* fn, const uint16_t* x, const uint32_t* w, con
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // one row of x times one weight matrix: the single-column streaming kernel
   if (M == 1 && batch == 1 && !lhs && !rhs && n_x >= 1 && n_w >= 1 && aligned16(y)) {
-    if (!decode_v1() && d2_qmv_eligible(N, K, gs, x, w, s, b)) return d2_qmv(x, w, s, b, y, N, K, gs, st);
-    if (decode_v1() && d1_qmv_eligible(N, K, gs, x, w, s, b)) return d1_qmv(x, w, s, b, y, N, K, gs, st);
+    if (d2_qmv_eligible(N, K, gs, x, w, s, b)) return d2_qmv(x, w, s, b, y, N, K, gs, st);
   }
   const bool engine_ok = M <= eng::MAX_COLS && engine_k_ok(K, gs) && aligned16(w) && aligned16(s) &&
                          aligned16(b);
@@ -221,14 +219,11 @@ int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, co
   const void* ptrs[] = {x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd};
   bool all_aligned = true;
   for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
-  if (S == 1 && all_aligned && !decode_v1() && d2_moe_eligible(H, E, F, k, group_size)) {
+  if (S == 1 && all_aligned && d2_moe_eligible(H, E, F, k, group_size)) {
     const D2Scratch scr{&ws.hdr->error, ws.ctr, ws.logits, ws.act, ws.asc};
     return d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size, scr,
                          st);
   }
-  if (S == 1 && all_aligned && decode_v1() && d1_moe_eligible(H, E, F, k, group_size))
-    return d1_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size,
-                         &ws.hdr->error, ws.hdr->counters, ws.hdr->sched, ws.logits, ws.act, st);
   if (S == 1) {
     eng::Params p;
     base_params(p, eng::MODE_FUSED, group_size);

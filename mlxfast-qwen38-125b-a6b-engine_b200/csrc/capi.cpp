@@ -27,14 +27,6 @@ int set_error(int code, const char* fmt, ...) {
 
 void clear_error() { g_last_error.clear(); }
 
-bool decode_v1() {
-  static const bool v = [] {
-    const char* e = std::getenv("B2Q_DECODE_V1");
-    return e && e[0] == '1';
-  }();
-  return v;
-}
-
 int device_info(DeviceInfo* out) {
   static std::mutex mu;
   static DeviceInfo cache[64];

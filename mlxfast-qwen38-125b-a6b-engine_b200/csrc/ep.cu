@@ -30,7 +30,6 @@
 #include <mutex>
 
 #include "common.cuh"
-#include "decode1.cuh"
 #include "decode2.cuh"
 #include "decode_ws.hpp"
 #include "engine.cuh"
@@ -340,17 +339,10 @@ int b2q_ep_moe_decode(void* comm, const uint16_t* x, const uint16_t* wr, const u
     const void* ptrs[] = {x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, partial};
     bool all_aligned = true;
     for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
-    if (all_aligned && !decode_v1() && d2_moe_eligible(H, E, F, k, group_size)) {
+    if (all_aligned && d2_moe_eligible(H, E, F, k, group_size)) {
       const D2Scratch scr{ws.err, ws.ctr, ws.logits, ws.act, ws.asc};
       rc = d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, nullptr, idx, w, nullptr, H, E, F, k, group_size,
                          scr, st, e_lo, e_local, partial);
-      if (rc) return rc;
-      return ep_finish(static_cast<EpComm*>(comm), partial, out, (size_t)S * H, st);
-    }
-    if (all_aligned && decode_v1() && d1_moe_eligible(H, E, F, k, group_size)) {
-      WsHeader* hdr = static_cast<WsHeader*>(workspace);
-      rc = d1_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, nullptr, idx, w, nullptr, H, E, F, k, group_size,
-                         &hdr->error, hdr->counters, hdr->sched, ws.logits, ws.act, st, e_lo, e_local, partial);
       if (rc) return rc;
       return ep_finish(static_cast<EpComm*>(comm), partial, out, (size_t)S * H, st);
     }

@@ -33,10 +33,6 @@ int device_info(DeviceInfo* out);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// A/B switch while the single-column kernels are replaced: B2Q_DECODE_V1=1
-// selects the previous kernel (read once).
-bool decode_v1();
-
 }  // namespace b2q
 
 #define B2Q_TRY_CUDA(expr)                                 \
