@@ -236,8 +236,11 @@ B2Q_API int b2q_ep_moe_prefill(void* comm, const uint16_t* x, const uint16_t* wr
  * b2q_ep_moe_prefill_a2a chains the three over the library's communicator
  *   (comm == NULL: one rank): all-gather of the counts, grouped NCCL send /
  *   recv of the blocks, the experts, the partial rows back, the combine. Every
- *   rank calls it (T may be 0, T <= T_max); it reads the counts on the host,
- *   so it returns after the dispatch has run. */
+ *   rank calls it (T may be 0, T <= T_max); it reads the counts on the host
+ *   (a copy to the host and a synchronisation of `stream`, once per call), so
+ *   it returns after the dispatch has run, blocks the calling thread until
+ *   then, and cannot be captured in a CUDA graph. The three phase entry
+ *   points above are stream-ordered and asynchronous. */
 #define B2Q_EP_MAX_RANKS 8
 B2Q_API int b2q_ep_expert_range(int E, int nranks, int rank, int* e_lo, int* e_local);
 B2Q_API size_t b2q_ep_a2a_dispatch_workspace_size(int T, int H, int E, int k, int nranks);

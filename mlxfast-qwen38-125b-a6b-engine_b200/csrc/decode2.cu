@@ -1042,11 +1042,15 @@ static int launch_t(const D2Params& p, cudaStream_t st, int grid) {
   cfg.blockDim = dim3(NTH);
   cfg.dynamicSmemBytes = p.smem_bytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  // one CTA per SM, all resident at once (the fused kernel's CTAs wait on
+  // each other's counts): a cooperative launch guarantees it or fails
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   B2Q_TRY_CUDA(cudaLaunchKernelEx(&cfg, d2_kernel<CPG, MODE>, p));
   return B2Q_OK;
 }

@@ -24,6 +24,7 @@ namespace b2q {
 
 constexpr int SORT_THREADS = 1024;
 constexpr int SORT_WARPS = SORT_THREADS / 32;
+constexpr int BATCH = 8;  // chunks of 32 ids loaded together
 
 __global__ void __launch_bounds__(SORT_THREADS, 1)
     expert_sort_kernel(const uint32_t* __restrict__ ids, uint32_t* __restrict__ sorted_ids,
@@ -40,17 +41,27 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
   const int per = (R + SORT_WARPS - 1) / SORT_WARPS;
   const int i0 = min(R, warp * per), i1 = min(R, i0 + per);
   unsigned* wc = cnt + warp * E;
-  // ---- pass 1: counts per expert of the warp's range ----
-  for (int c0 = i0; c0 < i1; c0 += 32) {
-    const int i = c0 + lane;
-    uint32_t e = (i < i1) ? __ldg(ids + i) : 0xffffffffu;
-    if (i < i1 && e >= (uint32_t)E) {
-      record_error(err, B2Q_EINVAL);
-      e = 0xffffffffu;
+  // ---- pass 1: counts per expert of the warp's range (the ids of BATCH
+  // chunks of 32 are loaded together: one memory latency per batch) ----
+  for (int b0 = i0; b0 < i1; b0 += 32 * BATCH) {
+    uint32_t ev[BATCH];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const int i = b0 + 32 * j + lane;
+      ev[j] = (i < i1) ? __ldg(ids + i) : 0xffffffffu;
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e != 0xffffffffu && (peers & lt_mask) == 0) wc[e] += __popc(peers);
-    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const int i = b0 + 32 * j + lane;
+      uint32_t e = ev[j];
+      if (i < i1 && e >= (uint32_t)E) {
+        record_error(err, B2Q_EINVAL);
+        e = 0xffffffffu;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e != 0xffffffffu && (peers & lt_mask) == 0) wc[e] += __popc(peers);
+      __syncwarp();
+    }
   }
   __syncthreads();
   // ---- scan: base[w][e] over warps, offsets over experts ----
@@ -86,20 +97,29 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
   }
   __syncthreads();
   // ---- pass 2: place the warp's range in slot order ----
-  for (int c0 = i0; c0 < i1; c0 += 32) {
-    const int i = c0 + lane;
-    uint32_t e = (i < i1) ? __ldg(ids + i) : 0xffffffffu;
-    if (e >= (uint32_t)E) e = 0xffffffffu;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e != 0xffffffffu) {
-      const unsigned pos = tot[e] + wc[e] + __popc(peers & lt_mask);
-      if (sorted_ids) sorted_ids[pos] = e;
-      if (token_rows) token_rows[pos] = (uint32_t)(i / k);
-      if (inverse) inverse[i] = pos;
+  for (int b0 = i0; b0 < i1; b0 += 32 * BATCH) {
+    uint32_t ev[BATCH];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const int i = b0 + 32 * j + lane;
+      ev[j] = (i < i1) ? __ldg(ids + i) : 0xffffffffu;
     }
-    __syncwarp();
-    if (e != 0xffffffffu && (peers & lt_mask) == 0) wc[e] += __popc(peers);
-    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const int i = b0 + 32 * j + lane;
+      uint32_t e = ev[j];
+      if (e >= (uint32_t)E) e = 0xffffffffu;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e != 0xffffffffu) {
+        const unsigned pos = tot[e] + wc[e] + __popc(peers & lt_mask);
+        if (sorted_ids) sorted_ids[pos] = e;
+        if (token_rows) token_rows[pos] = (uint32_t)(i / k);
+        if (inverse) inverse[i] = pos;
+      }
+      __syncwarp();
+      if (e != 0xffffffffu && (peers & lt_mask) == 0) wc[e] += __popc(peers);
+      __syncwarp();
+    }
   }
 }
 
