@@ -649,7 +649,30 @@ def main():
             host_out.copy_(y, non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1) / max(1, n_e2e) if n_e2e else float("nan")
+    py_ms = e0.elapsed_time(e1) / max(1, n_e2e) if n_e2e else float("nan")
+    e2e_ms = py_ms
+    e2e_api = ("b2q.MoE.__call__" if comm is None else "b2q.ep.EPMoE.__call__") + \
+        " (pinned host token in, pinned host output back each step)"
+    if comm is None and n_e2e:
+        # the C ABI from a native host loop (as the reference's Swift runner would
+        # call it): b2q_moe_decode per step, token row in from pinned host memory and
+        # output row back every step, copies double-buffered on a second stream
+        import ctypes
+
+        hx = torch.empty((N_TOKENS, H), dtype=torch.bfloat16).pin_memory()
+        hx.copy_(xs.cpu())
+        ho = torch.empty((H,), dtype=torch.bfloat16).pin_memory()
+        dx2 = torch.empty((2, H), dtype=torch.bfloat16, device=dev)
+        dy2 = torch.empty((2, H), dtype=torch.bfloat16, device=dev)
+        wr_arr = (ctypes.c_void_p * n_layers)(*[routers[j].data_ptr() for j in range(n_layers)])
+        w9_arr = (ctypes.c_void_p * (9 * n_layers))(*[q for j in range(n_layers) for q in argsets[j]])
+        ms = ctypes.c_float(0.0)
+        check(L.b2q_moe_decode_host_loop(hx.data_ptr(), N_TOKENS, ho.data_ptr(), wr_arr, w9_arr, n_layers, H, E, F,
+                                         TOPK, GS, 4, dx2.data_ptr(), dy2.data_ptr(), wsp, ws_bytes, args.warmup,
+                                         n_e2e, sp, ctypes.byref(ms)))
+        e2e_ms = float(ms.value)
+        e2e_api = ("b2q_moe_decode through the C ABI from a native host loop (b2q_moe_decode_host_loop): pinned "
+                   "host token in and output back every step, copies double-buffered on a second stream")
     if pg:
         t = torch.tensor([e2e_ms], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -802,8 +825,10 @@ def main():
                      "bytes_per_launch": DECODE_BYTES,
                      "traffic": load_traffic("moe_decode_c1.json")},
         "e2e": ({"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
-                 "steps": n_e2e, "api": ("b2q.MoE.__call__" if comm is None else "b2q.ep.EPMoE.__call__")
-                 + " (pinned host token in, pinned host output back each step)"}
+                 "steps": n_e2e, "api": e2e_api,
+                 "python_api": {"value": 1000.0 / py_ms, "unit": "tok/s",
+                                "api": ("b2q.MoE.__call__" if comm is None else "b2q.ep.EPMoE.__call__")
+                                + " from a Python loop (pinned host token in, output back each step)"}}
                 if n_e2e else None),
         "gpu_launches": args.steps * (1 if world == 1 else 10),
         "clocks": clocks,

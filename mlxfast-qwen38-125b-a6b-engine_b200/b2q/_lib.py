@@ -40,6 +40,7 @@ SIGNATURES = {
     "b2q_moe_decode_workspace_size": (_SZ, [_I] * 5),
     "b2q_moe_decode": (_I, [_P] * 15 + [_I] * 7 + [_P, _SZ, _P]),
     "b2q_moe_decode_noalloc": (_I, [_P] * 15 + [_I] * 6 + [_P, _P]),
+    "b2q_moe_decode_host_loop": (_I, [_P, _I, _P, _P, _P, _I] + [_I] * 6 + [_P, _P, _P, _SZ, _I, _I, _P, _P]),
     "b2q_moe_prefill_workspace_size": (_SZ, [_I] * 5),
     "b2q_moe_prefill": (_I, [_P] * 14 + [_I] * 7 + [_P, _SZ, _P]),
     "b2q_swiglu": (_I, [_P, _P, _P, _I64, _P]),

@@ -196,6 +196,48 @@ def test_decoder_decode_forms_agree(cuda, b2q_mod):
     assert len(t0) == 4 and len(t1) == 5 and t0[0] == t1[0] and 0 <= acc <= 2
 
 
+def test_graph_token_stream_matches_eager_windows(cuda, b2q_mod):
+    """Sixteen greedy tokens from the CUDA-graph step against the eager one-row
+    windows, on a model whose output varies: with the tied table a random model
+    keeps predicting its input token, so the lm_head rows are a rotation of the
+    embedding rows (the prediction moves to another token every step)."""
+    import torch
+
+    from b2q.model import Decoder
+    from b2q.nn import QuantizedLinear
+
+    cfg = _tiny()
+    dec = Decoder(cfg, seed=11)
+    perm = torch.randperm(cfg.vocab, generator=torch.Generator().manual_seed(12)).cuda()
+    dec.lm_head = QuantizedLinear(dec.embed_w[perm].contiguous(), dec.embed_s[perm].contiguous(),
+                                  dec.embed_b[perm].contiguous(), cfg.group_size, 4)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(13)
+    ids = torch.randint(0, cfg.vocab, (8,), generator=g, device="cuda", dtype=torch.int32)
+    n = 16
+    # graph: prefill, then replays that read and write token / position on the device
+    replay, tok, pos, _ = dec.decode_graph()
+    _, lg = dec.forward(ids, 0)
+    graph = [int(lg.argmax(-1).item())]
+    tok.fill_(graph[0])
+    pos.fill_(8)
+    for _ in range(n - 1):
+        replay()
+        graph.append(int(tok.item()))
+    assert dec.status() == 0
+    assert len(set(graph)) > 1, graph
+    # eager one-row windows fed the graph's tokens (the KV rows are rewritten in
+    # the same order): every step's argmax is the graph's next token, up to
+    # near-ties of the two logits
+    dec.forward(ids, 0)
+    for i in range(n - 1):
+        hw = dec._window(torch.tensor([graph[i]], dtype=torch.int32, device="cuda"), 8 + i)
+        le = _bf(_np(dec.logits(hw))).reshape(-1)
+        e = int(le.argmax())
+        if e != graph[i + 1]:
+            assert le[e] - le[graph[i + 1]] <= 1e-2 * np.abs(le).max(), (i, e, graph[i + 1])
+
+
 def test_fused_norm_rope_kv_and_gqa_decode(cuda, b2q_mod):
     """add_rms_norm = bf16 add then the norm; rope_kv = rope in place + cache rows;
     gqa_decode over 3 key chunks (positions 5, 130, 299) against fp32 softmax attention."""

@@ -129,6 +129,43 @@ def test_moe_decode_fused_group_max_at_top_mantissa(c1, b2q_mod, oracle):
     assert rel_l2(_bf(_np(out)), _bf(ref)) < TIGHT
 
 
+def test_native_host_loop_matches_a_direct_call(c1, b2q_mod):
+    """b2q_moe_decode_host_loop (the C ABI driven from native code, copies
+    double-buffered) leaves in the host buffer what a direct call gives for the
+    last step's token and layer."""
+    import ctypes
+
+    import torch
+
+    from b2q import synth
+
+    lib = b2q_mod.lib()
+    H, E, F, k = c1["H"], c1["E"], c1["F"], c1["k"]
+    layers = [c1["L"], synth.moe_layer(E, H, F, 64, seed=11)]
+    routers = [c1["wr"], synth.router_weight(E, H, seed=3)]
+    names = ("wg", "sg", "bg", "wu", "su", "bu", "wd", "sd", "bd")
+    xs = synth.activations((5, H), seed=9)
+    hx = torch.empty((5, H), dtype=torch.bfloat16).pin_memory()
+    hx.copy_(xs.cpu())
+    ho = torch.empty((H,), dtype=torch.bfloat16).pin_memory()
+    dx2 = torch.empty((2, H), dtype=torch.bfloat16, device="cuda")
+    dy2 = torch.empty((2, H), dtype=torch.bfloat16, device="cuda")
+    wsb = lib.b2q_moe_decode_workspace_size(1, H, E, F, k)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    wr_arr = (ctypes.c_void_p * 2)(*[r.data_ptr() for r in routers])
+    w9 = (ctypes.c_void_p * 18)(*[L[n].data_ptr() for L in layers for n in names])
+    ms = ctypes.c_float(0.0)
+    stream = torch.cuda.current_stream().cuda_stream
+    warmup, steps = 2, 5  # last step 6: token 6 % 5 = 1, layer 6 % 2 = 0
+    rc = lib.b2q_moe_decode_host_loop(hx.data_ptr(), 5, ho.data_ptr(), wr_arr, w9, 2, H, E, F, k, 64, 4,
+                                      dx2.data_ptr(), dy2.data_ptr(), ws.data_ptr(), wsb, warmup, steps, stream,
+                                      ctypes.byref(ms))
+    assert rc == 0, lib.b2q_last_error()
+    assert ms.value > 0.0
+    ref = b2q_mod.moe_decode(xs[1:2], routers[0], layers[0], k)
+    assert torch.equal(ho.cuda().view(1, H), ref)
+
+
 def test_moe_decode_multi_token(c1, b2q_mod, oracle):
     from b2q import synth
 
