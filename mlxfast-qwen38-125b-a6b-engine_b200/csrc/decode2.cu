@@ -383,6 +383,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
     }
     for (int i = 0; i < MAXBLK; ++i) ycnt[i] = 0u;
     *abort_flag = 0;
+    nloc_sm[1] = 0;  // routed slots selected so far (the producer's early start)
     fence_barrier_init();
   }
   if (warp == NCW && lane == 0) {
@@ -496,6 +497,18 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   load_pieces<SLOT>(pieces, cc01, warp < NCW ? ncc1 : 0, xb);
   word_offsets<SLOT>(cc01, FUSED ? ROWS_GU : ROWS_QMV, woff);
   const int nslot1 = ncc1 / (SLOT / 32), slot01 = cc01 / (SLOT / 32);
+  // A fused call without expert parallelism lets the producer start on each
+  // unit as soon as top-k has chosen its slot's expert (a slot count in shared
+  // memory) instead of after the whole routing; it fills the stage that holds
+  // the staged pieces only after every consumer has its share in registers.
+  constexpr bool early = FUSED && !EP;
+  volatile int* topk_ready = nloc_sm + 1;
+  if (early) {
+    if (warp < NCW)
+      named_bar_arrive(2, (NCW + 1) * 32);
+    else if (warp == NCW)
+      named_bar_sync(2, (NCW + 1) * 32);
+  }
   // ---- routing (fused): every CTA selects the same top-k in warp 0 ----
   if (FUSED && warp == 0) {
     // lane l holds experts l, l + 32, ...: poll until every logit carries this
@@ -550,7 +563,11 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
       const int e = (int)__reduce_min_sync(0xffffffffu, bk == m ? be : 0xffffffffu);
       if (lane == slot) selv = __uint_as_float((m & 0x80000000u) ? (m & 0x7fffffffu) : ~m);
-      if (lane == 0) sidx[slot] = (uint32_t)e;
+      if (lane == 0) {
+        sidx[slot] = (uint32_t)e;
+        __threadfence_block();
+        *topk_ready = slot + 1;
+      }
 #pragma unroll
       for (int i = 0; i < EPL; ++i)
         if (e == lane + 32 * i) key[i] = 0u;
@@ -570,9 +587,14 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       *nloc_sm = n;
     }
   }
-  __syncthreads();
+  if (early) {
+    if (warp != NCW) named_bar_sync(1, (NWARP - 1) * 32);
+  } else {
+    __syncthreads();
+  }
 
-  const int nloc = FUSED ? *nloc_sm : 0;
+  // every routed slot is local without expert parallelism
+  const int nloc = !FUSED ? 0 : (EP ? *nloc_sm : p.k);
   const int F = p.F, H = p.H;
   // Static schedule. qmv: unit u to CTA u mod grid. Fused: gate|up unit u to
   // CTA grid - 1 - (u mod grid); 16-row down block j to CTA j mod grid, each
@@ -596,6 +618,18 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       int s = -1;
       uint32_t eph = 1u;  // parity of the empty phase the next reuse of stage s waits for
       uint32_t ready = 0u;  // slots whose activations this CTA has seen final
+      // top-k has chosen slot z's expert (bounded wait on the slot count)
+      auto slot_chosen = [&](int z) -> bool {
+        for (uint32_t n = 0; *topk_ready <= z; ++n) {
+          if (*abort_flag || ((n & 63u) == 63u && globaltimer() > deadline)) {
+            if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
+            *abort_flag = 1;
+            return false;
+          }
+        }
+        __threadfence_block();  // the slot's expert id is read after the count
+        return true;
+      };
       for (int it = 0;; ++it) {
         if (++s == NS) {
           s = 0;
@@ -623,6 +657,12 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         } else if (it < ngu) {
           const int u = G - 1 - bx + it * G;
           const int z = u / (F / ROWS_GU), rb = u % (F / ROWS_GU);
+          if (early && !slot_chosen(z)) {
+            info[s] = make_int4(U_END, 0, 0, 0);
+            mbar_arrive(&full[s]);
+            lastf[s] = (int)(eph ^ 1u);
+            break;
+          }
           const uint32_t e = EP ? sidx[lslot[z]] - (uint32_t)p.e_lo : sidx[z];
           const int row = (int)(e * (uint32_t)F) + rb * ROWS_GU;
           info[s] = make_int4(U_GU, z, rb, 0);
@@ -637,6 +677,12 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         } else {
           const int d = it - ngu, nbk = max(nblk, 1), quad = d / nbk, lb = d % nbk, blk = bx + lb * G;
           const int z0 = quad * SLOTS_D, nsl = min(SLOTS_D, nloc - z0);
+          if (early && !slot_chosen(z0 + nsl - 1)) {
+            info[s] = make_int4(U_END, 0, 0, 0);
+            mbar_arrive(&full[s]);
+            lastf[s] = (int)(eph ^ 1u);
+            break;
+          }
           // the slots' activations must be final: every gate|up unit of them
           // finished. The counts of the unit's slots not yet seen final are
           // read together (one round trip per poll, not one per slot).

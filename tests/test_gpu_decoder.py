@@ -209,8 +209,8 @@ def test_graph_token_stream_matches_eager_windows(cuda, b2q_mod):
     cfg = _tiny()
     dec = Decoder(cfg, seed=11)
     perm = torch.randperm(cfg.vocab, generator=torch.Generator().manual_seed(12)).cuda()
-    dec.lm_head = QuantizedLinear(dec.embed_w[perm].contiguous(), dec.embed_s[perm].contiguous(),
-                                  dec.embed_b[perm].contiguous(), cfg.group_size, 4)
+    rows = lambda t: t.view(torch.int16 if t.element_size() == 2 else torch.int32)[perm].contiguous().view(t.dtype)
+    dec.lm_head = QuantizedLinear(rows(dec.embed_w), rows(dec.embed_s), rows(dec.embed_b), cfg.group_size, 4)
     g = torch.Generator(device="cuda")
     g.manual_seed(13)
     ids = torch.randint(0, cfg.vocab, (8,), generator=g, device="cuda", dtype=torch.int32)
