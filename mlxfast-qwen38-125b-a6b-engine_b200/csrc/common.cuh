@@ -54,6 +54,24 @@ __device__ __forceinline__ uint16_t silu_bf16(uint16_t xb) {
 __device__ __forceinline__ uint16_t swiglu_bf16(uint16_t g, uint16_t u) {
   return f2bf(bf2f(silu_bf16(g)) * bf2f(u));
 }
+// The same SwiGLU with the conversion instruction for every rounding (equal to
+// f2bf except for NaN payloads) and the correctly rounded reciprocal (equal to
+// 1 / x): a shorter dependent chain, identical finite results.
+__device__ __forceinline__ float rb_cvt(float f) {
+  uint16_t h;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return bf2f(h);
+}
+__device__ __forceinline__ uint16_t swiglu_bf16_cvt(uint16_t gb, uint16_t ub) {
+  const float x = bf2f(gb);
+  const float e = rb_cvt(expf(rb_cvt(fabsf(x))));
+  const float y = rb_cvt(__frcp_rn(rb_cvt(1.0f + e)));
+  const float sg = x < 0.0f ? y : rb_cvt(1.0f - y);
+  const float si = rb_cvt(x * sg);
+  uint16_t h;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(si * bf2f(ub)));
+  return h;
+}
 
 // ---- nibble decode ------------------------------------------------------------
 // A packed word W holds values e0..e7 (e_j in bits [4j, 4j+4)). OR-ing a nibble

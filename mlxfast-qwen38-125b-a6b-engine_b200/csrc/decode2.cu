@@ -683,6 +683,20 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
             lastf[s] = (int)(eph ^ 1u);
             break;
           }
+          // the weights and their scales / biases do not depend on the gate|up
+          // units: they are requested before the wait for the slots
+          info[s] = make_int4(U_DOWN, quad, blk, lb | (nsl << 8));
+          const int wb = ROWS_D * F / 2;  // one slot's weight box
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(nsl * (wb + 2 * ROWS_D * p.mb2 + F * 2 + F / 2)));
+          for (int i = 0; i < nsl; ++i) {
+            const int z = z0 + i;
+            const uint32_t e = EP ? sidx[lslot[z]] - (uint32_t)p.e_lo : sidx[z];
+            const int row = (int)(e * (uint32_t)H) + blk * ROWS_D;
+            uint8_t* m = st + p.st_meta2 + i * 2 * p.st_mstep2;
+            tma3(st + i * wb, &p.map[MWD], 0, row, 0, &full[s], pol);
+            tc::tma_load_2d(m, &p.map[MSD], 0, row, &full[s], pol);
+            tc::tma_load_2d(m + p.st_mstep2, &p.map[MBD], 0, row, &full[s], pol);
+          }
           // the slots' activations must be final: every gate|up unit of them
           // finished. The counts of the unit's slots not yet seen final are
           // read together (one round trip per poll, not one per slot).
@@ -712,28 +726,17 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           if (!ok) {
             if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
             *abort_flag = 1;
-            info[s] = make_int4(U_END, 0, 0, 0);
-            mbar_arrive(&full[s]);
+          }
+          fence_proxy_async_global();  // the copies below read what generic stores wrote
+          // the unit's slots are consecutive: their activations and block
+          // scales (written by the epilogues, in L2) are one copy each; issued
+          // after a failed wait too, so the stage completes before the abort
+          bulk_g2s(st + p.st_act, p.ws_act + (size_t)z0 * F, (uint32_t)(nsl * F * 2), &full[s], pol_keep);
+          bulk_g2s(st + p.st_asc, p.ws_asc + (size_t)z0 * (F / 16), (uint32_t)(nsl * F / 2), &full[s], pol_keep);
+          if (!ok) {
             lastf[s] = (int)(eph ^ 1u);
             break;
           }
-          fence_proxy_async_global();  // the copies below read what generic stores wrote
-          info[s] = make_int4(U_DOWN, quad, blk, lb | (nsl << 8));
-          const int wb = ROWS_D * F / 2;  // one slot's weight box
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(nsl * (wb + 2 * ROWS_D * p.mb2 + F * 2 + F / 2)));
-          for (int i = 0; i < nsl; ++i) {
-            const int z = z0 + i;
-            const uint32_t e = EP ? sidx[lslot[z]] - (uint32_t)p.e_lo : sidx[z];
-            const int row = (int)(e * (uint32_t)H) + blk * ROWS_D;
-            uint8_t* m = st + p.st_meta2 + i * 2 * p.st_mstep2;
-            tma3(st + i * wb, &p.map[MWD], 0, row, 0, &full[s], pol);
-            tc::tma_load_2d(m, &p.map[MSD], 0, row, &full[s], pol);
-            tc::tma_load_2d(m + p.st_mstep2, &p.map[MBD], 0, row, &full[s], pol);
-          }
-          // the unit's slots are consecutive: their activations and block
-          // scales (written by the epilogues, in L2) are one copy each
-          bulk_g2s(st + p.st_act, p.ws_act + (size_t)z0 * F, (uint32_t)(nsl * F * 2), &full[s], pol_keep);
-          bulk_g2s(st + p.st_asc, p.ws_asc + (size_t)z0 * (F / 16), (uint32_t)(nsl * F / 2), &full[s], pol_keep);
         }
         lastf[s] = (int)(eph ^ 1u);
       }
@@ -794,17 +797,14 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         const int f = lane & 15;  // output f of the unit (lanes 16..31 repeat lanes 0..15)
         const float g = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + (f & 7));
         const float up = __shfl_sync(0xffffffffu, t0, 16 * (f >> 3) + 8 + (f & 7));
-        const uint16_t a = swiglu_bf16(f2bf(g), f2bf(up));
+        const uint16_t a = swiglu_bf16_cvt(f2bf(g), f2bf(up));
         // the block of 16 as int8 pieces: scale 2^(14 - E) from the max |a|,
         // X = round(a * 2^(14 - E)) <= 32639 (as for x), hi = byte 1 of
-        // X + 128, lo = byte 0 of X
-        unsigned mx = a & 0x7fffu;
+        // X + 128, lo = byte 0 of X (lanes 16..31 repeat lanes 0..15)
+        const unsigned mx = __reduce_max_sync(0xffffffffu, a & 0x7fffu);
         float sm = lane < 16 ? bf2f(a) : 0.0f;
 #pragma unroll
-        for (int off = 1; off < 16; off <<= 1) {
-          mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-          sm += __shfl_xor_sync(0xffffffffu, sm, off);
-        }
+        for (int off = 1; off < 16; off <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
         int e = (int)((mx >> 7) & 0xffu) - 127;
         if (mx == 0u || mx >= 0x7f80u) e = 0;
         e = max(-110, min(120, e));
