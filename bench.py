@@ -378,6 +378,89 @@ def run_c0(dev, stream, hbm_peak, peak_kind):
                     "d2h_bytes_per_step": 8192, "api": "b2q.quantized_matmul (pinned host x in, y back each call)"}}
 
 
+def _graph_us(stream, dev, n_calls, call, reps=8):
+    """us per call of a CUDA graph of n_calls calls, replayed reps times."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        for i in range(min(8, n_calls)):
+            call(i)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(n_calls):
+            call(i)
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    del g
+    return e0.elapsed_time(e1) * 1000.0 / (reps * n_calls)
+
+
+def run_lut(dev, stream, hbm_peak, peak_kind):
+    """The metadata pair index: one-row products with each
+    group's scale / bias read through a load-time table (u16 index per group in
+    place of two bf16), against the plain product on the same weights. Config
+    0's shape (graph of 256 calls over 32 copies) and an lm_head-sized product
+    (N = 151,936; graph of 16 calls over 2 copies). The weights' metadata is the
+    configs' own distribution, whose distinct pairs fit the table."""
+    import torch
+
+    from b2q import lut, synth
+    from b2q._lib import check, lib
+
+    L = lib()
+    sp = stream.cuda_stream
+    out = {}
+    for name, N, copies_n, calls in (("c0", 4096, C0_COPIES, C0_CALLS), ("lm_head", 151936, 2, 16)):
+        K = 4096
+        copies = [synth.packed_weights((N,), K, GS, device=dev, seed=700 + i) for i in range(copies_n)]
+        metas = [lut.AffineLUT.build(s_, b) for (_, s_, b) in copies]
+        if any(m is None for m in metas):
+            out[name] = {"skipped": "metadata not indexable"}
+            continue
+        xs = synth.activations((calls, K), device=dev, seed=701)
+        y = torch.empty((calls, N), dtype=torch.bfloat16, device=dev)
+
+        def plain(i):
+            w, s_, b = copies[i % copies_n]
+            rc = L.b2q_qmm(xs[i].data_ptr(), w.data_ptr(), s_.data_ptr(), b.data_ptr(), y[i].data_ptr(), 1, N, K, GS,
+                           4, 1, sp)
+            if rc:
+                check(rc)
+
+        def through_table(i):
+            w = copies[i % copies_n][0]
+            m = metas[i % copies_n]
+            rc = L.b2q_qmv_lut(xs[i].data_ptr(), w.data_ptr(), m.index.data_ptr(), m.table.data_ptr(), m.count,
+                               y[i].data_ptr(), N, K, GS, 4, sp)
+            if rc:
+                check(rc)
+
+        us_plain = _graph_us(stream, dev, calls, plain)
+        us_lut = _graph_us(stream, dev, calls, through_table)
+        b_plain = N * (K // 2 + 4 * K // GS) + 2 * K + 2 * N
+        count = max(m.count for m in metas)
+        b_lut = N * (K // 2 + 2 * K // GS) + count * 4 + 2 * K + 2 * N
+        out[name] = {"N": N, "K": K, "table_entries": count,
+                     "us_per_call": us_lut, "us_per_call_plain": us_plain,
+                     "bytes_per_call": b_lut, "bytes_per_call_plain": b_plain,
+                     "roofline": {"bound": "hbm", "achieved": b_lut / (us_lut * 1e-6) / 1e9, "peak": hbm_peak,
+                                  "unit": "GB/s", "frac": b_lut / (us_lut * 1e-6) / 1e9 / hbm_peak,
+                                  "peak_kind": peak_kind},
+                     "form": f"CUDA graph of {calls} calls over {copies_n} weight copies"}
+        del copies, metas, xs, y
+        torch.cuda.empty_cache()
+    return out
+
+
 EP_PROMPT, EP_NEW = 8192, 512
 
 
@@ -773,6 +856,9 @@ def main():
     c0 = None
     if world == 1 and not args.no_c0:
         c0 = run_c0(dev, stream, hbm_peak, peak_kind)
+    affine_lut = None
+    if world == 1 and not args.no_c0:
+        affine_lut = run_lut(dev, stream, hbm_peak, peak_kind)
 
     # ---------------- full decoder (config 3), one GPU ----------------
     decoder = None
@@ -835,6 +921,7 @@ def main():
         "prefill": prefill,
         "decoder": decoder,
         "c0": c0,
+        "affine_lut": affine_lut,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)

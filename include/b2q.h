@@ -24,7 +24,8 @@
  *    completes without a device-side error. Calls sharing one workspace must
  *    be ordered on one stream. b2q_qmm and b2q_gather_qmm keep mlx-c's
  *    workspace-free signatures: with more than 8 rows per item they take
- *    stream-ordered temporaries (cudaMallocAsync / cudaFreeAsync on `stream`).
+ *    stream-ordered temporaries (cudaMallocAsync / cudaFreeAsync on `stream`);
+ *    b2q_qmm_ws / b2q_gather_qmm_ws take a caller workspace instead.
  *  - Only bits == 4 is implemented on the device (the packed format of the
  *    path); group_size is 32, 64 or 128. Other values return B2Q_EUNSUPPORTED.
  */
@@ -101,6 +102,63 @@ B2Q_API int b2q_gather_qmm(const uint16_t* x, const uint32_t* w, const uint16_t*
                    const uint32_t* rhs_indices, uint16_t* y, int batch, int M,
                    int N, int K, int n_x, int n_w, int group_size, int bits,
                    int transpose, int sorted_indices, void* stream);
+
+/* Workspace-taking forms of b2q_qmm / b2q_gather_qmm (same reference functions:
+ * MLXCAPI/ops.h:809-818 and :475-488). mlx-c's signatures carry no workspace,
+ * so b2q_qmm / b2q_gather_qmm take a stream-ordered temporary for the M > 8
+ * tensor-core path (sorted row tables and the grouped copy of x); these forms
+ * use the caller's buffer instead and allocate nothing, for a runtime that
+ * owns a fixed arena. workspace: 256-byte aligned, at least
+ * b2q_gather_qmm_workspace_size(batch, M, N, K, n_w) bytes (M <= 8 needs none
+ * beyond a non-null pointer); no contents carried between calls, so it needs no
+ * clearing. Calls sharing one workspace must be ordered on one stream. */
+B2Q_API size_t b2q_gather_qmm_workspace_size(int batch, int M, int N, int K, int n_w);
+B2Q_API int b2q_qmm_ws(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+                       const uint16_t* biases, uint16_t* y, int M, int N, int K,
+                       int group_size, int bits, int transpose, void* workspace,
+                       size_t workspace_bytes, void* stream);
+B2Q_API int b2q_gather_qmm_ws(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+                              const uint16_t* biases, const uint32_t* lhs_indices,
+                              const uint32_t* rhs_indices, uint16_t* y, int batch, int M,
+                              int N, int K, int n_x, int n_w, int group_size, int bits,
+                              int transpose, int sorted_indices, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* ---- metadata pair index (load-time derived cache) ------------------------ */
+
+/* Replaces TrackAffineLUT.build / buildOnDevice / verified
+ * (Runner/FastModel/TrackAffineLUT.swift:58-110). For one tensor's bf16
+ * scales / biases (n_groups groups, any shape), writes table (uint32, entry =
+ * scale_bits | bias_bits << 16, 16-byte aligned, max_entries entries of room)
+ * and index (uint16 per group, the scales' layout) and sets *count_out to the
+ * number of distinct pairs. Table order: first occurrence when
+ * n_groups < 2^20, ascending pair value otherwise (the reference's host loop
+ * and device sort). *count_out = -1 (status B2Q_OK) when the tensor is not
+ * indexed: more than max_entries distinct pairs (the reference's limit is
+ * 32768), or a group whose round trip table[index[g]] does not give back its
+ * exact bits. max_entries: 4..65536, a multiple of 4; table entries from the
+ * count up to the next multiple of 4 are zeroed. Load-time call: it reads two
+ * counts back to the host and synchronises the stream twice.
+ * workspace: 256-byte aligned, b2q_affine_lut_workspace_size(max_entries). */
+B2Q_API size_t b2q_affine_lut_workspace_size(int max_entries);
+B2Q_API int b2q_affine_lut_build(const uint16_t* scales, const uint16_t* biases, int64_t n_groups,
+                                 uint16_t* index, uint32_t* table, int max_entries, int* count_out,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+/* Replaces TrackAffineLUT.lazyScales / lazyBiases (TrackAffineLUT.swift:46-53):
+ * the bf16 scales and biases an index encodes, bit for bit. */
+B2Q_API int b2q_affine_lut_expand(const uint16_t* index, const uint32_t* table, int64_t n_groups,
+                                  uint16_t* scales, uint16_t* biases, void* stream);
+/* Replaces TrackLUTGemv.apply (TrackAffineLUT.swift:330-368): one row,
+ * y[1, N] = x[1, K] . dequant(w[N, K])^T with each group's scale / bias read
+ * as table[index[n, g]]. The same single-column kernel as b2q_qmm at M = 1,
+ * with a block of indices in place of the scale and bias blocks and the table
+ * copied into shared memory: bit-identical to b2q_qmm on the scales / biases
+ * the index encodes. B2Q_EUNSUPPORTED outside the kernel's shapes
+ * (N % 16 == 0, N >= 32, K % 512 == 0, gs 32/64/128, 16-byte aligned tensors,
+ * at most 16,384 table entries), where the reference also falls back. */
+B2Q_API int b2q_qmv_lut(const uint16_t* x, const uint32_t* w, const uint16_t* index,
+                        const uint32_t* table, int count, uint16_t* y, int N, int K,
+                        int group_size, int bits, void* stream);
 
 /* ---- MoE operators (the Runner's fused-operator surface) ------------------ */
 
@@ -323,6 +381,21 @@ B2Q_API size_t b2q_gqa_decode_workspace_size(int T, int nq, int nk, int head_dim
 B2Q_API int b2q_gqa_decode(const uint16_t* q, int q_ld, const uint16_t* k_cache, const uint16_t* v_cache,
                    const int32_t* positions, uint16_t* out, int T, int nq, int nk, int head_dim, int window,
                    int* status, void* workspace, size_t workspace_bytes, void* stream);
+/* b2q_attn_decode: b2q_rope_kv followed by b2q_gqa_decode in one launch, for
+ *   windows of at most 8 rows (qkv rows at qkv + t * q_ld are read, not
+ *   modified): the k / v rows go to the caches at their positions exactly as
+ *   b2q_rope_kv writes them, and each row attends cache rows [0, positions[t]]
+ *   with the window's own rows taken from qkv. The workspace
+ *   (b2q_attn_decode_workspace_size, 256-byte aligned; the size for 8 rows
+ *   serves every T) holds one counter per row and kv head, then the chunk
+ *   partials: zero it once before the first call; each call leaves the
+ *   counters at zero. Calls sharing a workspace must be ordered on one stream.
+ *   B2Q_EUNSUPPORTED when the window's merge buffers exceed shared memory
+ *   (past ~125k positions at 8 query heads per kv head). */
+B2Q_API size_t b2q_attn_decode_workspace_size(int T, int nq, int nk, int head_dim, int window);
+B2Q_API int b2q_attn_decode(const uint16_t* qkv, int q_ld, const int32_t* positions, uint16_t* k_cache,
+                   uint16_t* v_cache, uint16_t* out, int T, int nq, int nk, int head_dim, float theta,
+                   int window, int* status, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- checkpoint reading (per-layer packed-weight binding) ------------------ */
 

@@ -33,6 +33,13 @@ SIGNATURES = {
     "b2q_quantize": (_I, [_P, _P, _P, _P, _I64, _I, _I, _I, _P]),
     "b2q_qmm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
     "b2q_gather_qmm": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "b2q_gather_qmm_workspace_size": (_SZ, [_I] * 5),
+    "b2q_qmm_ws": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
+    "b2q_gather_qmm_ws": (_I, [_P] * 7 + [_I] * 10 + [_P, _SZ, _P]),
+    "b2q_affine_lut_workspace_size": (_SZ, [_I]),
+    "b2q_affine_lut_build": (_I, [_P, _P, _I64, _P, _P, _I, _P, _P, _SZ, _P]),
+    "b2q_affine_lut_expand": (_I, [_P, _P, _I64, _P, _P, _P]),
+    "b2q_qmv_lut": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
     "b2q_moe_router_logits": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "b2q_moe_route": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "b2q_moe_gate_up_act": (_I, [_P] * 10 + [_I] * 7 + [_P]),
@@ -69,6 +76,8 @@ SIGNATURES = {
     "b2q_rope_kv": (_I, [_P, _I, _I, _I, _I, _P, ctypes.c_float, _P, _P, _I, _P, _P]),
     "b2q_gqa_decode_workspace_size": (_SZ, [_I] * 5),
     "b2q_gqa_decode": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "b2q_attn_decode_workspace_size": (_SZ, [_I] * 5),
+    "b2q_attn_decode": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _SZ, _P]),
     "b2q_st_open": (_I, [ctypes.c_char_p, _P]),
     "b2q_st_close": (_I, [_P]),
     "b2q_st_count": (_I, [_P]),

@@ -132,24 +132,26 @@ class Block:
         """a [T, H] normed -> attention output [T, n_heads * hd] (bf16).
 
         positions: int32 [T] device tensor of the rows' positions (consecutive).
-        Windows of up to 8 rows (decode, verify) attend through b2q_gqa_decode,
-        which reads the positions on the device (graph-safe); longer windows
+        Windows of up to 8 rows (decode, verify) attend through b2q_attn_decode
+        (rope, KV append and attention in one launch), which reads the positions
+        on the device (graph-safe); longer windows
         (prefill) use the framework's causal attention from row pos0 on."""
         cfg = self.cfg
         T = a.shape[0]
         nq, nk, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         qkv = self.qkv(a)  # [T, (nq + 2 nk) hd]
         st = ops._stream(a.device)
+        if T <= 8:
+            # rope, KV append, attention and the chunk merge in one launch
+            out = torch.empty((T, nq * hd), dtype=torch.bfloat16, device=a.device)
+            check(lib().b2q_attn_decode(qkv.data_ptr(), cfg.qkv_rows, positions.data_ptr(), self.k_cache.data_ptr(),
+                                        self.v_cache.data_ptr(), out.data_ptr(), T, nq, nk, hd, cfg.rope_theta,
+                                        cfg.max_seq, self.status.data_ptr(), self.attn_ws.data_ptr(),
+                                        self.attn_ws.numel(), st))
+            return out
         check(lib().b2q_rope_kv(qkv.data_ptr(), T, nq, nk, hd, positions.data_ptr(), cfg.rope_theta,
                                 self.k_cache.data_ptr(), self.v_cache.data_ptr(), cfg.max_seq,
                                 self.status.data_ptr(), st))
-        if T <= 8:
-            out = torch.empty((T, nq * hd), dtype=torch.bfloat16, device=a.device)
-            check(lib().b2q_gqa_decode(qkv.data_ptr(), cfg.qkv_rows, self.k_cache.data_ptr(),
-                                       self.v_cache.data_ptr(), positions.data_ptr(), out.data_ptr(), T, nq, nk, hd,
-                                       cfg.max_seq, self.status.data_ptr(), self.attn_ws.data_ptr(),
-                                       self.attn_ws.numel(), st))
-            return out
         if pos0 is None:
             raise ValueError("a window of more than 8 rows needs its first position on the host")
         L = pos0 + T
@@ -210,8 +212,8 @@ class Decoder:
         self.embed_w, self.embed_s, self.embed_b = ew, es, eb
         self.lm_head = QuantizedLinear(ew, es, eb, cfg.group_size, 4)  # tied
         self._status = torch.zeros(1, dtype=torch.int32, device=dev)
-        ws = lib().b2q_gqa_decode_workspace_size(8, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.max_seq)
-        self._attn_ws = torch.empty(ws, dtype=torch.uint8, device=dev)
+        ws = lib().b2q_attn_decode_workspace_size(8, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.max_seq)
+        self._attn_ws = torch.zeros(ws, dtype=torch.uint8, device=dev)  # chunk counters start at zero
         self.blocks = [Block(cfg, dev, seed + 100 * (i + 1), self._status, self._attn_ws, expert_parallel)
                        for i in range(cfg.n_layers)]
         self.final_norm = _norm_weight(H, dev, seed + 7)

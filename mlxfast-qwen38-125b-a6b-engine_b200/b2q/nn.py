@@ -17,14 +17,28 @@ from __future__ import annotations
 
 import torch
 
-from . import ops
+from . import lut, ops
 
 
 class QuantizedLinear:
-    def __init__(self, weight, scales, biases, group_size: int = 64, bits: int = 4, bias=None):
+    def __init__(self, weight, scales, biases, group_size: int = 64, bits: int = 4, bias=None, meta=None):
         self.weight, self.scales, self.biases = weight, scales, biases
         self.group_size, self.bits = group_size, bits
         self.bias = bias
+        # load-time metadata pair index (TrackQuantWeight.meta,
+        # Runner/FastModel/TrackFastWeights.swift:15-17); None when absent
+        self.meta = meta
+
+    def with_pair_index(self, max_entries: int = lut.MAX_ENTRIES) -> "QuantizedLinear":
+        """The same layer with its metadata pair index built (load time only),
+        as TrackQuantWeight.withPairIndex (TrackFastWeights.swift:29-35); the
+        layer itself when the tensor does not qualify."""
+        if self.meta is not None or self.bits != 4:
+            return self
+        built = lut.AffineLUT.build(self.scales, self.biases, max_entries)
+        if built is None:
+            return self
+        return QuantizedLinear(self.weight, self.scales, self.biases, self.group_size, self.bits, self.bias, built)
 
     @property
     def rows(self) -> int:
@@ -36,7 +50,12 @@ class QuantizedLinear:
         return cls(wq, s, b, group_size, bits)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        y = ops.quantized_matmul(x.contiguous(), self.weight, self.scales, self.biases, True, self.group_size, self.bits)
+        # one-row windows read the metadata through the pair index when there is
+        # one (TrackQuantWeight.apply, TrackFastWeights.swift:41-53)
+        y = lut.qmv_lut(x, self.weight, self.meta, self.group_size, self.bits) if self.meta is not None else None
+        if y is None:
+            y = ops.quantized_matmul(x.contiguous(), self.weight, self.scales, self.biases, True, self.group_size,
+                                     self.bits)
         if self.bias is not None:
             y = y + self.bias
         return y

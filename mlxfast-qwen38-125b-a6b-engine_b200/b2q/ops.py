@@ -22,7 +22,7 @@ import torch
 from ._lib import B2QError, check, lib
 
 __all__ = [
-    "quantize", "dequantize", "quantized_matmul", "gather_qmm", "router_logits", "route",
+    "quantize", "dequantize", "quantized_matmul", "gather_qmm", "gather_qmm_workspace_size", "router_logits", "route",
     "gate_up_act", "down_combine", "swiglu", "sorted_combine", "moe_decode", "moe_prefill", "moe_sort", "Workspace", "B2QError",
 ]
 
@@ -99,8 +99,18 @@ def dequantize(w, scales, biases, group_size: int = 64, bits: int = 4) -> torch.
     return out
 
 
-def quantized_matmul(x, w, scales, biases, transpose: bool = True, group_size: int = 64, bits: int = 4):
-    """x [..., M, K] bf16, w [N, K/8] -> [..., M, N] (x . dequant(w)^T)."""
+def gather_qmm_workspace_size(batch: int, M: int, N: int, K: int, n_w: int) -> int:
+    """Bytes of caller workspace the allocation-free product forms need."""
+    return int(lib().b2q_gather_qmm_workspace_size(batch, M, N, K, n_w))
+
+
+def quantized_matmul(x, w, scales, biases, transpose: bool = True, group_size: int = 64, bits: int = 4,
+                     workspace=None):
+    """x [..., M, K] bf16, w [N, K/8] -> [..., M, N] (x . dequant(w)^T).
+
+    ``workspace`` (a uint8 device tensor of at least
+    ``gather_qmm_workspace_size(1, M, N, K, 1)`` bytes) selects the form that
+    allocates nothing (``b2q_qmm_ws``)."""
     _dev(x, "x", _BF16), _dev(w, "w", _PACK), _dev(scales, "scales", _BF16), _dev(biases, "biases", _BF16)
     if w.dim() != 2:
         raise ValueError("[quantized_matmul] w must be 2-D (use gather_qmm for stacked experts)")
@@ -110,18 +120,24 @@ def quantized_matmul(x, w, scales, biases, transpose: bool = True, group_size: i
     N = w.shape[0]
     M = x.numel() // K
     y = torch.empty(x.shape[:-1] + (N,), dtype=torch.bfloat16, device=x.device)
+    if workspace is not None:
+        check(lib().b2q_qmm_ws(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), y.data_ptr(), M, N,
+                               K, group_size, bits, 1 if transpose else 0, workspace.data_ptr(),
+                               workspace.numel() * workspace.element_size(), _stream()))
+        return y
     check(lib().b2q_qmm(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), y.data_ptr(), M, N, K,
                         group_size, bits, 1 if transpose else 0, _stream()))
     return y
 
 
 def gather_qmm(x, w, scales, biases, lhs_indices=None, rhs_indices=None, transpose: bool = True,
-               group_size: int = 64, bits: int = 4, sorted_indices: bool = False):
+               group_size: int = 64, bits: int = 4, sorted_indices: bool = False, workspace=None):
     """MLX gather_qmm: out[i] = x[lhs[i]] . dequant(w[rhs[i]])^T.
 
     x [..., M, K] (leading dims flattened into n_x matrices), w [E, N, K/8];
     indices of the same shape (broadcasting to a common shape is the caller's
     job, as in the reference's Runner); output lhs.shape + [M, N].
+    ``workspace`` selects the allocation-free form (``b2q_gather_qmm_ws``).
     """
     _dev(x, "x", _BF16), _dev(w, "w", _PACK), _dev(scales, "scales", _BF16), _dev(biases, "biases", _BF16)
     if w.dim() != 3:
@@ -146,6 +162,12 @@ def gather_qmm(x, w, scales, biases, lhs_indices=None, rhs_indices=None, transpo
     if lhs is None and batch > n_x:
         raise ValueError("[gather_qmm] without lhs indices the batch cannot exceed x's matrices")
     y = torch.empty(tuple(shape) + (M, N), dtype=torch.bfloat16, device=x.device)
+    if workspace is not None:
+        check(lib().b2q_gather_qmm_ws(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), _ptr(lhs),
+                                      _ptr(rhs), y.data_ptr(), batch, M, N, K, n_x, E, group_size, bits,
+                                      1 if transpose else 0, 1 if sorted_indices else 0, workspace.data_ptr(),
+                                      workspace.numel() * workspace.element_size(), _stream()))
+        return y
     check(lib().b2q_gather_qmm(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), _ptr(lhs), _ptr(rhs),
                                y.data_ptr(), batch, M, N, K, n_x, E, group_size, bits, 1 if transpose else 0,
                                1 if sorted_indices else 0, _stream()))

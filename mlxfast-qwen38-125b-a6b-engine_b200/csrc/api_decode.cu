@@ -49,7 +49,8 @@ int b2q_quantize(const uint16_t* w, uint32_t* w_q, uint16_t* scales, uint16_t* b
 
 static int gather_impl(const char* fn, const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b,
                        const uint32_t* lhs, const uint32_t* rhs, uint16_t* y, int batch, int M, int N, int K,
-                       int n_x, int n_w, int gs, int bits, int transpose, int sorted, void* stream) {
+                       int n_x, int n_w, int gs, int bits, int transpose, int sorted, void* workspace,
+                       size_t workspace_bytes, void* stream) {
   int rc = check_bits_gs(fn, bits, gs);
   if (rc) return rc;
   if (!transpose) return set_error(B2Q_EUNSUPPORTED, "%s: transpose=false is not implemented", fn);
@@ -84,7 +85,8 @@ static int gather_impl(const char* fn, const uint16_t* x, const uint32_t* w, con
     if (rc != B2Q_EUNSUPPORTED) return rc;
   }
   if (M > eng::MAX_COLS && prefill_qmm_eligible(batch, M, N, K, gs, x, w, s, b, y)) {
-    return launch_prefill_gather_qmm(x, w, s, b, lhs, rhs, y, batch, M, N, K, n_x, n_w, gs, sorted, st);
+    return launch_prefill_gather_qmm(x, w, s, b, lhs, rhs, y, batch, M, N, K, n_x, n_w, gs, sorted, workspace,
+                                     workspace_bytes, st);
   }
   GenericArgs a{x, w, s, b, lhs, rhs, y, batch, M, N, K, n_x, n_w, gs};
   return launch_generic_qmv(a, st);
@@ -94,7 +96,7 @@ int b2q_qmm(const uint16_t* x, const uint32_t* w, const uint16_t* scales, const 
             int N, int K, int group_size, int bits, int transpose, void* stream) {
   clear_error();
   return gather_impl("quantized_matmul", x, w, scales, biases, nullptr, nullptr, y, 1, M, N, K, 1, 1, group_size,
-                     bits, transpose, 0, stream);
+                     bits, transpose, 0, nullptr, 0, stream);
 }
 
 int b2q_gather_qmm(const uint16_t* x, const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
@@ -103,7 +105,32 @@ int b2q_gather_qmm(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
                    void* stream) {
   clear_error();
   return gather_impl("gather_qmm", x, w, scales, biases, lhs_indices, rhs_indices, y, batch, M, N, K, n_x, n_w,
-                     group_size, bits, transpose, sorted_indices, stream);
+                     group_size, bits, transpose, sorted_indices, nullptr, 0, stream);
+}
+
+size_t b2q_gather_qmm_workspace_size(int batch, int M, int N, int K, int n_w) {
+  (void)N;
+  if (M <= eng::MAX_COLS) return 256;  // the streaming kernels take no workspace
+  return prefill_gather_qmm_ws_bytes(batch, M, K, n_w);
+}
+
+int b2q_qmm_ws(const uint16_t* x, const uint32_t* w, const uint16_t* scales, const uint16_t* biases, uint16_t* y,
+               int M, int N, int K, int group_size, int bits, int transpose, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (!workspace) return set_error(B2Q_EINVAL, "quantized_matmul_ws: null workspace");
+  return gather_impl("quantized_matmul_ws", x, w, scales, biases, nullptr, nullptr, y, 1, M, N, K, 1, 1,
+                     group_size, bits, transpose, 0, workspace, workspace_bytes, stream);
+}
+
+int b2q_gather_qmm_ws(const uint16_t* x, const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                      const uint32_t* lhs_indices, const uint32_t* rhs_indices, uint16_t* y, int batch, int M, int N,
+                      int K, int n_x, int n_w, int group_size, int bits, int transpose, int sorted_indices,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (!workspace) return set_error(B2Q_EINVAL, "gather_qmm_ws: null workspace");
+  return gather_impl("gather_qmm_ws", x, w, scales, biases, lhs_indices, rhs_indices, y, batch, M, N, K, n_x, n_w,
+                     group_size, bits, transpose, sorted_indices, workspace, workspace_bytes, stream);
 }
 
 int b2q_moe_router_logits(const uint16_t* x, const uint16_t* wr, float* logits, int T, int E, int H, void* stream) {

@@ -197,10 +197,14 @@ __device__ __forceinline__ void word_offsets(int cc0, int rows, uint32_t (&woff)
 }
 
 // Row block b's P rows start at b * bstride, its Q rows qoff further.
-template <int SLOT, int NRB>
+// LUT: the metadata blocks hold u16 pair indices (sP / sQ) into `lut`, a
+// shared-memory copy of the pair table (scale bits | bias bits << 16): the same
+// bf16 bits reach the same arithmetic as with the scale / bias blocks.
+template <int SLOT, int NRB, bool LUT = false>
 __device__ __forceinline__ void dot_i8(const uint8_t* st_base, const uint32_t (&woff)[XB / 2], int bstride, int qoff,
                                        int slot0, int nslot, int gs, const uint32_t (&xb)[XB], const float2* gsc,
-                                       const Meta (&m)[NRB], float (&accP)[NRB], float (&accQ)[NRB]) {
+                                       const Meta (&m)[NRB], float (&accP)[NRB], float (&accQ)[NRB],
+                                       const uint32_t* lut = nullptr) {
   constexpr int WS = SLOT / 8;
   const int c = threadIdx.x & 3;
   const int spg = gs / SLOT;  // slots per group (1 or 2)
@@ -240,10 +244,20 @@ __device__ __forceinline__ void dot_i8(const uint8_t* st_base, const uint32_t (&
         if (live) {
           const float2 sc = gsc[g];
           const float xg = (spg == 1 || (c & 1) == 0) ? sc.y : 0.0f;
-          const float sP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
-          const float bP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
-          const float sQ = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw)));
-          const float bQ = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw)));
+          float sP, bP, sQ, bQ;
+          if (LUT) {
+            const uint32_t pP = lut[*reinterpret_cast<const uint16_t*>(m[b].sP + moff(m[b].rowP, g, m[b].mb, m[b].sw))];
+            const uint32_t pQ = lut[*reinterpret_cast<const uint16_t*>(m[b].sQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw))];
+            sP = lbf(pP);
+            bP = hbf(pP);
+            sQ = lbf(pQ);
+            bQ = hbf(pQ);
+          } else {
+            sP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
+            bP = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bP + moff(m[b].rowP, g, m[b].mb, m[b].sw)));
+            sQ = bf2f(*reinterpret_cast<const uint16_t*>(m[b].sQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw)));
+            bQ = bf2f(*reinterpret_cast<const uint16_t*>(m[b].bQ + moff(m[b].rowQ, g, m[b].mb, m[b].sw)));
+          }
           accP[b] = fmaf(sP, (float)vP * sc.x, fmaf(bP, xg, accP[b]));
           accQ[b] = fmaf(sQ, (float)vQ * sc.x, fmaf(bQ, xg, accQ[b]));
         }
@@ -352,8 +366,9 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   // aligned by pointer arithmetic on the shared array (an integer round trip
   // would hide the address space and turn every shared access generic)
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  constexpr bool FUSED = MODE != D2_QMV;
+  constexpr bool FUSED = MODE == D2_FUSED || MODE == D2_FUSED_EP;
   constexpr bool EP = MODE == D2_FUSED_EP;
+  constexpr bool LUT = MODE == D2_QMV_LUT;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int NS = p.nstage;
 
@@ -370,6 +385,8 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   float* rsum = reinterpret_cast<float*>(lslot + MAXK);          // [NWARP]
   int* lastf_sm = reinterpret_cast<int*>(rsum + NWARP);          // [MAXST] producer bookkeeping
   unsigned* ycnt = reinterpret_cast<unsigned*>(lastf_sm + MAXST); // [MAXBLK] down units finished per block
+  uint64_t* lutbar = reinterpret_cast<uint64_t*>(misc + 640);   // the pair table's copy landed (LUT)
+  uint32_t* lut_sm = reinterpret_cast<uint32_t*>(smem + p.off_lut);
   float* ysm = reinterpret_cast<float*>(smem + p.off_ysm);       // [MAXBLK][MAXK][ROWS_D] slot products
   float* red = reinterpret_cast<float*>(smem + p.off_red);       // [nstage][NCW][32]
   float2* gsc = reinterpret_cast<float2*>(smem + p.off_xs);     // per group: 2^(E_g - 14), sum(x)
@@ -382,6 +399,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       mbar_init(&rfull[i], NCW);
     }
     for (int i = 0; i < MAXBLK; ++i) ycnt[i] = 0u;
+    if (LUT) mbar_init(lutbar, 1);
     *abort_flag = 0;
     nloc_sm[1] = 0;  // routed slots selected so far (the producer's early start)
     fence_barrier_init();
@@ -414,6 +432,12 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   const unsigned tag = FUSED ? __ldcg(p.ctr + D2_CTR_TAG) + 1u : 0u;
   unsigned long long* tlg = reinterpret_cast<unsigned long long*>(p.ctr + D2_CTR_LOGITS);
   __syncthreads();
+  if (LUT && warp == NCW && lane == 0) {
+    // the pair table, one bulk copy; the consumers wait for it before their
+    // first unit's scaling (after the pass over x)
+    mbar_arrive_expect_tx(lutbar, (uint32_t)p.lut_words * 4u);
+    bulk_g2s(lut_sm, p.lut, (uint32_t)p.lut_words * 4u, lutbar, policy_evict_last());
+  }
 
   const int K1 = p.K1;
   constexpr int CPC = CPG * 4;  // 8-value chunks per group
@@ -650,10 +674,11 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
           const int u = bx + it * G;
           const int row = u * ROWS_QMV;
           info[s] = make_int4(U_QMV, 0, u, 0);
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(ROWS_QMV * K1 / 2 + 2 * ROWS_QMV * p.mb1));
+          // LUT: one block of pair indices in place of the scale and bias blocks
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(ROWS_QMV * K1 / 2 + (LUT ? 1 : 2) * ROWS_QMV * p.mb1));
           tma3(st, &p.map[MW], 0, row, 0, &full[s], pol);
           tc::tma_load_2d(st + p.st_meta1, &p.map[MS], 0, row, &full[s], pol);
-          tc::tma_load_2d(st + p.st_meta1 + p.st_mstep1, &p.map[MB], 0, row, &full[s], pol);
+          if (!LUT) tc::tma_load_2d(st + p.st_meta1 + p.st_mstep1, &p.map[MB], 0, row, &full[s], pol);
         } else if (it < ngu) {
           const int u = G - 1 - bx + it * G;
           const int z = u / (F / ROWS_GU), rb = u % (F / ROWS_GU);
@@ -902,6 +927,10 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
 
     int4 inf = make_int4(U_END, 0, 0, 0);
     bool live = true;
+    if (LUT && !__all_sync(0xffffffffu, tc::wait(lutbar, 0u, deadline, abort_flag))) {
+      if (!*abort_flag && lane == 0) record_error(p.err, B2Q_ETIMEOUT);
+      *abort_flag = 1;
+    }
     // ---- phase 1: gate|up (fused) or qmv units ----
     for (;; advance()) {
       if (!wait_full()) {
@@ -938,7 +967,7 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         const Meta m[2] = {{mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, r, 8 + r, p.mb1, p.sw1 != 0},
                            {mb, mb + p.st_mstep1, mb, mb + p.st_mstep1, 16 + r, 24 + r, p.mb1, p.sw1 != 0}};
         float accP[2] = {0.0f, 0.0f}, accQ[2] = {0.0f, 0.0f};
-        dot_i8<SLOT, 2>(st, woff, 2048, 1024, slot01, nslot1, p.gs, xb, gsc, m, accP, accQ);
+        dot_i8<SLOT, 2, LUT>(st, woff, 2048, 1024, slot01, nslot1, p.gs, xb, gsc, m, accP, accQ, lut_sm);
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
           accP[b] += __shfl_xor_sync(0xffffffffu, accP[b], 1);
@@ -1024,10 +1053,12 @@ static int plan(D2Params& p, int mode) {
   p.mb1 = K1 / p.gs * 2;
   p.sw1 = p.mb1 == 128;
   int st;
-  if (mode == D2_QMV) {
+  const bool qmv = mode == D2_QMV || mode == D2_QMV_LUT;
+  if (qmv) {
     p.st_meta1 = ROWS_QMV * K1 / 2;
     p.st_mstep1 = round_up(ROWS_QMV * p.mb1, p.sw1 ? 1024 : 128);
-    st = p.st_meta1 + 2 * p.st_mstep1;
+    // scale and bias blocks, or (LUT) one block of pair indices of the same layout
+    st = p.st_meta1 + (mode == D2_QMV_LUT ? 1 : 2) * p.st_mstep1;
     p.mb2 = p.sw2 = p.st_meta2 = p.st_mstep2 = p.st_act = p.st_asc = 0;
   } else {
     p.st_meta1 = 2 * ROWS_GU * K1 / 2;
@@ -1051,10 +1082,12 @@ static int plan(D2Params& p, int mode) {
   // of every stage and the barriers / routing state
   const int xs_bytes = round_up(K1 / p.gs * 8, 128);
   // down blocks' slot tables (fused)
-  const int ys_bytes = mode == D2_QMV ? 0 : (p.H / ROWS_D + di.sm_count - 1) / di.sm_count * MAXK * ROWS_D * 4;
+  const int ys_bytes = qmv ? 0 : (p.H / ROWS_D + di.sm_count - 1) / di.sm_count * MAXK * ROWS_D * 4;
+  // the shared-memory copy of the pair table (LUT)
+  const int lut_bytes = mode == D2_QMV_LUT ? round_up(p.lut_words * 4, 128) : 0;
   int ns = MAXST;
   for (; ns >= 2; --ns) {
-    const int total = ns * p.stage_bytes + xs_bytes + ys_bytes + ns * NCW * 32 * 4 + MISC_BYTES + 1024;
+    const int total = ns * p.stage_bytes + xs_bytes + ys_bytes + ns * NCW * 32 * 4 + MISC_BYTES + lut_bytes + 1024;
     if (total <= di.smem_optin) break;
   }
   if (ns < 2) return set_error(B2Q_EUNSUPPORTED, "decode kernel: stages of %d bytes do not fit", p.stage_bytes);
@@ -1068,6 +1101,8 @@ static int plan(D2Params& p, int mode) {
   off += ns * NCW * 32 * 4;
   p.off_misc = off;
   off += MISC_BYTES;
+  p.off_lut = off;
+  off += lut_bytes;
   p.smem_bytes = off + 1024;
   return B2Q_OK;
 }
@@ -1111,6 +1146,9 @@ static int launch(const D2Params& p, int mode, cudaStream_t st) {
     case 1 * 4 + D2_QMV: return launch_t<1, D2_QMV>(p, st, grid);
     case 2 * 4 + D2_QMV: return launch_t<2, D2_QMV>(p, st, grid);
     case 4 * 4 + D2_QMV: return launch_t<4, D2_QMV>(p, st, grid);
+    case 1 * 4 + D2_QMV_LUT: return launch_t<1, D2_QMV_LUT>(p, st, grid);
+    case 2 * 4 + D2_QMV_LUT: return launch_t<2, D2_QMV_LUT>(p, st, grid);
+    case 4 * 4 + D2_QMV_LUT: return launch_t<4, D2_QMV_LUT>(p, st, grid);
     case 1 * 4 + D2_FUSED: return launch_t<1, D2_FUSED>(p, st, grid);
     case 2 * 4 + D2_FUSED: return launch_t<2, D2_FUSED>(p, st, grid);
     case 4 * 4 + D2_FUSED: return launch_t<4, D2_FUSED>(p, st, grid);
@@ -1228,6 +1266,51 @@ int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16
     put_maps(key, p.map, 3);
   }
   return launch(p, D2_QMV, st);
+}
+
+// Largest pair table the kernel copies into shared memory: 16,384 entries
+// (64 KB) leave room for a ring of two 68 KB stages at K = 4096.
+constexpr int LUT_MAX_WORDS = 16384;
+
+bool d2_qmv_lut_eligible(int N, int K, int gs, int count, const void* x, const void* w, const void* index,
+                         const void* table) {
+  if (!(gs_ok(gs) && N >= ROWS_QMV && N % 16 == 0 && xreg_split_ok(K, gs) && count >= 1 &&
+        round_up(count, 4) <= LUT_MAX_WORDS && aligned16(x) && aligned16(w) && aligned16(index) &&
+        aligned16(table)))
+    return false;
+  D2Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.gs = gs;
+  p.K1 = K;
+  p.lut_words = round_up(count, 4);
+  const bool fits = plan(p, D2_QMV_LUT) == B2Q_OK;
+  clear_error();
+  return fits;
+}
+
+int d2_qmv_lut(const uint16_t* x, const uint32_t* w, const uint16_t* index, const uint32_t* table, int count,
+               uint16_t* y, int N, int K, int gs, cudaStream_t st) {
+  D2Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.gs = gs;
+  p.K1 = K;
+  p.N = N;
+  p.x = x;
+  p.y = y;
+  p.lut = table;
+  p.lut_words = round_up(count, 4);
+  p.timeout_ns = 2000000000ll;
+  int rc = plan(p, D2_QMV_LUT);
+  if (rc) return rc;
+  const void* ptrs[3] = {w, index, nullptr};
+  const MapKey key = map_key(D2_QMV_LUT, ptrs, 3, N, K, 0, gs);
+  if (!find_maps(key, p.map, 3)) {
+    // the index has the layout of the scales ([N, K/gs] 16-bit): the same maps
+    rc = set_family(p, MW, MS, MB, w, index, index, (uint64_t)N, K, ROWS_QMV);
+    if (rc) return rc;
+    put_maps(key, p.map, 3);
+  }
+  return launch(p, D2_QMV_LUT, st);
 }
 
 bool d2_moe_eligible(int H, int E, int F, int k, int gs) {

@@ -8,7 +8,7 @@
 
 namespace b2q {
 
-enum { D2_QMV = 0, D2_FUSED = 1, D2_FUSED_EP = 2 };
+enum { D2_QMV = 0, D2_FUSED = 1, D2_FUSED_EP = 2, D2_QMV_LUT = 3 };
 
 // Grid words of the fused kernel (the last CTA out re-arms them):
 //   [2] CTAs exited, [3] tag of the last call,
@@ -39,6 +39,9 @@ struct alignas(64) D2Params {
   long long timeout_ns;
   int e_lo, e_local;  // expert parallel: this rank holds experts [e_lo, e_lo + e_local) (e_local 0: all)
   float* out_f32;     // expert parallel: fp32 partial output instead of bf16 `out`
+  const uint32_t* lut;  // qmv through the metadata pair table: scale_bits | bias_bits << 16 per entry
+  int lut_words;        // table entries copied into shared memory (a multiple of 4)
+  int off_lut;          // shared-memory offset of the table copy
   // launch plan (host)
   int nstage, stage_bytes, smem_bytes;
   int off_xs, off_ysm, off_red, off_misc;
@@ -51,6 +54,12 @@ struct alignas(64) D2Params {
 bool d2_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const void* s, const void* b);
 int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b, uint16_t* y, int N, int K,
            int gs, cudaStream_t st);
+// qmv with the group metadata read through a pair table (index u16 [N, K/gs],
+// table of `count` entries, 16-byte aligned, readable up to round_up(count, 4)).
+bool d2_qmv_lut_eligible(int N, int K, int gs, int count, const void* x, const void* w, const void* index,
+                         const void* table);
+int d2_qmv_lut(const uint16_t* x, const uint32_t* w, const uint16_t* index, const uint32_t* table, int count,
+               uint16_t* y, int N, int K, int gs, cudaStream_t st);
 bool d2_moe_eligible(int H, int E, int F, int k, int gs);
 // Device scratch of one fused call (all caller-owned; ctr zeroed once: the
 // grid words and tagged router logits, 4096 bytes).

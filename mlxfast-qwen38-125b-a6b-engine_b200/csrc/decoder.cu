@@ -20,6 +20,8 @@
 //                  then k and v appended to the bf16 KV cache at each row's
 //                  position (one launch instead of copies, two ropes and two
 //                  scatters).
+//   attn_decode  : rope_kv + gqa_decode in one launch for windows of up to 8
+//                  rows, the chunks merged by the last CTA of each kv head.
 //   gqa_decode   : attention of a few query rows over the KV cache rows
 //                  [0, position] (decode and short windows): split over key
 //                  chunks of 128, each CTA one kv head and chunk with the g
@@ -32,6 +34,31 @@
 
 namespace b2q {
 namespace dec {
+
+// Programmatic dependent launch for the per-layer kernels of a decode step: a
+// kernel waits for its predecessor in the stream before reading anything
+// (griddepcontrol.wait), then lets its own successor start launching, so each
+// launch's set-up overlaps the previous kernel's tail.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 __global__ void embed_gather_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
                                     const uint16_t* __restrict__ b, const int32_t* __restrict__ ids,
@@ -133,6 +160,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
                         uint16_t* h_out, uint16_t* __restrict__ out, int H, float eps) {
   // h_out may be h (in place): each thread re-reads only the words it wrote
   __shared__ float red[NORM_THREADS / 32];
+  pdl_enter();
   const int t = blockIdx.x;
   const uint4* hr = reinterpret_cast<const uint4*>(h + (size_t)t * H);
   const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + (size_t)t * H) : nullptr;
@@ -389,6 +417,285 @@ __global__ void gqa_merge_kernel(const float* __restrict__ part, uint16_t* __res
   }
 }
 
+// ---- one-launch attention of a decode window -----------------------------------
+// rope_kv + gqa_chunk + gqa_merge in one kernel for windows of at most 8 rows
+// (the graph decode step and the MTP verify windows). CTA (kv head kh, chunk c,
+// row t) covers keys [c * AD_CH, c * AD_CH + AD_CH) up to row t's position:
+//  * keys at positions of the window's own rows are taken from the q|k|v rows
+//    (k roped here), not from the cache, so no CTA waits for another's append;
+//    the CTA whose chunk holds row t's position appends row t's k / v of head kh
+//    to the cache (one writer per row and head);
+//  * cache keys are staged with cp.async (every 16-byte piece in flight at once);
+//  * scores, chunk max / sum and weighted values as gqa_chunk (fp32, log2 domain);
+//  * the last CTA of (t, kh) to finish (a counter per (t, kh) in the workspace,
+//    re-armed by that CTA) merges the chunks and writes the bf16 output.
+// q and k are rounded to bf16 after the rotation and v is read as bf16, as the
+// separate kernels store them, so the cache rows are bit-identical to rope_kv's.
+constexpr int AD_CH = 64;        // keys per CTA
+constexpr int AD_THREADS = 128;  // two threads per key in the score phase
+constexpr int AD_MAXT = 8;       // window rows
+
+// K rows (padded), V rows, g roped q rows (fp32), g x AD_CH probabilities, and
+// the merge's per-(head, chunk) maxima, sums and weights
+__host__ __device__ inline size_t ad_smem_bytes(int g, int d, int n_chunks) {
+  return (size_t)AD_CH * gqa_kld(d) * 2 + (size_t)AD_CH * d * 2 + (size_t)g * d * 4 + (size_t)g * AD_CH * 4 +
+         (size_t)3 * g * n_chunks * 4;
+}
+
+// partial of one (row, kv head, chunk): [g][d] weighted values (16-byte
+// aligned for the merge's vector loads), then [g] maxima, [g] sums, padding
+__host__ __device__ inline int ad_stride(int g, int d) { return g * d + (2 * g + 3) / 4 * 4; }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// roped pair (p, p + half) of one head row at position pos, rounded to bf16
+__device__ __forceinline__ void rope_pair(const uint16_t* x, int p, int half, int pos, float log2_theta,
+                                          uint16_t& r0, uint16_t& r1) {
+  const float inv_freq = exp2f(-((float)p / (float)half) * log2_theta);
+  float sn, cs;
+  sincosf((float)pos * inv_freq, &sn, &cs);
+  const float a = bf2f(x[p]), c = bf2f(x[p + half]);
+  r0 = f2bf(a * cs - c * sn);
+  r1 = f2bf(a * sn + c * cs);
+}
+
+__global__ void __launch_bounds__(AD_THREADS)
+    attn_decode_kernel(const uint16_t* __restrict__ qkv, int q_ld, int T, const int32_t* __restrict__ positions,
+                       int nq, int nk, int d, float log2_theta, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
+                       int window, int n_chunks, float scale_log2, float* __restrict__ part, unsigned* __restrict__ cnt,
+                       uint16_t* __restrict__ out, int* err) {
+  extern __shared__ __align__(16) unsigned char asm_[];
+  const int kld = gqa_kld(d);
+  uint16_t* ks = reinterpret_cast<uint16_t*>(asm_);
+  uint16_t* vs = ks + (size_t)AD_CH * kld;
+  float* qs = reinterpret_cast<float*>(vs + (size_t)AD_CH * d);
+  float* ps = qs + (size_t)nq / nk * d;
+  __shared__ float red[ATT_MAXG][AD_CH / 32];
+  __shared__ float stat[ATT_MAXG];
+  __shared__ int wpos[AD_MAXT];
+  __shared__ int last_sm;
+  const int kh = blockIdx.x, chunk = blockIdx.y, t = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = nq / nk, half = d / 2, vpr = d / 8;
+  pdl_enter();
+  if (tid < T) wpos[tid] = positions[tid];
+  __syncthreads();
+  int pos = wpos[t];
+  const bool bad = pos < 0 || pos >= window;
+  if (bad) {  // outside the cache window: recorded, attends row 0 only, appends nothing
+    if (kh == 0 && chunk == 0 && tid == 0) record_error(err, B2Q_EINVAL);
+    pos = 0;
+  }
+  const uint16_t* row_t = qkv + (size_t)t * q_ld;
+  const int k0 = chunk * AD_CH;
+  const int nkeys = min(AD_CH, pos + 1 - k0);  // <= 0: chunk entirely after the position
+  // the window row whose position is key j (the last such row), or -1
+  auto window_row = [&](int j) {
+    int w = -1;
+    for (int u = 0; u < T; ++u)
+      if (wpos[u] == j) w = u;
+    return w;
+  };
+  // row t's k / v of head kh into the cache, by the chunk holding its position
+  if (!bad && chunk == pos / AD_CH) {
+    const uint16_t* krow = row_t + (size_t)(nq + kh) * d;
+    const uint16_t* vrow = row_t + (size_t)(nq + nk + kh) * d;
+    uint16_t* kdst = kc + ((size_t)pos * nk + kh) * d;
+    uint16_t* vdst = vc + ((size_t)pos * nk + kh) * d;
+    for (int p = tid; p < half; p += AD_THREADS) {
+      uint16_t r0, r1;
+      rope_pair(krow, p, half, pos, log2_theta, r0, r1);
+      kdst[p] = r0;
+      kdst[p + half] = r1;
+      vdst[p] = vrow[p];
+      vdst[p + half] = vrow[p + half];
+    }
+  }
+  const int stride = ad_stride(g, d);
+  float* pout = part + (((size_t)t * nk + kh) * n_chunks + chunk) * (size_t)stride;
+  float* pm = pout + (size_t)g * d;  // maxima, then sums
+  if (nkeys <= 0) {
+    for (int j = tid; j < g; j += AD_THREADS) {
+      pm[j] = -INFINITY;
+      pm[g + j] = 0.0f;
+    }
+  } else {
+    // cache keys: every 16-byte piece in flight at once
+    for (int i = tid; i < nkeys * vpr; i += AD_THREADS) {
+      const int key = i / vpr, c = i % vpr;
+      if (window_row(k0 + key) >= 0) continue;
+      const size_t src = ((size_t)(k0 + key) * nk + kh) * d + (size_t)c * 8;
+      cp_async16(ks + (size_t)key * kld + c * 8, kc + src);
+      cp_async16(vs + (size_t)key * d + c * 8, vc + src);
+    }
+    // keys of the window's rows from the q|k|v rows (k roped at the key's position)
+    for (int u = 0; u < T; ++u) {
+      const int j = wpos[u];
+      if (j < k0 || j >= k0 + nkeys || window_row(j) != u) continue;
+      const uint16_t* urow = qkv + (size_t)u * q_ld;
+      const uint16_t* krow = urow + (size_t)(nq + kh) * d;
+      const uint16_t* vrow = urow + (size_t)(nq + nk + kh) * d;
+      for (int p = tid; p < half; p += AD_THREADS) {
+        uint16_t r0, r1;
+        rope_pair(krow, p, half, j, log2_theta, r0, r1);
+        ks[(size_t)(j - k0) * kld + p] = r0;
+        ks[(size_t)(j - k0) * kld + p + half] = r1;
+        vs[(size_t)(j - k0) * d + p] = vrow[p];
+        vs[(size_t)(j - k0) * d + p + half] = vrow[p + half];
+      }
+    }
+    // row t's g query heads, roped at its position
+    for (int i = tid; i < g * half; i += AD_THREADS) {
+      const int j = i / half, p = i % half;
+      uint16_t r0, r1;
+      rope_pair(row_t + (size_t)(kh * g + j) * d, p, half, pos, log2_theta, r0, r1);
+      qs[j * d + p] = bf2f(r0);
+      qs[j * d + p + half] = bf2f(r1);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    // scores: thread (key, head parity hs): heads hs, hs + 2, ...
+    const int key = tid % AD_CH, hs = tid / AD_CH;
+    constexpr int HPT = ATT_MAXG / 2;
+    float sc[HPT];
+#pragma unroll
+    for (int jj = 0; jj < HPT; ++jj) sc[jj] = 0.0f;
+    const bool kl = key < nkeys;
+    if (kl) {
+      const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)key * kld);
+      for (int v = 0; v < vpr; ++v) {
+        const uint4 kv = kr[v];
+        const uint32_t u[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const float a = bf2f((uint16_t)(u[m] & 0xFFFF)), c = bf2f((uint16_t)(u[m] >> 16));
+          const int e = v * 8 + 2 * m;
+#pragma unroll
+          for (int jj = 0; jj < HPT; ++jj) {
+            const int j = hs + 2 * jj;
+            if (j < g) sc[jj] = fmaf(c, qs[j * d + e + 1], fmaf(a, qs[j * d + e], sc[jj]));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < HPT; ++jj) sc[jj] = kl ? sc[jj] * scale_log2 : -INFINITY;
+    // per head: chunk max (the two warps of a head parity), then 2^(s - max) and its sum
+    const int hw = warp & 1;  // warp within the head parity
+#pragma unroll
+    for (int jj = 0; jj < HPT; ++jj) {
+      const int j = hs + 2 * jj;
+      if (j < g) {
+        float m = sc[jj];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        if (lane == 0) red[j][hw] = m;
+      }
+    }
+    __syncthreads();
+    if (tid < g) stat[tid] = fmaxf(red[tid][0], red[tid][1]);
+    __syncthreads();
+#pragma unroll
+    for (int jj = 0; jj < HPT; ++jj) {
+      const int j = hs + 2 * jj;
+      if (j < g) {
+        const float pj = kl ? exp2f(sc[jj] - stat[j]) : 0.0f;
+        ps[j * AD_CH + key] = pj;
+        float l = pj;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        if (lane == 0) red[j][hw] = l;
+      }
+    }
+    __syncthreads();
+    if (tid < g) {
+      pm[tid] = stat[tid];
+      pm[g + tid] = red[tid][0] + red[tid][1];
+    }
+    // weighted values: thread = dimension
+    for (int e = tid; e < d; e += AD_THREADS) {
+      float acc[ATT_MAXG];
+#pragma unroll
+      for (int j = 0; j < ATT_MAXG; ++j) acc[j] = 0.0f;
+#pragma unroll 4
+      for (int k2 = 0; k2 < nkeys; ++k2) {
+        const float vv = bf2f(vs[(size_t)k2 * d + e]);
+#pragma unroll
+        for (int j = 0; j < ATT_MAXG; ++j)
+          if (j < g) acc[j] = fmaf(ps[j * AD_CH + k2], vv, acc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < ATT_MAXG; ++j)
+        if (j < g) pout[(size_t)j * d + e] = acc[j];
+    }
+  }
+  // the last CTA of (t, kh) merges the chunks holding keys (each thread's
+  // partial stores fenced before the block's arrival is counted)
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&cnt[t * nk + kh], 1u);
+    last_sm = prev == (unsigned)(n_chunks - 1);
+    if (last_sm) cnt[t * nk + kh] = 0u;  // re-armed for the next call
+  }
+  __syncthreads();
+  if (!last_sm) return;
+  __threadfence();
+  // merge: every chunk's max and sum staged at once, one weight per (head,
+  // chunk), then each 4-value column of the outputs over the chunks with its
+  // loads in flight together
+  const int nc = pos / AD_CH + 1;  // chunks with keys
+  const float* base = part + ((size_t)t * nk + kh) * n_chunks * (size_t)stride;
+  float* cm = ps + (size_t)g * AD_CH;  // [g][nc] maxima, [g][nc] sums, [g][nc] weights
+  float* cl = cm + (size_t)g * n_chunks;
+  float* cw = cl + (size_t)g * n_chunks;
+  for (int i = tid; i < g * nc; i += AD_THREADS) {
+    const int j = i / nc, c = i % nc;
+    cm[i] = __ldcg(base + (size_t)c * stride + (size_t)g * d + j);
+    cl[i] = __ldcg(base + (size_t)c * stride + (size_t)g * d + g + j);
+  }
+  __syncthreads();
+  if (tid < g) {
+    float M = -INFINITY;
+    for (int c = 0; c < nc; ++c) M = fmaxf(M, cm[tid * nc + c]);
+    float L = 0.0f;
+    for (int c = 0; c < nc; ++c) L += exp2f(cm[tid * nc + c] - M) * cl[tid * nc + c];
+    const float invL = 1.0f / L;
+    for (int c = 0; c < nc; ++c) cw[tid * nc + c] = exp2f(cm[tid * nc + c] - M) * invL;
+  }
+  __syncthreads();
+  constexpr int MB = 8;  // chunks whose loads are in flight together
+  const int ncol = g * d / 4;
+  for (int q = tid; q < ncol; q += AD_THREADS) {
+    const int j = 4 * q / d;
+    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int c0 = 0; c0 < nc; c0 += MB) {
+      float4 v[MB];
+#pragma unroll
+      for (int u = 0; u < MB; ++u)
+        v[u] = c0 + u < nc ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)(c0 + u) * stride) + q)
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int u = 0; u < MB; ++u) {
+        const float wgt = c0 + u < nc ? cw[j * nc + c0 + u] : 0.0f;
+        a.x = fmaf(wgt, v[u].x, a.x);
+        a.y = fmaf(wgt, v[u].y, a.y);
+        a.z = fmaf(wgt, v[u].z, a.z);
+        a.w = fmaf(wgt, v[u].w, a.w);
+      }
+    }
+    const int e = 4 * q - j * d;
+    uint16_t* o = out + (size_t)t * nq * d + (size_t)(kh * g + j) * d + e;
+    o[0] = f2bf(a.x);
+    o[1] = f2bf(a.y);
+    o[2] = f2bf(a.z);
+    o[3] = f2bf(a.w);
+  }
+}
+
 }  // namespace dec
 }  // namespace b2q
 
@@ -451,7 +758,8 @@ int b2q_add_rms_norm(const uint16_t* h, const uint16_t* delta, const uint16_t* w
   if (!h || !weight || !out || (delta && !h_out)) return set_error(B2Q_EINVAL, "add_rms_norm: null pointer");
   if (!aligned16(h) || !aligned16(weight) || !aligned16(out) || (delta && (!aligned16(delta) || !aligned16(h_out))))
     return set_error(B2Q_EINVAL, "add_rms_norm: tensors must be 16-byte aligned");
-  add_rms_norm_kernel<<<T, NORM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(h, delta, weight, h_out, out, H, eps);
+  B2Q_TRY_CUDA(launch_pdl(add_rms_norm_kernel, dim3(T), dim3(NORM_THREADS), 0, static_cast<cudaStream_t>(stream), h,
+                          delta, weight, h_out, out, H, eps));
   B2Q_TRY_CUDA(cudaGetLastError());
   return B2Q_OK;
 }
@@ -513,6 +821,58 @@ int b2q_gqa_decode(const uint16_t* q, int q_ld, const uint16_t* k_cache, const u
                                                                 head_dim, chunks, window, scale_log2, part, status);
   B2Q_TRY_CUDA(cudaGetLastError());
   gqa_merge_kernel<<<dim3(nk, g, T), 128, 0, st>>>(part, out, nk, g, head_dim, chunks);
+  B2Q_TRY_CUDA(cudaGetLastError());
+  return B2Q_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+size_t b2q_attn_decode_workspace_size(int T, int nq, int nk, int head_dim, int window) {
+  if (T < 1 || T > AD_MAXT || nq < 1 || nk < 1 || nq % nk || head_dim < 1 || window < 1) return 0;
+  const size_t chunks = (size_t)(window + AD_CH - 1) / AD_CH;
+  const size_t part = sizeof(float) * (size_t)T * nk * chunks * (size_t)ad_stride(nq / nk, head_dim);
+  return ((size_t)AD_MAXT * nk * 4 + 255) / 256 * 256 + part;
+}
+
+int b2q_attn_decode(const uint16_t* qkv, int q_ld, const int32_t* positions, uint16_t* k_cache, uint16_t* v_cache,
+                    uint16_t* out, int T, int nq, int nk, int head_dim, float theta, int window, int* status,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (T < 0 || T > AD_MAXT || nq < 1 || nk < 1 || nq % nk || nq / nk > ATT_MAXG || head_dim < 8 || head_dim % 8 ||
+      head_dim > ATT_MAXD || window < 1 || q_ld < (nq + 2 * nk) * head_dim || q_ld % 8 || !(theta > 1.0f))
+    return set_error(B2Q_EINVAL, "attn_decode: bad shape (T=%d nq=%d nk=%d head_dim=%d window=%d)", T, nq, nk,
+                     head_dim, window);
+  if (T == 0) return B2Q_OK;
+  if (!qkv || !positions || !k_cache || !v_cache || !out || !workspace)
+    return set_error(B2Q_EINVAL, "attn_decode: null pointer");
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(qkv) || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return set_error(B2Q_EINVAL, "attn_decode: qkv, k_cache, v_cache 16-byte and workspace 256-byte aligned");
+  const size_t need = b2q_attn_decode_workspace_size(T, nq, nk, head_dim, window);
+  if (workspace_bytes < need) return set_error(B2Q_EINVAL, "attn_decode: workspace of %zu bytes needed", need);
+  const int g = nq / nk;
+  const int chunks = (window + AD_CH - 1) / AD_CH;
+  if (chunks > 65535) return set_error(B2Q_EINVAL, "attn_decode: window %d", window);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // counters first (at the same place whatever T), then the chunk partials
+  unsigned* cnt = static_cast<unsigned*>(workspace);
+  float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((size_t)AD_MAXT * nk * 4 + 255) / 256 * 256);
+  const float scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  const size_t smem = ad_smem_bytes(g, head_dim, chunks);
+  static size_t attr_bytes[64] = {};  // dynamic shared memory allowed so far, per device
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (smem + 1024 > (size_t)di.smem_optin)  // the kernel's static shared memory is under 1 KB
+    return set_error(B2Q_EUNSUPPORTED, "attn_decode: %zu bytes of shared memory (window %d)", smem, window);
+  if (smem > attr_bytes[di.device & 63]) {
+    B2Q_TRY_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_bytes[di.device & 63] = smem;
+  }
+  B2Q_TRY_CUDA(launch_pdl(attn_decode_kernel, dim3(nk, chunks, T), dim3(AD_THREADS), smem, st, qkv, q_ld, T,
+                          positions, nq, nk, head_dim, log2f(theta), k_cache, v_cache, window, chunks, scale_log2,
+                          part, cnt, out, status));
   B2Q_TRY_CUDA(cudaGetLastError());
   return B2Q_OK;
 }

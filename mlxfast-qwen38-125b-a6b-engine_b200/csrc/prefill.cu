@@ -148,30 +148,60 @@ __global__ void item_rows_kernel(const uint32_t* __restrict__ item_of, const uin
   out_row[t] = item * (uint32_t)M + (uint32_t)m;
 }
 
+// Temporaries of the tensor-core gather GEMM, in one region: ids, sorted ids,
+// item order, inverse, offsets, row offsets, unit prefix, error word, source /
+// output row tables, sorted x rows.
+struct GatherQmmWs {
+  size_t o_ids, o_sid, o_item, o_inv, o_off, o_roff, o_pre, o_err, o_src, o_out, o_xs, bytes;
+};
+
+static GatherQmmWs gather_qmm_ws_layout(int batch, int M, int K, int E) {
+  auto a256 = [](size_t v) { return (v + 255) / 256 * 256; };
+  const size_t R = (size_t)batch * M;
+  GatherQmmWs l{};
+  size_t off = 0;
+  l.o_ids = off; off = a256(off + 4 * (size_t)batch);
+  l.o_sid = off; off = a256(off + 4 * (size_t)batch);
+  l.o_item = off; off = a256(off + 4 * (size_t)batch);
+  l.o_inv = off; off = a256(off + 4 * (size_t)batch);
+  l.o_off = off; off = a256(off + 4 * ((size_t)E + 1));
+  l.o_roff = off; off = a256(off + 4 * ((size_t)E + 1));
+  l.o_pre = off; off = a256(off + 4 * ((size_t)E + 1));
+  l.o_err = off; off = a256(off + 4);
+  l.o_src = off; off = a256(off + 4 * R);
+  l.o_out = off; off = a256(off + 4 * R);
+  l.o_xs = off; off = a256(off + 2 * R * (size_t)K);
+  l.bytes = off;
+  return l;
+}
+
+size_t prefill_gather_qmm_ws_bytes(int batch, int M, int K, int n_w) {
+  if (batch <= 0 || M <= 0 || K <= 0 || n_w <= 0) return 0;
+  return gather_qmm_ws_layout(batch, M, K, n_w).bytes;
+}
+
 int launch_prefill_gather_qmm(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b,
                               const uint32_t* lhs, const uint32_t* rhs, uint16_t* y, int batch, int M, int N, int K,
-                              int n_x, int n_w, int gs, int sorted, cudaStream_t st) {
+                              int n_x, int n_w, int gs, int sorted, void* workspace, size_t workspace_bytes,
+                              cudaStream_t st) {
   (void)sorted;  // the items are grouped by a stable sort either way
   const int E = n_w;
   if (E < 1 || E > 1024) return set_error(B2Q_EUNSUPPORTED, "gather_qmm: %d weight matrices on tensor cores", E);
   const size_t R = (size_t)batch * M;
-  // temporaries (stream-ordered): ids, sorted ids, item order, inverse, offsets, row offsets,
-  // unit prefix, error word, source / output row tables, sorted x rows
-  auto a256 = [](size_t v) { return (v + 255) / 256 * 256; };
-  size_t off = 0;
-  const size_t o_ids = off; off = a256(off + 4 * (size_t)batch);
-  const size_t o_sid = off; off = a256(off + 4 * (size_t)batch);
-  const size_t o_item = off; off = a256(off + 4 * (size_t)batch);
-  const size_t o_inv = off; off = a256(off + 4 * (size_t)batch);
-  const size_t o_off = off; off = a256(off + 4 * ((size_t)E + 1));
-  const size_t o_roff = off; off = a256(off + 4 * ((size_t)E + 1));
-  const size_t o_pre = off; off = a256(off + 4 * ((size_t)E + 1));
-  const size_t o_err = off; off = a256(off + 4);
-  const size_t o_src = off; off = a256(off + 4 * R);
-  const size_t o_out = off; off = a256(off + 4 * R);
-  const size_t o_xs = off; off = a256(off + 2 * R * (size_t)K);
-  char* tmp = nullptr;
-  B2Q_TRY_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&tmp), off, st));
+  const GatherQmmWs l = gather_qmm_ws_layout(batch, M, K, E);
+  const size_t o_ids = l.o_ids, o_sid = l.o_sid, o_item = l.o_item, o_inv = l.o_inv, o_off = l.o_off,
+               o_roff = l.o_roff, o_pre = l.o_pre, o_err = l.o_err, o_src = l.o_src, o_out = l.o_out, o_xs = l.o_xs;
+  // caller's workspace when given (256-byte aligned, at least l.bytes), else a
+  // stream-ordered temporary freed at the end of the call
+  char* tmp = static_cast<char*>(workspace);
+  const bool owned = tmp == nullptr;
+  if (!owned) {
+    if (workspace_bytes < l.bytes || (reinterpret_cast<uintptr_t>(tmp) & 255))
+      return set_error(B2Q_EINVAL, "gather_qmm: workspace of %zu bytes (256-byte aligned) needed, %zu given",
+                       l.bytes, workspace_bytes);
+  } else {
+    B2Q_TRY_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&tmp), l.bytes, st));
+  }
   auto U32 = [&](size_t o) { return reinterpret_cast<uint32_t*>(tmp + o); };
   int rc = B2Q_OK;
   do {
@@ -211,7 +241,7 @@ int launch_prefill_gather_qmm(const uint16_t* x, const uint32_t* w, const uint16
     if (rc) break;
     rc = tc_launch(p, TC_PLAIN, st);
   } while (0);
-  cudaFreeAsync(tmp, st);
+  if (owned) cudaFreeAsync(tmp, st);
   return rc;
 }
 

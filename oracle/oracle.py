@@ -83,6 +83,58 @@ def ep_a2a_plan(idx: np.ndarray, E: int, nranks: int):
     return pos, counts
 
 
+AFFINE_LUT_MAX = 32768          # TrackAffineLUT.maxEntries (TrackAffineLUT.swift:57)
+AFFINE_LUT_DEVICE_FROM = 1 << 20  # groups from which the reference builds on the device (:63)
+
+
+def affine_lut_pairs(scales: np.ndarray, biases: np.ndarray) -> np.ndarray:
+    """scale_bits | bias_bits << 16 per group (TrackAffineLUT.swift:62)."""
+    return scales.astype(np.uint32) | (biases.astype(np.uint32) << 16)
+
+
+def affine_lut_build_loop(scales: np.ndarray, biases: np.ndarray, max_entries: int = AFFINE_LUT_MAX):
+    """The reference's host loop, restated literally in Python (small tensors
+    only): TrackAffineLUT.build, Runner/FastModel/TrackAffineLUT.swift:64-83.
+    Entries in first-occurrence order; None past max_entries."""
+    pairs = affine_lut_pairs(scales, biases).reshape(-1)
+    seen: dict[int, int] = {}
+    table: list[int] = []
+    index = np.zeros(pairs.size, np.uint16)
+    for i, p in enumerate(pairs.tolist()):
+        j = seen.get(p)
+        if j is None:
+            if len(table) >= max_entries:
+                return None
+            j = len(table)
+            seen[p] = j
+            table.append(p)
+        index[i] = j
+    return index.reshape(scales.shape), np.array(table, np.uint32)
+
+
+def affine_lut_build(scales: np.ndarray, biases: np.ndarray, max_entries: int = AFFINE_LUT_MAX):
+    """(index u16 in the scales' shape, table u32) as the reference builds them,
+    or None when the tensor does not qualify. Below 2^20 groups the host loop's
+    first-occurrence order (TrackAffineLUT.swift:64-83), otherwise the device
+    build's ascending pair value (argSort, run starts, cumsum ranks: :88-103);
+    both verified by the round trip (:106-110). Vectorised with numpy."""
+    pairs = affine_lut_pairs(scales, biases).reshape(-1)
+    uniq, first, inv = np.unique(pairs, return_index=True, return_inverse=True)
+    if uniq.size > max_entries:
+        return None
+    if pairs.size < AFFINE_LUT_DEVICE_FROM:
+        order = np.argsort(first, kind="stable")  # entry j = j-th pair to appear
+        rank = np.empty(uniq.size, np.int64)
+        rank[order] = np.arange(uniq.size)
+        table, index = uniq[order], rank[inv.reshape(-1)]
+    else:
+        table, index = uniq, inv.reshape(-1)
+    index = index.astype(np.uint16)
+    if not np.array_equal(table[index], pairs):
+        return None
+    return index.reshape(scales.shape), table.astype(np.uint32)
+
+
 class Oracle:
     def __init__(self, path: str = ORACLE_SO):
         if not os.path.exists(path):

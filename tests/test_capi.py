@@ -61,6 +61,25 @@ def test_workspace_sizes(b2q_mod):
     p = lib.b2q_moe_prefill_workspace_size(2048, 4096, 128, 1536, 8)
     assert p >= 16384 * (3 * 1536 * 2 + 4096 * 2)
     assert lib.b2q_moe_decode_workspace_size(0, 4096, 128, 1536, 8) == 0
+    # the allocation-free product forms: the sorted copy of x dominates
+    q = lib.b2q_gather_qmm_workspace_size(64, 32, 4096, 4096, 16)
+    assert q >= 64 * 32 * 4096 * 2
+    assert lib.b2q_gather_qmm_workspace_size(1, 8, 4096, 4096, 1) > 0
+
+
+def test_ws_products_refuse_small_or_null_workspace(b2q_mod):
+    """Checked on the host before any device call: fake 16-byte aligned
+    addresses are never dereferenced."""
+    lib = b2q_mod.lib()
+    fake = 1 << 20  # aligned, never touched
+    M, N, K = 64, 256, 1024
+    need = lib.b2q_gather_qmm_workspace_size(1, M, N, K, 1)
+    assert lib.b2q_qmm_ws(fake, fake, fake, fake, fake, M, N, K, 64, 4, 1, None, 0, None) == -1
+    assert b"null workspace" in lib.b2q_last_error()
+    assert lib.b2q_qmm_ws(fake, fake, fake, fake, fake, M, N, K, 64, 4, 1, fake, need - 256, None) == -1
+    assert b"workspace" in lib.b2q_last_error()
+    assert lib.b2q_gather_qmm_ws(fake, fake, fake, fake, None, None, fake, 2, M, N, K, 2, 2, 64, 4, 1, 0,
+                                 fake + 16, 1 << 30, None) == -1  # not 256-byte aligned
 
 
 def test_python_ops_validate_inputs(b2q_mod):

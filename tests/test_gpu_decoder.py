@@ -142,8 +142,8 @@ def test_attention_half_against_fp32(cuda, b2q_mod):
 
     cfg = _tiny()
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    ws = torch.empty(b2q_mod.lib().b2q_gqa_decode_workspace_size(8, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
-                                                                  cfg.max_seq), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(b2q_mod.lib().b2q_attn_decode_workspace_size(8, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+                                                                   cfg.max_seq), dtype=torch.uint8, device="cuda")
     blk = Block(cfg, torch.device("cuda"), 50, status, ws)
     h = synth.activations((12, cfg.hidden), seed=51)
     pos = torch.arange(12, dtype=torch.int32, device="cuda")
@@ -321,3 +321,54 @@ def test_expert_parallel_decoder_one_rank(cuda, b2q_mod):
     torch.cuda.synchronize()
     assert rel_l2(_bf(_np(lg)).reshape(-1), _bf(_np(la)).reshape(-1)) < 2e-2
     assert dec.status() == 0
+
+
+@pytest.mark.parametrize("positions", [[0], [63], [64], [1279], [62, 63, 64], [5, 130, 299], [127, 128]])
+def test_attn_decode_matches_two_kernel_path(cuda, b2q_mod, positions):
+    """b2q_attn_decode (one launch) = b2q_rope_kv + b2q_gqa_decode: identical
+    cache rows, outputs within rounding (the chunk sizes differ: 64 vs 128 keys),
+    and both against fp32 softmax attention; the window's own rows are read from
+    q|k|v (rows 62, 63, 64 cross a chunk boundary). Two calls in a row on one
+    workspace (its counters re-arm)."""
+    import torch
+
+    from b2q import synth
+    from b2q._lib import check, lib
+
+    st = torch.cuda.current_stream().cuda_stream
+    nq, nk, hd, S = 32, 4, 128, 1280
+    T = len(positions)
+    qkv = synth.activations((T, (nq + 2 * nk) * hd), seed=70 + T)
+    pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+    kc0 = synth.activations((S, nk, hd), seed=71)
+    vc0 = synth.activations((S, nk, hd), seed=72)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # the two-kernel path
+    x = qkv.clone()
+    kc1, vc1 = kc0.clone(), vc0.clone()
+    check(lib().b2q_rope_kv(x.data_ptr(), T, nq, nk, hd, pos.data_ptr(), 1e6, kc1.data_ptr(), vc1.data_ptr(), S,
+                            status.data_ptr(), st))
+    ws1 = torch.empty(lib().b2q_gqa_decode_workspace_size(T, nq, nk, hd, S), dtype=torch.uint8, device="cuda")
+    ref = torch.empty((T, nq * hd), dtype=torch.bfloat16, device="cuda")
+    check(lib().b2q_gqa_decode(x.data_ptr(), (nq + 2 * nk) * hd, kc1.data_ptr(), vc1.data_ptr(), pos.data_ptr(),
+                               ref.data_ptr(), T, nq, nk, hd, S, status.data_ptr(), ws1.data_ptr(), ws1.numel(), st))
+    # the fused path
+    ws2 = torch.zeros(lib().b2q_attn_decode_workspace_size(T, nq, nk, hd, S), dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        kc2, vc2 = kc0.clone(), vc0.clone()
+        out = torch.empty((T, nq * hd), dtype=torch.bfloat16, device="cuda")
+        check(lib().b2q_attn_decode(qkv.data_ptr(), (nq + 2 * nk) * hd, pos.data_ptr(), kc2.data_ptr(),
+                                    vc2.data_ptr(), out.data_ptr(), T, nq, nk, hd, 1e6, S, status.data_ptr(),
+                                    ws2.data_ptr(), ws2.numel(), st))
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+        assert rel_l2(_bf(_np(out)), _bf(_np(ref))) < 2e-3
+    qf, kf, vf = x[:, :nq * hd].float().view(T, nq, hd), kc1.float(), vc1.float()
+    exact = torch.empty(T, nq, hd, device="cuda")
+    for t in range(T):
+        p = positions[t]
+        for j in range(nq):
+            s = (kf[:p + 1, j // (nq // nk)] @ qf[t, j]) / hd ** 0.5
+            exact[t, j] = torch.softmax(s, 0) @ vf[:p + 1, j // (nq // nk)]
+    assert rel_l2(_bf(_np(out)), exact.view(T, -1).cpu().numpy()) < 4e-3

@@ -204,3 +204,31 @@ def test_gather_qmm_tensor_core(cuda, b2q_mod, oracle):
             continue
         ref = oracle.qmm_tile_f32(xs[l], ws_[r], ss[r], bs[r], 64, 4)
         assert rel_l2(_bf(yy[i]), ref) < TIGHT, i
+
+
+def test_ws_forms_match_allocating_forms(cuda, b2q_mod):
+    """b2q_qmm_ws / b2q_gather_qmm_ws run the same kernels as b2q_qmm /
+    b2q_gather_qmm on the caller's workspace: identical bits, two calls in a
+    row on one uncleared workspace, M on both sides of the tensor-core switch."""
+    import torch
+
+    from b2q import synth
+
+    E, N, K = 5, 256, 1024
+    w, s, b = synth.packed_weights((E, N), K, 64, seed=31)
+    lhs = torch.tensor([3, 0, 2, 1, 0, 2], dtype=torch.int32, device="cuda").view(torch.uint32)
+    rhs = torch.tensor([4, 0, 4, 2, 1, 0], dtype=torch.int32, device="cuda").view(torch.uint32)
+    for M in (1, 5, 24, 130):
+        x = synth.activations((4, M, K), seed=32 + M)
+        need = b2q_mod.gather_qmm_workspace_size(6, M, N, K, E)
+        ws = torch.full((need,), 0xA5, dtype=torch.uint8, device="cuda")  # garbage: nothing is read before written
+        ref = b2q_mod.gather_qmm(x, w, s, b, lhs, rhs)
+        for _ in range(2):
+            y = b2q_mod.gather_qmm(x, w, s, b, lhs, rhs, workspace=ws)
+            assert torch.equal(y, ref), M
+        x1 = synth.activations((M, K), seed=40 + M)
+        need1 = b2q_mod.gather_qmm_workspace_size(1, M, N, K, 1)
+        ws1 = torch.full((need1,), 0x5A, dtype=torch.uint8, device="cuda")
+        ref1 = b2q_mod.quantized_matmul(x1, w[1], s[1], b[1])
+        for _ in range(2):
+            assert torch.equal(b2q_mod.quantized_matmul(x1, w[1], s[1], b[1], workspace=ws1), ref1), M
