@@ -426,19 +426,26 @@ __global__ void gqa_merge_kernel(const float* __restrict__ part, uint16_t* __res
 //    the CTA whose chunk holds row t's position appends row t's k / v of head kh
 //    to the cache (one writer per row and head);
 //  * cache keys are staged with cp.async (every 16-byte piece in flight at once);
-//  * scores, chunk max / sum and weighted values as gqa_chunk (fp32, log2 domain);
+//  * scores and weighted values on the tensor cores (mma.sync m16n8k16 bf16,
+//    fp32 accumulation): warp w takes keys [16 w, 16 w + 16) of the chunk, the
+//    g query heads (zero-padded to 16) are the M rows; S = Q K^T, then the
+//    chunk's per-head max and 2^(S - max) in fp32, rounded to bf16 as the A
+//    operand of P V (the score fragments are the A fragments: no shuffle);
+//    V fragments by ldmatrix.trans; the four warps' P V partials are added in
+//    warp order (deterministic);
 //  * the last CTA of (t, kh) to finish (a counter per (t, kh) in the workspace,
 //    re-armed by that CTA) merges the chunks and writes the bf16 output.
 // q and k are rounded to bf16 after the rotation and v is read as bf16, as the
 // separate kernels store them, so the cache rows are bit-identical to rope_kv's.
 constexpr int AD_CH = 64;        // keys per CTA
-constexpr int AD_THREADS = 128;  // two threads per key in the score phase
+constexpr int AD_THREADS = 128;  // four warps of 16 keys
 constexpr int AD_MAXT = 8;       // window rows
 
-// K rows (padded), V rows, g roped q rows (fp32), g x AD_CH probabilities, and
+// K and V rows padded by 8 values (ldmatrix / fragment reads of 8 consecutive
+// rows fall in distinct banks), 16 q rows, each warp's g x d P V partial (fp32), and
 // the merge's per-(head, chunk) maxima, sums and weights
 __host__ __device__ inline size_t ad_smem_bytes(int g, int d, int n_chunks) {
-  return (size_t)AD_CH * gqa_kld(d) * 2 + (size_t)AD_CH * d * 2 + (size_t)g * d * 4 + (size_t)g * AD_CH * 4 +
+  return (size_t)2 * AD_CH * gqa_kld(d) * 2 + (size_t)16 * gqa_kld(d) * 2 + (size_t)(AD_THREADS / 32) * g * d * 4 +
          (size_t)3 * g * n_chunks * 4;
 }
 
@@ -450,6 +457,14 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+}
 
 // roped pair (p, p + half) of one head row at position pos, rounded to bf16
 __device__ __forceinline__ void rope_pair(const uint16_t* x, int p, int half, int pos, float log2_theta,
@@ -471,10 +486,11 @@ __global__ void __launch_bounds__(AD_THREADS)
   const int kld = gqa_kld(d);
   uint16_t* ks = reinterpret_cast<uint16_t*>(asm_);
   uint16_t* vs = ks + (size_t)AD_CH * kld;
-  float* qs = reinterpret_cast<float*>(vs + (size_t)AD_CH * d);
-  float* ps = qs + (size_t)nq / nk * d;
-  __shared__ float red[ATT_MAXG][AD_CH / 32];
-  __shared__ float stat[ATT_MAXG];
+  uint16_t* qb = vs + (size_t)AD_CH * kld;                     // [16][kld] bf16 q rows (rows >= g zero)
+  float* ob = reinterpret_cast<float*>(qb + (size_t)16 * kld);  // [warp][g][d] P V partials
+  __shared__ float red[AD_THREADS / 32][16];
+  __shared__ float stat[16];
+  __shared__ float2 rot[ATT_MAXD / 2];  // (cos, sin) of row t's angles
   __shared__ int wpos[AD_MAXT];
   __shared__ int last_sm;
   const int kh = blockIdx.x, chunk = blockIdx.y, t = blockIdx.z;
@@ -523,13 +539,20 @@ __global__ void __launch_bounds__(AD_THREADS)
       pm[g + j] = 0.0f;
     }
   } else {
-    // cache keys: every 16-byte piece in flight at once
-    for (int i = tid; i < nkeys * vpr; i += AD_THREADS) {
+    // cache keys: every 16-byte piece in flight at once; key rows past nkeys zeroed
+    for (int i = tid; i < AD_CH * vpr; i += AD_THREADS) {
       const int key = i / vpr, c = i % vpr;
+      uint16_t* kd = ks + (size_t)key * kld + c * 8;
+      uint16_t* vd = vs + (size_t)key * kld + c * 8;
+      if (key >= nkeys) {
+        *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
       if (window_row(k0 + key) >= 0) continue;
       const size_t src = ((size_t)(k0 + key) * nk + kh) * d + (size_t)c * 8;
-      cp_async16(ks + (size_t)key * kld + c * 8, kc + src);
-      cp_async16(vs + (size_t)key * d + c * 8, vc + src);
+      cp_async16(kd, kc + src);
+      cp_async16(vd, vc + src);
     }
     // keys of the window's rows from the q|k|v rows (k roped at the key's position)
     for (int u = 0; u < T; ++u) {
@@ -543,93 +566,146 @@ __global__ void __launch_bounds__(AD_THREADS)
         rope_pair(krow, p, half, j, log2_theta, r0, r1);
         ks[(size_t)(j - k0) * kld + p] = r0;
         ks[(size_t)(j - k0) * kld + p + half] = r1;
-        vs[(size_t)(j - k0) * d + p] = vrow[p];
-        vs[(size_t)(j - k0) * d + p + half] = vrow[p + half];
+        vs[(size_t)(j - k0) * kld + p] = vrow[p];
+        vs[(size_t)(j - k0) * kld + p + half] = vrow[p + half];
       }
     }
-    // row t's g query heads, roped at its position
-    for (int i = tid; i < g * half; i += AD_THREADS) {
+    // row t's g query heads roped at its position (bf16 rows 0..g-1 of qb; rows
+    // g..15 zero): the half angles once, then every head (the same arithmetic
+    // as rope_pair)
+    for (int p = tid; p < half; p += AD_THREADS) {
+      const float inv_freq = exp2f(-((float)p / (float)half) * log2_theta);
+      float sn, cs;
+      sincosf((float)pos * inv_freq, &sn, &cs);
+      rot[p] = make_float2(cs, sn);
+    }
+    __syncthreads();
+    for (int i = tid; i < 16 * half; i += AD_THREADS) {
       const int j = i / half, p = i % half;
-      uint16_t r0, r1;
-      rope_pair(row_t + (size_t)(kh * g + j) * d, p, half, pos, log2_theta, r0, r1);
-      qs[j * d + p] = bf2f(r0);
-      qs[j * d + p + half] = bf2f(r1);
+      uint16_t r0 = 0, r1 = 0;
+      if (j < g) {
+        const uint16_t* x = row_t + (size_t)(kh * g + j) * d;
+        const float2 cssn = rot[p];
+        const float a = bf2f(x[p]), c2 = bf2f(x[p + half]);
+        r0 = f2bf(a * cssn.x - c2 * cssn.y);
+        r1 = f2bf(a * cssn.y + c2 * cssn.x);
+      }
+      qb[j * kld + p] = r0;
+      qb[j * kld + p + half] = r1;
     }
     cp_async_wait_all();
     __syncthreads();
-    // scores: thread (key, head parity hs): heads hs, hs + 2, ...
-    const int key = tid % AD_CH, hs = tid / AD_CH;
-    constexpr int HPT = ATT_MAXG / 2;
-    float sc[HPT];
+    // ---- S = Q K^T for the warp's 16 keys (two n8 tiles), fp32 ----
+    const int r = lane >> 2, c = lane & 3;
+    const int kb = warp * 16;  // the warp's first key in the chunk
+    float sc[2][4];
 #pragma unroll
-    for (int jj = 0; jj < HPT; ++jj) sc[jj] = 0.0f;
-    const bool kl = key < nkeys;
-    if (kl) {
-      const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)key * kld);
-      for (int v = 0; v < vpr; ++v) {
-        const uint4 kv = kr[v];
-        const uint32_t u[4] = {kv.x, kv.y, kv.z, kv.w};
+    for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+    for (int k0e = 0; k0e < d; k0e += 16) {
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(qb + r * kld + k0e + 2 * c);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(qb + (r + 8) * kld + k0e + 2 * c);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(qb + r * kld + k0e + 8 + 2 * c);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(qb + (r + 8) * kld + k0e + 8 + 2 * c);
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const float a = bf2f((uint16_t)(u[m] & 0xFFFF)), c = bf2f((uint16_t)(u[m] >> 16));
-          const int e = v * 8 + 2 * m;
-#pragma unroll
-          for (int jj = 0; jj < HPT; ++jj) {
-            const int j = hs + 2 * jj;
-            if (j < g) sc[jj] = fmaf(c, qs[j * d + e + 1], fmaf(a, qs[j * d + e], sc[jj]));
-          }
-        }
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint16_t* krow = ks + (size_t)(kb + nt * 8 + r) * kld + k0e + 2 * c;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 8);
+        mma_bf16_16816(sc[nt], a0, a1, a2, a3, b0, b1);
       }
     }
+    // lane: head rows r (d0, d1) and r + 8 (d2, d3), keys kb + 8 nt + 2 c, + 1
+    float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-    for (int jj = 0; jj < HPT; ++jj) sc[jj] = kl ? sc[jj] * scale_log2 : -INFINITY;
-    // per head: chunk max (the two warps of a head parity), then 2^(s - max) and its sum
-    const int hw = warp & 1;  // warp within the head parity
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-    for (int jj = 0; jj < HPT; ++jj) {
-      const int j = hs + 2 * jj;
-      if (j < g) {
-        float m = sc[jj];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        if (lane == 0) red[j][hw] = m;
+      for (int q = 0; q < 4; ++q) {
+        const int key = kb + nt * 8 + 2 * c + (q & 1);
+        sc[nt][q] = key < nkeys ? sc[nt][q] * scale_log2 : -INFINITY;
+        if (q < 2) mx0 = fmaxf(mx0, sc[nt][q]);
+        else mx1 = fmaxf(mx1, sc[nt][q]);
       }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    if (c == 0) {
+      red[warp][r] = mx0;
+      red[warp][r + 8] = mx1;
     }
     __syncthreads();
-    if (tid < g) stat[tid] = fmaxf(red[tid][0], red[tid][1]);
+    if (tid < 16) {
+      float m = red[0][tid];
+#pragma unroll
+      for (int w = 1; w < AD_THREADS / 32; ++w) m = fmaxf(m, red[w][tid]);
+      stat[tid] = m;  // finite: every chunk with keys has a valid key in some warp
+    }
     __syncthreads();
+    const float M0 = stat[r], M1 = stat[r + 8];
+    float l0 = 0.0f, l1 = 0.0f;
+    uint32_t pa[4];  // P as the A operand of the warp's one k16 step
 #pragma unroll
-    for (int jj = 0; jj < HPT; ++jj) {
-      const int j = hs + 2 * jj;
-      if (j < g) {
-        const float pj = kl ? exp2f(sc[jj] - stat[j]) : 0.0f;
-        ps[j * AD_CH + key] = pj;
-        float l = pj;
+    for (int nt = 0; nt < 2; ++nt) {
+      const float p0 = exp2f(sc[nt][0] - M0), p1 = exp2f(sc[nt][1] - M0);
+      const float p2 = exp2f(sc[nt][2] - M1), p3 = exp2f(sc[nt][3] - M1);
+      l0 += p0 + p1;
+      l1 += p2 + p3;
+      pa[2 * nt] = pack_bf16(p0, p1);      // row r, keys 8 nt + 2 c, + 1
+      pa[2 * nt + 1] = pack_bf16(p2, p3);  // row r + 8
+    }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-        if (lane == 0) red[j][hw] = l;
+    for (int off = 1; off <= 2; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    __syncthreads();  // every warp has read stat from red's maxima
+    if (c == 0) {
+      red[warp][r] = l0;
+      red[warp][r + 8] = l1;
+    }
+    // ---- O += P V over the warp's 16 keys: 8-column tiles of d, two per ldmatrix ----
+    // A fragment order: a0 row r keys 0-7, a1 row r + 8 keys 0-7, a2 row r keys 8-15, a3 row r + 8 keys 8-15
+    const uint32_t A0 = pa[0], A1 = pa[1], A2 = pa[2], A3 = pa[3];
+    const int mi = lane >> 3, mr = lane & 7;  // the ldmatrix row this lane addresses
+    for (int e0 = 0; e0 < d; e0 += 16) {
+      // matrices: keys 0-7 / 8-15 of the warp x columns e0..e0+7 / e0+8..e0+15
+      uint32_t v[4];
+      ldsm_x4_trans(v, vs + (size_t)(kb + (mi & 1) * 8 + mr) * kld + e0 + (mi >> 1) * 8);
+      float o0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, o1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      mma_bf16_16816(o0, A0, A1, A2, A3, v[0], v[1]);
+      mma_bf16_16816(o1, A0, A1, A2, A3, v[2], v[3]);
+      // rows r (o[0], o[1]) and r + 8 (o[2], o[3]), columns e + 2 c, + 1
+      float* ow = ob + (size_t)warp * g * d;
+      if (r < g) {
+        *reinterpret_cast<float2*>(ow + r * d + e0 + 2 * c) = make_float2(o0[0], o0[1]);
+        *reinterpret_cast<float2*>(ow + r * d + e0 + 8 + 2 * c) = make_float2(o1[0], o1[1]);
+      }
+      if (r + 8 < g) {
+        *reinterpret_cast<float2*>(ow + (r + 8) * d + e0 + 2 * c) = make_float2(o0[2], o0[3]);
+        *reinterpret_cast<float2*>(ow + (r + 8) * d + e0 + 8 + 2 * c) = make_float2(o1[2], o1[3]);
       }
     }
     __syncthreads();
     if (tid < g) {
+      float l = 0.0f;
+#pragma unroll
+      for (int w = 0; w < AD_THREADS / 32; ++w) l += red[w][tid];
       pm[tid] = stat[tid];
-      pm[g + tid] = red[tid][0] + red[tid][1];
+      pm[g + tid] = l;
     }
-    // weighted values: thread = dimension
-    for (int e = tid; e < d; e += AD_THREADS) {
-      float acc[ATT_MAXG];
+    const int n4 = g * d / 4;
+    for (int i = tid; i < n4; i += AD_THREADS) {
+      float4 a = reinterpret_cast<const float4*>(ob)[i];
 #pragma unroll
-      for (int j = 0; j < ATT_MAXG; ++j) acc[j] = 0.0f;
-#pragma unroll 4
-      for (int k2 = 0; k2 < nkeys; ++k2) {
-        const float vv = bf2f(vs[(size_t)k2 * d + e]);
-#pragma unroll
-        for (int j = 0; j < ATT_MAXG; ++j)
-          if (j < g) acc[j] = fmaf(ps[j * AD_CH + k2], vv, acc[j]);
+      for (int w = 1; w < AD_THREADS / 32; ++w) {
+        const float4 b = reinterpret_cast<const float4*>(ob)[(size_t)w * n4 + i];
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
       }
-#pragma unroll
-      for (int j = 0; j < ATT_MAXG; ++j)
-        if (j < g) pout[(size_t)j * d + e] = acc[j];
+      reinterpret_cast<float4*>(pout)[i] = a;
     }
   }
   // the last CTA of (t, kh) merges the chunks holding keys (each thread's
@@ -649,7 +725,7 @@ __global__ void __launch_bounds__(AD_THREADS)
   // loads in flight together
   const int nc = pos / AD_CH + 1;  // chunks with keys
   const float* base = part + ((size_t)t * nk + kh) * n_chunks * (size_t)stride;
-  float* cm = ps + (size_t)g * AD_CH;  // [g][nc] maxima, [g][nc] sums, [g][nc] weights
+  float* cm = ob + (size_t)(AD_THREADS / 32) * g * d;  // [g][nc] maxima, [g][nc] sums, [g][nc] weights
   float* cl = cm + (size_t)g * n_chunks;
   float* cw = cl + (size_t)g * n_chunks;
   for (int i = tid; i < g * nc; i += AD_THREADS) {
@@ -667,32 +743,45 @@ __global__ void __launch_bounds__(AD_THREADS)
     for (int c = 0; c < nc; ++c) cw[tid * nc + c] = exp2f(cm[tid * nc + c] - M) * invL;
   }
   __syncthreads();
-  constexpr int MB = 8;  // chunks whose loads are in flight together
+  // each thread's columns q and q + 128 (g * d / 4 <= 2 * AD_THREADS when
+  // g * d <= 1024; more columns loop) with the loads of MB chunks of both in
+  // flight together
+  constexpr int MB = 8;
   const int ncol = g * d / 4;
-  for (int q = tid; q < ncol; q += AD_THREADS) {
-    const int j = 4 * q / d;
-    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int q0 = tid; q0 < ncol; q0 += 2 * AD_THREADS) {
+    const int q1 = q0 + AD_THREADS;
+    const bool has1 = q1 < ncol;
+    const int j0 = 4 * q0 / d, j1 = has1 ? 4 * q1 / d : j0;
+    float4 a0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), a1 = a0;
     for (int c0 = 0; c0 < nc; c0 += MB) {
-      float4 v[MB];
-#pragma unroll
-      for (int u = 0; u < MB; ++u)
-        v[u] = c0 + u < nc ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)(c0 + u) * stride) + q)
-                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      float4 v0[MB], v1[MB];
 #pragma unroll
       for (int u = 0; u < MB; ++u) {
-        const float wgt = c0 + u < nc ? cw[j * nc + c0 + u] : 0.0f;
-        a.x = fmaf(wgt, v[u].x, a.x);
-        a.y = fmaf(wgt, v[u].y, a.y);
-        a.z = fmaf(wgt, v[u].z, a.z);
-        a.w = fmaf(wgt, v[u].w, a.w);
+        const bool in = c0 + u < nc;
+        const float4* src = reinterpret_cast<const float4*>(base + (size_t)(c0 + u) * stride);
+        v0[u] = in ? __ldcg(src + q0) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        v1[u] = in && has1 ? __ldcg(src + q1) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < MB; ++u) {
+        const bool in = c0 + u < nc;
+        const float w0 = in ? cw[j0 * nc + c0 + u] : 0.0f, w1 = in ? cw[j1 * nc + c0 + u] : 0.0f;
+        a0.x = fmaf(w0, v0[u].x, a0.x);
+        a0.y = fmaf(w0, v0[u].y, a0.y);
+        a0.z = fmaf(w0, v0[u].z, a0.z);
+        a0.w = fmaf(w0, v0[u].w, a0.w);
+        a1.x = fmaf(w1, v1[u].x, a1.x);
+        a1.y = fmaf(w1, v1[u].y, a1.y);
+        a1.z = fmaf(w1, v1[u].z, a1.z);
+        a1.w = fmaf(w1, v1[u].w, a1.w);
       }
     }
-    const int e = 4 * q - j * d;
-    uint16_t* o = out + (size_t)t * nq * d + (size_t)(kh * g + j) * d + e;
-    o[0] = f2bf(a.x);
-    o[1] = f2bf(a.y);
-    o[2] = f2bf(a.z);
-    o[3] = f2bf(a.w);
+    uint16_t* ob0 = out + (size_t)t * nq * d + (size_t)kh * g * d + 4 * q0;
+    *reinterpret_cast<uint2*>(ob0) = make_uint2(pack_bf16(a0.x, a0.y), pack_bf16(a0.z, a0.w));
+    if (has1) {
+      uint16_t* ob1 = out + (size_t)t * nq * d + (size_t)kh * g * d + 4 * q1;
+      *reinterpret_cast<uint2*>(ob1) = make_uint2(pack_bf16(a1.x, a1.y), pack_bf16(a1.z, a1.w));
+    }
   }
 }
 
@@ -840,15 +929,17 @@ int b2q_attn_decode(const uint16_t* qkv, int q_ld, const int32_t* positions, uin
                     uint16_t* out, int T, int nq, int nk, int head_dim, float theta, int window, int* status,
                     void* workspace, size_t workspace_bytes, void* stream) {
   clear_error();
-  if (T < 0 || T > AD_MAXT || nq < 1 || nk < 1 || nq % nk || nq / nk > ATT_MAXG || head_dim < 8 || head_dim % 8 ||
+  if (T < 0 || T > AD_MAXT || nq < 1 || nk < 1 || nq % nk || nq / nk > ATT_MAXG || head_dim < 16 || head_dim % 16 ||
       head_dim > ATT_MAXD || window < 1 || q_ld < (nq + 2 * nk) * head_dim || q_ld % 8 || !(theta > 1.0f))
     return set_error(B2Q_EINVAL, "attn_decode: bad shape (T=%d nq=%d nk=%d head_dim=%d window=%d)", T, nq, nk,
                      head_dim, window);
   if (T == 0) return B2Q_OK;
   if (!qkv || !positions || !k_cache || !v_cache || !out || !workspace)
     return set_error(B2Q_EINVAL, "attn_decode: null pointer");
-  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(qkv) || (reinterpret_cast<uintptr_t>(workspace) & 255))
-    return set_error(B2Q_EINVAL, "attn_decode: qkv, k_cache, v_cache 16-byte and workspace 256-byte aligned");
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(qkv) || (reinterpret_cast<uintptr_t>(out) & 7) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return set_error(B2Q_EINVAL,
+                     "attn_decode: qkv, k_cache, v_cache 16-byte, out 8-byte and workspace 256-byte aligned");
   const size_t need = b2q_attn_decode_workspace_size(T, nq, nk, head_dim, window);
   if (workspace_bytes < need) return set_error(B2Q_EINVAL, "attn_decode: workspace of %zu bytes needed", need);
   const int g = nq / nk;

@@ -326,10 +326,13 @@ def test_expert_parallel_decoder_one_rank(cuda, b2q_mod):
 @pytest.mark.parametrize("positions", [[0], [63], [64], [1279], [62, 63, 64], [5, 130, 299], [127, 128]])
 def test_attn_decode_matches_two_kernel_path(cuda, b2q_mod, positions):
     """b2q_attn_decode (one launch) = b2q_rope_kv + b2q_gqa_decode: identical
-    cache rows, outputs within rounding (the chunk sizes differ: 64 vs 128 keys),
-    and both against fp32 softmax attention; the window's own rows are read from
-    q|k|v (rows 62, 63, 64 cross a chunk boundary). Two calls in a row on one
-    workspace (its counters re-arm)."""
+    cache rows, outputs within rounding, and both against fp32 softmax
+    attention; the window's own rows are read from q|k|v (rows 62, 63, 64 cross
+    a chunk boundary). Two calls in a row on one workspace (its counters
+    re-arm). The one-launch kernel multiplies bf16 probabilities by V on the
+    tensor cores (normalised by the fp32 sum) where the two-kernel path keeps
+    them in fp32, so the two paths are held to the bound each meets against
+    fp32 attention (4e-3), not to each other's rounding."""
     import torch
 
     from b2q import synth
@@ -363,7 +366,7 @@ def test_attn_decode_matches_two_kernel_path(cuda, b2q_mod, positions):
         torch.cuda.synchronize()
         assert int(status.item()) == 0
         assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
-        assert rel_l2(_bf(_np(out)), _bf(_np(ref))) < 2e-3
+        assert rel_l2(_bf(_np(out)), _bf(_np(ref))) < 4e-3
     qf, kf, vf = x[:, :nq * hd].float().view(T, nq, hd), kc1.float(), vc1.float()
     exact = torch.empty(T, nq, hd, device="cuda")
     for t in range(T):
