@@ -785,6 +785,316 @@ __global__ void __launch_bounds__(AD_THREADS)
   }
 }
 
+// ---- the same attention as one thread-block cluster per (row, kv head) -------------
+// For head_dim 128: the AC_CL CTAs of a cluster share a kv head and row t; CTA
+// rank r takes chunks r, r + AC_CL, ... of AD_CH keys (a 3-buffer cp.async
+// ring), and each warp keeps an online softmax over its 16 keys of every chunk
+// (running max, sum and P V accumulators in registers; the same tensor-core
+// arithmetic as attn_decode_kernel). The four warps are merged in shared
+// memory, then the cluster's CTAs exchange their (max, sum, partial) through
+// distributed shared memory and each writes a slice of the output: no global
+// partials, fences or arrival counters.
+constexpr int AC_CL = 8;  // CTAs per cluster
+constexpr int AC_NB = 3;  // chunk buffers of the ring
+constexpr int AC_D = 128;
+
+__host__ __device__ inline size_t ac_smem_bytes(int g) {
+  const int kld = AC_D + 8;
+  return (size_t)AC_NB * 2 * AD_CH * kld * 2 + (size_t)16 * kld * 2 + (size_t)(AD_THREADS / 32) * g * AC_D * 4 +
+         (size_t)g * AC_D * 4;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ float ld_dsmem(uint32_t a) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(AD_THREADS)
+    attn_cluster_kernel(const uint16_t* __restrict__ qkv, int q_ld, int T, const int32_t* __restrict__ positions,
+                        int nq, int nk, float log2_theta, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
+                        int window, float scale_log2, uint16_t* __restrict__ out, int* err) {
+  constexpr int D = AC_D, KLD = D + 8, HALF = D / 2, VPR = D / 8;
+  extern __shared__ __align__(16) unsigned char acs_[];
+  uint16_t* kbuf = reinterpret_cast<uint16_t*>(acs_);      // [AC_NB][AD_CH][KLD]
+  uint16_t* vbuf = kbuf + (size_t)AC_NB * AD_CH * KLD;       // [AC_NB][AD_CH][KLD]
+  uint16_t* qb = vbuf + (size_t)AC_NB * AD_CH * KLD;         // [16][KLD]
+  float* wo = reinterpret_cast<float*>(qb + (size_t)16 * KLD);  // [warp][g][D] warp partials
+  const int g = nq / nk;
+  float* co = wo + (size_t)(AD_THREADS / 32) * g * D;          // [g][D] the CTA's partial
+  __shared__ float wm[AD_THREADS / 32][16], wl[AD_THREADS / 32][16];
+  __shared__ float cm[16], cl[16];
+  __shared__ float2 rot[HALF];
+  __shared__ int wpos[AD_MAXT];
+  const uint32_t rank = cluster_rank();
+  const int kh = blockIdx.y, t = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_enter();
+  if (tid < T) wpos[tid] = positions[tid];
+  __syncthreads();
+  int pos = wpos[t];
+  const bool bad = pos < 0 || pos >= window;
+  if (bad) {  // outside the cache window: recorded, attends row 0 only, appends nothing
+    if (kh == 0 && rank == 0 && tid == 0) record_error(err, B2Q_EINVAL);
+    pos = 0;
+  }
+  const uint16_t* row_t = qkv + (size_t)t * q_ld;
+  auto window_row = [&](int j) {
+    int w = -1;
+    for (int u = 0; u < T; ++u)
+      if (wpos[u] == j) w = u;
+    return w;
+  };
+  // row t's k / v of head kh into the cache, by the CTA whose chunks hold its position
+  if (!bad && (pos / AD_CH) % AC_CL == (int)rank) {
+    const uint16_t* krow = row_t + (size_t)(nq + kh) * D;
+    const uint16_t* vrow = row_t + (size_t)(nq + nk + kh) * D;
+    uint16_t* kdst = kc + ((size_t)pos * nk + kh) * D;
+    uint16_t* vdst = vc + ((size_t)pos * nk + kh) * D;
+    for (int p = tid; p < HALF; p += AD_THREADS) {
+      uint16_t r0, r1;
+      rope_pair(krow, p, HALF, pos, log2_theta, r0, r1);
+      kdst[p] = r0;
+      kdst[p + HALF] = r1;
+      vdst[p] = vrow[p];
+      vdst[p + HALF] = vrow[p + HALF];
+    }
+  }
+  const int nc = pos / AD_CH + 1;  // chunks with keys
+  const int mc = (int)rank < nc ? (nc - 1 - (int)rank) / AC_CL + 1 : 0;  // this CTA's chunks
+  // stage chunk i of this CTA into buffer b: cache keys by cp.async, the
+  // window's own keys from q|k|v (roped), rows past the position zeroed
+  auto issue = [&](int i, int b) {
+    const int k0 = ((int)rank + i * AC_CL) * AD_CH;
+    const int nkeys = min(AD_CH, pos + 1 - k0);
+    uint16_t* ks = kbuf + (size_t)b * AD_CH * KLD;
+    uint16_t* vs = vbuf + (size_t)b * AD_CH * KLD;
+    for (int q = tid; q < AD_CH * VPR; q += AD_THREADS) {
+      const int key = q / VPR, c = q % VPR;
+      uint16_t* kd = ks + (size_t)key * KLD + c * 8;
+      uint16_t* vd = vs + (size_t)key * KLD + c * 8;
+      if (key >= nkeys) {
+        *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
+      if (window_row(k0 + key) >= 0) continue;
+      const size_t src = ((size_t)(k0 + key) * nk + kh) * D + (size_t)c * 8;
+      cp_async16(kd, kc + src);
+      cp_async16(vd, vc + src);
+    }
+    for (int u = 0; u < T; ++u) {
+      const int j = wpos[u];
+      if (j < k0 || j >= k0 + nkeys || window_row(j) != u) continue;
+      const uint16_t* urow = qkv + (size_t)u * q_ld;
+      const uint16_t* krow = urow + (size_t)(nq + kh) * D;
+      const uint16_t* vrow = urow + (size_t)(nq + nk + kh) * D;
+      for (int p = tid; p < HALF; p += AD_THREADS) {
+        uint16_t r0, r1;
+        rope_pair(krow, p, HALF, j, log2_theta, r0, r1);
+        ks[(size_t)(j - k0) * KLD + p] = r0;
+        ks[(size_t)(j - k0) * KLD + p + HALF] = r1;
+        vs[(size_t)(j - k0) * KLD + p] = vrow[p];
+        vs[(size_t)(j - k0) * KLD + p + HALF] = vrow[p + HALF];
+      }
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < AC_NB - 1; ++i) {
+    if (i < mc) issue(i, i);
+    cp_async_commit();
+  }
+  // q rows roped at row t's position: the angles once, then every head
+  for (int p = tid; p < HALF; p += AD_THREADS) {
+    const float inv_freq = exp2f(-((float)p / (float)HALF) * log2_theta);
+    float sn, cs;
+    sincosf((float)pos * inv_freq, &sn, &cs);
+    rot[p] = make_float2(cs, sn);
+  }
+  __syncthreads();
+  for (int q = tid; q < 16 * HALF; q += AD_THREADS) {
+    const int j = q / HALF, p = q % HALF;
+    uint16_t r0 = 0, r1 = 0;
+    if (j < g) {
+      const uint16_t* x = row_t + (size_t)(kh * g + j) * D;
+      const float2 cssn = rot[p];
+      const float a = bf2f(x[p]), c2 = bf2f(x[p + HALF]);
+      r0 = f2bf(a * cssn.x - c2 * cssn.y);
+      r1 = f2bf(a * cssn.y + c2 * cssn.x);
+    }
+    qb[j * KLD + p] = r0;
+    qb[j * KLD + p + HALF] = r1;
+  }
+  // ---- online softmax over this CTA's chunks; warp w: keys [16 w, 16 w + 16) ----
+  const int r = lane >> 2, c = lane & 3;
+  const int kb = warp * 16;
+  const int mi = lane >> 3, mr = lane & 7;  // the ldmatrix row this lane addresses
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // rows r, r + 8
+  float o[D / 8][4];  // n8 tiles of d: rows r (0, 1) and r + 8 (2, 3), columns 8 nt + 2 c, + 1
+#pragma unroll
+  for (int nt = 0; nt < D / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
+  for (int i = 0; i < mc; ++i) {
+    if (i + AC_NB - 1 < mc) issue(i + AC_NB - 1, (i + AC_NB - 1) % AC_NB);
+    cp_async_commit();
+    cp_async_wait_group<AC_NB - 1>();
+    __syncthreads();
+    const int b = i % AC_NB;
+    const int k0 = ((int)rank + i * AC_CL) * AD_CH;
+    const int nkeys = min(AD_CH, pos + 1 - k0);
+    const uint16_t* ks = kbuf + (size_t)b * AD_CH * KLD;
+    const uint16_t* vs = vbuf + (size_t)b * AD_CH * KLD;
+    if (kb < nkeys) {  // warp-uniform: a warp whose keys are all past the position adds nothing
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+      for (int k0e = 0; k0e < D; k0e += 16) {
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(qb + r * KLD + k0e + 2 * c);
+        const uint32_t a1 = *reinterpret_cast<const uint32_t*>(qb + (r + 8) * KLD + k0e + 2 * c);
+        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(qb + r * KLD + k0e + 8 + 2 * c);
+        const uint32_t a3 = *reinterpret_cast<const uint32_t*>(qb + (r + 8) * KLD + k0e + 8 + 2 * c);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const uint16_t* krow = ks + (size_t)(kb + nt * 8 + r) * KLD + k0e + 2 * c;
+          mma_bf16_16816(sc[nt], a0, a1, a2, a3, *reinterpret_cast<const uint32_t*>(krow),
+                         *reinterpret_cast<const uint32_t*>(krow + 8));
+        }
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int key = kb + nt * 8 + 2 * c + (q & 1);
+          sc[nt][q] = key < nkeys ? sc[nt][q] * scale_log2 : -INFINITY;
+          if (q < 2) mx0 = fmaxf(mx0, sc[nt][q]);
+          else mx1 = fmaxf(mx1, sc[nt][q]);
+        }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      // key kb (the warp's first) is valid, so the new maxima are finite
+      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+      const float s0 = exp2f(m0 - n0), s1 = exp2f(m1 - n1);  // 0 on the first chunk (m = -inf)
+      m0 = n0;
+      m1 = n1;
+      uint32_t pa[4];
+      float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const float p0 = exp2f(sc[nt][0] - n0), p1 = exp2f(sc[nt][1] - n0);
+        const float p2 = exp2f(sc[nt][2] - n1), p3 = exp2f(sc[nt][3] - n1);
+        ps0 += p0 + p1;
+        ps1 += p2 + p3;
+        pa[2 * nt] = pack_bf16(p0, p1);
+        pa[2 * nt + 1] = pack_bf16(p2, p3);
+      }
+      l0 = l0 * s0 + ps0;  // lane partial (the quad's sum is taken at the end)
+      l1 = l1 * s1 + ps1;
+#pragma unroll
+      for (int nt = 0; nt < D / 8; ++nt) {
+        o[nt][0] *= s0;
+        o[nt][1] *= s0;
+        o[nt][2] *= s1;
+        o[nt][3] *= s1;
+      }
+#pragma unroll
+      for (int e0 = 0; e0 < D; e0 += 16) {
+        uint32_t v[4];
+        ldsm_x4_trans(v, vs + (size_t)(kb + (mi & 1) * 8 + mr) * KLD + e0 + (mi >> 1) * 8);
+        mma_bf16_16816(o[e0 / 8], pa[0], pa[1], pa[2], pa[3], v[0], v[1]);
+        mma_bf16_16816(o[e0 / 8 + 1], pa[0], pa[1], pa[2], pa[3], v[2], v[3]);
+      }
+    }
+    __syncthreads();  // buffer b is refilled by the next iteration's issue
+  }
+  cp_async_wait_group<0>();
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  // ---- the four warps into the CTA's partial ----
+  if (c == 0) {
+    wm[warp][r] = m0;
+    wm[warp][r + 8] = m1;
+    wl[warp][r] = l0;
+    wl[warp][r + 8] = l1;
+  }
+  {
+    float* ow = wo + (size_t)warp * g * D;
+#pragma unroll
+    for (int nt = 0; nt < D / 8; ++nt) {
+      if (r < g) *reinterpret_cast<float2*>(ow + r * D + nt * 8 + 2 * c) = make_float2(o[nt][0], o[nt][1]);
+      if (r + 8 < g) *reinterpret_cast<float2*>(ow + (r + 8) * D + nt * 8 + 2 * c) = make_float2(o[nt][2], o[nt][3]);
+    }
+  }
+  __syncthreads();
+  if (tid < g) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < AD_THREADS / 32; ++w) M = fmaxf(M, wm[w][tid]);
+    float L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < AD_THREADS / 32; ++w) {
+      const float a = M == -INFINITY ? 0.0f : exp2f(wm[w][tid] - M);
+      wm[w][tid] = a;  // the warp's weight in the CTA's partial
+      L += a * wl[w][tid];
+    }
+    cm[tid] = M;
+    cl[tid] = L;
+  }
+  __syncthreads();
+  for (int q = tid; q < g * D; q += AD_THREADS) {
+    const int j = q / D;
+    float a = 0.0f;
+#pragma unroll
+    for (int w = 0; w < AD_THREADS / 32; ++w) a = fmaf(wm[w][j], wo[(size_t)w * g * D + q], a);
+    co[q] = a;
+  }
+  // ---- the cluster's CTAs through distributed shared memory ----
+  cluster_sync_all();
+  const int per = (g * D + AC_CL - 1) / AC_CL;
+  for (int q = (int)rank * per + tid; q < min(g * D, ((int)rank + 1) * per); q += AD_THREADS) {
+    const int j = q / D;
+    float M = -INFINITY, mv[AC_CL];
+#pragma unroll
+    for (int cr = 0; cr < AC_CL; ++cr) {
+      mv[cr] = ld_dsmem(dsmem_addr(&cm[j], cr));
+      M = fmaxf(M, mv[cr]);  // finite: rank 0 holds chunk 0, whose first key is valid
+    }
+    float L = 0.0f, a = 0.0f;
+#pragma unroll
+    for (int cr = 0; cr < AC_CL; ++cr) {
+      const float w = exp2f(mv[cr] - M);
+      L = fmaf(w, ld_dsmem(dsmem_addr(&cl[j], cr)), L);
+      a = fmaf(w, ld_dsmem(dsmem_addr(co + q, cr)), a);
+    }
+    out[(size_t)t * nq * D + (size_t)kh * g * D + q] = f2bf(a / L);
+  }
+  cluster_sync_all();  // every CTA's shared memory stays until the cluster has read it
+}
+
 }  // namespace dec
 }  // namespace b2q
 
@@ -946,6 +1256,39 @@ int b2q_attn_decode(const uint16_t* qkv, int q_ld, const int32_t* positions, uin
   const int chunks = (window + AD_CH - 1) / AD_CH;
   if (chunks > 65535) return set_error(B2Q_EINVAL, "attn_decode: window %d", window);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == AC_D) {
+    // one cluster of AC_CL CTAs per (row, kv head), merged in distributed shared memory
+    const size_t smem = ac_smem_bytes(g);
+    static bool attr_set[64] = {};
+    DeviceInfo di;
+    int rc = device_info(&di);
+    if (rc) return rc;
+    if (smem + 2048 > (size_t)di.smem_optin)
+      return set_error(B2Q_EUNSUPPORTED, "attn_decode: %zu bytes of shared memory", smem);
+    if (!attr_set[di.device & 63]) {  // the largest g's need, once per device
+      B2Q_TRY_CUDA(cudaFuncSetAttribute(attn_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)ac_smem_bytes(ATT_MAXG)));
+      attr_set[di.device & 63] = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(AC_CL, nk, T);
+    cfg.blockDim = dim3(AD_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = AC_CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const float scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+    B2Q_TRY_CUDA(cudaLaunchKernelEx(&cfg, attn_cluster_kernel, qkv, q_ld, T, positions, nq, nk, log2f(theta), k_cache,
+                                    v_cache, window, scale_log2, out, status));
+    return B2Q_OK;
+  }
   // counters first (at the same place whatever T), then the chunk partials
   unsigned* cnt = static_cast<unsigned*>(workspace);
   float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((size_t)AD_MAXT * nk * 4 + 255) / 256 * 256);
