@@ -392,6 +392,26 @@ B2Q_API int b2q_gqa_decode(const uint16_t* q, int q_ld, const uint16_t* k_cache,
  *   counters at zero. Calls sharing a workspace must be ordered on one stream.
  *   B2Q_EUNSUPPORTED when the window's merge buffers exceed shared memory
  *   (past ~125k positions at 8 query heads per kv head). */
+/* b2q_qmv_norm / b2q_moe_decode_norm: b2q_add_rms_norm fused into the
+ *   one-token product that consumes its output (the q|k|v product and the MoE
+ *   layer of a decode step): every CTA of the single-column kernel computes
+ *   x = rms_norm(bf16(h + delta)) * norm_weight itself during its pass over x
+ *   (one launch instead of two; the block sum of squares is taken in another
+ *   order than b2q_add_rms_norm's, so x can differ from it in the last bit),
+ *   and CTA 0 writes h_out = bf16(h + delta) (delta NULL: x = rms_norm(h) and
+ *   h_out is not written). h_out must not alias h or delta. The rest as
+ *   b2q_qmm (M = 1) / b2q_moe_decode (S = 1). B2Q_EUNSUPPORTED outside the
+ *   single-column kernel's shapes (H or K at most 4864): the caller then uses
+ *   b2q_add_rms_norm and the plain call. */
+B2Q_API int b2q_qmv_norm(const uint16_t* h, const uint16_t* delta, const uint16_t* norm_weight, float eps,
+                   uint16_t* h_out, const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                   uint16_t* y, int N, int K, int group_size, int bits, void* stream);
+B2Q_API int b2q_moe_decode_norm(const uint16_t* h, const uint16_t* delta, const uint16_t* norm_weight, float eps,
+                   uint16_t* h_out, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg,
+                   const uint16_t* bg, const uint32_t* wu, const uint16_t* su, const uint16_t* bu,
+                   const uint32_t* wd, const uint16_t* sd, const uint16_t* bd, uint16_t* out,
+                   uint32_t* idx, float* w, float* logits, int H, int E, int F, int k, int group_size,
+                   int bits, void* workspace, size_t workspace_bytes, void* stream);
 B2Q_API size_t b2q_attn_decode_workspace_size(int T, int nq, int nk, int head_dim, int window);
 B2Q_API int b2q_attn_decode(const uint16_t* qkv, int q_ld, const int32_t* positions, uint16_t* k_cache,
                    uint16_t* v_cache, uint16_t* out, int T, int nq, int nk, int head_dim, float theta,

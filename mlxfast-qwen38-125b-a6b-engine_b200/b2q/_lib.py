@@ -76,6 +76,8 @@ SIGNATURES = {
     "b2q_rope_kv": (_I, [_P, _I, _I, _I, _I, _P, ctypes.c_float, _P, _P, _I, _P, _P]),
     "b2q_gqa_decode_workspace_size": (_SZ, [_I] * 5),
     "b2q_gqa_decode": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "b2q_qmv_norm": (_I, [_P, _P, _P, ctypes.c_float] + [_P] * 5 + [_I] * 4 + [_P]),
+    "b2q_moe_decode_norm": (_I, [_P, _P, _P, ctypes.c_float] + [_P] * 15 + [_I] * 6 + [_P, _SZ, _P]),
     "b2q_attn_decode_workspace_size": (_SZ, [_I] * 5),
     "b2q_attn_decode": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _SZ, _P]),
     "b2q_st_open": (_I, [ctypes.c_char_p, _P]),

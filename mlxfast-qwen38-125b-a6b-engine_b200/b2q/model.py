@@ -127,6 +127,35 @@ class Block:
         self.k_cache = torch.zeros((cfg.max_seq, cfg.n_kv_heads, hd), dtype=torch.bfloat16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.status, self.attn_ws = status, attn_ws
+        # one-token steps with the norms fused into the products (the plain MoE;
+        # the expert-parallel layer keeps the separate norm)
+        self._fused_norm = ep is None
+
+    def _decode_one(self, h: torch.Tensor, delta, positions):
+        """One token: norm + q|k|v in one launch, attention, o, norm + MoE in one
+        launch. None when a fused call is outside its kernel (the separate path
+        is taken and this block stops trying)."""
+        cfg = self.cfg
+        st = ops._stream(h.device)
+        q = self.qkv
+        h2 = torch.empty_like(h) if delta is not None else h
+        qkv = torch.empty((1, cfg.qkv_rows), dtype=torch.bfloat16, device=h.device)
+        rc = lib().b2q_qmv_norm(h.data_ptr(), None if delta is None else delta.data_ptr(), self.attn_norm.data_ptr(),
+                                cfg.rms_eps, None if delta is None else h2.data_ptr(), q.weight.data_ptr(),
+                                q.scales.data_ptr(), q.biases.data_ptr(), qkv.data_ptr(), cfg.qkv_rows, cfg.hidden,
+                                q.group_size, q.bits, st)
+        if rc == -2:  # B2Q_EUNSUPPORTED
+            self._fused_norm = False
+            return None
+        check(rc)
+        o = self.o(self._attend(qkv, positions))
+        h3 = torch.empty_like(h)
+        out = self.moe.decode_norm(h2, o, self.mlp_norm, cfg.rms_eps, h3)
+        if out is None:
+            self._fused_norm = False
+            m = add_rms_norm(h2, o, self.mlp_norm, cfg.rms_eps)
+            return h2, self.moe(m)
+        return h3, out
 
     def attention(self, a: torch.Tensor, positions: torch.Tensor, pos0: int | None = None) -> torch.Tensor:
         """a [T, H] normed -> attention output [T, n_heads * hd] (bf16).
@@ -136,10 +165,14 @@ class Block:
         (rope, KV append and attention in one launch), which reads the positions
         on the device (graph-safe); longer windows
         (prefill) use the framework's causal attention from row pos0 on."""
+        return self._attend(self.qkv(a), positions, pos0)
+
+    def _attend(self, qkv: torch.Tensor, positions: torch.Tensor, pos0: int | None = None) -> torch.Tensor:
+        """The attention of `attention` from the fused q|k|v rows [T, (nq + 2 nk) hd]."""
         cfg = self.cfg
-        T = a.shape[0]
+        T = qkv.shape[0]
         nq, nk, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
-        qkv = self.qkv(a)  # [T, (nq + 2 nk) hd]
+        a = qkv
         st = ops._stream(a.device)
         if T <= 8:
             # rope, KV append, attention and the chunk merge in one launch
@@ -168,8 +201,15 @@ class Block:
         return o.squeeze(0).permute(1, 0, 2).reshape(T, nq * hd).contiguous()
 
     def __call__(self, h: torch.Tensor, delta, positions, pos0=None):
-        """(h, delta) -> (h + delta + attention, MoE output): h is updated in place."""
+        """(h, delta) -> (h + delta + attention, MoE output). Windows of several
+        rows update h in place; one-token steps return a new residual tensor
+        (the norms are fused into the q|k|v product and the MoE kernel, whose
+        CTAs all read h while one of them writes the sum)."""
         cfg = self.cfg
+        if h.shape[0] == 1 and self._fused_norm:
+            r = self._decode_one(h, delta, positions)
+            if r is not None:
+                return r
         a = add_rms_norm(h, delta, self.attn_norm, cfg.rms_eps)
         o = self.o(self.attention(a, positions, pos0))
         m = add_rms_norm(h, o, self.mlp_norm, cfg.rms_eps)

@@ -139,6 +139,28 @@ class MoE:
                                            self._ws1.buf.numel(), ops._stream(x2.device)))
         return out
 
+    def decode_norm(self, h: torch.Tensor, delta, norm_weight: torch.Tensor, eps: float, h_out,
+                    out: torch.Tensor | None = None):
+        """One token with the residual add + RMSNorm of its input fused into the
+        decode kernel: h_out = h + delta (skipped when delta is None), the layer
+        applied to rms_norm(h_out) * norm_weight. Returns the layer output, or
+        None when the shape is outside the fused kernel (the caller then takes
+        the separate norm and the plain call)."""
+        if self._ws1 is None or self._ws1.buf.device != h.device:
+            size = ops.lib().b2q_moe_decode_workspace_size(1, self._H, self._E, self._F, self.top_k)
+            self._ws1 = ops.Workspace(size, h.device)
+        if out is None:
+            out = torch.empty((1, self._H), dtype=torch.bfloat16, device=h.device)
+        rc = ops.lib().b2q_moe_decode_norm(h.data_ptr(), None if delta is None else delta.data_ptr(),
+                                           norm_weight.data_ptr(), eps, None if h_out is None else h_out.data_ptr(),
+                                           *self._wptrs, out.data_ptr(), None, None, None, self._H, self._E, self._F,
+                                           self.top_k, self.group_size, self.bits, self._ws1.ptr(),
+                                           self._ws1.buf.numel(), ops._stream(h.device))
+        if rc == -2:  # B2Q_EUNSUPPORTED
+            return None
+        ops.check(rc)
+        return out
+
     def __call__(self, x: torch.Tensor, return_routing: bool = False, out: torch.Tensor | None = None):
         """``out`` (one-token calls only): a persistent output buffer the call writes."""
         x2 = x.contiguous().view(-1, x.shape[-1])

@@ -291,6 +291,71 @@ int b2q_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, co
   return b2q_moe_down_combine(ws.act, wd, sd, bd, ix, ww, out, S, H, E, F, k, group_size, bits, stream);
 }
 
+// ---- the residual add + RMSNorm fused into the one-token products ----------
+static int norm_args_ok(const char* fn, const uint16_t* h, const uint16_t* delta, const uint16_t* nw, float eps,
+                        const uint16_t* h_out, int K) {
+  if (!h || !nw) return set_error(B2Q_EINVAL, "%s: null pointer", fn);
+  if (delta && !h_out) return set_error(B2Q_EINVAL, "%s: h_out is needed with delta", fn);
+  if (delta && (h_out == h || h_out == delta))
+    return set_error(B2Q_EINVAL, "%s: h_out must not alias h or delta (every CTA reads them)", fn);
+  if (!(eps >= 0.0f)) return set_error(B2Q_EINVAL, "%s: eps", fn);
+  if (!aligned16(h) || !aligned16(nw) || (delta && (!aligned16(delta) || !aligned16(h_out))))
+    return set_error(B2Q_EINVAL, "%s: h, delta, h_out and the norm weight must be 16-byte aligned", fn);
+  if (!d2_norm_ok(K)) return set_error(B2Q_EUNSUPPORTED, "%s: K=%d outside the fused norm", fn, K);
+  return B2Q_OK;
+}
+
+int b2q_qmv_norm(const uint16_t* h, const uint16_t* delta, const uint16_t* norm_weight, float eps, uint16_t* h_out,
+                 const uint32_t* w, const uint16_t* scales, const uint16_t* biases, uint16_t* y, int N, int K,
+                 int group_size, int bits, void* stream) {
+  clear_error();
+  int rc = check_bits_gs("qmv_norm", bits, group_size);
+  if (rc) return rc;
+  if (N <= 0 || K <= 0 || K % group_size) return set_error(B2Q_EINVAL, "qmv_norm: bad shape");
+  rc = norm_args_ok("qmv_norm", h, delta, norm_weight, eps, h_out, K);
+  if (rc) return rc;
+  if (!w || !scales || !biases || !y) return set_error(B2Q_EINVAL, "qmv_norm: null pointer");
+  if (!aligned16(y) || !d2_qmv_eligible(N, K, group_size, h, w, scales, biases))
+    return set_error(B2Q_EUNSUPPORTED, "qmv_norm: shape outside the single-column kernel");
+  D2Norm nm;
+  nm.weight = norm_weight;
+  nm.delta = delta;
+  nm.h_out = h_out;
+  nm.eps = eps;
+  return d2_qmv(h, w, scales, biases, y, N, K, group_size, static_cast<cudaStream_t>(stream), nm);
+}
+
+int b2q_moe_decode_norm(const uint16_t* h, const uint16_t* delta, const uint16_t* norm_weight, float eps,
+                        uint16_t* h_out, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
+                        const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd,
+                        const uint16_t* sd, const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits,
+                        int H, int E, int F, int k, int group_size, int bits, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  clear_error();
+  int rc = check_bits_gs("moe_decode_norm", bits, group_size);
+  if (rc) return rc;
+  rc = norm_args_ok("moe_decode_norm", h, delta, norm_weight, eps, h_out, H);
+  if (rc) return rc;
+  if (!wr || !wg || !sg || !bg || !wu || !su || !bu || !wd || !sd || !bd || !out)
+    return set_error(B2Q_EINVAL, "moe_decode_norm: null pointer");
+  const void* ptrs[] = {wr, wg, sg, bg, wu, su, bu, wd, sd, bd};
+  bool all_aligned = true;
+  for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
+  if (!all_aligned || k < 1 || E < k || !d2_moe_eligible(H, E, F, k, group_size))
+    return set_error(B2Q_EUNSUPPORTED, "moe_decode_norm: shape outside the single-column kernel");
+  const DecodeWs ws = decode_ws_layout(workspace, 1, H, E, F, k);
+  if (!workspace || workspace_bytes < ws.bytes || !aligned16(workspace))
+    return set_error(B2Q_EINVAL, "moe_decode_norm: workspace of %zu bytes needed", ws.bytes);
+  const D2Scratch scr{&ws.hdr->error, ws.ctr, ws.logits, ws.act, ws.asc};
+  D2Norm nm;
+  nm.weight = norm_weight;
+  nm.delta = delta;
+  nm.h_out = h_out;
+  nm.eps = eps;
+  return d2_moe_decode(h, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, logits, H, E, F, k, group_size, scr,
+                       static_cast<cudaStream_t>(stream), 0, 0, nullptr, nm);
+}
+
 int b2q_workspace_status(void* workspace, size_t workspace_bytes, void* stream) {
   if (!workspace || workspace_bytes < sizeof(WsHeader)) return set_error(B2Q_EINVAL, "workspace_status: no workspace");
   cudaStream_t st = static_cast<cudaStream_t>(stream);

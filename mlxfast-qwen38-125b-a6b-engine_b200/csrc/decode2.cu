@@ -446,13 +446,62 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   // word (staged at the end of the stage ring, which the producer does not
   // fill before the block barrier after routing) ----
   uint8_t* pieces = smem + (size_t)NS * p.stage_bytes - (size_t)K1 * 2;
+  // fused residual add + RMSNorm (one chunk of 8 values per thread, checked on
+  // the host): h' = bf16(h + delta) (CTA 0 stores it), the block's sum of h'^2
+  // in warp order, then x = bf16(h' * r * w), as the separate norm kernel
+  uint4 xn = make_uint4(0u, 0u, 0u, 0u);
+  if (p.nw) {
+    const bool live = tid < K1 / 8;
+    float ss = 0.0f;
+    uint32_t u[4] = {0u, 0u, 0u, 0u};
+    if (live) {
+      const uint4 hv = __ldg(reinterpret_cast<const uint4*>(p.x) + tid);
+      u[0] = hv.x;
+      u[1] = hv.y;
+      u[2] = hv.z;
+      u[3] = hv.w;
+      if (p.ndelta) {
+        const uint4 dq = __ldg(reinterpret_cast<const uint4*>(p.ndelta) + tid);
+        const uint32_t du[4] = {dq.x, dq.y, dq.z, dq.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = lbf(u[j]) + lbf(du[j]), c = hbf(u[j]) + hbf(du[j]);
+          u[j] = (uint32_t)f2bf(a) | ((uint32_t)f2bf(c) << 16);
+        }
+        if (blockIdx.x == 0) reinterpret_cast<uint4*>(p.nh_out)[tid] = make_uint4(u[0], u[1], u[2], u[3]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = lbf(u[j]), c = hbf(u[j]);
+        ss = fmaf(a, a, ss);
+        ss = fmaf(c, c, ss);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) rsum[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < NWARP; ++w) tot += rsum[w];
+    __syncthreads();  // rsum is the router's scratch below
+    const float rr = rsqrtf(tot / (float)K1 + p.neps);
+    if (live) {
+      const uint4 g = __ldg(reinterpret_cast<const uint4*>(p.nw) + tid);
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = (uint32_t)f2bf(lbf(u[j]) * rr * lbf(gw[j])) | ((uint32_t)f2bf(hbf(u[j]) * rr * hbf(gw[j])) << 16);
+      xn = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
   {
     const int nch = K1 / 8;
     for (int q0 = 0; q0 < nch; q0 += NTH) {
       const int q = q0 + tid;
       const bool live = q < nch;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (live) v = __ldg(reinterpret_cast<const uint4*>(p.x) + q);
+      if (live) v = p.nw ? xn : __ldg(reinterpret_cast<const uint4*>(p.x) + q);
       if (FUSED && q0 == 0 && nch <= NTH) {
         // router rows e = blockIdx.x + i * grid (x word q of each)
         for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
@@ -1246,10 +1295,16 @@ bool d2_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const v
          aligned16(s) && aligned16(b);
 }
 
+bool d2_norm_ok(int K) { return K > 0 && K % 8 == 0 && K / 8 <= NTH; }
+
 int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b, uint16_t* y, int N, int K,
-           int gs, cudaStream_t st) {
+           int gs, cudaStream_t st, const D2Norm& norm) {
   D2Params p;
   std::memset(&p, 0, sizeof(p));
+  p.nw = norm.weight;
+  p.ndelta = norm.delta;
+  p.nh_out = norm.h_out;
+  p.neps = norm.eps;
   p.gs = gs;
   p.K1 = K;
   p.N = N;
@@ -1337,9 +1392,14 @@ bool d2_moe_eligible(int H, int E, int F, int k, int gs) {
 int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
-                  int k, int gs, const D2Scratch& scr, cudaStream_t st, int e_lo, int e_local, float* out_f32) {
+                  int k, int gs, const D2Scratch& scr, cudaStream_t st, int e_lo, int e_local, float* out_f32,
+                  const D2Norm& norm) {
   D2Params p;
   std::memset(&p, 0, sizeof(p));
+  p.nw = norm.weight;
+  p.ndelta = norm.delta;
+  p.nh_out = norm.h_out;
+  p.neps = norm.eps;
   p.gs = gs;
   p.K1 = H;
   p.x = x;

@@ -39,6 +39,14 @@ struct alignas(64) D2Params {
   long long timeout_ns;
   int e_lo, e_local;  // expert parallel: this rank holds experts [e_lo, e_lo + e_local) (e_local 0: all)
   float* out_f32;     // expert parallel: fp32 partial output instead of bf16 `out`
+  // residual add + RMSNorm fused into the pass over x (nw != nullptr): x is
+  // h, the call multiplies bf16(bf16(h + ndelta) * r * nw) with
+  // r = rsqrt(mean(bf16(h + ndelta)^2) + neps); CTA 0 writes bf16(h + ndelta)
+  // to nh_out (ndelta nullptr: no add, nh_out unused)
+  const uint16_t* nw;
+  const uint16_t* ndelta;
+  uint16_t* nh_out;
+  float neps;
   const uint32_t* lut;  // qmv through the metadata pair table: scale_bits | bias_bits << 16 per entry
   int lut_words;        // table entries copied into shared memory (a multiple of 4)
   int off_lut;          // shared-memory offset of the table copy
@@ -52,8 +60,17 @@ struct alignas(64) D2Params {
 };
 
 bool d2_qmv_eligible(int N, int K, int gs, const void* x, const void* w, const void* s, const void* b);
+// The residual add + RMSNorm of the product's input, fused into its pass over x.
+struct D2Norm {
+  const uint16_t* weight = nullptr;  // nullptr: x is used as given
+  const uint16_t* delta = nullptr;
+  uint16_t* h_out = nullptr;
+  float eps = 0.0f;
+};
 int d2_qmv(const uint16_t* x, const uint32_t* w, const uint16_t* s, const uint16_t* b, uint16_t* y, int N, int K,
-           int gs, cudaStream_t st);
+           int gs, cudaStream_t st, const D2Norm& norm = D2Norm());
+// the fused norm needs one 8-value chunk of the reduction per thread
+bool d2_norm_ok(int K);
 // qmv with the group metadata read through a pair table (index u16 [N, K/gs],
 // table of `count` entries, 16-byte aligned, readable up to round_up(count, 4)).
 bool d2_qmv_lut_eligible(int N, int K, int gs, int count, const void* x, const void* w, const void* index,
@@ -74,6 +91,6 @@ int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
                   int k, int gs, const D2Scratch& scr, cudaStream_t st, int e_lo = 0, int e_local = 0,
-                  float* out_f32 = nullptr);
+                  float* out_f32 = nullptr, const D2Norm& norm = D2Norm());
 
 }  // namespace b2q

@@ -377,3 +377,46 @@ def test_attn_decode_matches_two_kernel_path(cuda, b2q_mod, positions, hd):
             s = (kf[:p + 1, j // (nq // nk)] @ qf[t, j]) / hd ** 0.5
             exact[t, j] = torch.softmax(s, 0) @ vf[:p + 1, j // (nq // nk)]
     assert rel_l2(_bf(_np(out)), exact.view(T, -1).cpu().numpy()) < 4e-3
+
+
+@pytest.mark.parametrize("with_delta", [True, False])
+def test_norm_fused_products(cuda, b2q_mod, with_delta):
+    """b2q_qmv_norm / b2q_moe_decode_norm = b2q_add_rms_norm then b2q_qmm /
+    b2q_moe_decode: the residual sum bit for bit, the products within rounding
+    (the fused norm sums the squares in another order, so a normalised value
+    can differ in its last bit); two calls in a row."""
+    import torch
+
+    from b2q import synth
+    from b2q._lib import check, lib
+    from b2q.model import add_rms_norm
+
+    st = torch.cuda.current_stream().cuda_stream
+    H, N, E, F, k = 4096, 5120, 32, 1536, 8
+    h = synth.activations((1, H), seed=90) * 3
+    delta = synth.activations((1, H), seed=91) if with_delta else None
+    nw = (1.0 + 0.1 * synth.activations((H,), seed=92)).to(torch.bfloat16)
+    w, s, b = synth.packed_weights((N,), H, 64, seed=93)
+    h_ref = h.clone()
+    a = add_rms_norm(h_ref, delta, nw, 1e-6)  # h_ref += delta in place
+    y_ref = b2q_mod.quantized_matmul(a, w, s, b)
+    L = synth.moe_layer(E, H, F, 64, seed=94)
+    wr = synth.router_weight(E, H, seed=95)
+    moe = b2q_mod.MoE(wr, L, k, 64)
+    out_ref = moe(a)
+    for _ in range(2):
+        h_out = torch.full_like(h, 7.0)
+        y = torch.empty((1, N), dtype=torch.bfloat16, device="cuda")
+        check(lib().b2q_qmv_norm(h.data_ptr(), None if delta is None else delta.data_ptr(), nw.data_ptr(), 1e-6,
+                                 h_out.data_ptr() if with_delta else None, w.data_ptr(), s.data_ptr(), b.data_ptr(),
+                                 y.data_ptr(), N, H, 64, 4, st))
+        torch.cuda.synchronize()
+        if with_delta:
+            assert torch.equal(h_out, h_ref)
+        assert rel_l2(_bf(_np(y)), _bf(_np(y_ref))) < 2e-3
+        h_out2 = torch.full_like(h, 7.0)
+        out = moe.decode_norm(h, delta, nw, 1e-6, h_out2 if with_delta else None)
+        torch.cuda.synchronize()
+        if with_delta:
+            assert torch.equal(h_out2, h_ref)
+        assert rel_l2(_bf(_np(out)), _bf(_np(out_ref))) < 5e-3
