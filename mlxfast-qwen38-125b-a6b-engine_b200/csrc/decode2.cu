@@ -432,6 +432,24 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   const unsigned tag = FUSED ? __ldcg(p.ctr + D2_CTR_TAG) + 1u : 0u;
   unsigned long long* tlg = reinterpret_cast<unsigned long long*>(p.ctr + D2_CTR_LOGITS);
   __syncthreads();
+  // qmv: the weights do not depend on x, so the producer issues the copies of
+  // its first units (stages 0 .. NS - 2; the last stage holds the staged x
+  // pieces) before the pass over x, which they overlap
+  int npre = 0;
+  if (!FUSED && warp == NCW && lane == 0) {
+    const int uq = (p.N + ROWS_QMV - 1) / ROWS_QMV;
+    npre = min(NS - 1, max((uq - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x, 0));
+    const uint64_t pol = policy_evict_first();
+    for (int i = 0; i < npre; ++i) {
+      const int u = (int)blockIdx.x + i * (int)gridDim.x, row = u * ROWS_QMV;
+      uint8_t* st = smem + (size_t)i * p.stage_bytes;
+      info[i] = make_int4(U_QMV, 0, u, 0);
+      mbar_arrive_expect_tx(&full[i], (uint32_t)(ROWS_QMV * p.K1 / 2 + (LUT ? 1 : 2) * ROWS_QMV * p.mb1));
+      tma3(st, &p.map[MW], 0, row, 0, &full[i], pol);
+      tc::tma_load_2d(st + p.st_meta1, &p.map[MS], 0, row, &full[i], pol);
+      if (!LUT) tc::tma_load_2d(st + p.st_meta1 + p.st_mstep1, &p.map[MB], 0, row, &full[i], pol);
+    }
+  }
   if (LUT && warp == NCW && lane == 0) {
     // the pair table, one bulk copy; the consumers wait for it before their
     // first unit's scaling (after the pass over x)
@@ -707,6 +725,10 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
         if (++s == NS) {
           s = 0;
           eph ^= 1u;
+        }
+        if (it < npre) {  // qmv units issued before the pass over x (it < NS - 1: no reuse yet)
+          lastf[s] = (int)(eph ^ 1u);
+          continue;
         }
         if (it >= NS && !tc::wait(&empty[s], eph, deadline, abort_flag)) {
           if (!*abort_flag) record_error(p.err, B2Q_ETIMEOUT);
