@@ -646,12 +646,12 @@ def main():
         pg.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     graphs = None
-    if True:
-        # The K steps replay from CUDA graphs of G captured steps (step i reads token
-        # i mod 4096 and layer i mod 8, as in the launch loop; with expert
-        # parallelism each step's NCCL all-reduce is captured with it, every rank
-        # capturing and replaying the same steps). The launch loop is timed too and
-        # reported beside it.
+    if comm is None:
+        # One GPU: the K steps replay from CUDA graphs of G captured steps (step i reads
+        # token i mod 4096 and layer i mod 8, as in the launch loop). The launch loop is
+        # timed too and reported beside it. (With expert parallelism the steps are
+        # timed as a launch loop: a capture of the steps' NCCL calls in this leg did
+        # not complete on two GPUs.)
         ev0.record(stream)
         for i in range(args.steps):
             step(args.warmup + i)
@@ -674,8 +674,6 @@ def main():
         with torch.cuda.stream(stream):
             graphs[0].replay()  # untimed warm replay
         torch.cuda.synchronize(dev)
-        if pg:
-            pg.barrier()
     with ClockSampler(local_rank) as clk:
         torch.cuda.synchronize(dev)
         if graphs is not None:
@@ -695,7 +693,7 @@ def main():
             ev1.record(stream)
         torch.cuda.synchronize(dev)
     ms_total = ev0.elapsed_time(ev1)
-    # graphs holding NCCL calls are released before the communicator
+    graph_timed = graphs is not None
     graphs = None
     if pg:
         t = torch.tensor([ms_total], device=dev)
@@ -908,7 +906,8 @@ def main():
                    "l2": f"cold: {n_layers} rotating layers ({n_layers * E * EXPERT_BYTES / 1e9:.1f} GB experts) "
                          f"and a fresh token per step"},
         "decode_form": ("CUDA-graph replays of the captured steps, the stream kept busy while the first graph "
-                        f"is launched (launch loop: {loop_ms * 1000.0:.2f} us per step)"),
+                        f"is launched (launch loop: {loop_ms * 1000.0:.2f} us per step)" if graph_timed
+                        else "launch loop"),
         "gather_qmv_hbm_gbs": achieved,
         "hbm_frac_of_8tbs": achieved / 8000.0,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",

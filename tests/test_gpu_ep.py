@@ -64,6 +64,33 @@ def test_two_shards_sum_to_the_layer(cuda, b2q_mod, oracle, T):
     assert e < REL_L2, e
 
 
+@pytest.mark.parametrize("nshards", [3, 4, 8])
+def test_config1_shards_sum_to_the_layer(cuda, b2q_mod, nshards):
+    """The configuration-1 layer (E 128, top 8, H 4096, F 1536) as 3, 4 or 8
+    expert shards of the one-token expert-parallel kernel (43/43/42, 32 or 16
+    experts per shard, shards holding none of the token's experts included):
+    the fp32 partials sum to the single-GPU layer. This is the kernel each rank
+    runs at 2..8 GPUs, checked on one GPU."""
+    import torch
+
+    from b2q import synth
+    from b2q.ep import EPMoE, expert_range, shard_layer
+
+    E, H, F, k = 128, 4096, 1536, 8
+    L, wr = _layer(E, H, F, 120)
+    ref_moe = b2q_mod.MoE(wr, L, k, 64)
+    for seed in (121, 122):
+        x = synth.activations((1, H), seed=seed)
+        ref = ref_moe(x)
+        total = torch.zeros((1, H), dtype=torch.float32, device="cuda")
+        for r in range(nshards):
+            lo, n = expert_range(E, nshards, r)
+            _, part = EPMoE(wr, shard_layer(L, lo, n), E, lo, k)(x, return_partial=True)
+            total += part
+        e = rel_l2(total.cpu().numpy(), _bf(_np(ref)))
+        assert e < 5e-3, e
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
