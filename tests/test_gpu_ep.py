@@ -64,13 +64,16 @@ def test_two_shards_sum_to_the_layer(cuda, b2q_mod, oracle, T):
     assert e < REL_L2, e
 
 
+@pytest.mark.parametrize("T", [1, 64])
 @pytest.mark.parametrize("nshards", [3, 4, 8])
-def test_config1_shards_sum_to_the_layer(cuda, b2q_mod, nshards):
+def test_config1_shards_sum_to_the_layer(cuda, b2q_mod, nshards, T):
     """The configuration-1 layer (E 128, top 8, H 4096, F 1536) as 3, 4 or 8
     expert shards of the one-token expert-parallel kernel (43/43/42, 32 or 16
     experts per shard, shards holding none of the token's experts included):
-    the fp32 partials sum to the single-GPU layer. This is the kernel each rank
-    runs at 2..8 GPUs, checked on one GPU."""
+    the fp32 partials sum to the single-GPU layer, for one token (the
+    single-column kernel) and a 64-token window (the tensor-core products over
+    the shard's sorted rows). These are the kernels each rank runs at 2..8 GPUs,
+    checked on one GPU."""
     import torch
 
     from b2q import synth
@@ -80,9 +83,9 @@ def test_config1_shards_sum_to_the_layer(cuda, b2q_mod, nshards):
     L, wr = _layer(E, H, F, 120)
     ref_moe = b2q_mod.MoE(wr, L, k, 64)
     for seed in (121, 122):
-        x = synth.activations((1, H), seed=seed)
+        x = synth.activations((T, H), seed=seed)
         ref = ref_moe(x)
-        total = torch.zeros((1, H), dtype=torch.float32, device="cuda")
+        total = torch.zeros((T, H), dtype=torch.float32, device="cuda")
         for r in range(nshards):
             lo, n = expert_range(E, nshards, r)
             _, part = EPMoE(wr, shard_layer(L, lo, n), E, lo, k)(x, return_partial=True)
@@ -210,7 +213,7 @@ def test_a2a_dispatch_plan_and_blocks(cuda, b2q_mod):
         assert np.array_equal(sm[d, :len(rows), k:], _np(w).view(np.uint32)[rows])
 
 
-@pytest.mark.parametrize("sizes", [(48, 48), (40, 0, 56), (10, 30, 1, 55)])
+@pytest.mark.parametrize("sizes", [(48, 48), (40, 0, 56), (10, 30, 1, 55), (12, 12, 0, 12, 12, 24, 12, 12)])
 def test_a2a_emulated_ranks_match_the_layer(cuda, b2q_mod, oracle, sizes):
     E, H, F, k = 16, 1024, 512, 4
     L, wr = _layer(E, H, F, 90)
