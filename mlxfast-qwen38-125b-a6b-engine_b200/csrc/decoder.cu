@@ -787,20 +787,22 @@ __global__ void __launch_bounds__(AD_THREADS)
 
 // ---- the same attention as one thread-block cluster per (row, kv head) -------------
 // For head_dim 128: the AC_CL CTAs of a cluster share a kv head and row t; CTA
-// rank r takes chunks r, r + AC_CL, ... of AD_CH keys (a 3-buffer cp.async
+// rank r takes chunks r, r + AC_CL, ... of AC_CH keys (a 2-buffer cp.async
 // ring), and each warp keeps an online softmax over its 16 keys of every chunk
 // (running max, sum and P V accumulators in registers; the same tensor-core
-// arithmetic as attn_decode_kernel). The four warps are merged in shared
+// arithmetic as attn_decode_kernel). The eight warps are merged in shared
 // memory, then the cluster's CTAs exchange their (max, sum, partial) through
 // distributed shared memory and each writes a slice of the output: no global
 // partials, fences or arrival counters.
-constexpr int AC_CL = 8;  // CTAs per cluster
-constexpr int AC_NB = 3;  // chunk buffers of the ring
+constexpr int AC_CL = 8;         // CTAs per cluster
+constexpr int AC_NB = 2;         // chunk buffers of the ring
 constexpr int AC_D = 128;
+constexpr int AC_CH = 128;       // keys per chunk: one 16-key slice per warp
+constexpr int AC_THREADS = 256;  // eight warps
 
 __host__ __device__ inline size_t ac_smem_bytes(int g) {
   const int kld = AC_D + 8;
-  return (size_t)AC_NB * 2 * AD_CH * kld * 2 + (size_t)16 * kld * 2 + (size_t)(AD_THREADS / 32) * g * AC_D * 4 +
+  return (size_t)AC_NB * 2 * AC_CH * kld * 2 + (size_t)16 * kld * 2 + (size_t)(AC_THREADS / 32) * g * AC_D * 4 +
          (size_t)g * AC_D * 4;
 }
 
@@ -828,19 +830,19 @@ __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__global__ void __launch_bounds__(AD_THREADS)
+__global__ void __launch_bounds__(AC_THREADS)
     attn_cluster_kernel(const uint16_t* __restrict__ qkv, int q_ld, int T, const int32_t* __restrict__ positions,
                         int nq, int nk, float log2_theta, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
                         int window, float scale_log2, uint16_t* __restrict__ out, int* err) {
   constexpr int D = AC_D, KLD = D + 8, HALF = D / 2, VPR = D / 8;
   extern __shared__ __align__(16) unsigned char acs_[];
-  uint16_t* kbuf = reinterpret_cast<uint16_t*>(acs_);      // [AC_NB][AD_CH][KLD]
-  uint16_t* vbuf = kbuf + (size_t)AC_NB * AD_CH * KLD;       // [AC_NB][AD_CH][KLD]
-  uint16_t* qb = vbuf + (size_t)AC_NB * AD_CH * KLD;         // [16][KLD]
+  uint16_t* kbuf = reinterpret_cast<uint16_t*>(acs_);      // [AC_NB][AC_CH][KLD]
+  uint16_t* vbuf = kbuf + (size_t)AC_NB * AC_CH * KLD;       // [AC_NB][AC_CH][KLD]
+  uint16_t* qb = vbuf + (size_t)AC_NB * AC_CH * KLD;         // [16][KLD]
   float* wo = reinterpret_cast<float*>(qb + (size_t)16 * KLD);  // [warp][g][D] warp partials
   const int g = nq / nk;
-  float* co = wo + (size_t)(AD_THREADS / 32) * g * D;          // [g][D] the CTA's partial
-  __shared__ float wm[AD_THREADS / 32][16], wl[AD_THREADS / 32][16];
+  float* co = wo + (size_t)(AC_THREADS / 32) * g * D;          // [g][D] the CTA's partial
+  __shared__ float wm[AC_THREADS / 32][16], wl[AC_THREADS / 32][16];
   __shared__ float cm[16], cl[16];
   __shared__ float2 rot[HALF];
   __shared__ int wpos[AD_MAXT];
@@ -857,6 +859,14 @@ __global__ void __launch_bounds__(AD_THREADS)
     pos = 0;
   }
   const uint16_t* row_t = qkv + (size_t)t * q_ld;
+  // the g query heads' rows (contiguous g * D bf16, at most two 16-byte pieces
+  // per thread) are requested now and stored to shared memory after the
+  // cache append and the first copies, whose latency they share
+  const uint4* qsrc = reinterpret_cast<const uint4*>(row_t + (size_t)kh * g * D);
+  const int nq16 = g * D / 8;
+  uint4 qv0 = make_uint4(0u, 0u, 0u, 0u), qv1 = qv0;
+  if (tid < nq16) qv0 = __ldg(qsrc + tid);
+  if (tid + AC_THREADS < nq16) qv1 = __ldg(qsrc + tid + AC_THREADS);
   auto window_row = [&](int j) {
     int w = -1;
     for (int u = 0; u < T; ++u)
@@ -864,12 +874,12 @@ __global__ void __launch_bounds__(AD_THREADS)
     return w;
   };
   // row t's k / v of head kh into the cache, by the CTA whose chunks hold its position
-  if (!bad && (pos / AD_CH) % AC_CL == (int)rank) {
+  if (!bad && (pos / AC_CH) % AC_CL == (int)rank) {
     const uint16_t* krow = row_t + (size_t)(nq + kh) * D;
     const uint16_t* vrow = row_t + (size_t)(nq + nk + kh) * D;
     uint16_t* kdst = kc + ((size_t)pos * nk + kh) * D;
     uint16_t* vdst = vc + ((size_t)pos * nk + kh) * D;
-    for (int p = tid; p < HALF; p += AD_THREADS) {
+    for (int p = tid; p < HALF; p += AC_THREADS) {
       uint16_t r0, r1;
       rope_pair(krow, p, HALF, pos, log2_theta, r0, r1);
       kdst[p] = r0;
@@ -878,16 +888,16 @@ __global__ void __launch_bounds__(AD_THREADS)
       vdst[p + HALF] = vrow[p + HALF];
     }
   }
-  const int nc = pos / AD_CH + 1;  // chunks with keys
+  const int nc = pos / AC_CH + 1;  // chunks with keys
   const int mc = (int)rank < nc ? (nc - 1 - (int)rank) / AC_CL + 1 : 0;  // this CTA's chunks
   // stage chunk i of this CTA into buffer b: cache keys by cp.async, the
   // window's own keys from q|k|v (roped), rows past the position zeroed
   auto issue = [&](int i, int b) {
-    const int k0 = ((int)rank + i * AC_CL) * AD_CH;
-    const int nkeys = min(AD_CH, pos + 1 - k0);
-    uint16_t* ks = kbuf + (size_t)b * AD_CH * KLD;
-    uint16_t* vs = vbuf + (size_t)b * AD_CH * KLD;
-    for (int q = tid; q < AD_CH * VPR; q += AD_THREADS) {
+    const int k0 = ((int)rank + i * AC_CL) * AC_CH;
+    const int nkeys = min(AC_CH, pos + 1 - k0);
+    uint16_t* ks = kbuf + (size_t)b * AC_CH * KLD;
+    uint16_t* vs = vbuf + (size_t)b * AC_CH * KLD;
+    for (int q = tid; q < AC_CH * VPR; q += AC_THREADS) {
       const int key = q / VPR, c = q % VPR;
       uint16_t* kd = ks + (size_t)key * KLD + c * 8;
       uint16_t* vd = vs + (size_t)key * KLD + c * 8;
@@ -907,7 +917,7 @@ __global__ void __launch_bounds__(AD_THREADS)
       const uint16_t* urow = qkv + (size_t)u * q_ld;
       const uint16_t* krow = urow + (size_t)(nq + kh) * D;
       const uint16_t* vrow = urow + (size_t)(nq + nk + kh) * D;
-      for (int p = tid; p < HALF; p += AD_THREADS) {
+      for (int p = tid; p < HALF; p += AC_THREADS) {
         uint16_t r0, r1;
         rope_pair(krow, p, HALF, j, log2_theta, r0, r1);
         ks[(size_t)(j - k0) * KLD + p] = r0;
@@ -922,19 +932,24 @@ __global__ void __launch_bounds__(AD_THREADS)
     if (i < mc) issue(i, i);
     cp_async_commit();
   }
-  // q rows roped at row t's position: the angles once, then every head
-  for (int p = tid; p < HALF; p += AD_THREADS) {
+  // q rows roped at row t's position: the g heads' rows (contiguous, g * D
+  // bf16) staged with one 16-byte load per thread, the angles once, then every
+  // head from shared memory
+  uint16_t* qraw = reinterpret_cast<uint16_t*>(co);  // free until the CTA merge
+  if (tid < nq16) reinterpret_cast<uint4*>(qraw)[tid] = qv0;
+  if (tid + AC_THREADS < nq16) reinterpret_cast<uint4*>(qraw)[tid + AC_THREADS] = qv1;
+  for (int p = tid; p < HALF; p += AC_THREADS) {
     const float inv_freq = exp2f(-((float)p / (float)HALF) * log2_theta);
     float sn, cs;
     sincosf((float)pos * inv_freq, &sn, &cs);
     rot[p] = make_float2(cs, sn);
   }
   __syncthreads();
-  for (int q = tid; q < 16 * HALF; q += AD_THREADS) {
+  for (int q = tid; q < 16 * HALF; q += AC_THREADS) {
     const int j = q / HALF, p = q % HALF;
     uint16_t r0 = 0, r1 = 0;
     if (j < g) {
-      const uint16_t* x = row_t + (size_t)(kh * g + j) * D;
+      const uint16_t* x = qraw + (size_t)j * D;
       const float2 cssn = rot[p];
       const float a = bf2f(x[p]), c2 = bf2f(x[p + HALF]);
       r0 = f2bf(a * cssn.x - c2 * cssn.y);
@@ -957,10 +972,10 @@ __global__ void __launch_bounds__(AD_THREADS)
     cp_async_wait_group<AC_NB - 1>();
     __syncthreads();
     const int b = i % AC_NB;
-    const int k0 = ((int)rank + i * AC_CL) * AD_CH;
-    const int nkeys = min(AD_CH, pos + 1 - k0);
-    const uint16_t* ks = kbuf + (size_t)b * AD_CH * KLD;
-    const uint16_t* vs = vbuf + (size_t)b * AD_CH * KLD;
+    const int k0 = ((int)rank + i * AC_CL) * AC_CH;
+    const int nkeys = min(AC_CH, pos + 1 - k0);
+    const uint16_t* ks = kbuf + (size_t)b * AC_CH * KLD;
+    const uint16_t* vs = vbuf + (size_t)b * AC_CH * KLD;
     if (kb < nkeys) {  // warp-uniform: a warp whose keys are all past the position adds nothing
       float sc[2][4];
 #pragma unroll
@@ -1053,10 +1068,10 @@ __global__ void __launch_bounds__(AD_THREADS)
   if (tid < g) {
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < AD_THREADS / 32; ++w) M = fmaxf(M, wm[w][tid]);
+    for (int w = 0; w < AC_THREADS / 32; ++w) M = fmaxf(M, wm[w][tid]);
     float L = 0.0f;
 #pragma unroll
-    for (int w = 0; w < AD_THREADS / 32; ++w) {
+    for (int w = 0; w < AC_THREADS / 32; ++w) {
       const float a = M == -INFINITY ? 0.0f : exp2f(wm[w][tid] - M);
       wm[w][tid] = a;  // the warp's weight in the CTA's partial
       L += a * wl[w][tid];
@@ -1065,17 +1080,17 @@ __global__ void __launch_bounds__(AD_THREADS)
     cl[tid] = L;
   }
   __syncthreads();
-  for (int q = tid; q < g * D; q += AD_THREADS) {
+  for (int q = tid; q < g * D; q += AC_THREADS) {
     const int j = q / D;
     float a = 0.0f;
 #pragma unroll
-    for (int w = 0; w < AD_THREADS / 32; ++w) a = fmaf(wm[w][j], wo[(size_t)w * g * D + q], a);
+    for (int w = 0; w < AC_THREADS / 32; ++w) a = fmaf(wm[w][j], wo[(size_t)w * g * D + q], a);
     co[q] = a;
   }
   // ---- the cluster's CTAs through distributed shared memory ----
   cluster_sync_all();
   const int per = (g * D + AC_CL - 1) / AC_CL;
-  for (int q = (int)rank * per + tid; q < min(g * D, ((int)rank + 1) * per); q += AD_THREADS) {
+  for (int q = (int)rank * per + tid; q < min(g * D, ((int)rank + 1) * per); q += AC_THREADS) {
     const int j = q / D;
     float M = -INFINITY, mv[AC_CL];
 #pragma unroll
@@ -1272,7 +1287,7 @@ int b2q_attn_decode(const uint16_t* qkv, int q_ld, const int32_t* positions, uin
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(AC_CL, nk, T);
-    cfg.blockDim = dim3(AD_THREADS);
+    cfg.blockDim = dim3(AC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
