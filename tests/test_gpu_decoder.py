@@ -323,10 +323,13 @@ def test_expert_parallel_decoder_one_rank(cuda, b2q_mod):
     assert dec.status() == 0
 
 
-@pytest.mark.parametrize("positions,hd", [([0], 128), ([63], 128), ([64], 128), ([1279], 128), ([62, 63, 64], 128),
-                                          ([5, 130, 299], 128), ([127, 128], 128), ([513, 514], 128),
-                                          ([1279], 64), ([62, 63, 64], 64)])
-def test_attn_decode_matches_two_kernel_path(cuda, b2q_mod, positions, hd):
+@pytest.mark.parametrize("positions,hd,nk,S", [([0], 128, 4, 1280), ([63], 128, 4, 1280), ([64], 128, 4, 1280),
+                                                ([1279], 128, 4, 1280), ([62, 63, 64], 128, 4, 1280),
+                                                ([5, 130, 299], 128, 4, 1280), ([127, 128], 128, 4, 1280),
+                                                ([513, 514], 128, 4, 1280), ([8703], 128, 4, 8704),
+                                                ([1000, 1001], 128, 2, 1280),
+                                                ([1279], 64, 4, 1280), ([62, 63, 64], 64, 4, 1280)])
+def test_attn_decode_matches_two_kernel_path(cuda, b2q_mod, positions, hd, nk, S):
     """b2q_attn_decode (one launch) = b2q_rope_kv + b2q_gqa_decode: identical
     cache rows, outputs within rounding, and both against fp32 softmax
     attention; the window's own rows are read from q|k|v (rows 62, 63, 64 cross
@@ -341,7 +344,7 @@ def test_attn_decode_matches_two_kernel_path(cuda, b2q_mod, positions, hd):
     from b2q._lib import check, lib
 
     st = torch.cuda.current_stream().cuda_stream
-    nq, nk, S = 32, 4, 1280  # head_dim 128: the cluster kernel; 64: the chunk-partials kernel
+    nq = 32  # head_dim 128: the cluster kernel; 64: the chunk-partials kernel; nk 2: 16 q heads per kv head
     T = len(positions)
     qkv = synth.activations((T, (nq + 2 * nk) * hd), seed=70 + T)
     pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
