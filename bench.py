@@ -533,6 +533,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the config-3 full-decoder leg")
     ap.add_argument("--no-c0", action="store_true", help="skip the config-0 single-qmv leg")
+    ap.add_argument("--ep-peer", action="store_true",
+                    help="expert parallel: one-token layers reduce over peer memory inside the kernel "
+                         "(b2q_ep_peer_setup / _open) instead of an NCCL all-reduce")
     ap.add_argument("--decoder-only", type=int, default=0, metavar="TOKENS",
                     help="run only the config-3 leg with this many generated tokens (a short case for profiling)")
     ap.add_argument("--decoder-layers", type=int, default=48, help="layers of the config-3 model (48 in the spec)")
@@ -611,6 +614,8 @@ def main():
         layers = [shard_layer(Ld, e_lo, e_local) for Ld in layers]
         torch.cuda.empty_cache()
         comm = EPComm(world, rank, group=pg.group.WORLD)
+        if args.ep_peer:
+            comm.enable_peer(H, group=pg.group.WORLD)
         ws_bytes = L.b2q_ep_moe_decode_workspace_size(1, H, E, F, TOPK)
         ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
         partial = torch.empty((1, H), dtype=torch.float32, device=dev)
@@ -646,12 +651,13 @@ def main():
         pg.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     graphs = None
-    if comm is None:
-        # One GPU: the K steps replay from CUDA graphs of G captured steps (step i reads
-        # token i mod 4096 and layer i mod 8, as in the launch loop). The launch loop is
-        # timed too and reported beside it. (With expert parallelism the steps are
-        # timed as a launch loop: a capture of the steps' NCCL calls in this leg did
-        # not complete on two GPUs.)
+    if comm is None or args.ep_peer:
+        # The K steps replay from CUDA graphs of G captured steps (step i reads token
+        # i mod 4096 and layer i mod 8, as in the launch loop). The launch loop is
+        # timed too and reported beside it. Expert parallel with the peer-memory
+        # exchange: each step is one kernel launch, captured the same way. (With
+        # the NCCL all-reduce the steps are timed as a launch loop: a capture of
+        # the steps' NCCL calls in this leg did not complete on two GPUs.)
         ev0.record(stream)
         for i in range(args.steps):
             step(args.warmup + i)
@@ -674,6 +680,8 @@ def main():
         with torch.cuda.stream(stream):
             graphs[0].replay()  # untimed warm replay
         torch.cuda.synchronize(dev)
+        if pg:
+            pg.barrier()
     with ClockSampler(local_rank) as clk:
         torch.cuda.synchronize(dev)
         if graphs is not None:
@@ -901,8 +909,10 @@ def main():
         "data": "synthetic (seeded; random-init 4-bit experts)",
         "config": {"workload": WORKLOAD,
                    "parallelism": "single GPU" if world == 1 else
-                   f"ep{world}: experts sharded {E}/{world} per GPU, router replicated, one NCCL all-reduce of "
-                   f"the fp32 hidden vector per layer",
+                   (f"ep{world}: experts sharded {E}/{world} per GPU, router replicated, the fp32 partials "
+                    f"exchanged over peer memory inside the kernel (no collective call)" if args.ep_peer else
+                    f"ep{world}: experts sharded {E}/{world} per GPU, router replicated, one NCCL all-reduce of "
+                    f"the fp32 hidden vector per layer"),
                    "l2": f"cold: {n_layers} rotating layers ({n_layers * E * EXPERT_BYTES / 1e9:.1f} GB experts) "
                          f"and a fresh token per step"},
         "decode_form": ("CUDA-graph replays of the captured steps, the stream kept busy while the first graph "
@@ -920,7 +930,9 @@ def main():
                                 "api": ("b2q.MoE.__call__" if comm is None else "b2q.ep.EPMoE.__call__")
                                 + " from a Python loop (pinned host token in, output back each step)"}}
                 if n_e2e else None),
-        "gpu_launches": args.steps * (1 if world == 1 else 10),
+        # one kernel per step (one GPU, or the peer-memory exchange); with the NCCL
+        # all-reduce: the kernel, the NCCL kernel and the bf16 conversion
+        "gpu_launches": args.steps * (1 if world == 1 or args.ep_peer else 3),
         "clocks": clocks,
         "prefill": prefill,
         "decoder": decoder,

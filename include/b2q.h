@@ -268,6 +268,22 @@ B2Q_API int b2q_moe_decode_host_loop(const uint16_t* host_x, int n_tokens, uint1
 B2Q_API int b2q_ep_unique_id(void* id_out, size_t id_bytes);
 B2Q_API int b2q_ep_comm_init(void** comm_out, int nranks, int rank, const void* id, size_t id_bytes);
 B2Q_API int b2q_ep_comm_destroy(void* comm);
+/* Peer-memory reduction of the one-token layer (no reference counterpart:
+ * the reference runs on one GPU). b2q_ep_peer_setup allocates this rank's
+ * exchange buffer (b2q_ep_peer_buffer_bytes(H), zeroed; the communicator owns
+ * it) and returns its CUDA IPC handle (64 bytes); the caller gathers every
+ * rank's handle (its own transport, rank order) and every rank calls
+ * b2q_ep_peer_open with the nranks handles of handle_bytes each. From then on
+ * b2q_ep_moe_decode with S == 1, this H and a non-NULL `out` runs without a
+ * collective call: each rank's kernel stores its fp32 partial rows into every
+ * rank's buffer (plain stores over NVLink, double-buffered by a per-call
+ * epoch), publishes the epoch, waits (bounded: B2Q_ETIMEOUT in the workspace)
+ * for every rank's, and writes the summed bf16 `out` itself; `partial` is not
+ * written on this path. Every rank must make the same sequence of such calls
+ * on the communicator, one per stream order. At most 8 ranks. */
+B2Q_API size_t b2q_ep_peer_buffer_bytes(int H);
+B2Q_API int b2q_ep_peer_setup(void* comm, int H, void* handle_out, size_t handle_bytes);
+B2Q_API int b2q_ep_peer_open(void* comm, const void* handles, size_t handle_bytes);
 B2Q_API size_t b2q_ep_moe_decode_workspace_size(int S, int H, int E, int F, int k);
 B2Q_API int b2q_ep_moe_decode(void* comm, const uint16_t* x, const uint16_t* wr,
                    const uint32_t* wg, const uint16_t* sg, const uint16_t* bg,

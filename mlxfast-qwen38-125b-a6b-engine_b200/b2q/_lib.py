@@ -57,6 +57,9 @@ SIGNATURES = {
     "b2q_ep_unique_id": (_I, [_P, _SZ]),
     "b2q_ep_comm_init": (_I, [_P, _I, _I, _P, _SZ]),
     "b2q_ep_comm_destroy": (_I, [_P]),
+    "b2q_ep_peer_buffer_bytes": (_SZ, [_I]),
+    "b2q_ep_peer_setup": (_I, [_P, _I, _P, _SZ]),
+    "b2q_ep_peer_open": (_I, [_P, _P, _SZ]),
     "b2q_ep_moe_decode_workspace_size": (_SZ, [_I] * 5),
     "b2q_ep_moe_decode": (_I, [_P] * 16 + [_I] * 9 + [_P, _SZ, _P]),
     "b2q_ep_moe_prefill_workspace_size": (_SZ, [_I] * 5),

@@ -80,6 +80,29 @@ class EPComm:
         check(lib().b2q_ep_comm_init(ctypes.byref(self.ptr), world, rank,
                                      ctypes.cast(uid, ctypes.c_void_p), NCCL_ID_BYTES))
 
+    def enable_peer(self, H: int, group=None):
+        """One-token layers of hidden size H reduce over peer memory from now on
+        (b2q_ep_peer_setup / _open): every rank's exchange-buffer handle is
+        gathered through the torch.distributed group. Every rank calls it."""
+        if self.world < 2:
+            return
+        import torch.distributed as dist
+
+        hb = 64
+        h = (ctypes.c_char * hb)()
+        check(lib().b2q_ep_peer_setup(self.ptr, H, ctypes.cast(h, ctypes.c_void_p), hb))
+        mine = torch.frombuffer(bytearray(bytes(h)), dtype=torch.uint8)
+        if group is not None and dist.get_backend(group) == "nccl":
+            parts = [torch.empty(hb, dtype=torch.uint8, device="cuda") for _ in range(self.world)]
+            dist.all_gather(parts, mine.cuda(), group=group)
+            parts = [t.cpu() for t in parts]
+        else:
+            parts = [torch.empty(hb, dtype=torch.uint8) for _ in range(self.world)]
+            dist.all_gather(parts, mine, group=group)
+        allh = b"".join(bytes(t.numpy().tobytes()) for t in parts)
+        buf = (ctypes.c_char * len(allh)).from_buffer_copy(allh)
+        check(lib().b2q_ep_peer_open(self.ptr, ctypes.cast(buf, ctypes.c_void_p), hb))
+
     def close(self):
         if self.ptr:
             check(lib().b2q_ep_comm_destroy(self.ptr))

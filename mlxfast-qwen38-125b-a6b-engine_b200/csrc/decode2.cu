@@ -94,6 +94,16 @@ __device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int c0, 
       : "memory");
 }
 
+// system-scope release store / acquire load (the exchange flags between GPUs)
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ float lbf(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float hbf(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
@@ -431,6 +441,11 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   // of this call with no separate count (the last CTA out advances it)
   const unsigned tag = FUSED ? __ldcg(p.ctr + D2_CTR_TAG) + 1u : 0u;
   unsigned long long* tlg = reinterpret_cast<unsigned long long*>(p.ctr + D2_CTR_LOGITS);
+  // peer exchange: this call's epoch (the last CTA of the previous call
+  // advanced the rank's counter) and its slot of the double buffer
+  const bool XP = EP && p.npeer > 0;
+  const unsigned xep = XP ? __ldcg(reinterpret_cast<const unsigned*>(p.xpeer[p.prank])) + 1u : 0u;
+  const int xslot = (int)(xep & 1u);
   __syncthreads();
   // qmv: the weights do not depend on x, so the producer issues the copies of
   // its first units (stages 0 .. NS - 2; the last stage holds the staged x
@@ -954,10 +969,15 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
               }
             }
             const int h = blk * ROWS_D + lane;
-            if (EP)
+            if (XP) {
+              // the rank's partial of row h into every rank's exchange slot
+              for (int r2 = 0; r2 < p.npeer; ++r2)
+                p.xpeer[r2][D2_XDATA + ((size_t)(xslot * D2_XMAX + p.prank)) * H + h] = total;
+            } else if (EP) {
               p.out_f32[h] = total;
-            else
+            } else {
               p.out[h] = f2bf(total);
+            }
           }
         }
       } else {
@@ -1094,8 +1114,19 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
   }
 
   // expert parallel with no routed slot here: the partial is zero
-  if (EP && nloc == 0)
-    for (int h = blockIdx.x * NTH + tid; h < H; h += gridDim.x * NTH) p.out_f32[h] = 0.0f;
+  if (EP && nloc == 0) {
+    for (int h = blockIdx.x * NTH + tid; h < H; h += gridDim.x * NTH) {
+      if (XP) {
+        for (int r2 = 0; r2 < p.npeer; ++r2)
+          p.xpeer[r2][D2_XDATA + ((size_t)(xslot * D2_XMAX + p.prank)) * H + h] = 0.0f;
+      } else {
+        p.out_f32[h] = 0.0f;
+      }
+    }
+  }
+  // every thread's stores into other GPUs' exchange buffers are visible there
+  // before this CTA is counted
+  if (XP) __threadfence_system();
 
   // ---- exit: the last CTA out re-arms the grid words for the next call ----
   __syncthreads();
@@ -1107,6 +1138,42 @@ __global__ void __launch_bounds__(NTH, 1) d2_kernel(const __grid_constant__ D2Pa
       p.ctr[D2_CTR_TAG] = tag;
       for (int i = 0; i < MAXK; ++i) done[i] = 0u;
       __threadfence();
+      if (XP) {
+        // the rank's whole partial is in every exchange buffer: advance the
+        // rank's epoch and publish this call's flag to every rank
+        __threadfence_system();
+        *reinterpret_cast<volatile unsigned*>(p.xpeer[p.prank]) = xep;
+        for (int r2 = 0; r2 < p.npeer; ++r2)
+          st_release_sys_u32(reinterpret_cast<unsigned*>(p.xpeer[r2]) + D2_XFLAGS + xslot * D2_XMAX + p.prank, xep);
+      }
+    }
+  }
+  if (XP) {
+    // every rank's partial of this call (bounded wait on the local flags), then
+    // the rows of this CTA's down blocks summed in rank order
+    if (tid == 0) {
+      const unsigned* fl = reinterpret_cast<const unsigned*>(p.xpeer[p.prank]) + D2_XFLAGS + xslot * D2_XMAX;
+      bool ok = !*abort_flag;
+      for (int r2 = 0; r2 < p.npeer && ok; ++r2) {
+        for (uint32_t n = 0; (int)(ld_acquire_sys_u32(fl + r2) - xep) < 0; ++n) {
+          if ((n & 63u) == 63u && globaltimer() > deadline) {
+            record_error(p.err, B2Q_ETIMEOUT);
+            ok = false;
+            break;
+          }
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+    __syncthreads();
+    if (!*abort_flag) {
+      const float* xd = p.xpeer[p.prank] + D2_XDATA + (size_t)xslot * D2_XMAX * H;
+      for (int i = tid; i < nblk * ROWS_D; i += NTH) {
+        const int h = ((int)blockIdx.x + (i / ROWS_D) * (int)gridDim.x) * ROWS_D + (i % ROWS_D);
+        float sum = 0.0f;
+        for (int r2 = 0; r2 < p.npeer; ++r2) sum += __ldcg(xd + (size_t)r2 * H + h);
+        p.out[h] = f2bf(sum);
+      }
     }
   }
 }
@@ -1415,9 +1482,16 @@ int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
                   int k, int gs, const D2Scratch& scr, cudaStream_t st, int e_lo, int e_local, float* out_f32,
-                  const D2Norm& norm) {
+                  const D2Norm& norm, float* const* xpeer, int npeer, int prank) {
   D2Params p;
   std::memset(&p, 0, sizeof(p));
+  if (npeer > 0) {
+    if (npeer > D2_XMAX || !out_f32 || !out)
+      return set_error(B2Q_EINVAL, "decode kernel: peer exchange needs the expert-parallel mode and bf16 out");
+    for (int r = 0; r < npeer; ++r) p.xpeer[r] = xpeer[r];
+    p.npeer = npeer;
+    p.prank = prank;
+  }
   p.nw = norm.weight;
   p.ndelta = norm.delta;
   p.nh_out = norm.h_out;

@@ -18,6 +18,15 @@ enum { D2_QMV = 0, D2_FUSED = 1, D2_FUSED_EP = 2, D2_QMV_LUT = 3 };
 constexpr int D2_CTR_TAG = 3;
 constexpr int D2_CTR_LOGITS = 512;
 
+// Exchange buffer of the peer-memory expert-parallel decode (one per rank):
+// bytes [0, 256) a header whose word 0 is the rank's call epoch; [256, 512)
+// flags[2][D2_XMAX] (u32: the epoch whose partial source s left in slot e);
+// from byte 512 data[2][D2_XMAX][H] fp32 partials.
+constexpr int D2_XMAX = 8;
+constexpr int D2_XFLAGS = 64;   // u32 index of flags[0][0]
+constexpr int D2_XDATA = 128;   // float index of data[0][0][0]
+inline size_t d2_xbuf_bytes(int H) { return 512 + sizeof(float) * 2 * D2_XMAX * (size_t)H; }
+
 struct alignas(64) D2Params {
   CUtensorMap map[9];  // qmv: W, S, B; fused: gate W/S/B, up W/S/B, down W/S/B
   int gs;
@@ -47,6 +56,12 @@ struct alignas(64) D2Params {
   const uint16_t* ndelta;
   uint16_t* nh_out;
   float neps;
+  // expert parallel over peer memory (npeer > 0): every rank's exchange
+  // buffer (this rank's at xpeer[prank]) mapped into this process; the
+  // kernel stores its fp32 block partials into all of them, publishes a
+  // per-call epoch, waits for every rank's and writes the summed bf16 `out`
+  float* xpeer[D2_XMAX];
+  int npeer, prank;
   const uint32_t* lut;  // qmv through the metadata pair table: scale_bits | bias_bits << 16 per entry
   int lut_words;        // table entries copied into shared memory (a multiple of 4)
   int off_lut;          // shared-memory offset of the table copy
@@ -91,6 +106,7 @@ int d2_moe_decode(const uint16_t* x, const uint16_t* wr, const uint32_t* wg, con
                   const uint32_t* wu, const uint16_t* su, const uint16_t* bu, const uint32_t* wd, const uint16_t* sd,
                   const uint16_t* bd, uint16_t* out, uint32_t* idx, float* w, float* logits, int H, int E, int F,
                   int k, int gs, const D2Scratch& scr, cudaStream_t st, int e_lo = 0, int e_local = 0,
-                  float* out_f32 = nullptr, const D2Norm& norm = D2Norm());
+                  float* out_f32 = nullptr, const D2Norm& norm = D2Norm(), float* const* xpeer = nullptr,
+                  int npeer = 0, int prank = 0);
 
 }  // namespace b2q

@@ -283,7 +283,9 @@ int b2q_ep_comm_init(void** comm_out, int nranks, int rank, const void* id, size
   clear_error();
   if (!comm_out || nranks < 1 || rank < 0 || rank >= nranks || (nranks > 1 && (!id || id_bytes < sizeof(NcclUid))))
     return set_error(B2Q_EINVAL, "ep_comm_init: bad arguments");
-  EpComm* c = new EpComm{nullptr, nranks, rank};
+  EpComm* c = new EpComm{};
+  c->nranks = nranks;
+  c->rank = rank;
   if (nranks > 1) {
     if (!nccl().ok) {
       delete c;
@@ -307,8 +309,52 @@ int b2q_ep_comm_destroy(void* comm) {
   EpComm* c = static_cast<EpComm*>(comm);
   int rc = B2Q_OK;
   if (c->comm) rc = nccl_check(nccl().comm_destroy(c->comm), "ncclCommDestroy");
+  for (int r = 0; r < c->nranks && r < 8; ++r)
+    if (c->xbuf[r] && r != c->rank) cudaIpcCloseMemHandle(c->xbuf[r]);
+  if (c->xlocal) cudaFree(c->xlocal);
   delete c;
   return rc;
+}
+
+size_t b2q_ep_peer_buffer_bytes(int H) { return H > 0 ? d2_xbuf_bytes(H) : 0; }
+
+int b2q_ep_peer_setup(void* comm, int H, void* handle_out, size_t handle_bytes) {
+  clear_error();
+  EpComm* c = static_cast<EpComm*>(comm);
+  if (!c || H <= 0 || H % 16 || !handle_out || handle_bytes < sizeof(cudaIpcMemHandle_t))
+    return set_error(B2Q_EINVAL, "ep_peer_setup: bad arguments (handle needs %zu bytes)", sizeof(cudaIpcMemHandle_t));
+  if (c->nranks > D2_XMAX) return set_error(B2Q_EUNSUPPORTED, "ep_peer_setup: at most %d ranks", D2_XMAX);
+  if (c->xlocal) return set_error(B2Q_EINVAL, "ep_peer_setup: already set up");
+  const size_t bytes = d2_xbuf_bytes(H);
+  B2Q_TRY_CUDA(cudaMalloc(reinterpret_cast<void**>(&c->xlocal), bytes));
+  B2Q_TRY_CUDA(cudaMemset(c->xlocal, 0, bytes));  // epoch 0, flags 0
+  B2Q_TRY_CUDA(cudaDeviceSynchronize());
+  cudaIpcMemHandle_t h;
+  B2Q_TRY_CUDA(cudaIpcGetMemHandle(&h, c->xlocal));
+  std::memcpy(handle_out, &h, sizeof(h));
+  c->xH = H;
+  return B2Q_OK;
+}
+
+int b2q_ep_peer_open(void* comm, const void* handles, size_t handle_bytes) {
+  clear_error();
+  EpComm* c = static_cast<EpComm*>(comm);
+  if (!c || !c->xlocal || !handles || handle_bytes < sizeof(cudaIpcMemHandle_t))
+    return set_error(B2Q_EINVAL, "ep_peer_open: call b2q_ep_peer_setup first; handles of every rank needed");
+  const uint8_t* hb = static_cast<const uint8_t*>(handles);
+  for (int r = 0; r < c->nranks; ++r) {
+    if (r == c->rank) {
+      c->xbuf[r] = c->xlocal;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hb + (size_t)r * handle_bytes, sizeof(h));
+    void* ptr = nullptr;
+    B2Q_TRY_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    c->xbuf[r] = static_cast<float*>(ptr);
+  }
+  c->xready = true;
+  return B2Q_OK;
 }
 
 size_t b2q_ep_moe_decode_workspace_size(int S, int H, int E, int F, int k) {
@@ -341,10 +387,16 @@ int b2q_ep_moe_decode(void* comm, const uint16_t* x, const uint16_t* wr, const u
     for (const void* q : ptrs) all_aligned = all_aligned && aligned16(q);
     if (all_aligned && d2_moe_eligible(H, E, F, k, group_size)) {
       const D2Scratch scr{ws.err, ws.ctr, ws.logits, ws.act, ws.asc};
+      EpComm* c = static_cast<EpComm*>(comm);
+      if (c && c->nranks > 1 && c->xready && c->xH == H && out) {
+        // the reduction inside the kernel over peer memory: no collective call
+        return d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, out, idx, w, nullptr, H, E, F, k,
+                             group_size, scr, st, e_lo, e_local, partial, D2Norm(), c->xbuf, c->nranks, c->rank);
+      }
       rc = d2_moe_decode(x, wr, wg, sg, bg, wu, su, bu, wd, sd, bd, nullptr, idx, w, nullptr, H, E, F, k, group_size,
                          scr, st, e_lo, e_local, partial);
       if (rc) return rc;
-      return ep_finish(static_cast<EpComm*>(comm), partial, out, (size_t)S * H, st);
+      return ep_finish(c, partial, out, (size_t)S * H, st);
     }
   }
   uint32_t* ix = idx ? idx : ws.idx;

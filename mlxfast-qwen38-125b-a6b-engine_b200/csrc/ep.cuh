@@ -47,6 +47,12 @@ int nccl_check(int r, const char* what);
 struct EpComm {
   NcclComm comm;
   int nranks, rank;
+  // peer-memory exchange of the one-token decode (b2q_ep_peer_setup / _open):
+  // this rank's buffer, every rank's mapped here (xbuf[rank] == local), hidden size
+  float* xlocal = nullptr;
+  float* xbuf[8] = {};
+  int xH = 0;
+  bool xready = false;
 };
 
 // Expert ownership: rank r holds the contiguous block [e_lo, e_lo + e_local),

@@ -159,6 +159,77 @@ def test_two_ranks_nccl(cuda, b2q_mod, tmp_path, T):
     assert rel_l2(_bf(o0), _bf(_np(ref))) < REL_L2
 
 
+def _rank_peer(rank, world, port, path):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [root, os.path.join(root, "mlxfast-qwen38-125b-a6b-engine_b200")]
+        from b2q import synth
+        from b2q.ep import EPComm, EPMoE, expert_range, shard_layer
+
+        E, H, F, k = 16, 1024, 512, 4
+        layers = [synth.moe_layer(E, H, F, 64, device="cuda", seed=90 + 10 * i) for i in range(2)]
+        wrs = [synth.router_weight(E, H, device="cuda", seed=91 + 10 * i) for i in range(2)]
+        xs = synth.activations((6, H), device="cuda", seed=92)
+        comm = EPComm(world, rank)
+        lo, n = expert_range(E, world, rank)
+        moes = [EPMoE(wrs[i], shard_layer(layers[i], lo, n), E, lo, k, comm) for i in range(2)]
+        # six one-token calls alternating the two layers: NCCL all-reduce, then
+        # the same calls with the reduction over peer memory
+        ref = [moes[i % 2](xs[i:i + 1]).clone() for i in range(6)]
+        comm.enable_peer(H)
+        got = [moes[i % 2](xs[i:i + 1]).clone() for i in range(6)]
+        torch.cuda.synchronize()
+        for i in range(2):
+            st = moes[i]._ws.get("decode")
+            assert int(st.view(torch.int32)[0].item()) == 0, "device-side error in the peer exchange"
+        np.save(path + f".{rank}.npy", np.stack([_np(t) for t in ref + got]))
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_peer_decode(cuda, b2q_mod, tmp_path):
+    """The one-token expert-parallel layer with its reduction inside the kernel
+    over peer memory (b2q_ep_peer_setup / _open) gives the same bits as the
+    NCCL all-reduce path on both ranks, over six calls of two layers (the
+    exchange's epochs and both halves of its double buffer), and matches the
+    single-GPU layer."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    from b2q import synth
+
+    path = str(tmp_path / "peer")
+    env = dict(os.environ)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        mp.start_processes(_rank_peer, args=(2, _free_port(), path), nprocs=2, start_method="spawn", join=True)
+    finally:
+        os.environ.clear()
+        os.environ.update(env)
+    o0, o1 = np.load(path + ".0.npy"), np.load(path + ".1.npy")
+    assert np.array_equal(o0, o1)
+    assert np.array_equal(o0[:6], o0[6:])  # peer path == NCCL path, bit for bit
+    E, H, F, k = 16, 1024, 512, 4
+    xs = synth.activations((6, H), seed=92)
+    for i in range(6):
+        L = synth.moe_layer(E, H, F, 64, seed=90 + 10 * (i % 2))
+        wr = synth.router_weight(E, H, seed=91 + 10 * (i % 2))
+        ref = b2q_mod.moe_decode(xs[i:i + 1], wr, L, k)
+        assert rel_l2(_bf(o0[6 + i]), _bf(_np(ref))) < REL_L2
+
+
 # ---- all-to-all prefill ---------------------------------------------------------
 def _emulate_a2a(x, wr, L, E, k, sizes):
     """Ranks emulated on one GPU through the three phase entry points: rank r owns
