@@ -533,15 +533,16 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the config-3 full-decoder leg")
     ap.add_argument("--no-c0", action="store_true", help="skip the config-0 single-qmv leg")
-    ap.add_argument("--ep-peer", action="store_true",
-                    help="expert parallel: one-token layers reduce over peer memory inside the kernel "
-                         "(b2q_ep_peer_setup / _open) instead of an NCCL all-reduce")
+    ap.add_argument("--ep-nccl", action="store_true",
+                    help="expert parallel: one-token layers end in an NCCL all-reduce instead of the default "
+                         "reduction over peer memory inside the kernel (b2q_ep_peer_setup / _open)")
     ap.add_argument("--decoder-only", type=int, default=0, metavar="TOKENS",
                     help="run only the config-3 leg with this many generated tokens (a short case for profiling)")
     ap.add_argument("--decoder-layers", type=int, default=48, help="layers of the config-3 model (48 in the spec)")
     ap.add_argument("--ep-decoder", type=int, default=0, metavar="TOKENS",
                     help="run only the config-4 leg (expert-parallel full model over the launched ranks)")
     args = ap.parse_args()
+    args.ep_peer = not args.ep_nccl
     args.warmup = max(3, args.warmup)
 
     rank = int(os.environ.get("RANK", "0"))

@@ -159,6 +159,23 @@ def test_two_ranks_nccl(cuda, b2q_mod, tmp_path, T):
     assert rel_l2(_bf(o0), _bf(_np(ref))) < REL_L2
 
 
+def _peer_case(E, H, F, device):
+    """Three layers: two with random routers, one whose router sends every token
+    to experts 0..3 (rank 0's), so the other ranks hold none of the token's
+    experts (their partial is zero); tokens with positive entries."""
+    import torch
+
+    from b2q import synth
+
+    layers = [synth.moe_layer(E, H, F, 64, device=device, seed=90 + 10 * i) for i in range(3)]
+    wrs = [synth.router_weight(E, H, device=device, seed=91 + 10 * i) for i in range(2)]
+    w3 = torch.full((E, H), -0.01, dtype=torch.float32, device=device)
+    w3[:4] = 0.01
+    wrs.append(w3.to(torch.bfloat16))
+    xs = synth.activations((9, H), device=device, seed=92).abs()
+    return layers, wrs, xs
+
+
 def _rank_peer(rank, world, port, path):
     import torch
     import torch.distributed as dist
@@ -175,19 +192,17 @@ def _rank_peer(rank, world, port, path):
         from b2q.ep import EPComm, EPMoE, expert_range, shard_layer
 
         E, H, F, k = 16, 1024, 512, 4
-        layers = [synth.moe_layer(E, H, F, 64, device="cuda", seed=90 + 10 * i) for i in range(2)]
-        wrs = [synth.router_weight(E, H, device="cuda", seed=91 + 10 * i) for i in range(2)]
-        xs = synth.activations((6, H), device="cuda", seed=92)
+        layers, wrs, xs = _peer_case(E, H, F, "cuda")
         comm = EPComm(world, rank)
         lo, n = expert_range(E, world, rank)
-        moes = [EPMoE(wrs[i], shard_layer(layers[i], lo, n), E, lo, k, comm) for i in range(2)]
-        # six one-token calls alternating the two layers: NCCL all-reduce, then
+        moes = [EPMoE(wrs[i], shard_layer(layers[i], lo, n), E, lo, k, comm) for i in range(3)]
+        # nine one-token calls cycling the three layers: NCCL all-reduce, then
         # the same calls with the reduction over peer memory
-        ref = [moes[i % 2](xs[i:i + 1]).clone() for i in range(6)]
+        ref = [moes[i % 3](xs[i:i + 1]).clone() for i in range(9)]
         comm.enable_peer(H)
-        got = [moes[i % 2](xs[i:i + 1]).clone() for i in range(6)]
+        got = [moes[i % 3](xs[i:i + 1]).clone() for i in range(9)]
         torch.cuda.synchronize()
-        for i in range(2):
+        for i in range(3):
             st = moes[i]._ws.get("decode")
             assert int(st.view(torch.int32)[0].item()) == 0, "device-side error in the peer exchange"
         np.save(path + f".{rank}.npy", np.stack([_np(t) for t in ref + got]))
@@ -199,35 +214,38 @@ def _rank_peer(rank, world, port, path):
 def test_two_ranks_peer_decode(cuda, b2q_mod, tmp_path):
     """The one-token expert-parallel layer with its reduction inside the kernel
     over peer memory (b2q_ep_peer_setup / _open) gives the same bits as the
-    NCCL all-reduce path on both ranks, over six calls of two layers (the
-    exchange's epochs and both halves of its double buffer), and matches the
+    NCCL all-reduce path on every rank (all visible GPUs, at most 8), over nine
+    calls of three layers (the exchange's epochs, both halves of its double
+    buffer, and ranks holding none of a token's experts), and matches the
     single-GPU layer."""
     import torch
 
-    if torch.cuda.device_count() < 2:
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
-
-    from b2q import synth
 
     path = str(tmp_path / "peer")
     env = dict(os.environ)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     try:
-        mp.start_processes(_rank_peer, args=(2, _free_port(), path), nprocs=2, start_method="spawn", join=True)
+        mp.start_processes(_rank_peer, args=(world, _free_port(), path), nprocs=world, start_method="spawn",
+                           join=True)
     finally:
         os.environ.clear()
         os.environ.update(env)
-    o0, o1 = np.load(path + ".0.npy"), np.load(path + ".1.npy")
-    assert np.array_equal(o0, o1)
-    assert np.array_equal(o0[:6], o0[6:])  # peer path == NCCL path, bit for bit
+    outs = [np.load(path + f".{r}.npy") for r in range(world)]
+    o0 = outs[0]
+    for o in outs[1:]:
+        assert np.array_equal(o0, o)
+    if world <= 2:  # with more ranks NCCL may sum the partials in another order
+        assert np.array_equal(o0[:9], o0[9:])  # peer path == NCCL path, bit for bit
     E, H, F, k = 16, 1024, 512, 4
-    xs = synth.activations((6, H), seed=92)
-    for i in range(6):
-        L = synth.moe_layer(E, H, F, 64, seed=90 + 10 * (i % 2))
-        wr = synth.router_weight(E, H, seed=91 + 10 * (i % 2))
-        ref = b2q_mod.moe_decode(xs[i:i + 1], wr, L, k)
-        assert rel_l2(_bf(o0[6 + i]), _bf(_np(ref))) < REL_L2
+    layers, wrs, xs = _peer_case(E, H, F, "cuda")
+    for i in range(9):
+        ref = b2q_mod.moe_decode(xs[i:i + 1], wrs[i % 3], layers[i % 3], k)
+        assert rel_l2(_bf(o0[9 + i]), _bf(_np(ref))) < REL_L2
+        assert rel_l2(_bf(o0[i]), _bf(_np(ref))) < REL_L2
 
 
 # ---- all-to-all prefill ---------------------------------------------------------
