@@ -685,6 +685,11 @@ def main():
             pg.barrier()
     with ClockSampler(local_rank) as clk:
         torch.cuda.synchronize(dev)
+        if pg:
+            # the ranks enter the timed region together: starting the clock
+            # sampler takes each rank a different time, and with expert
+            # parallelism every step waits for every rank
+            pg.barrier()
         if graphs is not None:
             with torch.cuda.stream(stream):
                 # a spin kernel keeps the stream busy while the host enqueues the
