@@ -94,3 +94,38 @@ def test_python_ops_validate_inputs(b2q_mod):
         b2q_mod.ops._check_quant(w, s, s[:, :4], 64, 4)
     with pytest.raises(ValueError, match="only 4-bit"):
         b2q_mod.ops._check_quant(w, s, s, 64, 8)
+
+
+def test_new_entry_points_refuse_bad_arguments(b2q_mod):
+    """Host-side refusals of the fused-norm products, the one-launch decode
+    attention and the peer exchange set-up, checked before any device call
+    (fake aligned addresses are never dereferenced)."""
+    import ctypes
+
+    lib = b2q_mod.lib()
+    fake = 1 << 20
+    # fused norm: h_out aliasing h, missing h_out with delta, unsupported bits
+    assert lib.b2q_qmv_norm(fake, fake + 4096, fake, 1e-6, fake, fake, fake, fake, fake, 4096, 4096, 64, 4,
+                            None) == -1
+    assert b"alias" in lib.b2q_last_error()
+    assert lib.b2q_qmv_norm(fake, fake, fake, 1e-6, None, fake, fake, fake, fake, 4096, 4096, 64, 4, None) == -1
+    assert lib.b2q_qmv_norm(fake, None, fake, 1e-6, None, fake, fake, fake, fake, 4096, 4096, 64, 8, None) == -2
+    assert lib.b2q_moe_decode_norm(fake, fake + 4096, fake, 1e-6, fake, *([fake] * 10), fake, None, None, None,
+                                   4096, 128, 1536, 8, 64, 4, None, 0, None) == -1
+    # attention: too many window rows, head_dim not a multiple of 16, q_ld too short, null workspace
+    assert lib.b2q_attn_decode(fake, 5120, fake, fake, fake, fake, 9, 32, 4, 128, 1e6, 1280, None, fake, 1 << 30,
+                               None) == -1
+    assert lib.b2q_attn_decode(fake, 5120, fake, fake, fake, fake, 1, 32, 4, 120, 1e6, 1280, None, fake, 1 << 30,
+                               None) == -1
+    assert lib.b2q_attn_decode(fake, 100, fake, fake, fake, fake, 1, 32, 4, 128, 1e6, 1280, None, fake, 1 << 30,
+                               None) == -1
+    assert lib.b2q_attn_decode(fake, 5120, fake, fake, fake, fake, 1, 32, 4, 128, 1e6, 1280, None, None, 0,
+                               None) == -1
+    assert lib.b2q_attn_decode_workspace_size(9, 32, 4, 128, 1280) == 0
+    assert lib.b2q_attn_decode_workspace_size(8, 32, 4, 128, 1280) >= 8 * 4 * 4
+    # peer exchange: no communicator, short handle buffer, open before set-up
+    h = (ctypes.c_char * 64)()
+    assert lib.b2q_ep_peer_setup(None, 4096, ctypes.cast(h, ctypes.c_void_p), 64) == -1
+    assert lib.b2q_ep_peer_open(None, ctypes.cast(h, ctypes.c_void_p), 64) == -1
+    assert lib.b2q_ep_peer_buffer_bytes(4096) >= 2 * 8 * 4096 * 4
+    assert lib.b2q_ep_peer_buffer_bytes(0) == 0
