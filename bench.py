@@ -405,7 +405,7 @@ def _graph_us(stream, dev, n_calls, call, reps=8):
 
 
 def run_lut(dev, stream, hbm_peak, peak_kind):
-    """The metadata pair index: one-row products with each
+    """The metadata pair index of a tensor (TrackAffineLUT): one-row products with each
     group's scale / bias read through a load-time table (u16 index per group in
     place of two bf16), against the plain product on the same weights. Config
     0's shape (graph of 256 calls over 32 copies) and an lm_head-sized product
