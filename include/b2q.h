@@ -280,7 +280,8 @@ B2Q_API int b2q_ep_comm_destroy(void* comm);
  * epoch), publishes the epoch, waits (bounded: B2Q_ETIMEOUT in the workspace)
  * for every rank's, and writes the summed bf16 `out` itself; `partial` is not
  * written on this path. Every rank must make the same sequence of such calls
- * on the communicator, one per stream order. At most 8 ranks.
+ * on the communicator, one per stream order. 2 to 8 ranks; set-up and open
+ * once per communicator (a repeat is refused with B2Q_EINVAL).
  * b2q_ep_comm_destroy releases the buffer and the peer mappings: call it after
  * this rank's last exchange call has completed on its stream (every peer's
  * stores into this rank's buffer precede the flags that call waited for). */

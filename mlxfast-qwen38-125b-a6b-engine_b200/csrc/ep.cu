@@ -323,6 +323,7 @@ int b2q_ep_peer_setup(void* comm, int H, void* handle_out, size_t handle_bytes) 
   EpComm* c = static_cast<EpComm*>(comm);
   if (!c || H <= 0 || H % 16 || !handle_out || handle_bytes < sizeof(cudaIpcMemHandle_t))
     return set_error(B2Q_EINVAL, "ep_peer_setup: bad arguments (handle needs %zu bytes)", sizeof(cudaIpcMemHandle_t));
+  if (c->nranks < 2) return set_error(B2Q_EINVAL, "ep_peer_setup: one rank has nothing to exchange");
   if (c->nranks > D2_XMAX) return set_error(B2Q_EUNSUPPORTED, "ep_peer_setup: at most %d ranks", D2_XMAX);
   if (c->xlocal) return set_error(B2Q_EINVAL, "ep_peer_setup: already set up");
   const size_t bytes = d2_xbuf_bytes(H);
@@ -341,6 +342,7 @@ int b2q_ep_peer_open(void* comm, const void* handles, size_t handle_bytes) {
   EpComm* c = static_cast<EpComm*>(comm);
   if (!c || !c->xlocal || !handles || handle_bytes < sizeof(cudaIpcMemHandle_t))
     return set_error(B2Q_EINVAL, "ep_peer_open: call b2q_ep_peer_setup first; handles of every rank needed");
+  if (c->xready) return set_error(B2Q_EINVAL, "ep_peer_open: already open");
   const uint8_t* hb = static_cast<const uint8_t*>(handles);
   for (int r = 0; r < c->nranks; ++r) {
     if (r == c->rank) {

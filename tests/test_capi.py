@@ -127,5 +127,15 @@ def test_new_entry_points_refuse_bad_arguments(b2q_mod):
     h = (ctypes.c_char * 64)()
     assert lib.b2q_ep_peer_setup(None, 4096, ctypes.cast(h, ctypes.c_void_p), 64) == -1
     assert lib.b2q_ep_peer_open(None, ctypes.cast(h, ctypes.c_void_p), 64) == -1
+    # a one-rank communicator (no NCCL needed) has nothing to exchange and no buffer to open
+    comm = ctypes.c_void_p()
+    assert lib.b2q_ep_comm_init(ctypes.byref(comm), 1, 0, None, 0) == 0
+    try:
+        assert lib.b2q_ep_peer_setup(comm, 4096, ctypes.cast(h, ctypes.c_void_p), 64) == -1
+        assert b"one rank" in lib.b2q_last_error()
+        assert lib.b2q_ep_peer_open(comm, ctypes.cast(h, ctypes.c_void_p), 64) == -1
+        assert b"setup first" in lib.b2q_last_error()
+    finally:
+        assert lib.b2q_ep_comm_destroy(comm) == 0
     assert lib.b2q_ep_peer_buffer_bytes(4096) >= 2 * 8 * 4096 * 4
     assert lib.b2q_ep_peer_buffer_bytes(0) == 0
