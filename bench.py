@@ -34,8 +34,12 @@ N_LAYERS = 8
 N_TOKENS = 4096
 # Algorithmic bytes of one decode step (8 experts x (gate + up + down) packed
 # weights with scales/biases, the bf16 router, activations): 86,049,344 B.
+# Activations: x and the output row (2 x 8,192), the SwiGLU rows written and
+# read back (2 x 8 x 1536 x 2), the router logits (512) and the selected
+# experts with their weights (64): 66,112 B.
 EXPERT_BYTES = 3 * (F * (H // 2 + 2 * 2 * H // GS))  # gate/up/down are the same size here
-DECODE_BYTES = TOPK * EXPERT_BYTES + E * H * 2 + 65_536
+ACT_BYTES = 2 * H * 2 + 2 * TOPK * F * 2 + E * 4 + TOPK * 4 * 2
+DECODE_BYTES = TOPK * EXPERT_BYTES + E * H * 2 + ACT_BYTES
 PREFILL_FLOP = PREFILL_T * TOPK * (2 * 2 * F * H + 2 * H * F) + 2 * PREFILL_T * E * H
 METRIC = "decode tok/s (bs=1) + gather_qmv HBM GB/s and % of 8 TB/s; prefill tok/s"
 WORKLOAD = "config 1: one MoE layer decode, bs=1, H4096 E128 top8 F1536 4-bit g64"
@@ -181,6 +185,30 @@ def prefill_cpu_baseline(t_row, kind):
             "sample": (f"extrapolated: measured per-row time of the reference's MLX CPU kernel (K=4096 4-bit g64, "
                        f"bf16 sum) x {rows} row-equivalents per 2048-token layer (16384 assignments x "
                        f"{prefill_rows_per_assignment()} + router); SwiGLU, sort and combine omitted")}
+
+
+# config 3 shape (the defaults of b2q.model.DecoderConfig)
+DEC_LAYERS, DEC_QKV_ROWS, DEC_ATTN_DIM, DEC_VOCAB = 48, (32 + 2 * 4) * 128, 32 * 128, 151936
+
+
+def decoder_rows_per_token(n_layers=DEC_LAYERS):
+    """K=4096 row-equivalents of the 4-bit products one decode token runs: per
+    layer q|k|v (5120 rows), o (4096 rows of K = 4096) and the k experts; then
+    the tied lm_head (151,936 rows)."""
+    return n_layers * (DEC_QKV_ROWS + H * DEC_ATTN_DIM // 4096 + decode_rows_per_token()) + DEC_VOCAB
+
+
+def decoder_cpu_baseline(t_row, kind, n_layers=DEC_LAYERS):
+    """Config 3 on one core, lower bound (quantized share only): the measured row
+    cost of the reference kernel times the 4-bit rows of one token; attention,
+    norms, the bf16 router and sampling are left out."""
+    rows = decoder_rows_per_token(n_layers)
+    return {"value": 1.0 / (rows * t_row), "unit": "tok/s", "cores": 1, "kind": kind,
+            "sample": (f"lower bound, quantized share only, extrapolated: measured per-row time of the reference's "
+                       f"MLX CPU kernel (K=4096 4-bit g64, bf16 sum) x {rows} row-equivalents per token "
+                       f"({n_layers} layers x (q|k|v {DEC_QKV_ROWS} + o {DEC_ATTN_DIM} + {TOPK} experts "
+                       f"{decode_rows_per_token()}) + lm_head {DEC_VOCAB}); attention, norms, router and "
+                       f"sampling omitted")}
 
 
 def cpu_baseline_sample(budget_s=12.0):
@@ -895,6 +923,8 @@ def main():
         cpu = cpu_baseline_sample()
         if prefill is not None:
             prefill["cpu_baseline"] = prefill_cpu_baseline(cpu["row_s"], cpu["kind"])
+        if decoder is not None and "decode_tok_s" in decoder:
+            decoder["cpu_baseline"] = decoder_cpu_baseline(cpu["row_s"], cpu["kind"])
         if c0 is not None:
             c0["cpu_baseline"] = {"value": 1.0 / (cpu["row_s"] * 4096), "unit": "calls/s", "cores": 1,
                                   "kind": cpu["kind"],
