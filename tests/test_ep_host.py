@@ -271,3 +271,73 @@ def test_a2a_layer_on_two_gloo_ranks(tmp_path):
     full = o.moe_experts_decode(x, idx, w, layer, shp["k"], group_size=shp["gs"])
     e = rel_l2(got, bf16_to_f32(full))
     assert e < REL_L2, e
+
+
+class _RecordingLib:
+    """Stands in for the library in the handshake test: records what the
+    host side hands to each entry point (no device, no NCCL)."""
+
+    def __init__(self, rank, world):
+        import ctypes
+
+        self.ctypes, self.rank, self.world = ctypes, rank, world
+        self.uid_seen = self.opened = None
+        self.setup_H = None
+
+    def b2q_ep_unique_id(self, p, n):
+        self.ctypes.memmove(p, bytes((i * 7 + 3) % 256 for i in range(n)), n)
+        return 0
+
+    def b2q_ep_comm_init(self, pptr, world, rank, uid, n):
+        assert (world, rank) == (self.world, self.rank)
+        self.uid_seen = self.ctypes.string_at(uid, n)
+        return 0
+
+    def b2q_ep_peer_setup(self, comm, H, h, hb):
+        self.setup_H = H
+        self.ctypes.memmove(h, bytes([0x40 + self.rank]) * hb, hb)
+        return 0
+
+    def b2q_ep_peer_open(self, comm, handles, hb):
+        self.opened = self.ctypes.string_at(handles, hb * self.world)
+        return 0
+
+
+def _handshake_rank_main(rank, world, port, result_path):
+    import json
+
+    import torch.distributed as dist
+
+    import b2q.ep as ep
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fake = _RecordingLib(rank, world)
+        ep.lib = lambda: fake
+        comm = ep.EPComm(world, rank, group=dist.group.WORLD)
+        comm.enable_peer(4096, group=dist.group.WORLD)
+        with open(f"{result_path}.{rank}", "w") as f:
+            json.dump({"uid": fake.uid_seen.hex(), "opened": fake.opened.hex(), "H": fake.setup_H}, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_comm_handshakes_on_gloo_ranks(tmp_path):
+    """EPComm over a gloo group: every rank's communicator gets rank 0's NCCL
+    id, and enable_peer hands b2q_ep_peer_open every rank's exchange handle in
+    rank order (the layout the library indexes by rank)."""
+    import json
+
+    import torch.multiprocessing as mp
+
+    world = 3
+    path = str(tmp_path / "hs")
+    mp.start_processes(_handshake_rank_main, args=(world, _free_port(), path), nprocs=world, start_method="spawn",
+                       join=True)
+    uid = bytes((i * 7 + 3) % 256 for i in range(128)).hex()
+    want = b"".join(bytes([0x40 + r]) * 64 for r in range(world)).hex()
+    for r in range(world):
+        with open(f"{path}.{r}") as f:
+            got = json.load(f)
+        assert got == {"uid": uid, "opened": want, "H": 4096}
