@@ -244,14 +244,14 @@ B2Q_API int b2q_moe_decode_noalloc(const uint16_t* x, const uint16_t* wr,
  * row is copied back to host_out (pinned). The copies run on a second stream
  * with two device buffers each way (dev_x2, dev_out2: 2 * H bf16), so they
  * overlap the kernels. *ms_per_step receives the CUDA-event time of the last
- * `steps` steps, from the first timed kernel's enqueue point to the last output
- * copy. Returns after the loop finished (it synchronises). */
+ * `steps` steps, from their first input copy to their last output copy (the
+ * timed steps start from an empty pipeline). Returns after the loop finished
+ * (it synchronises). */
 B2Q_API int b2q_moe_decode_host_loop(const uint16_t* host_x, int n_tokens, uint16_t* host_out,
                    const uint16_t* const* wr, const void* const* w9, int n_layers,
                    int H, int E, int F, int k, int group_size, int bits,
                    uint16_t* dev_x2, uint16_t* dev_out2, void* workspace, size_t workspace_bytes,
                    int warmup, int steps, void* stream, float* ms_per_step);
-
 /* Expert parallelism (experts sharded over ranks; one NCCL all-reduce per layer).
  * The reference's expert-parallel configuration of its MoE layer
  * (moeForwardShared, Runner/FastModel/TrackFastModel.swift:867-1009) with

@@ -123,6 +123,13 @@ def test_new_entry_points_refuse_bad_arguments(b2q_mod):
                                None) == -1
     assert lib.b2q_attn_decode_workspace_size(9, 32, 4, 128, 1280) == 0
     assert lib.b2q_attn_decode_workspace_size(8, 32, 4, 128, 1280) >= 8 * 4 * 4
+    # the native host loop: no steps, or null buffers
+    w9 = (ctypes.c_void_p * 9)(*([fake] * 9))
+    wr = (ctypes.c_void_p * 1)(fake)
+    assert lib.b2q_moe_decode_host_loop(fake, 1, fake, wr, w9, 1, 4096, 128, 1536, 8, 64, 4, fake, fake, fake,
+                                        1 << 20, 1, 0, None, ctypes.byref(ctypes.c_float())) == -1
+    assert lib.b2q_moe_decode_host_loop(fake, 1, fake, wr, w9, 1, 4096, 128, 1536, 8, 64, 4, None, fake, fake,
+                                        1 << 20, 1, 4, None, ctypes.byref(ctypes.c_float())) == -1
     # peer exchange: no communicator, short handle buffer, open before set-up
     h = (ctypes.c_char * 64)()
     assert lib.b2q_ep_peer_setup(None, 4096, ctypes.cast(h, ctypes.c_void_p), 64) == -1
