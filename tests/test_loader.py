@@ -6,7 +6,6 @@ from __future__ import annotations
 import json
 import struct
 
-import numpy as np
 import pytest
 
 
