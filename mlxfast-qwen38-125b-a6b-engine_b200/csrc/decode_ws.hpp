@@ -53,6 +53,7 @@ constexpr size_t D2_CTR_BYTES = 4096;
 static_assert(D2_CTR_LOGITS * 4 + 256 * 8 <= (int)D2_CTR_BYTES, "counter block");
 
 static inline DecodeWs decode_ws_layout(void* base, int S, int H, int E, int F, int k) {
+  (void)H;  // no region scales with the hidden size; kept for the size query's signature
   DecodeWs d{};
   size_t off = 0;
   char* b = static_cast<char*>(base);
