@@ -10,6 +10,12 @@ path never does.
                  :1158-1236) compiled from the reference tree: the bf16 kernel,
                  the same kernel over fp32 operands (fp32 accumulation) and the
                  gather loop over index pairs.
+* ``affine_lut_*`` -- the metadata pair index, restated from the Runner's
+                 Swift source (TrackAffineLUT.swift). No Swift toolchain is
+                 here and the reference holds no test vectors for it, so this
+                 part is parity unpinned: it is checked by its own exact round
+                 trip (table[index] reproduces every group's bits) and by the
+                 two build orders agreeing with the literal loop.
 
 bf16 arrays are numpy ``uint16`` bit patterns; packed weights are ``uint32``.
 """
