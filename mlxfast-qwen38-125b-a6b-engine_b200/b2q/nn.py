@@ -146,6 +146,14 @@ class MoE:
         applied to rms_norm(h_out) * norm_weight. Returns the layer output, or
         None when the shape is outside the fused kernel (the caller then takes
         the separate norm and the plain call)."""
+        for name, t in (("h", h), ("norm_weight", norm_weight), ("delta", delta), ("h_out", h_out), ("out", out)):
+            if t is None and name in ("delta", "h_out", "out"):
+                continue
+            # the kernel dereferences these pointers on the device: refuse host or mis-shaped tensors here
+            if (not isinstance(t, torch.Tensor) or t.dtype != torch.bfloat16 or t.device.type != "cuda"
+                    or t.device != h.device or t.numel() != self._H or not t.is_contiguous()):
+                raise ValueError(f"{name}: expected a contiguous CUDA bf16 tensor of H={self._H} elements on h's "
+                                 "device")
         if self._ws1 is None or self._ws1.buf.device != h.device:
             size = ops.lib().b2q_moe_decode_workspace_size(1, self._H, self._E, self._F, self.top_k)
             self._ws1 = ops.Workspace(size, h.device)

@@ -43,3 +43,21 @@ def test_decoder_kernels_refuse_bad_shapes(b2q_mod):
     assert lib.b2q_gqa_decode(None, 4096, None, None, None, None, 1, 30, 4, 128, 64, None, None, 0, None) == -1
     assert lib.b2q_rope_kv(None, 0, 8, 2, 128, None, 1e6, None, None, 64, None, None) == 0
     assert lib.b2q_add_rms_norm(None, None, None, None, None, 1, 1001, 1e-6, None) == -1
+
+
+def test_moe_decode_norm_refuses_host_tensors():
+    """MoE.decode_norm hands raw pointers to a kernel: host tensors, other
+    dtypes and wrong sizes are refused before the library is called."""
+    import pytest
+    import torch
+
+    from b2q.nn import MoE
+
+    m = MoE.__new__(MoE)  # the refusals need only the hidden size (no device here)
+    m._H, m._ws1 = 16, None
+    h = torch.zeros((1, 16), dtype=torch.bfloat16)
+    nw = torch.ones(16, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="h: expected"):
+        m.decode_norm(h, None, nw, 1e-6, None)
+    with pytest.raises(ValueError, match="expected"):
+        m.decode_norm(h.float(), None, nw, 1e-6, None)
