@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 
 from ._lib import B2QError, check, lib
-from .ops import _stream
+from .ops import _BF16, _PACK, _dev, _stream
 
 MAX_ENTRIES = 32768  # the reference's table limit (TrackAffineLUT.swift:57)
 
@@ -69,7 +69,10 @@ def qmv_lut(x: torch.Tensor, w: torch.Tensor, meta: AffineLUT, group_size: int =
     K, N = x.shape[-1], w.shape[0]
     if K != w.shape[1] * 8 or K % group_size or x.numel() != K:
         return None
-    x = x.contiguous()
+    x = _dev(x.contiguous(), "x", _BF16)
+    _dev(w, "w", _PACK)  # the kernel reads these pointers on the device
+    if x.device != w.device or meta.index.device != w.device:
+        raise ValueError("qmv_lut: x, w and the pair index must be on one CUDA device")
     y = torch.empty(x.shape[:-1] + (N,), dtype=torch.bfloat16, device=x.device)
     rc = lib().b2q_qmv_lut(x.data_ptr(), w.data_ptr(), meta.index.data_ptr(), meta.table.data_ptr(), meta.count,
                            y.data_ptr(), N, K, group_size, bits, _stream())

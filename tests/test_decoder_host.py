@@ -61,3 +61,20 @@ def test_moe_decode_norm_refuses_host_tensors():
         m.decode_norm(h, None, nw, 1e-6, None)
     with pytest.raises(ValueError, match="expected"):
         m.decode_norm(h.float(), None, nw, 1e-6, None)
+
+
+def test_qmv_lut_refuses_host_tensors():
+    """b2q.lut.qmv_lut hands raw pointers to a kernel: a host x or w of the
+    one-row shape is refused before the library is called."""
+    import pytest
+    import torch
+
+    from b2q.lut import AffineLUT, qmv_lut
+
+    meta = AffineLUT(torch.zeros((32, 8), dtype=torch.int16), torch.zeros(4, dtype=torch.int32), 1)
+    x = torch.zeros((1, 512), dtype=torch.bfloat16)
+    w = torch.zeros((32, 64), dtype=torch.int32)
+    with pytest.raises(ValueError, match="CUDA device"):
+        qmv_lut(x, w, meta)
+    # not the one-row product: left to the plain path
+    assert qmv_lut(torch.zeros((2, 512), dtype=torch.bfloat16), w, meta) is None
